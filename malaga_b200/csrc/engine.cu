@@ -1,0 +1,1255 @@
+// Host side of the decode engine: GGUF loading and weight repacking, the
+// encoder pass, the fixed-buffer greedy step and its CUDA-graph cache, and the
+// C ABI of include/malaga_b200.h.
+//
+// Reference structure mirrored here (crates/malaga-core/src/):
+//   model.rs:343-433   Nllb::load         -> Engine::load
+//   model.rs:463-500   encode_cross       -> mgb_encode
+//   graph.rs:23-135    StaticState        -> StaticState
+//   graph.rs:138-140   bucket()           -> bucket()
+//   graph.rs:173-334   GraphCache         -> Engine::greedy + the LRU cache
+//   model.rs:552-612   step_static        -> Engine::launch_step
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <functional>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/malaga_b200.h"
+#include "kernels.cuh"
+
+using namespace mgb;
+
+// ---------------------------------------------------------------------------
+// Errors
+
+static thread_local std::string g_err;
+
+static mgb_status set_err(mgb_status s, const char *fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return s;
+}
+
+static mgb_status cuda_err(cudaError_t e, const char *what) {
+    if (e == cudaErrorMemoryAllocation)
+        return set_err(MGB_ERR_OOM, "%s: CUDA_ERROR_OUT_OF_MEMORY (%s)", what, cudaGetErrorString(e));
+    return set_err(MGB_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+#define CK(call)                                                  \
+    do {                                                          \
+        cudaError_t e_ = (call);                                  \
+        if (e_ != cudaSuccess) return cuda_err(e_, #call);        \
+    } while (0)
+
+#define TRY(call)                           \
+    do {                                    \
+        mgb_status s_ = (call);             \
+        if (s_ != MGB_OK) return s_;        \
+    } while (0)
+
+// ---------------------------------------------------------------------------
+// GGUF
+
+namespace {
+
+struct GgufTensor {
+    std::string name;
+    int type = -1;
+    std::vector<uint64_t> dims;  // GGML order: dims[0] innermost
+    const uint8_t *data = nullptr;
+    long rows() const {
+        long r = 1;
+        for (size_t i = 1; i < dims.size(); ++i) r *= (long)dims[i];
+        return r;
+    }
+    long cols() const { return dims.empty() ? 0 : (long)dims[0]; }
+};
+
+struct GgufFile {
+    void *map = MAP_FAILED;
+    size_t size = 0;
+    std::map<std::string, uint64_t> u32;
+    std::map<std::string, GgufTensor> tensors;
+    ~GgufFile() {
+        if (map != MAP_FAILED) munmap(map, size);
+    }
+};
+
+long row_bytes(int type, long n) {
+    switch (type) {
+        case T_F32: return 4 * n;
+        case T_F16: return 2 * n;
+        case T_Q8_0: return n % 32 ? -1 : n / 32 * 34;
+        case T_Q4_K: return n % 256 ? -1 : n / 256 * 144;
+        case T_Q6_K: return n % 256 ? -1 : n / 256 * 210;
+    }
+    return -1;
+}
+
+mgb_status parse_gguf(const char *path, GgufFile &f) {
+    int fd = open(path, O_RDONLY);
+    if (fd < 0) return set_err(MGB_ERR_IO, "cannot open %s", path);
+    struct stat st;
+    fstat(fd, &st);
+    f.size = (size_t)st.st_size;
+    f.map = mmap(nullptr, f.size, PROT_READ, MAP_PRIVATE, fd, 0);
+    close(fd);
+    if (f.map == MAP_FAILED) return set_err(MGB_ERR_IO, "cannot map %s", path);
+    const uint8_t *base = (const uint8_t *)f.map, *p = base, *end = base + f.size;
+    auto need = [&](size_t n) { return (size_t)(end - p) >= n; };
+    auto r32 = [&]() { uint32_t v; memcpy(&v, p, 4); p += 4; return v; };
+    auto r64 = [&]() { uint64_t v; memcpy(&v, p, 8); p += 8; return v; };
+    auto rstr = [&](std::string &s) -> bool {
+        if (!need(8)) return false;
+        uint64_t n = r64();
+        if (!need(n)) return false;
+        s.assign((const char *)p, n);
+        p += n;
+        return true;
+    };
+    if (!need(24) || r32() != 0x46554747u) return set_err(MGB_ERR_IO, "%s is not a GGUF file", path);
+    uint32_t version = r32();
+    if (version < 2) return set_err(MGB_ERR_IO, "unsupported GGUF version %u", version);
+    uint64_t nt = r64(), nkv = r64();
+    uint64_t align = 32;
+    static const int scalar[] = {1, 1, 2, 2, 4, 4, 4, 1, 0, 0, 8, 8, 8};
+    std::function<bool(uint32_t)> skip = [&](uint32_t t) -> bool {
+        if (t == 8) { std::string s; return rstr(s); }
+        if (t == 9) {
+            if (!need(12)) return false;
+            uint32_t et = r32();
+            uint64_t n = r64();
+            for (uint64_t i = 0; i < n; ++i)
+                if (!skip(et)) return false;
+            return true;
+        }
+        if (t > 12 || !need(scalar[t])) return false;
+        p += scalar[t];
+        return true;
+    };
+    for (uint64_t i = 0; i < nkv; ++i) {
+        std::string key;
+        if (!rstr(key) || !need(4)) return set_err(MGB_ERR_IO, "truncated GGUF metadata");
+        uint32_t t = r32();
+        if (t == 4 || t == 5) {
+            if (!need(4)) return set_err(MGB_ERR_IO, "truncated GGUF metadata");
+            f.u32[key] = r32();
+        } else if (t == 7 || t == 0 || t == 1) {
+            if (!need(1)) return set_err(MGB_ERR_IO, "truncated GGUF metadata");
+            f.u32[key] = *p++;
+        } else if (t == 10 || t == 11) {
+            if (!need(8)) return set_err(MGB_ERR_IO, "truncated GGUF metadata");
+            f.u32[key] = r64();
+        } else if (!skip(t)) {
+            return set_err(MGB_ERR_IO, "bad GGUF metadata value for %s", key.c_str());
+        }
+    }
+    if (f.u32.count("general.alignment")) align = f.u32["general.alignment"];
+    std::vector<std::pair<std::string, uint64_t>> offs;
+    for (uint64_t i = 0; i < nt; ++i) {
+        GgufTensor t;
+        if (!rstr(t.name) || !need(4)) return set_err(MGB_ERR_IO, "truncated GGUF tensor info");
+        uint32_t nd = r32();
+        if (nd < 1 || nd > 4 || !need(8 * nd + 12)) return set_err(MGB_ERR_IO, "bad tensor info %s", t.name.c_str());
+        for (uint32_t k = 0; k < nd; ++k) t.dims.push_back(r64());
+        t.type = (int)r32();
+        offs.emplace_back(t.name, r64());
+        f.tensors[t.name] = t;
+    }
+    size_t data0 = ((size_t)(p - base) + align - 1) / align * align;
+    for (auto &o : offs) {
+        GgufTensor &t = f.tensors[o.first];
+        long rb = row_bytes(t.type, t.cols());
+        if (rb < 0) return set_err(MGB_ERR_UNSUPPORTED, "tensor %s: type %d with rows of %ld values", t.name.c_str(), t.type, t.cols());
+        if (data0 + o.second + (size_t)rb * t.rows() > f.size) return set_err(MGB_ERR_IO, "tensor %s past end of file", t.name.c_str());
+        t.data = base + data0 + o.second;
+    }
+    return MGB_OK;
+}
+
+int host_block_pos(int j, int nb, int G) { return nb <= 32 ? j : (j % G) * 32 + j / G; }
+
+// Unpacks the 32 values of 32-block `j` of a Q4_K row (0..15) / Q6_K row (0..63).
+void q4k_block_values(const uint8_t *row, int j, uint8_t *q) {
+    const uint8_t *sb = row + (j / 8) * 144, *qs = sb + 16;
+    const int i = j % 8, c = i / 2, hi = i & 1;
+    for (int k = 0; k < 32; ++k) q[k] = hi ? (qs[32 * c + k] >> 4) : (qs[32 * c + k] & 0xf);
+}
+
+void q6k_block_values(const uint8_t *row, int j, uint8_t *q) {
+    const uint8_t *b = row + (j / 8) * 210;
+    for (int k = 0; k < 32; ++k) {
+        const int i = (j % 8) * 32 + k, n = i / 128, g = (i % 128) / 32, l = i % 32;
+        const uint8_t *ql = b + 64 * n, *qh = b + 128 + 32 * n;
+        int v;
+        switch (g) {
+            case 0: v = (ql[l] & 0xf) | (((qh[l] >> 0) & 3) << 4); break;
+            case 1: v = (ql[l + 32] & 0xf) | (((qh[l] >> 2) & 3) << 4); break;
+            case 2: v = (ql[l] >> 4) | (((qh[l] >> 4) & 3) << 4); break;
+            default: v = (ql[l + 32] >> 4) | (((qh[l] >> 6) & 3) << 4); break;
+        }
+        q[k] = (uint8_t)v;
+    }
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Engine
+
+struct StaticState {
+    int b = 0, s = 0, m = 0;
+    uint32_t *ids = nullptr, *step = nullptr, *out = nullptr, *lens = nullptr;
+    uint8_t *finished = nullptr;
+    float *x = nullptr, *q = nullptr, *a = nullptr, *u = nullptr, *xf = nullptr;
+    QAct act;
+    std::vector<__half *> kc, vc, ck, cv;
+    float *part_v = nullptr;
+    uint32_t *part_i = nullptr;
+    float *logits = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    size_t graph_nodes = 0;
+    size_t bytes = 0;
+    uint64_t last_used = 0;
+    std::vector<void *> allocs;
+};
+
+struct mgb_batch {
+    int b = 0, s = 0;
+    std::vector<uint32_t> lens;
+    uint32_t *d_lens = nullptr;
+    __half *cross = nullptr;  // [L][2][b][H][s][hd]
+    size_t cross_bytes = 0;
+    mgb_ctx *owner = nullptr;
+};
+
+static constexpr int kLmParts = 148 * 8;  // CTAs of the fused LM-head argmax
+static constexpr size_t kGraphBytes = 32u << 20;
+
+struct mgb_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    mgb_options opts{};
+    Config cfg;
+    uint8_t *arena = nullptr;
+    size_t arena_bytes = 0;
+    Matrix embed;
+    std::vector<EncLayer> enc;
+    std::vector<DecLayer> dec;
+    Norm enc_norm, dec_norm;
+    float *pos = nullptr;
+    float embed_scale = 1.0f;
+    uint64_t launches = 0;
+    int alloc_count = 0;
+    bool inject_armed = false;  // fault injection counts allocations made after mgb_open
+    bool capture = true;
+    uint64_t clock = 0;
+    std::vector<std::unique_ptr<StaticState>> cache;
+    size_t weight_bytes = 0, step_bytes = 0;
+
+    mgb_status dalloc(void **p, size_t bytes) {
+        if (inject_armed && opts.fail_alloc_after >= 0 && alloc_count++ == opts.fail_alloc_after)
+            return set_err(MGB_ERR_OOM, "injected allocation failure: CUDA_ERROR_OUT_OF_MEMORY");
+        cudaError_t e = cudaMalloc(p, bytes < 256 ? 256 : bytes);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            *p = nullptr;
+            return cuda_err(e, "cudaMalloc");
+        }
+        return MGB_OK;
+    }
+};
+
+namespace {
+
+template <typename F>
+mgb_status launch_check(mgb_ctx *c, F &&f) {
+    f();
+    ++c->launches;
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_err(e, "kernel launch");
+    return MGB_OK;
+}
+
+// Loads one tensor into the arena in the engine layout. `cursor` advances.
+struct Loader {
+    mgb_ctx *c;
+    GgufFile *f;
+    std::vector<uint8_t> host;  // staging image of the whole arena
+    size_t cursor = 0;
+
+    size_t reserve(size_t n) {
+        cursor = (cursor + 255) / 256 * 256;
+        size_t at = cursor;
+        cursor += n;
+        return at;
+    }
+
+    const GgufTensor *get(const std::string &name) {
+        auto it = f->tensors.find(name);
+        return it == f->tensors.end() ? nullptr : &it->second;
+    }
+};
+
+// Two passes over the model: pass 0 sizes the arena, pass 1 fills the staging image.
+struct Planner {
+    Loader &L;
+    int pass;
+    std::vector<std::pair<const uint8_t **, size_t>> fix;  // device pointer slots -> arena offsets
+
+    void ptr(const uint8_t **slot, size_t off) { fix.emplace_back(slot, off); }
+
+    mgb_status dense(const std::string &name, long n, const float **out) {
+        const GgufTensor *t = L.get(name);
+        if (!t) return set_err(MGB_ERR_IO, "missing tensor %s", name.c_str());
+        if (t->type != T_F32 || t->cols() * t->rows() != n)
+            return set_err(MGB_ERR_UNSUPPORTED, "tensor %s must be f32 with %ld values", name.c_str(), n);
+        size_t off = L.reserve(4 * n);
+        if (pass == 1) memcpy(L.host.data() + off, t->data, 4 * n);
+        ptr(reinterpret_cast<const uint8_t **>(out), off);
+        return MGB_OK;
+    }
+
+    mgb_status norm(const std::string &name, long d, Norm &n) {
+        TRY(dense(name + ".weight", d, &n.g));
+        return dense(name + ".bias", d, &n.b);
+    }
+
+    mgb_status matrix(const std::string &name, Matrix &M, long want_rows, long want_cols, bool bias) {
+        const GgufTensor *t = L.get(name + ".weight");
+        if (!t) return set_err(MGB_ERR_IO, "missing tensor %s.weight", name.c_str());
+        const long N = t->rows(), K = t->cols();
+        if (N != want_rows || K != want_cols)
+            return set_err(MGB_ERR_INVALID, "tensor %s.weight is [%ld, %ld], expected [%ld, %ld]", name.c_str(), N, K,
+                           want_rows, want_cols);
+        if (t->type != T_F32 && t->type != T_Q8_0 && t->type != T_Q4_K && t->type != T_Q6_K)
+            return set_err(MGB_ERR_UNSUPPORTED, "tensor %s.weight: GGML type %d is not supported", name.c_str(), t->type);
+        if (K % 32 || (K / 32 > 32 && (K / 32) % 32))
+            return set_err(MGB_ERR_UNSUPPORTED, "tensor %s.weight: row length %ld", name.c_str(), K);
+        M.type = t->type;
+        M.N = (int)N;
+        M.K = (int)K;
+        M.nb = (int)(K / 32);
+        M.G = M.nb > 32 ? M.nb / 32 : 1;
+        const int nb = M.nb, G = M.G, nsb = (int)(K / 256);
+        const long rb = row_bytes(t->type, K);
+        M.bytes = (size_t)rb * N;
+        if (t->type == T_F32) {
+            size_t off = L.reserve((size_t)4 * N * K);
+            if (pass == 1) memcpy(L.host.data() + off, t->data, (size_t)4 * N * K);
+            ptr(&M.a, off);
+        } else if (t->type == T_Q8_0) {
+            size_t oq = L.reserve((size_t)N * nb * 32), od = L.reserve((size_t)N * nb * 2);
+            if (pass == 1) {
+                uint8_t *hq = L.host.data() + oq, *hd = L.host.data() + od;
+#pragma omp parallel for schedule(static)
+                for (long r = 0; r < N; ++r) {
+                    const uint8_t *row = t->data + (size_t)r * rb;
+                    for (int j = 0; j < nb; ++j) {
+                        const int pos = host_block_pos(j, nb, G);
+                        memcpy(hd + ((size_t)r * nb + pos) * 2, row + 34 * j, 2);
+                        memcpy(hq + ((size_t)r * nb + pos) * 32, row + 34 * j + 2, 32);
+                    }
+                }
+            }
+            ptr(&M.a, oq);
+            ptr(&M.b, od);
+        } else if (t->type == T_Q4_K) {
+            size_t oq = L.reserve((size_t)N * nb * 16), oh = L.reserve((size_t)N * nsb * 16);
+            if (pass == 1) {
+                uint8_t *hq = L.host.data() + oq, *hh = L.host.data() + oh;
+#pragma omp parallel for schedule(static)
+                for (long r = 0; r < N; ++r) {
+                    const uint8_t *row = t->data + (size_t)r * rb;
+                    uint8_t q[32];
+                    for (int j = 0; j < nb; ++j) {
+                        q4k_block_values(row, j, q);
+                        uint8_t *dst = hq + ((size_t)r * nb + host_block_pos(j, nb, G)) * 16;
+                        for (int k = 0; k < 16; ++k) dst[k] = (uint8_t)(q[k] | (q[k + 16] << 4));
+                    }
+                    for (int s = 0; s < nsb; ++s) memcpy(hh + ((size_t)r * nsb + s) * 16, row + 144 * s, 16);
+                }
+            }
+            ptr(&M.a, oq);
+            ptr(&M.b, oh);
+        } else {  // Q6_K
+            size_t ol = L.reserve((size_t)N * nb * 16), oh = L.reserve((size_t)N * nb * 8);
+            size_t os = L.reserve((size_t)N * nb * 2), od = L.reserve((size_t)N * nsb * 2);
+            if (pass == 1) {
+                uint8_t *hl = L.host.data() + ol, *hh = L.host.data() + oh, *hs = L.host.data() + os,
+                        *hd = L.host.data() + od;
+#pragma omp parallel for schedule(static)
+                for (long r = 0; r < N; ++r) {
+                    const uint8_t *row = t->data + (size_t)r * rb;
+                    uint8_t q[32];
+                    for (int j = 0; j < nb; ++j) {
+                        q6k_block_values(row, j, q);
+                        const size_t bi = (size_t)r * nb + host_block_pos(j, nb, G);
+                        for (int k = 0; k < 16; ++k) hl[bi * 16 + k] = (uint8_t)((q[k] & 0xf) | ((q[k + 16] & 0xf) << 4));
+                        uint32_t A = 0, B = 0;
+                        for (int k = 0; k < 16; ++k) {
+                            const int i = k / 4, bb = k % 4;
+                            A |= (uint32_t)(q[k] >> 4) << (8 * bb + 2 * i);
+                            B |= (uint32_t)(q[k + 16] >> 4) << (8 * bb + 2 * i);
+                        }
+                        memcpy(hh + bi * 8, &A, 4);
+                        memcpy(hh + bi * 8 + 4, &B, 4);
+                        const uint8_t *sc = row + (j / 8) * 210 + 192;
+                        hs[bi * 2] = sc[2 * (j % 8)];
+                        hs[bi * 2 + 1] = sc[2 * (j % 8) + 1];
+                    }
+                    for (int s = 0; s < nsb; ++s) memcpy(hd + ((size_t)r * nsb + s) * 2, row + 210 * s + 208, 2);
+                }
+            }
+            ptr(&M.a, ol);
+            ptr(&M.b, oh);
+            ptr(&M.c, os);
+            ptr(&M.e, od);
+        }
+        if (bias) TRY(dense(name + ".bias", N, &M.bias));
+        return MGB_OK;
+    }
+};
+
+uint32_t next_pow2(uint32_t n) {
+    uint32_t p = 1;
+    while (p < n) p <<= 1;
+    return p;
+}
+
+}  // namespace
+
+// bucket(n, min, max) = max(min(next_pow2(max(n, min)), max), n) (graph.rs:138-140)
+static int bucket(int n, int mn, int mx) {
+    int v = (int)next_pow2((uint32_t)std::max(n, mn));
+    return std::max(std::min(v, mx), n);
+}
+
+static mgb_status load_model(mgb_ctx *c, const char *path) {
+    GgufFile f;
+    TRY(parse_gguf(path, f));
+    auto u = [&](const char *k, int &dst, bool required = true) -> mgb_status {
+        auto it = f.u32.find(k);
+        if (it == f.u32.end()) {
+            if (required) return set_err(MGB_ERR_IO, "missing GGUF metadata key '%s'", k);
+            return MGB_OK;
+        }
+        dst = (int)it->second;
+        return MGB_OK;
+    };
+    Config &g = c->cfg;
+    TRY(u("nllb.vocab_size", g.V));
+    TRY(u("nllb.embedding_length", g.d));
+    TRY(u("nllb.encoder.block_count", g.enc_layers));
+    TRY(u("nllb.decoder.block_count", g.dec_layers));
+    TRY(u("nllb.encoder.attention.head_count", g.enc_heads));
+    TRY(u("nllb.decoder.attention.head_count", g.dec_heads));
+    TRY(u("nllb.encoder.feed_forward_length", g.enc_ffn));
+    TRY(u("nllb.decoder.feed_forward_length", g.dec_ffn));
+    TRY(u("nllb.context_length", g.max_pos));
+    TRY(u("nllb.scale_embedding", g.scale_embedding));
+    TRY(u("nllb.max_length", g.max_length));
+    TRY(u("tokenizer.ggml.padding_token_id", g.pad));
+    TRY(u("tokenizer.ggml.eos_token_id", g.eos));
+    TRY(u("tokenizer.ggml.decoder_start_token_id", g.start));
+    TRY(u("tokenizer.ggml.bos_token_id", g.bos, false));
+    if (g.d % 32 || g.d % g.dec_heads || g.d % g.enc_heads || g.d > 8192)
+        return set_err(MGB_ERR_UNSUPPORTED, "d_model %d with %d/%d heads", g.d, g.enc_heads, g.dec_heads);
+
+    Loader L{c, &f};
+    const int d = g.d;
+    c->enc.resize(g.enc_layers);
+    c->dec.resize(g.dec_layers);
+    for (int pass = 0; pass < 2; ++pass) {
+        if (pass == 1) L.host.assign(L.cursor + 256, 0);
+        L.cursor = 0;
+        Planner P{L, pass};
+        TRY(P.matrix("token_embd", c->embed, g.V, d, false));
+        char nm[128];
+        for (int i = 0; i < g.enc_layers; ++i) {
+            EncLayer &l = c->enc[i];
+            auto n = [&](const char *s) { snprintf(nm, sizeof nm, "enc.blk.%d.%s", i, s); return std::string(nm); };
+            TRY(P.norm(n("attn_norm"), d, l.attn_norm));
+            TRY(P.norm(n("ffn_norm"), d, l.ffn_norm));
+            TRY(P.matrix(n("attn_qkv"), l.qkv, 3 * d, d, true));
+            TRY(P.matrix(n("attn_out"), l.out, d, d, true));
+            TRY(P.matrix(n("ffn_up"), l.up, g.enc_ffn, d, true));
+            TRY(P.matrix(n("ffn_down"), l.down, d, g.enc_ffn, true));
+        }
+        for (int i = 0; i < g.dec_layers; ++i) {
+            DecLayer &l = c->dec[i];
+            auto n = [&](const char *s) { snprintf(nm, sizeof nm, "dec.blk.%d.%s", i, s); return std::string(nm); };
+            TRY(P.norm(n("attn_norm"), d, l.attn_norm));
+            TRY(P.norm(n("cross_attn_norm"), d, l.cross_norm));
+            TRY(P.norm(n("ffn_norm"), d, l.ffn_norm));
+            TRY(P.matrix(n("attn_qkv"), l.qkv, 3 * d, d, true));
+            TRY(P.matrix(n("attn_out"), l.out, d, d, true));
+            TRY(P.matrix(n("cross_attn_q"), l.cq, d, d, true));
+            TRY(P.matrix(n("cross_attn_kv"), l.ckv, 2 * d, d, true));
+            TRY(P.matrix(n("cross_attn_out"), l.co, d, d, true));
+            TRY(P.matrix(n("ffn_up"), l.up, g.dec_ffn, d, true));
+            TRY(P.matrix(n("ffn_down"), l.down, d, g.dec_ffn, true));
+        }
+        TRY(P.norm("enc.output_norm", d, c->enc_norm));
+        TRY(P.norm("dec.output_norm", d, c->dec_norm));
+        // Sinusoidal position table [max_pos + pad + 1, d] (model.rs:325-340, 361-366).
+        const int n_pos = g.max_pos + g.pad + 1;
+        size_t off = L.reserve((size_t)n_pos * d * 4);
+        if (pass == 1) {
+            float *tab = reinterpret_cast<float *>(L.host.data() + off);
+            const int half = d / 2;
+            const double st = std::log(10000.0) / ((double)half - 1.0);
+            for (int p = 0; p < n_pos; ++p)
+                for (int i = 0; i < half; ++i) {
+                    if (p == g.pad) continue;
+                    const double a = (double)p * std::exp(-(double)i * st);
+                    tab[(size_t)p * d + i] = (float)std::sin(a);
+                    tab[(size_t)p * d + half + i] = (float)std::cos(a);
+                }
+        }
+        P.ptr(reinterpret_cast<const uint8_t **>(const_cast<const float **>(&c->pos)), off);
+        if (pass == 1) {
+            void *arena = nullptr;
+            TRY(c->dalloc(&arena, L.cursor));
+            c->arena = (uint8_t *)arena;
+            c->arena_bytes = L.cursor;
+            CK(cudaMemcpy(c->arena, L.host.data(), L.cursor, cudaMemcpyHostToDevice));
+            for (auto &fx : P.fix) *fx.first = c->arena + fx.second;
+        }
+    }
+    c->embed_scale = g.scale_embedding ? (float)std::sqrt((double)d) : 1.0f;
+    c->weight_bytes = c->arena_bytes;
+    size_t step = c->embed.bytes;
+    for (auto &l : c->dec) step += l.qkv.bytes + l.out.bytes + l.cq.bytes + l.co.bytes + l.up.bytes + l.down.bytes;
+    c->step_bytes = step;
+    return MGB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Kernel launchers
+
+static int gemv_grid(int N) { return std::max(1, std::min((N + 7) / 8, 148 * 16)); }
+
+template <int TYPE>
+static void launch_gemv_t(int epi, const GemvArgs &g, int grid, cudaStream_t s) {
+    switch (epi) {
+        case EPI_STORE: gemv_kernel<TYPE, EPI_STORE><<<grid, 256, 0, s>>>(g); break;
+        case EPI_RELU: gemv_kernel<TYPE, EPI_RELU><<<grid, 256, 0, s>>>(g); break;
+        case EPI_RESID: gemv_kernel<TYPE, EPI_RESID><<<grid, 256, 0, s>>>(g); break;
+        case EPI_QKV: gemv_kernel<TYPE, EPI_QKV><<<grid, 256, 0, s>>>(g); break;
+        case EPI_CROSSKV: gemv_kernel<TYPE, EPI_CROSSKV><<<grid, 256, 0, s>>>(g); break;
+        case EPI_ARGMAX: gemv_kernel<TYPE, EPI_ARGMAX><<<grid, 256, 0, s>>>(g); break;
+    }
+}
+
+static mgb_status gemv(mgb_ctx *c, int epi, GemvArgs g, int grid = 0) {
+    if (!grid) grid = gemv_grid(g.W.N);
+    return launch_check(c, [&] {
+        switch (g.W.type) {
+            case T_F32: launch_gemv_t<T_F32>(epi, g, grid, c->stream); break;
+            case T_Q8_0: launch_gemv_t<T_Q8_0>(epi, g, grid, c->stream); break;
+            case T_Q4_K: launch_gemv_t<T_Q4_K>(epi, g, grid, c->stream); break;
+            case T_Q6_K: launch_gemv_t<T_Q6_K>(epi, g, grid, c->stream); break;
+        }
+    });
+}
+
+static mgb_status qprep(mgb_ctx *c, int mode, PrepArgs p) {
+    const int grid = (p.rows + 7) / 8;
+    return launch_check(c, [&] {
+        switch (mode) {
+            case PREP_PLAIN: qprep_kernel<PREP_PLAIN><<<grid, 256, 0, c->stream>>>(p); break;
+            case PREP_LN: qprep_kernel<PREP_LN><<<grid, 256, 0, c->stream>>>(p); break;
+            case PREP_EMBED_LN: qprep_kernel<PREP_EMBED_LN><<<grid, 256, 0, c->stream>>>(p); break;
+        }
+    });
+}
+
+template <typename KV>
+static mgb_status attend(mgb_ctx *c, AttnArgs a) {
+    const long tasks = (long)a.rows * a.H * a.queries;
+    const int grid = (int)((tasks + 3) / 4);
+    const size_t sh = (size_t)4 * a.max_keys * sizeof(float);
+    return launch_check(c, [&] { attend_kernel<KV><<<grid, 128, sh, c->stream>>>(a); });
+}
+
+static PrepArgs prep_args(const QAct &act, float *xf, bool keep_f32, const float *x, int rows, int K) {
+    PrepArgs p{};
+    p.x = x;
+    p.rows = rows;
+    p.K = K;
+    p.out = act;
+    p.out.rows = rows;
+    p.out.K = K;
+    p.keep_f32 = keep_f32;
+    p.xf = xf;
+    return p;
+}
+
+static GemvArgs gemv_args(const Matrix &W, const QAct &act, const float *xf, int rows) {
+    GemvArgs g{};
+    g.W = W;
+    g.x = act;
+    g.x.rows = rows;
+    g.x.K = W.K;
+    g.xf = xf;
+    g.rows = rows;
+    return g;
+}
+
+static bool any_f32(const mgb_ctx *c) {
+    if (c->embed.type == T_F32) return true;
+    for (auto &l : c->dec)
+        if (l.qkv.type == T_F32 || l.out.type == T_F32 || l.cq.type == T_F32 || l.ckv.type == T_F32 ||
+            l.co.type == T_F32 || l.up.type == T_F32 || l.down.type == T_F32)
+            return true;
+    for (auto &l : c->enc)
+        if (l.qkv.type == T_F32 || l.out.type == T_F32 || l.up.type == T_F32 || l.down.type == T_F32) return true;
+    return false;
+}
+
+// ---------------------------------------------------------------------------
+// Static state (graph.rs:23-135)
+
+static void free_state(StaticState *st) {
+    if (st->exec) cudaGraphExecDestroy(st->exec);
+    for (void *p : st->allocs) cudaFree(p);
+    st->allocs.clear();
+}
+
+static mgb_status new_state(mgb_ctx *c, int b, int s, int m, StaticState **out) {
+    auto st = std::make_unique<StaticState>();
+    st->b = b;
+    st->s = s;
+    st->m = m;
+    const Config &g = c->cfg;
+    const int d = g.d, H = g.dec_heads, hd = d / H, kmax = std::max(d, g.dec_ffn);
+    auto A = [&](void **p, size_t n) -> mgb_status {
+        TRY(c->dalloc(p, n));
+        st->allocs.push_back(*p);
+        st->bytes += n;
+        return MGB_OK;
+    };
+    TRY(A((void **)&st->ids, 4 * b));
+    TRY(A((void **)&st->step, 4));
+    TRY(A((void **)&st->out, (size_t)4 * b * m));
+    TRY(A((void **)&st->lens, 4 * b));
+    TRY(A((void **)&st->finished, b));
+    TRY(A((void **)&st->x, (size_t)4 * b * d));
+    TRY(A((void **)&st->q, (size_t)4 * b * d));
+    TRY(A((void **)&st->a, (size_t)4 * b * d));
+    TRY(A((void **)&st->u, (size_t)4 * b * g.dec_ffn));
+    if (any_f32(c)) TRY(A((void **)&st->xf, (size_t)4 * b * kmax));
+    TRY(A((void **)&st->act.q, (size_t)b * kmax));
+    TRY(A((void **)&st->act.d, (size_t)4 * b * kmax / 32));
+    TRY(A((void **)&st->act.s32, (size_t)4 * b * kmax / 32));
+    TRY(A((void **)&st->act.s16, (size_t)4 * b * kmax / 16));
+    st->kc.resize(g.dec_layers);
+    st->vc.resize(g.dec_layers);
+    st->ck.resize(g.dec_layers);
+    st->cv.resize(g.dec_layers);
+    for (int l = 0; l < g.dec_layers; ++l) {
+        TRY(A((void **)&st->kc[l], (size_t)2 * b * H * m * hd));
+        TRY(A((void **)&st->vc[l], (size_t)2 * b * H * m * hd));
+        TRY(A((void **)&st->ck[l], (size_t)2 * b * H * s * hd));
+        TRY(A((void **)&st->cv[l], (size_t)2 * b * H * s * hd));
+        CK(cudaMemsetAsync(st->kc[l], 0, (size_t)2 * b * H * m * hd, c->stream));
+        CK(cudaMemsetAsync(st->vc[l], 0, (size_t)2 * b * H * m * hd, c->stream));
+        CK(cudaMemsetAsync(st->ck[l], 0, (size_t)2 * b * H * s * hd, c->stream));
+        CK(cudaMemsetAsync(st->cv[l], 0, (size_t)2 * b * H * s * hd, c->stream));
+    }
+    TRY(A((void **)&st->part_v, (size_t)4 * b * kLmParts));
+    TRY(A((void **)&st->part_i, (size_t)4 * b * kLmParts));
+    *out = st.release();
+    return MGB_OK;
+}
+
+// One greedy decoder step on the state's fixed buffers (model.rs:552-612).
+static mgb_status launch_step(mgb_ctx *c, StaticState *st, float *logits, int force,
+                              cudaEvent_t lm0 = nullptr, cudaEvent_t lm1 = nullptr) {
+    const Config &g = c->cfg;
+    const int b = st->b, d = g.d, H = g.dec_heads, hd = d / H;
+    const bool f32 = st->xf != nullptr;
+    for (int l = 0; l < g.dec_layers; ++l) {
+        const DecLayer &L = c->dec[l];
+        // attn_norm(x) -> fused QKV -> q, K/V cache slot *step
+        PrepArgs p = prep_args(st->act, st->xf, f32, st->x, b, d);
+        p.gamma = L.attn_norm.g;
+        p.beta = L.attn_norm.b;
+        if (l == 0) {
+            p.x_out = st->x;
+            p.embed = c->embed;
+            p.ids = st->ids;
+            p.step = st->step;
+            p.pos_table = c->pos;
+            p.pos_base = (uint32_t)g.pad + 1;
+            p.scale = c->embed_scale;
+            TRY(qprep(c, PREP_EMBED_LN, p));
+        } else {
+            TRY(qprep(c, PREP_LN, p));
+        }
+        GemvArgs gq = gemv_args(L.qkv, st->act, st->xf, b);
+        gq.q = st->q;
+        gq.kc = st->kc[l];
+        gq.vc = st->vc[l];
+        gq.step = st->step;
+        gq.H = H;
+        gq.hd = hd;
+        gq.m = st->m;
+        TRY(gemv(c, EPI_QKV, gq));
+        AttnArgs sa{};
+        sa.q = st->q;
+        sa.q_row = d;
+        sa.K = st->kc[l];
+        sa.V = st->vc[l];
+        sa.kv_row = hd;
+        sa.kv_head = (long)st->m * hd;
+        sa.kv_batch = (long)H * st->m * hd;
+        sa.step = st->step;
+        sa.out = st->a;
+        sa.out_row = d;
+        sa.H = H;
+        sa.hd = hd;
+        sa.rows = b;
+        sa.queries = 1;
+        sa.max_keys = st->m;
+        TRY(attend<__half>(c, sa));
+        TRY(qprep(c, PREP_PLAIN, prep_args(st->act, st->xf, f32, st->a, b, d)));
+        GemvArgs go = gemv_args(L.out, st->act, st->xf, b);
+        go.y = st->x;
+        TRY(gemv(c, EPI_RESID, go));
+        // cross_norm -> cross_q -> cross attention -> cross_out + residual
+        p = prep_args(st->act, st->xf, f32, st->x, b, d);
+        p.gamma = L.cross_norm.g;
+        p.beta = L.cross_norm.b;
+        TRY(qprep(c, PREP_LN, p));
+        GemvArgs gc = gemv_args(L.cq, st->act, st->xf, b);
+        gc.y = st->q;
+        TRY(gemv(c, EPI_STORE, gc));
+        AttnArgs ca = sa;
+        ca.K = st->ck[l];
+        ca.V = st->cv[l];
+        ca.kv_head = (long)st->s * hd;
+        ca.kv_batch = (long)H * st->s * hd;
+        ca.step = nullptr;
+        ca.lens = st->lens;
+        ca.max_keys = st->s;
+        TRY(attend<__half>(c, ca));
+        TRY(qprep(c, PREP_PLAIN, prep_args(st->act, st->xf, f32, st->a, b, d)));
+        GemvArgs gco = gemv_args(L.co, st->act, st->xf, b);
+        gco.y = st->x;
+        TRY(gemv(c, EPI_RESID, gco));
+        // ffn_norm -> up + ReLU -> down + residual
+        p = prep_args(st->act, st->xf, f32, st->x, b, d);
+        p.gamma = L.ffn_norm.g;
+        p.beta = L.ffn_norm.b;
+        TRY(qprep(c, PREP_LN, p));
+        GemvArgs gu = gemv_args(L.up, st->act, st->xf, b);
+        gu.y = st->u;
+        TRY(gemv(c, EPI_RELU, gu));
+        TRY(qprep(c, PREP_PLAIN, prep_args(st->act, st->xf, f32, st->u, b, g.dec_ffn)));
+        GemvArgs gd = gemv_args(L.down, st->act, st->xf, b);
+        gd.y = st->x;
+        TRY(gemv(c, EPI_RESID, gd));
+    }
+    // dec_norm -> tied LM head fused with the first argmax pass -> greedy bookkeeping
+    PrepArgs p = prep_args(st->act, st->xf, f32, st->x, b, d);
+    p.gamma = c->dec_norm.g;
+    p.beta = c->dec_norm.b;
+    TRY(qprep(c, PREP_LN, p));
+    GemvArgs gl = gemv_args(c->embed, st->act, st->xf, b);
+    gl.part_v = st->part_v;
+    gl.part_i = st->part_i;
+    gl.logits = logits;
+    if (lm0) CK(cudaEventRecord(lm0, c->stream));
+    TRY(gemv(c, EPI_ARGMAX, gl, kLmParts));
+    if (lm1) CK(cudaEventRecord(lm1, c->stream));
+    const int threads = std::min(1024, std::max(32, 32 * b));
+    return launch_check(c, [&] {
+        greedy_finalize_kernel<<<1, threads, 0, c->stream>>>(st->part_v, st->part_i, kLmParts, b, st->finished,
+                                                             st->ids, st->out, st->m, st->step, (uint32_t)g.eos,
+                                                             (uint32_t)g.pad, force);
+    });
+}
+
+// ---------------------------------------------------------------------------
+// Encoder (model.rs:463-500)
+
+static mgb_status encode(mgb_ctx *c, const uint32_t *ids, const uint32_t *lens, int b, int S, mgb_batch **out) {
+    const Config &g = c->cfg;
+    const int d = g.d, H = g.enc_heads, hd = d / H, rows = b * S, ffn = g.enc_ffn, kmax = std::max(d, ffn);
+    std::vector<void *> tmp;
+    auto A = [&](void **p, size_t n) -> mgb_status {
+        TRY(c->dalloc(p, n));
+        tmp.push_back(*p);
+        return MGB_OK;
+    };
+    struct Guard {
+        std::vector<void *> &v;
+        ~Guard() {
+            for (void *p : v) cudaFree(p);
+        }
+    } guard{tmp};
+    uint32_t *d_ids, *d_lens;
+    float *x, *qkv, *a, *u, *xf = nullptr;
+    QAct act;
+    TRY(A((void **)&d_ids, (size_t)4 * rows));
+    TRY(A((void **)&d_lens, (size_t)4 * b));
+    TRY(A((void **)&x, (size_t)4 * rows * d));
+    TRY(A((void **)&qkv, (size_t)4 * rows * 3 * d));
+    TRY(A((void **)&a, (size_t)4 * rows * d));
+    TRY(A((void **)&u, (size_t)4 * rows * ffn));
+    const bool f32 = any_f32(c);
+    if (f32) TRY(A((void **)&xf, (size_t)4 * rows * kmax));
+    TRY(A((void **)&act.q, (size_t)rows * kmax));
+    TRY(A((void **)&act.d, (size_t)4 * rows * kmax / 32));
+    TRY(A((void **)&act.s32, (size_t)4 * rows * kmax / 32));
+    TRY(A((void **)&act.s16, (size_t)4 * rows * kmax / 16));
+    CK(cudaMemcpyAsync(d_ids, ids, (size_t)4 * rows, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(d_lens, lens, (size_t)4 * b, cudaMemcpyHostToDevice, c->stream));
+    TRY(launch_check(c, [&] {
+        embed_tokens_kernel<<<(rows + 7) / 8, 256, 0, c->stream>>>(c->embed, d_ids, d_lens, S, rows, c->pos,
+                                                                   (uint32_t)g.pad, c->embed_scale, x);
+    }));
+    for (int l = 0; l < g.enc_layers; ++l) {
+        const EncLayer &L = c->enc[l];
+        PrepArgs p = prep_args(act, xf, f32, x, rows, d);
+        p.gamma = L.attn_norm.g;
+        p.beta = L.attn_norm.b;
+        TRY(qprep(c, PREP_LN, p));
+        GemvArgs gq = gemv_args(L.qkv, act, xf, rows);
+        gq.y = qkv;
+        TRY(gemv(c, EPI_STORE, gq));
+        AttnArgs at{};
+        at.q = qkv;
+        at.q_row = 3 * d;
+        at.K = qkv + d;
+        at.V = qkv + 2 * d;
+        at.kv_row = 3 * d;
+        at.kv_head = hd;
+        at.kv_batch = (long)S * 3 * d;
+        at.lens = d_lens;
+        at.out = a;
+        at.out_row = d;
+        at.H = H;
+        at.hd = hd;
+        at.rows = b;
+        at.queries = S;
+        at.max_keys = S;
+        TRY(attend<float>(c, at));
+        TRY(qprep(c, PREP_PLAIN, prep_args(act, xf, f32, a, rows, d)));
+        GemvArgs go = gemv_args(L.out, act, xf, rows);
+        go.y = x;
+        TRY(gemv(c, EPI_RESID, go));
+        p = prep_args(act, xf, f32, x, rows, d);
+        p.gamma = L.ffn_norm.g;
+        p.beta = L.ffn_norm.b;
+        TRY(qprep(c, PREP_LN, p));
+        GemvArgs gu = gemv_args(L.up, act, xf, rows);
+        gu.y = u;
+        TRY(gemv(c, EPI_RELU, gu));
+        TRY(qprep(c, PREP_PLAIN, prep_args(act, xf, f32, u, rows, ffn)));
+        GemvArgs gd = gemv_args(L.down, act, xf, rows);
+        gd.y = x;
+        TRY(gemv(c, EPI_RESID, gd));
+    }
+    PrepArgs p = prep_args(act, xf, f32, x, rows, d);
+    p.gamma = c->enc_norm.g;
+    p.beta = c->enc_norm.b;
+    TRY(qprep(c, PREP_LN, p));
+    auto B = std::make_unique<mgb_batch>();
+    B->b = b;
+    B->s = S;
+    B->owner = c;
+    B->lens.assign(lens, lens + b);
+    const int Hd = g.dec_heads, hdd = d / Hd;
+    const size_t per = (size_t)b * Hd * S * hdd;
+    B->cross_bytes = per * 2 * 2 * g.dec_layers;
+    TRY(c->dalloc((void **)&B->cross, B->cross_bytes));
+    void *dl = nullptr;
+    mgb_status s = c->dalloc(&dl, (size_t)4 * b);
+    if (s != MGB_OK) {
+        cudaFree(B->cross);
+        return s;
+    }
+    B->d_lens = (uint32_t *)dl;
+    CK(cudaMemcpyAsync(B->d_lens, lens, (size_t)4 * b, cudaMemcpyHostToDevice, c->stream));
+    for (int l = 0; l < g.dec_layers; ++l) {
+        GemvArgs gk = gemv_args(c->dec[l].ckv, act, xf, rows);
+        gk.kc = B->cross + per * (2 * l);
+        gk.vc = B->cross + per * (2 * l + 1);
+        gk.H = Hd;
+        gk.hd = hdd;
+        gk.S = S;
+        mgb_status s2 = gemv(c, EPI_CROSSKV, gk);
+        if (s2 != MGB_OK) {
+            cudaFree(B->cross);
+            cudaFree(B->d_lens);
+            return s2;
+        }
+    }
+    CK(cudaStreamSynchronize(c->stream));
+    *out = B.release();
+    return MGB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Greedy decoding with the graph cache (graph.rs:204-298)
+
+static void evict(mgb_ctx *c, StaticState *keep) {
+    bool dropped_graph = false;
+    for (;;) {
+        size_t total = kGraphBytes;
+        for (auto &e : c->cache) total += e->bytes + (e->exec ? kGraphBytes : 0);
+        if (total <= c->opts.graph_cache_bytes || c->cache.size() <= 1) break;
+        int victim = -1;
+        for (size_t i = 0; i < c->cache.size(); ++i)
+            if (c->cache[i].get() != keep && (victim < 0 || c->cache[i]->last_used < c->cache[victim]->last_used))
+                victim = (int)i;
+        if (victim < 0) break;
+        dropped_graph |= c->cache[victim]->exec != nullptr;
+        free_state(c->cache[victim].get());
+        c->cache.erase(c->cache.begin() + victim);
+    }
+    if (dropped_graph) cudaDeviceGraphMemTrim(c->device);
+}
+
+static void clear_cache(mgb_ctx *c) {
+    cudaStreamSynchronize(c->stream);
+    for (auto &e : c->cache) free_state(e.get());
+    c->cache.clear();
+    cudaDeviceGraphMemTrim(c->device);
+}
+
+static mgb_status set_ids(mgb_ctx *c, StaticState *st, uint32_t id) {
+    std::vector<uint32_t> v(st->b, id);
+    CK(cudaMemcpyAsync(st->ids, v.data(), 4 * st->b, cudaMemcpyHostToDevice, c->stream));
+    return cudaStreamSynchronize(c->stream) == cudaSuccess ? MGB_OK : cuda_err(cudaGetLastError(), "set_ids");
+}
+
+static mgb_status reset_finished(mgb_ctx *c, StaticState *st, int active) {
+    std::vector<uint8_t> f(st->b);
+    for (int i = 0; i < st->b; ++i) f[i] = i >= active;
+    CK(cudaMemcpyAsync(st->finished, f.data(), st->b, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    return MGB_OK;
+}
+
+// Finds or creates the static state of the (rows, source, output) bucket and
+// loads the batch into it (graph.rs:236-268).
+static mgb_status acquire_state(mgb_ctx *c, const mgb_batch *B, int max_new, bool pad_rows, StaticState **out) {
+    const Config &g = c->cfg;
+    const int n = B->b, H = g.dec_heads, hd = g.d / H;
+    const int b = pad_rows ? (int)next_pow2((uint32_t)n) : n;
+    if (b > 64) return set_err(MGB_ERR_INVALID, "batch of %d rows exceeds 64", n);
+    const int s = bucket(B->s, 16, g.max_pos), m = bucket(max_new + 2, 32, g.max_pos);
+    StaticState *st = nullptr;
+    for (auto &e : c->cache)
+        if (e->b == b && e->s == s && e->m == m) st = e.get();
+    if (!st) {
+        TRY(new_state(c, b, s, m, &st));
+        c->cache.emplace_back(st);
+        evict(c, st);
+    }
+    st->last_used = ++c->clock;
+    // reset (graph.rs:91-113): cross K/V, lens, start token, step, finished
+    const size_t per = (size_t)n * H * B->s * hd;
+    for (int l = 0; l < g.dec_layers; ++l) {
+        CK(cudaMemcpy2DAsync(st->ck[l], (size_t)s * hd * 2, B->cross + per * 2 * l, (size_t)B->s * hd * 2,
+                             (size_t)B->s * hd * 2, (size_t)n * H, cudaMemcpyDeviceToDevice, c->stream));
+        CK(cudaMemcpy2DAsync(st->cv[l], (size_t)s * hd * 2, B->cross + per * (2 * l + 1), (size_t)B->s * hd * 2,
+                             (size_t)B->s * hd * 2, (size_t)n * H, cudaMemcpyDeviceToDevice, c->stream));
+    }
+    std::vector<uint32_t> lens(b, 1);
+    for (int i = 0; i < n; ++i) lens[i] = B->lens[i];
+    CK(cudaMemcpyAsync(st->lens, lens.data(), 4 * b, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemsetAsync(st->step, 0, 4, c->stream));
+    TRY(set_ids(c, st, (uint32_t)g.start));
+    TRY(reset_finished(c, st, n));
+    *out = st;
+    return MGB_OK;
+}
+
+static mgb_status run_greedy(mgb_ctx *c, const mgb_batch *B, uint32_t tgt, int max_new, int sync_every, int force,
+                             uint32_t *out_ids, uint32_t *out_lens, float *logits_host) {
+    const Config &g = c->cfg;
+    const int n = B->b;
+    const bool capture = c->capture && c->opts.use_graphs && !logits_host;
+    StaticState *st = nullptr;
+    TRY(acquire_state(c, B, max_new, capture, &st));
+    const int b = st->b, m = st->m;
+    float *d_logits = nullptr;
+    if (logits_host) {
+        if (!st->logits) {
+            void *p;
+            TRY(c->dalloc(&p, (size_t)4 * b * g.V));
+            st->logits = (float *)p;
+            st->allocs.push_back(p);
+        }
+        d_logits = st->logits;
+    }
+    // Step 0 consumes decoder_start; its output is replaced by the forced language token.
+    TRY(launch_step(c, st, nullptr, force));
+    TRY(set_ids(c, st, tgt));
+    TRY(reset_finished(c, st, n));
+    TRY(launch_step(c, st, d_logits, force));
+    if (logits_host) {
+        CK(cudaMemcpyAsync(logits_host, d_logits, (size_t)4 * n * g.V, cudaMemcpyDeviceToHost, c->stream));
+    }
+    int steps = 2;
+    const int max_steps = std::min(max_new + 1, m);
+    if (capture && !st->exec && steps < max_steps) {
+        cudaGraph_t graph = nullptr;
+        CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+        mgb_status cs = launch_step(c, st, nullptr, force);
+        cudaError_t ee = cudaStreamEndCapture(c->stream, &graph);
+        if (cs != MGB_OK) {
+            if (graph) cudaGraphDestroy(graph);
+            return cs;
+        }
+        if (ee != cudaSuccess) return cuda_err(ee, "cudaStreamEndCapture");
+        cudaError_t ie = cudaGraphInstantiate(&st->exec, graph, 0);
+        size_t nodes = 0;
+        cudaGraphGetNodes(graph, nullptr, &nodes);
+        cudaGraphDestroy(graph);
+        if (ie != cudaSuccess) {
+            st->exec = nullptr;
+            return cuda_err(ie, "cudaGraphInstantiate");
+        }
+        st->graph_nodes = nodes;
+        c->launches -= nodes;  // captured launches did not run
+        CK(cudaGraphUpload(st->exec, c->stream));
+    }
+    while (steps < max_steps) {
+        if (!force && steps % sync_every == 0) {
+            std::vector<uint8_t> fin(st->b);
+            CK(cudaMemcpyAsync(fin.data(), st->finished, st->b, cudaMemcpyDeviceToHost, c->stream));
+            CK(cudaStreamSynchronize(c->stream));
+            if (std::all_of(fin.begin(), fin.end(), [](uint8_t v) { return v != 0; })) break;
+        }
+        if (st->exec) {
+            CK(cudaGraphLaunch(st->exec, c->stream));
+            c->launches += st->graph_nodes;
+        } else {
+            TRY(launch_step(c, st, d_logits, force));
+            if (logits_host)
+                CK(cudaMemcpyAsync(logits_host + (size_t)(steps - 1) * n * g.V, d_logits, (size_t)4 * n * g.V,
+                                   cudaMemcpyDeviceToHost, c->stream));
+        }
+        ++steps;
+    }
+    std::vector<uint32_t> out((size_t)st->b * st->m);
+    CK(cudaMemcpyAsync(out.data(), st->out, 4 * out.size(), cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    for (int r = 0; r < n; ++r) {
+        uint32_t len = 0;
+        bool seen = false;
+        for (int t = 0; t < max_new; ++t) {
+            const uint32_t tok = t < steps - 1 ? out[(size_t)r * st->m + 1 + t] : (uint32_t)g.pad;
+            out_ids[(size_t)r * max_new + t] = tok;
+            if (!seen && t < steps - 1 && tok != (uint32_t)g.eos) ++len;
+            else seen = true;
+        }
+        if (out_lens) out_lens[r] = len;
+    }
+    return MGB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// C ABI
+
+extern "C" {
+
+void mgb_default_options(mgb_options *o) {
+    o->use_graphs = 1;
+    o->graph_cache_bytes = (uint64_t)512 << 20;
+    o->fail_alloc_after = -1;
+}
+
+const char *mgb_last_error(void) { return g_err.c_str(); }
+
+mgb_status mgb_open(const char *path, int device, const mgb_options *opts, mgb_ctx **out) {
+    if (!path || !out) return set_err(MGB_ERR_INVALID, "null argument");
+    *out = nullptr;
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess || n == 0) return set_err(MGB_ERR_CUDA, "no CUDA device available (%s)", cudaGetErrorString(e));
+    if (device < 0 || device >= n) return set_err(MGB_ERR_INVALID, "device %d out of range (%d devices)", device, n);
+    CK(cudaSetDevice(device));
+    auto c = std::make_unique<mgb_ctx>();
+    c->device = device;
+    if (opts) c->opts = *opts;
+    else mgb_default_options(&c->opts);
+    CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+    mgb_status s = load_model(c.get(), path);
+    if (s != MGB_OK) {
+        if (c->arena) cudaFree(c->arena);
+        cudaStreamDestroy(c->stream);
+        return s;
+    }
+    c->inject_armed = true;
+    *out = c.release();
+    return MGB_OK;
+}
+
+void mgb_close(mgb_ctx *c) {
+    if (!c) return;
+    cudaSetDevice(c->device);
+    clear_cache(c);
+    if (c->arena) cudaFree(c->arena);
+    cudaStreamDestroy(c->stream);
+    delete c;
+}
+
+mgb_status mgb_model_info_get(const mgb_ctx *c, mgb_model_info *o) {
+    if (!c || !o) return set_err(MGB_ERR_INVALID, "null argument");
+    const Config &g = c->cfg;
+    o->vocab_size = g.V;
+    o->d_model = g.d;
+    o->encoder_layers = g.enc_layers;
+    o->decoder_layers = g.dec_layers;
+    o->encoder_heads = g.enc_heads;
+    o->decoder_heads = g.dec_heads;
+    o->encoder_ffn = g.enc_ffn;
+    o->decoder_ffn = g.dec_ffn;
+    o->max_position_embeddings = g.max_pos;
+    o->max_length = g.max_length;
+    o->pad_token_id = g.pad;
+    o->eos_token_id = g.eos;
+    o->decoder_start_token_id = g.start;
+    o->bos_token_id = g.bos;
+    o->scale_embedding = g.scale_embedding;
+    o->weight_bytes = c->weight_bytes;
+    o->decoder_step_bytes = c->step_bytes;
+    o->lm_head_bytes = c->embed.bytes;
+    return MGB_OK;
+}
+
+mgb_status mgb_encode(mgb_ctx *c, const uint32_t *ids, const uint32_t *lens, uint32_t b, uint32_t s, mgb_batch **out) {
+    if (!c || !ids || !lens || !out) return set_err(MGB_ERR_INVALID, "null argument");
+    *out = nullptr;
+    if (b == 0 || s == 0) return set_err(MGB_ERR_INVALID, "empty batch");
+    if ((int)s > c->cfg.max_pos - 2) return set_err(MGB_ERR_INVALID, "source length %u > %d", s, c->cfg.max_pos - 2);
+    for (uint32_t i = 0; i < b; ++i) {
+        if (lens[i] < 1 || lens[i] > s) return set_err(MGB_ERR_INVALID, "lens[%u] = %u outside [1, %u]", i, lens[i], s);
+        for (uint32_t j = 0; j < lens[i]; ++j)
+            if (ids[(size_t)i * s + j] >= (uint32_t)c->cfg.V)
+                return set_err(MGB_ERR_INVALID, "token id %u >= vocab %d", ids[(size_t)i * s + j], c->cfg.V);
+    }
+    CK(cudaSetDevice(c->device));
+    return encode(c, ids, lens, (int)b, (int)s, out);
+}
+
+void mgb_batch_free(mgb_batch *B) {
+    if (!B) return;
+    if (B->owner) cudaSetDevice(B->owner->device);
+    cudaFree(B->cross);
+    cudaFree(B->d_lens);
+    delete B;
+}
+
+mgb_status mgb_batch_cross(mgb_ctx *c, const mgb_batch *B, uint32_t layer, int which, uint16_t *out) {
+    if (!c || !B || !out || layer >= (uint32_t)c->cfg.dec_layers || (which != 0 && which != 1))
+        return set_err(MGB_ERR_INVALID, "bad argument");
+    const size_t per = (size_t)B->b * c->cfg.d * B->s;
+    CK(cudaMemcpy(out, B->cross + per * (2 * layer + which), per * 2, cudaMemcpyDeviceToHost));
+    return MGB_OK;
+}
+
+static mgb_status check_greedy(mgb_ctx *c, const mgb_batch *B, uint32_t tgt, uint32_t max_new) {
+    if (!c || !B) return set_err(MGB_ERR_INVALID, "null argument");
+    if (B->owner != c) return set_err(MGB_ERR_INVALID, "batch belongs to another context");
+    if (tgt >= (uint32_t)c->cfg.V) return set_err(MGB_ERR_INVALID, "target language id %u >= vocab", tgt);
+    if (max_new < 1 || (int)max_new > c->cfg.max_pos - 2)
+        return set_err(MGB_ERR_INVALID, "max_new %u outside [1, %d]", max_new, c->cfg.max_pos - 2);
+    return MGB_OK;
+}
+
+mgb_status mgb_greedy(mgb_ctx *c, const mgb_batch *B, uint32_t tgt, uint32_t max_new, uint32_t sync_every, int force,
+                      uint32_t *out_ids, uint32_t *out_lens) {
+    TRY(check_greedy(c, B, tgt, max_new));
+    if (!out_ids) return set_err(MGB_ERR_INVALID, "null out_ids");
+    CK(cudaSetDevice(c->device));
+    mgb_status s = run_greedy(c, B, tgt, (int)max_new, std::max(1u, sync_every), force, out_ids, out_lens, nullptr);
+    if (s == MGB_OK) return s;
+    if (s == MGB_ERR_OOM && c->capture && c->opts.use_graphs) {
+        // graph.rs:214-222: drop graphs for good and retry eagerly
+        std::string why = g_err;
+        c->capture = false;
+        clear_cache(c);
+        s = run_greedy(c, B, tgt, (int)max_new, std::max(1u, sync_every), force, out_ids, out_lens, nullptr);
+        if (s != MGB_OK) g_err = why + "; retry without graphs: " + g_err;
+    }
+    return s;
+}
+
+mgb_status mgb_greedy_logits(mgb_ctx *c, const mgb_batch *B, uint32_t tgt, uint32_t max_new, int force,
+                             uint32_t *out_ids, float *logits) {
+    TRY(check_greedy(c, B, tgt, max_new));
+    if (!out_ids) return set_err(MGB_ERR_INVALID, "null out_ids");
+    CK(cudaSetDevice(c->device));
+    std::vector<float> dummy;
+    float *lg = logits;
+    if (!lg) {
+        dummy.resize((size_t)max_new * B->b * c->cfg.V);
+        lg = dummy.data();
+    }
+    return run_greedy(c, B, tgt, (int)max_new, 1 << 30, force, out_ids, nullptr, lg);
+}
+
+mgb_status mgb_clear_cache(mgb_ctx *c) {
+    if (!c) return set_err(MGB_ERR_INVALID, "null argument");
+    CK(cudaSetDevice(c->device));
+    clear_cache(c);
+    return MGB_OK;
+}
+
+void *mgb_cuda_stream(mgb_ctx *c) { return c ? (void *)c->stream : nullptr; }
+
+uint64_t mgb_kernel_launches(const mgb_ctx *c) { return c ? c->launches : 0; }
+
+mgb_status mgb_profile_step(mgb_ctx *c, const mgb_batch *B, uint32_t tgt, uint32_t iters, float *lm_head_ms,
+                            float *step_ms) {
+    TRY(check_greedy(c, B, tgt, iters + 1));
+    CK(cudaSetDevice(c->device));
+    StaticState *st = nullptr;
+    TRY(acquire_state(c, B, (int)iters + 1, true, &st));
+    TRY(set_ids(c, st, tgt));
+    cudaEvent_t ev[4];
+    for (auto &e : ev) CK(cudaEventCreate(&e));
+    double lm = 0.0, step = 0.0;
+    mgb_status s = MGB_OK;
+    for (uint32_t i = 0; i < iters && s == MGB_OK; ++i) {
+        cudaEventRecord(ev[0], c->stream);
+        s = launch_step(c, st, nullptr, 1, ev[1], ev[2]);
+        cudaEventRecord(ev[3], c->stream);
+        if (cudaEventSynchronize(ev[3]) != cudaSuccess) s = cuda_err(cudaGetLastError(), "profile");
+        float a = 0.f, b = 0.f;
+        cudaEventElapsedTime(&a, ev[1], ev[2]);
+        cudaEventElapsedTime(&b, ev[0], ev[3]);
+        lm += a;
+        step += b;
+    }
+    for (auto &e : ev) cudaEventDestroy(e);
+    if (lm_head_ms) *lm_head_ms = (float)(lm / std::max(1u, iters));
+    if (step_ms) *step_ms = (float)(step / std::max(1u, iters));
+    return s;
+}
+
+}  // extern "C"

@@ -1,0 +1,496 @@
+// Decode-step kernels of the engine (sm_100a).
+//
+// Reference kernels they replace (crates/malaga-core/kernels/malaga.cu, launched
+// by crates/malaga-core/src/kernels.rs) and candle ops (model.rs:552-612):
+//   qprep_*         embed_pos_ln (malaga.cu:110-130) + bias_residual_ln's LayerNorm
+//                   (malaga.cu:89-105) + candle's q8_1 activation quantization
+//   gemv            candle QMatMul::forward (MMVQ) + the bias/residual/ReLU/K-V
+//                   epilogues of bias_residual_ln, bias_relu (malaga.cu:133-138)
+//                   and qkv_decode (malaga.cu:142-154)
+//   attend          attn_decode (malaga.cu:165-227), also the encoder's masked
+//                   softmax attention (model.rs:101-109)
+//   lm head argmax  QMatMul::forward(token_embd) (model.rs:607) fused with
+//                   argmax_partial (malaga.cu:247-280): logits never reach HBM
+//   greedy_finalize greedy_finalize (malaga.cu:290-326)
+#pragma once
+#include "engine.h"
+#include "numerics.cuh"
+
+namespace mgb {
+
+// ---------------------------------------------------------------------------
+// Weight access
+
+__device__ __forceinline__ int block_pos(int j, int nb, int G) {
+    return nb <= 32 ? j : (j % G) * 32 + j / G;
+}
+
+// Dequantized element i of row `row` (every product below is exact in f32).
+__device__ __forceinline__ float deq_elem(const Matrix &W, int row, int i) {
+    const int j = i >> 5, k = i & 31;
+    const int pos = block_pos(j, W.nb, W.G);
+    const size_t bi = (size_t)row * W.nb + pos;
+    switch (W.type) {
+        case T_F32: return reinterpret_cast<const float *>(W.a)[(size_t)row * W.K + i];
+        case T_Q8_0: {
+            const float d = h2f(reinterpret_cast<const uint16_t *>(W.b)[bi]);
+            return __fmul_rn(d, (float)(int8_t)W.a[bi * 32 + k]);
+        }
+        case T_Q4_K: {
+            const uint8_t byte = W.a[bi * 16 + (k & 15)];
+            const int q = k < 16 ? (byte & 15) : (byte >> 4);
+            const uint8_t *h = W.b + ((size_t)row * (W.K / 256) + j / 8) * 16;
+            const int sb = j & 7;
+            const uint8_t *s = h + 4;
+            int sc, m;
+            if (sb < 4) {
+                sc = s[sb] & 63;
+                m = s[sb + 4] & 63;
+            } else {
+                sc = (s[sb + 4] & 0xf) | ((s[sb - 4] >> 6) << 4);
+                m = (s[sb + 4] >> 4) | ((s[sb] >> 6) << 4);
+            }
+            const float d = h2f(h[0] | (h[1] << 8)), dm = h2f(h[2] | (h[3] << 8));
+            return __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)q), __fmul_rn(dm, (float)m));
+        }
+        case T_Q6_K: {
+            const uint8_t byte = W.a[bi * 16 + (k & 15)];
+            const int lo = k < 16 ? (byte & 15) : (byte >> 4);
+            const uint32_t word = reinterpret_cast<const uint32_t *>(W.b)[bi * 2 + (k >> 4)];
+            const int kk = k & 15;
+            const int hi = (word >> (8 * (kk & 3) + 2 * (kk >> 2))) & 3;
+            const int q = lo | (hi << 4);
+            const int sc = (int8_t)W.c[bi * 2 + (k >> 4)];
+            const float d = h2f(reinterpret_cast<const uint16_t *>(W.e)[(size_t)row * (W.K / 256) + j / 8]);
+            return __fmul_rn(__fmul_rn(d, (float)sc), (float)(q - 32));
+        }
+    }
+    return 0.0f;
+}
+
+// ---------------------------------------------------------------------------
+// Activation preparation: one warp per row. Lane l owns elements l + 32 t, so
+// block t of the q8_1 activation is exactly "element t of every lane".
+
+enum PrepMode { PREP_PLAIN = 0, PREP_LN = 1, PREP_EMBED_LN = 2 };
+
+struct PrepArgs {
+    const float *x;       // input rows [rows][K] (PLAIN, LN)
+    float *x_out;         // EMBED_LN: residual stream written here
+    const float *gamma, *beta;
+    // EMBED_LN
+    Matrix embed;
+    const uint32_t *ids;
+    const uint32_t *step;
+    const float *pos_table;
+    uint32_t pos_base;
+    float scale;
+    int rows, K;
+    QAct out;
+    int keep_f32;  // also store the (normalised) f32 values (for F32 weights)
+    float *xf;     // [rows][K]
+};
+
+__device__ __forceinline__ void quantize_block(float y, const QAct &o, int row, int t, int lane) {
+    const float amax = warp_max(fabsf(y));
+    const float dd = __fdiv_rn(amax, 127.0f);
+    const int q = amax == 0.0f ? 0 : (int)roundf(__fdiv_rn(y, dd));
+    o.q[(size_t)row * o.K + 32 * t + lane] = (int8_t)q;
+    int s = q;
+#pragma unroll
+    for (int off = 1; off < 16; off <<= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    const int nb = o.K >> 5;
+    if (lane == 0) {
+        o.d[(size_t)row * nb + t] = round_h(dd);
+        o.s16[(size_t)row * 2 * nb + 2 * t] = s;
+    }
+    const int s_hi = __shfl_sync(0xffffffffu, s, 16);
+    const int s_lo = __shfl_sync(0xffffffffu, s, 0);
+    if (lane == 0) {
+        o.s16[(size_t)row * 2 * nb + 2 * t + 1] = s_hi;
+        o.s32[(size_t)row * nb + t] = s_lo + s_hi;
+    }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(256) qprep_kernel(PrepArgs p) {
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (row >= p.rows) return;
+    const int K = p.K, T = K >> 5;
+    const float *x = p.x + (size_t)row * K;
+    if constexpr (MODE == PREP_EMBED_LN) {
+        const uint32_t id = p.ids[row];
+        const float *pos = p.pos_table + (size_t)(*p.step + p.pos_base) * K;
+        float *xo = p.x_out + (size_t)row * K;
+        for (int t = 0; t < T; ++t) {
+            const int i = 32 * t + lane;
+            xo[i] = __fadd_rn(__fmul_rn(deq_elem(p.embed, (int)id, i), p.scale), pos[i]);
+        }
+        x = xo;
+        __syncwarp();
+    }
+    if constexpr (MODE == PREP_PLAIN) {
+        for (int t = 0; t < T; ++t) {
+            const float v = x[32 * t + lane];
+            if (p.keep_f32) p.xf[(size_t)row * K + 32 * t + lane] = v;
+            quantize_block(v, p.out, row, t, lane);
+        }
+        return;
+    }
+    // LayerNorm (eps 1e-5): mean and variance with the lane-ordered pairwise sum.
+    float s = 0.0f;
+    for (int t = 0; t < T; ++t) s = t == 0 ? x[lane] : __fadd_rn(s, x[32 * t + lane]);
+    const float mean = __fdiv_rn(warp_tree(s), (float)K);
+    float s2 = 0.0f;
+    for (int t = 0; t < T; ++t) {
+        const float c = __fsub_rn(x[32 * t + lane], mean);
+        const float c2 = __fmul_rn(c, c);
+        s2 = t == 0 ? c2 : __fadd_rn(s2, c2);
+    }
+    const float var = __fdiv_rn(warp_tree(s2), (float)K);
+    const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
+    for (int t = 0; t < T; ++t) {
+        const int i = 32 * t + lane;
+        const float y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(x[i], mean), rstd), p.gamma[i]), p.beta[i]);
+        if (p.keep_f32) p.xf[(size_t)row * K + i] = y;
+        quantize_block(y, p.out, row, t, lane);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Matmul rows: one warp per weight row, lane l owns blocks [l*G, l*G+G).
+
+enum Epi { EPI_STORE = 0, EPI_RELU = 1, EPI_RESID = 2, EPI_QKV = 3, EPI_CROSSKV = 4, EPI_ARGMAX = 5 };
+
+struct GemvArgs {
+    Matrix W;
+    QAct x;           // quantized activations [rows][K]
+    const float *xf;  // f32 activations (F32 weights)
+    int rows;         // activation rows (batch)
+    float *y;         // [rows][N] (STORE, RELU, RESID in place)
+    // QKV: q out [rows][d]; caches [rows][H][m][hd]
+    float *q;
+    __half *kc, *vc;
+    const uint32_t *step;
+    int H, hd, m;
+    // CROSSKV: caches [b][H][S][hd], token row = bi * S + j
+    int S;
+    // ARGMAX
+    float *part_v;
+    uint32_t *part_i;
+    float *logits;  // optional [rows][N]
+};
+
+// Partial p_j of one 32-block against activation row n (see numerics.cuh).
+template <int TYPE>
+struct BlockW;
+
+template <>
+struct BlockW<T_Q8_0> {
+    int w[8];
+    float d;
+    __device__ __forceinline__ void load(const Matrix &W, int row, int pos, int j) {
+        const size_t bi = (size_t)row * W.nb + pos;
+        const int4 *src = reinterpret_cast<const int4 *>(W.a + bi * 32);
+        const int4 a0 = __ldg(src), a1 = __ldg(src + 1);
+        w[0] = a0.x; w[1] = a0.y; w[2] = a0.z; w[3] = a0.w;
+        w[4] = a1.x; w[5] = a1.y; w[6] = a1.z; w[7] = a1.w;
+        d = h2f(__ldg(reinterpret_cast<const unsigned short *>(W.b) + bi));
+    }
+    __device__ __forceinline__ float dot(const int *x, float xd, const QAct &A, int n, int j) const {
+        int s = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) s = __dp4a(w[i], x[i], s);
+        return __fmul_rn(__fmul_rn(d, xd), (float)s);
+    }
+};
+
+template <>
+struct BlockW<T_Q4_K> {
+    int q[4];
+    float d, dm;
+    int sc, m;
+    __device__ __forceinline__ void load(const Matrix &W, int row, int pos, int j) {
+        const size_t bi = (size_t)row * W.nb + pos;
+        const int4 a = __ldg(reinterpret_cast<const int4 *>(W.a + bi * 16));
+        q[0] = a.x; q[1] = a.y; q[2] = a.z; q[3] = a.w;
+        const uint4 h = __ldg(reinterpret_cast<const uint4 *>(W.b + ((size_t)row * (W.K / 256) + j / 8) * 16));
+        d = h2f(h.x & 0xffff);
+        dm = h2f(h.x >> 16);
+        const uint32_t s0 = h.y, s1 = h.z, s2 = h.w;  // scales bytes 0-3, 4-7, 8-11
+        const int sb = j & 7;
+        auto byte = [&](int k) -> int {
+            const uint32_t w = k < 4 ? s0 : (k < 8 ? s1 : s2);
+            return (w >> (8 * (k & 3))) & 0xff;
+        };
+        if (sb < 4) {
+            sc = byte(sb) & 63;
+            m = byte(sb + 4) & 63;
+        } else {
+            sc = (byte(sb + 4) & 0xf) | ((byte(sb - 4) >> 6) << 4);
+            m = (byte(sb + 4) >> 4) | ((byte(sb) >> 6) << 4);
+        }
+    }
+    __device__ __forceinline__ float dot(const int *x, float xd, const QAct &A, int n, int j) const {
+        int s = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            s = __dp4a(q[i] & 0x0f0f0f0f, x[i], s);
+            s = __dp4a((q[i] >> 4) & 0x0f0f0f0f, x[4 + i], s);
+        }
+        const int s8 = A.s32[(size_t)n * (A.K >> 5) + j];
+        const float a = (float)(s * sc), c = (float)(s8 * m);
+        return __fmul_rn(xd, __fsub_rn(__fmul_rn(d, a), __fmul_rn(dm, c)));
+    }
+};
+
+template <>
+struct BlockW<T_Q6_K> {
+    int w[8];
+    int sa, sb;
+    float d;
+    __device__ __forceinline__ void load(const Matrix &W, int row, int pos, int j) {
+        const size_t bi = (size_t)row * W.nb + pos;
+        const int4 l = __ldg(reinterpret_cast<const int4 *>(W.a + bi * 16));
+        const uint2 h = __ldg(reinterpret_cast<const uint2 *>(W.b + bi * 8));
+        const int ql[4] = {l.x, l.y, l.z, l.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            w[i] = (ql[i] & 0x0f0f0f0f) | (int)(((h.x >> (2 * i)) & 0x03030303u) << 4);
+            w[4 + i] = ((ql[i] >> 4) & 0x0f0f0f0f) | (int)(((h.y >> (2 * i)) & 0x03030303u) << 4);
+        }
+        const unsigned short s = __ldg(reinterpret_cast<const unsigned short *>(W.c) + bi);
+        sa = (int8_t)(s & 0xff);
+        sb = (int8_t)(s >> 8);
+        d = h2f(__ldg(reinterpret_cast<const unsigned short *>(W.e) + (size_t)row * (W.K / 256) + j / 8));
+    }
+    __device__ __forceinline__ float dot(const int *x, float xd, const QAct &A, int n, int j) const {
+        int da = 0, db = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            da = __dp4a(w[i], x[i], da);
+            db = __dp4a(w[4 + i], x[4 + i], db);
+        }
+        const size_t o = (size_t)n * (A.K >> 4) + 2 * j;
+        da -= 32 * A.s16[o];
+        db -= 32 * A.s16[o + 1];
+        return __fmul_rn(__fmul_rn(d, xd), (float)(sa * da + sb * db));
+    }
+};
+
+template <int TYPE, int EPI>
+__global__ void __launch_bounds__(256) gemv_kernel(GemvArgs g) {
+    constexpr int NB = 8;  // activation rows per pass (registers)
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const Matrix &W = g.W;
+    const int nb = W.nb, G = W.G;
+    const bool active = nb >= 32 || lane < nb;
+    float best_v[2] = {kNegInf, kNegInf};
+    uint32_t best_i[2] = {0xffffffffu, 0xffffffffu};
+    const int total_warps = gridDim.x * 8;
+    for (int row = blockIdx.x * 8 + warp; row < W.N; row += total_warps) {
+        for (int n0 = 0; n0 < g.rows; n0 += NB) {
+            float acc[NB];
+#pragma unroll
+            for (int i = 0; i < NB; ++i) acc[i] = 0.0f;
+            if (active) {
+                for (int t = 0; t < G; ++t) {
+                    const int pos = nb <= 32 ? lane : t * 32 + lane;
+                    const int j = nb <= 32 ? lane : lane * G + t;
+                    if constexpr (TYPE == T_F32) {
+                        const float *wr = reinterpret_cast<const float *>(W.a) + (size_t)row * W.K + 32 * j;
+#pragma unroll
+                        for (int i = 0; i < NB; ++i) {
+                            if (n0 + i < g.rows) {
+                                const float *xr = g.xf + (size_t)(n0 + i) * W.K + 32 * j;
+                                float p = 0.0f;
+                                for (int e = 0; e < 32; ++e) p = __fmaf_rn(__ldg(wr + e), xr[e], p);
+                                acc[i] = t == 0 ? p : __fadd_rn(acc[i], p);
+                            }
+                        }
+                    } else {
+                        BlockW<TYPE> bw;
+                        bw.load(W, row, pos, j);
+#pragma unroll
+                        for (int i = 0; i < NB; ++i) {
+                            const int n = n0 + i;
+                            if (n < g.rows) {
+                                const int4 *xs = reinterpret_cast<const int4 *>(g.x.q + (size_t)n * W.K + 32 * j);
+                                const int4 x0 = xs[0], x1 = xs[1];
+                                const int xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                                const float xd = g.x.d[(size_t)n * nb + j];
+                                const float p = bw.dot(xv, xd, g.x, n, j);
+                                acc[i] = t == 0 ? p : __fadd_rn(acc[i], p);
+                            }
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < NB; ++i) {
+                const int n = n0 + i;
+                if (n >= g.rows) break;  // uniform across the warp
+                const float v = warp_tree(acc[i]);
+                if (lane != (n & 31)) continue;
+                const float b = W.bias ? W.bias[row] : 0.0f;
+                if constexpr (EPI == EPI_STORE) {
+                    g.y[(size_t)n * W.N + row] = W.bias ? __fadd_rn(v, b) : v;
+                } else if constexpr (EPI == EPI_RELU) {
+                    const float y = __fadd_rn(v, b);
+                    g.y[(size_t)n * W.N + row] = y > 0.0f ? y : 0.0f;
+                } else if constexpr (EPI == EPI_RESID) {
+                    float *xr = g.y + (size_t)n * W.N + row;
+                    *xr = __fadd_rn(__fadd_rn(v, b), *xr);
+                } else if constexpr (EPI == EPI_QKV) {
+                    const float y = __fadd_rn(v, b);
+                    const int dm = g.H * g.hd;
+                    if (row < dm) {
+                        g.q[(size_t)n * dm + row] = y;
+                    } else {
+                        const int c = row - dm, which = c / dm, h = (c % dm) / g.hd, t = c % g.hd;
+                        __half *cache = which == 0 ? g.kc : g.vc;
+                        cache[(((size_t)n * g.H + h) * g.m + *g.step) * g.hd + t] = __float2half_rn(y);
+                    }
+                } else if constexpr (EPI == EPI_CROSSKV) {
+                    const float y = __fadd_rn(v, b);
+                    const int dm = g.H * g.hd, which = row / dm, c = row % dm, h = c / g.hd, t = c % g.hd;
+                    const int bi = n / g.S, jj = n % g.S;
+                    __half *cache = which == 0 ? g.kc : g.vc;
+                    cache[(((size_t)bi * g.H + h) * g.S + jj) * g.hd + t] = __float2half_rn(y);
+                } else if constexpr (EPI == EPI_ARGMAX) {
+                    if (g.logits) g.logits[(size_t)n * W.N + row] = v;
+                    const int slot = n >> 5;  // lane == n & 31
+                    argmax_merge(best_v[slot], best_i[slot], v, (uint32_t)row);
+                }
+            }
+        }
+    }
+    if constexpr (EPI == EPI_ARGMAX) {
+        // Each lane tracked batch rows lane and lane + 32; merge across the CTA's warps.
+        __shared__ float sv[8][64];
+        __shared__ uint32_t si[8][64];
+        sv[warp][lane] = best_v[0];
+        si[warp][lane] = best_i[0];
+        sv[warp][lane + 32] = best_v[1];
+        si[warp][lane + 32] = best_i[1];
+        __syncthreads();
+        for (int n = threadIdx.x; n < g.rows; n += blockDim.x) {
+            float v = sv[0][n];
+            uint32_t i = si[0][n];
+            for (int w = 1; w < 8; ++w) argmax_merge(v, i, sv[w][n], si[w][n]);
+            g.part_v[(size_t)n * gridDim.x + blockIdx.x] = v;
+            g.part_i[(size_t)n * gridDim.x + blockIdx.x] = i;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Single-query attention: one warp per (row, head, query).
+
+struct AttnArgs {
+    const float *q;   // query base
+    long q_row;       // stride between query rows (batch / token)
+    const void *K, *V;
+    long kv_row;      // stride between key rows (elements)
+    long kv_head;     // stride between heads (elements)
+    long kv_batch;    // stride between batch rows (elements)
+    const uint32_t *lens;  // keys per batch row (cross / encoder)
+    const uint32_t *step;  // self: keys = *step + 1
+    float *out;       // [rows][H*hd]
+    long out_row;
+    int H, hd, rows, queries;  // queries per batch row (encoder: S)
+    int max_keys;
+};
+
+template <typename KV>
+__device__ __forceinline__ float load_kv(const KV *p) { return (float)*p; }
+template <>
+__device__ __forceinline__ float load_kv<__half>(const __half *p) { return __half2float(*p); }
+
+template <typename KV>
+__global__ void __launch_bounds__(128) attend_kernel(AttnArgs a) {
+    extern __shared__ float e_sh[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const long task = (long)blockIdx.x * 4 + warp;
+    const long total = (long)a.rows * a.H * a.queries;
+    if (task >= total) return;
+    const int qi = (int)(task % a.queries), h = (int)((task / a.queries) % a.H), n = (int)(task / ((long)a.queries * a.H));
+    float *e = e_sh + (size_t)warp * a.max_keys;
+    const int keys = a.lens ? (int)a.lens[n] : (int)(*a.step) + 1;
+    const float *q = a.q + (size_t)(n * (long)a.queries + qi) * a.q_row + h * a.hd;
+    const KV *K = reinterpret_cast<const KV *>(a.K) + n * a.kv_batch + h * a.kv_head;
+    const KV *V = reinterpret_cast<const KV *>(a.V) + n * a.kv_batch + h * a.kv_head;
+    float mx = kNegInf;
+    for (int j = lane; j < keys; j += 32) {
+        const KV *kr = K + (size_t)j * a.kv_row;
+        float acc = 0.0f;
+        for (int t = 0; t < a.hd; ++t) acc = __fmaf_rn(q[t], load_kv(kr + t), acc);
+        e[j] = acc;
+        mx = fmaxf(mx, acc);
+    }
+    mx = warp_max(mx);
+    float s = 0.0f;
+    for (int j = lane; j < keys; j += 32) {
+        const float ex = mgb_exp(__fsub_rn(e[j], mx));
+        e[j] = ex;
+        s = j == lane ? ex : __fadd_rn(s, ex);
+    }
+    const float inv = __fdiv_rn(1.0f, warp_tree(s));
+    __syncwarp();
+    float *o = a.out + (size_t)(n * (long)a.queries + qi) * a.out_row + h * a.hd;
+    for (int t = lane; t < a.hd; t += 32) {
+        float acc = 0.0f;
+        for (int j = 0; j < keys; ++j) acc = __fmaf_rn(e[j], load_kv(V + (size_t)j * a.kv_row + t), acc);
+        o[t] = __fmul_rn(acc, inv);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Greedy bookkeeping (malaga.cu:290-326): one warp per batch row, then ++step.
+
+__global__ void greedy_finalize_kernel(const float *pv, const uint32_t *pi, int parts, int rows, uint8_t *finished,
+                                       uint32_t *ids, uint32_t *out, int m, uint32_t *step, uint32_t eos, uint32_t pad,
+                                       int force) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const uint32_t s = *step;
+    for (int row = w; row < rows; row += nw) {
+        float best = kNegInf;
+        uint32_t bi = 0xffffffffu;
+        for (int p = lane; p < parts; p += 32) argmax_merge(best, bi, pv[(size_t)row * parts + p], pi[(size_t)row * parts + p]);
+        warp_argmax(best, bi);
+        if (lane == 0) {
+            uint32_t tok = bi;
+            if (finished[row]) tok = pad;
+            if (!force && tok == eos) finished[row] = 1;
+            ids[row] = tok;
+            out[(size_t)row * m + s] = tok;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) *step = s + 1;
+}
+
+// Encoder input: x = E[id] * scale + pos[p]; padded tokens use id = pad, p = pad.
+__global__ void __launch_bounds__(256) embed_tokens_kernel(Matrix E, const uint32_t *ids, const uint32_t *lens, int S,
+                                                           int rows, const float *pos_table, uint32_t pad,
+                                                           float scale, float *x) {
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const int bi = row / S, j = row % S;
+    const bool valid = j < (int)lens[bi];
+    const uint32_t id = valid ? ids[row] : pad;
+    const uint32_t p = valid ? (uint32_t)j + pad + 1 : pad;
+    const int K = E.K;
+    for (int i = lane; i < K; i += 32)
+        x[(size_t)row * K + i] = __fadd_rn(__fmul_rn(deq_elem(E, (int)id, i), scale), pos_table[(size_t)p * K + i]);
+}
+
+// x += y (residual add where the matmul output is not fused in place).
+__global__ void add_inplace_kernel(float *x, const float *y, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        x[i] = __fadd_rn(y[i], x[i]);
+}
+
+}  // namespace mgb

@@ -1,0 +1,105 @@
+"""Synthetic models and inputs of the benchmark configurations.
+
+No checkpoint or dataset is available offline, so every model is random-init
+from a seed with the NLLB-200 architecture of the configuration and converted
+to GGUF by malaga_b200.convert (the reference's converter layout); inputs are
+seeded uniform token ids with the configured length distributions.
+
+Files are generated on first use into $MGB_MODEL_DIR (default /tmp/mgb_models)
+and reused afterwards.
+"""
+from __future__ import annotations
+
+import dataclasses
+import os
+
+import numpy as np
+
+from . import convert as C
+
+MODEL_DIR = os.environ.get("MGB_MODEL_DIR", "/tmp/mgb_models")
+
+# Language tags of the synthetic large vocabulary (any in-vocabulary ids work
+# with random weights; these sit in NLLB's language-code range).
+SRC_TAG, TGT_TAG = 256047, 256147
+
+
+def _mid(vocab=4000, d=256, heads=4, ffn=1024, layers=2, max_pos=256):
+    return C.NllbConfig(vocab_size=vocab, d_model=d, encoder_layers=layers, decoder_layers=layers,
+                        encoder_attention_heads=heads, decoder_attention_heads=heads, encoder_ffn_dim=ffn,
+                        decoder_ffn_dim=ffn, max_position_embeddings=max_pos)
+
+
+SPECS = {
+    # name: (config, preset, seed, std)
+    "mid": (_mid(), 0.05),
+    "wide": (_mid(vocab=8192, d=1024, heads=16, ffn=4096, layers=2, max_pos=1024), 0.02),
+    "600m": (C.NLLB_600M, 0.02),
+    "1.3b": (C.NLLB_1_3B, 0.02),
+    "3.3b": (C.NLLB_3_3B, 0.02),
+}
+
+
+def model_path(name: str, preset: str, seed: int = 0, directory: str | None = None) -> str:
+    """Path of the GGUF for (architecture, preset, seed), generated on first use."""
+    directory = directory or MODEL_DIR
+    os.makedirs(directory, exist_ok=True)
+    path = os.path.join(directory, f"{name}-{preset}-s{seed}.gguf")
+    if os.path.exists(path):
+        return path
+    if name == "tiny":
+        cfg, get, tok = C.tiny_source(7 if seed == 0 else seed)
+        C.convert(cfg, get, path, preset, "tiny", tok)
+        return path
+    cfg, std = SPECS[name]
+    C.convert(cfg, C.random_init_source(cfg, seed, std), path, preset, f"synthetic-nllb-{name}")
+    return path
+
+
+def config_of(name: str) -> C.NllbConfig:
+    return C.TINY if name == "tiny" else SPECS[name][0]
+
+
+def random_sources(n: int, lo: int, hi: int, vocab: int, seed: int, src_tag: int = SRC_TAG, eos: int = 2,
+                   fixed_len: int | None = None) -> list[list[int]]:
+    """n sources `[src_tag] ids [eos]`, ids uniform in [4, vocab), body length uniform
+    in [lo, hi] (or fixed_len), seeded."""
+    lens = (np.full(n, fixed_len) if fixed_len is not None
+            else C.seeded_uniform_u32(n, seed, 1, lo, hi + 1).astype(int))
+    out = []
+    for i in range(n):
+        body = C.seeded_uniform_u32(int(lens[i]), seed, 1000 + i, 4, vocab)
+        out.append([src_tag] + [int(x) for x in body] + [eos])
+    return out
+
+
+def lognormal_sources(n: int, median: float, lo: int, hi: int, vocab: int, seed: int) -> list[list[int]]:
+    """Lengths lognormal(median, sigma 0.5) clipped to [lo, hi] (configs 4 and 5)."""
+    z = C.seeded_normal(n, seed, 2, 1.0).astype(np.float64)
+    lens = np.clip(np.round(median * np.exp(0.5 * z)), lo, hi).astype(int)
+    return [random_sources(1, 0, 0, vocab, seed * 100000 + i, fixed_len=int(lens[i]))[0] for i in range(n)]
+
+
+@dataclasses.dataclass
+class Workload:
+    name: str
+    model: str
+    preset: str
+    seed: int
+    batch: int
+    steps: int
+    sources: list
+
+
+def workload(key: str) -> Workload:
+    """The benchmark configurations as concrete inputs."""
+    V = C.NLLB_600M.vocab_size
+    if key == "c1":  # 600M q4_k_m, b1, 32-token source, 32 forced steps
+        return Workload("c1", "600m", "q4_k_m", 0, 1, 32, random_sources(1, 32, 32, V, 0, fixed_len=32))
+    if key == "c2":  # 600M q8_0, b64, lengths U[8,64], 64 forced steps
+        src = sorted(random_sources(64, 8, 64, V, 1), key=len, reverse=True)
+        return Workload("c2", "600m", "q8_0", 1, 64, 64, src)
+    if key == "c2q4":  # the headline metric's q4_k_m weights on config 2's batch
+        src = sorted(random_sources(64, 8, 64, V, 1), key=len, reverse=True)
+        return Workload("c2q4", "600m", "q4_k_m", 0, 64, 64, src)
+    raise KeyError(key)

@@ -1,0 +1,191 @@
+"""Host-side mirror of malaga-core's decode API over the C ABI.
+
+Follows crates/malaga-core/src/translator.rs on token ids (tokenisation,
+sentence segmentation and language aliases are host text processing outside
+the decode path):
+  GenOptions           translator.rs:16-53
+  Translator.generate  translator.rs:170-207 (generate_to: per-sentence budget
+                       2*len+16 clamped to min(max_length, max_pos-2), truncation)
+  Translator.translate_batch
+                       translator.rs:136-167 (length-sorted batches of max_batch,
+                       OOM -> halve the batch and clear the graph cache)
+  Engine.encode        model.rs:463-500 (Nllb::encode_cross)
+  Engine.greedy        graph.rs:204-298 (GraphCache::greedy)
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _lib
+from ._lib import MgbError, check
+
+
+@dataclass
+class GenOptions:
+    beam_size: int = 1
+    max_new_tokens: int | None = None
+    length_penalty: float = 1.0
+    sync_every: int = 4
+    max_batch: int = 32
+    # Decode every row to its full budget, ignoring end-of-sequence (the
+    # benchmark configurations' "forced steps"). Not a reference option.
+    force_steps: bool = False
+
+
+class Batch:
+    """An encoded batch: per-layer cross-attention K/V resident on the GPU."""
+
+    def __init__(self, engine: "Engine", handle: int, lens: list[int], s: int):
+        self.engine, self.h, self.lens, self.s = engine, handle, lens, s
+
+    @property
+    def size(self) -> int:
+        return len(self.lens)
+
+    def free(self):
+        if self.h:
+            _lib.load().mgb_batch_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.free()
+
+
+class Engine:
+    """One decode context on one GPU (mgb_open)."""
+
+    def __init__(self, gguf_path: str, device: int = 0, use_graphs: bool = True, graph_cache_mb: int = 512,
+                 fail_alloc_after: int = -1):
+        L = _lib.load()
+        opts = _lib.Options()
+        L.mgb_default_options(ctypes.byref(opts))
+        opts.use_graphs = int(use_graphs)
+        opts.graph_cache_bytes = graph_cache_mb << 20
+        opts.fail_alloc_after = fail_alloc_after
+        h = ctypes.c_void_p()
+        check(L.mgb_open(gguf_path.encode(), device, ctypes.byref(opts), ctypes.byref(h)))
+        self.h = h.value
+        self.device = device
+        info = _lib.ModelInfo()
+        check(L.mgb_model_info_get(self.h, ctypes.byref(info)))
+        self.info = {n: getattr(info, n) for n, _ in _lib.ModelInfo._fields_}
+
+    def close(self):
+        if getattr(self, "h", None):
+            _lib.load().mgb_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    @property
+    def stream(self) -> int:
+        return _lib.load().mgb_cuda_stream(self.h)
+
+    @property
+    def kernel_launches(self) -> int:
+        return _lib.load().mgb_kernel_launches(self.h)
+
+    def clear_cache(self):
+        check(_lib.load().mgb_clear_cache(self.h))
+
+    def encode(self, src: list[list[int]]) -> Batch:
+        s = max(len(r) for r in src)
+        ids = np.full((len(src), s), self.info["pad_token_id"], np.uint32)
+        for i, r in enumerate(src):
+            ids[i, : len(r)] = r
+        lens = np.array([len(r) for r in src], np.uint32)
+        return self.encode_array(ids, lens)
+
+    def encode_array(self, ids: np.ndarray, lens: np.ndarray) -> Batch:
+        ids = np.ascontiguousarray(ids, np.uint32)
+        lens = np.ascontiguousarray(lens, np.uint32)
+        h = ctypes.c_void_p()
+        check(_lib.load().mgb_encode(self.h, ids.ctypes.data, lens.ctypes.data, ids.shape[0], ids.shape[1],
+                                     ctypes.byref(h)))
+        return Batch(self, h.value, [int(x) for x in lens], int(ids.shape[1]))
+
+    def greedy(self, batch: Batch, tgt_lang: int, max_new: int, sync_every: int = 4, force: bool = False,
+               out: np.ndarray | None = None) -> tuple[np.ndarray, np.ndarray]:
+        """Raw columns [b, max_new] (pad after eos) and the lengths before eos."""
+        if out is None:
+            out = np.empty((batch.size, max_new), np.uint32)
+        lens = np.empty(batch.size, np.uint32)
+        check(_lib.load().mgb_greedy(self.h, batch.h, tgt_lang, max_new, sync_every, int(force), out.ctypes.data,
+                                     lens.ctypes.data))
+        return out, lens
+
+    def greedy_logits(self, batch: Batch, tgt_lang: int, max_new: int, force: bool = False):
+        out = np.empty((batch.size, max_new), np.uint32)
+        logits = np.empty((max_new, batch.size, self.info["vocab_size"]), np.float32)
+        check(_lib.load().mgb_greedy_logits(self.h, batch.h, tgt_lang, max_new, int(force), out.ctypes.data,
+                                            logits.ctypes.data))
+        return out, logits
+
+    def profile_step(self, batch: Batch, tgt_lang: int, iters: int) -> tuple[float, float]:
+        """(mean LM-head kernel ms, mean step ms) over `iters` eager steps."""
+        lm, st = ctypes.c_float(), ctypes.c_float()
+        check(_lib.load().mgb_profile_step(self.h, batch.h, tgt_lang, iters, ctypes.byref(lm), ctypes.byref(st)))
+        return lm.value, st.value
+
+    def cross(self, batch: Batch, layer: int, which: int) -> np.ndarray:
+        H, d = self.info["decoder_heads"], self.info["d_model"]
+        out = np.empty((batch.size, H, batch.s, d // H), np.uint16)
+        check(_lib.load().mgb_batch_cross(self.h, batch.h, layer, which, out.ctypes.data))
+        return out.view(np.float16)
+
+
+class Translator:
+    """translator.rs on token ids, driving one Engine."""
+
+    def __init__(self, engine: Engine):
+        self.engine = engine
+        i = engine.info
+        self.eos, self.pad = i["eos_token_id"], i["pad_token_id"]
+        self.cap = min(i["max_length"], i["max_position_embeddings"] - 2)
+
+    def budget(self, n: int, opts: GenOptions) -> int:
+        v = opts.max_new_tokens if opts.max_new_tokens is not None else 2 * n + 16
+        return max(1, min(v, self.cap))
+
+    def generate(self, src: list[list[int]], tgt_lang: int, opts: GenOptions = GenOptions()) -> list[list[int]]:
+        """Target ids without specials for already tokenised sources (generate_to)."""
+        if not src:
+            return []
+        if opts.beam_size > 1:
+            raise NotImplementedError("beam search is not built into this engine yet")
+        max_new = max(self.budget(len(s), opts) for s in src)
+        batch = self.engine.encode(src)
+        try:
+            out, lens = self.engine.greedy(batch, tgt_lang, max_new, max(1, opts.sync_every), opts.force_steps)
+        finally:
+            batch.free()
+        res = []
+        for i, s in enumerate(src):
+            row = [int(t) for t in out[i]] if opts.force_steps else [int(t) for t in out[i, : lens[i]]]
+            res.append(row[: self.budget(len(s), opts)])
+        return res
+
+    def translate_batch(self, src: list[list[int]], tgt_lang: int, opts: GenOptions = GenOptions()) -> list[list[int]]:
+        """Independent sentences in length-sorted batches; output order = input order."""
+        order = sorted(range(len(src)), key=lambda i: -len(src[i]))
+        out: list[list[int]] = [[] for _ in src]
+        max_batch = max(1, opts.max_batch)
+        done = 0
+        while done < len(order):
+            chunk = order[done: done + max_batch]
+            try:
+                ids = self.generate([src[i] for i in chunk], tgt_lang, opts)
+            except MgbError as e:
+                if e.is_oom and max_batch > 1:
+                    max_batch //= 2
+                    self.engine.clear_cache()
+                    continue
+                raise
+            for i, r in zip(chunk, ids):
+                out[i] = r
+            done += len(chunk)
+        return out
