@@ -132,6 +132,25 @@ MGB_API uint64_t mgb_kernel_launches(const mgb_ctx *ctx);
 MGB_API mgb_status mgb_profile_step(mgb_ctx *ctx, const mgb_batch *batch, uint32_t tgt_lang, uint32_t iters,
                             float *lm_head_ms, float *step_ms);
 
+/* Greedy token choice (highest logit, lowest index on ties) for `rows` rows of
+ * `vocab` f32 logits that are already in device memory, without allocating any
+ * device memory. No counterpart in the reference: malaga's greedy_select
+ * allocates its partial buffers on every call (crates/malaga-core/src/
+ * kernels.rs:306-307). For callers that cannot allocate at this point: code
+ * inside another framework's CUDA stream capture, hosts whose caching allocator
+ * already holds the GPU's memory, serving loops that forbid allocation.
+ *   logits: [rows, vocab] device memory; ids: [rows] device memory; vals: [rows]
+ *   device memory or NULL (the winning logits); stream: a cudaStream_t (NULL =
+ *   the legacy default stream) on the current device.
+ * rows must be <= 64 (the fixed scratch size); larger requests fail with
+ * MGB_ERR_INVALID. The scratch is a 128 KiB static device array that every
+ * GPU loading the library keeps until exit, shared by all calls: calls that
+ * overlap on the GPU race. The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress); make that first call before any
+ * stream capture. Asynchronous: results are ready when the stream reaches them. */
+MGB_API mgb_status mgb_argmax_noalloc(const float *logits, uint32_t rows, uint32_t vocab, uint32_t *ids, float *vals,
+                                      void *stream);
+
 #ifdef __cplusplus
 }
 #endif

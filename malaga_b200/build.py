@@ -26,7 +26,7 @@ NVCC_FLAGS = [
     "-Xcompiler", "-fPIC,-fopenmp,-fvisibility=hidden",
     "-shared", "-lgomp",
 ]
-ENGINE_SOURCES = ["engine.cu"]
+ENGINE_SOURCES = ["engine.cu", "noalloc.cu"]
 
 
 def _newer(target: str, sources: list[str]) -> bool:

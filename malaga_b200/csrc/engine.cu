@@ -45,6 +45,8 @@ static mgb_status set_err(mgb_status s, const char *fmt, ...) {
     return s;
 }
 
+void mgb_internal_set_error(const char *msg) { g_err = msg; }
+
 static mgb_status cuda_err(cudaError_t e, const char *what) {
     if (e == cudaErrorMemoryAllocation)
         return set_err(MGB_ERR_OOM, "%s: CUDA_ERROR_OUT_OF_MEMORY (%s)", what, cudaGetErrorString(e));
