@@ -1,0 +1,84 @@
+"""CPU: the oracle against the golden fixtures (tests/golden/make_golden.py)
+and the reference's own relative properties."""
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+from malaga_b200 import convert as C
+from malaga_b200 import gguf_io as G
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def test_oracle_matches_transformers_m2m100_on_tiny_model(model):
+    """f32 semantics pin: identical greedy ids over 16 steps for the 6 sentences of
+    pipeline.rs:132-134, logits within 5e-3 (f16 KV rounding of the fused path)."""
+    g = np.load(os.path.join(GOLDEN, "tiny_hf_greedy.npz"))
+    src = [list(map(int, r[:l])) for r, l in zip(g["src_ids"], g["src_lens"])]
+    orc = oracle.Oracle(model("tiny", "f32"))
+    ids, logits = orc.greedy(src, int(g["tgt"]), g["tokens"].shape[1], force=True, logits=True)
+    np.testing.assert_array_equal(ids, g["tokens"])
+    np.testing.assert_allclose(logits, g["logits"], atol=5e-3, rtol=1e-3)
+
+
+def test_dequantization_matches_gguf_py(tmp_path):
+    """Block layouts pin: our quantizer is deterministic, and the oracle dequantizes
+    its Q8_0 / Q4_K / Q6_K blocks exactly as gguf-py does."""
+    g = np.load(os.path.join(GOLDEN, "dequant_golden.npz"))
+    x = g["x"]
+    plans = []
+    for t, name in ((G.Q8_0, "Q8_0"), (G.Q4_K, "Q4_K"), (G.Q6_K, "Q6_K")):
+        q = C.quantize(x, t).reshape(x.shape[0], -1)
+        np.testing.assert_array_equal(q, g[f"{name}_bytes"])
+        plans.append(G.TensorPlan(f"t.{name}", x.shape, t, lambda q=q: q))
+    path = str(tmp_path / "blocks.gguf")
+    G.write_gguf(path, [("general.architecture", "nllb")], plans)
+    lib = oracle.lib()
+    h = lib.orc_load(path.encode())
+    try:
+        for name in ("Q8_0", "Q4_K", "Q6_K"):
+            want = g[f"{name}_deq"]
+            got = np.array([[lib.orc_dequant(h, f"t.{name}".encode(), r, j) for j in range(x.shape[1])]
+                            for r in range(x.shape[0])], np.float32)
+            assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), name
+    finally:
+        lib.orc_free(h)
+
+
+def test_exp_and_log_accuracy():
+    L = oracle.lib()
+    rng = np.random.default_rng(0)
+    xs = np.concatenate([-np.abs(rng.standard_normal(4000) * 20), np.linspace(-87, 0, 2000)]).astype(np.float32)
+    e = np.array([L.orc_exp(float(v)) for v in xs], np.float32)
+    ref = np.exp(xs.astype(np.float64))
+    assert (np.abs(e - ref) / np.spacing(ref.astype(np.float32))).max() <= 1.0
+    assert L.orc_exp(float("-inf")) == 0.0
+    ys = np.exp(rng.uniform(-80, 80, 4000)).astype(np.float32)
+    lg = np.array([L.orc_log(float(v)) for v in ys], np.float32)
+    rl = np.log(ys.astype(np.float64))
+    assert (np.abs(lg - rl) / np.spacing(np.abs(rl).astype(np.float32))).max() <= 2.0
+
+
+def _tiny_src():
+    return [[254] + C.tiny_sentence(3 + 4 * i, i) + [2] for i in range(6)]
+
+
+@pytest.mark.parametrize("preset", ["f32", "q8_0"])
+def test_batching_does_not_change_outputs(model, preset):
+    """pipeline.rs:45-57 (batch == single); bit-exact in this arithmetic."""
+    orc = oracle.Oracle(model("tiny", preset))
+    src = _tiny_src()
+    batched = orc.greedy(src, 256, 12)
+    for i, s in enumerate(src):
+        np.testing.assert_array_equal(orc.greedy([s], 256, 12)[0], batched[i])
+
+
+def test_beam_one_is_greedy_and_beam_is_deterministic(model):
+    """pipeline.rs:60-69."""
+    orc = oracle.Oracle(model("tiny", "f32"))
+    src = [[254] + C.tiny_sentence(8, 3) + [2]]
+    greedy = oracle.strip_eos(orc.greedy(src, 256, 20)[0], 2)
+    assert [int(t) for t in orc.beam(src, 256, 1, 20)[0]] == greedy
+    assert orc.beam(src, 256, 3, 20) == orc.beam(src, 256, 3, 20)
