@@ -22,11 +22,13 @@
 #include <functional>
 #include <map>
 #include <memory>
+#include <mutex>
+#include <set>
 #include <string>
 #include <vector>
 
 #include "../../include/malaga_b200.h"
-#include "kernels.cuh"
+#include "fused.cuh"
 
 using namespace mgb;
 
@@ -185,8 +187,6 @@ mgb_status parse_gguf(const char *path, GgufFile &f) {
     return MGB_OK;
 }
 
-int host_block_pos(int j, int nb, int G) { return nb <= 32 ? j : (j % G) * 32 + j / G; }
-
 // Unpacks the 32 values of 32-block `j` of a Q4_K row (0..15) / Q6_K row (0..63).
 void q4k_block_values(const uint8_t *row, int j, uint8_t *q) {
     const uint8_t *sb = row + (j / 8) * 144, *qs = sb + 16;
@@ -264,6 +264,7 @@ struct mgb_ctx {
     uint64_t clock = 0;
     std::vector<std::unique_ptr<StaticState>> cache;
     size_t weight_bytes = 0, step_bytes = 0;
+    uint32_t *d_err = nullptr;  // device-side error flags (a bounded wait ran out)
 
     mgb_status dalloc(void **p, size_t bytes) {
         if (inject_armed && opts.fail_alloc_after >= 0 && alloc_count++ == opts.fail_alloc_after)
@@ -342,38 +343,46 @@ struct Planner {
                            want_rows, want_cols);
         if (t->type != T_F32 && t->type != T_Q8_0 && t->type != T_Q4_K && t->type != T_Q6_K)
             return set_err(MGB_ERR_UNSUPPORTED, "tensor %s.weight: GGML type %d is not supported", name.c_str(), t->type);
-        if (K % 32 || (K / 32 > 32 && (K / 32) % 32))
-            return set_err(MGB_ERR_UNSUPPORTED, "tensor %s.weight: row length %ld", name.c_str(), K);
+        if (K % 32) return set_err(MGB_ERR_UNSUPPORTED, "tensor %s.weight: row length %ld", name.c_str(), K);
         M.type = t->type;
         M.N = (int)N;
+        M.Np = (int)((N + 31) / 32 * 32);
         M.K = (int)K;
         M.nb = (int)(K / 32);
-        M.G = M.nb > 32 ? M.nb / 32 : 1;
-        const int nb = M.nb, G = M.G, nsb = (int)(K / 256);
+        M.nsb = (int)(K / 256);
+        const int nb = M.nb, nsb = M.nsb;
+        const long Np = M.Np;
         const long rb = row_bytes(t->type, K);
         M.bytes = (size_t)rb * N;
+        auto slot = [&](long r, int j) { return ((size_t)(r / 32) * nb + j) * 32 + (size_t)(r % 32); };
+        auto sslot = [&](long r, int sb) { return ((size_t)(r / 32) * nsb + sb) * 32 + (size_t)(r % 32); };
         if (t->type == T_F32) {
-            size_t off = L.reserve((size_t)4 * N * K);
-            if (pass == 1) memcpy(L.host.data() + off, t->data, (size_t)4 * N * K);
+            size_t off = L.reserve((size_t)4 * Np * K);
+            if (pass == 1) {
+                uint8_t *h = L.host.data() + off;
+#pragma omp parallel for schedule(static)
+                for (long r = 0; r < N; ++r)
+                    for (int j = 0; j < nb; ++j)
+                        memcpy(h + slot(r, j) * 128, t->data + (size_t)r * rb + 128 * j, 128);
+            }
             ptr(&M.a, off);
         } else if (t->type == T_Q8_0) {
-            size_t oq = L.reserve((size_t)N * nb * 32), od = L.reserve((size_t)N * nb * 2);
+            size_t oq = L.reserve((size_t)Np * nb * 32), od = L.reserve((size_t)Np * nb * 2);
             if (pass == 1) {
                 uint8_t *hq = L.host.data() + oq, *hd = L.host.data() + od;
 #pragma omp parallel for schedule(static)
                 for (long r = 0; r < N; ++r) {
                     const uint8_t *row = t->data + (size_t)r * rb;
                     for (int j = 0; j < nb; ++j) {
-                        const int pos = host_block_pos(j, nb, G);
-                        memcpy(hd + ((size_t)r * nb + pos) * 2, row + 34 * j, 2);
-                        memcpy(hq + ((size_t)r * nb + pos) * 32, row + 34 * j + 2, 32);
+                        memcpy(hd + slot(r, j) * 2, row + 34 * j, 2);
+                        memcpy(hq + slot(r, j) * 32, row + 34 * j + 2, 32);
                     }
                 }
             }
             ptr(&M.a, oq);
             ptr(&M.b, od);
         } else if (t->type == T_Q4_K) {
-            size_t oq = L.reserve((size_t)N * nb * 16), oh = L.reserve((size_t)N * nsb * 16);
+            size_t oq = L.reserve((size_t)Np * nb * 16), oh = L.reserve((size_t)Np * nsb * 16);
             if (pass == 1) {
                 uint8_t *hq = L.host.data() + oq, *hh = L.host.data() + oh;
 #pragma omp parallel for schedule(static)
@@ -382,17 +391,17 @@ struct Planner {
                     uint8_t q[32];
                     for (int j = 0; j < nb; ++j) {
                         q4k_block_values(row, j, q);
-                        uint8_t *dst = hq + ((size_t)r * nb + host_block_pos(j, nb, G)) * 16;
+                        uint8_t *dst = hq + slot(r, j) * 16;
                         for (int k = 0; k < 16; ++k) dst[k] = (uint8_t)(q[k] | (q[k + 16] << 4));
                     }
-                    for (int s = 0; s < nsb; ++s) memcpy(hh + ((size_t)r * nsb + s) * 16, row + 144 * s, 16);
+                    for (int sb = 0; sb < nsb; ++sb) memcpy(hh + sslot(r, sb) * 16, row + 144 * sb, 16);
                 }
             }
             ptr(&M.a, oq);
             ptr(&M.b, oh);
         } else {  // Q6_K
-            size_t ol = L.reserve((size_t)N * nb * 16), oh = L.reserve((size_t)N * nb * 8);
-            size_t os = L.reserve((size_t)N * nb * 2), od = L.reserve((size_t)N * nsb * 2);
+            size_t ol = L.reserve((size_t)Np * nb * 16), oh = L.reserve((size_t)Np * nb * 8);
+            size_t os = L.reserve((size_t)Np * nb * 2), od = L.reserve((size_t)Np * nsb * 2);
             if (pass == 1) {
                 uint8_t *hl = L.host.data() + ol, *hh = L.host.data() + oh, *hs = L.host.data() + os,
                         *hd = L.host.data() + od;
@@ -402,7 +411,7 @@ struct Planner {
                     uint8_t q[32];
                     for (int j = 0; j < nb; ++j) {
                         q6k_block_values(row, j, q);
-                        const size_t bi = (size_t)r * nb + host_block_pos(j, nb, G);
+                        const size_t bi = slot(r, j);
                         for (int k = 0; k < 16; ++k) hl[bi * 16 + k] = (uint8_t)((q[k] & 0xf) | ((q[k + 16] & 0xf) << 4));
                         uint32_t A = 0, B = 0;
                         for (int k = 0; k < 16; ++k) {
@@ -416,7 +425,7 @@ struct Planner {
                         hs[bi * 2] = sc[2 * (j % 8)];
                         hs[bi * 2 + 1] = sc[2 * (j % 8) + 1];
                     }
-                    for (int s = 0; s < nsb; ++s) memcpy(hd + ((size_t)r * nsb + s) * 2, row + 210 * s + 208, 2);
+                    for (int sb = 0; sb < nsb; ++sb) memcpy(hd + sslot(r, sb) * 2, row + 210 * sb + 208, 2);
                 }
             }
             ptr(&M.a, ol);
@@ -471,7 +480,8 @@ static mgb_status load_model(mgb_ctx *c, const char *path) {
     TRY(u("tokenizer.ggml.eos_token_id", g.eos));
     TRY(u("tokenizer.ggml.decoder_start_token_id", g.start));
     TRY(u("tokenizer.ggml.bos_token_id", g.bos, false));
-    if (g.d % 32 || g.d % g.dec_heads || g.d % g.enc_heads || g.d > 8192)
+    // d_model <= 2048 as the reference's fused kernels (kernels.rs:44-47, 89-91)
+    if (g.d % 32 || g.d % g.dec_heads || g.d % g.enc_heads || g.d > 2048)
         return set_err(MGB_ERR_UNSUPPORTED, "d_model %d with %d/%d heads", g.d, g.enc_heads, g.dec_heads);
 
     Loader L{c, &f};
@@ -546,7 +556,7 @@ static mgb_status load_model(mgb_ctx *c, const char *path) {
 // ---------------------------------------------------------------------------
 // Kernel launchers
 
-static int gemv_grid(int N) { return std::max(1, std::min((N + 7) / 8, 148 * 16)); }
+static int gemv_grid(int Np) { return std::max(1, std::min((Np / 32 + 7) / 8, 148 * 16)); }
 
 template <int TYPE>
 static void launch_gemv_t(int epi, const GemvArgs &g, int grid, cudaStream_t s) {
@@ -554,14 +564,12 @@ static void launch_gemv_t(int epi, const GemvArgs &g, int grid, cudaStream_t s) 
         case EPI_STORE: gemv_kernel<TYPE, EPI_STORE><<<grid, 256, 0, s>>>(g); break;
         case EPI_RELU: gemv_kernel<TYPE, EPI_RELU><<<grid, 256, 0, s>>>(g); break;
         case EPI_RESID: gemv_kernel<TYPE, EPI_RESID><<<grid, 256, 0, s>>>(g); break;
-        case EPI_QKV: gemv_kernel<TYPE, EPI_QKV><<<grid, 256, 0, s>>>(g); break;
         case EPI_CROSSKV: gemv_kernel<TYPE, EPI_CROSSKV><<<grid, 256, 0, s>>>(g); break;
-        case EPI_ARGMAX: gemv_kernel<TYPE, EPI_ARGMAX><<<grid, 256, 0, s>>>(g); break;
     }
 }
 
 static mgb_status gemv(mgb_ctx *c, int epi, GemvArgs g, int grid = 0) {
-    if (!grid) grid = gemv_grid(g.W.N);
+    if (!grid) grid = gemv_grid(g.W.Np);
     return launch_check(c, [&] {
         switch (g.W.type) {
             case T_F32: launch_gemv_t<T_F32>(epi, g, grid, c->stream); break;
@@ -583,12 +591,139 @@ static mgb_status qprep(mgb_ctx *c, int mode, PrepArgs p) {
     });
 }
 
+// Launch with programmatic stream serialization: the kernel may begin (and
+// prefetch) while its predecessor finishes; it waits in griddepcontrol.wait.
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k, args...);
+}
+
+// Raises a kernel's dynamic shared-memory limit to the full 227 KB once
+// (before any graph capture: the first step of every shape runs eagerly).
+template <typename... KArgs>
+static cudaError_t allow_smem(void (*k)(KArgs...), size_t bytes) {
+    static std::mutex mu;
+    static std::set<const void *> done;
+    if (bytes <= 48 * 1024) return cudaSuccess;
+    std::lock_guard<std::mutex> lock(mu);
+    if (done.count((const void *)k)) return cudaSuccess;
+    int dev = 0, optin = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaFuncAttributes fa{};
+    cudaError_t e = cudaFuncGetAttributes(&fa, k);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes);
+    if (e == cudaSuccess) done.insert((const void *)k);
+    return e;
+}
+
 template <typename KV>
 static mgb_status attend(mgb_ctx *c, AttnArgs a) {
     const long tasks = (long)a.rows * a.H * a.queries;
     const int grid = (int)((tasks + 3) / 4);
-    const size_t sh = (size_t)4 * a.max_keys * sizeof(float);
-    return launch_check(c, [&] { attend_kernel<KV><<<grid, 128, sh, c->stream>>>(a); });
+    // 4 warps: score/probability rows (max_keys floats) + a 64-key V staging tile
+    const size_t sh = (size_t)4 * a.max_keys * sizeof(float) + (size_t)4 * 64 * a.hd * sizeof(KV);
+    auto go = [&](auto kern) -> mgb_status {
+        cudaError_t e = allow_smem(kern, sh);
+        if (e == cudaSuccess) e = launch_pdl(kern, dim3(grid), dim3(128), sh, c->stream, a);
+        ++c->launches;
+        if (e != cudaSuccess) return cuda_err(e, "attention launch");
+        return MGB_OK;
+    };
+    switch (a.hd) {
+        case 16: return go(attend_kernel<KV, 16>);
+        case 32: return go(attend_kernel<KV, 32>);
+        case 64: return go(attend_kernel<KV, 64>);
+        case 128: return go(attend_kernel<KV, 128>);
+    }
+    return set_err(MGB_ERR_UNSUPPORTED, "head dimension %d", a.hd);
+}
+
+// Fused small-batch matmul (fused.cuh). Splits the batch when its activations
+// would not fit in shared memory.
+template <int TYPE, int EPI, int MODE>
+static mgb_status fused_t(mgb_ctx *c, FusedArgs fa) {
+    const Matrix &W = fa.g.W;
+    const int B = fa.g.rows;
+    const bool f32 = TYPE == T_F32;
+    if constexpr (TYPE != T_F32 && EPI != EPI_ARGMAX) {
+        const size_t sh = staged_bytes(TYPE, W.nb, W.nsb) + smact_bytes(B, W.K, false) + (size_t)B * W.nb * 32 * 4;
+        if (B <= 8 && sh <= 200 * 1024) {
+            auto kern = gemv_staged_kernel<TYPE, EPI, MODE>;
+            cudaError_t e = allow_smem(kern, sh);
+            if (e == cudaSuccess) e = launch_pdl(kern, dim3(W.Np / 32), dim3(256), sh, c->stream, fa, c->d_err);
+            ++c->launches;
+            if (e != cudaSuccess) return cuda_err(e, "staged matmul launch");
+            return MGB_OK;
+        }
+    }
+    const int NBv = B == 1 ? 1 : 8;
+    int chunk = B;
+    while (chunk > 1 && smact_bytes(chunk, W.K, f32) > 160 * 1024) chunk = (chunk + 1) / 2;
+    if (EPI == EPI_ARGMAX) chunk = std::min(chunk, NBv);  // per-warp bests hold NB rows
+    const int groups = W.Np / 32;
+    int grid, gpc;
+    if (EPI == EPI_ARGMAX) {
+        grid = kLmParts;  // fixed: the partial buffers and greedy_finalize assume it
+        gpc = (groups + grid - 1) / grid;
+    } else {
+        const int ctas = std::min(groups, 296);
+        gpc = (groups + ctas - 1) / ctas;
+        grid = (groups + gpc - 1) / gpc;
+    }
+    fa.rows_per_cta = gpc;
+    for (int c0 = 0; c0 < B; c0 += chunk) {
+        FusedArgs f = fa;
+        const int nrow = std::min(chunk, B - c0);
+        f.g.rows = nrow;
+        f.p.rows = nrow;
+        if (MODE == PREP_EMBED_LN) {
+            f.p.ids += c0;
+            f.p.x_out += (size_t)c0 * W.K;
+        } else {
+            f.p.x += (size_t)c0 * W.K;
+        }
+        if (f.g.y) f.g.y += (size_t)c0 * W.N;
+        if (f.g.q) f.g.q += (size_t)c0 * f.g.H * f.g.hd;
+        if (f.g.kc) f.g.kc += (size_t)c0 * f.g.H * f.g.m * f.g.hd;
+        if (f.g.vc) f.g.vc += (size_t)c0 * f.g.H * f.g.m * f.g.hd;
+        if (f.g.part_v) f.g.part_v += (size_t)c0 * grid;
+        if (f.g.part_i) f.g.part_i += (size_t)c0 * grid;
+        if (f.g.logits) f.g.logits += (size_t)c0 * W.N;
+        const size_t sh = smact_bytes(nrow, W.K, f32) +
+                          (MODE != PREP_PLAIN && (size_t)nrow * W.K * 4 <= 64 * 1024 ? (size_t)nrow * W.K * 4 : 0);
+        auto go = [&](auto kern) -> cudaError_t {
+            cudaError_t e = allow_smem(kern, sh);
+            return e == cudaSuccess ? launch_pdl(kern, dim3(grid), dim3(256), sh, c->stream, f) : e;
+        };
+        cudaError_t e = nrow == 1 ? go(gemv_fused_kernel<TYPE, EPI, MODE, 1>) : go(gemv_fused_kernel<TYPE, EPI, MODE, 8>);
+        ++c->launches;
+        if (e != cudaSuccess) return cuda_err(e, "fused matmul launch");
+    }
+    return MGB_OK;
+}
+
+template <int EPI, int MODE>
+static mgb_status fused(mgb_ctx *c, const FusedArgs &fa) {
+    switch (fa.g.W.type) {
+        case T_F32: return fused_t<T_F32, EPI, MODE>(c, fa);
+        case T_Q8_0: return fused_t<T_Q8_0, EPI, MODE>(c, fa);
+        case T_Q4_K: return fused_t<T_Q4_K, EPI, MODE>(c, fa);
+        case T_Q6_K: return fused_t<T_Q6_K, EPI, MODE>(c, fa);
+    }
+    return set_err(MGB_ERR_UNSUPPORTED, "matrix type %d", fa.g.W.type);
 }
 
 static PrepArgs prep_args(const QAct &act, float *xf, bool keep_f32, const float *x, int rows, int K) {
@@ -641,7 +776,7 @@ static mgb_status new_state(mgb_ctx *c, int b, int s, int m, StaticState **out) 
     st->s = s;
     st->m = m;
     const Config &g = c->cfg;
-    const int d = g.d, H = g.dec_heads, hd = d / H, kmax = std::max(d, g.dec_ffn);
+    const int d = g.d, H = g.dec_heads, hd = d / H;
     auto A = [&](void **p, size_t n) -> mgb_status {
         TRY(c->dalloc(p, n));
         st->allocs.push_back(*p);
@@ -657,11 +792,6 @@ static mgb_status new_state(mgb_ctx *c, int b, int s, int m, StaticState **out) 
     TRY(A((void **)&st->q, (size_t)4 * b * d));
     TRY(A((void **)&st->a, (size_t)4 * b * d));
     TRY(A((void **)&st->u, (size_t)4 * b * g.dec_ffn));
-    if (any_f32(c)) TRY(A((void **)&st->xf, (size_t)4 * b * kmax));
-    TRY(A((void **)&st->act.q, (size_t)b * kmax));
-    TRY(A((void **)&st->act.d, (size_t)4 * b * kmax / 32));
-    TRY(A((void **)&st->act.s32, (size_t)4 * b * kmax / 32));
-    TRY(A((void **)&st->act.s16, (size_t)4 * b * kmax / 16));
     st->kc.resize(g.dec_layers);
     st->vc.resize(g.dec_layers);
     st->ck.resize(g.dec_layers);
@@ -682,39 +812,53 @@ static mgb_status new_state(mgb_ctx *c, int b, int s, int m, StaticState **out) 
     return MGB_OK;
 }
 
-// One greedy decoder step on the state's fixed buffers (model.rs:552-612).
+// One greedy decoder step on the state's fixed buffers (model.rs:552-612):
+// 6 fused matmuls + 2 attentions per layer, the LM head with argmax, finalize.
 static mgb_status launch_step(mgb_ctx *c, StaticState *st, float *logits, int force,
                               cudaEvent_t lm0 = nullptr, cudaEvent_t lm1 = nullptr) {
     const Config &g = c->cfg;
     const int b = st->b, d = g.d, H = g.dec_heads, hd = d / H;
-    const bool f32 = st->xf != nullptr;
+    auto src = [&](const float *x, int K, const Norm *n) {
+        PrepArgs p{};
+        p.x = x;
+        p.rows = b;
+        p.K = K;
+        if (n) {
+            p.gamma = n->g;
+            p.beta = n->b;
+        }
+        return p;
+    };
+    auto mm = [&](const Matrix &W) {
+        FusedArgs f{};
+        f.g.W = W;
+        f.g.rows = b;
+        return f;
+    };
     for (int l = 0; l < g.dec_layers; ++l) {
         const DecLayer &L = c->dec[l];
-        // attn_norm(x) -> fused QKV -> q, K/V cache slot *step
-        PrepArgs p = prep_args(st->act, st->xf, f32, st->x, b, d);
-        p.gamma = L.attn_norm.g;
-        p.beta = L.attn_norm.b;
+        // attn_norm(x) (layer 0: x = E[id]*scale + pos) -> fused QKV -> q, K/V cache slot *step
+        FusedArgs fq = mm(L.qkv);
+        fq.p = src(st->x, d, &L.attn_norm);
+        fq.g.q = st->q;
+        fq.g.kc = st->kc[l];
+        fq.g.vc = st->vc[l];
+        fq.g.step = st->step;
+        fq.g.H = H;
+        fq.g.hd = hd;
+        fq.g.m = st->m;
         if (l == 0) {
-            p.x_out = st->x;
-            p.embed = c->embed;
-            p.ids = st->ids;
-            p.step = st->step;
-            p.pos_table = c->pos;
-            p.pos_base = (uint32_t)g.pad + 1;
-            p.scale = c->embed_scale;
-            TRY(qprep(c, PREP_EMBED_LN, p));
+            fq.p.x_out = st->x;
+            fq.p.embed = c->embed;
+            fq.p.ids = st->ids;
+            fq.p.step = st->step;
+            fq.p.pos_table = c->pos;
+            fq.p.pos_base = (uint32_t)g.pad + 1;
+            fq.p.scale = c->embed_scale;
+            TRY((fused<EPI_QKV, PREP_EMBED_LN>(c, fq)));
         } else {
-            TRY(qprep(c, PREP_LN, p));
+            TRY((fused<EPI_QKV, PREP_LN>(c, fq)));
         }
-        GemvArgs gq = gemv_args(L.qkv, st->act, st->xf, b);
-        gq.q = st->q;
-        gq.kc = st->kc[l];
-        gq.vc = st->vc[l];
-        gq.step = st->step;
-        gq.H = H;
-        gq.hd = hd;
-        gq.m = st->m;
-        TRY(gemv(c, EPI_QKV, gq));
         AttnArgs sa{};
         sa.q = st->q;
         sa.q_row = d;
@@ -732,18 +876,15 @@ static mgb_status launch_step(mgb_ctx *c, StaticState *st, float *logits, int fo
         sa.queries = 1;
         sa.max_keys = st->m;
         TRY(attend<__half>(c, sa));
-        TRY(qprep(c, PREP_PLAIN, prep_args(st->act, st->xf, f32, st->a, b, d)));
-        GemvArgs go = gemv_args(L.out, st->act, st->xf, b);
-        go.y = st->x;
-        TRY(gemv(c, EPI_RESID, go));
+        FusedArgs fo = mm(L.out);
+        fo.p = src(st->a, d, nullptr);
+        fo.g.y = st->x;
+        TRY((fused<EPI_RESID, PREP_PLAIN>(c, fo)));
         // cross_norm -> cross_q -> cross attention -> cross_out + residual
-        p = prep_args(st->act, st->xf, f32, st->x, b, d);
-        p.gamma = L.cross_norm.g;
-        p.beta = L.cross_norm.b;
-        TRY(qprep(c, PREP_LN, p));
-        GemvArgs gc = gemv_args(L.cq, st->act, st->xf, b);
-        gc.y = st->q;
-        TRY(gemv(c, EPI_STORE, gc));
+        FusedArgs fc = mm(L.cq);
+        fc.p = src(st->x, d, &L.cross_norm);
+        fc.g.y = st->q;
+        TRY((fused<EPI_STORE, PREP_LN>(c, fc)));
         AttnArgs ca = sa;
         ca.K = st->ck[l];
         ca.V = st->cv[l];
@@ -753,41 +894,37 @@ static mgb_status launch_step(mgb_ctx *c, StaticState *st, float *logits, int fo
         ca.lens = st->lens;
         ca.max_keys = st->s;
         TRY(attend<__half>(c, ca));
-        TRY(qprep(c, PREP_PLAIN, prep_args(st->act, st->xf, f32, st->a, b, d)));
-        GemvArgs gco = gemv_args(L.co, st->act, st->xf, b);
-        gco.y = st->x;
-        TRY(gemv(c, EPI_RESID, gco));
+        FusedArgs fco = mm(L.co);
+        fco.p = src(st->a, d, nullptr);
+        fco.g.y = st->x;
+        TRY((fused<EPI_RESID, PREP_PLAIN>(c, fco)));
         // ffn_norm -> up + ReLU -> down + residual
-        p = prep_args(st->act, st->xf, f32, st->x, b, d);
-        p.gamma = L.ffn_norm.g;
-        p.beta = L.ffn_norm.b;
-        TRY(qprep(c, PREP_LN, p));
-        GemvArgs gu = gemv_args(L.up, st->act, st->xf, b);
-        gu.y = st->u;
-        TRY(gemv(c, EPI_RELU, gu));
-        TRY(qprep(c, PREP_PLAIN, prep_args(st->act, st->xf, f32, st->u, b, g.dec_ffn)));
-        GemvArgs gd = gemv_args(L.down, st->act, st->xf, b);
-        gd.y = st->x;
-        TRY(gemv(c, EPI_RESID, gd));
+        FusedArgs fu = mm(L.up);
+        fu.p = src(st->x, d, &L.ffn_norm);
+        fu.g.y = st->u;
+        TRY((fused<EPI_RELU, PREP_LN>(c, fu)));
+        FusedArgs fd = mm(L.down);
+        fd.p = src(st->u, g.dec_ffn, nullptr);
+        fd.g.y = st->x;
+        TRY((fused<EPI_RESID, PREP_PLAIN>(c, fd)));
     }
     // dec_norm -> tied LM head fused with the first argmax pass -> greedy bookkeeping
-    PrepArgs p = prep_args(st->act, st->xf, f32, st->x, b, d);
-    p.gamma = c->dec_norm.g;
-    p.beta = c->dec_norm.b;
-    TRY(qprep(c, PREP_LN, p));
-    GemvArgs gl = gemv_args(c->embed, st->act, st->xf, b);
-    gl.part_v = st->part_v;
-    gl.part_i = st->part_i;
-    gl.logits = logits;
+    FusedArgs fl = mm(c->embed);
+    fl.p = src(st->x, d, &c->dec_norm);
+    fl.g.part_v = st->part_v;
+    fl.g.part_i = st->part_i;
+    fl.g.logits = logits;
     if (lm0) CK(cudaEventRecord(lm0, c->stream));
-    TRY(gemv(c, EPI_ARGMAX, gl, kLmParts));
+    TRY((fused<EPI_ARGMAX, PREP_LN>(c, fl)));
     if (lm1) CK(cudaEventRecord(lm1, c->stream));
     const int threads = std::min(1024, std::max(32, 32 * b));
-    return launch_check(c, [&] {
-        greedy_finalize_kernel<<<1, threads, 0, c->stream>>>(st->part_v, st->part_i, kLmParts, b, st->finished,
-                                                             st->ids, st->out, st->m, st->step, (uint32_t)g.eos,
-                                                             (uint32_t)g.pad, force);
-    });
+    cudaError_t e = launch_pdl(greedy_finalize_kernel, dim3(1), dim3(threads), 0, c->stream,
+                               (const float *)st->part_v, (const uint32_t *)st->part_i, (int)kLmParts, b,
+                               st->finished, st->ids, st->out, st->m, st->step, (uint32_t)g.eos, (uint32_t)g.pad,
+                               force);
+    ++c->launches;
+    if (e != cudaSuccess) return cuda_err(e, "finalize launch");
+    return MGB_OK;
 }
 
 // ---------------------------------------------------------------------------
@@ -1057,8 +1194,14 @@ static mgb_status run_greedy(mgb_ctx *c, const mgb_batch *B, uint32_t tgt, int m
         ++steps;
     }
     std::vector<uint32_t> out((size_t)st->b * st->m);
+    uint32_t derr = 0;
     CK(cudaMemcpyAsync(out.data(), st->out, 4 * out.size(), cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaMemcpyAsync(&derr, c->d_err, 4, cudaMemcpyDeviceToHost, c->stream));
     CK(cudaStreamSynchronize(c->stream));
+    if (derr) {
+        cudaMemsetAsync(c->d_err, 0, 4, c->stream);
+        return set_err(MGB_ERR_CUDA, "a device-side wait on a weight copy ran out of time (flags %u)", derr);
+    }
     for (int r = 0; r < n; ++r) {
         uint32_t len = 0;
         bool seen = false;
@@ -1105,6 +1248,17 @@ mgb_status mgb_open(const char *path, int device, const mgb_options *opts, mgb_c
         cudaStreamDestroy(c->stream);
         return s;
     }
+    {
+        void *p = nullptr;
+        mgb_status es = c->dalloc(&p, 4);
+        if (es != MGB_OK) {
+            cudaFree(c->arena);
+            cudaStreamDestroy(c->stream);
+            return es;
+        }
+        c->d_err = (uint32_t *)p;
+        CK(cudaMemset(c->d_err, 0, 4));
+    }
     c->inject_armed = true;
     *out = c.release();
     return MGB_OK;
@@ -1115,6 +1269,7 @@ void mgb_close(mgb_ctx *c) {
     cudaSetDevice(c->device);
     clear_cache(c);
     if (c->arena) cudaFree(c->arena);
+    if (c->d_err) cudaFree(c->d_err);
     cudaStreamDestroy(c->stream);
     delete c;
 }

@@ -12,28 +12,29 @@ enum GgmlType : int { T_F32 = 0, T_F16 = 1, T_Q8_0 = 8, T_Q4_K = 12, T_Q6_K = 14
 
 // A matmul weight [N rows, K] in the engine's HBM layout.
 //
-// Blocks of 32 values are stored in "lane order": with nb = K/32 blocks and
-// G = max(1, nb/32) blocks per lane, block j = l*G + t of a row sits at
-// position t*32 + l (nb <= 32: position j). A warp reading iteration t of a
-// row therefore touches 32 consecutive block slots: fully coalesced.
-//   Q8_0: qs  [N][nb][32] int8           d   [N][nb] f16
-//   Q4_K: qs  [N][nb][16]  byte k = q[k] | q[k+16] << 4 (q in 0..15)
-//         hdr [N][K/256][16] = {f16 d, f16 dmin, 12 packed 6-bit sc/m} (GGUF)
-//   Q6_K: ql  [N][nb][16]  byte k = lo4(q[k]) | lo4(q[k+16]) << 4 (q in 0..63)
-//         qh  [N][nb][8]   u32 A: byte b bits 2i..2i+1 = hi2(q[4i+b]); u32 B: same for q[16..31]
-//         sc  [N][nb][2]   int8 scales of the two 16-value halves
-//         d   [N][K/256] f16
-//   F32 : w   [N][K] f32 (natural order)
-// Byte counts equal the GGUF block sizes (Q4_K 144 B, Q6_K 210 B per 256).
+// Rows are stored in groups of 32 ("row-interleaved"): for row group g and
+// 32-block j, the 32 rows' data for that block are consecutive slots, slot
+// s = (g*nb + j)*32 + (row % 32). A warp whose lane l owns row 32g+l therefore
+// reads one contiguous run per block (16 B x 32 lanes for Q4_K quants), and a
+// 128-row tensor-core tile is four consecutive groups. N is padded to Np (a
+// multiple of 32) with zero rows. Per slot:
+//   Q8_0: a = 32 B int8 q                      b = f16 d
+//   Q4_K: a = 16 B, byte k = q[k] | q[k+16]<<4  b = per (g, super-block, row) the
+//         GGUF 16 B header {f16 d, f16 dmin, 12 packed 6-bit sc/m}
+//   Q6_K: a = 16 B, byte k = lo4(q[k]) | lo4(q[k+16])<<4 (q in 0..63)
+//         b = 8 B: u32 A byte b bits 2i..2i+1 = hi2(q[4i+b]); u32 B the same for q[16..31]
+//         c = 2 B int8 scales of the two 16-value halves; e = per (g, super-block, row) f16 d
+//   F32 : a = 32 floats
+// Byte counts equal the GGUF block sizes (Q4_K 144 B, Q6_K 210 B per 256 values).
 struct Matrix {
     int type = -1;
-    int N = 0, K = 0, nb = 0, G = 1;
-    const uint8_t *a = nullptr;  // qs / ql / w
-    const uint8_t *b = nullptr;  // d / hdr / qh
-    const uint8_t *c = nullptr;  // Q6_K sc
-    const uint8_t *e = nullptr;  // Q6_K d
+    int N = 0, Np = 0, K = 0, nb = 0, nsb = 0;
+    const uint8_t *a = nullptr;
+    const uint8_t *b = nullptr;
+    const uint8_t *c = nullptr;
+    const uint8_t *e = nullptr;
     const float *bias = nullptr;
-    size_t bytes = 0;  // HBM bytes of the weight (algorithmic bytes of one pass)
+    size_t bytes = 0;  // GGUF bytes of the weight (algorithmic bytes of one pass)
 };
 
 struct Norm {

@@ -1,0 +1,464 @@
+// Fused decode-step matmul for small batches: activation prologue + weight rows
+// + epilogue in one kernel (sm_100a).
+//
+// One launch replaces the reference's chain "bias_residual_ln / embed_pos_ln
+// (malaga.cu:89-130) -> candle q8_1 quantize -> QMatMul MMVQ -> bias / ReLU /
+// residual / qkv_decode epilogue (malaga.cu:133-154)":
+//   1. the CTA asks L2 to prefetch its slice of the weight matrix (bulk
+//      prefetch; weights do not depend on the previous kernel),
+//   2. programmatic dependent launch: it lets the next kernel start and waits for
+//      the previous one,
+//   3. it builds the q8_1 activations of every batch row in shared memory
+//      (LayerNorm / embedding+position+LayerNorm / plain), in the engine's fixed
+//      reduction order,
+//   4. each warp computes a group of 32 weight rows (lane = row), summing the
+//      block partials left to right, and the epilogue writes the result.
+#pragma once
+#include "kernels.cuh"
+
+namespace mgb {
+
+struct FusedArgs {
+    GemvArgs g;     // matrix, outputs and epilogue parameters
+    PrepArgs p;     // activation source (x or a/u, LayerNorm, embedding)
+    int rows_per_cta;  // row groups (of 32) per CTA
+};
+
+// Bytes per 32-row group of each region of the engine layout (see engine.h).
+__device__ __forceinline__ void region_group_bytes(const Matrix &W, size_t (&rb)[4]) {
+    const size_t nb = W.nb, nsb = W.nsb;
+    switch (W.type) {
+        case T_F32: rb[0] = nb * 32 * 128; rb[1] = rb[2] = rb[3] = 0; break;
+        case T_Q8_0: rb[0] = nb * 32 * 32; rb[1] = nb * 32 * 2; rb[2] = rb[3] = 0; break;
+        case T_Q4_K: rb[0] = nb * 32 * 16; rb[1] = nsb * 32 * 16; rb[2] = rb[3] = 0; break;
+        default: rb[0] = nb * 32 * 16; rb[1] = nb * 32 * 8; rb[2] = nb * 32 * 2; rb[3] = nsb * 32 * 2; break;
+    }
+}
+
+// Bulk L2 prefetch of row groups [g0, g1) of every region (rounded out to 16
+// bytes; regions are 256-byte aligned inside the weight arena).
+__device__ __forceinline__ void prefetch_groups(const Matrix &W, int g0, int g1) {
+    if (threadIdx.x >= 4 || g0 >= g1) return;
+    size_t rb[4];
+    region_group_bytes(W, rb);
+    const uint8_t *base[4] = {W.a, W.b, W.c, W.e};
+    const int k = threadIdx.x;
+    if (!rb[k] || !base[k]) return;
+    uint64_t lo = (uint64_t)(base[k] + (size_t)g0 * rb[k]);
+    uint64_t hi = (uint64_t)(base[k] + (size_t)g1 * rb[k]);
+    lo &= ~15ull;
+    hi = (hi + 15) & ~15ull;
+    while (lo < hi) {
+        const uint64_t n = (hi - lo) > (1ull << 30) ? (1ull << 30) : (hi - lo);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(lo), "r"((uint32_t)n) : "memory");
+        lo += n;
+    }
+}
+
+// Shared-memory q8_1 activations of B rows.
+struct SmAct {
+    int8_t *q;   // [B][K]
+    float *d;    // [B][nb]
+    int *s32;    // [B][nb]
+    int *s16;    // [B][2nb]
+    float *st;   // [B][2] mean, rstd
+    float *xf;   // [B][K] (F32 weights only)
+};
+
+__host__ __device__ inline size_t smact_bytes(int B, int K, bool f32) {
+    const int nb = K / 32;
+    size_t n = (size_t)B * K;
+    n = (n + 15) / 16 * 16;
+    n += (size_t)B * nb * 4 * 4 + (size_t)B * 2 * 4;
+    if (f32) n += (size_t)B * K * 4;
+    return n + 64;
+}
+
+__device__ __forceinline__ SmAct smact_carve(uint8_t *sm, int B, int K, bool f32) {
+    const int nb = K / 32;
+    SmAct s;
+    size_t o = 0;
+    s.q = reinterpret_cast<int8_t *>(sm);
+    o += ((size_t)B * K + 15) / 16 * 16;
+    s.d = reinterpret_cast<float *>(sm + o);
+    o += (size_t)B * nb * 4;
+    s.s32 = reinterpret_cast<int *>(sm + o);
+    o += (size_t)B * nb * 4;
+    s.s16 = reinterpret_cast<int *>(sm + o);
+    o += (size_t)B * nb * 8;
+    s.st = reinterpret_cast<float *>(sm + o);
+    o += (size_t)B * 8;
+    s.xf = f32 ? reinterpret_cast<float *>(sm + o) : nullptr;
+    return s;
+}
+
+// Element i of batch row r of the activation input, before normalisation.
+// When the rows were staged in shared memory (p.x points there, MODE is then
+// treated as PLAIN/LN over those rows), the reads hit shared memory.
+template <int MODE>
+__device__ __forceinline__ float act_input(const PrepArgs &p, int r, int i) {
+    if constexpr (MODE == PREP_EMBED_LN) {
+        // p.ids / p.pos_table were rebased by the kernel: ids from shared memory,
+        // pos_table pointing at this step's position row.
+        return __fadd_rn(__fmul_rn(deq_elem(p.embed, (int)p.ids[r], i), p.scale), p.pos_table[i]);
+    } else {
+        return p.x[(size_t)r * p.K + i];
+    }
+}
+
+// Builds the activations of all B rows in shared memory. Phase A (LN modes):
+// one warp per row loads the whole row into registers (independent loads, one
+// memory latency), then computes mean and 1/std with the lane-ordered pairwise
+// sum. Phase B: warps quantize (row, block) pairs in parallel, loading the
+// inputs of 8 pairs before processing them.
+template <int MODE>
+__device__ void build_activations_impl(const PrepArgs &p, const SmAct &s, int B, bool write_x);
+
+// Entry point: for LN / embedding inputs of at most 64 KB, all threads first
+// bring the B input rows into shared memory (one memory round trip; the
+// embedding rows are dequantized once), then the LayerNorm statistics and the
+// quantization read them from there.
+template <int MODE>
+__device__ void build_activations(const PrepArgs &p, const SmAct &s, int B, bool write_x, float *xs) {
+    if constexpr (MODE != PREP_PLAIN) {
+        if (xs) {
+            const int K = p.K;
+            for (int idx = threadIdx.x; idx < B * K; idx += blockDim.x) {
+                const int r = idx / K, i = idx % K;
+                const float v = act_input<MODE>(p, r, i);
+                xs[idx] = v;
+                if constexpr (MODE == PREP_EMBED_LN)
+                    if (write_x) p.x_out[idx] = v;
+            }
+            __syncthreads();
+            PrepArgs q = p;
+            q.x = xs;
+            build_activations_impl<PREP_LN>(q, s, B, false);
+            return;
+        }
+    }
+    build_activations_impl<MODE>(p, s, B, write_x);
+}
+
+template <int MODE>
+__device__ void build_activations_impl(const PrepArgs &p, const SmAct &s, int B, bool write_x) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int K = p.K, T = K >> 5, nb = T;
+    if constexpr (MODE != PREP_PLAIN) {
+        constexpr int CH = 16;  // loads in flight per lane; the sums stay strictly in order
+        for (int r = warp; r < B; r += nw) {
+            float sum = 0.0f;
+            for (int t0 = 0; t0 < T; t0 += CH) {
+                float v[CH];
+#pragma unroll
+                for (int u = 0; u < CH; ++u)
+                    if (t0 + u < T) v[u] = act_input<MODE>(p, r, 32 * (t0 + u) + lane);
+#pragma unroll
+                for (int u = 0; u < CH; ++u) {
+                    if (t0 + u >= T) break;
+                    if constexpr (MODE == PREP_EMBED_LN)
+                        if (write_x) p.x_out[(size_t)r * K + 32 * (t0 + u) + lane] = v[u];
+                    sum = t0 + u == 0 ? v[u] : __fadd_rn(sum, v[u]);
+                }
+            }
+            const float mean = __fdiv_rn(warp_tree(sum), (float)K);
+            float s2 = 0.0f;
+            for (int t0 = 0; t0 < T; t0 += CH) {
+                float v[CH];
+#pragma unroll
+                for (int u = 0; u < CH; ++u)
+                    if (t0 + u < T) v[u] = act_input<MODE>(p, r, 32 * (t0 + u) + lane);
+#pragma unroll
+                for (int u = 0; u < CH; ++u) {
+                    if (t0 + u >= T) break;
+                    const float c = __fsub_rn(v[u], mean);
+                    const float c2 = __fmul_rn(c, c);
+                    s2 = t0 + u == 0 ? c2 : __fadd_rn(s2, c2);
+                }
+            }
+            const float var = __fdiv_rn(warp_tree(s2), (float)K);
+            if (lane == 0) {
+                s.st[2 * r] = mean;
+                s.st[2 * r + 1] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
+            }
+        }
+        __syncthreads();
+    }
+    constexpr int PIPE = 8;
+    const int tasks = B * T;
+    for (int base = warp; base < tasks; base += nw * PIPE) {
+        float y[PIPE];
+#pragma unroll
+        for (int u = 0; u < PIPE; ++u) {
+            const int task = base + u * nw;
+            y[u] = task < tasks ? act_input<MODE>(p, task / T, 32 * (task % T) + lane) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < PIPE; ++u) {
+            const int task = base + u * nw;
+            if (task >= tasks) break;  // uniform across the warp
+            const int r = task / T, t = task % T, i = 32 * t + lane;
+            float yy = y[u];
+            if constexpr (MODE != PREP_PLAIN)
+                yy = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(yy, s.st[2 * r]), s.st[2 * r + 1]), p.gamma[i]),
+                               p.beta[i]);
+            if (s.xf) s.xf[(size_t)r * K + i] = yy;
+            const float amax = warp_max(fabsf(yy));
+            const float dd = __fdiv_rn(amax, 127.0f);
+            const int q = amax == 0.0f ? 0 : (int)roundf(__fdiv_rn(yy, dd));
+            s.q[(size_t)r * K + i] = (int8_t)q;
+            int h = q;
+#pragma unroll
+            for (int off = 1; off < 16; off <<= 1) h += __shfl_xor_sync(0xffffffffu, h, off);
+            const int hb = __shfl_sync(0xffffffffu, h, 16);
+            if (lane == 0) {
+                s.d[(size_t)r * nb + t] = round_h(dd);
+                s.s16[(size_t)r * 2 * nb + 2 * t] = h;
+                s.s16[(size_t)r * 2 * nb + 2 * t + 1] = hb;
+                s.s32[(size_t)r * nb + t] = h + hb;
+            }
+        }
+    }
+    __syncthreads();
+}
+
+template <int TYPE, int EPI, int MODE, int NB>
+__global__ void __launch_bounds__(256) gemv_fused_kernel(FusedArgs fa) {
+    extern __shared__ __align__(16) uint8_t sm_raw[];
+    const GemvArgs &g = fa.g;
+    const Matrix &W = g.W;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int groups = W.Np >> 5;
+    const int g0 = blockIdx.x * fa.rows_per_cta, g1 = min(groups, g0 + fa.rows_per_cta);
+    prefetch_groups(W, g0, g1);
+    pdl_launch_dependents();
+    pdl_wait();
+    const int B = g.rows;
+    const SmAct s = smact_carve(sm_raw, B, W.K, TYPE == T_F32);
+    PrepArgs pa = fa.p;
+    if constexpr (MODE == PREP_EMBED_LN) {
+        __shared__ uint32_t ids_sh[64];
+        for (int r = threadIdx.x; r < B; r += blockDim.x) ids_sh[r] = pa.ids[r];
+        pa.pos_table += (size_t)(*pa.step + pa.pos_base) * pa.K;
+        pa.ids = ids_sh;
+        __syncthreads();
+    }
+    float *xs = nullptr;
+    if constexpr (MODE != PREP_PLAIN) xs = reinterpret_cast<float *>(sm_raw + smact_bytes(B, W.K, TYPE == T_F32));
+    build_activations<MODE>(pa, s, B, blockIdx.x == 0, (size_t)B * W.K * 4 <= 64 * 1024 ? xs : nullptr);
+
+    __shared__ float best_v[8][NB];
+    __shared__ uint32_t best_i[8][NB];
+    if constexpr (EPI == EPI_ARGMAX) {
+        if (lane < NB) {
+            best_v[warp][lane] = kNegInf;
+            best_i[warp][lane] = 0xffffffffu;
+        }
+    }
+    const int nb = W.nb;
+    for (int grp = g0 + warp; grp < g1; grp += 8) {
+        const int row = grp * 32 + lane;
+        for (int n0 = 0; n0 < B; n0 += NB) {
+            float acc[NB];
+#pragma unroll
+            for (int i = 0; i < NB; ++i) acc[i] = 0.0f;
+#pragma unroll 8
+            for (int j = 0; j < nb; ++j) {
+                if constexpr (TYPE == T_F32) {
+#pragma unroll
+                    for (int i = 0; i < NB; ++i) {
+                        if (n0 + i >= B) break;
+                        const float p = f32_block(W, row, j, s.xf + (size_t)(n0 + i) * W.K + 32 * j);
+                        acc[i] = j == 0 ? p : __fadd_rn(acc[i], p);
+                    }
+                } else {
+                    BlockW<TYPE> bw;
+                    bw.load(W, row, j);
+#pragma unroll
+                    for (int i = 0; i < NB; ++i) {
+                        const int n = n0 + i;
+                        if (n >= B) break;
+                        const int4 *xs = reinterpret_cast<const int4 *>(s.q + (size_t)n * W.K + 32 * j);
+                        const int4 x0 = xs[0], x1 = xs[1];
+                        const int xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                        const float xd = s.d[(size_t)n * nb + j];
+                        int s32 = 0, s16a = 0, s16b = 0;
+                        if constexpr (TYPE == T_Q4_K) s32 = s.s32[(size_t)n * nb + j];
+                        if constexpr (TYPE == T_Q6_K) {
+                            s16a = s.s16[(size_t)n * 2 * nb + 2 * j];
+                            s16b = s.s16[(size_t)n * 2 * nb + 2 * j + 1];
+                        }
+                        const float p = bw.dot(xv, xd, s32, s16a, s16b);
+                        acc[i] = j == 0 ? p : __fadd_rn(acc[i], p);
+                    }
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < NB; ++i) {
+                const int n = n0 + i;
+                if (n >= B) break;  // uniform across the warp
+                if constexpr (EPI == EPI_ARGMAX) {
+                    if (g.logits && row < W.N) g.logits[(size_t)n * W.N + row] = acc[i];
+                    float v = row < W.N ? acc[i] : kNegInf;
+                    uint32_t idx = row < W.N ? (uint32_t)row : 0xffffffffu;
+                    warp_argmax(v, idx);
+                    if (lane == 0) argmax_merge(best_v[warp][i], best_i[warp][i], v, idx);
+                } else {
+                    if (row < W.N) epilogue_store<EPI>(g, row, n, acc[i]);
+                }
+            }
+        }
+    }
+    if constexpr (EPI == EPI_ARGMAX) {
+        __syncthreads();
+        for (int n = threadIdx.x; n < B; n += blockDim.x) {
+            float v = best_v[0][n];
+            uint32_t i = best_i[0][n];
+            for (int w = 1; w < 8; ++w) argmax_merge(v, i, best_v[w][n], best_i[w][n]);
+            g.part_v[(size_t)n * gridDim.x + blockIdx.x] = v;
+            g.part_i[(size_t)n * gridDim.x + blockIdx.x] = i;
+        }
+    }
+}
+
+}  // namespace mgb
+
+namespace mgb {
+
+// ---------------------------------------------------------------------------
+// Small-batch matmul with TMA-staged weights: one CTA per group of 32 weight
+// rows. Before waiting on the previous kernel, thread 0 starts 1-D bulk copies
+// (cp.async.bulk, completion counted on an mbarrier) of the group's weight
+// slices into shared memory. After the activation prologue, the 8 warps split
+// the K blocks (lane = row) and write the block partials p[n][j][row] to shared
+// memory; then each row's partials are summed left to right in block order.
+
+constexpr uint32_t kWaitLimit = 1u << 26;  // mbarrier polls before giving up
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+// Bounded wait for phase `parity` of the mbarrier; false if the limit ran out.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    const uint32_t a = smem_u32(bar);
+    for (uint32_t it = 0; it < kWaitLimit; ++it) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
+// Shared-memory bytes of one group's staged weights (each region 16-B aligned).
+__host__ __device__ inline size_t staged_bytes(int type, int nb, int nsb) {
+    switch (type) {
+        case T_Q8_0: return (size_t)nb * 32 * 32 + (size_t)nb * 64;
+        case T_Q4_K: return (size_t)nb * 32 * 16 + (size_t)nsb * 32 * 16;
+        case T_Q6_K: return (size_t)nb * 32 * 16 + (size_t)nb * 32 * 8 + (size_t)nb * 64 + (size_t)nsb * 64;
+    }
+    return 0;
+}
+
+template <int TYPE, int EPI, int MODE>
+__global__ void __launch_bounds__(256) gemv_staged_kernel(FusedArgs fa, uint32_t *err) {
+    extern __shared__ __align__(16) uint8_t sm_raw[];
+    __shared__ __align__(8) uint64_t bar;
+    const GemvArgs &g = fa.g;
+    const Matrix &W = g.W;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int grp = blockIdx.x, nb = W.nb, nsb = W.nsb;
+    const size_t wbytes = staged_bytes(TYPE, nb, nsb);
+    // shared layout: [staged weights][activations][partials]
+    Matrix Ws = W;  // a view of this group as "group 0" in shared memory
+    Ws.Np = 32;
+    {
+        uint8_t *p = sm_raw;
+        size_t rb[4];
+        region_group_bytes(W, rb);
+        const uint8_t *src[4] = {W.a, W.b, W.c, W.e};
+        const uint8_t **dst[4] = {&Ws.a, &Ws.b, &Ws.c, &Ws.e};
+        if (threadIdx.x == 0) {
+            mbar_init(&bar, 1);
+            mbar_expect_tx(&bar, (uint32_t)wbytes);
+        }
+        __syncthreads();
+        for (int k = 0; k < 4; ++k) {
+            if (!rb[k] || !src[k]) continue;
+            if (threadIdx.x == 0) bulk_g2s(p, src[k] + (size_t)grp * rb[k], (uint32_t)rb[k], &bar);
+            *dst[k] = p;
+            p += rb[k];
+        }
+    }
+    pdl_launch_dependents();
+    pdl_wait();
+    const int B = g.rows;
+    const SmAct s = smact_carve(sm_raw + wbytes, B, W.K, false);
+    float *P = reinterpret_cast<float *>(sm_raw + wbytes + smact_bytes(B, W.K, false));
+    float *xs = MODE != PREP_PLAIN ? P : nullptr;  // input rows share the partials' space (used before them)
+    PrepArgs pa = fa.p;
+    if constexpr (MODE == PREP_EMBED_LN) {
+        __shared__ uint32_t ids_sh[64];
+        for (int r = threadIdx.x; r < B; r += blockDim.x) ids_sh[r] = pa.ids[r];
+        pa.pos_table += (size_t)(*pa.step + pa.pos_base) * pa.K;
+        pa.ids = ids_sh;
+        __syncthreads();
+    }
+    build_activations<MODE>(pa, s, B, blockIdx.x == 0,
+                            (size_t)B * W.K * 4 <= (size_t)B * W.nb * 32 * 4 ? xs : nullptr);
+    if (!mbar_wait(&bar, 0)) {
+        if (lane == 0) atomicOr(err, 1u);  // copy never completed: report, produce nothing
+        return;
+    }
+    const int cb = (nb + 7) / 8, j0 = warp * cb, j1 = min(nb, j0 + cb);
+    for (int n = 0; n < B; ++n) {
+        const int4 *xq = reinterpret_cast<const int4 *>(s.q + (size_t)n * W.K);
+#pragma unroll 4
+        for (int j = j0; j < j1; ++j) {
+            BlockW<TYPE> bw;
+            bw.template load<false>(Ws, lane, j);
+            const int4 x0 = xq[2 * j], x1 = xq[2 * j + 1];
+            const int xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+            int s32 = 0, s16a = 0, s16b = 0;
+            if constexpr (TYPE == T_Q4_K) s32 = s.s32[(size_t)n * nb + j];
+            if constexpr (TYPE == T_Q6_K) {
+                s16a = s.s16[(size_t)n * 2 * nb + 2 * j];
+                s16b = s.s16[(size_t)n * 2 * nb + 2 * j + 1];
+            }
+            P[((size_t)n * nb + j) * 32 + lane] = bw.dot(xv, s.d[(size_t)n * nb + j], s32, s16a, s16b);
+        }
+    }
+    __syncthreads();
+    const int row = grp * 32 + lane;
+    for (int n = warp; n < B; n += 8) {
+        const float *pn = P + (size_t)n * nb * 32 + lane;
+        float acc = pn[0];
+#pragma unroll 8
+        for (int j = 1; j < nb; ++j) acc = __fadd_rn(acc, pn[(size_t)j * 32]);
+        if (row < W.N) epilogue_store<EPI>(g, row, n, acc);
+    }
+}
+
+}  // namespace mgb

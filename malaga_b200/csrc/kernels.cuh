@@ -21,17 +21,19 @@ namespace mgb {
 // ---------------------------------------------------------------------------
 // Weight access
 
-__device__ __forceinline__ int block_pos(int j, int nb, int G) {
-    return nb <= 32 ? j : (j % G) * 32 + j / G;
+__device__ __forceinline__ size_t wslot(const Matrix &W, int row, int j) {
+    return ((size_t)(row >> 5) * W.nb + j) * 32 + (row & 31);
+}
+__device__ __forceinline__ size_t wsslot(const Matrix &W, int row, int sb) {
+    return ((size_t)(row >> 5) * W.nsb + sb) * 32 + (row & 31);
 }
 
 // Dequantized element i of row `row` (every product below is exact in f32).
 __device__ __forceinline__ float deq_elem(const Matrix &W, int row, int i) {
     const int j = i >> 5, k = i & 31;
-    const int pos = block_pos(j, W.nb, W.G);
-    const size_t bi = (size_t)row * W.nb + pos;
+    const size_t bi = wslot(W, row, j);
     switch (W.type) {
-        case T_F32: return reinterpret_cast<const float *>(W.a)[(size_t)row * W.K + i];
+        case T_F32: return reinterpret_cast<const float *>(W.a)[bi * 32 + k];
         case T_Q8_0: {
             const float d = h2f(reinterpret_cast<const uint16_t *>(W.b)[bi]);
             return __fmul_rn(d, (float)(int8_t)W.a[bi * 32 + k]);
@@ -39,7 +41,7 @@ __device__ __forceinline__ float deq_elem(const Matrix &W, int row, int i) {
         case T_Q4_K: {
             const uint8_t byte = W.a[bi * 16 + (k & 15)];
             const int q = k < 16 ? (byte & 15) : (byte >> 4);
-            const uint8_t *h = W.b + ((size_t)row * (W.K / 256) + j / 8) * 16;
+            const uint8_t *h = W.b + wsslot(W, row, j >> 3) * 16;
             const int sb = j & 7;
             const uint8_t *s = h + 4;
             int sc, m;
@@ -61,7 +63,7 @@ __device__ __forceinline__ float deq_elem(const Matrix &W, int row, int i) {
             const int hi = (word >> (8 * (kk & 3) + 2 * (kk >> 2))) & 3;
             const int q = lo | (hi << 4);
             const int sc = (int8_t)W.c[bi * 2 + (k >> 4)];
-            const float d = h2f(reinterpret_cast<const uint16_t *>(W.e)[(size_t)row * (W.K / 256) + j / 8]);
+            const float d = h2f(reinterpret_cast<const uint16_t *>(W.e)[wsslot(W, row, j >> 3)]);
             return __fmul_rn(__fmul_rn(d, (float)sc), (float)(q - 32));
         }
     }
@@ -182,6 +184,14 @@ struct GemvArgs {
     float *logits;  // optional [rows][N]
 };
 
+// Weight loads: read-only global loads, or plain loads when the weights were
+// staged in shared memory (GLOBAL = false).
+template <bool GLOBAL, typename T>
+__device__ __forceinline__ T ldw(const T *p) {
+    if constexpr (GLOBAL) return __ldg(p);
+    else return *p;
+}
+
 // Partial p_j of one 32-block against activation row n (see numerics.cuh).
 template <int TYPE>
 struct BlockW;
@@ -190,15 +200,16 @@ template <>
 struct BlockW<T_Q8_0> {
     int w[8];
     float d;
-    __device__ __forceinline__ void load(const Matrix &W, int row, int pos, int j) {
-        const size_t bi = (size_t)row * W.nb + pos;
+    template <bool GLOBAL = true>
+    __device__ __forceinline__ void load(const Matrix &W, int row, int j) {
+        const size_t bi = wslot(W, row, j);
         const int4 *src = reinterpret_cast<const int4 *>(W.a + bi * 32);
-        const int4 a0 = __ldg(src), a1 = __ldg(src + 1);
+        const int4 a0 = ldw<GLOBAL>(src), a1 = ldw<GLOBAL>(src + 1);
         w[0] = a0.x; w[1] = a0.y; w[2] = a0.z; w[3] = a0.w;
         w[4] = a1.x; w[5] = a1.y; w[6] = a1.z; w[7] = a1.w;
-        d = h2f(__ldg(reinterpret_cast<const unsigned short *>(W.b) + bi));
+        d = h2f(ldw<GLOBAL>(reinterpret_cast<const unsigned short *>(W.b) + bi));
     }
-    __device__ __forceinline__ float dot(const int *x, float xd, const QAct &A, int n, int j) const {
+    __device__ __forceinline__ float dot(const int *x, float xd, int, int, int) const {
         int s = 0;
 #pragma unroll
         for (int i = 0; i < 8; ++i) s = __dp4a(w[i], x[i], s);
@@ -211,11 +222,12 @@ struct BlockW<T_Q4_K> {
     int q[4];
     float d, dm;
     int sc, m;
-    __device__ __forceinline__ void load(const Matrix &W, int row, int pos, int j) {
-        const size_t bi = (size_t)row * W.nb + pos;
-        const int4 a = __ldg(reinterpret_cast<const int4 *>(W.a + bi * 16));
+    template <bool GLOBAL = true>
+    __device__ __forceinline__ void load(const Matrix &W, int row, int j) {
+        const size_t bi = wslot(W, row, j);
+        const int4 a = ldw<GLOBAL>(reinterpret_cast<const int4 *>(W.a + bi * 16));
         q[0] = a.x; q[1] = a.y; q[2] = a.z; q[3] = a.w;
-        const uint4 h = __ldg(reinterpret_cast<const uint4 *>(W.b + ((size_t)row * (W.K / 256) + j / 8) * 16));
+        const uint4 h = ldw<GLOBAL>(reinterpret_cast<const uint4 *>(W.b + wsslot(W, row, j >> 3) * 16));
         d = h2f(h.x & 0xffff);
         dm = h2f(h.x >> 16);
         const uint32_t s0 = h.y, s1 = h.z, s2 = h.w;  // scales bytes 0-3, 4-7, 8-11
@@ -232,14 +244,13 @@ struct BlockW<T_Q4_K> {
             m = (byte(sb + 4) >> 4) | ((byte(sb) >> 6) << 4);
         }
     }
-    __device__ __forceinline__ float dot(const int *x, float xd, const QAct &A, int n, int j) const {
+    __device__ __forceinline__ float dot(const int *x, float xd, int s8, int, int) const {
         int s = 0;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             s = __dp4a(q[i] & 0x0f0f0f0f, x[i], s);
             s = __dp4a((q[i] >> 4) & 0x0f0f0f0f, x[4 + i], s);
         }
-        const int s8 = A.s32[(size_t)n * (A.K >> 5) + j];
         const float a = (float)(s * sc), c = (float)(s8 * m);
         return __fmul_rn(xd, __fsub_rn(__fmul_rn(d, a), __fmul_rn(dm, c)));
     }
@@ -250,137 +261,136 @@ struct BlockW<T_Q6_K> {
     int w[8];
     int sa, sb;
     float d;
-    __device__ __forceinline__ void load(const Matrix &W, int row, int pos, int j) {
-        const size_t bi = (size_t)row * W.nb + pos;
-        const int4 l = __ldg(reinterpret_cast<const int4 *>(W.a + bi * 16));
-        const uint2 h = __ldg(reinterpret_cast<const uint2 *>(W.b + bi * 8));
+    template <bool GLOBAL = true>
+    __device__ __forceinline__ void load(const Matrix &W, int row, int j) {
+        const size_t bi = wslot(W, row, j);
+        const int4 l = ldw<GLOBAL>(reinterpret_cast<const int4 *>(W.a + bi * 16));
+        const uint2 h = ldw<GLOBAL>(reinterpret_cast<const uint2 *>(W.b + bi * 8));
         const int ql[4] = {l.x, l.y, l.z, l.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             w[i] = (ql[i] & 0x0f0f0f0f) | (int)(((h.x >> (2 * i)) & 0x03030303u) << 4);
             w[4 + i] = ((ql[i] >> 4) & 0x0f0f0f0f) | (int)(((h.y >> (2 * i)) & 0x03030303u) << 4);
         }
-        const unsigned short s = __ldg(reinterpret_cast<const unsigned short *>(W.c) + bi);
+        const unsigned short s = ldw<GLOBAL>(reinterpret_cast<const unsigned short *>(W.c) + bi);
         sa = (int8_t)(s & 0xff);
         sb = (int8_t)(s >> 8);
-        d = h2f(__ldg(reinterpret_cast<const unsigned short *>(W.e) + (size_t)row * (W.K / 256) + j / 8));
+        d = h2f(ldw<GLOBAL>(reinterpret_cast<const unsigned short *>(W.e) + wsslot(W, row, j >> 3)));
     }
-    __device__ __forceinline__ float dot(const int *x, float xd, const QAct &A, int n, int j) const {
+    __device__ __forceinline__ float dot(const int *x, float xd, int, int s16a, int s16b) const {
         int da = 0, db = 0;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             da = __dp4a(w[i], x[i], da);
             db = __dp4a(w[4 + i], x[4 + i], db);
         }
-        const size_t o = (size_t)n * (A.K >> 4) + 2 * j;
-        da -= 32 * A.s16[o];
-        db -= 32 * A.s16[o + 1];
+        da -= 32 * s16a;
+        db -= 32 * s16b;
         return __fmul_rn(__fmul_rn(d, xd), (float)(sa * da + sb * db));
     }
 };
 
+// Block partial p_j of row `row` against activation row n, for F32 weights:
+// an FMA chain over the block's 32 values.
+__device__ __forceinline__ float f32_block(const Matrix &W, int row, int j, const float *x) {
+    const float4 *w = reinterpret_cast<const float4 *>(W.a + wslot(W, row, j) * 128);
+    float p = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        const float4 v = __ldg(w + c);
+        p = __fmaf_rn(v.x, x[4 * c], p);
+        p = __fmaf_rn(v.y, x[4 * c + 1], p);
+        p = __fmaf_rn(v.z, x[4 * c + 2], p);
+        p = __fmaf_rn(v.w, x[4 * c + 3], p);
+    }
+    return p;
+}
+
+// Epilogue of one output element (row of W, activation row n); v = the
+// row sum in block order.
+template <int EPI>
+__device__ __forceinline__ void epilogue_store(const GemvArgs &g, int row, int n, float v) {
+    const Matrix &W = g.W;
+    const float b = W.bias ? W.bias[row] : 0.0f;
+    if constexpr (EPI == EPI_STORE) {
+        g.y[(size_t)n * W.N + row] = W.bias ? __fadd_rn(v, b) : v;
+    } else if constexpr (EPI == EPI_RELU) {
+        const float y = __fadd_rn(v, b);
+        g.y[(size_t)n * W.N + row] = y > 0.0f ? y : 0.0f;
+    } else if constexpr (EPI == EPI_RESID) {
+        float *xr = g.y + (size_t)n * W.N + row;
+        *xr = __fadd_rn(__fadd_rn(v, b), *xr);
+    } else if constexpr (EPI == EPI_QKV) {
+        const float y = __fadd_rn(v, b);
+        const int dm = g.H * g.hd;
+        if (row < dm) {
+            g.q[(size_t)n * dm + row] = y;
+        } else {
+            const int c = row - dm, which = c / dm, h = (c % dm) / g.hd, t = c % g.hd;
+            __half *cache = which == 0 ? g.kc : g.vc;
+            cache[(((size_t)n * g.H + h) * g.m + *g.step) * g.hd + t] = __float2half_rn(y);
+        }
+    } else if constexpr (EPI == EPI_CROSSKV) {
+        const float y = __fadd_rn(v, b);
+        const int dm = g.H * g.hd, which = row / dm, c = row % dm, h = c / g.hd, t = c % g.hd;
+        const int bi = n / g.S, jj = n % g.S;
+        __half *cache = which == 0 ? g.kc : g.vc;
+        cache[(((size_t)bi * g.H + h) * g.S + jj) * g.hd + t] = __float2half_rn(y);
+    }
+}
+
+// Matmul over activations already quantized in global memory (the encoder's
+// b*S token rows): one warp per group of 32 weight rows, lane = row, blocks
+// accumulated left to right; NB activation rows per pass.
 template <int TYPE, int EPI>
 __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs g) {
-    constexpr int NB = 8;  // activation rows per pass (registers)
+    constexpr int NB = 8;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const Matrix &W = g.W;
-    const int nb = W.nb, G = W.G;
-    const bool active = nb >= 32 || lane < nb;
-    float best_v[2] = {kNegInf, kNegInf};
-    uint32_t best_i[2] = {0xffffffffu, 0xffffffffu};
-    const int total_warps = gridDim.x * 8;
-    for (int row = blockIdx.x * 8 + warp; row < W.N; row += total_warps) {
+    const int nb = W.nb, groups = W.Np >> 5;
+    for (int grp = blockIdx.x * 8 + warp; grp < groups; grp += gridDim.x * 8) {
+        const int row = grp * 32 + lane;
         for (int n0 = 0; n0 < g.rows; n0 += NB) {
             float acc[NB];
 #pragma unroll
             for (int i = 0; i < NB; ++i) acc[i] = 0.0f;
-            if (active) {
-                for (int t = 0; t < G; ++t) {
-                    const int pos = nb <= 32 ? lane : t * 32 + lane;
-                    const int j = nb <= 32 ? lane : lane * G + t;
-                    if constexpr (TYPE == T_F32) {
-                        const float *wr = reinterpret_cast<const float *>(W.a) + (size_t)row * W.K + 32 * j;
+#pragma unroll 2
+            for (int j = 0; j < nb; ++j) {
+                if constexpr (TYPE == T_F32) {
 #pragma unroll
-                        for (int i = 0; i < NB; ++i) {
-                            if (n0 + i < g.rows) {
-                                const float *xr = g.xf + (size_t)(n0 + i) * W.K + 32 * j;
-                                float p = 0.0f;
-                                for (int e = 0; e < 32; ++e) p = __fmaf_rn(__ldg(wr + e), xr[e], p);
-                                acc[i] = t == 0 ? p : __fadd_rn(acc[i], p);
-                            }
-                        }
-                    } else {
-                        BlockW<TYPE> bw;
-                        bw.load(W, row, pos, j);
+                    for (int i = 0; i < NB; ++i) {
+                        if (n0 + i >= g.rows) break;
+                        const float p = f32_block(W, row, j, g.xf + (size_t)(n0 + i) * W.K + 32 * j);
+                        acc[i] = j == 0 ? p : __fadd_rn(acc[i], p);
+                    }
+                } else {
+                    BlockW<TYPE> bw;
+                    bw.load(W, row, j);
 #pragma unroll
-                        for (int i = 0; i < NB; ++i) {
-                            const int n = n0 + i;
-                            if (n < g.rows) {
-                                const int4 *xs = reinterpret_cast<const int4 *>(g.x.q + (size_t)n * W.K + 32 * j);
-                                const int4 x0 = xs[0], x1 = xs[1];
-                                const int xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-                                const float xd = g.x.d[(size_t)n * nb + j];
-                                const float p = bw.dot(xv, xd, g.x, n, j);
-                                acc[i] = t == 0 ? p : __fadd_rn(acc[i], p);
-                            }
+                    for (int i = 0; i < NB; ++i) {
+                        const int n = n0 + i;
+                        if (n >= g.rows) break;
+                        const int4 *xs = reinterpret_cast<const int4 *>(g.x.q + (size_t)n * W.K + 32 * j);
+                        const int4 x0 = xs[0], x1 = xs[1];
+                        const int xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                        const float xd = g.x.d[(size_t)n * nb + j];
+                        int s32 = 0, s16a = 0, s16b = 0;
+                        if constexpr (TYPE == T_Q4_K) s32 = g.x.s32[(size_t)n * nb + j];
+                        if constexpr (TYPE == T_Q6_K) {
+                            s16a = g.x.s16[(size_t)n * 2 * nb + 2 * j];
+                            s16b = g.x.s16[(size_t)n * 2 * nb + 2 * j + 1];
                         }
+                        const float p = bw.dot(xv, xd, s32, s16a, s16b);
+                        acc[i] = j == 0 ? p : __fadd_rn(acc[i], p);
                     }
                 }
             }
+            if (row < W.N)
 #pragma unroll
-            for (int i = 0; i < NB; ++i) {
-                const int n = n0 + i;
-                if (n >= g.rows) break;  // uniform across the warp
-                const float v = warp_tree(acc[i]);
-                if (lane != (n & 31)) continue;
-                const float b = W.bias ? W.bias[row] : 0.0f;
-                if constexpr (EPI == EPI_STORE) {
-                    g.y[(size_t)n * W.N + row] = W.bias ? __fadd_rn(v, b) : v;
-                } else if constexpr (EPI == EPI_RELU) {
-                    const float y = __fadd_rn(v, b);
-                    g.y[(size_t)n * W.N + row] = y > 0.0f ? y : 0.0f;
-                } else if constexpr (EPI == EPI_RESID) {
-                    float *xr = g.y + (size_t)n * W.N + row;
-                    *xr = __fadd_rn(__fadd_rn(v, b), *xr);
-                } else if constexpr (EPI == EPI_QKV) {
-                    const float y = __fadd_rn(v, b);
-                    const int dm = g.H * g.hd;
-                    if (row < dm) {
-                        g.q[(size_t)n * dm + row] = y;
-                    } else {
-                        const int c = row - dm, which = c / dm, h = (c % dm) / g.hd, t = c % g.hd;
-                        __half *cache = which == 0 ? g.kc : g.vc;
-                        cache[(((size_t)n * g.H + h) * g.m + *g.step) * g.hd + t] = __float2half_rn(y);
-                    }
-                } else if constexpr (EPI == EPI_CROSSKV) {
-                    const float y = __fadd_rn(v, b);
-                    const int dm = g.H * g.hd, which = row / dm, c = row % dm, h = c / g.hd, t = c % g.hd;
-                    const int bi = n / g.S, jj = n % g.S;
-                    __half *cache = which == 0 ? g.kc : g.vc;
-                    cache[(((size_t)bi * g.H + h) * g.S + jj) * g.hd + t] = __float2half_rn(y);
-                } else if constexpr (EPI == EPI_ARGMAX) {
-                    if (g.logits) g.logits[(size_t)n * W.N + row] = v;
-                    const int slot = n >> 5;  // lane == n & 31
-                    argmax_merge(best_v[slot], best_i[slot], v, (uint32_t)row);
+                for (int i = 0; i < NB; ++i) {
+                    if (n0 + i >= g.rows) break;
+                    epilogue_store<EPI>(g, row, n0 + i, acc[i]);
                 }
-            }
-        }
-    }
-    if constexpr (EPI == EPI_ARGMAX) {
-        // Each lane tracked batch rows lane and lane + 32; merge across the CTA's warps.
-        __shared__ float sv[8][64];
-        __shared__ uint32_t si[8][64];
-        sv[warp][lane] = best_v[0];
-        si[warp][lane] = best_i[0];
-        sv[warp][lane + 32] = best_v[1];
-        si[warp][lane + 32] = best_i[1];
-        __syncthreads();
-        for (int n = threadIdx.x; n < g.rows; n += blockDim.x) {
-            float v = sv[0][n];
-            uint32_t i = si[0][n];
-            for (int w = 1; w < 8; ++w) argmax_merge(v, i, sv[w][n], si[w][n]);
-            g.part_v[(size_t)n * gridDim.x + blockIdx.x] = v;
-            g.part_i[(size_t)n * gridDim.x + blockIdx.x] = i;
         }
     }
 }
@@ -403,14 +413,47 @@ struct AttnArgs {
     int max_keys;
 };
 
-template <typename KV>
-__device__ __forceinline__ float load_kv(const KV *p) { return (float)*p; }
-template <>
-__device__ __forceinline__ float load_kv<__half>(const __half *p) { return __half2float(*p); }
+// Programmatic dependent launch: a kernel may start while its predecessor in
+// the stream is still running; everything before pdl_wait() must not read the
+// predecessor's outputs. Every CTA calls pdl_wait() before it exits, so a
+// kernel completes only after its predecessor did (the chain stays ordered).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
-template <typename KV>
+// HD values of a K/V row into registers (HD/8 16-byte loads for f16, HD/4 for f32).
+template <int HD>
+__device__ __forceinline__ void load_row(const __half *p, float (&v)[HD]) {
+#pragma unroll
+    for (int c = 0; c < HD / 8; ++c) {
+        const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(p) + c);
+        const __half2 *h2 = reinterpret_cast<const __half2 *>(&raw);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const float2 f = __half22float2(h2[u]);
+            v[8 * c + 2 * u] = f.x;
+            v[8 * c + 2 * u + 1] = f.y;
+        }
+    }
+}
+template <int HD>
+__device__ __forceinline__ void load_row(const float *p, float (&v)[HD]) {
+#pragma unroll
+    for (int c = 0; c < HD / 4; ++c) {
+        const float4 f = *(reinterpret_cast<const float4 *>(p) + c);
+        v[4 * c] = f.x;
+        v[4 * c + 1] = f.y;
+        v[4 * c + 2] = f.z;
+        v[4 * c + 3] = f.w;
+    }
+}
+__device__ __forceinline__ float load_kv(const __half *p) { return __half2float(*p); }
+__device__ __forceinline__ float load_kv(const float *p) { return *p; }
+
+template <typename KV, int HD>
 __global__ void __launch_bounds__(128) attend_kernel(AttnArgs a) {
     extern __shared__ float e_sh[];
+    pdl_launch_dependents();
+    pdl_wait();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const long task = (long)blockIdx.x * 4 + warp;
     const long total = (long)a.rows * a.H * a.queries;
@@ -418,14 +461,20 @@ __global__ void __launch_bounds__(128) attend_kernel(AttnArgs a) {
     const int qi = (int)(task % a.queries), h = (int)((task / a.queries) % a.H), n = (int)(task / ((long)a.queries * a.H));
     float *e = e_sh + (size_t)warp * a.max_keys;
     const int keys = a.lens ? (int)a.lens[n] : (int)(*a.step) + 1;
-    const float *q = a.q + (size_t)(n * (long)a.queries + qi) * a.q_row + h * a.hd;
+    const float *qp = a.q + (size_t)(n * (long)a.queries + qi) * a.q_row + h * HD;
+    float q[HD];
+#pragma unroll
+    for (int t = 0; t < HD; ++t) q[t] = qp[t];
     const KV *K = reinterpret_cast<const KV *>(a.K) + n * a.kv_batch + h * a.kv_head;
     const KV *V = reinterpret_cast<const KV *>(a.V) + n * a.kv_batch + h * a.kv_head;
+    // scores: FMA chain over the head dimension, one key per lane
     float mx = kNegInf;
     for (int j = lane; j < keys; j += 32) {
-        const KV *kr = K + (size_t)j * a.kv_row;
+        float k[HD];
+        load_row<HD>(K + (size_t)j * a.kv_row, k);
         float acc = 0.0f;
-        for (int t = 0; t < a.hd; ++t) acc = __fmaf_rn(q[t], load_kv(kr + t), acc);
+#pragma unroll
+        for (int t = 0; t < HD; ++t) acc = __fmaf_rn(q[t], k[t], acc);
         e[j] = acc;
         mx = fmaxf(mx, acc);
     }
@@ -438,11 +487,34 @@ __global__ void __launch_bounds__(128) attend_kernel(AttnArgs a) {
     }
     const float inv = __fdiv_rn(1.0f, warp_tree(s));
     __syncwarp();
-    float *o = a.out + (size_t)(n * (long)a.queries + qi) * a.out_row + h * a.hd;
-    for (int t = lane; t < a.hd; t += 32) {
-        float acc = 0.0f;
-        for (int j = 0; j < keys; ++j) acc = __fmaf_rn(e[j], load_kv(V + (size_t)j * a.kv_row + t), acc);
-        o[t] = __fmul_rn(acc, inv);
+    // outputs: FMA chain over keys; lane owns dims lane, lane+32, ... V rows are
+    // staged in shared memory 64 keys at a time (one memory round trip per chunk).
+    constexpr int PER = HD >= 32 ? HD / 32 : 1;
+    constexpr int KC = 64, VEC = 16 / sizeof(KV);  // keys per chunk, elements per 16-byte load
+    KV *vs = reinterpret_cast<KV *>(e_sh + (size_t)4 * a.max_keys) + (size_t)warp * KC * HD;
+    float acc[PER];
+#pragma unroll
+    for (int c = 0; c < PER; ++c) acc[c] = 0.0f;
+    const bool live = HD >= 32 || lane < HD;
+    for (int j0 = 0; j0 < keys; j0 += KC) {
+        const int nk = min(KC, keys - j0);
+        for (int u = lane; u < nk * (HD / VEC); u += 32) {
+            const int jr = u / (HD / VEC), cc = u % (HD / VEC);
+            reinterpret_cast<uint4 *>(vs)[u] =
+                __ldg(reinterpret_cast<const uint4 *>(V + (size_t)(j0 + jr) * a.kv_row) + cc);
+        }
+        __syncwarp();
+        if (live)
+            for (int jj = 0; jj < nk; ++jj)
+#pragma unroll
+                for (int c = 0; c < PER; ++c)
+                    acc[c] = __fmaf_rn(e[j0 + jj], load_kv(vs + (size_t)jj * HD + lane + 32 * c), acc[c]);
+        __syncwarp();
+    }
+    if (live) {
+        float *o = a.out + (size_t)(n * (long)a.queries + qi) * a.out_row + h * HD;
+#pragma unroll
+        for (int c = 0; c < PER; ++c) o[lane + 32 * c] = __fmul_rn(acc[c], inv);
     }
 }
 
@@ -452,6 +524,8 @@ __global__ void __launch_bounds__(128) attend_kernel(AttnArgs a) {
 __global__ void greedy_finalize_kernel(const float *pv, const uint32_t *pi, int parts, int rows, uint8_t *finished,
                                        uint32_t *ids, uint32_t *out, int m, uint32_t *step, uint32_t eos, uint32_t pad,
                                        int force) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const uint32_t s = *step;
     for (int row = w; row < rows; row += nw) {

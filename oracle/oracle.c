@@ -29,9 +29,9 @@
  *   SUM32(v[0..n))  lane l (0..31) sums v[l], v[l+32], ... left to right
  *                   (empty lane = 0), then pairs are added at distances
  *                   1,2,4,8,16 (acc[l] + acc[l^o]); the result is acc[0].
- *   ROW(p[0..nb))   per-block partials of a matmul row: nb<=32: lane l holds
- *                   p[l]; nb=32G: lane l sums p[lG..lG+G) left to right;
- *                   then the same pairwise steps 1..16.
+ *   ROW(p[0..nb))   per-block partials of a matmul row, summed left to right
+ *                   in block order (one accumulator per output: the shape a
+ *                   tensor-core epilogue can keep per (row, column)).
  *   exp             own implementation (Cody-Waite reduction with a 2-term
  *                   ln2 split, degree-7 Taylor polynomial in fmaf, exact 2^k
  *                   scaling); see mgb_exp.
@@ -149,25 +149,11 @@ static float sum32(const float *v, int n, int st) {
     return a[0];
 }
 
-/* ROW reduction of nb per-block partials. */
+/* ROW reduction of nb per-block partials: left to right in block order. */
 static float row_reduce(const float *p, int nb) {
-    float a[32];
-    if (nb <= 32) {
-        for (int l = 0; l < 32; ++l) a[l] = l < nb ? p[l] : 0.0f;
-    } else {
-        int G = nb / 32;
-        for (int l = 0; l < 32; ++l) {
-            float acc = p[l * G];
-            for (int t = 1; t < G; ++t) acc = acc + p[l * G + t];
-            a[l] = acc;
-        }
-    }
-    for (int o = 1; o < 32; o <<= 1) {
-        float b[32];
-        for (int l = 0; l < 32; ++l) b[l] = a[l] + a[l ^ o];
-        memcpy(a, b, sizeof a);
-    }
-    return a[0];
+    float acc = p[0];
+    for (int j = 1; j < nb; ++j) acc = acc + p[j];
+    return acc;
 }
 
 /* ------------------------------------------------------------------------ */
