@@ -28,7 +28,7 @@
 #include <vector>
 
 #include "../../include/malaga_b200.h"
-#include "fused.cuh"
+#include "gemm_tc.cuh"
 
 using namespace mgb;
 
@@ -224,6 +224,7 @@ struct StaticState {
     std::vector<__half *> kc, vc, ck, cv;
     float *part_v = nullptr;
     uint32_t *part_i = nullptr;
+    int lm_parts = 0;  // CTAs of the LM-head launch = argmax partials per row
     float *logits = nullptr;
     cudaGraphExec_t exec = nullptr;
     size_t graph_nodes = 0;
@@ -265,6 +266,9 @@ struct mgb_ctx {
     std::vector<std::unique_ptr<StaticState>> cache;
     size_t weight_bytes = 0, step_bytes = 0;
     uint32_t *d_err = nullptr;  // device-side error flags (a bounded wait ran out)
+    // Activation rows from which matmuls run on the tensor cores (tcgen05)
+    // instead of the small-batch kernels; MGB_TC_MIN_ROWS overrides (tests).
+    int tc_min_rows = 16;
 
     mgb_status dalloc(void **p, size_t bytes) {
         if (inject_armed && opts.fail_alloc_after >= 0 && alloc_count++ == opts.fail_alloc_after)
@@ -346,7 +350,7 @@ struct Planner {
         if (K % 32) return set_err(MGB_ERR_UNSUPPORTED, "tensor %s.weight: row length %ld", name.c_str(), K);
         M.type = t->type;
         M.N = (int)N;
-        M.Np = (int)((N + 31) / 32 * 32);
+        M.Np = (int)((N + 127) / 128 * 128);  // whole 128-row tensor-core tiles
         M.K = (int)K;
         M.nb = (int)(K / 32);
         M.nsb = (int)(K / 256);
@@ -761,6 +765,99 @@ static bool any_f32(const mgb_ctx *c) {
     return false;
 }
 
+// Tensor-core path: q8_1 activations of `rows` rows into `act` (one CTA per row).
+template <int MODE>
+static mgb_status qprep_row(mgb_ctx *c, const PrepArgs &p, const QAct &act) {
+    auto kern = qprep_row_kernel<MODE>;
+    const size_t sh = (size_t)p.K * 4;
+    cudaError_t e = allow_smem(kern, sh);
+    if (e == cudaSuccess) e = launch_pdl(kern, dim3(p.rows), dim3(256), sh, c->stream, p, act);
+    ++c->launches;
+    return e == cudaSuccess ? MGB_OK : cuda_err(e, "activation prep launch");
+}
+
+// Tile width (activation rows per tile) and grid of a tensor-core matmul:
+// the widest tile that still gives every SM work, persistent CTAs.
+static void tc_shape(const Matrix &W, int rows, int &nt, int &grid) {
+    const int row_tiles = (W.Np + 127) / 128;
+    nt = 8;
+    for (int cand : {64, 32, 16}) {
+        if ((long)row_tiles * ((rows + cand - 1) / cand) >= 148) {
+            nt = cand;
+            break;
+        }
+    }
+    const long tiles = (long)row_tiles * ((rows + nt - 1) / nt);
+    grid = (int)std::min<long>(tiles, 2 * 148);  // two CTAs per SM (256 TMEM columns each)
+}
+
+template <int TYPE, int EPI>
+static mgb_status gemm_tc_t(mgb_ctx *c, tc::Args a, int nt, int grid) {
+    auto go = [&](auto kern, size_t sh) -> cudaError_t {
+        cudaError_t e = allow_smem(kern, sh);
+        return e == cudaSuccess ? launch_pdl(kern, dim3(grid), dim3(128), sh, c->stream, a) : e;
+    };
+    cudaError_t e;
+    switch (nt) {
+        case 8: e = go(gemm_tc_kernel<TYPE, EPI, 8>, gemm_tc_smem<TYPE, 8>()); break;
+        case 16: e = go(gemm_tc_kernel<TYPE, EPI, 16>, gemm_tc_smem<TYPE, 16>()); break;
+        case 32: e = go(gemm_tc_kernel<TYPE, EPI, 32>, gemm_tc_smem<TYPE, 32>()); break;
+        default: e = go(gemm_tc_kernel<TYPE, EPI, 64>, gemm_tc_smem<TYPE, 64>()); break;
+    }
+    ++c->launches;
+    return e == cudaSuccess ? MGB_OK : cuda_err(e, "tensor-core matmul launch");
+}
+
+// y = W . act for `rows` activation rows on the tensor cores, epilogue EPI.
+// Returns the number of CTAs launched in *ctas (the LM head's partial count).
+template <int EPI>
+static mgb_status gemm_tc(mgb_ctx *c, const Matrix &W, const QAct &act, int rows, const GemvArgs &g,
+                          int *ctas = nullptr) {
+    tc::Args a{};
+    a.W = W;
+    a.x = act;
+    a.x.rows = rows;
+    a.x.K = W.K;
+    a.rows = rows;
+    a.g = g;
+    a.g.W = W;
+    a.g.rows = rows;
+    a.err = c->d_err;
+    int nt, grid;
+    tc_shape(W, rows, nt, grid);
+    a.row_tiles = (W.Np + 127) / 128;
+    a.tok_tiles = (rows + nt - 1) / nt;
+    if (ctas) *ctas = grid;
+    switch (W.type) {
+        case T_Q8_0: return gemm_tc_t<T_Q8_0, EPI>(c, a, nt, grid);
+        case T_Q4_K: return gemm_tc_t<T_Q4_K, EPI>(c, a, nt, grid);
+        case T_Q6_K: return gemm_tc_t<T_Q6_K, EPI>(c, a, nt, grid);
+    }
+    return set_err(MGB_ERR_UNSUPPORTED, "tensor-core matmul of type %d", W.type);
+}
+
+static bool tc_ok(const Matrix &W) { return W.type == T_Q8_0 || W.type == T_Q4_K || W.type == T_Q6_K; }
+
+// q8_1 activation buffers of the tensor-core path: rows padded to 64, scales
+// also block-major.
+static mgb_status alloc_tc_act(mgb_ctx *c, int rows, int kmax, QAct &a, std::vector<void *> &allocs, size_t *bytes) {
+    const int rp = (rows + 63) / 64 * 64, nbm = kmax / 32;
+    auto A = [&](void **p, size_t n) -> mgb_status {
+        TRY(c->dalloc(p, n));
+        allocs.push_back(*p);
+        if (bytes) *bytes += n;
+        return MGB_OK;
+    };
+    TRY(A((void **)&a.q, (size_t)rp * kmax));
+    TRY(A((void **)&a.d, (size_t)4 * rp * nbm));
+    TRY(A((void **)&a.s32, (size_t)4 * rp * nbm));
+    TRY(A((void **)&a.s16, (size_t)8 * rp * nbm));
+    TRY(A((void **)&a.dT, (size_t)4 * rp * nbm));
+    TRY(A((void **)&a.sT, (size_t)4 * rp * nbm));
+    a.rs = rp;
+    return MGB_OK;
+}
+
 // ---------------------------------------------------------------------------
 // Static state (graph.rs:23-135)
 
@@ -808,8 +905,24 @@ static mgb_status new_state(mgb_ctx *c, int b, int s, int m, StaticState **out) 
     }
     TRY(A((void **)&st->part_v, (size_t)4 * b * kLmParts));
     TRY(A((void **)&st->part_i, (size_t)4 * b * kLmParts));
+    if (b >= c->tc_min_rows) TRY(alloc_tc_act(c, b, std::max(d, g.dec_ffn), st->act, st->allocs, &st->bytes));
     *out = st.release();
     return MGB_OK;
+}
+
+// One matmul of the step: tensor cores (activation prep kernel + tcgen05
+// matmul) from tc_min_rows rows, otherwise the fused small-batch kernel.
+template <int EPI, int MODE>
+static mgb_status step_op(mgb_ctx *c, StaticState *st, const FusedArgs &f, int *ctas = nullptr) {
+    const int b = f.g.rows;
+    if (b >= c->tc_min_rows && tc_ok(f.g.W) && st->act.q) {
+        PrepArgs p = f.p;
+        p.rows = b;
+        TRY(qprep_row<MODE>(c, p, st->act));
+        return gemm_tc<EPI>(c, f.g.W, st->act, b, f.g, ctas);
+    }
+    if (ctas) *ctas = kLmParts;
+    return fused<EPI, MODE>(c, f);
 }
 
 // One greedy decoder step on the state's fixed buffers (model.rs:552-612):
@@ -855,9 +968,9 @@ static mgb_status launch_step(mgb_ctx *c, StaticState *st, float *logits, int fo
             fq.p.pos_table = c->pos;
             fq.p.pos_base = (uint32_t)g.pad + 1;
             fq.p.scale = c->embed_scale;
-            TRY((fused<EPI_QKV, PREP_EMBED_LN>(c, fq)));
+            TRY((step_op<EPI_QKV, PREP_EMBED_LN>(c, st, fq)));
         } else {
-            TRY((fused<EPI_QKV, PREP_LN>(c, fq)));
+            TRY((step_op<EPI_QKV, PREP_LN>(c, st, fq)));
         }
         AttnArgs sa{};
         sa.q = st->q;
@@ -879,12 +992,12 @@ static mgb_status launch_step(mgb_ctx *c, StaticState *st, float *logits, int fo
         FusedArgs fo = mm(L.out);
         fo.p = src(st->a, d, nullptr);
         fo.g.y = st->x;
-        TRY((fused<EPI_RESID, PREP_PLAIN>(c, fo)));
+        TRY((step_op<EPI_RESID, PREP_PLAIN>(c, st, fo)));
         // cross_norm -> cross_q -> cross attention -> cross_out + residual
         FusedArgs fc = mm(L.cq);
         fc.p = src(st->x, d, &L.cross_norm);
         fc.g.y = st->q;
-        TRY((fused<EPI_STORE, PREP_LN>(c, fc)));
+        TRY((step_op<EPI_STORE, PREP_LN>(c, st, fc)));
         AttnArgs ca = sa;
         ca.K = st->ck[l];
         ca.V = st->cv[l];
@@ -897,16 +1010,16 @@ static mgb_status launch_step(mgb_ctx *c, StaticState *st, float *logits, int fo
         FusedArgs fco = mm(L.co);
         fco.p = src(st->a, d, nullptr);
         fco.g.y = st->x;
-        TRY((fused<EPI_RESID, PREP_PLAIN>(c, fco)));
+        TRY((step_op<EPI_RESID, PREP_PLAIN>(c, st, fco)));
         // ffn_norm -> up + ReLU -> down + residual
         FusedArgs fu = mm(L.up);
         fu.p = src(st->x, d, &L.ffn_norm);
         fu.g.y = st->u;
-        TRY((fused<EPI_RELU, PREP_LN>(c, fu)));
+        TRY((step_op<EPI_RELU, PREP_LN>(c, st, fu)));
         FusedArgs fd = mm(L.down);
         fd.p = src(st->u, g.dec_ffn, nullptr);
         fd.g.y = st->x;
-        TRY((fused<EPI_RESID, PREP_PLAIN>(c, fd)));
+        TRY((step_op<EPI_RESID, PREP_PLAIN>(c, st, fd)));
     }
     // dec_norm -> tied LM head fused with the first argmax pass -> greedy bookkeeping
     FusedArgs fl = mm(c->embed);
@@ -915,11 +1028,13 @@ static mgb_status launch_step(mgb_ctx *c, StaticState *st, float *logits, int fo
     fl.g.part_i = st->part_i;
     fl.g.logits = logits;
     if (lm0) CK(cudaEventRecord(lm0, c->stream));
-    TRY((fused<EPI_ARGMAX, PREP_LN>(c, fl)));
+    int parts = kLmParts;
+    TRY((step_op<EPI_ARGMAX, PREP_LN>(c, st, fl, &parts)));
+    st->lm_parts = parts;
     if (lm1) CK(cudaEventRecord(lm1, c->stream));
     const int threads = std::min(1024, std::max(32, 32 * b));
     cudaError_t e = launch_pdl(greedy_finalize_kernel, dim3(1), dim3(threads), 0, c->stream,
-                               (const float *)st->part_v, (const uint32_t *)st->part_i, (int)kLmParts, b,
+                               (const float *)st->part_v, (const uint32_t *)st->part_i, parts, b,
                                st->finished, st->ids, st->out, st->m, st->step, (uint32_t)g.eos, (uint32_t)g.pad,
                                force);
     ++c->launches;
@@ -956,25 +1071,38 @@ static mgb_status encode(mgb_ctx *c, const uint32_t *ids, const uint32_t *lens, 
     TRY(A((void **)&u, (size_t)4 * rows * ffn));
     const bool f32 = any_f32(c);
     if (f32) TRY(A((void **)&xf, (size_t)4 * rows * kmax));
-    TRY(A((void **)&act.q, (size_t)rows * kmax));
-    TRY(A((void **)&act.d, (size_t)4 * rows * kmax / 32));
-    TRY(A((void **)&act.s32, (size_t)4 * rows * kmax / 32));
-    TRY(A((void **)&act.s16, (size_t)4 * rows * kmax / 16));
+    TRY(alloc_tc_act(c, rows, kmax, act, tmp, nullptr));
     CK(cudaMemcpyAsync(d_ids, ids, (size_t)4 * rows, cudaMemcpyHostToDevice, c->stream));
     CK(cudaMemcpyAsync(d_lens, lens, (size_t)4 * b, cudaMemcpyHostToDevice, c->stream));
     TRY(launch_check(c, [&] {
         embed_tokens_kernel<<<(rows + 7) / 8, 256, 0, c->stream>>>(c->embed, d_ids, d_lens, S, rows, c->pos,
                                                                    (uint32_t)g.pad, c->embed_scale, x);
     }));
+    // One encoder matmul: tensor cores for quantized weights, else the
+    // row-per-lane kernel over activations quantized in global memory.
+    auto enc_mm = [&](int epi, int mode, const Matrix &W, const float *in, const Norm *nrm, GemvArgs gg) -> mgb_status {
+        PrepArgs p = prep_args(act, xf, f32, in, rows, W.K);
+        if (nrm) {
+            p.gamma = nrm->g;
+            p.beta = nrm->b;
+        }
+        if (tc_ok(W)) {
+            TRY(mode == PREP_LN ? qprep_row<PREP_LN>(c, p, act) : qprep_row<PREP_PLAIN>(c, p, act));
+            switch (epi) {
+                case EPI_STORE: return gemm_tc<EPI_STORE>(c, W, act, rows, gg);
+                case EPI_RELU: return gemm_tc<EPI_RELU>(c, W, act, rows, gg);
+                case EPI_RESID: return gemm_tc<EPI_RESID>(c, W, act, rows, gg);
+                default: return gemm_tc<EPI_CROSSKV>(c, W, act, rows, gg);
+            }
+        }
+        TRY(qprep(c, mode, p));
+        return gemv(c, epi, gg);
+    };
     for (int l = 0; l < g.enc_layers; ++l) {
         const EncLayer &L = c->enc[l];
-        PrepArgs p = prep_args(act, xf, f32, x, rows, d);
-        p.gamma = L.attn_norm.g;
-        p.beta = L.attn_norm.b;
-        TRY(qprep(c, PREP_LN, p));
         GemvArgs gq = gemv_args(L.qkv, act, xf, rows);
         gq.y = qkv;
-        TRY(gemv(c, EPI_STORE, gq));
+        TRY(enc_mm(EPI_STORE, PREP_LN, L.qkv, x, &L.attn_norm, gq));
         AttnArgs at{};
         at.q = qkv;
         at.q_row = 3 * d;
@@ -992,26 +1120,22 @@ static mgb_status encode(mgb_ctx *c, const uint32_t *ids, const uint32_t *lens, 
         at.queries = S;
         at.max_keys = S;
         TRY(attend<float>(c, at));
-        TRY(qprep(c, PREP_PLAIN, prep_args(act, xf, f32, a, rows, d)));
         GemvArgs go = gemv_args(L.out, act, xf, rows);
         go.y = x;
-        TRY(gemv(c, EPI_RESID, go));
-        p = prep_args(act, xf, f32, x, rows, d);
-        p.gamma = L.ffn_norm.g;
-        p.beta = L.ffn_norm.b;
-        TRY(qprep(c, PREP_LN, p));
+        TRY(enc_mm(EPI_RESID, PREP_PLAIN, L.out, a, nullptr, go));
         GemvArgs gu = gemv_args(L.up, act, xf, rows);
         gu.y = u;
-        TRY(gemv(c, EPI_RELU, gu));
-        TRY(qprep(c, PREP_PLAIN, prep_args(act, xf, f32, u, rows, ffn)));
+        TRY(enc_mm(EPI_RELU, PREP_LN, L.up, x, &L.ffn_norm, gu));
         GemvArgs gd = gemv_args(L.down, act, xf, rows);
         gd.y = x;
-        TRY(gemv(c, EPI_RESID, gd));
+        TRY(enc_mm(EPI_RESID, PREP_PLAIN, L.down, u, nullptr, gd));
     }
-    PrepArgs p = prep_args(act, xf, f32, x, rows, d);
-    p.gamma = c->enc_norm.g;
-    p.beta = c->enc_norm.b;
-    TRY(qprep(c, PREP_LN, p));
+    // enc_norm(x) is the input of every decoder layer's cross K/V projection
+    PrepArgs pn = prep_args(act, xf, f32, x, rows, d);
+    pn.gamma = c->enc_norm.g;
+    pn.beta = c->enc_norm.b;
+    const bool kv_tc = tc_ok(c->dec[0].ckv);
+    TRY(kv_tc ? qprep_row<PREP_LN>(c, pn, act) : qprep(c, PREP_LN, pn));
     auto B = std::make_unique<mgb_batch>();
     B->b = b;
     B->s = S;
@@ -1036,7 +1160,8 @@ static mgb_status encode(mgb_ctx *c, const uint32_t *ids, const uint32_t *lens, 
         gk.H = Hd;
         gk.hd = hdd;
         gk.S = S;
-        mgb_status s2 = gemv(c, EPI_CROSSKV, gk);
+        mgb_status s2 = tc_ok(c->dec[l].ckv) ? gemm_tc<EPI_CROSSKV>(c, c->dec[l].ckv, act, rows, gk)
+                                             : gemv(c, EPI_CROSSKV, gk);
         if (s2 != MGB_OK) {
             cudaFree(B->cross);
             cudaFree(B->d_lens);
@@ -1242,6 +1367,7 @@ mgb_status mgb_open(const char *path, int device, const mgb_options *opts, mgb_c
     if (opts) c->opts = *opts;
     else mgb_default_options(&c->opts);
     CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+    if (const char *v = getenv("MGB_TC_MIN_ROWS")) c->tc_min_rows = std::max(1, atoi(v));
     mgb_status s = load_model(c.get(), path);
     if (s != MGB_OK) {
         if (c->arena) cudaFree(c->arena);

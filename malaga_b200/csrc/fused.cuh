@@ -333,7 +333,13 @@ namespace mgb {
 // the K blocks (lane = row) and write the block partials p[n][j][row] to shared
 // memory; then each row's partials are summed left to right in block order.
 
-constexpr uint32_t kWaitLimit = 1u << 26;  // mbarrier polls before giving up
+constexpr uint64_t kWaitNs = 500000000ull;  // give up a wait after 0.5 s of device time
+
+__device__ __forceinline__ uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return (uint32_t)__cvta_generic_to_shared(p);
@@ -355,21 +361,27 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
                  : "memory");
 }
 
-// Bounded wait for phase `parity` of the mbarrier; false if the limit ran out.
+__device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Bounded wait for phase `parity` of the mbarrier; false once kWaitNs passed.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
     const uint32_t a = smem_u32(bar);
-    for (uint32_t it = 0; it < kWaitLimit; ++it) {
-        uint32_t done;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(done)
-            : "r"(a), "r"(parity)
-            : "memory");
-        if (done) return true;
+    if (mbar_try(a, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try(a, parity)) return true;
+        if ((it & 255) == 0 && globaltimer() - t0 > kWaitNs) return false;
     }
-    return false;
 }
 
 // Shared-memory bytes of one group's staged weights (each region 16-B aligned).

@@ -177,3 +177,38 @@ def test_600m_q4_k_m_b1_config1_prefix_bit_exact(gpu, model):
     got_ids, got_logits = eng.greedy_logits(eng.encode(w.sources), models.TGT_TAG, 3, force=True)
     np.testing.assert_array_equal(got_ids, want_ids)
     assert np.array_equal(got_logits.view(np.uint32), want_logits.view(np.uint32))
+
+
+@pytest.mark.parametrize("name,preset,b", [("mid", "q4_k_m", 64), ("mid", "q8_0", 24), ("wide", "q8_0", 64),
+                                           ("wide", "q4_k_m", 40)])
+def test_tensor_core_batches_bit_exact(gpu, model, name, preset, b):
+    """Batches of 16+ rows run the tcgen05 matmuls (and the encoder always does for
+    quantized weights): tokens and logits equal the oracle's bit for bit."""
+    path = model(name, preset)
+    V = models.config_of(name).vocab_size
+    src = models.random_sources(b, 2, 10, V, 11, src_tag=V - 1)
+    orc = oracle.Oracle(path)
+    want_ids, want_logits = orc.greedy(src, V - 2, 3, force=True, logits=True)
+    eng = Engine(path)
+    got_ids, got_logits = eng.greedy_logits(eng.encode(src), V - 2, 3, force=True)
+    np.testing.assert_array_equal(got_ids, want_ids)
+    assert np.array_equal(got_logits.view(np.uint32), want_logits.view(np.uint32)), \
+        f"max |diff| {np.abs(got_logits - want_logits).max()}"
+
+
+@pytest.mark.parametrize("preset", ["q4_k_m", "q8_0"])
+def test_tensor_core_equals_small_batch_kernels(gpu, model, preset, monkeypatch):
+    """The same small batch through the tcgen05 path (forced from 1 row) and the
+    small-batch kernels: identical logits, graph replay included."""
+    path = model("mid", preset)
+    V = models.config_of("mid").vocab_size
+    src = models.random_sources(5, 3, 14, V, 12, src_tag=V - 1)
+    eng = Engine(path)
+    ids_a, lg_a = eng.greedy_logits(eng.encode(src), V - 2, 4, force=True)
+    monkeypatch.setenv("MGB_TC_MIN_ROWS", "1")
+    eng_tc = Engine(path)
+    ids_b, lg_b = eng_tc.greedy_logits(eng_tc.encode(src), V - 2, 4, force=True)
+    np.testing.assert_array_equal(ids_a, ids_b)
+    assert np.array_equal(lg_a.view(np.uint32), lg_b.view(np.uint32))
+    out, _ = eng_tc.greedy(eng_tc.encode(src), V - 2, 4, force=True)
+    np.testing.assert_array_equal(out, ids_a)
