@@ -25,6 +25,8 @@ NVCC_FLAGS = [
     "-fmad=false", "-prec-div=true", "-prec-sqrt=true",
     "-Xcompiler", "-fPIC,-fopenmp,-fvisibility=hidden",
     "-shared", "-lgomp",
+    # device code of the many kernel instantiations is optimized in parallel
+    "--split-compile=0",
 ]
 ENGINE_SOURCES = ["engine.cu", "noalloc.cu"]
 

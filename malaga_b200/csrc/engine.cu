@@ -269,6 +269,7 @@ struct mgb_ctx {
     // Activation rows from which matmuls run on the tensor cores (tcgen05)
     // instead of the small-batch kernels; MGB_TC_MIN_ROWS overrides (tests).
     int tc_min_rows = 16;
+    int sms = 148;  // multiprocessor count of the device (one tensor-core CTA each)
 
     mgb_status dalloc(void **p, size_t bytes) {
         if (inject_armed && opts.fail_alloc_after >= 0 && alloc_count++ == opts.fail_alloc_after)
@@ -663,7 +664,7 @@ static mgb_status fused_t(mgb_ctx *c, FusedArgs fa) {
     const int B = fa.g.rows;
     const bool f32 = TYPE == T_F32;
     if constexpr (TYPE != T_F32 && EPI != EPI_ARGMAX) {
-        const size_t sh = staged_bytes(TYPE, W.nb, W.nsb) + smact_bytes(B, W.K, false) + (size_t)B * W.nb * 32 * 4;
+        const size_t sh = staged_bytes(TYPE, W.nb, W.nsb) + smact_bytes(B, W.K, false) + staged_partial_bytes(TYPE, B, W.nb);
         if (B <= 8 && sh <= 200 * 1024) {
             auto kern = gemv_staged_kernel<TYPE, EPI, MODE>;
             cudaError_t e = allow_smem(kern, sh);
@@ -765,37 +766,126 @@ static bool any_f32(const mgb_ctx *c) {
     return false;
 }
 
-// Tensor-core path: q8_1 activations of `rows` rows into `act` (one CTA per row).
+// Tensor-core path: activations of `rows` rows into `act` in the layout of the
+// consuming matrix W (one CTA per row).
 template <int MODE>
-static mgb_status qprep_row(mgb_ctx *c, const PrepArgs &p, const QAct &act) {
+static mgb_status qprep_row(mgb_ctx *c, PrepArgs p, const QAct &act, const Matrix &W) {
     auto kern = qprep_row_kernel<MODE>;
-    const size_t sh = (size_t)p.K * 4;
+    p.group = act_group(W.type);
+    p.ctype = W.type;
+    const size_t sh = (size_t)p.K * 5 + (size_t)(p.K / 32) * 16;
     cudaError_t e = allow_smem(kern, sh);
     if (e == cudaSuccess) e = launch_pdl(kern, dim3(p.rows), dim3(256), sh, c->stream, p, act);
     ++c->launches;
     return e == cudaSuccess ? MGB_OK : cuda_err(e, "activation prep launch");
 }
 
-// Tile width (activation rows per tile) and grid of a tensor-core matmul:
-// the widest tile that still gives every SM work, persistent CTAs.
-static void tc_shape(const Matrix &W, int rows, int &nt, int &grid) {
-    const int row_tiles = (W.Np + 127) / 128;
+// Tile width (activation rows per tile) of a tensor-core matmul: the widest
+// tile that still gives every SM a tile; persistent CTAs, one per SM.
+static void tc_shape(const Matrix &W, int rows, int sms, int &nt, int &grid) {
+    const int row_tiles = W.Np / 128;
     nt = 8;
     for (int cand : {64, 32, 16}) {
-        if ((long)row_tiles * ((rows + cand - 1) / cand) >= 148) {
+        if ((long)row_tiles * ((rows + cand - 1) / cand) >= sms) {
             nt = cand;
             break;
         }
     }
     const long tiles = (long)row_tiles * ((rows + nt - 1) / nt);
-    grid = (int)std::min<long>(tiles, 2 * 148);  // two CTAs per SM (256 TMEM columns each)
+    grid = (int)std::min<long>(tiles, sms);
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn)p;
+    });
+    return fn;
+}
+
+// A tensor map of 8-byte words: dims[0] innermost; strides in bytes for dims 1..
+static mgb_status tmap(CUtensorMap *m, const void *base, int rank, const uint64_t *dims, const uint64_t *strides,
+                       const uint32_t *box, bool weights) {
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn) return set_err(MGB_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+    cuuint64_t gd[4], gs[3];
+    cuuint32_t bx[4], es[4];
+    for (int i = 0; i < rank; ++i) {
+        gd[i] = dims[i];
+        bx[i] = box[i];
+        es[i] = 1;
+        if (i) gs[i - 1] = strides[i - 1];
+    }
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, (cuuint32_t)rank, const_cast<void *>(base), gd, gs, bx, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                    weights ? CU_TENSOR_MAP_L2_PROMOTION_L2_256B : CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_err(MGB_ERR_CUDA, "tensor map encoding failed (%d)", (int)r);
+    return MGB_OK;
+}
+
+// The launch's tensor maps (layouts: engine.h Matrix, gemm_tc.cuh tc::Maps).
+static mgb_status make_maps(const Matrix &W, const QAct &x, int nt, tc::Maps &m) {
+    memset(&m, 0, sizeof m);
+    const uint64_t G = (uint64_t)W.Np / 32, nb = W.nb, nsb = W.nsb;
+    // one weight region: X words per (group, block-or-super-block) slice, n slices, boxes of k slices
+    auto region = [&](CUtensorMap *mp, const uint8_t *base, uint64_t X, uint64_t n, uint32_t k) -> mgb_status {
+        const uint64_t dims[3] = {X, n, G}, str[2] = {X * 8, X * 8 * n};
+        const uint32_t box[3] = {(uint32_t)X, k, 4};
+        return tmap(mp, base, 3, dims, str, box, true);
+    };
+    switch (W.type) {
+        case T_Q8_0:
+            TRY(region(&m.w[0], W.a, 128, nb, 8));
+            TRY(region(&m.w[1], W.b, 8, nb, 8));
+            break;
+        case T_Q4_K:
+            TRY(region(&m.w[0], W.a, 64, nb, 8));
+            TRY(region(&m.w[1], W.b, 64, nsb, 1));
+            break;
+        case T_Q6_K:
+            TRY(region(&m.w[0], W.a, 64, nb, 8));
+            TRY(region(&m.w[1], W.b, 32, nb, 8));
+            TRY(region(&m.w[2], W.c, 8, nb, 8));
+            TRY(region(&m.w[3], W.e, 8, nsb, 1));
+            break;
+        default:
+            return set_err(MGB_ERR_UNSUPPORTED, "tensor-core matmul of type %d", W.type);
+    }
+    const uint64_t rs = (uint64_t)x.rs, H = W.type == T_Q6_K ? 2 : 1;
+    {
+        const uint64_t dims[4] = {32, rs / 8, H, nb}, str[3] = {256, rs * 32, H * rs * 32};
+        const uint32_t box[4] = {32, (uint32_t)nt / 8, (uint32_t)H, 8};
+        TRY(tmap(&m.xq, x.tq, 4, dims, str, box, false));
+    }
+    if (W.type == T_Q4_K) {
+        const uint64_t dims[2] = {rs * 4, nsb}, str[1] = {rs * 32};
+        const uint32_t box[2] = {(uint32_t)nt * 4, 1};
+        TRY(tmap(&m.xr, x.trec, 2, dims, str, box, false));
+    } else {
+        const uint64_t units = W.type == T_Q6_K ? nsb : nb;
+        const uint64_t dims[2] = {rs / 2, units}, str[1] = {rs * 4};
+        const uint32_t box[2] = {(uint32_t)nt / 2, W.type == T_Q6_K ? 1u : 8u};
+        TRY(tmap(&m.xr, x.trec, 2, dims, str, box, false));
+    }
+    return MGB_OK;
 }
 
 template <int TYPE, int EPI>
-static mgb_status gemm_tc_t(mgb_ctx *c, tc::Args a, int nt, int grid) {
+static mgb_status gemm_tc_t(mgb_ctx *c, const tc::Args &a, int nt, int grid) {
     auto go = [&](auto kern, size_t sh) -> cudaError_t {
         cudaError_t e = allow_smem(kern, sh);
-        return e == cudaSuccess ? launch_pdl(kern, dim3(grid), dim3(128), sh, c->stream, a) : e;
+        return e == cudaSuccess ? launch_pdl(kern, dim3(grid), dim3(tc::kThreads), sh, c->stream, a) : e;
     };
     cudaError_t e;
     switch (nt) {
@@ -809,52 +899,67 @@ static mgb_status gemm_tc_t(mgb_ctx *c, tc::Args a, int nt, int grid) {
 }
 
 // y = W . act for `rows` activation rows on the tensor cores, epilogue EPI.
-// Returns the number of CTAs launched in *ctas (the LM head's partial count).
+// The LM head (ARGMAX) runs in launches of at most 64 rows (one token tile
+// each); *ctas returns its CTA count, the partial count per row.
 template <int EPI>
 static mgb_status gemm_tc(mgb_ctx *c, const Matrix &W, const QAct &act, int rows, const GemvArgs &g,
                           int *ctas = nullptr) {
-    tc::Args a{};
-    a.W = W;
-    a.x = act;
-    a.x.rows = rows;
-    a.x.K = W.K;
-    a.rows = rows;
-    a.g = g;
-    a.g.W = W;
-    a.g.rows = rows;
-    a.err = c->d_err;
-    int nt, grid;
-    tc_shape(W, rows, nt, grid);
-    a.row_tiles = (W.Np + 127) / 128;
-    a.tok_tiles = (rows + nt - 1) / nt;
-    if (ctas) *ctas = grid;
-    switch (W.type) {
-        case T_Q8_0: return gemm_tc_t<T_Q8_0, EPI>(c, a, nt, grid);
-        case T_Q4_K: return gemm_tc_t<T_Q4_K, EPI>(c, a, nt, grid);
-        case T_Q6_K: return gemm_tc_t<T_Q6_K, EPI>(c, a, nt, grid);
+    const int chunk = EPI == EPI_ARGMAX ? 64 : rows;
+    for (int t0 = 0; t0 < rows; t0 += chunk) {
+        const int n = std::min(chunk, rows - t0);
+        tc::Args a;
+        memset(&a, 0, sizeof a);
+        a.W = W;
+        a.rows = n;
+        a.tok0 = t0;
+        a.g = g;
+        a.g.W = W;
+        a.g.rows = n;
+        a.err = c->d_err;
+        int nt, grid;
+        tc_shape(W, n, c->sms, nt, grid);
+        if (EPI == EPI_ARGMAX) {
+            if (a.g.logits) a.g.logits += (size_t)t0 * W.N;
+            a.g.part_v += (size_t)t0 * grid;
+            a.g.part_i += (size_t)t0 * grid;
+        }
+        a.row_tiles = W.Np / 128;
+        a.tok_tiles = (n + nt - 1) / nt;
+        if (ctas) *ctas = grid;
+        TRY(make_maps(W, act, nt, a.m));
+        switch (W.type) {
+            case T_Q8_0: TRY((gemm_tc_t<T_Q8_0, EPI>(c, a, nt, grid))); break;
+            case T_Q4_K: TRY((gemm_tc_t<T_Q4_K, EPI>(c, a, nt, grid))); break;
+            case T_Q6_K: TRY((gemm_tc_t<T_Q6_K, EPI>(c, a, nt, grid))); break;
+            default: return set_err(MGB_ERR_UNSUPPORTED, "tensor-core matmul of type %d", W.type);
+        }
     }
-    return set_err(MGB_ERR_UNSUPPORTED, "tensor-core matmul of type %d", W.type);
+    return MGB_OK;
 }
 
 static bool tc_ok(const Matrix &W) { return W.type == T_Q8_0 || W.type == T_Q4_K || W.type == T_Q6_K; }
 
-// q8_1 activation buffers of the tensor-core path: rows padded to 64, scales
-// also block-major.
+// Activation buffers: the tensor-core layout (rows padded to 64; tiles for up
+// to two copies per block for Q6_K consumers, records for the largest unit
+// count) and the row-major q8 arrays of the other matmul kernels.
 static mgb_status alloc_tc_act(mgb_ctx *c, int rows, int kmax, QAct &a, std::vector<void *> &allocs, size_t *bytes) {
     const int rp = (rows + 63) / 64 * 64, nbm = kmax / 32;
     auto A = [&](void **p, size_t n) -> mgb_status {
         TRY(c->dalloc(p, n));
         allocs.push_back(*p);
         if (bytes) *bytes += n;
+        CK(cudaMemsetAsync(*p, 0, n, c->stream));
         return MGB_OK;
     };
+    const size_t rec = std::max((size_t)(nbm / 8) * rp * 32, (size_t)nbm * rp * 4);
+    TRY(A((void **)&a.tq, (size_t)nbm * 2 * rp * 32));
+    TRY(A((void **)&a.trec, rec));
+    a.rs = rp;
+    // row-major q8 activations of the other matmul kernels (F32 and encoder fallbacks)
     TRY(A((void **)&a.q, (size_t)rp * kmax));
     TRY(A((void **)&a.d, (size_t)4 * rp * nbm));
     TRY(A((void **)&a.s32, (size_t)4 * rp * nbm));
     TRY(A((void **)&a.s16, (size_t)8 * rp * nbm));
-    TRY(A((void **)&a.dT, (size_t)4 * rp * nbm));
-    TRY(A((void **)&a.sT, (size_t)4 * rp * nbm));
-    a.rs = rp;
     return MGB_OK;
 }
 
@@ -915,10 +1020,10 @@ static mgb_status new_state(mgb_ctx *c, int b, int s, int m, StaticState **out) 
 template <int EPI, int MODE>
 static mgb_status step_op(mgb_ctx *c, StaticState *st, const FusedArgs &f, int *ctas = nullptr) {
     const int b = f.g.rows;
-    if (b >= c->tc_min_rows && tc_ok(f.g.W) && st->act.q) {
+    if (b >= c->tc_min_rows && tc_ok(f.g.W) && st->act.tq) {
         PrepArgs p = f.p;
         p.rows = b;
-        TRY(qprep_row<MODE>(c, p, st->act));
+        TRY(qprep_row<MODE>(c, p, st->act, f.g.W));
         return gemm_tc<EPI>(c, f.g.W, st->act, b, f.g, ctas);
     }
     if (ctas) *ctas = kLmParts;
@@ -1087,7 +1192,7 @@ static mgb_status encode(mgb_ctx *c, const uint32_t *ids, const uint32_t *lens, 
             p.beta = nrm->b;
         }
         if (tc_ok(W)) {
-            TRY(mode == PREP_LN ? qprep_row<PREP_LN>(c, p, act) : qprep_row<PREP_PLAIN>(c, p, act));
+            TRY(mode == PREP_LN ? qprep_row<PREP_LN>(c, p, act, W) : qprep_row<PREP_PLAIN>(c, p, act, W));
             switch (epi) {
                 case EPI_STORE: return gemm_tc<EPI_STORE>(c, W, act, rows, gg);
                 case EPI_RELU: return gemm_tc<EPI_RELU>(c, W, act, rows, gg);
@@ -1095,6 +1200,7 @@ static mgb_status encode(mgb_ctx *c, const uint32_t *ids, const uint32_t *lens, 
                 default: return gemm_tc<EPI_CROSSKV>(c, W, act, rows, gg);
             }
         }
+        p.group = act_group(W.type);
         TRY(qprep(c, mode, p));
         return gemv(c, epi, gg);
     };
@@ -1135,7 +1241,8 @@ static mgb_status encode(mgb_ctx *c, const uint32_t *ids, const uint32_t *lens, 
     pn.gamma = c->enc_norm.g;
     pn.beta = c->enc_norm.b;
     const bool kv_tc = tc_ok(c->dec[0].ckv);
-    TRY(kv_tc ? qprep_row<PREP_LN>(c, pn, act) : qprep(c, PREP_LN, pn));
+    pn.group = act_group(c->dec[0].ckv.type);
+    TRY(kv_tc ? qprep_row<PREP_LN>(c, pn, act, c->dec[0].ckv) : qprep(c, PREP_LN, pn));
     auto B = std::make_unique<mgb_batch>();
     B->b = b;
     B->s = S;
@@ -1368,6 +1475,8 @@ mgb_status mgb_open(const char *path, int device, const mgb_options *opts, mgb_c
     else mgb_default_options(&c->opts);
     CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
     if (const char *v = getenv("MGB_TC_MIN_ROWS")) c->tc_min_rows = std::max(1, atoi(v));
+    cudaDeviceGetAttribute(&c->sms, cudaDevAttrMultiProcessorCount, device);
+    if (c->sms <= 0) c->sms = 148;
     mgb_status s = load_model(c.get(), path);
     if (s != MGB_OK) {
         if (c->arena) cudaFree(c->arena);

@@ -63,9 +63,10 @@ struct QAct {
     int *s32 = nullptr;    // [rows][K/32] sum of q per block
     int *s16 = nullptr;    // [rows][K/16] sum of q per 16-value half
     int rows = 0, K = 0;
-    // Tensor-core layout (set when rs > 0): rows padded to a multiple of 64 and
-    // the block scales stored block-major, dT[j*rs + row], sT[j*rs + row] = float(s32).
-    float *dT = nullptr, *sT = nullptr;
+    // Tensor-core layout (rs > 0: rows padded to a multiple of 64), written by
+    // qprep_row_kernel for one consuming matrix: tq = int8 tiles in the UMMA
+    // K-major layout, trec = per-unit scale records (gemm_tc.cuh).
+    uint8_t *tq = nullptr, *trec = nullptr;
     int rs = 0;
 };
 

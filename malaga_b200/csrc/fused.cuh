@@ -111,14 +111,14 @@ __device__ __forceinline__ float act_input(const PrepArgs &p, int r, int i) {
 // memory latency), then computes mean and 1/std with the lane-ordered pairwise
 // sum. Phase B: warps quantize (row, block) pairs in parallel, loading the
 // inputs of 8 pairs before processing them.
-template <int MODE>
+template <int MODE, int G>
 __device__ void build_activations_impl(const PrepArgs &p, const SmAct &s, int B, bool write_x);
 
 // Entry point: for LN / embedding inputs of at most 64 KB, all threads first
 // bring the B input rows into shared memory (one memory round trip; the
 // embedding rows are dequantized once), then the LayerNorm statistics and the
 // quantization read them from there.
-template <int MODE>
+template <int MODE, int G>
 __device__ void build_activations(const PrepArgs &p, const SmAct &s, int B, bool write_x, float *xs) {
     if constexpr (MODE != PREP_PLAIN) {
         if (xs) {
@@ -133,14 +133,14 @@ __device__ void build_activations(const PrepArgs &p, const SmAct &s, int B, bool
             __syncthreads();
             PrepArgs q = p;
             q.x = xs;
-            build_activations_impl<PREP_LN>(q, s, B, false);
+            build_activations_impl<PREP_LN, G>(q, s, B, false);
             return;
         }
     }
-    build_activations_impl<MODE>(p, s, B, write_x);
+    build_activations_impl<MODE, G>(p, s, B, write_x);
 }
 
-template <int MODE>
+template <int MODE, int G>
 __device__ void build_activations_impl(const PrepArgs &p, const SmAct &s, int B, bool write_x) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const int K = p.K, T = K >> 5, nb = T;
@@ -184,39 +184,45 @@ __device__ void build_activations_impl(const PrepArgs &p, const SmAct &s, int B,
         }
         __syncthreads();
     }
-    constexpr int PIPE = 8;
-    const int tasks = B * T;
-    for (int base = warp; base < tasks; base += nw * PIPE) {
-        float y[PIPE];
+    auto norm = [&](float v, int r, int i) -> float {
+        if constexpr (MODE != PREP_PLAIN)
+            v = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v, s.st[2 * r]), s.st[2 * r + 1]), p.gamma[i]), p.beta[i]);
+        if (s.xf) s.xf[(size_t)r * K + i] = v;
+        return v;
+    };
+    if constexpr (G == 1) {
+        // (row, block) tasks, 8 in flight per warp
+        constexpr int PIPE = 8;
+        const int tasks = B * T;
+        for (int base = warp; base < tasks; base += nw * PIPE) {
+            float y[PIPE];
 #pragma unroll
-        for (int u = 0; u < PIPE; ++u) {
-            const int task = base + u * nw;
-            y[u] = task < tasks ? act_input<MODE>(p, task / T, 32 * (task % T) + lane) : 0.0f;
-        }
-#pragma unroll
-        for (int u = 0; u < PIPE; ++u) {
-            const int task = base + u * nw;
-            if (task >= tasks) break;  // uniform across the warp
-            const int r = task / T, t = task % T, i = 32 * t + lane;
-            float yy = y[u];
-            if constexpr (MODE != PREP_PLAIN)
-                yy = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(yy, s.st[2 * r]), s.st[2 * r + 1]), p.gamma[i]),
-                               p.beta[i]);
-            if (s.xf) s.xf[(size_t)r * K + i] = yy;
-            const float amax = warp_max(fabsf(yy));
-            const float dd = __fdiv_rn(amax, 127.0f);
-            const int q = amax == 0.0f ? 0 : (int)roundf(__fdiv_rn(yy, dd));
-            s.q[(size_t)r * K + i] = (int8_t)q;
-            int h = q;
-#pragma unroll
-            for (int off = 1; off < 16; off <<= 1) h += __shfl_xor_sync(0xffffffffu, h, off);
-            const int hb = __shfl_sync(0xffffffffu, h, 16);
-            if (lane == 0) {
-                s.d[(size_t)r * nb + t] = round_h(dd);
-                s.s16[(size_t)r * 2 * nb + 2 * t] = h;
-                s.s16[(size_t)r * 2 * nb + 2 * t + 1] = hb;
-                s.s32[(size_t)r * nb + t] = h + hb;
+            for (int u = 0; u < PIPE; ++u) {
+                const int task = base + u * nw;
+                y[u] = task < tasks ? act_input<MODE>(p, task / T, 32 * (task % T) + lane) : 0.0f;
             }
+#pragma unroll
+            for (int u = 0; u < PIPE; ++u) {
+                const int task = base + u * nw;
+                if (task >= tasks) break;  // uniform across the warp
+                const int r = task / T, t = task % T;
+                const float yy[1] = {norm(y[u], r, 32 * t + lane)};
+                quantize_group<1>(yy, s.q + (size_t)r * K, s.d + (size_t)r * nb, s.s32 + (size_t)r * nb,
+                                  s.s16 + (size_t)r * 2 * nb, t, lane);
+            }
+        }
+    } else {
+        // (row, super-block) tasks: the 8 blocks share one scale
+        const int tasks = B * (T / 8);
+        for (int task = warp; task < tasks; task += nw) {
+            const int r = task / (T / 8), t0 = 8 * (task % (T / 8));
+            float y[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) y[u] = act_input<MODE>(p, r, 32 * (t0 + u) + lane);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) y[u] = norm(y[u], r, 32 * (t0 + u) + lane);
+            quantize_group<8>(y, s.q + (size_t)r * K, s.d + (size_t)r * nb, s.s32 + (size_t)r * nb,
+                              s.s16 + (size_t)r * 2 * nb, t0, lane);
         }
     }
     __syncthreads();
@@ -245,7 +251,8 @@ __global__ void __launch_bounds__(256) gemv_fused_kernel(FusedArgs fa) {
     }
     float *xs = nullptr;
     if constexpr (MODE != PREP_PLAIN) xs = reinterpret_cast<float *>(sm_raw + smact_bytes(B, W.K, TYPE == T_F32));
-    build_activations<MODE>(pa, s, B, blockIdx.x == 0, (size_t)B * W.K * 4 <= 64 * 1024 ? xs : nullptr);
+    build_activations<MODE, act_group(TYPE)>(pa, s, B, blockIdx.x == 0,
+                                             (size_t)B * W.K * 4 <= 64 * 1024 ? xs : nullptr);
 
     __shared__ float best_v[8][NB];
     __shared__ uint32_t best_i[8][NB];
@@ -262,34 +269,47 @@ __global__ void __launch_bounds__(256) gemv_fused_kernel(FusedArgs fa) {
             float acc[NB];
 #pragma unroll
             for (int i = 0; i < NB; ++i) acc[i] = 0.0f;
+            if constexpr (TYPE == T_F32) {
 #pragma unroll 8
-            for (int j = 0; j < nb; ++j) {
-                if constexpr (TYPE == T_F32) {
+                for (int j = 0; j < nb; ++j)
 #pragma unroll
                     for (int i = 0; i < NB; ++i) {
                         if (n0 + i >= B) break;
                         const float p = f32_block(W, row, j, s.xf + (size_t)(n0 + i) * W.K + 32 * j);
                         acc[i] = j == 0 ? p : __fadd_rn(acc[i], p);
                     }
-                } else {
+            } else {
+                constexpr int UB = unit_blocks<TYPE>();
+                for (int u = 0; u < nb; u += UB) {
+                    int S1[NB], S2[NB];
+#pragma unroll
+                    for (int i = 0; i < NB; ++i) S1[i] = S2[i] = 0;
                     BlockW<TYPE> bw;
-                    bw.load(W, row, j);
+#pragma unroll 8
+                    for (int j = u; j < u + UB; ++j) {
+                        bw.load(W, row, j);
+#pragma unroll
+                        for (int i = 0; i < NB; ++i) {
+                            const int n = n0 + i;
+                            if (n >= B) break;
+                            const int4 *xs = reinterpret_cast<const int4 *>(s.q + (size_t)n * W.K + 32 * j);
+                            const int4 x0 = xs[0], x1 = xs[1];
+                            const int xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                            int s32 = 0, s16a = 0, s16b = 0;
+                            if constexpr (TYPE == T_Q4_K) s32 = s.s32[(size_t)n * nb + j];
+                            if constexpr (TYPE == T_Q6_K) {
+                                s16a = s.s16[(size_t)n * 2 * nb + 2 * j];
+                                s16b = s.s16[(size_t)n * 2 * nb + 2 * j + 1];
+                            }
+                            bw.accum(xv, s32, s16a, s16b, S1[i], S2[i]);
+                        }
+                    }
 #pragma unroll
                     for (int i = 0; i < NB; ++i) {
                         const int n = n0 + i;
                         if (n >= B) break;
-                        const int4 *xs = reinterpret_cast<const int4 *>(s.q + (size_t)n * W.K + 32 * j);
-                        const int4 x0 = xs[0], x1 = xs[1];
-                        const int xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-                        const float xd = s.d[(size_t)n * nb + j];
-                        int s32 = 0, s16a = 0, s16b = 0;
-                        if constexpr (TYPE == T_Q4_K) s32 = s.s32[(size_t)n * nb + j];
-                        if constexpr (TYPE == T_Q6_K) {
-                            s16a = s.s16[(size_t)n * 2 * nb + 2 * j];
-                            s16b = s.s16[(size_t)n * 2 * nb + 2 * j + 1];
-                        }
-                        const float p = bw.dot(xv, xd, s32, s16a, s16b);
-                        acc[i] = j == 0 ? p : __fadd_rn(acc[i], p);
+                        const float p = bw.finish(S1[i], S2[i], s.d[(size_t)n * nb + u]);
+                        acc[i] = u == 0 ? p : __fadd_rn(acc[i], p);
                     }
                 }
             }
@@ -330,8 +350,9 @@ namespace mgb {
 // rows. Before waiting on the previous kernel, thread 0 starts 1-D bulk copies
 // (cp.async.bulk, completion counted on an mbarrier) of the group's weight
 // slices into shared memory. After the activation prologue, the 8 warps split
-// the K blocks (lane = row) and write the block partials p[n][j][row] to shared
-// memory; then each row's partials are summed left to right in block order.
+// the K blocks (lane = row) and write each block's integer sums (k-quants) or
+// float partial (Q8_0) to shared memory; then each row's units are finished and
+// summed left to right.
 
 constexpr uint64_t kWaitNs = 500000000ull;  // give up a wait after 0.5 s of device time
 
@@ -382,6 +403,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
         if (mbar_try(a, parity)) return true;
         if ((it & 255) == 0 && globaltimer() - t0 > kWaitNs) return false;
     }
+}
+
+// Shared-memory bytes of the staged kernel's per-block partials: two ints per
+// (row, block, weight row) for Q4_K, one int or float otherwise.
+__host__ __device__ constexpr size_t staged_partial_bytes(int type, int B, int nb) {
+    return (size_t)B * nb * 32 * (type == T_Q4_K ? 8 : 4);
 }
 
 // Shared-memory bytes of one group's staged weights (each region 16-B aligned).
@@ -438,12 +465,16 @@ __global__ void __launch_bounds__(256) gemv_staged_kernel(FusedArgs fa, uint32_t
         pa.ids = ids_sh;
         __syncthreads();
     }
-    build_activations<MODE>(pa, s, B, blockIdx.x == 0,
-                            (size_t)B * W.K * 4 <= (size_t)B * W.nb * 32 * 4 ? xs : nullptr);
+    build_activations<MODE, act_group(TYPE)>(pa, s, B, blockIdx.x == 0,
+                                             (size_t)B * W.K * 4 <= staged_partial_bytes(TYPE, B, nb) ? xs : nullptr);
     if (!mbar_wait(&bar, 0)) {
         if (lane == 0) atomicOr(err, 1u);  // copy never completed: report, produce nothing
         return;
     }
+    // per-block integer sums (k-quants) or float partials (Q8_0) of every
+    // (activation row, block, weight row); units are then finished in order
+    constexpr int UB = unit_blocks<TYPE>();
+    int *P1 = reinterpret_cast<int *>(P), *P2 = P1 + (size_t)B * nb * 32;
     const int cb = (nb + 7) / 8, j0 = warp * cb, j1 = min(nb, j0 + cb);
     for (int n = 0; n < B; ++n) {
         const int4 *xq = reinterpret_cast<const int4 *>(s.q + (size_t)n * W.K);
@@ -459,16 +490,41 @@ __global__ void __launch_bounds__(256) gemv_staged_kernel(FusedArgs fa, uint32_t
                 s16a = s.s16[(size_t)n * 2 * nb + 2 * j];
                 s16b = s.s16[(size_t)n * 2 * nb + 2 * j + 1];
             }
-            P[((size_t)n * nb + j) * 32 + lane] = bw.dot(xv, s.d[(size_t)n * nb + j], s32, s16a, s16b);
+            int S1 = 0, S2 = 0;
+            bw.accum(xv, s32, s16a, s16b, S1, S2);
+            const size_t o = ((size_t)n * nb + j) * 32 + lane;
+            if constexpr (UB == 1) {
+                P[o] = bw.finish(S1, S2, s.d[(size_t)n * nb + j]);
+            } else {
+                P1[o] = S1;
+                if constexpr (TYPE == T_Q4_K) P2[o] = S2;
+            }
         }
     }
     __syncthreads();
     const int row = grp * 32 + lane;
     for (int n = warp; n < B; n += 8) {
-        const float *pn = P + (size_t)n * nb * 32 + lane;
-        float acc = pn[0];
+        float acc = 0.0f;
+        if constexpr (UB == 1) {
+            const float *pn = P + (size_t)n * nb * 32 + lane;
+            acc = pn[0];
 #pragma unroll 8
-        for (int j = 1; j < nb; ++j) acc = __fadd_rn(acc, pn[(size_t)j * 32]);
+            for (int j = 1; j < nb; ++j) acc = __fadd_rn(acc, pn[(size_t)j * 32]);
+        } else {
+            for (int u = 0; u < nb; u += UB) {
+                int S1 = 0, S2 = 0;
+#pragma unroll
+                for (int j = u; j < u + UB; ++j) {
+                    const size_t o = ((size_t)n * nb + j) * 32 + lane;
+                    S1 += P1[o];
+                    if constexpr (TYPE == T_Q4_K) S2 += P2[o];
+                }
+                BlockW<TYPE> bw;
+                bw.template load<false>(Ws, lane, u);
+                const float p = bw.finish(S1, S2, s.d[(size_t)n * nb + u]);
+                acc = u == 0 ? p : __fadd_rn(acc, p);
+            }
+        }
         if (row < W.N) epilogue_store<EPI>(g, row, n, acc);
     }
 }

@@ -2,29 +2,36 @@
 //
 // Replaces candle's MMQ path (QMatMul::forward for more than 8 activation rows,
 // model.rs:571-607, and the encoder's projections model.rs:137-154 / 463-477).
-// The arithmetic is the engine's (numerics.cuh): per 32-block j the integer
-// dot I_j = sum q_w * q_x is exact, so the tensor core computes it
-// (tcgen05.mma kind::i8, M = 128 weight rows x N = NT activation rows x K = 32),
-// each block into its own TMEM columns; the epilogue applies the block's float
-// scales exactly as the small-batch kernels do and sums the partials left to
-// right in block order, so results are bit-identical to them.
+// The arithmetic is the engine's (kernels.cuh, BlockW): per 32-block the
+// integer dot of weight and activation values is exact, so the tensor core
+// computes it (tcgen05.mma kind::i8, M = 128 weight rows x N = NT activation
+// rows x K = 32), each block into its own TMEM columns; the epilogue adds the
+// blocks of a unit (a 256-value super-block for Q4_K / Q6_K, one block for
+// Q8_0) in int32, applies the unit's float scales and sums the units left to
+// right, so the results are bit-identical to the small-batch kernels.
 //
-// A CTA (4 warps; thread t owns weight row t of its 128-row tile, which is also
-// TMEM lane t) walks the K blocks in chunks of CB blocks:
-//   * thread 0 bulk-copies (cp.async.bulk, 1-D TMA) the raw weight bytes of
-//     chunk c+2 into a 3-deep ring while chunk c is being processed;
-//   * all threads unpack chunk c (Q4_K nibbles, Q6_K 6-bit values, Q8_0 bytes)
-//     into int8 tiles in the canonical K-major no-swizzle UMMA layout (8-row x
-//     16-byte core matrices, SBO 256 B between row groups, LBO 128 B between the
-//     two 16-byte K chunks), copy the activation blocks the same way, and keep
-//     the block's scales in shared memory;
-//   * thread 0 issues the CB MMAs of chunk c into one half of the TMEM columns
-//     and commits them to an mbarrier;
-//   * meanwhile the epilogue reads chunk c-1 from the other half (tcgen05.ld).
-// Tiles, buffers and TMEM halves are double-buffered; every mbarrier wait is
-// bounded by time and, when it runs out, the CTA records an error flag, stops,
+// One persistent CTA per SM walks its (128-row x NT-token) tiles in stages of
+// 8 blocks (256 values) with warp-specialized roles linked by mbarriers:
+//   warp 12     producer: one TMA tensor copy per weight region, one for the
+//               activation tiles (already in the UMMA K-major layout), one for
+//               the activation scale records, into a ring of RS stages;
+//   warps 0-3   converters: thread t unpacks weight row t of each block (Q4_K
+//               nibbles, Q6_K 6-bit values minus 32, Q8_0 bytes) into an int8
+//               128x32 tile in the canonical no-swizzle layout (ring of AS);
+//   warp 13     MMA: one tcgen05.mma per block into a ring of TS TMEM slots,
+//               committed to the barriers that free the tile, the slot's
+//               readers and the stage;
+//   warps 4-11  epilogue: warp w reads TMEM lanes 32(w%4).. (its weight rows)
+//               for half of the tile's tokens, accumulates, and stores.
+// Q6_K needs the two 16-value halves of a block separately (their scales
+// differ): its activation tiles hold every token twice, once with each half
+// zeroed, so one MMA with N = 2 NT yields both sums.
+// Every mbarrier wait is bounded in time; when one runs out the CTA records an
+// error flag, every role stops, and the CTA waits for its own MMAs before it
 // releases TMEM and returns.
 #pragma once
+#include <cuda.h>
+
 #include "fused.cuh"
 
 namespace mgb {
@@ -62,108 +69,159 @@ __device__ __forceinline__ void commit(uint64_t *bar) {
                  : "memory");
 }
 
-template <int N>
-__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[N]);
-
-template <>
-__device__ __forceinline__ void tmem_ld<8>(uint32_t t, uint32_t (&r)[8]) {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-                 : "r"(t));
-}
-template <>
-__device__ __forceinline__ void tmem_ld<16>(uint32_t t, uint32_t (&r)[16]) {
+__device__ __forceinline__ void tmem_ld16(uint32_t t, int (&r)[16]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
           "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(t));
 }
-
+__device__ __forceinline__ void tmem_ld8(uint32_t t, int (&r)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(t));
+}
+__device__ __forceinline__ void tmem_ld4(uint32_t t, int (&r)[4]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(t));
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// TMA tensor copy (tile mode, no multicast) of box `coords` into shared memory.
+__device__ __forceinline__ void tma3(void *dst, const CUtensorMap *m, int c0, int c1, int c2, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(smem_u32(dst)),
+        "l"(m), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tma4(void *dst, const CUtensorMap *m, int c0, int c1, int c2, int c3, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+        "%5}], [%6];" ::"r"(smem_u32(dst)),
+        "l"(m), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tma2(void *dst, const CUtensorMap *m, int c0, int c1, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(smem_u32(dst)),
+        "l"(m), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+        : "memory");
+}
+
 // Byte offset of (row r, 16-byte K chunk k16) of a K=32 int8 operand tile.
-__device__ __forceinline__ int tile_off(int r, int k16) { return (r >> 3) * 256 + k16 * 128 + (r & 7) * 16; }
+__host__ __device__ __forceinline__ int tile_off(int r, int k16) { return (r >> 3) * 256 + k16 * 128 + (r & 7) * 16; }
+
+// Tensor maps of one launch: weight regions a, b, c, e (3-D: 8-byte words of
+// one (32-row group, block) slice, blocks or super-blocks, groups), activation
+// tiles (4-D: 8-byte words of an 8-row core group, row groups, halves, blocks)
+// and activation scale records (2-D: 8-byte words of a unit's rows, units).
+struct Maps {
+    CUtensorMap w[4];
+    CUtensorMap xq, xr;
+};
 
 struct Args {
+    Maps m;
     Matrix W;
-    QAct x;          // activations [rows][K], q8_1
     int rows;        // activation rows
-    int row_tiles;   // Np / 128 (rounded up)
+    int row_tiles;   // Np / 128
     int tok_tiles;   // ceil(rows / NT)
+    int tok0;        // first activation row (a multiple of 64) of this launch
     GemvArgs g;      // epilogue outputs
     uint32_t *err;
 };
 
-// Chunk geometry per weight type and tile width.
+// Stage geometry per weight type and tile width.
 template <int TYPE, int NT>
 struct Geo {
-    static constexpr bool Q6 = TYPE == T_Q6_K;
-    static constexpr int COLS = Q6 ? 2 * NT : NT;                    // TMEM columns per block
-    static constexpr int A_BYTES = Q6 ? 8192 : 4096;                 // int8 tile(s) of one block
-    // blocks per chunk: 2 TMEM halves <= 256 columns, 2 tile buffers <= 64 KB,
-    // and a divisor of 8 (a chunk never straddles a 256-value super-block)
-    static constexpr int CB1 = 128 / COLS < 32768 / A_BYTES ? 128 / COLS : 32768 / A_BYTES;
-    static constexpr int CB = CB1 >= 8 ? 8 : (CB1 >= 4 ? 4 : (CB1 >= 2 ? 2 : 1));
-    static constexpr int B_BYTES = NT * 32 < 256 ? 256 : NT * 32;    // one 8-row core group minimum
-    // raw bytes of one block for 32 rows, per region
-    static constexpr int RA = TYPE == T_Q8_0 ? 1024 : 512;           // q / qs / ql
-    static constexpr int RB = TYPE == T_Q8_0 ? 64 : (TYPE == T_Q6_K ? 256 : 0);  // d / qh
-    static constexpr int RC = Q6 ? 64 : 0;                           // Q6_K scales
-    static constexpr int WRAW = 4 * CB * (RA + RB + RC) + (TYPE == T_Q8_0 ? 0 : 4 * (Q6 ? 64 : 512));
-    // activation bytes of a chunk: NT rows x CB blocks x 32 B, then block-major scales
-    static constexpr int XQ = WRAW, XD = XQ + NT * CB * 32, XS = XD + CB * NT * 4;
-    static constexpr int RAW = XS + CB * NT * 4;
+    static constexpr bool Q6 = TYPE == T_Q6_K, Q4 = TYPE == T_Q4_K, Q8 = TYPE == T_Q8_0;
+    static constexpr int H = Q6 ? 2 : 1;   // activation copies per block
+    static constexpr int COLS = H * NT;    // TMEM columns per block
+    static constexpr int KB = 8;           // blocks per stage
+    static constexpr int WA = Q8 ? 4 * KB * 1024 : 4 * KB * 512;                   // q / qs / ql
+    static constexpr int WB = Q8 ? 4 * KB * 64 : (Q4 ? 4 * 512 : 4 * KB * 256);    // d / header / qh
+    static constexpr int WC = Q6 ? 4 * KB * 64 : 0;                                // Q6_K scales
+    static constexpr int WE = Q6 ? 4 * 64 : 0;                                     // Q6_K d
+    static constexpr int RB = Q4 ? 32 : 4;                                         // record bytes
+    static constexpr int UPS = Q8 ? KB : 1;                                        // units per stage
+    static constexpr int oB = WA, oC = oB + WB, oE = oC + WC;
+    static constexpr int oXQ = (oE + WE + 1023) / 1024 * 1024;
+    static constexpr int oXR = oXQ + KB * H * NT * 32;
+    static constexpr int STAGE = (oXR + UPS * NT * RB + 1023) / 1024 * 1024;
+    static constexpr uint32_t TX = WA + WB + WC + WE + KB * H * NT * 32 + UPS * NT * RB;
+    static constexpr int AS = 8;                                                   // A tile slots
+    static constexpr int RS = (220 * 1024 - AS * 4096) / STAGE >= 4 ? 4 : 3;       // raw stages
+    static constexpr int TS = 512 / COLS < 16 ? 512 / COLS : 16;                   // TMEM slots
+    static constexpr int TCOLS_RAW = TS * COLS;
+    static constexpr int TCOLS = TCOLS_RAW <= 32 ? 32 : (TCOLS_RAW <= 64 ? 64 : (TCOLS_RAW <= 128 ? 128 :
+                                 (TCOLS_RAW <= 256 ? 256 : 512)));
+    static constexpr int SMEM = 1024 + RS * STAGE + AS * 4096;
+    static_assert(SMEM <= 227 * 1024, "stage ring too large");
 };
+
+constexpr int kThreads = 448;  // 14 warps
+constexpr int kProducerWarp = 12, kMmaWarp = 13;
 
 }  // namespace tc
 
-// Dynamic shared memory of gemm_tc_kernel<TYPE, *, NT>.
 template <int TYPE, int NT>
 __host__ __device__ constexpr size_t gemm_tc_smem() {
-    using G = tc::Geo<TYPE, NT>;
-    return 1024 + 3 * (size_t)((G::RAW + 1023) / 1024 * 1024) + 2 * (size_t)G::CB * (G::A_BYTES + G::B_BYTES) +
-           2 * (size_t)G::CB * (NT * 8 + 128 * 8);
+    return (size_t)tc::Geo<TYPE, NT>::SMEM;
 }
 
 template <int TYPE, int EPI, int NT>
-__global__ void __launch_bounds__(128, 2) gemm_tc_kernel(tc::Args A) {
+__global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_constant__ tc::Args A) {
     using namespace tc;
     using G = Geo<TYPE, NT>;
-    constexpr bool Q6 = G::Q6;
-    constexpr int CB = G::CB, COLS = G::COLS;
-    constexpr int RAWSZ = (G::RAW + 1023) / 1024 * 1024;
-    constexpr uint32_t IDESC = idesc_i8(128, NT);
+    constexpr int RS = G::RS, AS = G::AS, TS = G::TS, COLS = G::COLS, H = G::H;
+    constexpr int NH = NT / 2;  // tokens per epilogue warp
+    constexpr uint32_t IDESC = idesc_i8(128, H * NT);
     extern __shared__ __align__(16) uint8_t smem_raw[];
-    __shared__ __align__(8) uint64_t tma_bar[3], mma_bar[2];
+    __shared__ __align__(8) uint64_t full[RS], empty[RS], afull[AS], aempty[AS], tfull[TS], tempty[TS], fin;
     __shared__ uint32_t tmem_base_sh;
-    __shared__ int abort_sh;
+    __shared__ volatile int abort_sh;
     __shared__ float best_v[4][64];
     __shared__ uint32_t best_i[4][64];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const Matrix &W = A.W;
-    const int nb = W.nb, nsb = W.nsb;
-    const int nchunks = (nb + CB - 1) / CB;
+    const int NS = (W.nb + 7) / 8;  // stages per tile (Q8_0: the last may hold fewer blocks)
+    const int tiles = A.row_tiles * A.tok_tiles;
     uint8_t *base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-    uint8_t *raw = base;                                          // 3 x RAWSZ
-    uint8_t *tA = raw + 3 * RAWSZ;                                // 2 x CB x A_BYTES
-    uint8_t *tB = tA + 2 * CB * G::A_BYTES;                       // 2 x CB x B_BYTES
-    float *tok_sc = reinterpret_cast<float *>(tB + 2 * CB * G::B_BYTES);   // [2][CB][NT][2]
-    float *row_sc = tok_sc + 2 * CB * NT * 2;                    // [2][CB][128][2]
+    uint8_t *ring = base;                            // RS x STAGE
+    uint8_t *atile = base + (size_t)RS * G::STAGE;   // AS x 4 KB
 
     if (tid == 0) {
-        for (int i = 0; i < 3; ++i) mbar_init(&tma_bar[i], 1);
-        for (int i = 0; i < 2; ++i) mbar_init(&mma_bar[i], 1);
+        for (int i = 0; i < RS; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 4 + 1 + 8);
+        }
+        for (int i = 0; i < AS; ++i) {
+            mbar_init(&afull[i], 4);
+            mbar_init(&aempty[i], 1);
+        }
+        for (int i = 0; i < TS; ++i) {
+            mbar_init(&tfull[i], 1);
+            mbar_init(&tempty[i], 8);
+        }
+        mbar_init(&fin, 1);
         abort_sh = 0;
     }
     if (EPI == EPI_ARGMAX)
-        for (int n = tid; n < 256; n += 128) {
+        for (int n = tid; n < 256; n += blockDim.x) {
             best_v[n >> 6][n & 63] = kNegInf;
             best_i[n >> 6][n & 63] = 0xffffffffu;
         }
-    if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_u32(&tmem_base_sh))
+    if (warp == kMmaWarp) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_sh)),
+                     "r"(G::TCOLS)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -171,112 +229,132 @@ __global__ void __launch_bounds__(128, 2) gemm_tc_kernel(tc::Args A) {
     __syncthreads();
     fence_after();
     const uint32_t tmem = tmem_base_sh;
-    const int tiles = A.row_tiles * A.tok_tiles;
     pdl_launch_dependents();
 
-    // Raw bytes of chunk `c` of row tile `rt` into ring slot `slot` (thread 0).
-    auto issue = [&](int rt, int tt, int c, int slot) {
-        const int j0 = c * CB, nj = min(CB, nb - j0);
-        uint8_t *dst = raw + (size_t)slot * RAWSZ;
-        uint32_t bytes = 4 * nj * (G::RA + G::RB + G::RC) + (TYPE == T_Q4_K ? 4 * 512 : 0) + (Q6 ? 4 * 64 : 0);
-        bytes += NT * nj * 32 + nj * NT * 4 * (TYPE == T_Q4_K ? 2 : 1);
-        mbar_expect_tx(&tma_bar[slot], bytes);
-        // activations of the token tile (rows padded to 64: always in bounds)
-        for (int n = 0; n < NT; ++n)
-            bulk_g2s(dst + G::XQ + n * CB * 32, A.x.q + (size_t)(tt * NT + n) * W.K + 32 * j0, nj * 32, &tma_bar[slot]);
-        for (int b = 0; b < nj; ++b) {
-            bulk_g2s(dst + G::XD + b * NT * 4, A.x.dT + (size_t)(j0 + b) * A.x.rs + tt * NT, NT * 4, &tma_bar[slot]);
-            if (TYPE == T_Q4_K)
-                bulk_g2s(dst + G::XS + b * NT * 4, A.x.sT + (size_t)(j0 + b) * A.x.rs + tt * NT, NT * 4, &tma_bar[slot]);
-        }
-        // per group: blocks j0..j0+nj of each region are contiguous
-        for (int gi = 0; gi < 4; ++gi) {
-            const size_t gg = (size_t)rt * 4 + gi;
-            bulk_g2s(dst + gi * CB * G::RA, W.a + (gg * nb + j0) * 32 * (G::RA / 32), nj * G::RA, &tma_bar[slot]);
-            if (G::RB)
-                bulk_g2s(dst + 4 * CB * G::RA + gi * CB * G::RB, W.b + (gg * nb + j0) * 32 * (G::RB / 32), nj * G::RB,
-                         &tma_bar[slot]);
-            if (G::RC)
-                bulk_g2s(dst + 4 * CB * (G::RA + G::RB) + gi * CB * G::RC, W.c + (gg * nb + j0) * 32 * 2, nj * G::RC,
-                         &tma_bar[slot]);
-            if (TYPE == T_Q4_K)  // the super-block header of this chunk (CB <= 8 blocks stay in one)
-                bulk_g2s(dst + 4 * CB * G::RA + gi * 512, W.b + (gg * nsb + j0 / 8) * 32 * 16, 512, &tma_bar[slot]);
-            if (Q6)
-                bulk_g2s(dst + 4 * CB * (G::RA + G::RB + G::RC) + gi * 64, W.e + (gg * nsb + j0 / 8) * 32 * 2, 64,
-                         &tma_bar[slot]);
-        }
+    // A failed wait: record it and make every role stop.
+    auto fail = [&](uint32_t code) {
+        atomicOr(A.err, code);
+        abort_sh = 1;
+    };
+    // Warp-uniform bounded wait (every lane polls; all agree on the outcome).
+    auto wwait = [&](uint64_t *bar, uint32_t parity, uint32_t code) -> bool {
+        bool ok = mbar_wait(bar, parity);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok && lane == 0) fail(code);
+        return ok && !abort_sh;
     };
 
-    uint32_t tma_uses[3] = {0, 0, 0}, mma_uses[2] = {0, 0};
-    bool waited = false;
-    for (int tile = blockIdx.x; tile < tiles && !abort_sh; tile += gridDim.x) {
-        const int rt = tile % A.row_tiles, tt = tile / A.row_tiles;
-        const int row = rt * 128 + tid;
-        const bool live = row < W.N;
-        float acc[NT];
-#pragma unroll
-        for (int n = 0; n < NT; ++n) acc[n] = 0.0f;
-        // chunks 0 and 1 in flight; the first tile waits for the previous kernel
-        // before copying activations
-        if (!waited) {
-            pdl_wait();
-            waited = true;
-        }
-        if (tid == 0) {
-            issue(rt, tt, 0, 0);
-            if (nchunks > 1) issue(rt, tt, 1, 1);
-        }
-        for (int c = 0; c <= nchunks; ++c) {
-            const int half = c & 1;
-            // every thread has finished the epilogue of chunk c-2, whose token
-            // scales and tiles the unpacking of chunk c overwrites
-            __syncthreads();
-            if (abort_sh) break;
-            if (c < nchunks) {
-                const int slot = c % 3, j0 = c * CB, nj = min(CB, nb - j0);
-                if (tid == 0 && c + 2 < nchunks) issue(rt, tt, c + 2, (c + 2) % 3);
-                if (!mbar_wait(&tma_bar[slot], tma_uses[slot] & 1)) {
-                    atomicOr(A.err, 2u);
-                    abort_sh = 1;
+    if (warp == kProducerWarp) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            const int first_stages = blockIdx.x < tiles ? min(RS, NS) : 0;
+            auto weights = [&](int rt, int s, uint8_t *dst, uint64_t *bar) {
+                const int g0 = 4 * rt;
+                tma3(dst, &A.m.w[0], 0, 8 * s, g0, bar);
+                if constexpr (G::Q4) tma3(dst + G::oB, &A.m.w[1], 0, s, g0, bar);
+                else tma3(dst + G::oB, &A.m.w[1], 0, 8 * s, g0, bar);
+                if constexpr (G::Q6) {
+                    tma3(dst + G::oC, &A.m.w[2], 0, 8 * s, g0, bar);
+                    tma3(dst + G::oE, &A.m.w[3], 0, s, g0, bar);
                 }
-                ++tma_uses[slot];
-                const uint8_t *rs = raw + (size_t)slot * RAWSZ;
-                const int gi = tid >> 5, l = tid & 31;  // this thread unpacks its own row
-                for (int b = 0; b < nj; ++b) {
-                    uint8_t *ta = tA + (size_t)(half * CB + b) * G::A_BYTES;
-                    float s0 = 0.f, s1 = 0.f;
-                    if constexpr (TYPE == T_Q8_0) {
-                        const int4 *src = reinterpret_cast<const int4 *>(rs + gi * CB * 1024 + b * 1024 + l * 32);
-                        *reinterpret_cast<int4 *>(ta + tile_off(tid, 0)) = src[0];
-                        *reinterpret_cast<int4 *>(ta + tile_off(tid, 1)) = src[1];
-                        s0 = h2f(*reinterpret_cast<const unsigned short *>(rs + 4 * CB * 1024 + gi * CB * 64 + b * 64 + l * 2));
-                    } else if constexpr (TYPE == T_Q4_K) {
-                        const int4 v = *reinterpret_cast<const int4 *>(rs + gi * CB * 512 + b * 512 + l * 16);
-                        *reinterpret_cast<int4 *>(ta + tile_off(tid, 0)) =
-                            make_int4(v.x & 0x0f0f0f0f, v.y & 0x0f0f0f0f, v.z & 0x0f0f0f0f, v.w & 0x0f0f0f0f);
-                        *reinterpret_cast<int4 *>(ta + tile_off(tid, 1)) =
-                            make_int4((v.x >> 4) & 0x0f0f0f0f, (v.y >> 4) & 0x0f0f0f0f, (v.z >> 4) & 0x0f0f0f0f,
-                                      (v.w >> 4) & 0x0f0f0f0f);
-                        const uint4 h = *reinterpret_cast<const uint4 *>(rs + 4 * CB * 512 + gi * 512 + l * 16);
-                        const int sbk = (j0 + b) & 7;
-                        auto byte = [&](int kk) -> int {
-                            const uint32_t w = kk < 4 ? h.y : (kk < 8 ? h.z : h.w);
-                            return (w >> (8 * (kk & 3))) & 0xff;
-                        };
-                        int sc, mm;
-                        if (sbk < 4) {
-                            sc = byte(sbk) & 63;
-                            mm = byte(sbk + 4) & 63;
-                        } else {
-                            sc = (byte(sbk + 4) & 0xf) | ((byte(sbk - 4) >> 6) << 4);
-                            mm = (byte(sbk + 4) >> 4) | ((byte(sbk) >> 6) << 4);
+            };
+            auto acts = [&](int tt, int s, uint8_t *dst, uint64_t *bar) {
+                const int t0 = A.tok0 + tt * NT;
+                tma4(dst + G::oXQ, &A.m.xq, 0, t0 / 8, 0, 8 * s, bar);
+                if constexpr (G::Q4) tma2(dst + G::oXR, &A.m.xr, t0 * 4, s, bar);
+                else if constexpr (G::Q6) tma2(dst + G::oXR, &A.m.xr, t0 / 2, s, bar);
+                else tma2(dst + G::oXR, &A.m.xr, t0 / 2, 8 * s, bar);
+            };
+            // weights of the first stages do not depend on the previous kernel
+            for (int s = 0; s < first_stages; ++s) {
+                mbar_expect_tx(&full[s], G::TX);
+                weights(blockIdx.x % A.row_tiles, s, ring + (size_t)s * G::STAGE, &full[s]);
+            }
+            pdl_wait();
+            uint32_t gs = 0;
+            for (int tile = blockIdx.x; tile < tiles && !abort_sh; tile += gridDim.x) {
+                const int rt = tile % A.row_tiles, tt = tile / A.row_tiles;
+                for (int s = 0; s < NS; ++s, ++gs) {
+                    const int slot = gs % RS;
+                    const uint32_t use = gs / RS;
+                    uint8_t *dst = ring + (size_t)slot * G::STAGE;
+                    if (gs >= (uint32_t)first_stages) {
+                        if (use > 0 && !mbar_wait(&empty[slot], (use - 1) & 1)) {
+                            fail(8u);
+                            break;
                         }
-                        // d*sc and dmin*m are exact products (11-bit f16 x 6-bit integer)
-                        s0 = __fmul_rn(h2f(h.x & 0xffff), (float)sc);
-                        s1 = __fmul_rn(h2f(h.x >> 16), (float)mm);
+                        if (abort_sh) break;
+                        mbar_expect_tx(&full[slot], G::TX);
+                        weights(rt, s, dst, &full[slot]);
+                    }
+                    acts(tt, s, dst, &full[slot]);
+                }
+            }
+        }
+    } else if (warp == kMmaWarp) {
+        // ----------------------------------------------------------------- MMA
+        if (lane == 0) {
+            uint32_t gs = 0, gb = 0;
+            for (int tile = blockIdx.x; tile < tiles && !abort_sh; tile += gridDim.x) {
+                for (int s = 0; s < NS && !abort_sh; ++s, ++gs) {
+                    const int slot = gs % RS;
+                    if (!mbar_wait(&full[slot], (gs / RS) & 1)) {
+                        fail(16u);
+                        break;
+                    }
+                    const uint8_t *xq = ring + (size_t)slot * G::STAGE + G::oXQ;
+                    const int nbs = min(8, W.nb - 8 * s);
+                    for (int b = 0; b < nbs; ++b, ++gb) {
+                        const int as = gb % AS, ts = gb % TS;
+                        const uint32_t au = gb / AS, tu = gb / TS;
+                        if (!mbar_wait(&afull[as], au & 1) || (tu > 0 && !mbar_wait(&tempty[ts], (tu - 1) & 1))) {
+                            fail(16u);
+                            break;
+                        }
+                        if (abort_sh) break;
+                        fence_after();
+                        mma_i8(tmem + ts * COLS, sdesc(atile + as * 4096, 128, 256),
+                               sdesc(xq + b * H * NT * 32, 128, 256), IDESC);
+                        commit(&aempty[as]);
+                        commit(&tfull[ts]);
+                    }
+                    commit(&empty[slot]);
+                }
+            }
+            // every MMA issued by this thread has completed before TMEM is released
+            commit(&fin);
+            if (!mbar_wait(&fin, 0)) fail(16u);
+        }
+    } else if (warp < 4) {
+        // ---------------------------------------------------------- converters
+        const int r = tid;  // weight row of the tile = TMEM lane
+        uint32_t gs = 0, gb = 0;
+        for (int tile = blockIdx.x; tile < tiles && !abort_sh; tile += gridDim.x) {
+            bool ok = true;
+            for (int s = 0; s < NS && ok; ++s, ++gs) {
+                const int slot = gs % RS;
+                if (!(ok = wwait(&full[slot], (gs / RS) & 1, 32u))) break;
+                const uint8_t *st = ring + (size_t)slot * G::STAGE;
+                const int nbs = min(8, W.nb - 8 * s);
+                for (int b = 0; b < nbs; ++b, ++gb) {
+                    const int as = gb % AS;
+                    const uint32_t au = gb / AS;
+                    if (au > 0 && !(ok = wwait(&aempty[as], (au - 1) & 1, 32u))) break;
+                    uint8_t *ta = atile + as * 4096;
+                    const int gi = r >> 5, l = r & 31;
+                    int4 lo, hi;
+                    if constexpr (G::Q8) {
+                        const int4 *src = reinterpret_cast<const int4 *>(st + (gi * 8 + b) * 1024 + l * 32);
+                        lo = src[0];
+                        hi = src[1];
+                    } else if constexpr (G::Q4) {
+                        const int4 v = *reinterpret_cast<const int4 *>(st + (gi * 8 + b) * 512 + l * 16);
+                        lo = make_int4(v.x & 0x0f0f0f0f, v.y & 0x0f0f0f0f, v.z & 0x0f0f0f0f, v.w & 0x0f0f0f0f);
+                        hi = make_int4((v.x >> 4) & 0x0f0f0f0f, (v.y >> 4) & 0x0f0f0f0f, (v.z >> 4) & 0x0f0f0f0f,
+                                       (v.w >> 4) & 0x0f0f0f0f);
                     } else {
-                        const int4 lq = *reinterpret_cast<const int4 *>(rs + gi * CB * 512 + b * 512 + l * 16);
-                        const uint2 hq = *reinterpret_cast<const uint2 *>(rs + 4 * CB * 512 + gi * CB * 256 + b * 256 + l * 8);
+                        const int4 lq = *reinterpret_cast<const int4 *>(st + (gi * 8 + b) * 512 + l * 16);
+                        const uint2 hq = *reinterpret_cast<const uint2 *>(st + G::oB + (gi * 8 + b) * 256 + l * 8);
                         const int ql[4] = {lq.x, lq.y, lq.z, lq.w};
                         int a4[4], b4[4];
 #pragma unroll
@@ -287,123 +365,190 @@ __global__ void __launch_bounds__(128, 2) gemm_tc_kernel(tc::Args A) {
                                 (uint32_t)(((ql[i] >> 4) & 0x0f0f0f0f) | (int)(((hq.y >> (2 * i)) & 0x03030303u) << 4)),
                                 0x20202020u);
                         }
-                        const int4 z = make_int4(0, 0, 0, 0);
-                        *reinterpret_cast<int4 *>(ta + tile_off(tid, 0)) = make_int4(a4[0], a4[1], a4[2], a4[3]);
-                        *reinterpret_cast<int4 *>(ta + tile_off(tid, 1)) = z;
-                        *reinterpret_cast<int4 *>(ta + 4096 + tile_off(tid, 0)) = z;
-                        *reinterpret_cast<int4 *>(ta + 4096 + tile_off(tid, 1)) = make_int4(b4[0], b4[1], b4[2], b4[3]);
-                        s0 = h2f(*reinterpret_cast<const unsigned short *>(rs + 4 * CB * (512 + 256 + 64) + gi * 64 + l * 2));
-                        s1 = __int_as_float(
-                            (int)*reinterpret_cast<const unsigned short *>(rs + 4 * CB * (512 + 256) + gi * CB * 64 + b * 64 + l * 2));
+                        lo = make_int4(a4[0], a4[1], a4[2], a4[3]);
+                        hi = make_int4(b4[0], b4[1], b4[2], b4[3]);
                     }
-                    row_sc[((half * CB + b) * 128 + tid) * 2] = s0;
-                    row_sc[((half * CB + b) * 128 + tid) * 2 + 1] = s1;
+                    *reinterpret_cast<int4 *>(ta + tile_off(r, 0)) = lo;
+                    *reinterpret_cast<int4 *>(ta + tile_off(r, 1)) = hi;
+                    fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&afull[as]);
                 }
-                // activation blocks (staged raw by the bulk copies) into the UMMA layout
-                for (int e = tid; e < NT * nj * 2; e += 128) {
-                    const int n = e / (nj * 2), b = (e >> 1) % nj, k16 = e & 1;
-                    *reinterpret_cast<int4 *>(tB + (size_t)(half * CB + b) * G::B_BYTES + tile_off(n, k16)) =
-                        *reinterpret_cast<const int4 *>(rs + G::XQ + n * CB * 32 + b * 32 + 16 * k16);
-                }
-                for (int e = tid; e < NT * nj; e += 128) {
-                    const int b = e / NT, n = e % NT;
-                    tok_sc[((half * CB + b) * NT + n) * 2] = reinterpret_cast<const float *>(rs + G::XD)[b * NT + n];
-                    tok_sc[((half * CB + b) * NT + n) * 2 + 1] =
-                        TYPE == T_Q4_K ? reinterpret_cast<const float *>(rs + G::XS)[b * NT + n] : 0.0f;
-                }
-                fence_async_smem();
-                fence_before();
-                __syncthreads();
-                fence_after();
-                if (tid == 0 && !abort_sh) {
-                    for (int b = 0; b < nj; ++b) {
-                        const uint64_t da = sdesc(tA + (size_t)(half * CB + b) * G::A_BYTES, 128, 256);
-                        const uint64_t db = sdesc(tB + (size_t)(half * CB + b) * G::B_BYTES, 128, 256);
-                        const uint32_t col = tmem + (half * CB + b) * COLS;
-                        mma_i8(col, da, db, IDESC);
-                        if constexpr (Q6)
-                            mma_i8(col + NT, sdesc(tA + (size_t)(half * CB + b) * G::A_BYTES + 4096, 128, 256), db, IDESC);
-                    }
-                    commit(&mma_bar[half]);
-                }
+                if (!ok) break;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[slot]);
             }
-            // epilogue of chunk c-1 (its MMAs overlap the unpacking of chunk c)
-            if (c > 0) {
-                const int pc = c - 1, ph = pc & 1, pj0 = pc * CB, pnj = min(CB, nb - pj0);
-                if (!mbar_wait(&mma_bar[ph], mma_uses[ph] & 1)) {
-                    atomicOr(A.err, 4u);
-                    abort_sh = 1;  // every thread stops at the next barrier
-                }
-                ++mma_uses[ph];
-                fence_after();
-                for (int b = 0; b < pnj && !abort_sh; ++b) {
-                    const int j = pj0 + b;
-                    const float r0 = row_sc[((ph * CB + b) * 128 + tid) * 2];
-                    const float r1 = row_sc[((ph * CB + b) * 128 + tid) * 2 + 1];
-                    int sa = 0, sb = 0;
-                    if constexpr (Q6) {
-                        const int packed = __float_as_int(r1);
-                        sa = (int8_t)(packed & 0xff);
-                        sb = (int8_t)((packed >> 8) & 0xff);
+            if (!ok) break;
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const int q = warp & 3, e = (warp - 4) >> 2;
+        const int r = 32 * q + lane, gi = q, l = lane;
+        const int n0 = e * NH;  // first token (within the tile) of this warp
+        pdl_wait();
+        uint32_t gs = 0, gb = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < tiles && ok && !abort_sh; tile += gridDim.x) {
+            const int rt = tile % A.row_tiles, tt = tile / A.row_tiles;
+            const int row = rt * 128 + r;
+            const bool live = row < W.N;
+            float acc[NH];
+#pragma unroll
+            for (int n = 0; n < NH; ++n) acc[n] = 0.0f;
+            for (int s = 0; s < NS && ok; ++s, ++gs) {
+                const int slot = gs % RS;
+                if (!(ok = wwait(&full[slot], (gs / RS) & 1, 64u))) break;
+                const uint8_t *st = ring + (size_t)slot * G::STAGE;
+                // this row's scales for the stage
+                float d = 0.f, dm = 0.f;
+                uint32_t mpk0 = 0, mpk1 = 0, scpk0 = 0, scpk1 = 0;
+                if constexpr (G::Q4) {
+                    const uint4 h = *reinterpret_cast<const uint4 *>(st + G::oB + gi * 512 + l * 16);
+                    d = h2f(h.x & 0xffff);
+                    dm = h2f(h.x >> 16);
+                    auto byte = [&](int k) -> uint32_t {
+                        const uint32_t w = k < 4 ? h.y : (k < 8 ? h.z : h.w);
+                        return (w >> (8 * (k & 3))) & 0xff;
+                    };
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        uint32_t sc, mm;
+                        if (k < 4) {
+                            sc = byte(k) & 63;
+                            mm = byte(k + 4) & 63;
+                        } else {
+                            sc = (byte(k + 4) & 0xf) | ((byte(k - 4) >> 6) << 4);
+                            mm = (byte(k + 4) >> 4) | ((byte(k) >> 6) << 4);
+                        }
+                        if (k < 4) {
+                            scpk0 |= sc << (8 * k);
+                            mpk0 |= mm << (8 * k);
+                        } else {
+                            scpk1 |= sc << (8 * (k - 4));
+                            mpk1 |= mm << (8 * (k - 4));
+                        }
                     }
-                    const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (ph * CB + b) * COLS;
-                    constexpr int CH = NT < 16 ? NT : 16;
+                } else if constexpr (G::Q6) {
+                    d = h2f(*reinterpret_cast<const unsigned short *>(st + G::oE + gi * 64 + l * 2));
+                }
+                int S[NH];
 #pragma unroll
-                    for (int c0 = 0; c0 < NT; c0 += CH) {
-                        uint32_t v[CH], v2[CH];
-                        tmem_ld<CH>(taddr + c0, v);
-                        if constexpr (Q6) tmem_ld<CH>(taddr + NT + c0, v2);
+                for (int n = 0; n < NH; ++n) S[n] = 0;
+                const int nbs = min(8, W.nb - 8 * s);
+                for (int b = 0; b < nbs; ++b, ++gb) {
+                    const int ts = gb % TS;
+                    if (!(ok = wwait(&tfull[ts], (gb / TS) & 1, 64u))) break;
+                    fence_after();
+                    const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + ts * COLS + n0;
+                    int sa = 0, sb = 0;
+                    float db = 0.f;
+                    if constexpr (G::Q4) {
+                        sa = (int)(((b < 4 ? scpk0 : scpk1) >> (8 * (b & 3))) & 0xff);
+                    } else if constexpr (G::Q6) {
+                        const unsigned short sc2 =
+                            *reinterpret_cast<const unsigned short *>(st + G::oC + (gi * 8 + b) * 64 + l * 2);
+                        sa = (int8_t)(sc2 & 0xff);
+                        sb = (int8_t)(sc2 >> 8);
+                    } else {
+                        db = h2f(*reinterpret_cast<const unsigned short *>(st + G::oB + (gi * 8 + b) * 64 + l * 2));
+                    }
+                    constexpr int CH = NH < 16 ? NH : 16;
+#pragma unroll
+                    for (int c0 = 0; c0 < NH; c0 += CH) {
+                        int va[16], vb[16];
+                        if constexpr (CH == 16) {
+                            tmem_ld16(ta + c0, va);
+                            if constexpr (G::Q6) tmem_ld16(ta + NT + c0, vb);
+                        } else if constexpr (CH == 8) {
+                            int t8[8], u8[8];
+                            tmem_ld8(ta + c0, t8);
+                            if constexpr (G::Q6) tmem_ld8(ta + NT + c0, u8);
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) {
+                                va[i] = t8[i];
+                                vb[i] = G::Q6 ? u8[i] : 0;
+                            }
+                        } else {
+                            static_assert(CH == 4, "token chunk");
+                            int t4[4], u4[4];
+                            tmem_ld4(ta + c0, t4);
+                            if constexpr (G::Q6) tmem_ld4(ta + NT + c0, u4);
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                va[i] = t4[i];
+                                vb[i] = G::Q6 ? u4[i] : 0;
+                            }
+                        }
                         tmem_wait_ld();
-                        const float *ts = tok_sc + ((ph * CB + b) * NT + c0) * 2;
 #pragma unroll
-                        for (int u = 0; u < CH; u += 2) {
-                            const float4 t4 = *reinterpret_cast<const float4 *>(ts + 2 * u);
-#pragma unroll
-                            for (int h = 0; h < 2; ++h) {
-                                const int n = c0 + u + h;
-                                const float xd = h ? t4.z : t4.x, s8f = h ? t4.w : t4.y;
-                                const int I = (int)v[u + h];
-                                float p;
-                                if constexpr (TYPE == T_Q8_0) {
-                                    p = __fmul_rn(__fmul_rn(r0, xd), (float)I);
-                                } else if constexpr (TYPE == T_Q4_K) {
-                                    // = xd * (d*float(I*sc) - dmin*float(s8*m)): the products are exact
-                                    p = __fmul_rn(xd, __fsub_rn(__fmul_rn(r0, (float)I), __fmul_rn(r1, s8f)));
-                                } else {
-                                    p = __fmul_rn(__fmul_rn(r0, xd), (float)(sa * I + sb * (int)v2[u + h]));
-                                }
-                                acc[n] = j == 0 ? p : __fadd_rn(acc[n], p);
+                        for (int i = 0; i < CH; ++i) {
+                            const int n = c0 + i;
+                            if constexpr (G::Q4) {
+                                S[n] += sa * va[i];
+                            } else if constexpr (G::Q6) {
+                                S[n] += sa * va[i] + sb * vb[i];
+                            } else {
+                                const float xd = reinterpret_cast<const float *>(st + G::oXR)[b * NT + n0 + n];
+                                const float p = __fmul_rn(__fmul_rn(db, xd), (float)va[i]);
+                                acc[n] = (s == 0 && b == 0) ? p : __fadd_rn(acc[n], p);
                             }
                         }
                     }
+                    fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tempty[ts]);
                 }
-                fence_before();
-            }
-        }
-        __syncthreads();
-        if (abort_sh) break;
-        // tile epilogue
+                if (!ok) break;
+                if constexpr (!G::Q8) {
+                    // finish the super-block: float scales once, then the row sum
 #pragma unroll
-        for (int n = 0; n < NT; ++n) {
-            const int tok = tt * NT + n;
-            if (tok >= A.rows) break;  // uniform across the CTA
-            if constexpr (EPI == EPI_ARGMAX) {
-                float bv = live ? acc[n] : kNegInf;
-                uint32_t bi = live ? (uint32_t)row : 0xffffffffu;
-                if (A.g.logits && live) A.g.logits[(size_t)tok * W.N + row] = acc[n];
-                warp_argmax(bv, bi);
-                if (lane == 0) argmax_merge(best_v[warp][tok & 63], best_i[warp][tok & 63], bv, bi);
-            } else if (live) {
-                epilogue_store<EPI>(A.g, row, tok, acc[n]);
+                    for (int n = 0; n < NH; ++n) {
+                        float p;
+                        if constexpr (G::Q4) {
+                            const int4 rec = *reinterpret_cast<const int4 *>(st + G::oXR + (n0 + n) * 32);
+                            const float xd = __int_as_float(rec.x);
+                            // S2 = sum_j m_j * s32_j (s32 pairs as int16x2, m_j as bytes)
+                            int S2 = __dp2a_lo(rec.y, (int)mpk0, 0);
+                            S2 = __dp2a_hi(rec.z, (int)mpk0, S2);
+                            S2 = __dp2a_lo(rec.w, (int)mpk1, S2);
+                            S2 = __dp2a_hi(*reinterpret_cast<const int *>(st + G::oXR + (n0 + n) * 32 + 16), (int)mpk1,
+                                           S2);
+                            p = __fmul_rn(xd, __fsub_rn(__fmul_rn(d, (float)S[n]), __fmul_rn(dm, (float)S2)));
+                        } else {
+                            const float xd = reinterpret_cast<const float *>(st + G::oXR)[n0 + n];
+                            p = __fmul_rn(__fmul_rn(d, xd), (float)S[n]);
+                        }
+                        acc[n] = s == 0 ? p : __fadd_rn(acc[n], p);
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[slot]);
+            }
+            if (!ok || abort_sh) break;
+            // tile epilogue
+#pragma unroll
+            for (int n = 0; n < NH; ++n) {
+                const int tok = tt * NT + n0 + n;
+                if (tok >= A.rows) break;  // uniform across the warp
+                if constexpr (EPI == EPI_ARGMAX) {
+                    float bv = live ? acc[n] : kNegInf;
+                    uint32_t bi = live ? (uint32_t)row : 0xffffffffu;
+                    if (A.g.logits && live) A.g.logits[(size_t)tok * W.N + row] = acc[n];
+                    warp_argmax(bv, bi);
+                    if (lane == 0) argmax_merge(best_v[q][tok], best_i[q][tok], bv, bi);  // tok < 64
+                } else if (live) {
+                    epilogue_store<EPI>(A.g, row, tok, acc[n]);
+                }
             }
         }
-        __syncthreads();  // the tile's buffers are reused by the next tile
     }
-    if (!waited) pdl_wait();  // a CTA without a tile still keeps the launch chain ordered
+    // (the producer's lane 0 and the epilogue warps waited on the previous
+    // kernel, so this CTA cannot finish before it)
     fence_before();
     __syncthreads();
     if constexpr (EPI == EPI_ARGMAX) {
-        for (int n = tid; n < A.rows && n < 64; n += 128) {
+        // one partial per (activation row, CTA); ARGMAX launches cover at most 64 rows
+        for (int n = tid; n < A.rows && n < 64; n += blockDim.x) {
             float v = best_v[0][n];
             uint32_t i = best_i[0][n];
             for (int w = 1; w < 4; ++w) argmax_merge(v, i, best_v[w][n], best_i[w][n]);
@@ -411,24 +556,39 @@ __global__ void __launch_bounds__(128, 2) gemm_tc_kernel(tc::Args A) {
             A.g.part_i[(size_t)n * gridDim.x + blockIdx.x] = i;
         }
     }
-    if (warp == 0) {
+    if (warp == kMmaWarp) {
         fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(G::TCOLS) : "memory");
     }
 }
 
-// q8_1 activations of one row per CTA into global memory (the tensor-core
-// matmul's input): the row is staged in shared memory (embedding rows are
-// dequantized once), LayerNorm statistics by one warp in the fixed order, and
-// the 8 warps quantize the blocks.
+// Tensor-core layout of one activation row (one CTA per row): the row is staged
+// in shared memory (embedding rows dequantized once), LayerNorm statistics by
+// one warp in the fixed order, quantized with the consumer's scale groups, then
+// written as
+//   tq : per block j and copy h, 8-row core groups of 256 bytes
+//        [j][h][row/8][k16][row%8][16 B] (the UMMA K-major no-swizzle layout;
+//        for Q6_K consumers copy 0 keeps values 0-15 and copy 1 values 16-31,
+//        the other half zeroed);
+//   trec: per unit u (super-block, or block for Q8_0 consumers) and row:
+//        Q4_K: {f32 scale, int16 block sums x 8, 12 zero bytes} (32 B);
+//        Q6_K: f32 scale; Q8_0: f32 (f16-rounded) scale.
 template <int MODE>
 __global__ void __launch_bounds__(256) qprep_row_kernel(PrepArgs p, QAct out) {
-    extern __shared__ __align__(16) float xs[];
+    extern __shared__ __align__(16) uint8_t qsm[];
     __shared__ float st[2];
     __shared__ uint32_t id_sh[1];
     pdl_launch_dependents();
     pdl_wait();
     const int r = blockIdx.x, K = p.K, nb = K >> 5;
+    float *xs = reinterpret_cast<float *>(qsm);                 // K floats
+    SmAct s;
+    s.q = reinterpret_cast<int8_t *>(qsm + (size_t)K * 4);      // K bytes
+    s.d = reinterpret_cast<float *>(qsm + (size_t)K * 5);       // nb
+    s.s32 = reinterpret_cast<int *>(s.d + nb);                  // nb
+    s.s16 = s.s32 + nb;                                         // 2 nb
+    s.st = st;
+    s.xf = nullptr;
     PrepArgs pa = p;
     if constexpr (MODE == PREP_EMBED_LN) {
         if (threadIdx.x == 0) id_sh[0] = p.ids[r];
@@ -442,23 +602,36 @@ __global__ void __launch_bounds__(256) qprep_row_kernel(PrepArgs p, QAct out) {
         if constexpr (MODE == PREP_EMBED_LN) p.x_out[(size_t)r * K + i] = v;
     }
     __syncthreads();
-    SmAct s;
-    s.q = out.q + (size_t)r * K;
-    s.d = out.d + (size_t)r * nb;
-    s.s32 = out.s32 + (size_t)r * nb;
-    s.s16 = out.s16 + (size_t)r * 2 * nb;
-    s.st = st;
-    s.xf = nullptr;
     PrepArgs q = p;
     q.x = xs;
     q.rows = 1;
-    build_activations_impl<MODE == PREP_PLAIN ? PREP_PLAIN : PREP_LN>(q, s, 1, false);
-    if (out.rs) {  // block-major copies of the scales for the tensor-core matmul
-        __syncthreads();
-        for (int j = threadIdx.x; j < nb; j += blockDim.x) {
-            out.dT[(size_t)j * out.rs + r] = s.d[j];
-            out.sT[(size_t)j * out.rs + r] = (float)s.s32[j];
+    constexpr int M2 = MODE == PREP_PLAIN ? PREP_PLAIN : PREP_LN;
+    if (p.group == 8) build_activations_impl<M2, 8>(q, s, 1, false);
+    else build_activations_impl<M2, 1>(q, s, 1, false);
+    // build_activations_impl ends with __syncthreads
+    const int H = p.ctype == T_Q6_K ? 2 : 1, rs = out.rs;
+    for (int c = threadIdx.x; c < nb * H * 2; c += blockDim.x) {
+        const int j = c / (2 * H), h = (c >> 1) % H, k16 = c & 1;
+        int4 v = *reinterpret_cast<const int4 *>(s.q + 32 * j + 16 * k16);
+        if (H == 2 && h != k16) v = make_int4(0, 0, 0, 0);
+        *reinterpret_cast<int4 *>(out.tq + (((size_t)j * H + h) * (rs / 8) + (r >> 3)) * 256 + tc::tile_off(r & 7, k16)) = v;
+    }
+    if (p.ctype == T_Q4_K) {
+        for (int u = threadIdx.x; u < nb / 8; u += blockDim.x) {
+            int w[8];
+            w[0] = __float_as_int(s.d[8 * u]);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                w[1 + k] = (s.s32[8 * u + 2 * k] & 0xffff) | (s.s32[8 * u + 2 * k + 1] << 16);
+            w[5] = w[6] = w[7] = 0;
+            int4 *dst = reinterpret_cast<int4 *>(out.trec + ((size_t)u * rs + r) * 32);
+            dst[0] = make_int4(w[0], w[1], w[2], w[3]);
+            dst[1] = make_int4(w[4], w[5], w[6], w[7]);
         }
+    } else {
+        const int units = p.ctype == T_Q6_K ? nb / 8 : nb, step = p.ctype == T_Q6_K ? 8 : 1;
+        for (int u = threadIdx.x; u < units; u += blockDim.x)
+            reinterpret_cast<float *>(out.trec)[(size_t)u * rs + r] = s.d[u * step];
     }
 }
 

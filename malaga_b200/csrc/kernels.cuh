@@ -91,35 +91,53 @@ struct PrepArgs {
     QAct out;
     int keep_f32;  // also store the (normalised) f32 values (for F32 weights)
     float *xf;     // [rows][K]
+    int group;     // blocks per activation scale: 1 (Q8_0 consumers) or 8 (Q4_K / Q6_K)
+    int ctype;     // weight type of the consuming matrix (tensor-core layout)
 };
 
-__device__ __forceinline__ void quantize_block(float y, const QAct &o, int row, int t, int lane) {
-    const float amax = warp_max(fabsf(y));
-    const float dd = __fdiv_rn(amax, 127.0f);
-    const int q = amax == 0.0f ? 0 : (int)roundf(__fdiv_rn(y, dd));
-    o.q[(size_t)row * o.K + 32 * t + lane] = (int8_t)q;
-    int s = q;
+// Activation scale group of a consumer weight type: k-quants take one f32 scale
+// per 256-value super-block (Q8_K style), Q8_0 one f16-rounded scale per block.
+__host__ __device__ constexpr int act_group(int type) { return type == T_Q4_K || type == T_Q6_K ? 8 : 1; }
+
+// Quantizes G consecutive blocks (y[u] = element lane of block t0+u of `row`)
+// with one scale: d = amax/127 over the G*32 values, q = round(y/d). G = 1
+// stores the scale f16-rounded (q8_1 / Q8_0 style), G = 8 as f32 (Q8_K style).
+template <int G>
+__device__ __forceinline__ void quantize_group(const float (&y)[G], int8_t *q, float *d, int *s32, int *s16, int t0,
+                                               int lane) {
+    float m = fabsf(y[0]);
 #pragma unroll
-    for (int off = 1; off < 16; off <<= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-    const int nb = o.K >> 5;
-    if (lane == 0) {
-        o.d[(size_t)row * nb + t] = round_h(dd);
-        o.s16[(size_t)row * 2 * nb + 2 * t] = s;
-    }
-    const int s_hi = __shfl_sync(0xffffffffu, s, 16);
-    const int s_lo = __shfl_sync(0xffffffffu, s, 0);
-    if (lane == 0) {
-        o.s16[(size_t)row * 2 * nb + 2 * t + 1] = s_hi;
-        o.s32[(size_t)row * nb + t] = s_lo + s_hi;
+    for (int u = 1; u < G; ++u) m = fmaxf(m, fabsf(y[u]));
+    const float amax = warp_max(m);
+    const float dd = __fdiv_rn(amax, 127.0f);
+#pragma unroll
+    for (int u = 0; u < G; ++u) {
+        const int t = t0 + u;
+        const int v = amax == 0.0f ? 0 : (int)roundf(__fdiv_rn(y[u], dd));
+        q[32 * t + lane] = (int8_t)v;
+        int s = v;
+#pragma unroll
+        for (int off = 1; off < 16; off <<= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+        const int s_hi = __shfl_sync(0xffffffffu, s, 16);
+        if (lane == 0) {
+            d[t] = G == 1 ? round_h(dd) : dd;
+            s16[2 * t] = s;
+            s16[2 * t + 1] = s_hi;
+            s32[t] = s + s_hi;
+        }
     }
 }
+
+// Row `row` of a global QAct as quantize_group destinations.
+#define QACT_ROW(o, row) (o).q + (size_t)(row) * (o).K, (o).d + (size_t)(row) * ((o).K >> 5), \
+                         (o).s32 + (size_t)(row) * ((o).K >> 5), (o).s16 + (size_t)(row) * ((o).K >> 4)
 
 template <int MODE>
 __global__ void __launch_bounds__(256) qprep_kernel(PrepArgs p) {
     const int lane = threadIdx.x & 31;
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
     if (row >= p.rows) return;
-    const int K = p.K, T = K >> 5;
+    const int K = p.K, T = K >> 5, G = p.group == 8 ? 8 : 1;
     const float *x = p.x + (size_t)row * K;
     if constexpr (MODE == PREP_EMBED_LN) {
         const uint32_t id = p.ids[row];
@@ -133,10 +151,15 @@ __global__ void __launch_bounds__(256) qprep_kernel(PrepArgs p) {
         __syncwarp();
     }
     if constexpr (MODE == PREP_PLAIN) {
-        for (int t = 0; t < T; ++t) {
-            const float v = x[32 * t + lane];
-            if (p.keep_f32) p.xf[(size_t)row * K + 32 * t + lane] = v;
-            quantize_block(v, p.out, row, t, lane);
+        for (int t = 0; t < T; t += G) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                v[u] = u < G ? x[32 * (t + u) + lane] : 0.0f;
+                if (u < G && p.keep_f32) p.xf[(size_t)row * K + 32 * (t + u) + lane] = v[u];
+            }
+            if (G == 8) quantize_group<8>(v, QACT_ROW(p.out, row), t, lane);
+            else quantize_group<1>(reinterpret_cast<const float(&)[1]>(v[0]), QACT_ROW(p.out, row), t, lane);
         }
         return;
     }
@@ -152,11 +175,19 @@ __global__ void __launch_bounds__(256) qprep_kernel(PrepArgs p) {
     }
     const float var = __fdiv_rn(warp_tree(s2), (float)K);
     const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
-    for (int t = 0; t < T; ++t) {
-        const int i = 32 * t + lane;
-        const float y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(x[i], mean), rstd), p.gamma[i]), p.beta[i]);
-        if (p.keep_f32) p.xf[(size_t)row * K + i] = y;
-        quantize_block(y, p.out, row, t, lane);
+    for (int t = 0; t < T; t += G) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = 32 * (t + u) + lane;
+            v[u] = 0.0f;
+            if (u < G) {
+                v[u] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(x[i], mean), rstd), p.gamma[i]), p.beta[i]);
+                if (p.keep_f32) p.xf[(size_t)row * K + i] = v[u];
+            }
+        }
+        if (G == 8) quantize_group<8>(v, QACT_ROW(p.out, row), t, lane);
+        else quantize_group<1>(reinterpret_cast<const float(&)[1]>(v[0]), QACT_ROW(p.out, row), t, lane);
     }
 }
 
@@ -192,9 +223,20 @@ __device__ __forceinline__ T ldw(const T *p) {
     else return *p;
 }
 
-// Partial p_j of one 32-block against activation row n (see numerics.cuh).
+// One 32-block of a weight row against one activation row. The integer part
+// of the block is accumulated exactly into (S1, S2) by accum(); finish() turns
+// the sums of a whole unit into its float partial. A unit is one block for
+// Q8_0 and one 256-value super-block (8 blocks) for Q4_K / Q6_K:
+//   Q8_0: S1 = I;                          p = (d*xd) * float(S1)
+//   Q4_K: S1 += sc*I, S2 += m*sum(xq);     p = xd * (d*float(S1) - dmin*float(S2))
+//   Q6_K: S1 += sc_a*I_a + sc_b*I_b;       p = (d*xd) * float(S1)
+// (I = sum of weight x activation integers over the block, I_a / I_b over its
+// 16-value halves with the 6-bit values offset by -32.)
 template <int TYPE>
 struct BlockW;
+
+template <int TYPE>
+__host__ __device__ constexpr int unit_blocks() { return TYPE == T_Q4_K || TYPE == T_Q6_K ? 8 : 1; }
 
 template <>
 struct BlockW<T_Q8_0> {
@@ -209,11 +251,14 @@ struct BlockW<T_Q8_0> {
         w[4] = a1.x; w[5] = a1.y; w[6] = a1.z; w[7] = a1.w;
         d = h2f(ldw<GLOBAL>(reinterpret_cast<const unsigned short *>(W.b) + bi));
     }
-    __device__ __forceinline__ float dot(const int *x, float xd, int, int, int) const {
+    __device__ __forceinline__ void accum(const int *x, int, int, int, int &S1, int &) const {
         int s = 0;
 #pragma unroll
         for (int i = 0; i < 8; ++i) s = __dp4a(w[i], x[i], s);
-        return __fmul_rn(__fmul_rn(d, xd), (float)s);
+        S1 += s;
+    }
+    __device__ __forceinline__ float finish(int S1, int, float xd) const {
+        return __fmul_rn(__fmul_rn(d, xd), (float)S1);
     }
 };
 
@@ -244,15 +289,18 @@ struct BlockW<T_Q4_K> {
             m = (byte(sb + 4) >> 4) | ((byte(sb) >> 6) << 4);
         }
     }
-    __device__ __forceinline__ float dot(const int *x, float xd, int s8, int, int) const {
+    __device__ __forceinline__ void accum(const int *x, int s8, int, int, int &S1, int &S2) const {
         int s = 0;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             s = __dp4a(q[i] & 0x0f0f0f0f, x[i], s);
             s = __dp4a((q[i] >> 4) & 0x0f0f0f0f, x[4 + i], s);
         }
-        const float a = (float)(s * sc), c = (float)(s8 * m);
-        return __fmul_rn(xd, __fsub_rn(__fmul_rn(d, a), __fmul_rn(dm, c)));
+        S1 += sc * s;
+        S2 += m * s8;
+    }
+    __device__ __forceinline__ float finish(int S1, int S2, float xd) const {
+        return __fmul_rn(xd, __fsub_rn(__fmul_rn(d, (float)S1), __fmul_rn(dm, (float)S2)));
     }
 };
 
@@ -277,7 +325,7 @@ struct BlockW<T_Q6_K> {
         sb = (int8_t)(s >> 8);
         d = h2f(ldw<GLOBAL>(reinterpret_cast<const unsigned short *>(W.e) + wsslot(W, row, j >> 3)));
     }
-    __device__ __forceinline__ float dot(const int *x, float xd, int, int s16a, int s16b) const {
+    __device__ __forceinline__ void accum(const int *x, int, int s16a, int s16b, int &S1, int &) const {
         int da = 0, db = 0;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -286,7 +334,10 @@ struct BlockW<T_Q6_K> {
         }
         da -= 32 * s16a;
         db -= 32 * s16b;
-        return __fmul_rn(__fmul_rn(d, xd), (float)(sa * da + sb * db));
+        S1 += sa * da + sb * db;
+    }
+    __device__ __forceinline__ float finish(int S1, int, float xd) const {
+        return __fmul_rn(__fmul_rn(d, xd), (float)S1);
     }
 };
 
@@ -339,9 +390,9 @@ __device__ __forceinline__ void epilogue_store(const GemvArgs &g, int row, int n
     }
 }
 
-// Matmul over activations already quantized in global memory (the encoder's
-// b*S token rows): one warp per group of 32 weight rows, lane = row, blocks
-// accumulated left to right; NB activation rows per pass.
+// Matmul over activations already quantized in global memory: one warp per
+// group of 32 weight rows, lane = row, unit partials accumulated left to right;
+// NB activation rows per pass.
 template <int TYPE, int EPI>
 __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs g) {
     constexpr int NB = 8;
@@ -354,34 +405,46 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs g) {
             float acc[NB];
 #pragma unroll
             for (int i = 0; i < NB; ++i) acc[i] = 0.0f;
-#pragma unroll 2
-            for (int j = 0; j < nb; ++j) {
-                if constexpr (TYPE == T_F32) {
+            if constexpr (TYPE == T_F32) {
+                for (int j = 0; j < nb; ++j)
 #pragma unroll
                     for (int i = 0; i < NB; ++i) {
                         if (n0 + i >= g.rows) break;
                         const float p = f32_block(W, row, j, g.xf + (size_t)(n0 + i) * W.K + 32 * j);
                         acc[i] = j == 0 ? p : __fadd_rn(acc[i], p);
                     }
-                } else {
+            } else {
+                constexpr int UB = unit_blocks<TYPE>();
+                for (int u = 0; u < nb; u += UB) {
+                    int S1[NB], S2[NB];
+#pragma unroll
+                    for (int i = 0; i < NB; ++i) S1[i] = S2[i] = 0;
                     BlockW<TYPE> bw;
-                    bw.load(W, row, j);
+#pragma unroll 2
+                    for (int j = u; j < u + UB; ++j) {
+                        bw.load(W, row, j);
+#pragma unroll
+                        for (int i = 0; i < NB; ++i) {
+                            const int n = n0 + i;
+                            if (n >= g.rows) break;
+                            const int4 *xs = reinterpret_cast<const int4 *>(g.x.q + (size_t)n * W.K + 32 * j);
+                            const int4 x0 = xs[0], x1 = xs[1];
+                            const int xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                            int s32 = 0, s16a = 0, s16b = 0;
+                            if constexpr (TYPE == T_Q4_K) s32 = g.x.s32[(size_t)n * nb + j];
+                            if constexpr (TYPE == T_Q6_K) {
+                                s16a = g.x.s16[(size_t)n * 2 * nb + 2 * j];
+                                s16b = g.x.s16[(size_t)n * 2 * nb + 2 * j + 1];
+                            }
+                            bw.accum(xv, s32, s16a, s16b, S1[i], S2[i]);
+                        }
+                    }
 #pragma unroll
                     for (int i = 0; i < NB; ++i) {
                         const int n = n0 + i;
                         if (n >= g.rows) break;
-                        const int4 *xs = reinterpret_cast<const int4 *>(g.x.q + (size_t)n * W.K + 32 * j);
-                        const int4 x0 = xs[0], x1 = xs[1];
-                        const int xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-                        const float xd = g.x.d[(size_t)n * nb + j];
-                        int s32 = 0, s16a = 0, s16b = 0;
-                        if constexpr (TYPE == T_Q4_K) s32 = g.x.s32[(size_t)n * nb + j];
-                        if constexpr (TYPE == T_Q6_K) {
-                            s16a = g.x.s16[(size_t)n * 2 * nb + 2 * j];
-                            s16b = g.x.s16[(size_t)n * 2 * nb + 2 * j + 1];
-                        }
-                        const float p = bw.dot(xv, xd, s32, s16a, s16b);
-                        acc[i] = j == 0 ? p : __fadd_rn(acc[i], p);
+                        const float p = bw.finish(S1[i], S2[i], g.x.d[(size_t)n * nb + u]);
+                        acc[i] = u == 0 ? p : __fadd_rn(acc[i], p);
                     }
                 }
             }

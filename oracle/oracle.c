@@ -17,11 +17,14 @@
  *     pad-after-finish bookkeeping), driven as graph.rs:262-297 does (step 0
  *     consumes </s> and is discarded, the target-language token is forced).
  *   - beam search: translator.rs:250-335 and topk 343-358.
- *   - quantized matmuls: candle-core 0.11.0's CUDA QMatMul (not in the
- *     reference tree) quantizes activations to q8_1 blocks (32 values, f16
- *     scale) and takes integer block dot products against the GGUF blocks,
- *     applying the float scales per block (llama.cpp's published MMVQ/MMQ
- *     algorithm). That is restated below.
+ *   - quantized matmuls: candle-core 0.11.0's QMatMul (not in the reference
+ *     tree) quantizes activations and takes integer block dot products against
+ *     the GGUF blocks. Restated below: Q8_0 weights against 32-value
+ *     activation blocks with f16 scales (per-block float scale, as candle's
+ *     q8_0 vec_dot and MMVQ); Q4_K / Q6_K weights against Q8_K-style
+ *     activations (one f32 scale per 256 values) with integer sums over each
+ *     super-block and the float scales applied once per super-block, as
+ *     candle's CPU k-quant vec_dot does (ggml's published algorithm).
  *
  * Reduction orders are not specified by the reference (candle leaves them to
  * its kernels). This oracle FIXES one order for every float reduction, and the
@@ -29,9 +32,10 @@
  *   SUM32(v[0..n))  lane l (0..31) sums v[l], v[l+32], ... left to right
  *                   (empty lane = 0), then pairs are added at distances
  *                   1,2,4,8,16 (acc[l] + acc[l^o]); the result is acc[0].
- *   ROW(p[0..nb))   per-block partials of a matmul row, summed left to right
- *                   in block order (one accumulator per output: the shape a
- *                   tensor-core epilogue can keep per (row, column)).
+ *   ROW(p[0..n))    per-unit partials of a matmul row (32-blocks, or 256-value
+ *                   super-blocks for k-quants), summed left to right (one
+ *                   accumulator per output: the shape a tensor-core epilogue
+ *                   can keep per (row, column)).
  *   exp             own implementation (Cody-Waite reduction with a 2-term
  *                   ln2 split, degree-7 Taylor polynomial in fmaf, exact 2^k
  *                   scaling); see mgb_exp.
@@ -39,7 +43,8 @@
  *                   -ffp-contract=off so nothing else is fused.
  * Parity is pinned by tests/ against gguf-py's dequantizer (block layouts)
  * and Hugging Face transformers' M2M100 (f32 model semantics, tiny model);
- * the q8_1 matmul arithmetic itself is unpinned (candle cannot be built here).
+ * the quantized matmul arithmetic itself is unpinned (candle cannot be built
+ * here).
  */
 #include <math.h>
 #include <stdint.h>
@@ -420,24 +425,28 @@ ORC_EXPORT int orc_config(orc_model *m, int *out) {
 }
 
 /* ------------------------------------------------------------------------ */
-/* Activation quantization (q8_1 blocks) and the matmul spec                  */
+/* Activation quantization and the matmul spec                                */
 
 typedef struct {
     int8_t *q;  /* [rows, K] */
-    float *d;   /* [rows, K/32] */
+    float *d;   /* [rows, K/32]: the scale of the group holding each 32-block */
 } qact_t;
 
-static void quantize_act(const float *x, int rows, int K, qact_t *out) {
-    int nb = K / 32;
+/* group = 1: blocks of 32 values with an f16-rounded scale (q8_1 / Q8_0 style,
+ * consumed by Q8_0 weights). group = 8: one f32 scale per 256-value
+ * super-block (Q8_K style, consumed by Q4_K and Q6_K weights, as candle's
+ * k-quant vec_dot does). Both: d = amax/127, q = round(v/d), q = 0 if amax = 0. */
+static void quantize_act(const float *x, int rows, int K, int group, qact_t *out) {
+    int nb = K / 32, gv = 32 * group;
     for (int r = 0; r < rows; ++r) {
-        for (int j = 0; j < nb; ++j) {
-            const float *v = x + (size_t)r * K + 32 * j;
+        for (int u = 0; u < K / gv; ++u) {
+            const float *v = x + (size_t)r * K + (size_t)gv * u;
             float amax = 0.0f;
-            for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+            for (int i = 0; i < gv; ++i) amax = fmaxf(amax, fabsf(v[i]));
             float dd = amax / 127.0f;
-            for (int i = 0; i < 32; ++i)
-                out->q[(size_t)r * K + 32 * j + i] = amax == 0.0f ? 0 : (int8_t)roundf(v[i] / dd);
-            out->d[(size_t)r * nb + j] = rnd_h(dd);
+            for (int i = 0; i < gv; ++i)
+                out->q[(size_t)r * K + (size_t)gv * u + i] = amax == 0.0f ? 0 : (int8_t)roundf(v[i] / dd);
+            for (int j = 0; j < group; ++j) out->d[(size_t)r * nb + group * u + j] = group == 1 ? rnd_h(dd) : dd;
         }
     }
 }
@@ -501,21 +510,29 @@ static void unpack_row(const tensor_t *t, long r, wrow_t *w) {
 }
 
 /*
- * y[n, r] = ROW(p_j) + bias[r] for every activation row n and weight row r.
- * Per 32-block j (xq = activation q8_1 values, xd = its f16-rounded scale):
+ * y[n, r] = ROW(p_u) + bias[r] for every activation row n and weight row r,
+ * over the row's units u: 32-blocks for F32 / Q8_0, 256-value super-blocks for
+ * Q4_K / Q6_K. xq = activation values, xd = the unit's activation scale;
+ * integer sums are exact (int32), float operations as written:
  *   F32  : p = fmaf chain of w*x over the block (activations not quantized)
  *   Q8_0 : p = (d*xd) * float(sum w*xq)
- *   Q4_K : p = xd * (d*float(sc*sum q*xq) - dmin*float(m*sum xq))
- *   Q6_K : p = (d*xd) * float(sc_a*sum_a (q-32)*xq + sc_b*sum_b (q-32)*xq)
+ *   Q4_K : S1 = sum_j sc_j * (sum_{i in j} q*xq), S2 = sum_j m_j * (sum_{i in j} xq)
+ *          p = xd * (d*float(S1) - dmin*float(S2))
+ *   Q6_K : S = sum over the 16 halves h of sc_h * (sum_{i in h} (q-32)*xq)
+ *          p = (d*xd) * float(S)
+ * This is the arithmetic of candle's CPU k-quant dot products against Q8_K
+ * activations (ggml's vec_dot_q4_K_q8_K / vec_dot_q6_K_q8_K: integer sums per
+ * super-block, float scales once per super-block).
  */
 static void linear(const linear_t *L, const float *x, int rows, float *y, int relu) {
     const tensor_t *t = L->w;
     int K = (int)t->cols, N = (int)t->rows, nb = K / 32;
+    const int kq = t->type == GT_Q4_K || t->type == GT_Q6_K;
     qact_t xa = {0};
     if (t->type != GT_F32) {
         xa.q = malloc((size_t)rows * K);
         xa.d = malloc((size_t)rows * nb * sizeof(float));
-        quantize_act(x, rows, K, &xa);
+        quantize_act(x, rows, K, kq ? 8 : 1, &xa);
     }
 #pragma omp parallel
     {
@@ -530,6 +547,32 @@ static void linear(const linear_t *L, const float *x, int rows, float *y, int re
             if (t->type == GT_F32) wr32 = (const float *)(t->data + (size_t)r * 4 * K);
             else unpack_row(t, r, &w);
             for (int n = 0; n < rows; ++n) {
+                if (kq) {
+                    for (int u = 0; u < nb / 8; ++u) {
+                        int S1 = 0, S2 = 0;
+                        for (int j = 8 * u; j < 8 * u + 8; ++j) {
+                            const int8_t *xq = xa.q + (size_t)n * K + 32 * j, *wq = w.q + 32 * j;
+                            if (t->type == GT_Q4_K) {
+                                int dot = 0, s8 = 0;
+                                for (int i = 0; i < 32; ++i) { dot += wq[i] * xq[i]; s8 += xq[i]; }
+                                S1 += w.sc0[j] * dot;
+                                S2 += w.sc1[j] * s8;
+                            } else {
+                                int da = 0, db = 0;
+                                for (int i = 0; i < 16; ++i) { da += wq[i] * xq[i]; db += wq[16 + i] * xq[16 + i]; }
+                                S1 += w.sc0[j] * da + w.sc1[j] * db;
+                            }
+                        }
+                        float xd = xa.d[(size_t)n * nb + 8 * u];
+                        if (t->type == GT_Q4_K) p[u] = xd * (w.s0[8 * u] * (float)S1 - w.s1[8 * u] * (float)S2);
+                        else p[u] = (w.s0[8 * u] * xd) * (float)S1;
+                    }
+                    float v = row_reduce(p, nb / 8);
+                    if (L->b) v = v + L->b[r];
+                    if (relu) v = v > 0.0f ? v : 0.0f;
+                    y[(size_t)n * N + r] = v;
+                    continue;
+                }
                 for (int j = 0; j < nb; ++j) {
                     if (t->type == GT_F32) {
                         const float *xv = x + (size_t)n * K + 32 * j;
@@ -540,21 +583,9 @@ static void linear(const linear_t *L, const float *x, int rows, float *y, int re
                     }
                     const int8_t *xq = xa.q + (size_t)n * K + 32 * j, *wq = w.q + 32 * j;
                     float xd = xa.d[(size_t)n * nb + j];
-                    if (t->type == GT_Q8_0) {
-                        int s = 0;
-                        for (int i = 0; i < 32; ++i) s += wq[i] * xq[i];
-                        p[j] = (w.s0[j] * xd) * (float)s;
-                    } else if (t->type == GT_Q4_K) {
-                        int dot = 0, s8 = 0;
-                        for (int i = 0; i < 32; ++i) { dot += wq[i] * xq[i]; s8 += xq[i]; }
-                        float a = (float)(dot * w.sc0[j]), c = (float)(s8 * w.sc1[j]);
-                        p[j] = xd * (w.s0[j] * a - w.s1[j] * c);
-                    } else { /* Q6_K */
-                        int da = 0, db = 0;
-                        for (int i = 0; i < 16; ++i) { da += wq[i] * xq[i]; db += wq[16 + i] * xq[16 + i]; }
-                        int s = w.sc0[j] * da + w.sc1[j] * db;
-                        p[j] = (w.s0[j] * xd) * (float)s;
-                    }
+                    int s = 0;
+                    for (int i = 0; i < 32; ++i) s += wq[i] * xq[i];
+                    p[j] = (w.s0[j] * xd) * (float)s;
                 }
                 float v = row_reduce(p, nb);
                 if (L->b) v = v + L->b[r];
