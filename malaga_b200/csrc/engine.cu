@@ -269,7 +269,11 @@ struct mgb_ctx {
     // Activation rows from which matmuls run on the tensor cores (tcgen05)
     // instead of the small-batch kernels; MGB_TC_MIN_ROWS overrides (tests).
     int tc_min_rows = 16;
+    // Decode-step tensor-core matmuls build their activations in the kernel
+    // (1) or read them from qprep_row_kernel (0); MGB_TC_FUSED overrides.
+    int tc_fused = 0;
     int sms = 148;  // multiprocessor count of the device (one tensor-core CTA each)
+    size_t smem_optin = 227 * 1024 - 4096;  // dynamic shared memory a tensor-core CTA may take
 
     mgb_status dalloc(void **p, size_t bytes) {
         if (inject_armed && opts.fail_alloc_after >= 0 && alloc_count++ == opts.fail_alloc_after)
@@ -780,19 +784,52 @@ static mgb_status qprep_row(mgb_ctx *c, PrepArgs p, const QAct &act, const Matri
     return e == cudaSuccess ? MGB_OK : cuda_err(e, "activation prep launch");
 }
 
-// Tile width (activation rows per tile) of a tensor-core matmul: the widest
-// tile that still gives every SM a tile; persistent CTAs, one per SM.
-static void tc_shape(const Matrix &W, int rows, int sms, int &nt, int &grid) {
-    const int row_tiles = W.Np / 128;
-    nt = 8;
-    for (int cand : {64, 32, 16}) {
-        if ((long)row_tiles * ((rows + cand - 1) / cand) >= sms) {
-            nt = cand;
-            break;
-        }
+// Shared memory of a tensor-core launch (gemm_tc.cuh): the stage and tile
+// rings, plus the resident activations when the kernel builds them.
+template <int TYPE>
+static size_t tc_smem_t(int nt, bool fused, int nb) {
+    auto base = [&](auto ntc) -> size_t {
+        constexpr int NT = decltype(ntc)::value;
+        return fused ? gemm_tc_smem_base<TYPE, NT, true>() + tc::fused_act_bytes(TYPE, NT, nb)
+                     : gemm_tc_smem_base<TYPE, NT, false>();
+    };
+    switch (nt) {
+        case 8: return base(std::integral_constant<int, 8>{});
+        case 16: return base(std::integral_constant<int, 16>{});
+        case 32: return base(std::integral_constant<int, 32>{});
+        default: return base(std::integral_constant<int, 64>{});
     }
-    const long tiles = (long)row_tiles * ((rows + nt - 1) / nt);
-    grid = (int)std::min<long>(tiles, sms);
+}
+
+static size_t tc_smem(int type, int nt, bool fused, int nb) {
+    switch (type) {
+        case T_Q8_0: return tc_smem_t<T_Q8_0>(nt, fused, nb);
+        case T_Q4_K: return tc_smem_t<T_Q4_K>(nt, fused, nb);
+        default: return tc_smem_t<T_Q6_K>(nt, fused, nb);
+    }
+}
+
+// Tile width (activation rows per tile) and grid of a tensor-core matmul: the
+// widest tile that still gives every SM a tile (and, for activations built in
+// the kernel, whose resident activations fit in shared memory); persistent
+// CTAs, one per SM. Fused launches give each token tile the same number of CTAs.
+static bool tc_shape(const Matrix &W, int rows, int sms, bool fused, size_t smem_limit, int &nt, int &grid) {
+    const int row_tiles = W.Np / 128;
+    nt = 0;
+    for (int cand : {64, 32, 16, 8}) {
+        if (fused && tc_smem(W.type, cand, true, W.nb) > smem_limit) continue;
+        nt = cand;  // narrower tiles until every SM has one (or the narrowest that fits)
+        if ((long)row_tiles * ((rows + cand - 1) / cand) >= sms) break;
+    }
+    if (!nt) return false;
+    const int tok_tiles = (rows + nt - 1) / nt;
+    if (fused) {
+        const int per = std::max(1, std::min(row_tiles, sms / tok_tiles));
+        grid = per * tok_tiles;
+    } else {
+        grid = (int)std::min<long>((long)row_tiles * tok_tiles, sms);
+    }
+    return true;
 }
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
@@ -834,8 +871,9 @@ static mgb_status tmap(CUtensorMap *m, const void *base, int rank, const uint64_
     return MGB_OK;
 }
 
-// The launch's tensor maps (layouts: engine.h Matrix, gemm_tc.cuh tc::Maps).
-static mgb_status make_maps(const Matrix &W, const QAct &x, int nt, tc::Maps &m) {
+// The launch's tensor maps (layouts: engine.h Matrix, gemm_tc.cuh tc::Maps);
+// x = null when the kernel builds its activations.
+static mgb_status make_maps(const Matrix &W, const QAct *x, int nt, tc::Maps &m) {
     memset(&m, 0, sizeof m);
     const uint64_t G = (uint64_t)W.Np / 32, nb = W.nb, nsb = W.nsb;
     // one weight region: X words per (group, block-or-super-block) slice, n slices, boxes of k slices
@@ -862,48 +900,51 @@ static mgb_status make_maps(const Matrix &W, const QAct &x, int nt, tc::Maps &m)
         default:
             return set_err(MGB_ERR_UNSUPPORTED, "tensor-core matmul of type %d", W.type);
     }
-    const uint64_t rs = (uint64_t)x.rs, H = W.type == T_Q6_K ? 2 : 1;
+    if (!x) return MGB_OK;  // activations built in the kernel
+    const uint64_t rs = (uint64_t)x->rs;
     {
-        const uint64_t dims[4] = {32, rs / 8, H, nb}, str[3] = {256, rs * 32, H * rs * 32};
-        const uint32_t box[4] = {32, (uint32_t)nt / 8, (uint32_t)H, 8};
-        TRY(tmap(&m.xq, x.tq, 4, dims, str, box, false));
+        const uint64_t dims[3] = {32, rs / 8, nb}, str[2] = {256, rs * 32};
+        const uint32_t box[3] = {32, (uint32_t)nt / 8, 8};
+        TRY(tmap(&m.xq, x->tq, 3, dims, str, box, false));
     }
     if (W.type == T_Q4_K) {
         const uint64_t dims[2] = {rs * 4, nsb}, str[1] = {rs * 32};
         const uint32_t box[2] = {(uint32_t)nt * 4, 1};
-        TRY(tmap(&m.xr, x.trec, 2, dims, str, box, false));
+        TRY(tmap(&m.xr, x->trec, 2, dims, str, box, false));
     } else {
         const uint64_t units = W.type == T_Q6_K ? nsb : nb;
         const uint64_t dims[2] = {rs / 2, units}, str[1] = {rs * 4};
         const uint32_t box[2] = {(uint32_t)nt / 2, W.type == T_Q6_K ? 1u : 8u};
-        TRY(tmap(&m.xr, x.trec, 2, dims, str, box, false));
+        TRY(tmap(&m.xr, x->trec, 2, dims, str, box, false));
     }
     return MGB_OK;
 }
 
-template <int TYPE, int EPI>
+template <int TYPE, int EPI, int XM>
 static mgb_status gemm_tc_t(mgb_ctx *c, const tc::Args &a, int nt, int grid) {
-    auto go = [&](auto kern, size_t sh) -> cudaError_t {
+    const size_t sh = tc_smem(TYPE, nt, XM >= 0, a.W.nb);
+    auto go = [&](auto kern) -> cudaError_t {
         cudaError_t e = allow_smem(kern, sh);
         return e == cudaSuccess ? launch_pdl(kern, dim3(grid), dim3(tc::kThreads), sh, c->stream, a) : e;
     };
     cudaError_t e;
     switch (nt) {
-        case 8: e = go(gemm_tc_kernel<TYPE, EPI, 8>, gemm_tc_smem<TYPE, 8>()); break;
-        case 16: e = go(gemm_tc_kernel<TYPE, EPI, 16>, gemm_tc_smem<TYPE, 16>()); break;
-        case 32: e = go(gemm_tc_kernel<TYPE, EPI, 32>, gemm_tc_smem<TYPE, 32>()); break;
-        default: e = go(gemm_tc_kernel<TYPE, EPI, 64>, gemm_tc_smem<TYPE, 64>()); break;
+        case 8: e = go(gemm_tc_kernel<TYPE, EPI, 8, XM>); break;
+        case 16: e = go(gemm_tc_kernel<TYPE, EPI, 16, XM>); break;
+        case 32: e = go(gemm_tc_kernel<TYPE, EPI, 32, XM>); break;
+        default: e = go(gemm_tc_kernel<TYPE, EPI, 64, XM>); break;
     }
     ++c->launches;
     return e == cudaSuccess ? MGB_OK : cuda_err(e, "tensor-core matmul launch");
 }
 
-// y = W . act for `rows` activation rows on the tensor cores, epilogue EPI.
-// The LM head (ARGMAX) runs in launches of at most 64 rows (one token tile
-// each); *ctas returns its CTA count, the partial count per row.
-template <int EPI>
-static mgb_status gemm_tc(mgb_ctx *c, const Matrix &W, const QAct &act, int rows, const GemvArgs &g,
-                          int *ctas = nullptr) {
+// y = W . x for `rows` activation rows on the tensor cores, epilogue EPI.
+// XM < 0: x was written by qprep_row (act); otherwise the kernel builds it from
+// p in mode XM. The LM head (ARGMAX) runs in launches of at most 64 rows (one
+// token tile each); *ctas returns its CTA count, the partial count per row.
+template <int EPI, int XM>
+static mgb_status gemm_tc(mgb_ctx *c, const Matrix &W, const QAct *act, const PrepArgs *p, int rows,
+                          const GemvArgs &g, int *ctas = nullptr) {
     const int chunk = EPI == EPI_ARGMAX ? 64 : rows;
     for (int t0 = 0; t0 < rows; t0 += chunk) {
         const int n = std::min(chunk, rows - t0);
@@ -916,8 +957,14 @@ static mgb_status gemm_tc(mgb_ctx *c, const Matrix &W, const QAct &act, int rows
         a.g.W = W;
         a.g.rows = n;
         a.err = c->d_err;
+        if (p) {
+            a.p = *p;
+            a.p.K = W.K;
+            if (a.p.x) a.p.x += (size_t)t0 * W.K;
+        }
         int nt, grid;
-        tc_shape(W, n, c->sms, nt, grid);
+        if (!tc_shape(W, n, c->sms, XM >= 0, c->smem_optin, nt, grid))
+            return set_err(MGB_ERR_UNSUPPORTED, "no tensor-core tile fits a %d-value row", W.K);
         if (EPI == EPI_ARGMAX) {
             if (a.g.logits) a.g.logits += (size_t)t0 * W.N;
             a.g.part_v += (size_t)t0 * grid;
@@ -926,11 +973,11 @@ static mgb_status gemm_tc(mgb_ctx *c, const Matrix &W, const QAct &act, int rows
         a.row_tiles = W.Np / 128;
         a.tok_tiles = (n + nt - 1) / nt;
         if (ctas) *ctas = grid;
-        TRY(make_maps(W, act, nt, a.m));
+        TRY(make_maps(W, XM >= 0 ? nullptr : act, nt, a.m));
         switch (W.type) {
-            case T_Q8_0: TRY((gemm_tc_t<T_Q8_0, EPI>(c, a, nt, grid))); break;
-            case T_Q4_K: TRY((gemm_tc_t<T_Q4_K, EPI>(c, a, nt, grid))); break;
-            case T_Q6_K: TRY((gemm_tc_t<T_Q6_K, EPI>(c, a, nt, grid))); break;
+            case T_Q8_0: TRY((gemm_tc_t<T_Q8_0, EPI, XM>(c, a, nt, grid))); break;
+            case T_Q4_K: TRY((gemm_tc_t<T_Q4_K, EPI, XM>(c, a, nt, grid))); break;
+            case T_Q6_K: TRY((gemm_tc_t<T_Q6_K, EPI, XM>(c, a, nt, grid))); break;
             default: return set_err(MGB_ERR_UNSUPPORTED, "tensor-core matmul of type %d", W.type);
         }
     }
@@ -1015,16 +1062,24 @@ static mgb_status new_state(mgb_ctx *c, int b, int s, int m, StaticState **out) 
     return MGB_OK;
 }
 
-// One matmul of the step: tensor cores (activation prep kernel + tcgen05
-// matmul) from tc_min_rows rows, otherwise the fused small-batch kernel.
+// One matmul of the step: from tc_min_rows rows the tcgen05 matmul, which
+// builds its LayerNorm / embedding / plain activations itself (rows of at most
+// 2048 values under LayerNorm, token tiles that fit in shared memory; others go
+// through qprep_row first); otherwise the fused small-batch kernel.
 template <int EPI, int MODE>
 static mgb_status step_op(mgb_ctx *c, StaticState *st, const FusedArgs &f, int *ctas = nullptr) {
     const int b = f.g.rows;
-    if (b >= c->tc_min_rows && tc_ok(f.g.W) && st->act.tq) {
+    if (b >= c->tc_min_rows && tc_ok(f.g.W)) {
         PrepArgs p = f.p;
         p.rows = b;
+        p.K = f.g.W.K;
+        int nt, grid;
+        if (c->tc_fused && (MODE == PREP_PLAIN || f.g.W.K <= 2048) &&
+            tc_shape(f.g.W, std::min(b, EPI == EPI_ARGMAX ? 64 : b), c->sms, true, c->smem_optin, nt, grid))
+            return gemm_tc<EPI, MODE>(c, f.g.W, nullptr, &p, b, f.g, ctas);
+        if (!st->act.tq) return set_err(MGB_ERR_INVALID, "tensor-core activation buffers missing");
         TRY(qprep_row<MODE>(c, p, st->act, f.g.W));
-        return gemm_tc<EPI>(c, f.g.W, st->act, b, f.g, ctas);
+        return gemm_tc<EPI, -1>(c, f.g.W, &st->act, nullptr, b, f.g, ctas);
     }
     if (ctas) *ctas = kLmParts;
     return fused<EPI, MODE>(c, f);
@@ -1194,10 +1249,10 @@ static mgb_status encode(mgb_ctx *c, const uint32_t *ids, const uint32_t *lens, 
         if (tc_ok(W)) {
             TRY(mode == PREP_LN ? qprep_row<PREP_LN>(c, p, act, W) : qprep_row<PREP_PLAIN>(c, p, act, W));
             switch (epi) {
-                case EPI_STORE: return gemm_tc<EPI_STORE>(c, W, act, rows, gg);
-                case EPI_RELU: return gemm_tc<EPI_RELU>(c, W, act, rows, gg);
-                case EPI_RESID: return gemm_tc<EPI_RESID>(c, W, act, rows, gg);
-                default: return gemm_tc<EPI_CROSSKV>(c, W, act, rows, gg);
+                case EPI_STORE: return gemm_tc<EPI_STORE, -1>(c, W, &act, nullptr, rows, gg);
+                case EPI_RELU: return gemm_tc<EPI_RELU, -1>(c, W, &act, nullptr, rows, gg);
+                case EPI_RESID: return gemm_tc<EPI_RESID, -1>(c, W, &act, nullptr, rows, gg);
+                default: return gemm_tc<EPI_CROSSKV, -1>(c, W, &act, nullptr, rows, gg);
             }
         }
         p.group = act_group(W.type);
@@ -1267,7 +1322,7 @@ static mgb_status encode(mgb_ctx *c, const uint32_t *ids, const uint32_t *lens, 
         gk.H = Hd;
         gk.hd = hdd;
         gk.S = S;
-        mgb_status s2 = tc_ok(c->dec[l].ckv) ? gemm_tc<EPI_CROSSKV>(c, c->dec[l].ckv, act, rows, gk)
+        mgb_status s2 = tc_ok(c->dec[l].ckv) ? gemm_tc<EPI_CROSSKV, -1>(c, c->dec[l].ckv, &act, nullptr, rows, gk)
                                              : gemv(c, EPI_CROSSKV, gk);
         if (s2 != MGB_OK) {
             cudaFree(B->cross);
@@ -1475,8 +1530,14 @@ mgb_status mgb_open(const char *path, int device, const mgb_options *opts, mgb_c
     else mgb_default_options(&c->opts);
     CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
     if (const char *v = getenv("MGB_TC_MIN_ROWS")) c->tc_min_rows = std::max(1, atoi(v));
+    if (const char *v = getenv("MGB_TC_FUSED")) c->tc_fused = atoi(v) != 0;
     cudaDeviceGetAttribute(&c->sms, cudaDevAttrMultiProcessorCount, device);
     if (c->sms <= 0) c->sms = 148;
+    {
+        int optin = 0;
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+        if (optin > 8192) c->smem_optin = (size_t)optin - 4096;  // room for the kernel's static shared memory
+    }
     mgb_status s = load_model(c.get(), path);
     if (s != MGB_OK) {
         if (c->arena) cudaFree(c->arena);

@@ -382,14 +382,17 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
                  : "memory");
 }
 
+// One try_wait with a suspend-time hint: a thread whose phase is not complete
+// sleeps until it completes (or the hint runs out) instead of spinning, so
+// waiting warps do not take issue slots from working ones.
 __device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
     uint32_t done;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(done)
-        : "r"(a), "r"(parity)
+        : "r"(a), "r"(parity), "r"(20000u)
         : "memory");
     return done != 0;
 }
@@ -399,9 +402,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
     const uint32_t a = smem_u32(bar);
     if (mbar_try(a, parity)) return true;
     const uint64_t t0 = globaltimer();
-    for (uint32_t it = 1;; ++it) {
+    for (;;) {
         if (mbar_try(a, parity)) return true;
-        if ((it & 255) == 0 && globaltimer() - t0 > kWaitNs) return false;
+        if (globaltimer() - t0 > kWaitNs) return false;
     }
 }
 

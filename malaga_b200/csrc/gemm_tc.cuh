@@ -12,20 +12,28 @@
 //
 // One persistent CTA per SM walks its (128-row x NT-token) tiles in stages of
 // 8 blocks (256 values) with warp-specialized roles linked by mbarriers:
-//   warp 12     producer: one TMA tensor copy per weight region, one for the
-//               activation tiles (already in the UMMA K-major layout), one for
-//               the activation scale records, into a ring of RS stages;
-//   warps 0-3   converters: thread t unpacks weight row t of each block (Q4_K
-//               nibbles, Q6_K 6-bit values minus 32, Q8_0 bytes) into an int8
-//               128x32 tile in the canonical no-swizzle layout (ring of AS);
-//   warp 13     MMA: one tcgen05.mma per block into a ring of TS TMEM slots,
-//               committed to the barriers that free the tile, the slot's
-//               readers and the stage;
-//   warps 4-11  epilogue: warp w reads TMEM lanes 32(w%4).. (its weight rows)
+//   warp 10     producer: one TMA tensor copy per weight region (and, when the
+//               activations come from global memory, one for their tiles and
+//               one for their scale records) into a ring of RS stages;
+//   warps 8-9   converters: thread t unpacks weight rows t and t+64 of each
+//               block (Q4_K nibbles, Q6_K 6-bit values minus 32, Q8_0 bytes)
+//               into int8 128x32 tiles in the canonical no-swizzle layout (ring
+//               of AG groups); Q6_K gets two tiles per block, each with the
+//               other 16-value half zeroed, since the halves carry different
+//               scales;
+//   warp 11     MMA: each block's tcgen05.mma (two for Q6_K) into its TMEM
+//               columns (ring of TG groups), one commit per group to the
+//               barriers that free the tiles and wake the epilogue, one per
+//               stage to free the stage;
+//   warps 0-7   epilogue: warp w reads TMEM lanes 32(w%4).. (its weight rows)
 //               for half of the tile's tokens, accumulates, and stores.
-// Q6_K needs the two 16-value halves of a block separately (their scales
-// differ): its activation tiles hold every token twice, once with each half
-// zeroed, so one MMA with N = 2 NT yields both sums.
+// (12 warps: three per scheduler leave 168 registers per thread.)
+// Activations either arrive by TMA in the layout qprep_row_kernel writes (XM <
+// 0: the encoder's long inputs), or (XM = a PrepMode: the decode step) the
+// epilogue warps build the CTA's whole token tile in shared memory first
+// (LayerNorm / embedding / plain input, quantized in the engine's order), so
+// no separate activation kernel runs. A CTA then serves one token tile.
+// Roles hand over groups of BG blocks (2-8), one mbarrier operation per group.
 // Every mbarrier wait is bounded in time; when one runs out the CTA records an
 // error flag, every role stops, and the CTA waits for its own MMAs before it
 // releases TMEM and returns.
@@ -92,19 +100,12 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// TMA tensor copy (tile mode, no multicast) of box `coords` into shared memory.
+// TMA tensor copies (tile mode, no multicast) of one box into shared memory.
 __device__ __forceinline__ void tma3(void *dst, const CUtensorMap *m, int c0, int c1, int c2, uint64_t *bar) {
     asm volatile(
         "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
         "[%5];" ::"r"(smem_u32(dst)),
         "l"(m), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
-        : "memory");
-}
-__device__ __forceinline__ void tma4(void *dst, const CUtensorMap *m, int c0, int c1, int c2, int c3, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
-        "%5}], [%6];" ::"r"(smem_u32(dst)),
-        "l"(m), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
         : "memory");
 }
 __device__ __forceinline__ void tma2(void *dst, const CUtensorMap *m, int c0, int c1, uint64_t *bar) {
@@ -120,8 +121,8 @@ __host__ __device__ __forceinline__ int tile_off(int r, int k16) { return (r >> 
 
 // Tensor maps of one launch: weight regions a, b, c, e (3-D: 8-byte words of
 // one (32-row group, block) slice, blocks or super-blocks, groups), activation
-// tiles (4-D: 8-byte words of an 8-row core group, row groups, halves, blocks)
-// and activation scale records (2-D: 8-byte words of a unit's rows, units).
+// tiles (3-D: 8-byte words of an 8-row core group, row groups, blocks) and
+// activation scale records (2-D: 8-byte words of a unit's rows, units).
 struct Maps {
     CUtensorMap w[4];
     CUtensorMap xq, xr;
@@ -133,18 +134,19 @@ struct Args {
     int rows;        // activation rows
     int row_tiles;   // Np / 128
     int tok_tiles;   // ceil(rows / NT)
-    int tok0;        // first activation row (a multiple of 64) of this launch
+    int tok0;        // first activation row (a multiple of 64) of this launch (TMA activations)
     GemvArgs g;      // epilogue outputs
+    PrepArgs p;      // activation source (activations built in the kernel)
     uint32_t *err;
 };
 
-// Stage geometry per weight type and tile width.
-template <int TYPE, int NT>
+// Stage geometry per weight type, tile width and activation source.
+template <int TYPE, int NT, bool FX>
 struct Geo {
     static constexpr bool Q6 = TYPE == T_Q6_K, Q4 = TYPE == T_Q4_K, Q8 = TYPE == T_Q8_0;
-    static constexpr int H = Q6 ? 2 : 1;   // activation copies per block
-    static constexpr int COLS = H * NT;    // TMEM columns per block
-    static constexpr int KB = 8;           // blocks per stage
+    static constexpr int COLS = Q6 ? 2 * NT : NT;   // TMEM columns per block
+    static constexpr int ABYTES = Q6 ? 8192 : 4096;  // converted tile(s) of one block
+    static constexpr int KB = 8;                     // blocks per stage
     static constexpr int WA = Q8 ? 4 * KB * 1024 : 4 * KB * 512;                   // q / qs / ql
     static constexpr int WB = Q8 ? 4 * KB * 64 : (Q4 ? 4 * 512 : 4 * KB * 256);    // d / header / qh
     static constexpr int WC = Q6 ? 4 * KB * 64 : 0;                                // Q6_K scales
@@ -153,38 +155,249 @@ struct Geo {
     static constexpr int UPS = Q8 ? KB : 1;                                        // units per stage
     static constexpr int oB = WA, oC = oB + WB, oE = oC + WC;
     static constexpr int oXQ = (oE + WE + 1023) / 1024 * 1024;
-    static constexpr int oXR = oXQ + KB * H * NT * 32;
-    static constexpr int STAGE = (oXR + UPS * NT * RB + 1023) / 1024 * 1024;
-    static constexpr uint32_t TX = WA + WB + WC + WE + KB * H * NT * 32 + UPS * NT * RB;
-    static constexpr int AS = 8;                                                   // A tile slots
-    static constexpr int RS = (220 * 1024 - AS * 4096) / STAGE >= 4 ? 4 : 3;       // raw stages
-    static constexpr int TS = 512 / COLS < 16 ? 512 / COLS : 16;                   // TMEM slots
-    static constexpr int TCOLS_RAW = TS * COLS;
+    static constexpr int oXR = oXQ + (FX ? 0 : KB * NT * 32);
+    static constexpr int STAGE = (oXR + (FX ? 0 : UPS * NT * RB) + 1023) / 1024 * 1024;
+    static constexpr uint32_t TX = WA + WB + WC + WE + (FX ? 0 : KB * NT * 32 + UPS * NT * RB);
+    // Handoffs between roles move groups of BG blocks (one mbarrier operation
+    // per group, not per block). TMEM holds TG groups of BG * COLS columns; the
+    // converted tiles AG groups of BG tiles.
+    static constexpr int BG = Q6 ? (NT >= 64 ? 2 : 4) : (NT >= 64 ? 4 : 8);
+    static constexpr int GCOLS = BG * COLS;
+    static constexpr int TG = 512 / GCOLS >= 4 ? 4 : 512 / GCOLS;
+    static constexpr int AGB = BG * ABYTES;   // bytes of one converted group
+    // resident activations (fused: room for 4096-value rows, at most 66 KB)
+    static constexpr int RES = NT * 32 * 128 + 2048 < 66 * 1024 ? NT * 32 * 128 + 2048 : 66 * 1024;
+    // converted groups: 3 when two stages still fit beside them, else 2
+    static constexpr int AG = 220 * 1024 - (FX ? RES : 0) - 2 * STAGE >= 3 * AGB ? 3 : 2;
+    // raw stages: as many as fit (2 to 4) beside the rest
+    static constexpr int BUDGET = 220 * 1024 - AG * AGB - (FX ? RES : 0);
+    static constexpr int RS = BUDGET / STAGE >= 4 ? 4 : (BUDGET / STAGE >= 3 ? 3 : 2);
+    static_assert(2 * STAGE <= BUDGET, "stage ring does not fit");
+    static_assert(8 % BG == 0 && TG >= 2, "group geometry");
+    static constexpr int TCOLS_RAW = TG * GCOLS;
     static constexpr int TCOLS = TCOLS_RAW <= 32 ? 32 : (TCOLS_RAW <= 64 ? 64 : (TCOLS_RAW <= 128 ? 128 :
                                  (TCOLS_RAW <= 256 ? 256 : 512)));
-    static constexpr int SMEM = 1024 + RS * STAGE + AS * 4096;
-    static_assert(SMEM <= 227 * 1024, "stage ring too large");
+    static constexpr int oRES = RS * STAGE + AG * AGB;   // resident activations (fused)
 };
 
-constexpr int kThreads = 448;  // 14 warps
-constexpr int kProducerWarp = 12, kMmaWarp = 13;
+constexpr int kThreads = 384;  // 12 warps
+constexpr int kConvWarp = 8, kProducerWarp = 10, kMmaWarp = 11;
+
+// Resident activation bytes of a fused launch: tiles of every block, then the
+// scale records of every unit.
+__host__ __device__ inline size_t fused_act_bytes(int type, int nt, int nb) {
+    const int units = type == T_Q8_0 ? nb : nb / 8, rb = type == T_Q4_K ? 32 : 4;
+    return (size_t)nb * nt * 32 + (size_t)units * nt * rb;
+}
 
 }  // namespace tc
 
-template <int TYPE, int NT>
-__host__ __device__ constexpr size_t gemm_tc_smem() {
-    return (size_t)tc::Geo<TYPE, NT>::SMEM;
+template <int TYPE, int NT, bool FX>
+__host__ __device__ constexpr size_t gemm_tc_smem_base() {
+    return 1024 + (size_t)tc::Geo<TYPE, NT, FX>::oRES;
 }
 
-template <int TYPE, int EPI, int NT>
+// Argmax over the 32 lanes of NH tokens at once: halving steps hand half of the
+// remaining tokens to the partner lane, so after log2(NH) steps every lane
+// holds one token (lane >> (5 - log2 NH)) and plain butterfly steps finish it.
+// The merge keeps the larger value and the lower index on ties, so the result
+// is the same as any other order of comparisons.
+template <int NH>
+__device__ __forceinline__ void argmax_scatter(float (&v)[NH], uint32_t (&ix)[NH], int lane) {
+    int c = NH, o = 16;
+#pragma unroll
+    for (int step = 0; step < 6; ++step) {
+        if (c <= 1) break;
+        const bool up = (lane & o) != 0;
+        const int h = c / 2;
+#pragma unroll
+        for (int t = 0; t < NH / 2; ++t) {
+            if (t >= h) break;
+            const float mv = up ? v[t + h] : v[t], tv = up ? v[t] : v[t + h];
+            const uint32_t mi = up ? ix[t + h] : ix[t], ti = up ? ix[t] : ix[t + h];
+            const float rv = __shfl_xor_sync(0xffffffffu, tv, o);
+            const uint32_t ri = __shfl_xor_sync(0xffffffffu, ti, o);
+            float bv = mv;
+            uint32_t bi = mi;
+            argmax_merge(bv, bi, rv, ri);
+            v[t] = bv;
+            ix[t] = bi;
+        }
+        c = h;
+        o >>= 1;
+    }
+#pragma unroll
+    for (int step = 0; step < 5; ++step) {
+        if (o == 0) break;
+        const float rv = __shfl_xor_sync(0xffffffffu, v[0], o);
+        const uint32_t ri = __shfl_xor_sync(0xffffffffu, ix[0], o);
+        argmax_merge(v[0], ix[0], rv, ri);
+        o >>= 1;
+    }
+}
+
+// Builds the q8 activations of token tile `tt` in shared memory (fused mode):
+// tiles [block][NT rows][32] in the UMMA K-major layout and the unit records.
+// One warp per token (warps w, w+nw, ...); same arithmetic as the activation
+// kernels: SUM32 LayerNorm statistics, then one scale per unit (the consumer's
+// groups). Units are handled UC at a time so that their loads and their amax
+// reductions overlap; Q4_K's per-block sums are added afterwards from the bytes.
+template <int TYPE, int NT, int MODE>
+__device__ void fused_prologue(const PrepArgs &p, int rows, int tt, bool write_x, uint8_t *xt, uint8_t *xr, int w,
+                               int nw, int lane) {
+    constexpr int G = act_group(TYPE), MAXV = 64;  // LayerNorm rows up to 2048 values
+    constexpr int UC = G == 8 ? 4 : 16;            // units per batch (32 or 16 values per lane)
+    const int K = p.K, T = K >> 5, nb = T, nu = nb / G;
+    for (int n = w; n < NT; n += nw) {
+        const int tok = tt * NT + n;
+        if (tok >= rows) break;  // uniform across the warp
+        uint32_t id = 0;
+        const float *pos = nullptr;
+        if constexpr (MODE == PREP_EMBED_LN) {
+            id = p.ids[tok];
+            pos = p.pos_table + (size_t)(*p.step + p.pos_base) * K;
+        }
+        auto input = [&](int i) -> float {
+            if constexpr (MODE == PREP_EMBED_LN) {
+                const float v = __fadd_rn(__fmul_rn(deq_elem(p.embed, (int)id, i), p.scale), pos[i]);
+                if (write_x) p.x_out[(size_t)tok * K + i] = v;
+                return v;
+            } else {
+                return p.x[(size_t)tok * K + i];
+            }
+        };
+        float vals[MAXV];
+        float mean = 0.f, rstd = 0.f;
+        if constexpr (MODE != PREP_PLAIN) {
+            // the whole row in registers: element 32t + lane in vals[t]
+#pragma unroll
+            for (int t = 0; t < MAXV; ++t)
+                if (t < T) vals[t] = input(32 * t + lane);
+            float sum = 0.0f;
+#pragma unroll
+            for (int t = 0; t < MAXV; ++t)
+                if (t < T) sum = t == 0 ? vals[t] : __fadd_rn(sum, vals[t]);
+            mean = __fdiv_rn(warp_tree(sum), (float)K);
+            float s2 = 0.0f;
+#pragma unroll
+            for (int t = 0; t < MAXV; ++t)
+                if (t < T) {
+                    const float c = __fsub_rn(vals[t], mean);
+                    const float c2 = __fmul_rn(c, c);
+                    s2 = t == 0 ? c2 : __fadd_rn(s2, c2);
+                }
+            const float var = __fdiv_rn(warp_tree(s2), (float)K);
+            rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
+            // normalized values in place
+#pragma unroll
+            for (int t = 0; t < MAXV; ++t)
+                if (t < T) {
+                    const int i = 32 * t + lane;
+                    vals[t] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(vals[t], mean), rstd), p.gamma[i]), p.beta[i]);
+                }
+        }
+        // a batch of UC units: amax of each (interleaved reductions), then the bytes
+        auto batch = [&](int u0, float (&y)[UC][G]) {
+            float m[UC];
+#pragma unroll
+            for (int c = 0; c < UC; ++c) {
+                m[c] = fabsf(y[c][0]);
+#pragma unroll
+                for (int g = 1; g < G; ++g) m[c] = fmaxf(m[c], fabsf(y[c][g]));
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                for (int c = 0; c < UC; ++c) m[c] = fmaxf(m[c], __shfl_xor_sync(0xffffffffu, m[c], o));
+#pragma unroll
+            for (int c = 0; c < UC; ++c) {
+                const int u = u0 + c;
+                if (u >= nu) break;
+                const float dd = __fdiv_rn(m[c], 127.0f);
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    const int t = u * G + g;
+                    const int q = m[c] == 0.0f ? 0 : (int)roundf(__fdiv_rn(y[c][g], dd));
+                    xt[(size_t)t * NT * 32 + tc::tile_off(n, lane >> 4) + (lane & 15)] = (uint8_t)(int8_t)q;
+                }
+                if (lane == 0) {
+                    if constexpr (TYPE == T_Q4_K) reinterpret_cast<float *>(xr)[((size_t)u * NT + n) * 8] = dd;
+                    else reinterpret_cast<float *>(xr)[(size_t)u * NT + n] = G == 1 ? round_h(dd) : dd;
+                }
+            }
+        };
+        if constexpr (MODE != PREP_PLAIN) {
+#pragma unroll
+            for (int u0 = 0; u0 < MAXV / G; u0 += UC) {
+                if (u0 >= nu) break;
+                float y[UC][G];
+#pragma unroll
+                for (int c = 0; c < UC; ++c)
+#pragma unroll
+                    for (int g = 0; g < G; ++g) {
+                        const int t = (u0 + c) * G + g;
+                        y[c][g] = t < MAXV ? vals[t < MAXV ? t : 0] : 0.0f;
+                    }
+                batch(u0, y);
+            }
+        } else {
+            // next batch's loads are issued before this batch is quantized
+            float y[2][UC][G];
+            auto load = [&](int u0, float (&yy)[UC][G]) {
+#pragma unroll
+                for (int c = 0; c < UC; ++c)
+#pragma unroll
+                    for (int g = 0; g < G; ++g)
+                        yy[c][g] = u0 + c < nu ? input(32 * ((u0 + c) * G + g) + lane) : 0.0f;
+            };
+            load(0, y[0]);
+            for (int u0 = 0, k = 0; u0 < nu; u0 += UC, k ^= 1) {
+                if (u0 + UC < nu) {
+                    if (k == 0) load(u0 + UC, y[1]);
+                    else load(u0 + UC, y[0]);
+                }
+                if (k == 0) batch(u0, y[0]);
+                else batch(u0, y[1]);
+            }
+        }
+    }
+}
+
+// Per-block sums of the quantized activations into the Q4_K records (after the
+// tiles are complete): thread i handles (token, block) pairs i, i+nthreads, ...
+template <int NT>
+__device__ void fused_block_sums(int nb, int rows_here, const uint8_t *xt, uint8_t *xr, int i0, int nthreads) {
+    for (int i = i0; i < rows_here * nb; i += nthreads) {
+        const int n = i % rows_here, t = i / rows_here;
+        const uint8_t *row = xt + (size_t)t * NT * 32;
+        const int4 a = *reinterpret_cast<const int4 *>(row + tc::tile_off(n, 0));
+        const int4 b = *reinterpret_cast<const int4 *>(row + tc::tile_off(n, 1));
+        int s = 0;
+        s = __dp4a(a.x, 0x01010101, s);
+        s = __dp4a(a.y, 0x01010101, s);
+        s = __dp4a(a.z, 0x01010101, s);
+        s = __dp4a(a.w, 0x01010101, s);
+        s = __dp4a(b.x, 0x01010101, s);
+        s = __dp4a(b.y, 0x01010101, s);
+        s = __dp4a(b.z, 0x01010101, s);
+        s = __dp4a(b.w, 0x01010101, s);
+        // record of unit t/8: {f32 scale, int16 sums of its 8 blocks}
+        reinterpret_cast<int16_t *>(xr + ((size_t)(t >> 3) * NT + n) * 32 + 4)[t & 7] = (int16_t)s;
+    }
+}
+
+// XM < 0: activations by TMA from the qprep_row_kernel layout; otherwise the
+// PrepMode of the activations the CTA builds itself.
+template <int TYPE, int EPI, int NT, int XM>
 __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_constant__ tc::Args A) {
     using namespace tc;
-    using G = Geo<TYPE, NT>;
-    constexpr int RS = G::RS, AS = G::AS, TS = G::TS, COLS = G::COLS, H = G::H;
+    constexpr bool FX = XM >= 0;
+    using G = Geo<TYPE, NT, FX>;
+    constexpr int RS = G::RS, AG = G::AG, TG = G::TG, BG = G::BG, COLS = G::COLS;
     constexpr int NH = NT / 2;  // tokens per epilogue warp
-    constexpr uint32_t IDESC = idesc_i8(128, H * NT);
+    constexpr uint32_t IDESC = idesc_i8(128, NT);
     extern __shared__ __align__(16) uint8_t smem_raw[];
-    __shared__ __align__(8) uint64_t full[RS], empty[RS], afull[AS], aempty[AS], tfull[TS], tempty[TS], fin;
+    __shared__ __align__(8) uint64_t full[RS], empty[RS], afull[AG], aempty[AG], tfull[TG], tempty[TG], fin, xready;
     __shared__ uint32_t tmem_base_sh;
     __shared__ volatile int abort_sh;
     __shared__ float best_v[4][64];
@@ -193,25 +406,35 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const Matrix &W = A.W;
     const int NS = (W.nb + 7) / 8;  // stages per tile (Q8_0: the last may hold fewer blocks)
+    // tiles of this CTA: TMA activations walk all tiles; fused activations keep
+    // one token tile per CTA (gridDim.x is then a multiple of tok_tiles)
     const int tiles = A.row_tiles * A.tok_tiles;
+    const int my_tt = FX ? (int)blockIdx.x % A.tok_tiles : 0;
+    const int first = FX ? (int)blockIdx.x / A.tok_tiles : (int)blockIdx.x;
+    const int stride = FX ? (int)gridDim.x / A.tok_tiles : (int)gridDim.x;
+    const int count = FX ? A.row_tiles : tiles;
+    const int my_tiles = first < count ? (count - first + stride - 1) / stride : 0;
     uint8_t *base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-    uint8_t *ring = base;                            // RS x STAGE
-    uint8_t *atile = base + (size_t)RS * G::STAGE;   // AS x 4 KB
+    uint8_t *ring = base;                                 // RS x STAGE
+    uint8_t *atile = base + (size_t)RS * G::STAGE;        // AG x BG x ABYTES
+    uint8_t *xt = base + G::oRES;                         // fused: [nb][NT x 32]
+    uint8_t *xr = xt + (size_t)W.nb * NT * 32;            // fused: [units][NT x RB]
 
     if (tid == 0) {
         for (int i = 0; i < RS; ++i) {
             mbar_init(&full[i], 1);
-            mbar_init(&empty[i], 4 + 1 + 8);
+            mbar_init(&empty[i], 2 + 1 + 8);
         }
-        for (int i = 0; i < AS; ++i) {
-            mbar_init(&afull[i], 4);
+        for (int i = 0; i < AG; ++i) {
+            mbar_init(&afull[i], 2);
             mbar_init(&aempty[i], 1);
         }
-        for (int i = 0; i < TS; ++i) {
+        for (int i = 0; i < TG; ++i) {
             mbar_init(&tfull[i], 1);
             mbar_init(&tempty[i], 8);
         }
         mbar_init(&fin, 1);
+        mbar_init(&xready, 8);
         abort_sh = 0;
     }
     if (EPI == EPI_ARGMAX)
@@ -219,12 +442,20 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
             best_v[n >> 6][n & 63] = kNegInf;
             best_i[n >> 6][n & 63] = 0xffffffffu;
         }
+    if constexpr (G::Q6) {
+        // the zero halves of the masked Q6_K tiles never change
+        for (int i = tid; i < AG * BG * 2 * 128; i += blockDim.x) {
+            const int slot = i >> 8, h = (i >> 7) & 1, r = i & 127;
+            *reinterpret_cast<int4 *>(atile + slot * 8192 + h * 4096 + tile_off(r, h ^ 1)) = make_int4(0, 0, 0, 0);
+        }
+    }
     if (warp == kMmaWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_sh)),
                      "r"(G::TCOLS)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
+    fence_async_smem();
     fence_before();
     __syncthreads();
     fence_after();
@@ -243,11 +474,28 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
         if (!ok && lane == 0) fail(code);
         return ok && !abort_sh;
     };
+    auto tile_rt = [&](int k) { return FX ? first + k * stride : (first + k * stride) % A.row_tiles; };
+    auto tile_tt = [&](int k) { return FX ? my_tt : (first + k * stride) / A.row_tiles; };
+
+    // Ring position: slot and phase parity, advanced by next().
+    struct Pos {
+        int slot = 0;
+        uint32_t phase = 0, n = 0;
+        __device__ void next(int size) {
+            ++n;
+            if (++slot == size) {
+                slot = 0;
+                phase ^= 1;
+            }
+        }
+    };
+    // blocks [g * BG, ...) of a stage holding nbs blocks
+    auto group_blocks = [&](int g, int nbs) { return min(BG, nbs - g * BG); };
 
     if (warp == kProducerWarp) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
-            const int first_stages = blockIdx.x < tiles ? min(RS, NS) : 0;
+            const int first_stages = my_tiles > 0 ? min(RS, NS) : 0;
             auto weights = [&](int rt, int s, uint8_t *dst, uint64_t *bar) {
                 const int g0 = 4 * rt;
                 tma3(dst, &A.m.w[0], 0, 8 * s, g0, bar);
@@ -259,244 +507,265 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
                 }
             };
             auto acts = [&](int tt, int s, uint8_t *dst, uint64_t *bar) {
-                const int t0 = A.tok0 + tt * NT;
-                tma4(dst + G::oXQ, &A.m.xq, 0, t0 / 8, 0, 8 * s, bar);
-                if constexpr (G::Q4) tma2(dst + G::oXR, &A.m.xr, t0 * 4, s, bar);
-                else if constexpr (G::Q6) tma2(dst + G::oXR, &A.m.xr, t0 / 2, s, bar);
-                else tma2(dst + G::oXR, &A.m.xr, t0 / 2, 8 * s, bar);
+                if constexpr (!FX) {
+                    const int t0 = A.tok0 + tt * NT;
+                    tma3(dst + G::oXQ, &A.m.xq, 0, t0 / 8, 8 * s, bar);
+                    if constexpr (G::Q4) tma2(dst + G::oXR, &A.m.xr, t0 * 4, s, bar);
+                    else if constexpr (G::Q6) tma2(dst + G::oXR, &A.m.xr, t0 / 2, s, bar);
+                    else tma2(dst + G::oXR, &A.m.xr, t0 / 2, 8 * s, bar);
+                }
             };
             // weights of the first stages do not depend on the previous kernel
             for (int s = 0; s < first_stages; ++s) {
                 mbar_expect_tx(&full[s], G::TX);
-                weights(blockIdx.x % A.row_tiles, s, ring + (size_t)s * G::STAGE, &full[s]);
+                weights(tile_rt(0), s, ring + (size_t)s * G::STAGE, &full[s]);
             }
             pdl_wait();
-            uint32_t gs = 0;
-            for (int tile = blockIdx.x; tile < tiles && !abort_sh; tile += gridDim.x) {
-                const int rt = tile % A.row_tiles, tt = tile / A.row_tiles;
-                for (int s = 0; s < NS; ++s, ++gs) {
-                    const int slot = gs % RS;
-                    const uint32_t use = gs / RS;
-                    uint8_t *dst = ring + (size_t)slot * G::STAGE;
-                    if (gs >= (uint32_t)first_stages) {
-                        if (use > 0 && !mbar_wait(&empty[slot], (use - 1) & 1)) {
+            Pos st;
+            for (int k = 0; k < my_tiles && !abort_sh; ++k) {
+                const int rt = tile_rt(k), tt = tile_tt(k);
+                for (int s = 0; s < NS; ++s, st.next(RS)) {
+                    uint8_t *dst = ring + (size_t)st.slot * G::STAGE;
+                    if (st.n >= (uint32_t)first_stages) {
+                        if (st.n >= (uint32_t)RS && !mbar_wait(&empty[st.slot], st.phase ^ 1)) {
                             fail(8u);
                             break;
                         }
                         if (abort_sh) break;
-                        mbar_expect_tx(&full[slot], G::TX);
-                        weights(rt, s, dst, &full[slot]);
+                        mbar_expect_tx(&full[st.slot], G::TX);
+                        weights(rt, s, dst, &full[st.slot]);
                     }
-                    acts(tt, s, dst, &full[slot]);
+                    acts(tt, s, dst, &full[st.slot]);
                 }
             }
         }
     } else if (warp == kMmaWarp) {
         // ----------------------------------------------------------------- MMA
         if (lane == 0) {
-            uint32_t gs = 0, gb = 0;
-            for (int tile = blockIdx.x; tile < tiles && !abort_sh; tile += gridDim.x) {
-                for (int s = 0; s < NS && !abort_sh; ++s, ++gs) {
-                    const int slot = gs % RS;
-                    if (!mbar_wait(&full[slot], (gs / RS) & 1)) {
+            Pos st, ag, tg;
+            if (FX && my_tiles > 0 && !mbar_wait(&xready, 0)) fail(16u);
+            for (int k = 0; k < my_tiles && !abort_sh; ++k) {
+                for (int s = 0; s < NS && !abort_sh; ++s, st.next(RS)) {
+                    if (!mbar_wait(&full[st.slot], st.phase)) {
                         fail(16u);
                         break;
                     }
-                    const uint8_t *xq = ring + (size_t)slot * G::STAGE + G::oXQ;
+                    const uint8_t *xq = FX ? xt + (size_t)8 * s * NT * 32 : ring + (size_t)st.slot * G::STAGE + G::oXQ;
                     const int nbs = min(8, W.nb - 8 * s);
-                    for (int b = 0; b < nbs; ++b, ++gb) {
-                        const int as = gb % AS, ts = gb % TS;
-                        const uint32_t au = gb / AS, tu = gb / TS;
-                        if (!mbar_wait(&afull[as], au & 1) || (tu > 0 && !mbar_wait(&tempty[ts], (tu - 1) & 1))) {
+                    for (int g = 0; g * BG < nbs; ++g, ag.next(AG), tg.next(TG)) {
+                        if (!mbar_wait(&afull[ag.slot], ag.phase) ||
+                            (tg.n >= (uint32_t)TG && !mbar_wait(&tempty[tg.slot], tg.phase ^ 1))) {
                             fail(16u);
                             break;
                         }
                         if (abort_sh) break;
                         fence_after();
-                        mma_i8(tmem + ts * COLS, sdesc(atile + as * 4096, 128, 256),
-                               sdesc(xq + b * H * NT * 32, 128, 256), IDESC);
-                        commit(&aempty[as]);
-                        commit(&tfull[ts]);
+                        const uint8_t *at = atile + (size_t)ag.slot * G::AGB;
+                        const uint32_t td = tmem + tg.slot * G::GCOLS;
+                        for (int b = 0; b < group_blocks(g, nbs); ++b) {
+                            const uint64_t db = sdesc(xq + (g * BG + b) * NT * 32, 128, 256);
+                            mma_i8(td + b * COLS, sdesc(at + b * G::ABYTES, 128, 256), db, IDESC);
+                            if constexpr (G::Q6)
+                                mma_i8(td + b * COLS + NT, sdesc(at + b * G::ABYTES + 4096, 128, 256), db, IDESC);
+                        }
+                        commit(&aempty[ag.slot]);
+                        commit(&tfull[tg.slot]);
                     }
-                    commit(&empty[slot]);
+                    commit(&empty[st.slot]);
                 }
             }
             // every MMA issued by this thread has completed before TMEM is released
             commit(&fin);
             if (!mbar_wait(&fin, 0)) fail(16u);
         }
-    } else if (warp < 4) {
+    } else if (warp >= kConvWarp) {
         // ---------------------------------------------------------- converters
-        const int r = tid;  // weight row of the tile = TMEM lane
-        uint32_t gs = 0, gb = 0;
-        for (int tile = blockIdx.x; tile < tiles && !abort_sh; tile += gridDim.x) {
-            bool ok = true;
-            for (int s = 0; s < NS && ok; ++s, ++gs) {
-                const int slot = gs % RS;
-                if (!(ok = wwait(&full[slot], (gs / RS) & 1, 32u))) break;
-                const uint8_t *st = ring + (size_t)slot * G::STAGE;
+        const int r0 = tid - 32 * kConvWarp;  // weight rows r0 and r0 + 64 of the tile
+        Pos st, ag;
+        bool ok = true;
+        for (int k = 0; k < my_tiles && ok && !abort_sh; ++k) {
+            for (int s = 0; s < NS && ok; ++s, st.next(RS)) {
+                if (!(ok = wwait(&full[st.slot], st.phase, 32u))) break;
+                const uint8_t *stg = ring + (size_t)st.slot * G::STAGE;
                 const int nbs = min(8, W.nb - 8 * s);
-                for (int b = 0; b < nbs; ++b, ++gb) {
-                    const int as = gb % AS;
-                    const uint32_t au = gb / AS;
-                    if (au > 0 && !(ok = wwait(&aempty[as], (au - 1) & 1, 32u))) break;
-                    uint8_t *ta = atile + as * 4096;
-                    const int gi = r >> 5, l = r & 31;
-                    int4 lo, hi;
-                    if constexpr (G::Q8) {
-                        const int4 *src = reinterpret_cast<const int4 *>(st + (gi * 8 + b) * 1024 + l * 32);
-                        lo = src[0];
-                        hi = src[1];
-                    } else if constexpr (G::Q4) {
-                        const int4 v = *reinterpret_cast<const int4 *>(st + (gi * 8 + b) * 512 + l * 16);
-                        lo = make_int4(v.x & 0x0f0f0f0f, v.y & 0x0f0f0f0f, v.z & 0x0f0f0f0f, v.w & 0x0f0f0f0f);
-                        hi = make_int4((v.x >> 4) & 0x0f0f0f0f, (v.y >> 4) & 0x0f0f0f0f, (v.z >> 4) & 0x0f0f0f0f,
-                                       (v.w >> 4) & 0x0f0f0f0f);
-                    } else {
-                        const int4 lq = *reinterpret_cast<const int4 *>(st + (gi * 8 + b) * 512 + l * 16);
-                        const uint2 hq = *reinterpret_cast<const uint2 *>(st + G::oB + (gi * 8 + b) * 256 + l * 8);
-                        const int ql[4] = {lq.x, lq.y, lq.z, lq.w};
-                        int a4[4], b4[4];
+                for (int g = 0; g * BG < nbs; ++g, ag.next(AG)) {
+                    if (ag.n >= (uint32_t)AG && !(ok = wwait(&aempty[ag.slot], ag.phase ^ 1, 32u))) break;
+                    for (int bb = 0; bb < group_blocks(g, nbs); ++bb) {
+                        const int b = g * BG + bb;
+                        uint8_t *ta = atile + (size_t)ag.slot * G::AGB + bb * G::ABYTES;
 #pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            a4[i] = (int)__vsub4((uint32_t)((ql[i] & 0x0f0f0f0f) | (int)(((hq.x >> (2 * i)) & 0x03030303u) << 4)),
-                                                 0x20202020u);
-                            b4[i] = (int)__vsub4(
-                                (uint32_t)(((ql[i] >> 4) & 0x0f0f0f0f) | (int)(((hq.y >> (2 * i)) & 0x03030303u) << 4)),
-                                0x20202020u);
+                        for (int half = 0; half < 2; ++half) {
+                            const int r = r0 + 64 * half, gi = r >> 5, l = r & 31;
+                            if constexpr (G::Q8) {
+                                const int4 *src = reinterpret_cast<const int4 *>(stg + (gi * 8 + b) * 1024 + l * 32);
+                                *reinterpret_cast<int4 *>(ta + tile_off(r, 0)) = src[0];
+                                *reinterpret_cast<int4 *>(ta + tile_off(r, 1)) = src[1];
+                            } else if constexpr (G::Q4) {
+                                const int4 v = *reinterpret_cast<const int4 *>(stg + (gi * 8 + b) * 512 + l * 16);
+                                *reinterpret_cast<int4 *>(ta + tile_off(r, 0)) =
+                                    make_int4(v.x & 0x0f0f0f0f, v.y & 0x0f0f0f0f, v.z & 0x0f0f0f0f, v.w & 0x0f0f0f0f);
+                                *reinterpret_cast<int4 *>(ta + tile_off(r, 1)) =
+                                    make_int4((v.x >> 4) & 0x0f0f0f0f, (v.y >> 4) & 0x0f0f0f0f,
+                                              (v.z >> 4) & 0x0f0f0f0f, (v.w >> 4) & 0x0f0f0f0f);
+                            } else {
+                                const int4 lq = *reinterpret_cast<const int4 *>(stg + (gi * 8 + b) * 512 + l * 16);
+                                const uint2 hq =
+                                    *reinterpret_cast<const uint2 *>(stg + G::oB + (gi * 8 + b) * 256 + l * 8);
+                                const int ql[4] = {lq.x, lq.y, lq.z, lq.w};
+                                int a4[4], b4[4];
+#pragma unroll
+                                for (int i = 0; i < 4; ++i) {
+                                    a4[i] = (int)__vsub4(
+                                        (uint32_t)((ql[i] & 0x0f0f0f0f) | (int)(((hq.x >> (2 * i)) & 0x03030303u) << 4)),
+                                        0x20202020u);
+                                    b4[i] = (int)__vsub4((uint32_t)(((ql[i] >> 4) & 0x0f0f0f0f) |
+                                                                    (int)(((hq.y >> (2 * i)) & 0x03030303u) << 4)),
+                                                         0x20202020u);
+                                }
+                                // tile 0: values 0-15 (k16 = 0), tile 1: values 16-31 (k16 = 1)
+                                *reinterpret_cast<int4 *>(ta + tile_off(r, 0)) = make_int4(a4[0], a4[1], a4[2], a4[3]);
+                                *reinterpret_cast<int4 *>(ta + 4096 + tile_off(r, 1)) =
+                                    make_int4(b4[0], b4[1], b4[2], b4[3]);
+                            }
                         }
-                        lo = make_int4(a4[0], a4[1], a4[2], a4[3]);
-                        hi = make_int4(b4[0], b4[1], b4[2], b4[3]);
                     }
-                    *reinterpret_cast<int4 *>(ta + tile_off(r, 0)) = lo;
-                    *reinterpret_cast<int4 *>(ta + tile_off(r, 1)) = hi;
                     fence_async_smem();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&afull[as]);
+                    if (lane == 0) mbar_arrive(&afull[ag.slot]);
                 }
                 if (!ok) break;
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[slot]);
+                if (lane == 0) mbar_arrive(&empty[st.slot]);
             }
-            if (!ok) break;
         }
     } else {
         // ------------------------------------------------------------ epilogue
-        const int q = warp & 3, e = (warp - 4) >> 2;
+        const int q = warp & 3, e = warp >> 2;
         const int r = 32 * q + lane, gi = q, l = lane;
         const int n0 = e * NH;  // first token (within the tile) of this warp
         pdl_wait();
-        uint32_t gs = 0, gb = 0;
+        if constexpr (FX) {
+            // this CTA's token tile, built once; the first row tile writes x (embedding)
+            if (my_tiles > 0) {
+                fused_prologue<TYPE, NT, (FX ? XM : 0)>(A.p, A.rows, my_tt, first == 0, xt, xr, warp, 8, lane);
+                if constexpr (G::Q4) {
+                    asm volatile("bar.sync 1, 256;" ::: "memory");  // the 8 epilogue warps
+                    fused_block_sums<NT>(W.nb, min(NT, A.rows - my_tt * NT), xt, xr, tid, 256);
+                }
+            }
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&xready);
+        }
+        Pos st, tg;
         bool ok = true;
-        for (int tile = blockIdx.x; tile < tiles && ok && !abort_sh; tile += gridDim.x) {
-            const int rt = tile % A.row_tiles, tt = tile / A.row_tiles;
+        for (int k = 0; k < my_tiles && ok && !abort_sh; ++k) {
+            const int rt = tile_rt(k), tt = tile_tt(k);
             const int row = rt * 128 + r;
             const bool live = row < W.N;
             float acc[NH];
 #pragma unroll
             for (int n = 0; n < NH; ++n) acc[n] = 0.0f;
-            for (int s = 0; s < NS && ok; ++s, ++gs) {
-                const int slot = gs % RS;
-                if (!(ok = wwait(&full[slot], (gs / RS) & 1, 64u))) break;
-                const uint8_t *st = ring + (size_t)slot * G::STAGE;
+            for (int s = 0; s < NS && ok; ++s, st.next(RS)) {
+                if (!(ok = wwait(&full[st.slot], st.phase, 64u))) break;
+                const uint8_t *stg = ring + (size_t)st.slot * G::STAGE;
+                // records of this stage's units: [unit][NT x RB]
+                const uint8_t *rec = FX ? xr + (size_t)(G::Q8 ? 8 * s : s) * NT * G::RB : stg + G::oXR;
                 // this row's scales for the stage
                 float d = 0.f, dm = 0.f;
                 uint32_t mpk0 = 0, mpk1 = 0, scpk0 = 0, scpk1 = 0;
                 if constexpr (G::Q4) {
-                    const uint4 h = *reinterpret_cast<const uint4 *>(st + G::oB + gi * 512 + l * 16);
+                    const uint4 h = *reinterpret_cast<const uint4 *>(stg + G::oB + gi * 512 + l * 16);
                     d = h2f(h.x & 0xffff);
                     dm = h2f(h.x >> 16);
-                    auto byte = [&](int k) -> uint32_t {
-                        const uint32_t w = k < 4 ? h.y : (k < 8 ? h.z : h.w);
-                        return (w >> (8 * (k & 3))) & 0xff;
+                    auto byte = [&](int kk) -> uint32_t {
+                        const uint32_t w = kk < 4 ? h.y : (kk < 8 ? h.z : h.w);
+                        return (w >> (8 * (kk & 3))) & 0xff;
                     };
 #pragma unroll
-                    for (int k = 0; k < 8; ++k) {
+                    for (int kk = 0; kk < 8; ++kk) {
                         uint32_t sc, mm;
-                        if (k < 4) {
-                            sc = byte(k) & 63;
-                            mm = byte(k + 4) & 63;
+                        if (kk < 4) {
+                            sc = byte(kk) & 63;
+                            mm = byte(kk + 4) & 63;
                         } else {
-                            sc = (byte(k + 4) & 0xf) | ((byte(k - 4) >> 6) << 4);
-                            mm = (byte(k + 4) >> 4) | ((byte(k) >> 6) << 4);
+                            sc = (byte(kk + 4) & 0xf) | ((byte(kk - 4) >> 6) << 4);
+                            mm = (byte(kk + 4) >> 4) | ((byte(kk) >> 6) << 4);
                         }
-                        if (k < 4) {
-                            scpk0 |= sc << (8 * k);
-                            mpk0 |= mm << (8 * k);
+                        if (kk < 4) {
+                            scpk0 |= sc << (8 * kk);
+                            mpk0 |= mm << (8 * kk);
                         } else {
-                            scpk1 |= sc << (8 * (k - 4));
-                            mpk1 |= mm << (8 * (k - 4));
+                            scpk1 |= sc << (8 * (kk - 4));
+                            mpk1 |= mm << (8 * (kk - 4));
                         }
                     }
                 } else if constexpr (G::Q6) {
-                    d = h2f(*reinterpret_cast<const unsigned short *>(st + G::oE + gi * 64 + l * 2));
+                    d = h2f(*reinterpret_cast<const unsigned short *>(stg + G::oE + gi * 64 + l * 2));
                 }
                 int S[NH];
 #pragma unroll
                 for (int n = 0; n < NH; ++n) S[n] = 0;
                 const int nbs = min(8, W.nb - 8 * s);
-                for (int b = 0; b < nbs; ++b, ++gb) {
-                    const int ts = gb % TS;
-                    if (!(ok = wwait(&tfull[ts], (gb / TS) & 1, 64u))) break;
+                for (int g = 0; g * BG < nbs && ok; ++g, tg.next(TG)) {
+                    if (!(ok = wwait(&tfull[tg.slot], tg.phase, 64u))) break;
                     fence_after();
-                    const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + ts * COLS + n0;
+                    for (int bb = 0; bb < group_blocks(g, nbs); ++bb) {
+                    const int b = g * BG + bb;
+                    const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + tg.slot * G::GCOLS + bb * COLS + n0;
                     int sa = 0, sb = 0;
                     float db = 0.f;
                     if constexpr (G::Q4) {
                         sa = (int)(((b < 4 ? scpk0 : scpk1) >> (8 * (b & 3))) & 0xff);
                     } else if constexpr (G::Q6) {
                         const unsigned short sc2 =
-                            *reinterpret_cast<const unsigned short *>(st + G::oC + (gi * 8 + b) * 64 + l * 2);
+                            *reinterpret_cast<const unsigned short *>(stg + G::oC + (gi * 8 + b) * 64 + l * 2);
                         sa = (int8_t)(sc2 & 0xff);
                         sb = (int8_t)(sc2 >> 8);
                     } else {
-                        db = h2f(*reinterpret_cast<const unsigned short *>(st + G::oB + (gi * 8 + b) * 64 + l * 2));
+                        db = h2f(*reinterpret_cast<const unsigned short *>(stg + G::oB + (gi * 8 + b) * 64 + l * 2));
                     }
-                    constexpr int CH = NH < 16 ? NH : 16;
-#pragma unroll
-                    for (int c0 = 0; c0 < NH; c0 += CH) {
-                        int va[16], vb[16];
+                    // TMEM -> registers in chunks of up to 16 tokens; the next chunk's
+                    // load is in flight while the current one is accumulated
+                    constexpr int CH = NH < 16 ? NH : 16, NC = NH / CH;
+                    int va[2][CH], vb[2][CH];
+                    auto ld = [&](int c, int (&a)[CH], int (&bv)[CH]) {
                         if constexpr (CH == 16) {
-                            tmem_ld16(ta + c0, va);
-                            if constexpr (G::Q6) tmem_ld16(ta + NT + c0, vb);
+                            tmem_ld16(ta + c * CH, a);
+                            if constexpr (G::Q6) tmem_ld16(ta + NT + c * CH, bv);
                         } else if constexpr (CH == 8) {
-                            int t8[8], u8[8];
-                            tmem_ld8(ta + c0, t8);
-                            if constexpr (G::Q6) tmem_ld8(ta + NT + c0, u8);
-#pragma unroll
-                            for (int i = 0; i < 8; ++i) {
-                                va[i] = t8[i];
-                                vb[i] = G::Q6 ? u8[i] : 0;
-                            }
+                            tmem_ld8(ta + c * CH, a);
+                            if constexpr (G::Q6) tmem_ld8(ta + NT + c * CH, bv);
                         } else {
                             static_assert(CH == 4, "token chunk");
-                            int t4[4], u4[4];
-                            tmem_ld4(ta + c0, t4);
-                            if constexpr (G::Q6) tmem_ld4(ta + NT + c0, u4);
-#pragma unroll
-                            for (int i = 0; i < 4; ++i) {
-                                va[i] = t4[i];
-                                vb[i] = G::Q6 ? u4[i] : 0;
-                            }
+                            tmem_ld4(ta + c * CH, a);
+                            if constexpr (G::Q6) tmem_ld4(ta + NT + c * CH, bv);
                         }
+                    };
+                    ld(0, va[0], vb[0]);
+#pragma unroll
+                    for (int c = 0; c < NC; ++c) {
                         tmem_wait_ld();
+                        if (c + 1 < NC) ld(c + 1, va[(c + 1) & 1], vb[(c + 1) & 1]);
 #pragma unroll
                         for (int i = 0; i < CH; ++i) {
-                            const int n = c0 + i;
+                            const int n = c * CH + i;
+                            const int I = va[c & 1][i];
                             if constexpr (G::Q4) {
-                                S[n] += sa * va[i];
+                                S[n] += sa * I;
                             } else if constexpr (G::Q6) {
-                                S[n] += sa * va[i] + sb * vb[i];
+                                S[n] += sa * I + sb * vb[c & 1][i];
                             } else {
-                                const float xd = reinterpret_cast<const float *>(st + G::oXR)[b * NT + n0 + n];
-                                const float p = __fmul_rn(__fmul_rn(db, xd), (float)va[i]);
+                                const float xd = reinterpret_cast<const float *>(rec)[b * NT + n0 + n];
+                                const float p = __fmul_rn(__fmul_rn(db, xd), (float)I);
                                 acc[n] = (s == 0 && b == 0) ? p : __fadd_rn(acc[n], p);
                             }
                         }
                     }
+                    }
                     fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&tempty[ts]);
+                    if (lane == 0) mbar_arrive(&tempty[tg.slot]);
                 }
                 if (!ok) break;
                 if constexpr (!G::Q8) {
@@ -505,39 +774,47 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
                     for (int n = 0; n < NH; ++n) {
                         float p;
                         if constexpr (G::Q4) {
-                            const int4 rec = *reinterpret_cast<const int4 *>(st + G::oXR + (n0 + n) * 32);
-                            const float xd = __int_as_float(rec.x);
+                            const int4 rv = *reinterpret_cast<const int4 *>(rec + (n0 + n) * 32);
+                            const float xd = __int_as_float(rv.x);
                             // S2 = sum_j m_j * s32_j (s32 pairs as int16x2, m_j as bytes)
-                            int S2 = __dp2a_lo(rec.y, (int)mpk0, 0);
-                            S2 = __dp2a_hi(rec.z, (int)mpk0, S2);
-                            S2 = __dp2a_lo(rec.w, (int)mpk1, S2);
-                            S2 = __dp2a_hi(*reinterpret_cast<const int *>(st + G::oXR + (n0 + n) * 32 + 16), (int)mpk1,
-                                           S2);
+                            int S2 = __dp2a_lo(rv.y, (int)mpk0, 0);
+                            S2 = __dp2a_hi(rv.z, (int)mpk0, S2);
+                            S2 = __dp2a_lo(rv.w, (int)mpk1, S2);
+                            S2 = __dp2a_hi(*reinterpret_cast<const int *>(rec + (n0 + n) * 32 + 16), (int)mpk1, S2);
                             p = __fmul_rn(xd, __fsub_rn(__fmul_rn(d, (float)S[n]), __fmul_rn(dm, (float)S2)));
                         } else {
-                            const float xd = reinterpret_cast<const float *>(st + G::oXR)[n0 + n];
+                            const float xd = reinterpret_cast<const float *>(rec)[n0 + n];
                             p = __fmul_rn(__fmul_rn(d, xd), (float)S[n]);
                         }
                         acc[n] = s == 0 ? p : __fadd_rn(acc[n], p);
                     }
                 }
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[slot]);
+                if (lane == 0) mbar_arrive(&empty[st.slot]);
             }
             if (!ok || abort_sh) break;
             // tile epilogue
+            if constexpr (EPI == EPI_ARGMAX) {
+                uint32_t bi[NH];
 #pragma unroll
-            for (int n = 0; n < NH; ++n) {
-                const int tok = tt * NT + n0 + n;
-                if (tok >= A.rows) break;  // uniform across the warp
-                if constexpr (EPI == EPI_ARGMAX) {
-                    float bv = live ? acc[n] : kNegInf;
-                    uint32_t bi = live ? (uint32_t)row : 0xffffffffu;
-                    if (A.g.logits && live) A.g.logits[(size_t)tok * W.N + row] = acc[n];
-                    warp_argmax(bv, bi);
-                    if (lane == 0) argmax_merge(best_v[q][tok], best_i[q][tok], bv, bi);  // tok < 64
-                } else if (live) {
-                    epilogue_store<EPI>(A.g, row, tok, acc[n]);
+                for (int n = 0; n < NH; ++n) {
+                    const int tok = tt * NT + n0 + n;
+                    if (A.g.logits && live && tok < A.rows) A.g.logits[(size_t)tok * W.N + row] = acc[n];
+                    if (!live) acc[n] = kNegInf;
+                    bi[n] = live ? (uint32_t)row : 0xffffffffu;
+                }
+                argmax_scatter<NH>(acc, bi, lane);
+                constexpr int LPT = 32 / NH;  // lanes per token after the scatter
+                if (lane % LPT == 0) {
+                    const int tok = tt * NT + n0 + lane / LPT;  // < 64 in an ARGMAX launch
+                    if (tok < A.rows) argmax_merge(best_v[q][tok], best_i[q][tok], acc[0], bi[0]);
+                }
+            } else {
+#pragma unroll
+                for (int n = 0; n < NH; ++n) {
+                    const int tok = tt * NT + n0 + n;
+                    if (tok >= A.rows) break;  // uniform across the warp
+                    if (live) epilogue_store<EPI>(A.g, row, tok, acc[n]);
                 }
             }
         }
@@ -566,10 +843,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
 // in shared memory (embedding rows dequantized once), LayerNorm statistics by
 // one warp in the fixed order, quantized with the consumer's scale groups, then
 // written as
-//   tq : per block j and copy h, 8-row core groups of 256 bytes
-//        [j][h][row/8][k16][row%8][16 B] (the UMMA K-major no-swizzle layout;
-//        for Q6_K consumers copy 0 keeps values 0-15 and copy 1 values 16-31,
-//        the other half zeroed);
+//   tq : per block j, 8-row core groups of 256 bytes [j][row/8][k16][row%8][16 B]
+//        (the UMMA K-major no-swizzle layout);
 //   trec: per unit u (super-block, or block for Q8_0 consumers) and row:
 //        Q4_K: {f32 scale, int16 block sums x 8, 12 zero bytes} (32 B);
 //        Q6_K: f32 scale; Q8_0: f32 (f16-rounded) scale.
@@ -609,12 +884,11 @@ __global__ void __launch_bounds__(256) qprep_row_kernel(PrepArgs p, QAct out) {
     if (p.group == 8) build_activations_impl<M2, 8>(q, s, 1, false);
     else build_activations_impl<M2, 1>(q, s, 1, false);
     // build_activations_impl ends with __syncthreads
-    const int H = p.ctype == T_Q6_K ? 2 : 1, rs = out.rs;
-    for (int c = threadIdx.x; c < nb * H * 2; c += blockDim.x) {
-        const int j = c / (2 * H), h = (c >> 1) % H, k16 = c & 1;
-        int4 v = *reinterpret_cast<const int4 *>(s.q + 32 * j + 16 * k16);
-        if (H == 2 && h != k16) v = make_int4(0, 0, 0, 0);
-        *reinterpret_cast<int4 *>(out.tq + (((size_t)j * H + h) * (rs / 8) + (r >> 3)) * 256 + tc::tile_off(r & 7, k16)) = v;
+    const int rs = out.rs;
+    for (int c = threadIdx.x; c < nb * 2; c += blockDim.x) {
+        const int j = c >> 1, k16 = c & 1;
+        *reinterpret_cast<int4 *>(out.tq + ((size_t)j * (rs / 8) + (r >> 3)) * 256 + tc::tile_off(r & 7, k16)) =
+            *reinterpret_cast<const int4 *>(s.q + 32 * j + 16 * k16);
     }
     if (p.ctype == T_Q4_K) {
         for (int u = threadIdx.x; u < nb / 8; u += blockDim.x) {
