@@ -220,7 +220,9 @@ struct StaticState {
     uint32_t *ids = nullptr, *step = nullptr, *out = nullptr, *lens = nullptr;
     uint8_t *finished = nullptr;
     float *x = nullptr, *q = nullptr, *a = nullptr, *u = nullptr, *xf = nullptr;
-    QAct act;
+    QAct act, act2;                  // tensor-core activations (the step alternates between them)
+    uint32_t *counters = nullptr;    // completion counters of the matmuls' post steps
+    size_t counter_bytes = 0;
     std::vector<__half *> kc, vc, ck, cv;
     float *part_v = nullptr;
     uint32_t *part_i = nullptr;
@@ -272,6 +274,10 @@ struct mgb_ctx {
     // Decode-step tensor-core matmuls build their activations in the kernel
     // (1) or read them from qprep_row_kernel (0); MGB_TC_FUSED overrides.
     int tc_fused = 0;
+    // Producers prepare the next matmul's tensor-core activations (post steps,
+    // attention) (1) or qprep_row does (0, faster on B200 so far: one CTA per
+    // row in parallel beats the last CTA of a token tile); MGB_TC_POST overrides.
+    int tc_post = 0;
     int sms = 148;  // multiprocessor count of the device (one tensor-core CTA each)
     size_t smem_optin = 227 * 1024 - 4096;  // dynamic shared memory a tensor-core CTA may take
 
@@ -944,7 +950,7 @@ static mgb_status gemm_tc_t(mgb_ctx *c, const tc::Args &a, int nt, int grid) {
 // token tile each); *ctas returns its CTA count, the partial count per row.
 template <int EPI, int XM>
 static mgb_status gemm_tc(mgb_ctx *c, const Matrix &W, const QAct *act, const PrepArgs *p, int rows,
-                          const GemvArgs &g, int *ctas = nullptr) {
+                          const GemvArgs &g, int *ctas = nullptr, const tc::Post *post = nullptr) {
     const int chunk = EPI == EPI_ARGMAX ? 64 : rows;
     for (int t0 = 0; t0 < rows; t0 += chunk) {
         const int n = std::min(chunk, rows - t0);
@@ -957,6 +963,7 @@ static mgb_status gemm_tc(mgb_ctx *c, const Matrix &W, const QAct *act, const Pr
         a.g.W = W;
         a.g.rows = n;
         a.err = c->d_err;
+        a.post = post ? *post : tc::Post{};  // (after the memset: mode -1 = no post step)
         if (p) {
             a.p = *p;
             a.p.K = W.K;
@@ -1057,7 +1064,14 @@ static mgb_status new_state(mgb_ctx *c, int b, int s, int m, StaticState **out) 
     }
     TRY(A((void **)&st->part_v, (size_t)4 * b * kLmParts));
     TRY(A((void **)&st->part_i, (size_t)4 * b * kLmParts));
-    if (b >= c->tc_min_rows) TRY(alloc_tc_act(c, b, std::max(d, g.dec_ffn), st->act, st->allocs, &st->bytes));
+    if (b >= c->tc_min_rows) {
+        TRY(alloc_tc_act(c, b, std::max(d, g.dec_ffn), st->act, st->allocs, &st->bytes));
+        TRY(alloc_tc_act(c, b, std::max(d, g.dec_ffn), st->act2, st->allocs, &st->bytes));
+        // one counter per (token tile of 8 rows, 256-row super-block) covers every post step
+        st->counter_bytes = (size_t)4 * ((b + 7) / 8) * std::max(1, std::max(d, g.dec_ffn) / 256);
+        TRY(A((void **)&st->counters, st->counter_bytes));
+        CK(cudaMemsetAsync(st->counters, 0, st->counter_bytes, c->stream));
+    }
     *out = st.release();
     return MGB_OK;
 }
@@ -1085,10 +1099,185 @@ static mgb_status step_op(mgb_ctx *c, StaticState *st, const FusedArgs &f, int *
     return fused<EPI, MODE>(c, f);
 }
 
+// The decode step on the tensor cores (batches of tc_min_rows rows or more).
+// Every matmul reads activations in the tensor-core layout from one of two
+// buffers and the producer of its input writes them there: the LayerNorm
+// inputs by the previous matmul's last CTA per token tile (post step), the
+// attention outputs by the attention kernel, the FFN hidden layer by the up
+// projection per super-block; layer 0's embedding input by qprep_row. Where a
+// shape does not allow that, qprep_row prepares the input instead.
+static mgb_status launch_step_tc(mgb_ctx *c, StaticState *st, float *logits, int force, cudaEvent_t lm0,
+                                 cudaEvent_t lm1) {
+    const Config &g = c->cfg;
+    const int b = st->b, d = g.d, H = g.dec_heads, hd = d / H;
+    QAct *X = &st->act, *Y = &st->act2;  // X: input of the next matmul in program order
+    auto plain = [&](const float *x, int K) {
+        PrepArgs p{};
+        p.x = x;
+        p.rows = b;
+        p.K = K;
+        return p;
+    };
+    auto gemv = [&](const Matrix &W) {
+        GemvArgs gg{};
+        gg.W = W;
+        gg.rows = b;
+        return gg;
+    };
+    // post step of a matmul whose output (rows of width W.N) feeds `next`
+    auto post_for = [&](int mode, const Matrix &W, const Norm *nrm, const Matrix &next, QAct *dst, tc::Post &po) {
+        po = tc::Post{};
+        if (!c->tc_post || !tc_ok(next)) return false;
+        if (mode == PREP_LN && W.N > 2048) return false;
+        if (mode == PREP_PLAIN && (W.N % 256 || (W.Np / 128) % 2)) return false;
+        po.mode = mode;
+        if (nrm) {
+            po.gamma = nrm->g;
+            po.beta = nrm->b;
+        }
+        po.group = act_group(next.type);
+        po.ctype = next.type;
+        po.out = *dst;
+        po.counters = st->counters;
+        return true;
+    };
+    // prepare `next`'s input from f32 rows when no producer did it
+    auto prep = [&](int mode, const float *x, int K, const Norm *nrm, const Matrix &next, QAct *dst) -> mgb_status {
+        PrepArgs p = plain(x, K);
+        if (nrm) {
+            p.gamma = nrm->g;
+            p.beta = nrm->b;
+        }
+        return mode == PREP_LN ? qprep_row<PREP_LN>(c, p, *dst, next) : qprep_row<PREP_PLAIN>(c, p, *dst, next);
+    };
+    // attention that also quantizes its outputs for `next` when the shape allows
+    auto attn_q = [&](AttnArgs aa, const Matrix &next, QAct *dst) -> mgb_status {
+        const int G = act_group(next.type);
+        const bool ok = c->tc_post && tc_ok(next) && aa.queries == 1 && H % 4 == 0 && hd <= 128 &&
+                        (4 * hd) % (32 * G) == 0;
+        if (ok) {
+            aa.qo = *dst;
+            aa.qo_ctype = next.type;
+        }
+        TRY(attend<__half>(c, aa));
+        if (!ok) TRY(prep(PREP_PLAIN, aa.out, d, nullptr, next, dst));
+        return MGB_OK;
+    };
+    for (int l = 0; l < g.dec_layers; ++l) {
+        const DecLayer &L = c->dec[l];
+        if (l == 0) {
+            PrepArgs p = plain(st->x, d);
+            p.gamma = L.attn_norm.g;
+            p.beta = L.attn_norm.b;
+            p.x_out = st->x;
+            p.embed = c->embed;
+            p.ids = st->ids;
+            p.step = st->step;
+            p.pos_table = c->pos;
+            p.pos_base = (uint32_t)g.pad + 1;
+            p.scale = c->embed_scale;
+            TRY(qprep_row<PREP_EMBED_LN>(c, p, *X, L.qkv));
+        }
+        // (X holds attn_norm(x) for qkv)
+        GemvArgs gq = gemv(L.qkv);
+        gq.q = st->q;
+        gq.kc = st->kc[l];
+        gq.vc = st->vc[l];
+        gq.step = st->step;
+        gq.H = H;
+        gq.hd = hd;
+        gq.m = st->m;
+        TRY((gemm_tc<EPI_QKV, -1>(c, L.qkv, X, nullptr, b, gq)));
+        AttnArgs sa{};
+        sa.q = st->q;
+        sa.q_row = d;
+        sa.K = st->kc[l];
+        sa.V = st->vc[l];
+        sa.kv_row = hd;
+        sa.kv_head = (long)st->m * hd;
+        sa.kv_batch = (long)H * st->m * hd;
+        sa.step = st->step;
+        sa.out = st->a;
+        sa.out_row = d;
+        sa.H = H;
+        sa.hd = hd;
+        sa.rows = b;
+        sa.queries = 1;
+        sa.max_keys = st->m;
+        TRY(attn_q(sa, L.out, Y));
+        std::swap(X, Y);
+        // out projection + residual; its post step: cross_norm(x) for cross_q
+        tc::Post po;
+        GemvArgs go = gemv(L.out);
+        go.y = st->x;
+        bool posted = post_for(PREP_LN, L.out, &L.cross_norm, L.cq, Y, po);
+        TRY((gemm_tc<EPI_RESID, -1>(c, L.out, X, nullptr, b, go, nullptr, posted ? &po : nullptr)));
+        if (!posted) TRY(prep(PREP_LN, st->x, d, &L.cross_norm, L.cq, Y));
+        std::swap(X, Y);
+        GemvArgs gc = gemv(L.cq);
+        gc.y = st->q;
+        TRY((gemm_tc<EPI_STORE, -1>(c, L.cq, X, nullptr, b, gc)));
+        AttnArgs ca = sa;
+        ca.K = st->ck[l];
+        ca.V = st->cv[l];
+        ca.kv_head = (long)st->s * hd;
+        ca.kv_batch = (long)H * st->s * hd;
+        ca.step = nullptr;
+        ca.lens = st->lens;
+        ca.max_keys = st->s;
+        TRY(attn_q(ca, L.co, Y));
+        std::swap(X, Y);
+        // cross out + residual; post: ffn_norm(x) for up
+        GemvArgs gco = gemv(L.co);
+        gco.y = st->x;
+        posted = post_for(PREP_LN, L.co, &L.ffn_norm, L.up, Y, po);
+        TRY((gemm_tc<EPI_RESID, -1>(c, L.co, X, nullptr, b, gco, nullptr, posted ? &po : nullptr)));
+        if (!posted) TRY(prep(PREP_LN, st->x, d, &L.ffn_norm, L.up, Y));
+        std::swap(X, Y);
+        // up + ReLU; post: the hidden layer per super-block for down
+        GemvArgs gu = gemv(L.up);
+        gu.y = st->u;
+        posted = post_for(PREP_PLAIN, L.up, nullptr, L.down, Y, po);
+        TRY((gemm_tc<EPI_RELU, -1>(c, L.up, X, nullptr, b, gu, nullptr, posted ? &po : nullptr)));
+        if (!posted) TRY(prep(PREP_PLAIN, st->u, g.dec_ffn, nullptr, L.down, Y));
+        std::swap(X, Y);
+        // down + residual; post: the next layer's attn_norm(x), or dec_norm(x) for the LM head
+        const bool last = l + 1 == g.dec_layers;
+        const Norm &nn = last ? c->dec_norm : c->dec[l + 1].attn_norm;
+        const Matrix &nm = last ? c->embed : c->dec[l + 1].qkv;
+        GemvArgs gd = gemv(L.down);
+        gd.y = st->x;
+        posted = post_for(PREP_LN, L.down, &nn, nm, Y, po);
+        TRY((gemm_tc<EPI_RESID, -1>(c, L.down, X, nullptr, b, gd, nullptr, posted ? &po : nullptr)));
+        if (!posted) TRY(prep(PREP_LN, st->x, d, &nn, nm, Y));
+        std::swap(X, Y);
+    }
+    // tied LM head fused with the first argmax pass, then greedy bookkeeping
+    GemvArgs gl = gemv(c->embed);
+    gl.part_v = st->part_v;
+    gl.part_i = st->part_i;
+    gl.logits = logits;
+    if (lm0) CK(cudaEventRecord(lm0, c->stream));
+    int parts = kLmParts;
+    TRY((gemm_tc<EPI_ARGMAX, -1>(c, c->embed, X, nullptr, b, gl, &parts)));
+    st->lm_parts = parts;
+    if (lm1) CK(cudaEventRecord(lm1, c->stream));
+    const int threads = std::min(1024, std::max(32, 32 * b));
+    cudaError_t e = launch_pdl(greedy_finalize_kernel, dim3(1), dim3(threads), 0, c->stream,
+                               (const float *)st->part_v, (const uint32_t *)st->part_i, parts, b,
+                               st->finished, st->ids, st->out, st->m, st->step, (uint32_t)g.eos, (uint32_t)g.pad,
+                               force);
+    ++c->launches;
+    if (e != cudaSuccess) return cuda_err(e, "finalize launch");
+    return MGB_OK;
+}
+
 // One greedy decoder step on the state's fixed buffers (model.rs:552-612):
 // 6 fused matmuls + 2 attentions per layer, the LM head with argmax, finalize.
 static mgb_status launch_step(mgb_ctx *c, StaticState *st, float *logits, int force,
                               cudaEvent_t lm0 = nullptr, cudaEvent_t lm1 = nullptr) {
+    if (st->b >= c->tc_min_rows && st->act.tq && !c->tc_fused && tc_ok(c->embed) && tc_ok(c->dec[0].qkv))
+        return launch_step_tc(c, st, logits, force, lm0, lm1);
     const Config &g = c->cfg;
     const int b = st->b, d = g.d, H = g.dec_heads, hd = d / H;
     auto src = [&](const float *x, int K, const Norm *n) {
@@ -1406,6 +1595,7 @@ static mgb_status acquire_state(mgb_ctx *c, const mgb_batch *B, int max_new, boo
     for (int i = 0; i < n; ++i) lens[i] = B->lens[i];
     CK(cudaMemcpyAsync(st->lens, lens.data(), 4 * b, cudaMemcpyHostToDevice, c->stream));
     CK(cudaMemsetAsync(st->step, 0, 4, c->stream));
+    if (st->counters) CK(cudaMemsetAsync(st->counters, 0, st->counter_bytes, c->stream));
     TRY(set_ids(c, st, (uint32_t)g.start));
     TRY(reset_finished(c, st, n));
     *out = st;
@@ -1531,6 +1721,7 @@ mgb_status mgb_open(const char *path, int device, const mgb_options *opts, mgb_c
     CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
     if (const char *v = getenv("MGB_TC_MIN_ROWS")) c->tc_min_rows = std::max(1, atoi(v));
     if (const char *v = getenv("MGB_TC_FUSED")) c->tc_fused = atoi(v) != 0;
+    if (const char *v = getenv("MGB_TC_POST")) c->tc_post = atoi(v) != 0;
     cudaDeviceGetAttribute(&c->sms, cudaDevAttrMultiProcessorCount, device);
     if (c->sms <= 0) c->sms = 148;
     {

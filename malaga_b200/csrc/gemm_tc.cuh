@@ -116,9 +116,6 @@ __device__ __forceinline__ void tma2(void *dst, const CUtensorMap *m, int c0, in
         : "memory");
 }
 
-// Byte offset of (row r, 16-byte K chunk k16) of a K=32 int8 operand tile.
-__host__ __device__ __forceinline__ int tile_off(int r, int k16) { return (r >> 3) * 256 + k16 * 128 + (r & 7) * 16; }
-
 // Tensor maps of one launch: weight regions a, b, c, e (3-D: 8-byte words of
 // one (32-row group, block) slice, blocks or super-blocks, groups), activation
 // tiles (3-D: 8-byte words of an 8-row core group, row groups, blocks) and
@@ -128,8 +125,23 @@ struct Maps {
     CUtensorMap xq, xr;
 };
 
+// The next matmul's activations, written by the CTA that completes them
+// (RESID / RELU launches of the decode step): mode PREP_LN = LayerNorm of the
+// finished output rows, once every row tile of a token tile is done (the last
+// CTA of the token tile, found with an atomic counter); mode PREP_PLAIN = the
+// output quantized per 256-row super-block, once both row tiles of it are done.
+// mode < 0: none.
+struct Post {
+    int mode = -1;
+    const float *gamma = nullptr, *beta = nullptr;
+    int group = 1, ctype = 0;   // the consumer's activation format
+    QAct out;                   // the consumer's tensor-core layout (tq, trec, rs)
+    uint32_t *counters = nullptr;  // one per token tile (LN) or (token tile, super-block); zero between launches
+};
+
 struct Args {
     Maps m;
+    Post post;
     Matrix W;
     int rows;        // activation rows
     int row_tiles;   // Np / 128
@@ -306,9 +318,7 @@ __device__ void fused_prologue(const PrepArgs &p, int rows, int tt, bool write_x
                 for (int g = 1; g < G; ++g) m[c] = fmaxf(m[c], fabsf(y[c][g]));
             }
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-                for (int c = 0; c < UC; ++c) m[c] = fmaxf(m[c], __shfl_xor_sync(0xffffffffu, m[c], o));
+            for (int c = 0; c < UC; ++c) m[c] = warp_max_nonneg(m[c]);
 #pragma unroll
             for (int c = 0; c < UC; ++c) {
                 const int u = u0 + c;
@@ -318,7 +328,7 @@ __device__ void fused_prologue(const PrepArgs &p, int rows, int tt, bool write_x
                 for (int g = 0; g < G; ++g) {
                     const int t = u * G + g;
                     const int q = m[c] == 0.0f ? 0 : (int)roundf(__fdiv_rn(y[c][g], dd));
-                    xt[(size_t)t * NT * 32 + tc::tile_off(n, lane >> 4) + (lane & 15)] = (uint8_t)(int8_t)q;
+                    xt[(size_t)t * NT * 32 + tile_off(n, lane >> 4) + (lane & 15)] = (uint8_t)(int8_t)q;
                 }
                 if (lane == 0) {
                     if constexpr (TYPE == T_Q4_K) reinterpret_cast<float *>(xr)[((size_t)u * NT + n) * 8] = dd;
@@ -370,8 +380,8 @@ __device__ void fused_block_sums(int nb, int rows_here, const uint8_t *xt, uint8
     for (int i = i0; i < rows_here * nb; i += nthreads) {
         const int n = i % rows_here, t = i / rows_here;
         const uint8_t *row = xt + (size_t)t * NT * 32;
-        const int4 a = *reinterpret_cast<const int4 *>(row + tc::tile_off(n, 0));
-        const int4 b = *reinterpret_cast<const int4 *>(row + tc::tile_off(n, 1));
+        const int4 a = *reinterpret_cast<const int4 *>(row + tile_off(n, 0));
+        const int4 b = *reinterpret_cast<const int4 *>(row + tile_off(n, 1));
         int s = 0;
         s = __dp4a(a.x, 0x01010101, s);
         s = __dp4a(a.y, 0x01010101, s);
@@ -386,6 +396,67 @@ __device__ void fused_block_sums(int nb, int rows_here, const uint8_t *xt, uint8
     }
 }
 
+// LayerNorm of finished rows y[tok][0..K) (K <= 2048) into the consumer's
+// layout: one warp per token, SUM32 statistics in the engine's order.
+template <int G>
+__device__ void post_ln(const tc::Post &P, const float *y, int K, int t0, int t1, int w, int nw, int lane) {
+    constexpr int MAXV = 64;
+    const int T = K >> 5;
+    for (int tok = t0 + w; tok < t1; tok += nw) {
+        float vals[MAXV];
+#pragma unroll
+        for (int t = 0; t < MAXV; ++t)
+            if (t < T) vals[t] = __ldcg(y + (size_t)tok * K + 32 * t + lane);
+        float sum = 0.0f;
+#pragma unroll
+        for (int t = 0; t < MAXV; ++t)
+            if (t < T) sum = t == 0 ? vals[t] : __fadd_rn(sum, vals[t]);
+        const float mean = __fdiv_rn(warp_tree(sum), (float)K);
+        float s2 = 0.0f;
+#pragma unroll
+        for (int t = 0; t < MAXV; ++t)
+            if (t < T) {
+                const float c = __fsub_rn(vals[t], mean);
+                const float c2 = __fmul_rn(c, c);
+                s2 = t == 0 ? c2 : __fadd_rn(s2, c2);
+            }
+        const float var = __fdiv_rn(warp_tree(s2), (float)K);
+        const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
+#pragma unroll
+        for (int u = 0; u < MAXV / G; ++u) {
+            if (u * G >= T) break;
+            float v[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const int t = u * G + g;
+                v[g] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(vals[t], mean), rstd), __ldg(P.gamma + 32 * t + lane)),
+                                 __ldg(P.beta + 32 * t + lane));
+            }
+            store_unit<G>(P.out, P.ctype, tok, u * G, v, lane);
+        }
+    }
+}
+
+// Super-block `sb` (256 values) of finished rows y[tok][0..K) into the
+// consumer's layout: one warp per token.
+template <int G>
+__device__ void post_plain(const tc::Post &P, const float *y, int K, int sb, int t0, int t1, int w, int nw, int lane) {
+    for (int tok = t0 + w; tok < t1; tok += nw) {
+        float v[8];
+#pragma unroll
+        for (int g = 0; g < 8; ++g) v[g] = __ldcg(y + (size_t)tok * K + 256 * sb + 32 * g + lane);
+        if constexpr (G == 8) {
+            store_unit<8>(P.out, P.ctype, tok, 8 * sb, v, lane);
+        } else {
+#pragma unroll
+            for (int g = 0; g < 8; ++g) {
+                const float one[1] = {v[g]};
+                store_unit<1>(P.out, P.ctype, tok, 8 * sb + g, one, lane);
+            }
+        }
+    }
+}
+
 // XM < 0: activations by TMA from the qprep_row_kernel layout; otherwise the
 // PrepMode of the activations the CTA builds itself.
 template <int TYPE, int EPI, int NT, int XM>
@@ -397,11 +468,13 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
     constexpr int NH = NT / 2;  // tokens per epilogue warp
     constexpr uint32_t IDESC = idesc_i8(128, NT);
     extern __shared__ __align__(16) uint8_t smem_raw[];
-    __shared__ __align__(8) uint64_t full[RS], empty[RS], afull[AG], aempty[AG], tfull[TG], tempty[TG], fin, xready;
+    __shared__ __align__(8) uint64_t full[RS], empty[RS], afull[AG], aempty[AG], tfull[TG], tempty[TG], fin, xready,
+        ebar;
     __shared__ uint32_t tmem_base_sh;
     __shared__ volatile int abort_sh;
     __shared__ float best_v[4][64];
     __shared__ uint32_t best_i[4][64];
+    __shared__ int post_last;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const Matrix &W = A.W;
@@ -435,6 +508,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
         }
         mbar_init(&fin, 1);
         mbar_init(&xready, 8);
+        mbar_init(&ebar, 8);
         abort_sh = 0;
     }
     if (EPI == EPI_ARGMAX)
@@ -658,6 +732,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
             if (lane == 0) mbar_arrive(&xready);
         }
         Pos st, tg;
+        uint32_t ephase = 0;
         bool ok = true;
         for (int k = 0; k < my_tiles && ok && !abort_sh; ++k) {
             const int rt = tile_rt(k), tt = tile_tt(k);
@@ -816,6 +891,43 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
                     if (tok >= A.rows) break;  // uniform across the warp
                     if (live) epilogue_store<EPI>(A.g, row, tok, acc[n]);
                 }
+                if constexpr (EPI == EPI_RESID || EPI == EPI_RELU) {
+                    if (A.post.mode >= 0) {
+                        // the tile's outputs are stored; count it, and the CTA that
+                        // completes a token tile (LN) / super-block (PLAIN) prepares it
+                        const bool ln = A.post.mode == PREP_LN;
+                        // the 8 epilogue warps meet on a bounded mbarrier (a warp that
+                        // stopped on an error makes the others time out, not hang)
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&ebar);
+                        if (!(ok = wwait(&ebar, ephase, 128u))) break;
+                        ephase ^= 1;
+                        if (tid == 0) {
+                            __threadfence();
+                            const int idx = ln ? tt : tt * (A.row_tiles / 2) + rt / 2;
+                            const uint32_t old = atomicAdd(&A.post.counters[idx], 1u);
+                            post_last = old + 1 == (ln ? (uint32_t)A.row_tiles : 2u);
+                            if (post_last) {
+                                A.post.counters[idx] = 0;  // every CTA of this launch has counted
+                                __threadfence();
+                            }
+                        }
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&ebar);
+                        if (!(ok = wwait(&ebar, ephase, 128u))) break;
+                        ephase ^= 1;
+                        if (post_last) {
+                            const int t0 = tt * NT, t1 = min(A.rows, t0 + NT);
+                            if (ln) {
+                                if (A.post.group == 8) post_ln<8>(A.post, A.g.y, W.N, t0, t1, warp, 8, lane);
+                                else post_ln<1>(A.post, A.g.y, W.N, t0, t1, warp, 8, lane);
+                            } else {
+                                if (A.post.group == 8) post_plain<8>(A.post, A.g.y, W.N, rt / 2, t0, t1, warp, 8, lane);
+                                else post_plain<1>(A.post, A.g.y, W.N, rt / 2, t0, t1, warp, 8, lane);
+                            }
+                        }
+                    }
+                }
             }
         }
     }
@@ -887,7 +999,7 @@ __global__ void __launch_bounds__(256) qprep_row_kernel(PrepArgs p, QAct out) {
     const int rs = out.rs;
     for (int c = threadIdx.x; c < nb * 2; c += blockDim.x) {
         const int j = c >> 1, k16 = c & 1;
-        *reinterpret_cast<int4 *>(out.tq + ((size_t)j * (rs / 8) + (r >> 3)) * 256 + tc::tile_off(r & 7, k16)) =
+        *reinterpret_cast<int4 *>(out.tq + ((size_t)j * (rs / 8) + (r >> 3)) * 256 + tile_off(r & 7, k16)) =
             *reinterpret_cast<const int4 *>(s.q + 32 * j + 16 * k16);
     }
     if (p.ctype == T_Q4_K) {

@@ -108,16 +108,14 @@ __device__ __forceinline__ void quantize_group(const float (&y)[G], int8_t *q, f
     float m = fabsf(y[0]);
 #pragma unroll
     for (int u = 1; u < G; ++u) m = fmaxf(m, fabsf(y[u]));
-    const float amax = warp_max(m);
+    const float amax = warp_max_nonneg(m);
     const float dd = __fdiv_rn(amax, 127.0f);
 #pragma unroll
     for (int u = 0; u < G; ++u) {
         const int t = t0 + u;
         const int v = amax == 0.0f ? 0 : (int)roundf(__fdiv_rn(y[u], dd));
         q[32 * t + lane] = (int8_t)v;
-        int s = v;
-#pragma unroll
-        for (int off = 1; off < 16; off <<= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+        const int s = half_isum_redux(v, lane);          // this lane's 16-value half
         const int s_hi = __shfl_sync(0xffffffffu, s, 16);
         if (lane == 0) {
             d[t] = G == 1 ? round_h(dd) : dd;
@@ -459,6 +457,47 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs g) {
 }
 
 // ---------------------------------------------------------------------------
+// Tensor-core activation layout (QAct tq / trec, written for one consumer)
+
+// Byte offset of (row r, 16-byte K chunk k16) of a K=32 int8 operand tile in
+// the UMMA K-major no-swizzle layout: 8-row core groups of 256 bytes.
+__host__ __device__ __forceinline__ int tile_off(int r, int k16) { return (r >> 3) * 256 + k16 * 128 + (r & 7) * 16; }
+
+// One unit (G blocks of 32 values, y[g] = value lane of block j0+g of token
+// `tok`) into a tensor-core activation buffer: one scale, the bytes in the UMMA
+// layout, the unit record (same arithmetic as qprep_row_kernel).
+template <int G>
+__device__ __forceinline__ void store_unit(const QAct &o, int ctype, int tok, int j0, const float (&y)[G], int lane) {
+    float m = fabsf(y[0]);
+#pragma unroll
+    for (int g = 1; g < G; ++g) m = fmaxf(m, fabsf(y[g]));
+    const float amax = warp_max_nonneg(m);
+    const float dd = __fdiv_rn(amax, 127.0f);
+    const int rs = o.rs;
+    const bool sums = ctype == T_Q4_K && G == 8;  // only Q4_K records carry block sums
+    int s32[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const int q = amax == 0.0f ? 0 : (int)roundf(__fdiv_rn(y[g], dd));
+        o.tq[((size_t)(j0 + g) * (rs / 8) + (tok >> 3)) * 256 + tile_off(tok & 7, lane >> 4) + (lane & 15)] =
+            (uint8_t)(int8_t)q;
+        s32[g] = sums ? warp_isum_redux(q) : 0;
+    }
+    if (lane == 0) {
+        if (sums) {
+            int4 *rec = reinterpret_cast<int4 *>(o.trec + ((size_t)(j0 / 8) * rs + tok) * 32);
+            rec[0] = make_int4(__float_as_int(dd), (s32[0] & 0xffff) | (s32[1 % G] << 16),
+                               (s32[2 % G] & 0xffff) | (s32[3 % G] << 16), (s32[4 % G] & 0xffff) | (s32[5 % G] << 16));
+            rec[1] = make_int4((s32[6 % G] & 0xffff) | (s32[7 % G] << 16), 0, 0, 0);
+        } else if (G == 8) {
+            reinterpret_cast<float *>(o.trec)[(size_t)(j0 / 8) * rs + tok] = dd;
+        } else {
+            reinterpret_cast<float *>(o.trec)[(size_t)j0 * rs + tok] = round_h(dd);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
 // Single-query attention: one warp per (row, head, query).
 
 struct AttnArgs {
@@ -474,6 +513,11 @@ struct AttnArgs {
     long out_row;
     int H, hd, rows, queries;  // queries per batch row (encoder: S)
     int max_keys;
+    // Optional: the outputs also quantized into the next matmul's tensor-core
+    // layout (qo.tq != null; single queries, 4 heads of one row per CTA whose
+    // 4*hd values are whole units of the consumer qo_ctype).
+    QAct qo;
+    int qo_ctype;
 };
 
 // Programmatic dependent launch: a kernel may start while its predecessor in
@@ -520,7 +564,7 @@ __global__ void __launch_bounds__(128) attend_kernel(AttnArgs a) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const long task = (long)blockIdx.x * 4 + warp;
     const long total = (long)a.rows * a.H * a.queries;
-    if (task >= total) return;
+    if (task >= total) return;  // (never with qo: the host launches whole CTAs then)
     const int qi = (int)(task % a.queries), h = (int)((task / a.queries) % a.H), n = (int)(task / ((long)a.queries * a.H));
     float *e = e_sh + (size_t)warp * a.max_keys;
     const int keys = a.lens ? (int)a.lens[n] : (int)(*a.step) + 1;
@@ -578,6 +622,28 @@ __global__ void __launch_bounds__(128) attend_kernel(AttnArgs a) {
         float *o = a.out + (size_t)(n * (long)a.queries + qi) * a.out_row + h * HD;
 #pragma unroll
         for (int c = 0; c < PER; ++c) o[lane + 32 * c] = __fmul_rn(acc[c], inv);
+    }
+    if (a.qo.tq) {
+        // the CTA's 4 heads (4*HD consecutive values of row n) as units of the consumer
+        __shared__ float ov[4 * 128];
+        if (live)
+#pragma unroll
+            for (int c = 0; c < PER; ++c) ov[warp * HD + lane + 32 * c] = __fmul_rn(acc[c], inv);
+        __syncthreads();
+        const int j0 = (h - warp) * HD / 32;  // first block of the CTA's values
+        if (a.qo_ctype == T_Q4_K || a.qo_ctype == T_Q6_K) {
+            for (int u = warp; u < 4 * HD / 256; u += 4) {
+                float y[8];
+#pragma unroll
+                for (int g = 0; g < 8; ++g) y[g] = ov[256 * u + 32 * g + lane];
+                store_unit<8>(a.qo, a.qo_ctype, n, j0 + 8 * u, y, lane);
+            }
+        } else {
+            for (int t = warp; t < 4 * HD / 32; t += 4) {
+                const float y[1] = {ov[32 * t + lane]};
+                store_unit<1>(a.qo, a.qo_ctype, n, j0 + t, y, lane);
+            }
+        }
     }
 }
 
