@@ -93,6 +93,34 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.rows)}
 
 
+DESCRIBE = {
+    "c1": "batch 1, source 32 random ids + language tag + </s>, 32 forced greedy steps",
+    "c2": "batch 64 (q8_0 weights), source lengths U[8,64], 64 forced greedy steps",
+    "c2q4": "batch 64, source lengths U[8,64], 64 forced greedy steps",
+}
+
+# The LM-head kernel each workload runs (the roofline's dominant kernel).
+LM_KERNEL = {
+    "c1": "gemv_fused_kernel<Q6_K, ARGMAX, LN, 1> (small-batch LM head + argmax)",
+    "c2": "gemm_tc_kernel<Q8_0, ARGMAX, 64> (tcgen05 LM head + argmax)",
+    "c2q4": "gemm_tc_kernel<Q6_K, ARGMAX, 64> (tcgen05 LM head + argmax)",
+}
+
+
+def measured_traffic(workload: str):
+    """DRAM bytes per launch of the workload's LM-head kernel from the ncu capture
+    summarized in profiles/traffic.txt (lines: workload bytes_per_launch)."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.txt")) as f:
+            for line in f:
+                parts = line.split()
+                if len(parts) >= 2 and parts[0] == workload and not line.startswith("#"):
+                    return int(parts[1])
+    except OSError:
+        pass
+    return None
+
+
 def cpu_baseline(w, max_seconds: float = 20.0):
     """The oracle (CPU restatement, OpenMP on every host core) on a bounded sample:
     the workload's full batch decoding 2 steps from synthetic cross K/V."""
@@ -226,17 +254,16 @@ def main():
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8 dot / f32 (q8_1 activations x GGUF blocks)", "data": "synthetic",
-            "config": {"workload": f"{w.name}: NLLB-600M {w.preset} (random init, seed {w.seed}), batch {rows}, "
-                                   f"source lengths U[8,64], {steps} forced greedy steps",
+            "config": {"workload": f"{w.name}: NLLB-600M {w.preset} (random init, seed {w.seed}), {DESCRIBE[w.name]}",
                        "global_batch": rows * world, "decode_steps": steps, "parallelism": f"dp{world}",
                        "l2": "weights (%.0f MB/step) exceed the 126 MB L2" % (step_bytes / 1e6)},
             "gpu_launches": launches,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": int(ids_host.nbytes + lens_host.nbytes),
                     "d2h_bytes_per_step": int(out.nbytes)},
-            "roofline": {"bound": "hbm", "kernel": "gemv_kernel<EPI_ARGMAX> (tied LM head + argmax)",
+            "roofline": {"bound": "hbm", "kernel": LM_KERNEL[w.name],
                          "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                         "peak_source": peak_kind, "traffic": None, "algorithmic_bytes": lm_bytes,
-                         "launch_ms": lm_ms},
+                         "peak_source": peak_kind, "traffic": measured_traffic(w.name),
+                         "algorithmic_bytes": lm_bytes, "launch_ms": lm_ms},
             "step_roofline": {"weight_bytes_per_step": step_bytes, "eager_step_ms": step_ms,
                               "graph_step_ms": ms_step / steps,
                               "frac_of_hbm": step_bytes / (ms_step / steps / 1e3) / 1e9 / hbm},

@@ -279,6 +279,8 @@ struct mgb_ctx {
     // row in parallel beats the last CTA of a token tile); MGB_TC_POST overrides.
     int tc_post = 0;
     int sms = 148;  // multiprocessor count of the device (one tensor-core CTA each)
+    void *enc_ws = nullptr;  // encoder temporaries (grown on demand)
+    size_t enc_ws_bytes = 0;
     size_t smem_optin = 227 * 1024 - 4096;  // dynamic shared memory a tensor-core CTA may take
 
     mgb_status dalloc(void **p, size_t bytes) {
@@ -1397,30 +1399,49 @@ static mgb_status launch_step(mgb_ctx *c, StaticState *st, float *logits, int fo
 static mgb_status encode(mgb_ctx *c, const uint32_t *ids, const uint32_t *lens, int b, int S, mgb_batch **out) {
     const Config &g = c->cfg;
     const int d = g.d, H = g.enc_heads, hd = d / H, rows = b * S, ffn = g.enc_ffn, kmax = std::max(d, ffn);
-    std::vector<void *> tmp;
-    auto A = [&](void **p, size_t n) -> mgb_status {
-        TRY(c->dalloc(p, n));
-        tmp.push_back(*p);
-        return MGB_OK;
-    };
-    struct Guard {
-        std::vector<void *> &v;
-        ~Guard() {
-            for (void *p : v) cudaFree(p);
-        }
-    } guard{tmp};
     uint32_t *d_ids, *d_lens;
     float *x, *qkv, *a, *u, *xf = nullptr;
     QAct act;
-    TRY(A((void **)&d_ids, (size_t)4 * rows));
-    TRY(A((void **)&d_lens, (size_t)4 * b));
-    TRY(A((void **)&x, (size_t)4 * rows * d));
-    TRY(A((void **)&qkv, (size_t)4 * rows * 3 * d));
-    TRY(A((void **)&a, (size_t)4 * rows * d));
-    TRY(A((void **)&u, (size_t)4 * rows * ffn));
     const bool f32 = any_f32(c);
-    if (f32) TRY(A((void **)&xf, (size_t)4 * rows * kmax));
-    TRY(alloc_tc_act(c, rows, kmax, act, tmp, nullptr));
+    // temporaries carved from the context's encoder workspace (grown, never
+    // shrunk, released by mgb_clear_cache / mgb_close): no allocation per call
+    {
+        const int rp = (rows + 63) / 64 * 64, nbm = kmax / 32;
+        const size_t sz[] = {(size_t)4 * rows, (size_t)4 * b, (size_t)4 * rows * d, (size_t)4 * rows * 3 * d,
+                             (size_t)4 * rows * d, (size_t)4 * rows * ffn, f32 ? (size_t)4 * rows * kmax : 0,
+                             (size_t)nbm * 2 * rp * 32,
+                             std::max((size_t)(nbm / 8) * rp * 32, (size_t)nbm * rp * 4),
+                             (size_t)rp * kmax, (size_t)4 * rp * nbm, (size_t)4 * rp * nbm, (size_t)8 * rp * nbm};
+        size_t total = 0;
+        for (size_t n : sz) total += (n + 255) / 256 * 256;
+        if (total > c->enc_ws_bytes) {
+            if (c->enc_ws) cudaFree(c->enc_ws);
+            c->enc_ws = nullptr;
+            c->enc_ws_bytes = 0;
+            TRY(c->dalloc(&c->enc_ws, total));
+            c->enc_ws_bytes = total;
+        }
+        uint8_t *w = reinterpret_cast<uint8_t *>(c->enc_ws);
+        void *ptrs[13];
+        for (int i = 0; i < 13; ++i) {
+            ptrs[i] = sz[i] ? w : nullptr;
+            w += (sz[i] + 255) / 256 * 256;
+        }
+        d_ids = (uint32_t *)ptrs[0];
+        d_lens = (uint32_t *)ptrs[1];
+        x = (float *)ptrs[2];
+        qkv = (float *)ptrs[3];
+        a = (float *)ptrs[4];
+        u = (float *)ptrs[5];
+        xf = (float *)ptrs[6];
+        act.tq = (uint8_t *)ptrs[7];
+        act.trec = (uint8_t *)ptrs[8];
+        act.q = (int8_t *)ptrs[9];
+        act.d = (float *)ptrs[10];
+        act.s32 = (int *)ptrs[11];
+        act.s16 = (int *)ptrs[12];
+        act.rs = rp;
+    }
     CK(cudaMemcpyAsync(d_ids, ids, (size_t)4 * rows, cudaMemcpyHostToDevice, c->stream));
     CK(cudaMemcpyAsync(d_lens, lens, (size_t)4 * b, cudaMemcpyHostToDevice, c->stream));
     TRY(launch_check(c, [&] {
@@ -1549,6 +1570,9 @@ static void clear_cache(mgb_ctx *c) {
     cudaStreamSynchronize(c->stream);
     for (auto &e : c->cache) free_state(e.get());
     c->cache.clear();
+    if (c->enc_ws) cudaFree(c->enc_ws);
+    c->enc_ws = nullptr;
+    c->enc_ws_bytes = 0;
     cudaDeviceGraphMemTrim(c->device);
 }
 
