@@ -1540,7 +1540,15 @@ static mgb_status encode(mgb_ctx *c, const uint32_t *ids, const uint32_t *lens, 
             return s2;
         }
     }
+    uint32_t derr = 0;
+    CK(cudaMemcpyAsync(&derr, c->d_err, 4, cudaMemcpyDeviceToHost, c->stream));
     CK(cudaStreamSynchronize(c->stream));
+    if (derr) {
+        cudaMemsetAsync(c->d_err, 0, 4, c->stream);
+        cudaFree(B->cross);
+        cudaFree(B->d_lens);
+        return set_err(MGB_ERR_CUDA, "a device-side wait ran out of time in the encoder (flags %u)", derr);
+    }
     *out = B.release();
     return MGB_OK;
 }
@@ -1701,7 +1709,7 @@ static mgb_status run_greedy(mgb_ctx *c, const mgb_batch *B, uint32_t tgt, int m
     CK(cudaStreamSynchronize(c->stream));
     if (derr) {
         cudaMemsetAsync(c->d_err, 0, 4, c->stream);
-        return set_err(MGB_ERR_CUDA, "a device-side wait on a weight copy ran out of time (flags %u)", derr);
+        return set_err(MGB_ERR_CUDA, "a device-side wait ran out of time (flags %u)", derr);
     }
     for (int r = 0; r < n; ++r) {
         uint32_t len = 0;
