@@ -115,6 +115,15 @@ MGB_API mgb_status mgb_greedy(mgb_ctx *ctx, const mgb_batch *batch, uint32_t tgt
 MGB_API mgb_status mgb_greedy_logits(mgb_ctx *ctx, const mgb_batch *batch, uint32_t tgt_lang, uint32_t max_new,
                              int force_steps, uint32_t *out_ids, float *logits);
 
+/* Beam search over an encoded batch (Translator::beam_search, translator.rs:250-358):
+ * beam width k (1..8), length penalty (score / (len+1)^penalty), at most max_new
+ * tokens; batch * k <= 64 rows. The prefix [decoder_start, tgt_lang] is fed first.
+ * out_ids: [b, max_new] the best hypothesis per sentence (eos not included, pad
+ * after it); out_lens: [b] its length. Log-softmax statistics and per-row top-k
+ * run on the device, the k*k candidate merge on the host, as in the reference. */
+MGB_API mgb_status mgb_beam(mgb_ctx *ctx, const mgb_batch *batch, uint32_t tgt_lang, uint32_t k, float length_penalty,
+                    uint32_t max_new, uint32_t *out_ids, uint32_t *out_lens);
+
 /* Frees every cached static state and CUDA graph (GraphCache::clear, graph.rs:193-200). */
 MGB_API mgb_status mgb_clear_cache(mgb_ctx *ctx);
 

@@ -41,6 +41,7 @@ SIGNATURES = {
     "mgb_batch_free": (None, [_vp]),
     "mgb_batch_cross": (_i, [_vp, _vp, _u32, _i, _vp]),
     "mgb_greedy": (_i, [_vp, _vp, _u32, _u32, _u32, _i, _vp, _vp]),
+    "mgb_beam": (_i, [_vp, _vp, _u32, _u32, ctypes.c_float, _u32, _vp, _vp]),
     "mgb_greedy_logits": (_i, [_vp, _vp, _u32, _u32, _i, _vp, _vp]),
     "mgb_clear_cache": (_i, [_vp]),
     "mgb_cuda_stream": (_vp, [_vp]),

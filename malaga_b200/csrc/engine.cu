@@ -28,6 +28,7 @@
 #include <vector>
 
 #include "../../include/malaga_b200.h"
+#include "beam.cuh"
 #include "gemm_tc.cuh"
 
 using namespace mgb;
@@ -223,6 +224,12 @@ struct StaticState {
     QAct act, act2;                  // tensor-core activations (the step alternates between them)
     uint32_t *counters = nullptr;    // completion counters of the matmuls' post steps
     size_t counter_bytes = 0;
+    // beam search (allocated on first use): step logits, top-k, row sources and a
+    // second set of self-attention caches to gather into
+    float *beam_logits = nullptr, *beam_vals = nullptr;
+    uint32_t *beam_idx = nullptr;
+    int *beam_from = nullptr;
+    std::vector<__half *> kc2, vc2;
     std::vector<__half *> kc, vc, ck, cv;
     float *part_v = nullptr;
     uint32_t *part_i = nullptr;
@@ -1109,7 +1116,7 @@ static mgb_status step_op(mgb_ctx *c, StaticState *st, const FusedArgs &f, int *
 // projection per super-block; layer 0's embedding input by qprep_row. Where a
 // shape does not allow that, qprep_row prepares the input instead.
 static mgb_status launch_step_tc(mgb_ctx *c, StaticState *st, float *logits, int force, cudaEvent_t lm0,
-                                 cudaEvent_t lm1) {
+                                 cudaEvent_t lm1, bool finalize) {
     const Config &g = c->cfg;
     const int b = st->b, d = g.d, H = g.dec_heads, hd = d / H;
     QAct *X = &st->act, *Y = &st->act2;  // X: input of the next matmul in program order
@@ -1264,6 +1271,7 @@ static mgb_status launch_step_tc(mgb_ctx *c, StaticState *st, float *logits, int
     TRY((gemm_tc<EPI_ARGMAX, -1>(c, c->embed, X, nullptr, b, gl, &parts)));
     st->lm_parts = parts;
     if (lm1) CK(cudaEventRecord(lm1, c->stream));
+    if (!finalize) return MGB_OK;
     const int threads = std::min(1024, std::max(32, 32 * b));
     cudaError_t e = launch_pdl(greedy_finalize_kernel, dim3(1), dim3(threads), 0, c->stream,
                                (const float *)st->part_v, (const uint32_t *)st->part_i, parts, b,
@@ -1277,9 +1285,9 @@ static mgb_status launch_step_tc(mgb_ctx *c, StaticState *st, float *logits, int
 // One greedy decoder step on the state's fixed buffers (model.rs:552-612):
 // 6 fused matmuls + 2 attentions per layer, the LM head with argmax, finalize.
 static mgb_status launch_step(mgb_ctx *c, StaticState *st, float *logits, int force,
-                              cudaEvent_t lm0 = nullptr, cudaEvent_t lm1 = nullptr) {
+                              cudaEvent_t lm0 = nullptr, cudaEvent_t lm1 = nullptr, bool finalize = true) {
     if (st->b >= c->tc_min_rows && st->act.tq && !c->tc_fused && tc_ok(c->embed) && tc_ok(c->dec[0].qkv))
-        return launch_step_tc(c, st, logits, force, lm0, lm1);
+        return launch_step_tc(c, st, logits, force, lm0, lm1, finalize);
     const Config &g = c->cfg;
     const int b = st->b, d = g.d, H = g.dec_heads, hd = d / H;
     auto src = [&](const float *x, int K, const Norm *n) {
@@ -1383,6 +1391,7 @@ static mgb_status launch_step(mgb_ctx *c, StaticState *st, float *logits, int fo
     TRY((step_op<EPI_ARGMAX, PREP_LN>(c, st, fl, &parts)));
     st->lm_parts = parts;
     if (lm1) CK(cudaEventRecord(lm1, c->stream));
+    if (!finalize) return MGB_OK;
     const int threads = std::min(1024, std::max(32, 32 * b));
     cudaError_t e = launch_pdl(greedy_finalize_kernel, dim3(1), dim3(threads), 0, c->stream,
                                (const float *)st->part_v, (const uint32_t *)st->part_i, parts, b,
@@ -1600,9 +1609,11 @@ static mgb_status reset_finished(mgb_ctx *c, StaticState *st, int active) {
 
 // Finds or creates the static state of the (rows, source, output) bucket and
 // loads the batch into it (graph.rs:236-268).
-static mgb_status acquire_state(mgb_ctx *c, const mgb_batch *B, int max_new, bool pad_rows, StaticState **out) {
+// rep > 1: every sentence fills rep consecutive rows (beam search).
+static mgb_status acquire_state(mgb_ctx *c, const mgb_batch *B, int max_new, bool pad_rows, StaticState **out,
+                                int rep = 1) {
     const Config &g = c->cfg;
-    const int n = B->b, H = g.dec_heads, hd = g.d / H;
+    const int n = B->b * rep, H = g.dec_heads, hd = g.d / H;
     const int b = pad_rows ? (int)next_pow2((uint32_t)n) : n;
     if (b > 64) return set_err(MGB_ERR_INVALID, "batch of %d rows exceeds 64", n);
     const int s = bucket(B->s, 16, g.max_pos), m = bucket(max_new + 2, 32, g.max_pos);
@@ -1616,21 +1627,254 @@ static mgb_status acquire_state(mgb_ctx *c, const mgb_batch *B, int max_new, boo
     }
     st->last_used = ++c->clock;
     // reset (graph.rs:91-113): cross K/V, lens, start token, step, finished
-    const size_t per = (size_t)n * H * B->s * hd;
+    const size_t per = (size_t)B->b * H * B->s * hd;
     for (int l = 0; l < g.dec_layers; ++l) {
-        CK(cudaMemcpy2DAsync(st->ck[l], (size_t)s * hd * 2, B->cross + per * 2 * l, (size_t)B->s * hd * 2,
-                             (size_t)B->s * hd * 2, (size_t)n * H, cudaMemcpyDeviceToDevice, c->stream));
-        CK(cudaMemcpy2DAsync(st->cv[l], (size_t)s * hd * 2, B->cross + per * (2 * l + 1), (size_t)B->s * hd * 2,
-                             (size_t)B->s * hd * 2, (size_t)n * H, cudaMemcpyDeviceToDevice, c->stream));
+        if (rep == 1) {
+            CK(cudaMemcpy2DAsync(st->ck[l], (size_t)s * hd * 2, B->cross + per * 2 * l, (size_t)B->s * hd * 2,
+                                 (size_t)B->s * hd * 2, (size_t)n * H, cudaMemcpyDeviceToDevice, c->stream));
+            CK(cudaMemcpy2DAsync(st->cv[l], (size_t)s * hd * 2, B->cross + per * (2 * l + 1), (size_t)B->s * hd * 2,
+                                 (size_t)B->s * hd * 2, (size_t)n * H, cudaMemcpyDeviceToDevice, c->stream));
+        } else {
+            TRY(launch_check(c, [&] {
+                cross_replicate_kernel<<<c->sms * 4, 256, 0, c->stream>>>(B->cross + per * 2 * l, st->ck[l], n, rep, H,
+                                                                          B->s, s, hd);
+                cross_replicate_kernel<<<c->sms * 4, 256, 0, c->stream>>>(B->cross + per * (2 * l + 1), st->cv[l], n,
+                                                                          rep, H, B->s, s, hd);
+            }));
+        }
     }
     std::vector<uint32_t> lens(b, 1);
-    for (int i = 0; i < n; ++i) lens[i] = B->lens[i];
+    for (int i = 0; i < n; ++i) lens[i] = B->lens[i / rep];
     CK(cudaMemcpyAsync(st->lens, lens.data(), 4 * b, cudaMemcpyHostToDevice, c->stream));
     CK(cudaMemsetAsync(st->step, 0, 4, c->stream));
     if (st->counters) CK(cudaMemsetAsync(st->counters, 0, st->counter_bytes, c->stream));
     TRY(set_ids(c, st, (uint32_t)g.start));
     TRY(reset_finished(c, st, n));
     *out = st;
+    return MGB_OK;
+}
+
+// Beam-search buffers of a state (first use).
+static mgb_status ensure_beam(mgb_ctx *c, StaticState *st) {
+    if (st->beam_logits) return MGB_OK;
+    const Config &g = c->cfg;
+    const int b = st->b, H = g.dec_heads, hd = g.d / H;
+    auto A = [&](void **p, size_t n) -> mgb_status {
+        TRY(c->dalloc(p, n));
+        st->allocs.push_back(*p);
+        st->bytes += n;
+        return MGB_OK;
+    };
+    TRY(A((void **)&st->beam_logits, (size_t)4 * b * g.V));
+    TRY(A((void **)&st->beam_vals, (size_t)4 * b * 8));
+    TRY(A((void **)&st->beam_idx, (size_t)4 * b * 8));
+    TRY(A((void **)&st->beam_from, (size_t)4 * b));
+    st->kc2.resize(g.dec_layers);
+    st->vc2.resize(g.dec_layers);
+    for (int l = 0; l < g.dec_layers; ++l) {
+        TRY(A((void **)&st->kc2[l], (size_t)2 * b * H * st->m * hd));
+        TRY(A((void **)&st->vc2[l], (size_t)2 * b * H * st->m * hd));
+    }
+    return MGB_OK;
+}
+
+// Rust's f32::total_cmp key (IEEE total order as a signed integer).
+static int32_t total_key(float f) {
+    int32_t v;
+    memcpy(&v, &f, 4);
+    return v ^ (int32_t)(((uint32_t)(v >> 31)) >> 1);
+}
+
+// Beam search (translator.rs:250-335; top-k 343-358): rows = sentences x k on
+// the device; per step the engine's decode step writes every row's logits, the
+// device computes log_softmax statistics and each row's top k, and the host
+// merges the k*k candidates of every sentence (score descending, ties in
+// insertion order, beam-major then rank), retires hypotheses that end in eos
+// or at max_new with score / (len+1)^lp, and reorders the self-attention
+// caches by source row. Prefill [</s>, tgt] as two single-token steps.
+static mgb_status run_beam(mgb_ctx *c, const mgb_batch *B, uint32_t tgt, int k, float lp, int max_new,
+                           uint32_t *out_ids, uint32_t *out_lens) {
+    const Config &g = c->cfg;
+    const int nb = B->b, rows = nb * k, V = g.V, H = g.dec_heads, hd = g.d / H;
+    const uint32_t eos = (uint32_t)g.eos;
+    StaticState *st = nullptr;
+    TRY(acquire_state(c, B, max_new, false, &st, k));
+    TRY(ensure_beam(c, st));
+    const std::vector<__half *> kc0 = st->kc, vc0 = st->vc;
+    struct Restore {  // the state's cache pointers back as they were (graphs of other runs hold them)
+        StaticState *st;
+        const std::vector<__half *> &k, &v;
+        ~Restore() {
+            if (st->kc != k) {
+                std::swap(st->kc, st->kc2);
+                std::swap(st->vc, st->vc2);
+            }
+        }
+    } restore{st, kc0, vc0};
+    auto set_step = [&](uint32_t v) -> mgb_status {
+        CK(cudaMemcpyAsync(st->step, &v, 4, cudaMemcpyHostToDevice, c->stream));
+        return cudaStreamSynchronize(c->stream) == cudaSuccess ? MGB_OK : cuda_err(cudaGetLastError(), "beam step");
+    };
+    TRY(set_step(0));
+    TRY(launch_step(c, st, st->beam_logits, 1, nullptr, nullptr, false));
+    TRY(set_ids(c, st, tgt));
+    TRY(set_step(1));
+    TRY(launch_step(c, st, st->beam_logits, 1, nullptr, nullptr, false));
+    const int L = max_new + 1;
+    std::vector<float> alive_score(rows, 0.0f), nscore(rows), vals((size_t)rows * k);
+    std::vector<uint32_t> alive_tok((size_t)rows * L, 0), ntok((size_t)rows * L, 0), idx((size_t)rows * k);
+    std::vector<int> alive_len(rows, 0), nlen(rows), n_alive(nb, 1), reorder(rows);
+    std::vector<uint32_t> next(rows);
+    struct Done {
+        float score;
+        std::vector<uint32_t> tok;
+    };
+    std::vector<std::vector<Done>> done(nb);
+    std::vector<uint8_t> is_done(nb, 0);
+    const size_t cap_done = (size_t)4 * k * L;
+    struct Cand {
+        float score;
+        int beam;
+        uint32_t tok;
+    };
+    std::vector<Cand> cands((size_t)k * k);
+    for (int step = 1; step <= max_new; ++step) {
+        TRY(launch_check(c, [&] {
+            switch (k) {
+                case 1: beam_topk_kernel<1><<<rows, 256, 0, c->stream>>>(st->beam_logits, V, st->beam_vals, st->beam_idx); break;
+                case 2: beam_topk_kernel<2><<<rows, 256, 0, c->stream>>>(st->beam_logits, V, st->beam_vals, st->beam_idx); break;
+                case 3: beam_topk_kernel<3><<<rows, 256, 0, c->stream>>>(st->beam_logits, V, st->beam_vals, st->beam_idx); break;
+                case 4: beam_topk_kernel<4><<<rows, 256, 0, c->stream>>>(st->beam_logits, V, st->beam_vals, st->beam_idx); break;
+                case 5: beam_topk_kernel<5><<<rows, 256, 0, c->stream>>>(st->beam_logits, V, st->beam_vals, st->beam_idx); break;
+                case 6: beam_topk_kernel<6><<<rows, 256, 0, c->stream>>>(st->beam_logits, V, st->beam_vals, st->beam_idx); break;
+                case 7: beam_topk_kernel<7><<<rows, 256, 0, c->stream>>>(st->beam_logits, V, st->beam_vals, st->beam_idx); break;
+                default: beam_topk_kernel<8><<<rows, 256, 0, c->stream>>>(st->beam_logits, V, st->beam_vals, st->beam_idx); break;
+            }
+        }));
+        CK(cudaMemcpyAsync(vals.data(), st->beam_vals, 4 * vals.size(), cudaMemcpyDeviceToHost, c->stream));
+        CK(cudaMemcpyAsync(idx.data(), st->beam_idx, 4 * idx.size(), cudaMemcpyDeviceToHost, c->stream));
+        CK(cudaStreamSynchronize(c->stream));
+        int nr = 0;
+        for (int s = 0; s < nb; ++s) {
+            int nc = 0;
+            for (int bi = 0; bi < n_alive[s]; ++bi) {
+                const int row = s * k + bi;
+                for (int j = 0; j < k; ++j)
+                    cands[nc++] = {alive_score[row] + vals[(size_t)row * k + j], bi, idx[(size_t)row * k + j]};
+            }
+            // stable sort, descending by total order
+            for (int i = 1; i < nc; ++i) {
+                const Cand t = cands[i];
+                int q = i - 1;
+                while (q >= 0 && total_key(t.score) > total_key(cands[q].score)) {
+                    cands[q + 1] = cands[q];
+                    --q;
+                }
+                cands[q + 1] = t;
+            }
+            int na = 0;
+            for (int ci = 0; ci < nc && na < k; ++ci) {
+                const Cand &cd = cands[ci];
+                const int src = s * k + cd.beam;
+                if (cd.tok == eos || step == max_new) {
+                    if (!is_done[s] && done[s].size() < cap_done) {
+                        Done dn;
+                        dn.tok.assign(alive_tok.begin() + (size_t)src * L, alive_tok.begin() + (size_t)src * L + alive_len[src]);
+                        if (cd.tok != eos) dn.tok.push_back(cd.tok);
+                        const int dl = (int)dn.tok.size();
+                        const float pen = powf((float)(dl + 1 > 1 ? dl + 1 : 1), lp);
+                        dn.score = cd.score / pen;
+                        done[s].push_back(std::move(dn));
+                    }
+                    continue;
+                }
+                const int dst = s * k + na;
+                std::copy(alive_tok.begin() + (size_t)src * L, alive_tok.begin() + (size_t)src * L + alive_len[src],
+                          ntok.begin() + (size_t)dst * L);
+                ntok[(size_t)dst * L + alive_len[src]] = cd.tok;
+                nlen[dst] = alive_len[src] + 1;
+                nscore[dst] = cd.score;
+                reorder[nr] = src;
+                next[nr] = cd.tok;
+                ++nr;
+                ++na;
+            }
+            float best_done = -INFINITY;
+            for (const Done &dn : done[s]) best_done = std::max(best_done, dn.score);
+            const float best_alive = na > 0 ? nscore[s * k] / powf((float)(step + 1), lp) : -INFINITY;
+            if ((int)done[s].size() >= k && best_done >= best_alive) is_done[s] = 1;
+            while (na < k) {
+                const int dst = s * k + na;
+                reorder[nr] = s * k;
+                next[nr] = eos;
+                ++nr;
+                nscore[dst] = -INFINITY;
+                nlen[dst] = 0;
+                ++na;
+            }
+            n_alive[s] = k;
+        }
+        alive_score = nscore;
+        alive_tok = ntok;
+        alive_len = nlen;
+        bool all = true;
+        for (int s = 0; s < nb; ++s) all = all && is_done[s];
+        if (step == max_new || all) break;
+        // reorder the self-attention caches (positions 0..step) by source row
+        CK(cudaMemcpyAsync(st->beam_from, reorder.data(), 4 * rows, cudaMemcpyHostToDevice, c->stream));
+        CK(cudaMemcpyAsync(st->ids, next.data(), 4 * rows, cudaMemcpyHostToDevice, c->stream));
+        for (int l0 = 0; l0 < g.dec_layers; l0 += 64) {
+            KvGather kg{};
+            kg.n = 0;
+            for (int l = l0; l < std::min(g.dec_layers, l0 + 64); ++l) {
+                kg.src[kg.n] = st->kc[l];
+                kg.dst[kg.n++] = st->kc2[l];
+                kg.src[kg.n] = st->vc[l];
+                kg.dst[kg.n++] = st->vc2[l];
+            }
+            TRY(launch_check(c, [&] {
+                kv_gather_kernel<<<c->sms * 4, 256, 0, c->stream>>>(kg, st->beam_from, rows, H, st->m, hd, step + 1);
+            }));
+        }
+        std::swap(st->kc, st->kc2);
+        std::swap(st->vc, st->vc2);
+        TRY(set_step((uint32_t)step + 1));
+        TRY(launch_step(c, st, st->beam_logits, 1, nullptr, nullptr, false));
+    }
+    uint32_t derr = 0;
+    CK(cudaMemcpyAsync(&derr, c->d_err, 4, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    if (derr) {
+        cudaMemsetAsync(c->d_err, 0, 4, c->stream);
+        return set_err(MGB_ERR_CUDA, "a device-side wait ran out of time (flags %u)", derr);
+    }
+    for (int s = 0; s < nb; ++s) {
+        const uint32_t *tok = nullptr;
+        int len = 0;
+        if (!done[s].empty()) {
+            int best = -1;
+            float bs = -INFINITY;
+            for (int q = 0; q < (int)done[s].size(); ++q)
+                if (best < 0 || done[s][q].score >= bs) {  // max_by: the last maximum wins
+                    bs = done[s][q].score;
+                    best = q;
+                }
+            tok = done[s][best].tok.data();
+            len = (int)done[s][best].tok.size();
+        } else {
+            int best = -1;
+            float bs = -INFINITY;
+            for (int bi = 0; bi < k; ++bi)
+                if (best < 0 || alive_score[s * k + bi] >= bs) {
+                    bs = alive_score[s * k + bi];
+                    best = bi;
+                }
+            tok = alive_tok.data() + (size_t)(s * k + best) * L;
+            len = alive_len[s * k + best];
+        }
+        if (out_lens) out_lens[s] = (uint32_t)len;
+        for (int t = 0; t < max_new; ++t) out_ids[(size_t)s * max_new + t] = t < len ? tok[t] : (uint32_t)g.pad;
+    }
     return MGB_OK;
 }
 
@@ -1873,6 +2117,17 @@ mgb_status mgb_greedy(mgb_ctx *c, const mgb_batch *B, uint32_t tgt, uint32_t max
         if (s != MGB_OK) g_err = why + "; retry without graphs: " + g_err;
     }
     return s;
+}
+
+mgb_status mgb_beam(mgb_ctx *c, const mgb_batch *B, uint32_t tgt, uint32_t k, float length_penalty, uint32_t max_new,
+                    uint32_t *out_ids, uint32_t *out_lens) {
+    TRY(check_greedy(c, B, tgt, max_new));
+    if (!out_ids) return set_err(MGB_ERR_INVALID, "null out_ids");
+    if (k < 1 || k > 8) return set_err(MGB_ERR_INVALID, "beam width %u outside 1..8", k);
+    if ((uint64_t)B->b * k > 64) return set_err(MGB_ERR_INVALID, "batch x beam = %llu rows exceeds 64",
+                                                (unsigned long long)B->b * k);
+    CK(cudaSetDevice(c->device));
+    return run_beam(c, B, tgt, (int)k, length_penalty, (int)max_new, out_ids, out_lens);
 }
 
 mgb_status mgb_greedy_logits(mgb_ctx *c, const mgb_batch *B, uint32_t tgt, uint32_t max_new, int force,

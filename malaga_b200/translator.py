@@ -118,6 +118,16 @@ class Engine:
                                      lens.ctypes.data))
         return out, lens
 
+    def beam(self, batch: Batch, tgt_lang: int, k: int, max_new: int,
+             length_penalty: float = 1.0) -> tuple[np.ndarray, np.ndarray]:
+        """Beam search (translator.rs:250-358): the best hypothesis per row [b, max_new]
+        (pad after its end, eos excluded) and its length."""
+        out = np.empty((batch.size, max_new), np.uint32)
+        lens = np.empty(batch.size, np.uint32)
+        check(_lib.load().mgb_beam(self.h, batch.h, tgt_lang, k, float(length_penalty), max_new, out.ctypes.data,
+                                   lens.ctypes.data))
+        return out, lens
+
     def greedy_logits(self, batch: Batch, tgt_lang: int, max_new: int, force: bool = False):
         out = np.empty((batch.size, max_new), np.uint32)
         logits = np.empty((max_new, batch.size, self.info["vocab_size"]), np.float32)
@@ -155,17 +165,19 @@ class Translator:
         """Target ids without specials for already tokenised sources (generate_to)."""
         if not src:
             return []
-        if opts.beam_size > 1:
-            raise NotImplementedError("beam search is not built into this engine yet")
         max_new = max(self.budget(len(s), opts) for s in src)
         batch = self.engine.encode(src)
         try:
-            out, lens = self.engine.greedy(batch, tgt_lang, max_new, max(1, opts.sync_every), opts.force_steps)
+            if opts.beam_size > 1:
+                out, lens = self.engine.beam(batch, tgt_lang, opts.beam_size, max_new, opts.length_penalty)
+            else:
+                out, lens = self.engine.greedy(batch, tgt_lang, max_new, max(1, opts.sync_every), opts.force_steps)
         finally:
             batch.free()
         res = []
         for i, s in enumerate(src):
-            row = [int(t) for t in out[i]] if opts.force_steps else [int(t) for t in out[i, : lens[i]]]
+            row = ([int(t) for t in out[i]] if opts.force_steps and opts.beam_size <= 1
+                   else [int(t) for t in out[i, : lens[i]]])
             res.append(row[: self.budget(len(s), opts)])
         return res
 

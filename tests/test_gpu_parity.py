@@ -212,3 +212,32 @@ def test_tensor_core_equals_small_batch_kernels(gpu, model, preset, monkeypatch)
     assert np.array_equal(lg_a.view(np.uint32), lg_b.view(np.uint32))
     out, _ = eng_tc.greedy(eng_tc.encode(src), V - 2, 4, force=True)
     np.testing.assert_array_equal(out, ids_a)
+
+
+@pytest.mark.parametrize("name,preset,n,k", [("tiny", "q8_0", 6, 3), ("tiny", "f32", 4, 2), ("mid", "q4_k_m", 4, 4),
+                                             ("mid", "q8_0", 3, 5)])
+def test_beam_search_matches_oracle(gpu, model, name, preset, n, k):
+    """Beam search (translator.rs:250-358): device log_softmax + top-k, host merge;
+    the hypotheses equal the oracle's (mid q4_k_m: 16 rows run the tcgen05 step)."""
+    path = model(name, preset)
+    if name == "tiny":
+        src, tgt = tiny_sentences()[:n], TINY_TGT
+    else:
+        V = models.config_of(name).vocab_size
+        src, tgt = mid_sentences(V, n=n, seed=9), V - 2
+    want = oracle.Oracle(path).beam(src, tgt, k, 12)
+    eng = Engine(path)
+    out, lens = eng.beam(eng.encode(src), tgt, k, 12)
+    got = [[int(t) for t in out[i, : lens[i]]] for i in range(len(src))]
+    assert got == [[int(t) for t in r] for r in want]
+
+
+def test_beam_one_equals_greedy_on_device(gpu, model):
+    """pipeline.rs:60-69: beam 1 gives the greedy output."""
+    path = model("tiny", "q8_0")
+    src = tiny_sentences()
+    t = Translator(Engine(path))
+    greedy = t.generate(src, TINY_TGT, GenOptions(max_new_tokens=16))
+    eng = Engine(path)
+    out, lens = eng.beam(eng.encode(src), TINY_TGT, 1, 16)
+    assert [[int(x) for x in out[i, : lens[i]]] for i in range(len(src))] == greedy
