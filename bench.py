@@ -253,7 +253,7 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "int8 dot / f32 (q8_1 activations x GGUF blocks)", "data": "synthetic",
+            "vs_baseline": None, "dtype": "int8 dot / f32 (q8 activations x GGUF blocks)", "data": "synthetic",
             "config": {"workload": f"{w.name}: NLLB-600M {w.preset} (random init, seed {w.seed}), {DESCRIBE[w.name]}",
                        "global_batch": rows * world, "decode_steps": steps, "parallelism": f"dp{world}",
                        "l2": "weights (%.0f MB/step) exceed the 126 MB L2" % (step_bytes / 1e6)},

@@ -216,6 +216,13 @@ void q6k_block_values(const uint8_t *row, int j, uint8_t *q) {
 // ---------------------------------------------------------------------------
 // Engine
 
+// Split-K buffers of a decode step (StaticState): partials and tile counters.
+struct SplitBufs {
+    float *part = nullptr;
+    uint32_t *count = nullptr;
+    size_t part_floats = 0;
+};
+
 struct StaticState {
     int b = 0, s = 0, m = 0;
     uint32_t *ids = nullptr, *step = nullptr, *out = nullptr, *lens = nullptr;
@@ -224,6 +231,7 @@ struct StaticState {
     QAct act, act2;                  // tensor-core activations (the step alternates between them)
     uint32_t *counters = nullptr;    // completion counters of the matmuls' post steps
     size_t counter_bytes = 0;
+    SplitBufs split;                 // split-K partials and tile counters
     // beam search (allocated on first use): step logits, top-k, row sources and a
     // second set of self-attention caches to gather into
     float *beam_logits = nullptr, *beam_vals = nullptr;
@@ -281,10 +289,15 @@ struct mgb_ctx {
     // Decode-step tensor-core matmuls build their activations in the kernel
     // (1) or read them from qprep_row_kernel (0); MGB_TC_FUSED overrides.
     int tc_fused = 0;
-    // Producers prepare the next matmul's tensor-core activations (post steps,
-    // attention) (1) or qprep_row does (0, faster on B200 so far: one CTA per
-    // row in parallel beats the last CTA of a token tile); MGB_TC_POST overrides.
+    // Matmuls' post steps prepare the next LayerNorm / hidden-layer activations
+    // (1) or qprep_row does (0, faster on B200 so far: one CTA per row in parallel
+    // beats the last CTA of a token tile); MGB_TC_POST overrides.
     int tc_post = 0;
+    // The attention kernel quantizes its outputs for the next matmul (1) or
+    // qprep_row does (0); MGB_TC_ATTN_Q overrides.
+    int tc_attn_q = 1;
+    // Matmuls with too few tiles for the SMs split their K stages (MGB_TC_SPLIT overrides).
+    int tc_split = 1;
     int sms = 148;  // multiprocessor count of the device (one tensor-core CTA each)
     void *enc_ws = nullptr;  // encoder temporaries (grown on demand)
     size_t enc_ws_bytes = 0;
@@ -959,7 +972,8 @@ static mgb_status gemm_tc_t(mgb_ctx *c, const tc::Args &a, int nt, int grid) {
 // token tile each); *ctas returns its CTA count, the partial count per row.
 template <int EPI, int XM>
 static mgb_status gemm_tc(mgb_ctx *c, const Matrix &W, const QAct *act, const PrepArgs *p, int rows,
-                          const GemvArgs &g, int *ctas = nullptr, const tc::Post *post = nullptr) {
+                          const GemvArgs &g, int *ctas = nullptr, const tc::Post *post = nullptr,
+                          const SplitBufs *split = nullptr) {
     const int chunk = EPI == EPI_ARGMAX ? 64 : rows;
     for (int t0 = 0; t0 < rows; t0 += chunk) {
         const int n = std::min(chunk, rows - t0);
@@ -988,6 +1002,22 @@ static mgb_status gemm_tc(mgb_ctx *c, const Matrix &W, const QAct *act, const Pr
         }
         a.row_tiles = W.Np / 128;
         a.tok_tiles = (n + nt - 1) / nt;
+        a.splits = 1;
+        if (split && split->part && XM < 0 && EPI != EPI_ARGMAX) {
+            // too few tiles for the SMs: split the stages (2 or 4 ways) if they divide
+            const int tiles = a.row_tiles * a.tok_tiles, ns = (W.nb + 7) / 8;
+            const int nu = W.type == T_Q8_0 ? W.nb : W.nsb;
+            // (each split keeps 4+ stages: below that the fixup costs more than the parallelism gains)
+            while (a.splits < 4 && tiles * a.splits * 2 <= c->sms && ns % (a.splits * 2) == 0 &&
+                   ns / (a.splits * 2) >= 4)
+                a.splits *= 2;
+            if (a.splits > 1 && (size_t)a.tok_tiles * nt * W.Np * nu > split->part_floats) a.splits = 1;
+            if (a.splits > 1) {
+                a.kpart = split->part;
+                a.kcount = split->count;
+                grid = std::min(tiles * a.splits, c->sms);
+            }
+        }
         if (ctas) *ctas = grid;
         TRY(make_maps(W, XM >= 0 ? nullptr : act, nt, a.m));
         switch (W.type) {
@@ -1080,6 +1110,15 @@ static mgb_status new_state(mgb_ctx *c, int b, int s, int m, StaticState **out) 
         st->counter_bytes = (size_t)4 * ((b + 7) / 8) * std::max(1, std::max(d, g.dec_ffn) / 256);
         TRY(A((void **)&st->counters, st->counter_bytes));
         CK(cudaMemsetAsync(st->counters, 0, st->counter_bytes, c->stream));
+        // split-K: the largest (rows x units) of the step's matrices, rows padded to 8
+        size_t pf = 0;
+        for (const DecLayer &L : c->dec)
+            for (const Matrix *M : {&L.qkv, &L.out, &L.cq, &L.co, &L.up, &L.down})
+                pf = std::max(pf, (size_t)M->Np * ((b + 7) / 8 * 8) * (M->type == T_Q8_0 ? M->nb : std::max(1, M->nsb)));
+        st->split.part_floats = pf;
+        TRY(A((void **)&st->split.part, 4 * pf));
+        TRY(A((void **)&st->split.count, 4 * 4096));
+        CK(cudaMemsetAsync(st->split.count, 0, 4 * 4096, c->stream));
     }
     *out = st.release();
     return MGB_OK;
@@ -1120,6 +1159,7 @@ static mgb_status launch_step_tc(mgb_ctx *c, StaticState *st, float *logits, int
     const Config &g = c->cfg;
     const int b = st->b, d = g.d, H = g.dec_heads, hd = d / H;
     QAct *X = &st->act, *Y = &st->act2;  // X: input of the next matmul in program order
+    const SplitBufs *sp = c->tc_split ? &st->split : nullptr;
     auto plain = [&](const float *x, int K) {
         PrepArgs p{};
         p.x = x;
@@ -1162,7 +1202,7 @@ static mgb_status launch_step_tc(mgb_ctx *c, StaticState *st, float *logits, int
     // attention that also quantizes its outputs for `next` when the shape allows
     auto attn_q = [&](AttnArgs aa, const Matrix &next, QAct *dst) -> mgb_status {
         const int G = act_group(next.type);
-        const bool ok = c->tc_post && tc_ok(next) && aa.queries == 1 && H % 4 == 0 && hd <= 128 &&
+        const bool ok = c->tc_attn_q && tc_ok(next) && aa.queries == 1 && H % 4 == 0 && hd <= 128 &&
                         (4 * hd) % (32 * G) == 0;
         if (ok) {
             aa.qo = *dst;
@@ -1196,7 +1236,7 @@ static mgb_status launch_step_tc(mgb_ctx *c, StaticState *st, float *logits, int
         gq.H = H;
         gq.hd = hd;
         gq.m = st->m;
-        TRY((gemm_tc<EPI_QKV, -1>(c, L.qkv, X, nullptr, b, gq)));
+        TRY((gemm_tc<EPI_QKV, -1>(c, L.qkv, X, nullptr, b, gq, nullptr, nullptr, sp)));
         AttnArgs sa{};
         sa.q = st->q;
         sa.q_row = d;
@@ -1220,12 +1260,12 @@ static mgb_status launch_step_tc(mgb_ctx *c, StaticState *st, float *logits, int
         GemvArgs go = gemv(L.out);
         go.y = st->x;
         bool posted = post_for(PREP_LN, L.out, &L.cross_norm, L.cq, Y, po);
-        TRY((gemm_tc<EPI_RESID, -1>(c, L.out, X, nullptr, b, go, nullptr, posted ? &po : nullptr)));
+        TRY((gemm_tc<EPI_RESID, -1>(c, L.out, X, nullptr, b, go, nullptr, posted ? &po : nullptr, sp)));
         if (!posted) TRY(prep(PREP_LN, st->x, d, &L.cross_norm, L.cq, Y));
         std::swap(X, Y);
         GemvArgs gc = gemv(L.cq);
         gc.y = st->q;
-        TRY((gemm_tc<EPI_STORE, -1>(c, L.cq, X, nullptr, b, gc)));
+        TRY((gemm_tc<EPI_STORE, -1>(c, L.cq, X, nullptr, b, gc, nullptr, nullptr, sp)));
         AttnArgs ca = sa;
         ca.K = st->ck[l];
         ca.V = st->cv[l];
@@ -1240,14 +1280,14 @@ static mgb_status launch_step_tc(mgb_ctx *c, StaticState *st, float *logits, int
         GemvArgs gco = gemv(L.co);
         gco.y = st->x;
         posted = post_for(PREP_LN, L.co, &L.ffn_norm, L.up, Y, po);
-        TRY((gemm_tc<EPI_RESID, -1>(c, L.co, X, nullptr, b, gco, nullptr, posted ? &po : nullptr)));
+        TRY((gemm_tc<EPI_RESID, -1>(c, L.co, X, nullptr, b, gco, nullptr, posted ? &po : nullptr, sp)));
         if (!posted) TRY(prep(PREP_LN, st->x, d, &L.ffn_norm, L.up, Y));
         std::swap(X, Y);
         // up + ReLU; post: the hidden layer per super-block for down
         GemvArgs gu = gemv(L.up);
         gu.y = st->u;
         posted = post_for(PREP_PLAIN, L.up, nullptr, L.down, Y, po);
-        TRY((gemm_tc<EPI_RELU, -1>(c, L.up, X, nullptr, b, gu, nullptr, posted ? &po : nullptr)));
+        TRY((gemm_tc<EPI_RELU, -1>(c, L.up, X, nullptr, b, gu, nullptr, posted ? &po : nullptr, sp)));
         if (!posted) TRY(prep(PREP_PLAIN, st->u, g.dec_ffn, nullptr, L.down, Y));
         std::swap(X, Y);
         // down + residual; post: the next layer's attn_norm(x), or dec_norm(x) for the LM head
@@ -1257,7 +1297,7 @@ static mgb_status launch_step_tc(mgb_ctx *c, StaticState *st, float *logits, int
         GemvArgs gd = gemv(L.down);
         gd.y = st->x;
         posted = post_for(PREP_LN, L.down, &nn, nm, Y, po);
-        TRY((gemm_tc<EPI_RESID, -1>(c, L.down, X, nullptr, b, gd, nullptr, posted ? &po : nullptr)));
+        TRY((gemm_tc<EPI_RESID, -1>(c, L.down, X, nullptr, b, gd, nullptr, posted ? &po : nullptr, sp)));
         if (!posted) TRY(prep(PREP_LN, st->x, d, &nn, nm, Y));
         std::swap(X, Y);
     }
@@ -1648,6 +1688,7 @@ static mgb_status acquire_state(mgb_ctx *c, const mgb_batch *B, int max_new, boo
     CK(cudaMemcpyAsync(st->lens, lens.data(), 4 * b, cudaMemcpyHostToDevice, c->stream));
     CK(cudaMemsetAsync(st->step, 0, 4, c->stream));
     if (st->counters) CK(cudaMemsetAsync(st->counters, 0, st->counter_bytes, c->stream));
+    if (st->split.count) CK(cudaMemsetAsync(st->split.count, 0, 4 * 4096, c->stream));
     TRY(set_ids(c, st, (uint32_t)g.start));
     TRY(reset_finished(c, st, n));
     *out = st;
@@ -1998,6 +2039,8 @@ mgb_status mgb_open(const char *path, int device, const mgb_options *opts, mgb_c
     if (const char *v = getenv("MGB_TC_MIN_ROWS")) c->tc_min_rows = std::max(1, atoi(v));
     if (const char *v = getenv("MGB_TC_FUSED")) c->tc_fused = atoi(v) != 0;
     if (const char *v = getenv("MGB_TC_POST")) c->tc_post = atoi(v) != 0;
+    if (const char *v = getenv("MGB_TC_ATTN_Q")) c->tc_attn_q = atoi(v) != 0;
+    if (const char *v = getenv("MGB_TC_SPLIT")) c->tc_split = atoi(v) != 0;
     cudaDeviceGetAttribute(&c->sms, cudaDevAttrMultiProcessorCount, device);
     if (c->sms <= 0) c->sms = 148;
     {

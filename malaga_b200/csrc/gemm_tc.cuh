@@ -149,6 +149,12 @@ struct Args {
     int tok0;        // first activation row (a multiple of 64) of this launch (TMA activations)
     GemvArgs g;      // epilogue outputs
     PrepArgs p;      // activation source (activations built in the kernel)
+    // split-K (TMA activations): `splits` CTAs share a tile's stages; split 0
+    // keeps the running row sum, the others store their unit partials in kpart,
+    // and the last of them (kcount) continues the sum in unit order
+    int splits;
+    float *kpart;
+    uint32_t *kcount;
     uint32_t *err;
 };
 
@@ -481,7 +487,9 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
     const int NS = (W.nb + 7) / 8;  // stages per tile (Q8_0: the last may hold fewer blocks)
     // tiles of this CTA: TMA activations walk all tiles; fused activations keep
     // one token tile per CTA (gridDim.x is then a multiple of tok_tiles)
-    const int tiles = A.row_tiles * A.tok_tiles;
+    const int splits = FX ? 1 : max(1, A.splits), NSS = NS / splits;  // stages per split
+    const int NU = G::Q8 ? W.nb : W.nsb;                                 // units of a row
+    const int tiles = A.row_tiles * A.tok_tiles * splits;
     const int my_tt = FX ? (int)blockIdx.x % A.tok_tiles : 0;
     const int first = FX ? (int)blockIdx.x / A.tok_tiles : (int)blockIdx.x;
     const int stride = FX ? (int)gridDim.x / A.tok_tiles : (int)gridDim.x;
@@ -549,7 +557,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
         return ok && !abort_sh;
     };
     auto tile_rt = [&](int k) { return FX ? first + k * stride : (first + k * stride) % A.row_tiles; };
-    auto tile_tt = [&](int k) { return FX ? my_tt : (first + k * stride) / A.row_tiles; };
+    auto tile_tt = [&](int k) { return FX ? my_tt : ((first + k * stride) / A.row_tiles) % A.tok_tiles; };
+    auto tile_s0 = [&](int k) { return FX ? 0 : (first + k * stride) / (A.row_tiles * A.tok_tiles) * NSS; };
 
     // Ring position: slot and phase parity, advanced by next().
     struct Pos {
@@ -569,7 +578,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
     if (warp == kProducerWarp) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
-            const int first_stages = my_tiles > 0 ? min(RS, NS) : 0;
+            const int first_stages = my_tiles > 0 ? min(RS, NSS) : 0;
             auto weights = [&](int rt, int s, uint8_t *dst, uint64_t *bar) {
                 const int g0 = 4 * rt;
                 tma3(dst, &A.m.w[0], 0, 8 * s, g0, bar);
@@ -592,13 +601,13 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
             // weights of the first stages do not depend on the previous kernel
             for (int s = 0; s < first_stages; ++s) {
                 mbar_expect_tx(&full[s], G::TX);
-                weights(tile_rt(0), s, ring + (size_t)s * G::STAGE, &full[s]);
+                weights(tile_rt(0), tile_s0(0) + s, ring + (size_t)s * G::STAGE, &full[s]);
             }
             pdl_wait();
             Pos st;
             for (int k = 0; k < my_tiles && !abort_sh; ++k) {
-                const int rt = tile_rt(k), tt = tile_tt(k);
-                for (int s = 0; s < NS; ++s, st.next(RS)) {
+                const int rt = tile_rt(k), tt = tile_tt(k), s0 = tile_s0(k);
+                for (int s = s0; s < s0 + NSS; ++s, st.next(RS)) {
                     uint8_t *dst = ring + (size_t)st.slot * G::STAGE;
                     if (st.n >= (uint32_t)first_stages) {
                         if (st.n >= (uint32_t)RS && !mbar_wait(&empty[st.slot], st.phase ^ 1)) {
@@ -619,7 +628,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
             Pos st, ag, tg;
             if (FX && my_tiles > 0 && !mbar_wait(&xready, 0)) fail(16u);
             for (int k = 0; k < my_tiles && !abort_sh; ++k) {
-                for (int s = 0; s < NS && !abort_sh; ++s, st.next(RS)) {
+                const int s0 = tile_s0(k);
+                for (int s = s0; s < s0 + NSS && !abort_sh; ++s, st.next(RS)) {
                     if (!mbar_wait(&full[st.slot], st.phase)) {
                         fail(16u);
                         break;
@@ -658,7 +668,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
         Pos st, ag;
         bool ok = true;
         for (int k = 0; k < my_tiles && ok && !abort_sh; ++k) {
-            for (int s = 0; s < NS && ok; ++s, st.next(RS)) {
+            const int s0 = tile_s0(k);
+            for (int s = s0; s < s0 + NSS && ok; ++s, st.next(RS)) {
                 if (!(ok = wwait(&full[st.slot], st.phase, 32u))) break;
                 const uint8_t *stg = ring + (size_t)st.slot * G::STAGE;
                 const int nbs = min(8, W.nb - 8 * s);
@@ -735,13 +746,15 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
         uint32_t ephase = 0;
         bool ok = true;
         for (int k = 0; k < my_tiles && ok && !abort_sh; ++k) {
-            const int rt = tile_rt(k), tt = tile_tt(k);
+            const int rt = tile_rt(k), tt = tile_tt(k), s0 = tile_s0(k);
             const int row = rt * 128 + r;
             const bool live = row < W.N;
+            // split-K partials of this tile: [unit][NT tokens][128 rows]
+            float *kp = splits > 1 ? A.kpart + (size_t)(tt * A.row_tiles + rt) * NU * NT * 128 : nullptr;
             float acc[NH];
 #pragma unroll
             for (int n = 0; n < NH; ++n) acc[n] = 0.0f;
-            for (int s = 0; s < NS && ok; ++s, st.next(RS)) {
+            for (int s = s0; s < s0 + NSS && ok; ++s, st.next(RS)) {
                 if (!(ok = wwait(&full[st.slot], st.phase, 64u))) break;
                 const uint8_t *stg = ring + (size_t)st.slot * G::STAGE;
                 // records of this stage's units: [unit][NT x RB]
@@ -833,7 +846,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
                             } else {
                                 const float xd = reinterpret_cast<const float *>(rec)[b * NT + n0 + n];
                                 const float p = __fmul_rn(__fmul_rn(db, xd), (float)I);
-                                acc[n] = (s == 0 && b == 0) ? p : __fadd_rn(acc[n], p);
+                                if (s0 == 0) acc[n] = (s == 0 && b == 0) ? p : __fadd_rn(acc[n], p);
+                                else kp[((size_t)(8 * s + b) * NT + n0 + n) * 128 + r] = p;
                             }
                         }
                     }
@@ -861,13 +875,46 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
                             const float xd = reinterpret_cast<const float *>(rec)[n0 + n];
                             p = __fmul_rn(__fmul_rn(d, xd), (float)S[n]);
                         }
-                        acc[n] = s == 0 ? p : __fadd_rn(acc[n], p);
+                        if (s0 == 0) acc[n] = s == 0 ? p : __fadd_rn(acc[n], p);
+                        else kp[((size_t)s * NT + n0 + n) * 128 + r] = p;
                     }
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[st.slot]);
             }
             if (!ok || abort_sh) break;
+            if (splits > 1) {
+                // split 0 leaves its running sum in unit slot 0 (a unit it summed itself)
+                if (s0 == 0)
+#pragma unroll
+                    for (int n = 0; n < NH; ++n) kp[(size_t)(n0 + n) * 128 + r] = acc[n];
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ebar);
+                if (!(ok = wwait(&ebar, ephase, 128u))) break;
+                ephase ^= 1;
+                if (tid == 0) {
+                    __threadfence();
+                    const uint32_t old = atomicAdd(&A.kcount[tt * A.row_tiles + rt], 1u);
+                    post_last = old + 1 == (uint32_t)splits;
+                    if (post_last) {
+                        A.kcount[tt * A.row_tiles + rt] = 0;  // every split of this launch has counted
+                        __threadfence();
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ebar);
+                if (!(ok = wwait(&ebar, ephase, 128u))) break;
+                ephase ^= 1;
+                if (!post_last) continue;  // another split finishes this tile
+                // the row sum continued in unit order from the stored partials
+                const int u1 = G::Q8 ? 8 * NSS : NSS;  // first unit of split 1
+#pragma unroll
+                for (int n = 0; n < NH; ++n) {
+                    float a = __ldcg(kp + (size_t)(n0 + n) * 128 + r);
+                    for (int u = u1; u < NU; ++u) a = __fadd_rn(a, __ldcg(kp + ((size_t)u * NT + n0 + n) * 128 + r));
+                    acc[n] = a;
+                }
+            }
             // tile epilogue
             if constexpr (EPI == EPI_ARGMAX) {
                 uint32_t bi[NH];
