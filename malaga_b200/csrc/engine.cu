@@ -298,6 +298,8 @@ struct mgb_ctx {
     int tc_attn_q = 1;
     // Matmuls with too few tiles for the SMs split their K stages (MGB_TC_SPLIT overrides).
     int tc_split = 1;
+    // Batches up to this many rows fold the attention into the next matmul (MGB_ATTN_FUSE_ROWS).
+    int attn_fuse_rows = 0;
     int sms = 148;  // multiprocessor count of the device (one tensor-core CTA each)
     void *enc_ws = nullptr;  // encoder temporaries (grown on demand)
     size_t enc_ws_bytes = 0;
@@ -696,7 +698,9 @@ static mgb_status fused_t(mgb_ctx *c, FusedArgs fa) {
     const int B = fa.g.rows;
     const bool f32 = TYPE == T_F32;
     if constexpr (TYPE != T_F32 && EPI != EPI_ARGMAX) {
-        const size_t sh = staged_bytes(TYPE, W.nb, W.nsb) + smact_bytes(B, W.K, false) + staged_partial_bytes(TYPE, B, W.nb);
+        size_t sh = staged_bytes(TYPE, W.nb, W.nsb) + smact_bytes(B, W.K, false) + staged_partial_bytes(TYPE, B, W.nb);
+        if (MODE == PREP_ATTN) sh += attn_prologue_bytes(fa.at.max_keys, fa.at.hd);
+        if (MODE == PREP_LN || MODE == PREP_EMBED_LN) sh += (size_t)8 * W.K;  // LayerNorm parameters
         if (B <= 8 && sh <= 200 * 1024) {
             auto kern = gemv_staged_kernel<TYPE, EPI, MODE>;
             cudaError_t e = allow_smem(kern, sh);
@@ -706,6 +710,9 @@ static mgb_status fused_t(mgb_ctx *c, FusedArgs fa) {
             return MGB_OK;
         }
     }
+    if constexpr (MODE == PREP_ATTN) {
+        return set_err(MGB_ERR_UNSUPPORTED, "attention prologue needs the staged matmul");
+    } else {
     const int NBv = B == 1 ? 1 : 8;
     int chunk = B;
     while (chunk > 1 && smact_bytes(chunk, W.K, f32) > 160 * 1024) chunk = (chunk + 1) / 2;
@@ -750,6 +757,7 @@ static mgb_status fused_t(mgb_ctx *c, FusedArgs fa) {
         if (e != cudaSuccess) return cuda_err(e, "fused matmul launch");
     }
     return MGB_OK;
+    }
 }
 
 template <int EPI, int MODE>
@@ -1124,6 +1132,18 @@ static mgb_status new_state(mgb_ctx *c, int b, int s, int m, StaticState **out) 
     return MGB_OK;
 }
 
+// Whether the small-batch out / cross-out matmul computes the attention itself
+// (prologue of the staged matmul: every CTA recomputes all heads of its rows,
+// which costs little at 1-2 rows and saves the attention launch).
+static bool attn_in_matmul(const mgb_ctx *c, const Matrix &W, int b, const AttnArgs &a) {
+    if (b > c->attn_fuse_rows || b >= c->tc_min_rows) return false;
+    if (W.type != T_Q8_0 && W.type != T_Q4_K && W.type != T_Q6_K) return false;
+    if (a.queries != 1 || (a.hd != 64 && a.hd != 128)) return false;
+    const size_t sh = staged_bytes(W.type, W.nb, W.nsb) + smact_bytes(b, W.K, false) +
+                      staged_partial_bytes(W.type, b, W.nb) + attn_prologue_bytes(a.max_keys, a.hd);
+    return sh <= 200 * 1024 && (size_t)b * W.K * 4 <= staged_partial_bytes(W.type, b, W.nb);
+}
+
 // One matmul of the step: from tc_min_rows rows the tcgen05 matmul, which
 // builds its LayerNorm / embedding / plain activations itself (rows of at most
 // 2048 values under LayerNorm, token tiles that fit in shared memory; others go
@@ -1131,6 +1151,7 @@ static mgb_status new_state(mgb_ctx *c, int b, int s, int m, StaticState **out) 
 template <int EPI, int MODE>
 static mgb_status step_op(mgb_ctx *c, StaticState *st, const FusedArgs &f, int *ctas = nullptr) {
     const int b = f.g.rows;
+    if constexpr (MODE == PREP_ATTN) return fused<EPI, MODE>(c, f);  // staged small-batch matmul only
     if (b >= c->tc_min_rows && tc_ok(f.g.W)) {
         PrepArgs p = f.p;
         p.rows = b;
@@ -1387,11 +1408,16 @@ static mgb_status launch_step(mgb_ctx *c, StaticState *st, float *logits, int fo
         sa.rows = b;
         sa.queries = 1;
         sa.max_keys = st->m;
-        TRY(attend<__half>(c, sa));
         FusedArgs fo = mm(L.out);
         fo.p = src(st->a, d, nullptr);
         fo.g.y = st->x;
-        TRY((step_op<EPI_RESID, PREP_PLAIN>(c, st, fo)));
+        if (attn_in_matmul(c, L.out, b, sa)) {
+            fo.at = sa;
+            TRY((step_op<EPI_RESID, PREP_ATTN>(c, st, fo)));
+        } else {
+            TRY(attend<__half>(c, sa));
+            TRY((step_op<EPI_RESID, PREP_PLAIN>(c, st, fo)));
+        }
         // cross_norm -> cross_q -> cross attention -> cross_out + residual
         FusedArgs fc = mm(L.cq);
         fc.p = src(st->x, d, &L.cross_norm);
@@ -1405,11 +1431,16 @@ static mgb_status launch_step(mgb_ctx *c, StaticState *st, float *logits, int fo
         ca.step = nullptr;
         ca.lens = st->lens;
         ca.max_keys = st->s;
-        TRY(attend<__half>(c, ca));
         FusedArgs fco = mm(L.co);
         fco.p = src(st->a, d, nullptr);
         fco.g.y = st->x;
-        TRY((step_op<EPI_RESID, PREP_PLAIN>(c, st, fco)));
+        if (attn_in_matmul(c, L.co, b, ca)) {
+            fco.at = ca;
+            TRY((step_op<EPI_RESID, PREP_ATTN>(c, st, fco)));
+        } else {
+            TRY(attend<__half>(c, ca));
+            TRY((step_op<EPI_RESID, PREP_PLAIN>(c, st, fco)));
+        }
         // ffn_norm -> up + ReLU -> down + residual
         FusedArgs fu = mm(L.up);
         fu.p = src(st->x, d, &L.ffn_norm);
@@ -2041,6 +2072,7 @@ mgb_status mgb_open(const char *path, int device, const mgb_options *opts, mgb_c
     if (const char *v = getenv("MGB_TC_POST")) c->tc_post = atoi(v) != 0;
     if (const char *v = getenv("MGB_TC_ATTN_Q")) c->tc_attn_q = atoi(v) != 0;
     if (const char *v = getenv("MGB_TC_SPLIT")) c->tc_split = atoi(v) != 0;
+    if (const char *v = getenv("MGB_ATTN_FUSE_ROWS")) c->attn_fuse_rows = atoi(v);
     cudaDeviceGetAttribute(&c->sms, cudaDevAttrMultiProcessorCount, device);
     if (c->sms <= 0) c->sms = 148;
     {

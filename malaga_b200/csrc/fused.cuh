@@ -22,7 +22,14 @@ struct FusedArgs {
     GemvArgs g;     // matrix, outputs and epilogue parameters
     PrepArgs p;     // activation source (x or a/u, LayerNorm, embedding)
     int rows_per_cta;  // row groups (of 32) per CTA
+    AttnArgs at;    // PREP_ATTN: the attention whose outputs are the input
 };
+
+// Shared memory of the attention prologue (PREP_ATTN): per warp the scores of
+// max_keys keys and a 64-key f16 V staging tile.
+__host__ __device__ inline size_t attn_prologue_bytes(int max_keys, int hd) {
+    return 16 + (size_t)8 * max_keys * 4 + (size_t)8 * 64 * hd * 2;  // (16: alignment of the scratch)
+}
 
 // Bytes per 32-row group of each region of the engine layout (see engine.h).
 __device__ __forceinline__ void region_group_bytes(const Matrix &W, size_t (&rb)[4]) {
@@ -123,12 +130,22 @@ __device__ void build_activations(const PrepArgs &p, const SmAct &s, int B, bool
     if constexpr (MODE != PREP_PLAIN) {
         if (xs) {
             const int K = p.K;
-            for (int idx = threadIdx.x; idx < B * K; idx += blockDim.x) {
-                const int r = idx / K, i = idx % K;
-                const float v = act_input<MODE>(p, r, i);
-                xs[idx] = v;
-                if constexpr (MODE == PREP_EMBED_LN)
-                    if (write_x) p.x_out[idx] = v;
+            // 8 loads in flight per thread before their stores (one memory round trip)
+            for (int base = threadIdx.x; base < B * K; base += 8 * blockDim.x) {
+                float v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const int idx = base + u * blockDim.x;
+                    v[u] = idx < B * K ? act_input<MODE>(p, idx / K, idx % K) : 0.0f;
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const int idx = base + u * blockDim.x;
+                    if (idx >= B * K) break;
+                    xs[idx] = v[u];
+                    if constexpr (MODE == PREP_EMBED_LN)
+                        if (write_x) p.x_out[idx] = v[u];
+                }
             }
             __syncthreads();
             PrepArgs q = p;
@@ -454,13 +471,27 @@ __global__ void __launch_bounds__(256) gemv_staged_kernel(FusedArgs fa, uint32_t
             p += rb[k];
         }
     }
+    const int B = g.rows;
+    // LayerNorm parameters (constant weights) into shared memory while the
+    // previous kernel finishes: after the partials (and any attention scratch)
+    float *gb = nullptr;
+    if constexpr (MODE == PREP_LN || MODE == PREP_EMBED_LN) {
+        gb = reinterpret_cast<float *>(sm_raw + wbytes + smact_bytes(B, W.K, false) + staged_partial_bytes(TYPE, B, W.nb));
+        for (int i = threadIdx.x; i < W.K; i += blockDim.x) {
+            gb[i] = __ldg(fa.p.gamma + i);
+            gb[W.K + i] = __ldg(fa.p.beta + i);
+        }
+    }
     pdl_launch_dependents();
     pdl_wait();
-    const int B = g.rows;
     const SmAct s = smact_carve(sm_raw + wbytes, B, W.K, false);
     float *P = reinterpret_cast<float *>(sm_raw + wbytes + smact_bytes(B, W.K, false));
     float *xs = MODE != PREP_PLAIN ? P : nullptr;  // input rows share the partials' space (used before them)
     PrepArgs pa = fa.p;
+    if (gb) {
+        pa.gamma = gb;
+        pa.beta = gb + W.K;
+    }
     if constexpr (MODE == PREP_EMBED_LN) {
         __shared__ uint32_t ids_sh[64];
         for (int r = threadIdx.x; r < B; r += blockDim.x) ids_sh[r] = pa.ids[r];
@@ -468,8 +499,39 @@ __global__ void __launch_bounds__(256) gemv_staged_kernel(FusedArgs fa, uint32_t
         pa.ids = ids_sh;
         __syncthreads();
     }
-    build_activations<MODE, act_group(TYPE)>(pa, s, B, blockIdx.x == 0,
-                                             (size_t)B * W.K * 4 <= staged_partial_bytes(TYPE, B, nb) ? xs : nullptr);
+    if constexpr (MODE == PREP_ATTN) {
+        // the attention outputs of the B rows (every head; one warp per (row, head),
+        // the attention kernel's arithmetic) into shared memory, then quantized
+        const AttnArgs &at = fa.at;
+        float *xa = reinterpret_cast<float *>(sm_raw + wbytes + smact_bytes(B, W.K, false));  // B x K (partials' space)
+        // scratch after the partials, 16-byte aligned (V rows are staged with 16-byte stores)
+        uint8_t *eb = reinterpret_cast<uint8_t *>(xa) + staged_partial_bytes(TYPE, B, nb);
+        float *esc = reinterpret_cast<float *>(eb + ((16 - (smem_u32(eb) & 15)) & 15));
+        float *e = esc + (size_t)warp * at.max_keys;
+        __half *vs = reinterpret_cast<__half *>(esc + (size_t)8 * at.max_keys) + (size_t)warp * 64 * at.hd;
+        for (int t = warp; t < B * at.H; t += 8) {
+            const int n = t / at.H, h = t % at.H;
+            bool live;
+            if (at.hd == 64) {
+                float res[2];
+                attend_one<__half, 64>(at, n, h, 0, e, vs, lane, res, live);
+                xa[(size_t)n * W.K + h * 64 + lane] = res[0];
+                xa[(size_t)n * W.K + h * 64 + 32 + lane] = res[1];
+            } else {
+                float res[4];
+                attend_one<__half, 128>(at, n, h, 0, e, vs, lane, res, live);
+#pragma unroll
+                for (int c = 0; c < 4; ++c) xa[(size_t)n * W.K + h * 128 + 32 * c + lane] = res[c];
+            }
+        }
+        __syncthreads();
+        PrepArgs q = pa;
+        q.x = xa;
+        build_activations_impl<PREP_PLAIN, act_group(TYPE)>(q, s, B, false);
+    } else {
+        build_activations<MODE, act_group(TYPE)>(pa, s, B, blockIdx.x == 0,
+                                                 (size_t)B * W.K * 4 <= staged_partial_bytes(TYPE, B, nb) ? xs : nullptr);
+    }
     if (!mbar_wait(&bar, 0)) {
         if (lane == 0) atomicOr(err, 1u);  // copy never completed: report, produce nothing
         return;

@@ -329,11 +329,11 @@ __device__ void fused_prologue(const PrepArgs &p, int rows, int tt, bool write_x
             for (int c = 0; c < UC; ++c) {
                 const int u = u0 + c;
                 if (u >= nu) break;
-                const float dd = __fdiv_rn(m[c], 127.0f);
+                const float dd = __fdiv_rn(m[c], 127.0f), id = __fdiv_rn(127.0f, m[c]);
 #pragma unroll
                 for (int g = 0; g < G; ++g) {
                     const int t = u * G + g;
-                    const int q = m[c] == 0.0f ? 0 : (int)roundf(__fdiv_rn(y[c][g], dd));
+                    const int q = m[c] == 0.0f ? 0 : (int)roundf(__fmul_rn(y[c][g], id));
                     xt[(size_t)t * NT * 32 + tile_off(n, lane >> 4) + (lane & 15)] = (uint8_t)(int8_t)q;
                 }
                 if (lane == 0) {
@@ -1030,10 +1030,21 @@ __global__ void __launch_bounds__(256) qprep_row_kernel(PrepArgs p, QAct out) {
         pa.ids = id_sh;
         __syncthreads();
     }
-    for (int i = threadIdx.x; i < K; i += blockDim.x) {
-        const float v = act_input<MODE>(pa, MODE == PREP_EMBED_LN ? 0 : r, i);
-        xs[i] = v;
-        if constexpr (MODE == PREP_EMBED_LN) p.x_out[(size_t)r * K + i] = v;
+    // 8 loads in flight per thread before their stores (one memory round trip)
+    for (int base = threadIdx.x; base < K; base += 8 * blockDim.x) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = base + u * blockDim.x;
+            v[u] = i < K ? act_input<MODE>(pa, MODE == PREP_EMBED_LN ? 0 : r, i) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = base + u * blockDim.x;
+            if (i >= K) break;
+            xs[i] = v[u];
+            if constexpr (MODE == PREP_EMBED_LN) p.x_out[(size_t)r * K + i] = v[u];
+        }
     }
     __syncthreads();
     PrepArgs q = p;

@@ -74,7 +74,7 @@ __device__ __forceinline__ float deq_elem(const Matrix &W, int row, int i) {
 // Activation preparation: one warp per row. Lane l owns elements l + 32 t, so
 // block t of the q8_1 activation is exactly "element t of every lane".
 
-enum PrepMode { PREP_PLAIN = 0, PREP_LN = 1, PREP_EMBED_LN = 2 };
+enum PrepMode { PREP_PLAIN = 0, PREP_LN = 1, PREP_EMBED_LN = 2, PREP_ATTN = 3 };
 
 struct PrepArgs {
     const float *x;       // input rows [rows][K] (PLAIN, LN)
@@ -100,8 +100,8 @@ struct PrepArgs {
 __host__ __device__ constexpr int act_group(int type) { return type == T_Q4_K || type == T_Q6_K ? 8 : 1; }
 
 // Quantizes G consecutive blocks (y[u] = element lane of block t0+u of `row`)
-// with one scale: d = amax/127 over the G*32 values, q = round(y/d). G = 1
-// stores the scale f16-rounded (q8_1 / Q8_0 style), G = 8 as f32 (Q8_K style).
+// with one scale: d = amax/127 over the G*32 values, q = round(y * (127/amax)).
+// G = 1 stores the scale f16-rounded (q8_1 / Q8_0 style), G = 8 as f32 (Q8_K).
 template <int G>
 __device__ __forceinline__ void quantize_group(const float (&y)[G], int8_t *q, float *d, int *s32, int *s16, int t0,
                                                int lane) {
@@ -109,11 +109,11 @@ __device__ __forceinline__ void quantize_group(const float (&y)[G], int8_t *q, f
 #pragma unroll
     for (int u = 1; u < G; ++u) m = fmaxf(m, fabsf(y[u]));
     const float amax = warp_max_nonneg(m);
-    const float dd = __fdiv_rn(amax, 127.0f);
+    const float dd = __fdiv_rn(amax, 127.0f), id = __fdiv_rn(127.0f, amax);
 #pragma unroll
     for (int u = 0; u < G; ++u) {
         const int t = t0 + u;
-        const int v = amax == 0.0f ? 0 : (int)roundf(__fdiv_rn(y[u], dd));
+        const int v = amax == 0.0f ? 0 : (int)roundf(__fmul_rn(y[u], id));
         q[32 * t + lane] = (int8_t)v;
         const int s = half_isum_redux(v, lane);          // this lane's 16-value half
         const int s_hi = __shfl_sync(0xffffffffu, s, 16);
@@ -472,13 +472,13 @@ __device__ __forceinline__ void store_unit(const QAct &o, int ctype, int tok, in
 #pragma unroll
     for (int g = 1; g < G; ++g) m = fmaxf(m, fabsf(y[g]));
     const float amax = warp_max_nonneg(m);
-    const float dd = __fdiv_rn(amax, 127.0f);
+    const float dd = __fdiv_rn(amax, 127.0f), id = __fdiv_rn(127.0f, amax);
     const int rs = o.rs;
     const bool sums = ctype == T_Q4_K && G == 8;  // only Q4_K records carry block sums
     int s32[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-        const int q = amax == 0.0f ? 0 : (int)roundf(__fdiv_rn(y[g], dd));
+        const int q = amax == 0.0f ? 0 : (int)roundf(__fmul_rn(y[g], id));
         o.tq[((size_t)(j0 + g) * (rs / 8) + (tok >> 3)) * 256 + tile_off(tok & 7, lane >> 4) + (lane & 15)] =
             (uint8_t)(int8_t)q;
         s32[g] = sums ? warp_isum_redux(q) : 0;
@@ -556,17 +556,15 @@ __device__ __forceinline__ void load_row(const float *p, float (&v)[HD]) {
 __device__ __forceinline__ float load_kv(const __half *p) { return __half2float(*p); }
 __device__ __forceinline__ float load_kv(const float *p) { return *p; }
 
+// One (row n, head h, query qi) of single-query attention by one warp: lane
+// `lane` gets the outputs of dims lane, lane+32, ... (res[c], valid when
+// live). e: the warp's max_keys floats of scores; vs: its staging tile of 64 V
+// rows. Scores by an FMA chain over the head dimension (one key per lane),
+// e = exp(s - max), the sum in SUM32 order, outputs by an FMA chain over keys
+// times 1/sum. Shared by the attention kernel and the fused matmul prologue.
 template <typename KV, int HD>
-__global__ void __launch_bounds__(128) attend_kernel(AttnArgs a) {
-    extern __shared__ float e_sh[];
-    pdl_launch_dependents();
-    pdl_wait();
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const long task = (long)blockIdx.x * 4 + warp;
-    const long total = (long)a.rows * a.H * a.queries;
-    if (task >= total) return;  // (never with qo: the host launches whole CTAs then)
-    const int qi = (int)(task % a.queries), h = (int)((task / a.queries) % a.H), n = (int)(task / ((long)a.queries * a.H));
-    float *e = e_sh + (size_t)warp * a.max_keys;
+__device__ __forceinline__ void attend_one(const AttnArgs &a, int n, int h, int qi, float *e, KV *vs, int lane,
+                                           float (&res)[HD >= 32 ? HD / 32 : 1], bool &live) {
     const int keys = a.lens ? (int)a.lens[n] : (int)(*a.step) + 1;
     const float *qp = a.q + (size_t)(n * (long)a.queries + qi) * a.q_row + h * HD;
     float q[HD];
@@ -574,7 +572,6 @@ __global__ void __launch_bounds__(128) attend_kernel(AttnArgs a) {
     for (int t = 0; t < HD; ++t) q[t] = qp[t];
     const KV *K = reinterpret_cast<const KV *>(a.K) + n * a.kv_batch + h * a.kv_head;
     const KV *V = reinterpret_cast<const KV *>(a.V) + n * a.kv_batch + h * a.kv_head;
-    // scores: FMA chain over the head dimension, one key per lane
     float mx = kNegInf;
     for (int j = lane; j < keys; j += 32) {
         float k[HD];
@@ -594,15 +591,12 @@ __global__ void __launch_bounds__(128) attend_kernel(AttnArgs a) {
     }
     const float inv = __fdiv_rn(1.0f, warp_tree(s));
     __syncwarp();
-    // outputs: FMA chain over keys; lane owns dims lane, lane+32, ... V rows are
-    // staged in shared memory 64 keys at a time (one memory round trip per chunk).
     constexpr int PER = HD >= 32 ? HD / 32 : 1;
     constexpr int KC = 64, VEC = 16 / sizeof(KV);  // keys per chunk, elements per 16-byte load
-    KV *vs = reinterpret_cast<KV *>(e_sh + (size_t)4 * a.max_keys) + (size_t)warp * KC * HD;
     float acc[PER];
 #pragma unroll
     for (int c = 0; c < PER; ++c) acc[c] = 0.0f;
-    const bool live = HD >= 32 || lane < HD;
+    live = HD >= 32 || lane < HD;
     for (int j0 = 0; j0 < keys; j0 += KC) {
         const int nk = min(KC, keys - j0);
         for (int u = lane; u < nk * (HD / VEC); u += 32) {
@@ -618,17 +612,37 @@ __global__ void __launch_bounds__(128) attend_kernel(AttnArgs a) {
                     acc[c] = __fmaf_rn(e[j0 + jj], load_kv(vs + (size_t)jj * HD + lane + 32 * c), acc[c]);
         __syncwarp();
     }
+#pragma unroll
+    for (int c = 0; c < PER; ++c) res[c] = __fmul_rn(acc[c], inv);
+}
+
+template <typename KV, int HD>
+__global__ void __launch_bounds__(128) attend_kernel(AttnArgs a) {
+    extern __shared__ float e_sh[];
+    pdl_launch_dependents();
+    pdl_wait();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const long task = (long)blockIdx.x * 4 + warp;
+    const long total = (long)a.rows * a.H * a.queries;
+    if (task >= total) return;  // (never with qo: the host launches whole CTAs then)
+    const int qi = (int)(task % a.queries), h = (int)((task / a.queries) % a.H), n = (int)(task / ((long)a.queries * a.H));
+    constexpr int PER = HD >= 32 ? HD / 32 : 1;
+    constexpr int KC = 64;
+    KV *vs = reinterpret_cast<KV *>(e_sh + (size_t)4 * a.max_keys) + (size_t)warp * KC * HD;
+    float res[PER];
+    bool live;
+    attend_one<KV, HD>(a, n, h, qi, e_sh + (size_t)warp * a.max_keys, vs, lane, res, live);
     if (live) {
         float *o = a.out + (size_t)(n * (long)a.queries + qi) * a.out_row + h * HD;
 #pragma unroll
-        for (int c = 0; c < PER; ++c) o[lane + 32 * c] = __fmul_rn(acc[c], inv);
+        for (int c = 0; c < PER; ++c) o[lane + 32 * c] = res[c];
     }
     if (a.qo.tq) {
         // the CTA's 4 heads (4*HD consecutive values of row n) as units of the consumer
         __shared__ float ov[4 * 128];
         if (live)
 #pragma unroll
-            for (int c = 0; c < PER; ++c) ov[warp * HD + lane + 32 * c] = __fmul_rn(acc[c], inv);
+            for (int c = 0; c < PER; ++c) ov[warp * HD + lane + 32 * c] = res[c];
         __syncthreads();
         const int j0 = (h - warp) * HD / 32;  // first block of the CTA's values
         if (a.qo_ctype == T_Q4_K || a.qo_ctype == T_Q6_K) {

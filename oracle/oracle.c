@@ -435,7 +435,8 @@ typedef struct {
 /* group = 1: blocks of 32 values with an f16-rounded scale (q8_1 / Q8_0 style,
  * consumed by Q8_0 weights). group = 8: one f32 scale per 256-value
  * super-block (Q8_K style, consumed by Q4_K and Q6_K weights, as candle's
- * k-quant vec_dot does). Both: d = amax/127, q = round(v/d), q = 0 if amax = 0. */
+ * k-quant vec_dot does). Both: d = amax/127 (the scale), q = round(v * (127/amax))
+ * (one reciprocal per group, as ggml's Q8_K quantizer), q = 0 if amax = 0. */
 static void quantize_act(const float *x, int rows, int K, int group, qact_t *out) {
     int nb = K / 32, gv = 32 * group;
     for (int r = 0; r < rows; ++r) {
@@ -443,9 +444,9 @@ static void quantize_act(const float *x, int rows, int K, int group, qact_t *out
             const float *v = x + (size_t)r * K + (size_t)gv * u;
             float amax = 0.0f;
             for (int i = 0; i < gv; ++i) amax = fmaxf(amax, fabsf(v[i]));
-            float dd = amax / 127.0f;
+            float dd = amax / 127.0f, id = 127.0f / amax;
             for (int i = 0; i < gv; ++i)
-                out->q[(size_t)r * K + (size_t)gv * u + i] = amax == 0.0f ? 0 : (int8_t)roundf(v[i] / dd);
+                out->q[(size_t)r * K + (size_t)gv * u + i] = amax == 0.0f ? 0 : (int8_t)roundf(v[i] * id);
             for (int j = 0; j < group; ++j) out->d[(size_t)r * nb + group * u + j] = group == 1 ? rnd_h(dd) : dd;
         }
     }

@@ -241,3 +241,17 @@ def test_beam_one_equals_greedy_on_device(gpu, model):
     eng = Engine(path)
     out, lens = eng.beam(eng.encode(src), TINY_TGT, 1, 16)
     assert [[int(x) for x in out[i, : lens[i]]] for i in range(len(src))] == greedy
+
+
+@pytest.mark.parametrize("preset,n", [("q4_k_m", 1), ("q8_0", 2)])
+def test_attention_in_matmul_prologue_bit_exact(gpu, model, preset, n):
+    """At 1-2 rows the out / cross-out matmuls compute the attention in their
+    prologue (no attention launch): logits still equal the oracle's bit for bit."""
+    path = model("mid", preset)
+    V = models.config_of("mid").vocab_size
+    src = mid_sentences(V, n=n, seed=21)
+    want_ids, want_logits = oracle.Oracle(path).greedy(src, V - 2, 6, force=True, logits=True)
+    eng = Engine(path)
+    got_ids, got_logits = eng.greedy_logits(eng.encode(src), V - 2, 6, force=True)
+    np.testing.assert_array_equal(got_ids, want_ids)
+    assert np.array_equal(got_logits.view(np.uint32), want_logits.view(np.uint32))
