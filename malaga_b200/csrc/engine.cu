@@ -286,6 +286,7 @@ struct mgb_ctx {
     // Activation rows from which matmuls run on the tensor cores (tcgen05)
     // instead of the small-batch kernels; MGB_TC_MIN_ROWS overrides (tests).
     int tc_min_rows = 16;
+    int tc_min_nt = 8;  // narrowest token tile (MGB_TC_MIN_NT)
     // Decode-step tensor-core matmuls build their activations in the kernel
     // (1) or read them from qprep_row_kernel (0); MGB_TC_FUSED overrides.
     int tc_fused = 0;
@@ -849,10 +850,12 @@ static size_t tc_smem(int type, int nt, bool fused, int nb) {
 // widest tile that still gives every SM a tile (and, for activations built in
 // the kernel, whose resident activations fit in shared memory); persistent
 // CTAs, one per SM. Fused launches give each token tile the same number of CTAs.
-static bool tc_shape(const Matrix &W, int rows, int sms, bool fused, size_t smem_limit, int &nt, int &grid) {
+static bool tc_shape(const Matrix &W, int rows, int sms, bool fused, size_t smem_limit, int min_nt, int &nt,
+                     int &grid) {
     const int row_tiles = W.Np / 128;
     nt = 0;
     for (int cand : {64, 32, 16, 8}) {
+        if (cand < min_nt && nt) break;
         if (fused && tc_smem(W.type, cand, true, W.nb) > smem_limit) continue;
         nt = cand;  // narrower tiles until every SM has one (or the narrowest that fits)
         if ((long)row_tiles * ((rows + cand - 1) / cand) >= sms) break;
@@ -1001,7 +1004,7 @@ static mgb_status gemm_tc(mgb_ctx *c, const Matrix &W, const QAct *act, const Pr
             if (a.p.x) a.p.x += (size_t)t0 * W.K;
         }
         int nt, grid;
-        if (!tc_shape(W, n, c->sms, XM >= 0, c->smem_optin, nt, grid))
+        if (!tc_shape(W, n, c->sms, XM >= 0, c->smem_optin, c->tc_min_nt, nt, grid))
             return set_err(MGB_ERR_UNSUPPORTED, "no tensor-core tile fits a %d-value row", W.K);
         if (EPI == EPI_ARGMAX) {
             if (a.g.logits) a.g.logits += (size_t)t0 * W.N;
@@ -1158,7 +1161,8 @@ static mgb_status step_op(mgb_ctx *c, StaticState *st, const FusedArgs &f, int *
         p.K = f.g.W.K;
         int nt, grid;
         if (c->tc_fused && (MODE == PREP_PLAIN || f.g.W.K <= 2048) &&
-            tc_shape(f.g.W, std::min(b, EPI == EPI_ARGMAX ? 64 : b), c->sms, true, c->smem_optin, nt, grid))
+            tc_shape(f.g.W, std::min(b, EPI == EPI_ARGMAX ? 64 : b), c->sms, true, c->smem_optin, c->tc_min_nt, nt,
+                     grid))
             return gemm_tc<EPI, MODE>(c, f.g.W, nullptr, &p, b, f.g, ctas);
         if (!st->act.tq) return set_err(MGB_ERR_INVALID, "tensor-core activation buffers missing");
         TRY(qprep_row<MODE>(c, p, st->act, f.g.W));
@@ -2068,6 +2072,7 @@ mgb_status mgb_open(const char *path, int device, const mgb_options *opts, mgb_c
     else mgb_default_options(&c->opts);
     CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
     if (const char *v = getenv("MGB_TC_MIN_ROWS")) c->tc_min_rows = std::max(1, atoi(v));
+    if (const char *v = getenv("MGB_TC_MIN_NT")) c->tc_min_nt = atoi(v);
     if (const char *v = getenv("MGB_TC_FUSED")) c->tc_fused = atoi(v) != 0;
     if (const char *v = getenv("MGB_TC_POST")) c->tc_post = atoi(v) != 0;
     if (const char *v = getenv("MGB_TC_ATTN_Q")) c->tc_attn_q = atoi(v) != 0;

@@ -399,18 +399,32 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
                  : "memory");
 }
 
-// One try_wait with a suspend-time hint: a thread whose phase is not complete
-// sleeps until it completes (or the hint runs out) instead of spinning, so
-// waiting warps do not take issue slots from working ones.
+// One try_wait: a thread whose phase is not complete may sleep until it
+// completes (or a time limit runs out: MGB_WAIT_HINT_NS when nonzero, else the
+// hardware's own) instead of spinning, so waiting warps do not take issue
+// slots from working ones.
+#ifndef MGB_WAIT_HINT_NS
+#define MGB_WAIT_HINT_NS 0
+#endif
 __device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
     uint32_t done;
+#if MGB_WAIT_HINT_NS > 0
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(done)
-        : "r"(a), "r"(parity), "r"(20000u)
+        : "r"(a), "r"(parity), "r"((uint32_t)MGB_WAIT_HINT_NS)
         : "memory");
+#else
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+#endif
     return done != 0;
 }
 

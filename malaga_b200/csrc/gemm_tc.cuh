@@ -15,8 +15,9 @@
 //   warp 10     producer: one TMA tensor copy per weight region (and, when the
 //               activations come from global memory, one for their tiles and
 //               one for their scale records) into a ring of RS stages;
-//   warps 8-9   converters: thread t unpacks weight rows t and t+64 of each
-//               block (Q4_K nibbles, Q6_K 6-bit values minus 32, Q8_0 bytes)
+//   warps EW-9  converters (EW = 4 for tiles of at most 16 tokens, else 8):
+//               they unpack each block's 128 weight rows (Q4_K nibbles, Q6_K
+//               6-bit values minus 32, Q8_0 bytes), loads batched ahead of stores,
 //               into int8 128x32 tiles in the canonical no-swizzle layout (ring
 //               of AG groups); Q6_K gets two tiles per block, each with the
 //               other 16-value half zeroed, since the halves carry different
@@ -25,8 +26,9 @@
 //               columns (ring of TG groups), one commit per group to the
 //               barriers that free the tiles and wake the epilogue, one per
 //               stage to free the stage;
-//   warps 0-7   epilogue: warp w reads TMEM lanes 32(w%4).. (its weight rows)
-//               for half of the tile's tokens, accumulates, and stores.
+//   warps 0..EW-1 epilogue: warp w reads TMEM lanes 32(w%4).. (its weight
+//               rows) for all (EW = 4) or half (EW = 8) of the tile's tokens,
+//               accumulates, and stores.
 // (12 warps: three per scheduler leave 168 registers per thread.)
 // Activations either arrive by TMA in the layout qprep_row_kernel writes (XM <
 // 0: the encoder's long inputs), or (XM = a PrepMode: the decode step) the
@@ -158,11 +160,25 @@ struct Args {
     uint32_t *err;
 };
 
+// N of the MMA instruction: at least MGB_MMA_MIN_N (16, the smallest N of an
+// M = 128 tcgen05.mma); a narrower token tile (NT = 8) is read twice (the
+// descriptor's 8-row stride is 0), and the duplicate columns are not read.
+#ifndef MGB_MMA_MIN_N
+#define MGB_MMA_MIN_N 16
+#endif
+template <int NT>
+struct MmaN {
+    static constexpr int N = NT < MGB_MMA_MIN_N ? MGB_MMA_MIN_N : NT;
+    static constexpr uint32_t SBO = NT < N ? 0u : 256u;  // B: bytes between 8-row core groups
+    static_assert(N == NT || NT == 8, "narrow tile");
+};
+
 // Stage geometry per weight type, tile width and activation source.
 template <int TYPE, int NT, bool FX>
 struct Geo {
     static constexpr bool Q6 = TYPE == T_Q6_K, Q4 = TYPE == T_Q4_K, Q8 = TYPE == T_Q8_0;
-    static constexpr int COLS = Q6 ? 2 * NT : NT;   // TMEM columns per block
+    static constexpr int MN = MmaN<NT>::N;            // MMA columns per block (half)
+    static constexpr int COLS = Q6 ? 2 * MN : MN;   // TMEM columns per block
     static constexpr int ABYTES = Q6 ? 8192 : 4096;  // converted tile(s) of one block
     static constexpr int KB = 8;                     // blocks per stage
     static constexpr int WA = Q8 ? 4 * KB * 1024 : 4 * KB * 512;                   // q / qs / ql
@@ -199,7 +215,16 @@ struct Geo {
 };
 
 constexpr int kThreads = 384;  // 12 warps
-constexpr int kConvWarp = 8, kProducerWarp = 10, kMmaWarp = 11;
+constexpr int kProducerWarp = 10, kMmaWarp = 11;
+// Epilogue warps 0..EW-1 and converter warps EW..9: narrow tiles (NT <= 16)
+// leave the epilogue little to do per block, so four warps take all the tile's
+// tokens and six convert; wider tiles split their tokens over eight epilogue
+// warps and convert with two.
+template <int NT>
+struct Roles {
+    static constexpr int EW = NT <= 16 ? 4 : 8;
+    static constexpr int CW = kProducerWarp - EW;
+};
 
 // Resident activation bytes of a fused launch: tiles of every block, then the
 // scale records of every unit.
@@ -471,8 +496,9 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
     constexpr bool FX = XM >= 0;
     using G = Geo<TYPE, NT, FX>;
     constexpr int RS = G::RS, AG = G::AG, TG = G::TG, BG = G::BG, COLS = G::COLS;
-    constexpr int NH = NT / 2;  // tokens per epilogue warp
-    constexpr uint32_t IDESC = idesc_i8(128, NT);
+    constexpr int EW = Roles<NT>::EW, CW = Roles<NT>::CW;
+    constexpr int NH = NT * 4 / EW;  // tokens per epilogue warp
+    constexpr uint32_t IDESC = idesc_i8(128, G::MN);
     extern __shared__ __align__(16) uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t full[RS], empty[RS], afull[AG], aempty[AG], tfull[TG], tempty[TG], fin, xready,
         ebar;
@@ -504,19 +530,19 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
     if (tid == 0) {
         for (int i = 0; i < RS; ++i) {
             mbar_init(&full[i], 1);
-            mbar_init(&empty[i], 2 + 1 + 8);
+            mbar_init(&empty[i], CW + 1 + EW);
         }
         for (int i = 0; i < AG; ++i) {
-            mbar_init(&afull[i], 2);
+            mbar_init(&afull[i], CW);
             mbar_init(&aempty[i], 1);
         }
         for (int i = 0; i < TG; ++i) {
             mbar_init(&tfull[i], 1);
-            mbar_init(&tempty[i], 8);
+            mbar_init(&tempty[i], EW);
         }
         mbar_init(&fin, 1);
-        mbar_init(&xready, 8);
-        mbar_init(&ebar, 8);
+        mbar_init(&xready, EW);
+        mbar_init(&ebar, EW);
         abort_sh = 0;
     }
     if (EPI == EPI_ARGMAX)
@@ -647,10 +673,10 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
                         const uint8_t *at = atile + (size_t)ag.slot * G::AGB;
                         const uint32_t td = tmem + tg.slot * G::GCOLS;
                         for (int b = 0; b < group_blocks(g, nbs); ++b) {
-                            const uint64_t db = sdesc(xq + (g * BG + b) * NT * 32, 128, 256);
+                            const uint64_t db = sdesc(xq + (g * BG + b) * NT * 32, 128, MmaN<NT>::SBO);
                             mma_i8(td + b * COLS, sdesc(at + b * G::ABYTES, 128, 256), db, IDESC);
                             if constexpr (G::Q6)
-                                mma_i8(td + b * COLS + NT, sdesc(at + b * G::ABYTES + 4096, 128, 256), db, IDESC);
+                                mma_i8(td + b * COLS + G::MN, sdesc(at + b * G::ABYTES + 4096, 128, 256), db, IDESC);
                         }
                         commit(&aempty[ag.slot]);
                         commit(&tfull[tg.slot]);
@@ -662,9 +688,17 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
             commit(&fin);
             if (!mbar_wait(&fin, 0)) fail(16u);
         }
-    } else if (warp >= kConvWarp) {
+    } else if (warp >= EW) {
         // ---------------------------------------------------------- converters
-        const int r0 = tid - 32 * kConvWarp;  // weight rows r0 and r0 + 64 of the tile
+        // items of a group: (weight row r, block bb) = (i % 128, i / 128) for
+        // i = ct, ct + CT, ...; a warp's 32 items are 32 consecutive rows of one
+        // block. Each batch of LB items is loaded before any of it is stored.
+        constexpr int CT = 32 * CW, IPT = (128 * BG + CT - 1) / CT, LB = IPT < 8 ? IPT : 8;
+        const int ct = tid - 32 * EW;
+        struct Raw {
+            int4 a;
+            int4 b;  // Q8_0: bytes 16-31; Q6_K: high bits in b.x, b.y
+        };
         Pos st, ag;
         bool ok = true;
         for (int k = 0; k < my_tiles && ok && !abort_sh; ++k) {
@@ -675,36 +709,56 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
                 const int nbs = min(8, W.nb - 8 * s);
                 for (int g = 0; g * BG < nbs; ++g, ag.next(AG)) {
                     if (ag.n >= (uint32_t)AG && !(ok = wwait(&aempty[ag.slot], ag.phase ^ 1, 32u))) break;
-                    for (int bb = 0; bb < group_blocks(g, nbs); ++bb) {
-                        const int b = g * BG + bb;
-                        uint8_t *ta = atile + (size_t)ag.slot * G::AGB + bb * G::ABYTES;
+                    const int items = 128 * group_blocks(g, nbs);
+                    uint8_t *tg0 = atile + (size_t)ag.slot * G::AGB;
 #pragma unroll
-                        for (int half = 0; half < 2; ++half) {
-                            const int r = r0 + 64 * half, gi = r >> 5, l = r & 31;
+                    for (int k0 = 0; k0 < IPT; k0 += LB) {
+                        Raw raw[LB];
+#pragma unroll
+                        for (int u = 0; u < LB; ++u) {
+                            const int i = ct + (k0 + u) * CT;
+                            if (k0 + u >= IPT || i >= items) break;
+                            const int r = i & 127, b = g * BG + (i >> 7), gi = r >> 5, l = r & 31;
                             if constexpr (G::Q8) {
                                 const int4 *src = reinterpret_cast<const int4 *>(stg + (gi * 8 + b) * 1024 + l * 32);
-                                *reinterpret_cast<int4 *>(ta + tile_off(r, 0)) = src[0];
-                                *reinterpret_cast<int4 *>(ta + tile_off(r, 1)) = src[1];
+                                raw[u].a = src[0];
+                                raw[u].b = src[1];
                             } else if constexpr (G::Q4) {
-                                const int4 v = *reinterpret_cast<const int4 *>(stg + (gi * 8 + b) * 512 + l * 16);
+                                raw[u].a = *reinterpret_cast<const int4 *>(stg + (gi * 8 + b) * 512 + l * 16);
+                            } else {
+                                raw[u].a = *reinterpret_cast<const int4 *>(stg + (gi * 8 + b) * 512 + l * 16);
+                                const uint2 hq = *reinterpret_cast<const uint2 *>(stg + G::oB + (gi * 8 + b) * 256 + l * 8);
+                                raw[u].b.x = (int)hq.x;
+                                raw[u].b.y = (int)hq.y;
+                            }
+                        }
+#pragma unroll
+                        for (int u = 0; u < LB; ++u) {
+                            const int i = ct + (k0 + u) * CT;
+                            if (k0 + u >= IPT || i >= items) break;
+                            const int r = i & 127;
+                            uint8_t *ta = tg0 + (i >> 7) * G::ABYTES;
+                            const int4 v = raw[u].a;
+                            if constexpr (G::Q8) {
+                                *reinterpret_cast<int4 *>(ta + tile_off(r, 0)) = v;
+                                *reinterpret_cast<int4 *>(ta + tile_off(r, 1)) = raw[u].b;
+                            } else if constexpr (G::Q4) {
                                 *reinterpret_cast<int4 *>(ta + tile_off(r, 0)) =
                                     make_int4(v.x & 0x0f0f0f0f, v.y & 0x0f0f0f0f, v.z & 0x0f0f0f0f, v.w & 0x0f0f0f0f);
                                 *reinterpret_cast<int4 *>(ta + tile_off(r, 1)) =
                                     make_int4((v.x >> 4) & 0x0f0f0f0f, (v.y >> 4) & 0x0f0f0f0f,
                                               (v.z >> 4) & 0x0f0f0f0f, (v.w >> 4) & 0x0f0f0f0f);
                             } else {
-                                const int4 lq = *reinterpret_cast<const int4 *>(stg + (gi * 8 + b) * 512 + l * 16);
-                                const uint2 hq =
-                                    *reinterpret_cast<const uint2 *>(stg + G::oB + (gi * 8 + b) * 256 + l * 8);
-                                const int ql[4] = {lq.x, lq.y, lq.z, lq.w};
+                                const uint32_t hx = (uint32_t)raw[u].b.x, hy = (uint32_t)raw[u].b.y;
+                                const int ql[4] = {v.x, v.y, v.z, v.w};
                                 int a4[4], b4[4];
 #pragma unroll
-                                for (int i = 0; i < 4; ++i) {
-                                    a4[i] = (int)__vsub4(
-                                        (uint32_t)((ql[i] & 0x0f0f0f0f) | (int)(((hq.x >> (2 * i)) & 0x03030303u) << 4)),
+                                for (int e = 0; e < 4; ++e) {
+                                    a4[e] = (int)__vsub4(
+                                        (uint32_t)((ql[e] & 0x0f0f0f0f) | (int)(((hx >> (2 * e)) & 0x03030303u) << 4)),
                                         0x20202020u);
-                                    b4[i] = (int)__vsub4((uint32_t)(((ql[i] >> 4) & 0x0f0f0f0f) |
-                                                                    (int)(((hq.y >> (2 * i)) & 0x03030303u) << 4)),
+                                    b4[e] = (int)__vsub4((uint32_t)(((ql[e] >> 4) & 0x0f0f0f0f) |
+                                                                    (int)(((hy >> (2 * e)) & 0x03030303u) << 4)),
                                                          0x20202020u);
                                 }
                                 // tile 0: values 0-15 (k16 = 0), tile 1: values 16-31 (k16 = 1)
@@ -732,10 +786,10 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
         if constexpr (FX) {
             // this CTA's token tile, built once; the first row tile writes x (embedding)
             if (my_tiles > 0) {
-                fused_prologue<TYPE, NT, (FX ? XM : 0)>(A.p, A.rows, my_tt, first == 0, xt, xr, warp, 8, lane);
+                fused_prologue<TYPE, NT, (FX ? XM : 0)>(A.p, A.rows, my_tt, first == 0, xt, xr, warp, EW, lane);
                 if constexpr (G::Q4) {
-                    asm volatile("bar.sync 1, 256;" ::: "memory");  // the 8 epilogue warps
-                    fused_block_sums<NT>(W.nb, min(NT, A.rows - my_tt * NT), xt, xr, tid, 256);
+                    asm volatile("bar.sync 1, %0;" ::"r"(32 * EW) : "memory");  // the epilogue warps
+                    fused_block_sums<NT>(W.nb, min(NT, A.rows - my_tt * NT), xt, xr, tid, 32 * EW);
                 }
             }
             fence_async_smem();
@@ -754,6 +808,17 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
             float acc[NH];
 #pragma unroll
             for (int n = 0; n < NH; ++n) acc[n] = 0.0f;
+            // RESID: the residual rows and bias of this tile, read while the
+            // tile's stages are still in flight (no other CTA writes them)
+            float res[EPI == EPI_RESID ? NH : 1], bias = 0.0f;
+            if constexpr (EPI == EPI_RESID) {
+                if (live && W.bias) bias = __ldg(W.bias + row);
+#pragma unroll
+                for (int n = 0; n < NH; ++n) {
+                    const int tok = tt * NT + n0 + n;
+                    res[n] = live && tok < A.rows ? __ldcg(A.g.y + (size_t)tok * W.N + row) : 0.0f;
+                }
+            }
             for (int s = s0; s < s0 + NSS && ok; ++s, st.next(RS)) {
                 if (!(ok = wwait(&full[st.slot], st.phase, 64u))) break;
                 const uint8_t *stg = ring + (size_t)st.slot * G::STAGE;
@@ -820,14 +885,14 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
                     auto ld = [&](int c, int (&a)[CH], int (&bv)[CH]) {
                         if constexpr (CH == 16) {
                             tmem_ld16(ta + c * CH, a);
-                            if constexpr (G::Q6) tmem_ld16(ta + NT + c * CH, bv);
+                            if constexpr (G::Q6) tmem_ld16(ta + G::MN + c * CH, bv);
                         } else if constexpr (CH == 8) {
                             tmem_ld8(ta + c * CH, a);
-                            if constexpr (G::Q6) tmem_ld8(ta + NT + c * CH, bv);
+                            if constexpr (G::Q6) tmem_ld8(ta + G::MN + c * CH, bv);
                         } else {
                             static_assert(CH == 4, "token chunk");
                             tmem_ld4(ta + c * CH, a);
-                            if constexpr (G::Q6) tmem_ld4(ta + NT + c * CH, bv);
+                            if constexpr (G::Q6) tmem_ld4(ta + G::MN + c * CH, bv);
                         }
                     };
                     ld(0, va[0], vb[0]);
@@ -936,7 +1001,11 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
                 for (int n = 0; n < NH; ++n) {
                     const int tok = tt * NT + n0 + n;
                     if (tok >= A.rows) break;  // uniform across the warp
-                    if (live) epilogue_store<EPI>(A.g, row, tok, acc[n]);
+                    if constexpr (EPI == EPI_RESID) {
+                        if (live) A.g.y[(size_t)tok * W.N + row] = __fadd_rn(__fadd_rn(acc[n], bias), res[n]);
+                    } else if (live) {
+                        epilogue_store<EPI>(A.g, row, tok, acc[n]);
+                    }
                 }
                 if constexpr (EPI == EPI_RESID || EPI == EPI_RELU) {
                     if (A.post.mode >= 0) {
@@ -966,11 +1035,11 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
                         if (post_last) {
                             const int t0 = tt * NT, t1 = min(A.rows, t0 + NT);
                             if (ln) {
-                                if (A.post.group == 8) post_ln<8>(A.post, A.g.y, W.N, t0, t1, warp, 8, lane);
-                                else post_ln<1>(A.post, A.g.y, W.N, t0, t1, warp, 8, lane);
+                                if (A.post.group == 8) post_ln<8>(A.post, A.g.y, W.N, t0, t1, warp, EW, lane);
+                                else post_ln<1>(A.post, A.g.y, W.N, t0, t1, warp, EW, lane);
                             } else {
-                                if (A.post.group == 8) post_plain<8>(A.post, A.g.y, W.N, rt / 2, t0, t1, warp, 8, lane);
-                                else post_plain<1>(A.post, A.g.y, W.N, rt / 2, t0, t1, warp, 8, lane);
+                                if (A.post.group == 8) post_plain<8>(A.post, A.g.y, W.N, rt / 2, t0, t1, warp, EW, lane);
+                                else post_plain<1>(A.post, A.g.y, W.N, rt / 2, t0, t1, warp, EW, lane);
                             }
                         }
                     }
