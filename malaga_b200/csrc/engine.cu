@@ -299,6 +299,8 @@ struct mgb_ctx {
     int tc_attn_q = 1;
     // Matmuls with too few tiles for the SMs split their K stages (MGB_TC_SPLIT overrides).
     int tc_split = 1;
+    int tc_split_stages = 4;  // fewest stages per split (MGB_TC_SPLIT_STAGES)
+    int tc_split_max = 4;     // most splits of a tile (MGB_TC_SPLIT_MAX)
     // Batches up to this many rows fold the attention into the next matmul (MGB_ATTN_FUSE_ROWS).
     int attn_fuse_rows = 0;
     int sms = 148;  // multiprocessor count of the device (one tensor-core CTA each)
@@ -814,7 +816,8 @@ static mgb_status qprep_row(mgb_ctx *c, PrepArgs p, const QAct &act, const Matri
     auto kern = qprep_row_kernel<MODE>;
     p.group = act_group(W.type);
     p.ctype = W.type;
-    const size_t sh = (size_t)p.K * 5 + (size_t)(p.K / 32) * 16;
+    // row, bytes, block scales and sums; LayerNorm parameters for LN modes
+    const size_t sh = (size_t)p.K * 5 + (size_t)(p.K / 32) * 16 + (MODE != PREP_PLAIN ? (size_t)p.K * 8 : 0);
     cudaError_t e = allow_smem(kern, sh);
     if (e == cudaSuccess) e = launch_pdl(kern, dim3(p.rows), dim3(256), sh, c->stream, p, act);
     ++c->launches;
@@ -854,11 +857,27 @@ static bool tc_shape(const Matrix &W, int rows, int sms, bool fused, size_t smem
                      int &grid) {
     const int row_tiles = W.Np / 128;
     nt = 0;
-    for (int cand : {64, 32, 16, 8}) {
-        if (cand < min_nt && nt) break;
-        if (fused && tc_smem(W.type, cand, true, W.nb) > smem_limit) continue;
-        nt = cand;  // narrower tiles until every SM has one (or the narrowest that fits)
-        if ((long)row_tiles * ((rows + cand - 1) / cand) >= sms) break;
+    if (fused) {
+        // one token tile per CTA: narrower tiles until every SM has one (or the
+        // narrowest whose activations fit)
+        for (int cand : {64, 32, 16, 8}) {
+            if (cand < min_nt && nt) break;
+            if (tc_smem(W.type, cand, true, W.nb) > smem_limit) continue;
+            nt = cand;
+            if ((long)row_tiles * ((rows + cand - 1) / cand) >= sms) break;
+        }
+    } else {
+        // the token tile (of at least min_nt rows) that needs the fewest waves
+        // of tiles over the SMs; on a tie the narrowest, whose tiles finish soonest
+        long best = 0;
+        for (int cand : {8, 16, 32, 64}) {
+            if (cand < min_nt && cand != 64) continue;
+            const long waves = ((long)row_tiles * ((rows + cand - 1) / cand) + sms - 1) / sms;
+            if (!nt || waves < best) {
+                nt = cand;
+                best = waves;
+            }
+        }
     }
     if (!nt) return false;
     const int tok_tiles = (rows + nt - 1) / nt;
@@ -1018,9 +1037,9 @@ static mgb_status gemm_tc(mgb_ctx *c, const Matrix &W, const QAct *act, const Pr
             // too few tiles for the SMs: split the stages (2 or 4 ways) if they divide
             const int tiles = a.row_tiles * a.tok_tiles, ns = (W.nb + 7) / 8;
             const int nu = W.type == T_Q8_0 ? W.nb : W.nsb;
-            // (each split keeps 4+ stages: below that the fixup costs more than the parallelism gains)
-            while (a.splits < 4 && tiles * a.splits * 2 <= c->sms && ns % (a.splits * 2) == 0 &&
-                   ns / (a.splits * 2) >= 4)
+            // (each split keeps tc_split_stages or more stages)
+            while (a.splits * 2 <= c->tc_split_max && tiles * a.splits * 2 <= c->sms && ns % (a.splits * 2) == 0 &&
+                   ns / (a.splits * 2) >= c->tc_split_stages)
                 a.splits *= 2;
             if (a.splits > 1 && (size_t)a.tok_tiles * nt * W.Np * nu > split->part_floats) a.splits = 1;
             if (a.splits > 1) {
@@ -1121,11 +1140,11 @@ static mgb_status new_state(mgb_ctx *c, int b, int s, int m, StaticState **out) 
         st->counter_bytes = (size_t)4 * ((b + 7) / 8) * std::max(1, std::max(d, g.dec_ffn) / 256);
         TRY(A((void **)&st->counters, st->counter_bytes));
         CK(cudaMemsetAsync(st->counters, 0, st->counter_bytes, c->stream));
-        // split-K: the largest (rows x units) of the step's matrices, rows padded to 8
+        // split-K: the largest (rows x units) of the step's matrices, rows padded to 64
         size_t pf = 0;
         for (const DecLayer &L : c->dec)
             for (const Matrix *M : {&L.qkv, &L.out, &L.cq, &L.co, &L.up, &L.down})
-                pf = std::max(pf, (size_t)M->Np * ((b + 7) / 8 * 8) * (M->type == T_Q8_0 ? M->nb : std::max(1, M->nsb)));
+                pf = std::max(pf, (size_t)M->Np * ((b + 63) / 64 * 64) * (M->type == T_Q8_0 ? M->nb : std::max(1, M->nsb)));
         st->split.part_floats = pf;
         TRY(A((void **)&st->split.part, 4 * pf));
         TRY(A((void **)&st->split.count, 4 * 4096));
@@ -2077,6 +2096,8 @@ mgb_status mgb_open(const char *path, int device, const mgb_options *opts, mgb_c
     if (const char *v = getenv("MGB_TC_POST")) c->tc_post = atoi(v) != 0;
     if (const char *v = getenv("MGB_TC_ATTN_Q")) c->tc_attn_q = atoi(v) != 0;
     if (const char *v = getenv("MGB_TC_SPLIT")) c->tc_split = atoi(v) != 0;
+    if (const char *v = getenv("MGB_TC_SPLIT_STAGES")) c->tc_split_stages = std::max(1, atoi(v));
+    if (const char *v = getenv("MGB_TC_SPLIT_MAX")) c->tc_split_max = std::max(1, atoi(v));
     if (const char *v = getenv("MGB_ATTN_FUSE_ROWS")) c->attn_fuse_rows = atoi(v);
     cudaDeviceGetAttribute(&c->sms, cudaDevAttrMultiProcessorCount, device);
     if (c->sms <= 0) c->sms = 148;

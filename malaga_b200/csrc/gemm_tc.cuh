@@ -652,6 +652,11 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
         // ----------------------------------------------------------------- MMA
         if (lane == 0) {
             Pos st, ag, tg;
+            // Descriptors are formed once and advanced by constant 16-byte
+            // steps (shared-memory offsets stay below 256 KB, so the 14-bit
+            // address field never carries): the issue loop is the MMAs alone.
+            const uint64_t a_base = sdesc(atile, 128, 256);
+            const uint64_t x_base = sdesc(FX ? xt : ring + G::oXQ, 128, MmaN<NT>::SBO);
             if (FX && my_tiles > 0 && !mbar_wait(&xready, 0)) fail(16u);
             for (int k = 0; k < my_tiles && !abort_sh; ++k) {
                 const int s0 = tile_s0(k);
@@ -660,7 +665,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
                         fail(16u);
                         break;
                     }
-                    const uint8_t *xq = FX ? xt + (size_t)8 * s * NT * 32 : ring + (size_t)st.slot * G::STAGE + G::oXQ;
+                    const uint64_t xs =
+                        x_base + (uint64_t)(FX ? (8 * s * NT * 32) >> 4 : (st.slot * G::STAGE) >> 4);
                     const int nbs = min(8, W.nb - 8 * s);
                     for (int g = 0; g * BG < nbs; ++g, ag.next(AG), tg.next(TG)) {
                         if (!mbar_wait(&afull[ag.slot], ag.phase) ||
@@ -670,13 +676,17 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
                         }
                         if (abort_sh) break;
                         fence_after();
-                        const uint8_t *at = atile + (size_t)ag.slot * G::AGB;
+                        const uint64_t ag0 = a_base + (uint64_t)((ag.slot * G::AGB) >> 4);
+                        const uint64_t xg0 = xs + (uint64_t)((g * BG * NT * 32) >> 4);
                         const uint32_t td = tmem + tg.slot * G::GCOLS;
-                        for (int b = 0; b < group_blocks(g, nbs); ++b) {
-                            const uint64_t db = sdesc(xq + (g * BG + b) * NT * 32, 128, MmaN<NT>::SBO);
-                            mma_i8(td + b * COLS, sdesc(at + b * G::ABYTES, 128, 256), db, IDESC);
+                        const int gb = group_blocks(g, nbs);
+#pragma unroll
+                        for (int b = 0; b < BG; ++b) {
+                            if (b >= gb) break;
+                            const uint64_t db = xg0 + (uint64_t)((b * NT * 32) >> 4);
+                            mma_i8(td + b * COLS, ag0 + (uint64_t)((b * G::ABYTES) >> 4), db, IDESC);
                             if constexpr (G::Q6)
-                                mma_i8(td + b * COLS + G::MN, sdesc(at + b * G::ABYTES + 4096, 128, 256), db, IDESC);
+                                mma_i8(td + b * COLS + G::MN, ag0 + (uint64_t)((b * G::ABYTES + 4096) >> 4), db, IDESC);
                         }
                         commit(&aempty[ag.slot]);
                         commit(&tfull[tg.slot]);
@@ -971,13 +981,25 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
                 if (!(ok = wwait(&ebar, ephase, 128u))) break;
                 ephase ^= 1;
                 if (!post_last) continue;  // another split finishes this tile
-                // the row sum continued in unit order from the stored partials
+                // the row sum continued in unit order from the stored partials,
+                // UB units x NH tokens of loads in flight per batch
                 const int u1 = G::Q8 ? 8 * NSS : NSS;  // first unit of split 1
+                constexpr int UB = NH <= 8 ? 8 : (NH <= 16 ? 4 : 2);
 #pragma unroll
-                for (int n = 0; n < NH; ++n) {
-                    float a = __ldcg(kp + (size_t)(n0 + n) * 128 + r);
-                    for (int u = u1; u < NU; ++u) a = __fadd_rn(a, __ldcg(kp + ((size_t)u * NT + n0 + n) * 128 + r));
-                    acc[n] = a;
+                for (int n = 0; n < NH; ++n) acc[n] = __ldcg(kp + (size_t)(n0 + n) * 128 + r);
+                for (int u0 = u1; u0 < NU; u0 += UB) {
+                    float v[UB][NH];
+#pragma unroll
+                    for (int j = 0; j < UB; ++j)
+#pragma unroll
+                        for (int n = 0; n < NH; ++n)
+                            v[j][n] = u0 + j < NU ? __ldcg(kp + ((size_t)(u0 + j) * NT + n0 + n) * 128 + r) : 0.0f;
+#pragma unroll
+                    for (int j = 0; j < UB; ++j) {
+                        if (u0 + j >= NU) break;
+#pragma unroll
+                        for (int n = 0; n < NH; ++n) acc[n] = __fadd_rn(acc[n], v[j][n]);
+                    }
                 }
             }
             // tile epilogue
@@ -1081,9 +1103,18 @@ __global__ void __launch_bounds__(256) qprep_row_kernel(PrepArgs p, QAct out) {
     extern __shared__ __align__(16) uint8_t qsm[];
     __shared__ float st[2];
     __shared__ uint32_t id_sh[1];
+    const int r = blockIdx.x, K = p.K, nb = K >> 5;
+    // LayerNorm parameters into shared memory before the dependency wait (they
+    // are weights, not the predecessor's output)
+    float *gb = reinterpret_cast<float *>(qsm + (size_t)K * 5 + (size_t)nb * 16);  // gamma[K], beta[K]
+    if constexpr (MODE != PREP_PLAIN) {
+        for (int i = threadIdx.x; i < K / 4; i += blockDim.x) {
+            reinterpret_cast<float4 *>(gb)[i] = __ldg(reinterpret_cast<const float4 *>(p.gamma) + i);
+            reinterpret_cast<float4 *>(gb + K)[i] = __ldg(reinterpret_cast<const float4 *>(p.beta) + i);
+        }
+    }
     pdl_launch_dependents();
     pdl_wait();
-    const int r = blockIdx.x, K = p.K, nb = K >> 5;
     float *xs = reinterpret_cast<float *>(qsm);                 // K floats
     SmAct s;
     s.q = reinterpret_cast<int8_t *>(qsm + (size_t)K * 4);      // K bytes
@@ -1119,6 +1150,10 @@ __global__ void __launch_bounds__(256) qprep_row_kernel(PrepArgs p, QAct out) {
     PrepArgs q = p;
     q.x = xs;
     q.rows = 1;
+    if constexpr (MODE != PREP_PLAIN) {
+        q.gamma = gb;
+        q.beta = gb + K;
+    }
     constexpr int M2 = MODE == PREP_PLAIN ? PREP_PLAIN : PREP_LN;
     if (p.group == 8) build_activations_impl<M2, 8>(q, s, 1, false);
     else build_activations_impl<M2, 1>(q, s, 1, false);

@@ -556,10 +556,26 @@ __device__ __forceinline__ void load_row(const float *p, float (&v)[HD]) {
 __device__ __forceinline__ float load_kv(const __half *p) { return __half2float(*p); }
 __device__ __forceinline__ float load_kv(const float *p) { return *p; }
 
+// Element t of a K/V row held as raw 16-byte words.
+template <typename KV, int RW>
+__device__ __forceinline__ float kv_at(const uint4 (&r)[RW], int t) {
+    if constexpr (sizeof(KV) == 2) return __half2float(reinterpret_cast<const __half *>(r)[t]);
+    else return reinterpret_cast<const float *>(r)[t];
+}
+
+// 16 bytes global -> shared without registers (completion by cp_async_wait).
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 // One (row n, head h, query qi) of single-query attention by one warp: lane
 // `lane` gets the outputs of dims lane, lane+32, ... (res[c], valid when
 // live). e: the warp's max_keys floats of scores; vs: its staging tile of 64 V
-// rows. Scores by an FMA chain over the head dimension (one key per lane),
+// rows (filled by cp.async while the scores run). Scores by an FMA chain over
+// the head dimension (keys lane and lane+32 of each round of 64 side by side),
 // e = exp(s - max), the sum in SUM32 order, outputs by an FMA chain over keys
 // times 1/sum. Shared by the attention kernel and the fused matmul prologue.
 template <typename KV, int HD>
@@ -567,22 +583,47 @@ __device__ __forceinline__ void attend_one(const AttnArgs &a, int n, int h, int 
                                            float (&res)[HD >= 32 ? HD / 32 : 1], bool &live) {
     const int keys = a.lens ? (int)a.lens[n] : (int)(*a.step) + 1;
     const float *qp = a.q + (size_t)(n * (long)a.queries + qi) * a.q_row + h * HD;
+    const KV *K = reinterpret_cast<const KV *>(a.K) + n * a.kv_batch + h * a.kv_head;
+    const KV *V = reinterpret_cast<const KV *>(a.V) + n * a.kv_batch + h * a.kv_head;
+    constexpr int KC = 64, VEC = 16 / sizeof(KV), RW = HD / VEC;  // keys per chunk; 16-byte words per row
+    // the first chunk of V rows is copied into shared memory while the scores run
+    auto stage_v = [&](int j0, int nk) {
+        for (int u = lane; u < nk * RW; u += 32)
+            cp_async16(vs + (size_t)u * VEC, V + (size_t)(j0 + u / RW) * a.kv_row + (u % RW) * VEC);
+        cp_async_commit();
+    };
+    stage_v(0, min(KC, keys));
     float q[HD];
 #pragma unroll
     for (int t = 0; t < HD; ++t) q[t] = qp[t];
-    const KV *K = reinterpret_cast<const KV *>(a.K) + n * a.kv_batch + h * a.kv_head;
-    const KV *V = reinterpret_cast<const KV *>(a.V) + n * a.kv_batch + h * a.kv_head;
+    // scores: keys j0 + lane and j0 + 32 + lane per round, both rows loaded
+    // before either FMA chain (each chain in head-dimension order)
     float mx = kNegInf;
-    for (int j = lane; j < keys; j += 32) {
-        float k[HD];
-        load_row<HD>(K + (size_t)j * a.kv_row, k);
-        float acc = 0.0f;
+    for (int j0 = 0; j0 < keys; j0 += 64) {
+        const int ja = j0 + lane, jb = j0 + 32 + lane;
+        uint4 ra[RW], rb[RW];
 #pragma unroll
-        for (int t = 0; t < HD; ++t) acc = __fmaf_rn(q[t], k[t], acc);
-        e[j] = acc;
-        mx = fmaxf(mx, acc);
+        for (int c = 0; c < RW; ++c) {
+            ra[c] = ja < keys ? __ldg(reinterpret_cast<const uint4 *>(K + (size_t)ja * a.kv_row) + c) : make_uint4(0, 0, 0, 0);
+            rb[c] = jb < keys ? __ldg(reinterpret_cast<const uint4 *>(K + (size_t)jb * a.kv_row) + c) : make_uint4(0, 0, 0, 0);
+        }
+        float sa = 0.0f, sb = 0.0f;
+#pragma unroll
+        for (int t = 0; t < HD; ++t) {
+            sa = __fmaf_rn(q[t], kv_at<KV, RW>(ra, t), sa);
+            sb = __fmaf_rn(q[t], kv_at<KV, RW>(rb, t), sb);
+        }
+        if (ja < keys) {
+            e[ja] = sa;
+            mx = fmaxf(mx, sa);
+        }
+        if (jb < keys) {
+            e[jb] = sb;
+            mx = fmaxf(mx, sb);
+        }
     }
     mx = warp_max(mx);
+    __syncwarp();
     float s = 0.0f;
     for (int j = lane; j < keys; j += 32) {
         const float ex = mgb_exp(__fsub_rn(e[j], mx));
@@ -590,20 +631,15 @@ __device__ __forceinline__ void attend_one(const AttnArgs &a, int n, int h, int 
         s = j == lane ? ex : __fadd_rn(s, ex);
     }
     const float inv = __fdiv_rn(1.0f, warp_tree(s));
-    __syncwarp();
     constexpr int PER = HD >= 32 ? HD / 32 : 1;
-    constexpr int KC = 64, VEC = 16 / sizeof(KV);  // keys per chunk, elements per 16-byte load
     float acc[PER];
 #pragma unroll
     for (int c = 0; c < PER; ++c) acc[c] = 0.0f;
     live = HD >= 32 || lane < HD;
     for (int j0 = 0; j0 < keys; j0 += KC) {
         const int nk = min(KC, keys - j0);
-        for (int u = lane; u < nk * (HD / VEC); u += 32) {
-            const int jr = u / (HD / VEC), cc = u % (HD / VEC);
-            reinterpret_cast<uint4 *>(vs)[u] =
-                __ldg(reinterpret_cast<const uint4 *>(V + (size_t)(j0 + jr) * a.kv_row) + cc);
-        }
+        if (j0 > 0) stage_v(j0, nk);
+        cp_async_wait();
         __syncwarp();
         if (live)
             for (int jj = 0; jj < nk; ++jj)
