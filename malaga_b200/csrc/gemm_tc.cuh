@@ -793,6 +793,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
         const int r = 32 * q + lane, gi = q, l = lane;
         const int n0 = e * NH;  // first token (within the tile) of this warp
         pdl_wait();
+        // the decode step (QKV cache position), written by the previous step's kernels
+        const int qkv_step = EPI == EPI_QKV ? (int)*A.g.step : 0;
         if constexpr (FX) {
             // this CTA's token tile, built once; the first row tile writes x (embedding)
             if (my_tiles > 0) {
@@ -818,15 +820,31 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
             float acc[NH];
 #pragma unroll
             for (int n = 0; n < NH; ++n) acc[n] = 0.0f;
-            // RESID: the residual rows and bias of this tile, read while the
-            // tile's stages are still in flight (no other CTA writes them)
-            float res[EPI == EPI_RESID ? NH : 1], bias = 0.0f;
+            // This row's bias (and for RESID the tile's residual values) read
+            // while the tile's stages are still in flight, so the stores below
+            // wait on no load (no other CTA writes these residual values)
+            const float bias = live && W.bias ? __ldg(W.bias + row) : 0.0f;
+            float res[EPI == EPI_RESID ? NH : 1];
             if constexpr (EPI == EPI_RESID) {
-                if (live && W.bias) bias = __ldg(W.bias + row);
 #pragma unroll
                 for (int n = 0; n < NH; ++n) {
                     const int tok = tt * NT + n0 + n;
                     res[n] = live && tok < A.rows ? __ldcg(A.g.y + (size_t)tok * W.N + row) : 0.0f;
+                }
+            }
+            // QKV: q row, or this row's place in the step's K or V cache entry
+            float *qkv_q = nullptr;
+            __half *qkv_c = nullptr;
+            size_t qkv_tok = 0;
+            if constexpr (EPI == EPI_QKV) {
+                const int dm = A.g.H * A.g.hd;
+                if (row < dm) {
+                    qkv_q = A.g.q + row;
+                    qkv_tok = dm;
+                } else if (live) {
+                    const int c = row - dm, which = c / dm, h = (c % dm) / A.g.hd, t = c % A.g.hd;
+                    qkv_c = (which == 0 ? A.g.kc : A.g.vc) + ((size_t)h * A.g.m + qkv_step) * A.g.hd + t;
+                    qkv_tok = (size_t)A.g.H * A.g.m * A.g.hd;
                 }
             }
             for (int s = s0; s < s0 + NSS && ok; ++s, st.next(RS)) {
@@ -1023,9 +1041,19 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
                 for (int n = 0; n < NH; ++n) {
                     const int tok = tt * NT + n0 + n;
                     if (tok >= A.rows) break;  // uniform across the warp
+                    if (!live) continue;
                     if constexpr (EPI == EPI_RESID) {
-                        if (live) A.g.y[(size_t)tok * W.N + row] = __fadd_rn(__fadd_rn(acc[n], bias), res[n]);
-                    } else if (live) {
+                        A.g.y[(size_t)tok * W.N + row] = __fadd_rn(__fadd_rn(acc[n], bias), res[n]);
+                    } else if constexpr (EPI == EPI_STORE) {
+                        A.g.y[(size_t)tok * W.N + row] = W.bias ? __fadd_rn(acc[n], bias) : acc[n];
+                    } else if constexpr (EPI == EPI_RELU) {
+                        const float y = __fadd_rn(acc[n], bias);
+                        A.g.y[(size_t)tok * W.N + row] = y > 0.0f ? y : 0.0f;
+                    } else if constexpr (EPI == EPI_QKV) {
+                        const float y = __fadd_rn(acc[n], bias);
+                        if (qkv_q) qkv_q[tok * qkv_tok] = y;
+                        else qkv_c[tok * qkv_tok] = __float2half_rn(y);
+                    } else {
                         epilogue_store<EPI>(A.g, row, tok, acc[n]);
                     }
                 }
