@@ -1220,7 +1220,7 @@ static mgb_status launch_step_tc(mgb_ctx *c, StaticState *st, float *logits, int
     // post step of a matmul whose output (rows of width W.N) feeds `next`
     auto post_for = [&](int mode, const Matrix &W, const Norm *nrm, const Matrix &next, QAct *dst, tc::Post &po) {
         po = tc::Post{};
-        if (!c->tc_post || !tc_ok(next)) return false;
+        if (!MGB_TC_POST_STEPS || !c->tc_post || !tc_ok(next)) return false;
         if (mode == PREP_LN && W.N > 2048) return false;
         if (mode == PREP_PLAIN && (W.N % 256 || (W.Np / 128) % 2)) return false;
         po.mode = mode;

@@ -132,7 +132,12 @@ struct Maps {
 // finished output rows, once every row tile of a token tile is done (the last
 // CTA of the token tile, found with an atomic counter); mode PREP_PLAIN = the
 // output quantized per 256-row super-block, once both row tiles of it are done.
-// mode < 0: none.
+// mode < 0: none. Compiled only with MGB_TC_POST_STEPS=1: the decode step
+// measured slower with them, and their registers make the RESID / RELU
+// epilogues spill.
+#ifndef MGB_TC_POST_STEPS
+#define MGB_TC_POST_STEPS 0
+#endif
 struct Post {
     int mode = -1;
     const float *gamma = nullptr, *beta = nullptr;
@@ -650,6 +655,9 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
         }
     } else if (warp == kMmaWarp) {
         // ----------------------------------------------------------------- MMA
+        // (nothing to do before the predecessor's outputs exist: waiting here
+        // keeps this warp off the issue slots of the predecessor's warps)
+        if constexpr (!FX) pdl_wait();
         if (lane == 0) {
             Pos st, ag, tg;
             // Descriptors are formed once and advanced by constant 16-byte
@@ -700,6 +708,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
         }
     } else if (warp >= EW) {
         // ---------------------------------------------------------- converters
+        if constexpr (!FX) pdl_wait();  // (as the MMA warp)
         // items of a group: (weight row r, block bb) = (i % 128, i / 128) for
         // i = ct, ct + CT, ...; a warp's 32 items are 32 consecutive rows of one
         // block. Each batch of LB items is loaded before any of it is stored.
@@ -1057,7 +1066,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
                         epilogue_store<EPI>(A.g, row, tok, acc[n]);
                     }
                 }
-                if constexpr (EPI == EPI_RESID || EPI == EPI_RELU) {
+                if constexpr (MGB_TC_POST_STEPS && (EPI == EPI_RESID || EPI == EPI_RELU)) {
                     if (A.post.mode >= 0) {
                         // the tile's outputs are stored; count it, and the CTA that
                         // completes a token tile (LN) / super-block (PLAIN) prepares it
