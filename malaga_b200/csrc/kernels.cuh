@@ -587,17 +587,29 @@ __device__ __forceinline__ void attend_one(const AttnArgs &a, int n, int h, int 
     const KV *V = reinterpret_cast<const KV *>(a.V) + n * a.kv_batch + h * a.kv_head;
     constexpr int KC = 64, VEC = 16 / sizeof(KV), RW = HD / VEC;  // keys per chunk; 16-byte words per row
     // the first chunk of V rows is copied into shared memory while the scores run
+    // (requested right after the first round of K rows)
     auto stage_v = [&](int j0, int nk) {
         for (int u = lane; u < nk * RW; u += 32)
             cp_async16(vs + (size_t)u * VEC, V + (size_t)(j0 + u / RW) * a.kv_row + (u % RW) * VEC);
         cp_async_commit();
     };
-    stage_v(0, min(KC, keys));
     float q[HD];
+    if (HD % 4 == 0 && (a.q_row & 3) == 0) {
 #pragma unroll
-    for (int t = 0; t < HD; ++t) q[t] = qp[t];
+        for (int t = 0; t < HD / 4; ++t) {
+            const float4 v = reinterpret_cast<const float4 *>(qp)[t];
+            q[4 * t] = v.x;
+            q[4 * t + 1] = v.y;
+            q[4 * t + 2] = v.z;
+            q[4 * t + 3] = v.w;
+        }
+    } else {
+#pragma unroll
+        for (int t = 0; t < HD; ++t) q[t] = qp[t];
+    }
     // scores: keys j0 + lane and j0 + 32 + lane per round, both rows loaded
-    // before either FMA chain (each chain in head-dimension order)
+    // before either FMA chain (each chain in head-dimension order); the first
+    // round's rows are requested before the V rows
     float mx = kNegInf;
     for (int j0 = 0; j0 < keys; j0 += 64) {
         const int ja = j0 + lane, jb = j0 + 32 + lane;
@@ -607,6 +619,7 @@ __device__ __forceinline__ void attend_one(const AttnArgs &a, int n, int h, int 
             ra[c] = ja < keys ? __ldg(reinterpret_cast<const uint4 *>(K + (size_t)ja * a.kv_row) + c) : make_uint4(0, 0, 0, 0);
             rb[c] = jb < keys ? __ldg(reinterpret_cast<const uint4 *>(K + (size_t)jb * a.kv_row) + c) : make_uint4(0, 0, 0, 0);
         }
+        if (j0 == 0) stage_v(0, min(KC, keys));
         float sa = 0.0f, sb = 0.0f;
 #pragma unroll
         for (int t = 0; t < HD; ++t) {
