@@ -684,11 +684,13 @@ static mgb_status attend(mgb_ctx *c, AttnArgs a) {
         if (e != cudaSuccess) return cuda_err(e, "attention launch");
         return MGB_OK;
     };
+    // single-query attention of a small decode batch releases the next kernel late
+    const bool late = a.queries == 1 && a.rows < c->tc_min_rows;
     switch (a.hd) {
-        case 16: return go(attend_kernel<KV, 16>);
-        case 32: return go(attend_kernel<KV, 32>);
-        case 64: return go(attend_kernel<KV, 64>);
-        case 128: return go(attend_kernel<KV, 128>);
+        case 16: return late ? go(attend_kernel<KV, 16, true>) : go(attend_kernel<KV, 16, false>);
+        case 32: return late ? go(attend_kernel<KV, 32, true>) : go(attend_kernel<KV, 32, false>);
+        case 64: return late ? go(attend_kernel<KV, 64, true>) : go(attend_kernel<KV, 64, false>);
+        case 128: return late ? go(attend_kernel<KV, 128, true>) : go(attend_kernel<KV, 128, false>);
     }
     return set_err(MGB_ERR_UNSUPPORTED, "head dimension %d", a.hd);
 }

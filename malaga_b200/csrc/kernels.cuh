@@ -665,10 +665,12 @@ __device__ __forceinline__ void attend_one(const AttnArgs &a, int n, int h, int 
     for (int c = 0; c < PER; ++c) res[c] = __fmul_rn(acc[c], inv);
 }
 
-template <typename KV, int HD>
+// LATE: the next kernel is released after this one's attention rather than at
+// its start (small decode batches: measured faster at batch 1, slower at 64).
+template <typename KV, int HD, bool LATE>
 __global__ void __launch_bounds__(128) attend_kernel(AttnArgs a) {
     extern __shared__ float e_sh[];
-    pdl_launch_dependents();
+    if constexpr (!LATE) pdl_launch_dependents();
     pdl_wait();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const long task = (long)blockIdx.x * 4 + warp;
@@ -681,6 +683,7 @@ __global__ void __launch_bounds__(128) attend_kernel(AttnArgs a) {
     float res[PER];
     bool live;
     attend_one<KV, HD>(a, n, h, qi, e_sh + (size_t)warp * a.max_keys, vs, lane, res, live);
+    if constexpr (LATE) pdl_launch_dependents();
     if (live) {
         float *o = a.out + (size_t)(n * (long)a.queries + qi) * a.out_row + h * HD;
 #pragma unroll
