@@ -110,18 +110,27 @@ __device__ __forceinline__ void quantize_group(const float (&y)[G], int8_t *q, f
     for (int u = 1; u < G; ++u) m = fmaxf(m, fabsf(y[u]));
     const float amax = warp_max_nonneg(m);
     const float dd = __fdiv_rn(amax, 127.0f), id = __fdiv_rn(127.0f, amax);
+    // every block's values first, then the half sums as independent full-warp
+    // reductions (no divergent branch between them), then one lane's stores
+    int v[G], lo[G], hi[G];
 #pragma unroll
     for (int u = 0; u < G; ++u) {
-        const int t = t0 + u;
-        const int v = amax == 0.0f ? 0 : (int)roundf(__fmul_rn(y[u], id));
-        q[32 * t + lane] = (int8_t)v;
-        const int s = half_isum_redux(v, lane);          // this lane's 16-value half
-        const int s_hi = __shfl_sync(0xffffffffu, s, 16);
-        if (lane == 0) {
+        v[u] = amax == 0.0f ? 0 : (int)roundf(__fmul_rn(y[u], id));
+        q[32 * (t0 + u) + lane] = (int8_t)v[u];
+    }
+#pragma unroll
+    for (int u = 0; u < G; ++u) {
+        lo[u] = warp_isum_redux(lane < 16 ? v[u] : 0);
+        hi[u] = warp_isum_redux(lane < 16 ? 0 : v[u]);
+    }
+    if (lane == 0) {
+#pragma unroll
+        for (int u = 0; u < G; ++u) {
+            const int t = t0 + u;
             d[t] = G == 1 ? round_h(dd) : dd;
-            s16[2 * t] = s;
-            s16[2 * t + 1] = s_hi;
-            s32[t] = s + s_hi;
+            s16[2 * t] = lo[u];
+            s16[2 * t + 1] = hi[u];
+            s32[t] = lo[u] + hi[u];
         }
     }
 }
