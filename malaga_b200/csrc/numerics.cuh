@@ -97,11 +97,8 @@ __device__ __forceinline__ float warp_max_nonneg(float v) {
     return __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(v)));
 }
 
-// Integer sums across the warp / each 16-lane half, one reduction instruction.
+// Integer sum across the warp, one reduction instruction.
 __device__ __forceinline__ int warp_isum_redux(int v) { return __reduce_add_sync(0xffffffffu, v); }
-__device__ __forceinline__ int half_isum_redux(int v, int lane) {
-    return lane < 16 ? __reduce_add_sync(0x0000ffffu, v) : __reduce_add_sync(0xffff0000u, v);
-}
 
 __device__ __forceinline__ int warp_isum(int v) {
 #pragma unroll
