@@ -1033,23 +1033,42 @@ static mgb_status gemm_tc(mgb_ctx *c, const Matrix &W, const QAct *act, const Pr
             a.g.part_i += (size_t)t0 * grid;
         }
         a.row_tiles = W.Np / 128;
-        a.tok_tiles = (n + nt - 1) / nt;
         a.splits = 1;
         if (split && split->part && XM < 0 && EPI != EPI_ARGMAX) {
-            // too few tiles for the SMs: split the stages (2 or 4 ways) if they divide
-            const int tiles = a.row_tiles * a.tok_tiles, ns = (W.nb + 7) / 8;
+            // Too few tiles for the SMs: split the stages (2 or 4 ways) where they divide, each split keeping
+            // tc_split_stages or more. Token tile and split count together: the fewest stages per CTA times
+            // waves over the SMs (on a tie the narrowest tile), e.g. the 16-stage FFN down at batch 64 runs as
+            // 16-token tiles split 4 ways (4 stages a CTA) rather than 8-token tiles split 2 ways (8).
+            const int ns = (W.nb + 7) / 8;
             const int nu = W.type == T_Q8_0 ? W.nb : W.nsb;
-            // (each split keeps tc_split_stages or more stages)
-            while (a.splits * 2 <= c->tc_split_max && tiles * a.splits * 2 <= c->sms && ns % (a.splits * 2) == 0 &&
-                   ns / (a.splits * 2) >= c->tc_split_stages)
-                a.splits *= 2;
-            if (a.splits > 1 && (size_t)a.tok_tiles * nt * W.Np * nu > split->part_floats) a.splits = 1;
+            long best = 0;
+            int best_nt = nt, best_splits = 1;
+            for (int cand : {8, 16, 32, 64}) {
+                if (cand < c->tc_min_nt && cand != 64) continue;
+                const int tt = (n + cand - 1) / cand, tiles = a.row_tiles * tt;
+                int sp = 1;
+                while (sp * 2 <= c->tc_split_max && tiles * sp * 2 <= c->sms && ns % (sp * 2) == 0 &&
+                       ns / (sp * 2) >= c->tc_split_stages)
+                    sp *= 2;
+                if (sp > 1 && (size_t)tt * cand * W.Np * nu > split->part_floats) sp = 1;
+                const long waves = ((long)tiles * sp + c->sms - 1) / c->sms;
+                const long cost = waves * (ns / sp);
+                if (best == 0 || cost < best) {
+                    best = cost;
+                    best_nt = cand;
+                    best_splits = sp;
+                }
+            }
+            nt = best_nt;
+            a.splits = best_splits;
+            const int tiles = a.row_tiles * ((n + nt - 1) / nt);
+            grid = (int)std::min<long>((long)tiles * a.splits, c->sms);
             if (a.splits > 1) {
                 a.kpart = split->part;
                 a.kcount = split->count;
-                grid = std::min(tiles * a.splits, c->sms);
             }
         }
+        a.tok_tiles = (n + nt - 1) / nt;
         if (ctas) *ctas = grid;
         TRY(make_maps(W, XM >= 0 ? nullptr : act, nt, a.m));
         switch (W.type) {
