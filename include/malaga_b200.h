@@ -156,7 +156,10 @@ MGB_API mgb_status mgb_profile_step(mgb_ctx *ctx, const mgb_batch *batch, uint32
  * GPU loading the library keeps until exit, shared by all calls: calls that
  * overlap on the GPU race. The first call on a device looks up the array's
  * device address (cudaGetSymbolAddress); make that first call before any
- * stream capture. Asynchronous: results are ready when the stream reaches them. */
+ * stream capture. The cached address belongs to the device's current context:
+ * after cudaDeviceReset on that device it is stale and the library must be
+ * reloaded. NaN logits never win; a row of only NaNs gives id 0 and value
+ * -inf. Asynchronous: results are ready when the stream reaches them. */
 MGB_API mgb_status mgb_argmax_noalloc(const float *logits, uint32_t rows, uint32_t vocab, uint32_t *ids, float *vals,
                                       void *stream);
 

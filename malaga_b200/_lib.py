@@ -47,6 +47,7 @@ SIGNATURES = {
     "mgb_cuda_stream": (_vp, [_vp]),
     "mgb_kernel_launches": (_u64, [_vp]),
     "mgb_profile_step": (_i, [_vp, _vp, _u32, _u32, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_float)]),
+    "mgb_argmax_noalloc": (_i, [_vp, _u32, _u32, _vp, _vp, _vp]),
 }
 
 

@@ -30,6 +30,7 @@
 #include "../../include/malaga_b200.h"
 #include "beam.cuh"
 #include "gemm_tc.cuh"
+#include "smallmm.cuh"
 
 using namespace mgb;
 
@@ -218,9 +219,9 @@ void q6k_block_values(const uint8_t *row, int j, uint8_t *q) {
 
 // Split-K buffers of a decode step (StaticState): partials and tile counters.
 struct SplitBufs {
-    float *part = nullptr;
+    float2 *part = nullptr;
     uint32_t *count = nullptr;
-    size_t part_floats = 0;
+    size_t part_units = 0;
 };
 
 struct StaticState {
@@ -228,9 +229,7 @@ struct StaticState {
     uint32_t *ids = nullptr, *step = nullptr, *out = nullptr, *lens = nullptr;
     uint8_t *finished = nullptr;
     float *x = nullptr, *q = nullptr, *a = nullptr, *u = nullptr, *xf = nullptr;
-    QAct act, act2;                  // tensor-core activations (the step alternates between them)
-    uint32_t *counters = nullptr;    // completion counters of the matmuls' post steps
-    size_t counter_bytes = 0;
+    QAct act;                        // q8_1 tensor-core activations of the next matmul
     SplitBufs split;                 // split-K partials and tile counters
     // beam search (allocated on first use): step logits, top-k, row sources and a
     // second set of self-attention caches to gather into
@@ -259,7 +258,10 @@ struct mgb_batch {
     mgb_ctx *owner = nullptr;
 };
 
-static constexpr int kLmParts = 148 * 8;  // CTAs of the fused LM-head argmax
+static constexpr int kLmParts = 148 * 8;  // most CTAs of a fused LM-head argmax launch (partials per row)
+// Matmuls of at most this many activation rows run the reference's MMVQ
+// arithmetic (candle-core's QMatMul picks MMVQ up to 8 rows, MMQ above).
+static constexpr int kSmallRows = 8;
 static constexpr size_t kGraphBytes = 32u << 20;
 
 struct mgb_ctx {
@@ -283,26 +285,11 @@ struct mgb_ctx {
     std::vector<std::unique_ptr<StaticState>> cache;
     size_t weight_bytes = 0, step_bytes = 0;
     uint32_t *d_err = nullptr;  // device-side error flags (a bounded wait ran out)
-    // Activation rows from which matmuls run on the tensor cores (tcgen05)
-    // instead of the small-batch kernels; MGB_TC_MIN_ROWS overrides (tests).
-    int tc_min_rows = 16;
-    int tc_min_nt = 8;  // narrowest token tile (MGB_TC_MIN_NT)
-    // Decode-step tensor-core matmuls build their activations in the kernel
-    // (1) or read them from qprep_row_kernel (0); MGB_TC_FUSED overrides.
-    int tc_fused = 0;
-    // Matmuls' post steps prepare the next LayerNorm / hidden-layer activations
-    // (1) or qprep_row does (0, faster on B200 so far: one CTA per row in parallel
-    // beats the last CTA of a token tile); MGB_TC_POST overrides.
-    int tc_post = 0;
-    // The attention kernel quantizes its outputs for the next matmul (1) or
-    // qprep_row does (0); MGB_TC_ATTN_Q overrides.
-    int tc_attn_q = 1;
+    int tc_min_nt = 8;  // narrowest token tile of the tensor-core matmul (MGB_TC_MIN_NT)
     // Matmuls with too few tiles for the SMs split their K stages (MGB_TC_SPLIT overrides).
     int tc_split = 1;
     int tc_split_stages = 4;  // fewest stages per split (MGB_TC_SPLIT_STAGES)
     int tc_split_max = 4;     // most splits of a tile (MGB_TC_SPLIT_MAX)
-    // Batches up to this many rows fold the attention into the next matmul (MGB_ATTN_FUSE_ROWS).
-    int attn_fuse_rows = 0;
     int sms = 148;  // multiprocessor count of the device (one tensor-core CTA each)
     void *enc_ws = nullptr;  // encoder temporaries (grown on demand)
     size_t enc_ws_bytes = 0;
@@ -398,16 +385,54 @@ struct Planner {
         M.bytes = (size_t)rb * N;
         auto slot = [&](long r, int j) { return ((size_t)(r / 32) * nb + j) * 32 + (size_t)(r % 32); };
         auto sslot = [&](long r, int sb) { return ((size_t)(r / 32) * nsb + sb) * 32 + (size_t)(r % 32); };
+        // row layout (engine.h): the GGUF bytes row by row, split into aligned regions
         if (t->type == T_F32) {
             size_t off = L.reserve((size_t)4 * Np * K);
+            if (pass == 1) memcpy(L.host.data() + off, t->data, (size_t)rb * N);
+            ptr(&M.ra, off);
+        } else if (t->type == T_Q4_K) {
+            size_t off = L.reserve((size_t)Np * rb);
+            if (pass == 1) memcpy(L.host.data() + off, t->data, (size_t)rb * N);
+            ptr(&M.ra, off);
+        } else if (t->type == T_Q8_0) {
+            size_t oq = L.reserve((size_t)Np * nb * 32), od = L.reserve((size_t)Np * nb * 2);
             if (pass == 1) {
-                uint8_t *h = L.host.data() + off;
+                uint8_t *hq = L.host.data() + oq, *hd = L.host.data() + od;
 #pragma omp parallel for schedule(static)
                 for (long r = 0; r < N; ++r)
-                    for (int j = 0; j < nb; ++j)
-                        memcpy(h + slot(r, j) * 128, t->data + (size_t)r * rb + 128 * j, 128);
+                    for (int j = 0; j < nb; ++j) {
+                        const uint8_t *blk = t->data + (size_t)r * rb + 34 * j;
+                        memcpy(hd + ((size_t)r * nb + j) * 2, blk, 2);
+                        memcpy(hq + ((size_t)r * nb + j) * 32, blk + 2, 32);
+                    }
             }
-            ptr(&M.a, off);
+            ptr(&M.ra, oq);
+            ptr(&M.rb, od);
+        } else {  // Q6_K
+            size_t ol = L.reserve((size_t)Np * nsb * 128), oh = L.reserve((size_t)Np * nsb * 64);
+            size_t os = L.reserve((size_t)Np * nsb * 16), od = L.reserve((size_t)Np * nsb * 2);
+            if (pass == 1) {
+                uint8_t *hl = L.host.data() + ol, *hh = L.host.data() + oh, *hs = L.host.data() + os,
+                        *hd = L.host.data() + od;
+#pragma omp parallel for schedule(static)
+                for (long r = 0; r < N; ++r)
+                    for (int sb = 0; sb < nsb; ++sb) {
+                        const uint8_t *blk = t->data + (size_t)r * rb + 210 * sb;
+                        const size_t u = (size_t)r * nsb + sb;
+                        memcpy(hl + u * 128, blk, 128);
+                        memcpy(hh + u * 64, blk + 128, 64);
+                        memcpy(hs + u * 16, blk + 192, 16);
+                        memcpy(hd + u * 2, blk + 208, 2);
+                    }
+            }
+            ptr(&M.ra, ol);
+            ptr(&M.rb, oh);
+            ptr(&M.rc, os);
+            ptr(&M.re, od);
+        }
+        // tensor-core layout
+        if (t->type == T_F32) {
+            // (small-batch kernels only)
         } else if (t->type == T_Q8_0) {
             size_t oq = L.reserve((size_t)Np * nb * 32), od = L.reserve((size_t)Np * nb * 2);
             if (pass == 1) {
@@ -598,41 +623,6 @@ static mgb_status load_model(mgb_ctx *c, const char *path) {
 // ---------------------------------------------------------------------------
 // Kernel launchers
 
-static int gemv_grid(int Np) { return std::max(1, std::min((Np / 32 + 7) / 8, 148 * 16)); }
-
-template <int TYPE>
-static void launch_gemv_t(int epi, const GemvArgs &g, int grid, cudaStream_t s) {
-    switch (epi) {
-        case EPI_STORE: gemv_kernel<TYPE, EPI_STORE><<<grid, 256, 0, s>>>(g); break;
-        case EPI_RELU: gemv_kernel<TYPE, EPI_RELU><<<grid, 256, 0, s>>>(g); break;
-        case EPI_RESID: gemv_kernel<TYPE, EPI_RESID><<<grid, 256, 0, s>>>(g); break;
-        case EPI_CROSSKV: gemv_kernel<TYPE, EPI_CROSSKV><<<grid, 256, 0, s>>>(g); break;
-    }
-}
-
-static mgb_status gemv(mgb_ctx *c, int epi, GemvArgs g, int grid = 0) {
-    if (!grid) grid = gemv_grid(g.W.Np);
-    return launch_check(c, [&] {
-        switch (g.W.type) {
-            case T_F32: launch_gemv_t<T_F32>(epi, g, grid, c->stream); break;
-            case T_Q8_0: launch_gemv_t<T_Q8_0>(epi, g, grid, c->stream); break;
-            case T_Q4_K: launch_gemv_t<T_Q4_K>(epi, g, grid, c->stream); break;
-            case T_Q6_K: launch_gemv_t<T_Q6_K>(epi, g, grid, c->stream); break;
-        }
-    });
-}
-
-static mgb_status qprep(mgb_ctx *c, int mode, PrepArgs p) {
-    const int grid = (p.rows + 7) / 8;
-    return launch_check(c, [&] {
-        switch (mode) {
-            case PREP_PLAIN: qprep_kernel<PREP_PLAIN><<<grid, 256, 0, c->stream>>>(p); break;
-            case PREP_LN: qprep_kernel<PREP_LN><<<grid, 256, 0, c->stream>>>(p); break;
-            case PREP_EMBED_LN: qprep_kernel<PREP_EMBED_LN><<<grid, 256, 0, c->stream>>>(p); break;
-        }
-    });
-}
-
 // Launch with programmatic stream serialization: the kernel may begin (and
 // prefetch) while its predecessor finishes; it waits in griddepcontrol.wait.
 template <typename... KArgs, typename... Args>
@@ -685,7 +675,7 @@ static mgb_status attend(mgb_ctx *c, AttnArgs a) {
         return MGB_OK;
     };
     // single-query attention of a small decode batch releases the next kernel late
-    const bool late = a.queries == 1 && a.rows < c->tc_min_rows;
+    const bool late = a.queries == 1 && a.rows <= kSmallRows;
     switch (a.hd) {
         case 16: return late ? go(attend_kernel<KV, 16, true>) : go(attend_kernel<KV, 16, false>);
         case 32: return late ? go(attend_kernel<KV, 32, true>) : go(attend_kernel<KV, 32, false>);
@@ -695,201 +685,118 @@ static mgb_status attend(mgb_ctx *c, AttnArgs a) {
     return set_err(MGB_ERR_UNSUPPORTED, "head dimension %d", a.hd);
 }
 
-// Fused small-batch matmul (fused.cuh). Splits the batch when its activations
-// would not fit in shared memory.
+// Small-batch matmul (smallmm.cuh). NC = the launch's rows rounded up to a
+// power of two; the MMVQ warp count follows from it as in candle's launch
+// table (4 warps for 1-4 rows, 2 for 5-8). At least 8 weight rows per CTA, at
+// most two CTAs per SM, stages of about 24 KB.
+template <int TYPE, int EPI, int MODE, int NC>
+static cudaError_t small_launch(mgb_ctx *c, const SmallArgs &a, int grid, size_t smem) {
+    auto kern = small_mm_kernel<TYPE, EPI, MODE, NC, NC <= 4 ? 4 : 2>;
+    cudaError_t e = allow_smem(kern, smem);
+    return e == cudaSuccess ? launch_pdl(kern, dim3(grid), dim3(256), smem, c->stream, a) : e;
+}
+
 template <int TYPE, int EPI, int MODE>
-static mgb_status fused_t(mgb_ctx *c, FusedArgs fa) {
-    const Matrix &W = fa.g.W;
-    const int B = fa.g.rows;
-    const bool f32 = TYPE == T_F32;
-    if constexpr (TYPE != T_F32 && EPI != EPI_ARGMAX) {
-        size_t sh = staged_bytes(TYPE, W.nb, W.nsb) + smact_bytes(B, W.K, false) + staged_partial_bytes(TYPE, B, W.nb);
-        if (MODE == PREP_ATTN) sh += attn_prologue_bytes(fa.at.max_keys, fa.at.hd);
-        if (MODE == PREP_LN || MODE == PREP_EMBED_LN) sh += (size_t)8 * W.K;  // LayerNorm parameters
-        if (B <= 8 && sh <= 200 * 1024) {
-            auto kern = gemv_staged_kernel<TYPE, EPI, MODE>;
-            cudaError_t e = allow_smem(kern, sh);
-            if (e == cudaSuccess) e = launch_pdl(kern, dim3(W.Np / 32), dim3(256), sh, c->stream, fa, c->d_err);
-            ++c->launches;
-            if (e != cudaSuccess) return cuda_err(e, "staged matmul launch");
-            return MGB_OK;
+static mgb_status small_t(mgb_ctx *c, const GemvArgs &g, const PrepArgs &p, int *ctas) {
+    const Matrix &W = g.W;
+    const int RB = row_bytes_of(TYPE, W.K), groups = W.Np / 8;
+    int grid = std::min(groups, 2 * c->sms);
+    const int rpc = (groups + grid - 1) / grid * 8;
+    grid = (W.Np + rpc - 1) / rpc;
+    if (ctas) *ctas = grid;
+    // launches of at most 8 activation rows (more only for F32 weights)
+    for (int n0 = 0; n0 < g.rows; n0 += kSmallRows) {
+        const int here = std::min(kSmallRows, g.rows - n0);
+        const int NC = here <= 1 ? 1 : here <= 2 ? 2 : here <= 4 ? 4 : 8;
+        SmallArgs a{};
+        a.g = g;
+        a.p = p;
+        a.n0 = n0;
+        a.rows_per_cta = rpc;
+        a.chunk = std::max(1, std::min(rpc / 8, 24 * 1024 / (8 * RB))) * 8;
+        a.stages = TYPE == T_F32 ? 0 : std::min(3, (rpc + a.chunk - 1) / a.chunk);
+        a.err = c->d_err;
+        const size_t act = small_act_bytes(NC, W.K, TYPE, MODE);
+        while (a.stages > 1 && (size_t)a.stages * a.chunk * RB + act > c->smem_optin) --a.stages;
+        const size_t smem = (size_t)a.stages * a.chunk * RB + act;
+        if (smem > c->smem_optin)
+            return set_err(MGB_ERR_UNSUPPORTED, "small-batch matmul of a %d-value row needs %zu B of shared memory",
+                           W.K, smem);
+        cudaError_t e;
+        switch (NC) {
+            case 1: e = small_launch<TYPE, EPI, MODE, 1>(c, a, grid, smem); break;
+            case 2: e = small_launch<TYPE, EPI, MODE, 2>(c, a, grid, smem); break;
+            case 4: e = small_launch<TYPE, EPI, MODE, 4>(c, a, grid, smem); break;
+            default: e = small_launch<TYPE, EPI, MODE, 8>(c, a, grid, smem); break;
         }
-    }
-    if constexpr (MODE == PREP_ATTN) {
-        return set_err(MGB_ERR_UNSUPPORTED, "attention prologue needs the staged matmul");
-    } else {
-    const int NBv = B == 1 ? 1 : 8;
-    int chunk = B;
-    while (chunk > 1 && smact_bytes(chunk, W.K, f32) > 160 * 1024) chunk = (chunk + 1) / 2;
-    if (EPI == EPI_ARGMAX) chunk = std::min(chunk, NBv);  // per-warp bests hold NB rows
-    const int groups = W.Np / 32;
-    int grid, gpc;
-    if (EPI == EPI_ARGMAX) {
-        grid = kLmParts;  // fixed: the partial buffers and greedy_finalize assume it
-        gpc = (groups + grid - 1) / grid;
-    } else {
-        const int ctas = std::min(groups, 296);
-        gpc = (groups + ctas - 1) / ctas;
-        grid = (groups + gpc - 1) / gpc;
-    }
-    fa.rows_per_cta = gpc;
-    for (int c0 = 0; c0 < B; c0 += chunk) {
-        FusedArgs f = fa;
-        const int nrow = std::min(chunk, B - c0);
-        f.g.rows = nrow;
-        f.p.rows = nrow;
-        if (MODE == PREP_EMBED_LN) {
-            f.p.ids += c0;
-            f.p.x_out += (size_t)c0 * W.K;
-        } else {
-            f.p.x += (size_t)c0 * W.K;
-        }
-        if (f.g.y) f.g.y += (size_t)c0 * W.N;
-        if (f.g.q) f.g.q += (size_t)c0 * f.g.H * f.g.hd;
-        if (f.g.kc) f.g.kc += (size_t)c0 * f.g.H * f.g.m * f.g.hd;
-        if (f.g.vc) f.g.vc += (size_t)c0 * f.g.H * f.g.m * f.g.hd;
-        if (f.g.part_v) f.g.part_v += (size_t)c0 * grid;
-        if (f.g.part_i) f.g.part_i += (size_t)c0 * grid;
-        if (f.g.logits) f.g.logits += (size_t)c0 * W.N;
-        const size_t sh = smact_bytes(nrow, W.K, f32) +
-                          (MODE != PREP_PLAIN && (size_t)nrow * W.K * 4 <= 64 * 1024 ? (size_t)nrow * W.K * 4 : 0);
-        auto go = [&](auto kern) -> cudaError_t {
-            cudaError_t e = allow_smem(kern, sh);
-            return e == cudaSuccess ? launch_pdl(kern, dim3(grid), dim3(256), sh, c->stream, f) : e;
-        };
-        cudaError_t e = nrow == 1 ? go(gemv_fused_kernel<TYPE, EPI, MODE, 1>) : go(gemv_fused_kernel<TYPE, EPI, MODE, 8>);
         ++c->launches;
-        if (e != cudaSuccess) return cuda_err(e, "fused matmul launch");
+        if (e != cudaSuccess) return cuda_err(e, "small-batch matmul launch");
     }
     return MGB_OK;
-    }
 }
 
+// y = W . act(p) with the reference's MMVQ arithmetic (at most 8 rows; F32
+// weights any number). *ctas: CTAs of the launch (argmax partials per row).
 template <int EPI, int MODE>
-static mgb_status fused(mgb_ctx *c, const FusedArgs &fa) {
-    switch (fa.g.W.type) {
-        case T_F32: return fused_t<T_F32, EPI, MODE>(c, fa);
-        case T_Q8_0: return fused_t<T_Q8_0, EPI, MODE>(c, fa);
-        case T_Q4_K: return fused_t<T_Q4_K, EPI, MODE>(c, fa);
-        case T_Q6_K: return fused_t<T_Q6_K, EPI, MODE>(c, fa);
+static mgb_status small_mm(mgb_ctx *c, GemvArgs g, PrepArgs p, int *ctas = nullptr) {
+    p.rows = g.rows;
+    p.K = g.W.K;
+    switch (g.W.type) {
+        case T_F32: return small_t<T_F32, EPI, MODE>(c, g, p, ctas);
+        case T_Q8_0: return small_t<T_Q8_0, EPI, MODE>(c, g, p, ctas);
+        case T_Q4_K: return small_t<T_Q4_K, EPI, MODE>(c, g, p, ctas);
+        case T_Q6_K: return small_t<T_Q6_K, EPI, MODE>(c, g, p, ctas);
     }
-    return set_err(MGB_ERR_UNSUPPORTED, "matrix type %d", fa.g.W.type);
+    return set_err(MGB_ERR_UNSUPPORTED, "matrix type %d", g.W.type);
 }
 
-static PrepArgs prep_args(const QAct &act, float *xf, bool keep_f32, const float *x, int rows, int K) {
-    PrepArgs p{};
-    p.x = x;
-    p.rows = rows;
-    p.K = K;
-    p.out = act;
-    p.out.rows = rows;
-    p.out.K = K;
-    p.keep_f32 = keep_f32;
-    p.xf = xf;
-    return p;
-}
+static bool tc_ok(const Matrix &W) { return W.type == T_Q8_0 || W.type == T_Q4_K || W.type == T_Q6_K; }
 
-static GemvArgs gemv_args(const Matrix &W, const QAct &act, const float *xf, int rows) {
-    GemvArgs g{};
-    g.W = W;
-    g.x = act;
-    g.x.rows = rows;
-    g.x.K = W.K;
-    g.xf = xf;
-    g.rows = rows;
-    return g;
-}
-
-static bool any_f32(const mgb_ctx *c) {
-    if (c->embed.type == T_F32) return true;
-    for (auto &l : c->dec)
-        if (l.qkv.type == T_F32 || l.out.type == T_F32 || l.cq.type == T_F32 || l.ckv.type == T_F32 ||
-            l.co.type == T_F32 || l.up.type == T_F32 || l.down.type == T_F32)
-            return true;
-    for (auto &l : c->enc)
-        if (l.qkv.type == T_F32 || l.out.type == T_F32 || l.up.type == T_F32 || l.down.type == T_F32) return true;
-    return false;
-}
-
-// Tensor-core path: activations of `rows` rows into `act` in the layout of the
-// consuming matrix W (one CTA per row).
+// Tensor-core path: q8_1 activations of `rows` rows into `act` (one CTA per row).
 template <int MODE>
-static mgb_status qprep_row(mgb_ctx *c, PrepArgs p, const QAct &act, const Matrix &W) {
+static mgb_status qprep_row(mgb_ctx *c, PrepArgs p, const QAct &act) {
     auto kern = qprep_row_kernel<MODE>;
-    p.group = act_group(W.type);
-    p.ctype = W.type;
-    // row, bytes, block scales and sums; LayerNorm parameters for LN modes
-    const size_t sh = (size_t)p.K * 5 + (size_t)(p.K / 32) * 16 + (MODE != PREP_PLAIN ? (size_t)p.K * 8 : 0);
+    const size_t sh = (size_t)p.K * 4 + (MODE != PREP_PLAIN ? (size_t)p.K * 8 : 0);  // row; gamma, beta
     cudaError_t e = allow_smem(kern, sh);
     if (e == cudaSuccess) e = launch_pdl(kern, dim3(p.rows), dim3(256), sh, c->stream, p, act);
     ++c->launches;
     return e == cudaSuccess ? MGB_OK : cuda_err(e, "activation prep launch");
 }
 
-// Shared memory of a tensor-core launch (gemm_tc.cuh): the stage and tile
-// rings, plus the resident activations when the kernel builds them.
 template <int TYPE>
-static size_t tc_smem_t(int nt, bool fused, int nb) {
-    auto base = [&](auto ntc) -> size_t {
-        constexpr int NT = decltype(ntc)::value;
-        return fused ? gemm_tc_smem_base<TYPE, NT, true>() + tc::fused_act_bytes(TYPE, NT, nb)
-                     : gemm_tc_smem_base<TYPE, NT, false>();
-    };
+static size_t tc_smem_t(int nt) {
     switch (nt) {
-        case 8: return base(std::integral_constant<int, 8>{});
-        case 16: return base(std::integral_constant<int, 16>{});
-        case 32: return base(std::integral_constant<int, 32>{});
-        default: return base(std::integral_constant<int, 64>{});
+        case 8: return gemm_tc_smem<TYPE, 8>();
+        case 16: return gemm_tc_smem<TYPE, 16>();
+        case 32: return gemm_tc_smem<TYPE, 32>();
+        default: return gemm_tc_smem<TYPE, 64>();
     }
 }
 
-static size_t tc_smem(int type, int nt, bool fused, int nb) {
+static size_t tc_smem(int type, int nt) {
     switch (type) {
-        case T_Q8_0: return tc_smem_t<T_Q8_0>(nt, fused, nb);
-        case T_Q4_K: return tc_smem_t<T_Q4_K>(nt, fused, nb);
-        default: return tc_smem_t<T_Q6_K>(nt, fused, nb);
+        case T_Q8_0: return tc_smem_t<T_Q8_0>(nt);
+        case T_Q4_K: return tc_smem_t<T_Q4_K>(nt);
+        default: return tc_smem_t<T_Q6_K>(nt);
     }
 }
 
-// Tile width (activation rows per tile) and grid of a tensor-core matmul: the
-// widest tile that still gives every SM a tile (and, for activations built in
-// the kernel, whose resident activations fit in shared memory); persistent
-// CTAs, one per SM. Fused launches give each token tile the same number of CTAs.
-static bool tc_shape(const Matrix &W, int rows, int sms, bool fused, size_t smem_limit, int min_nt, int &nt,
-                     int &grid) {
+// Token tile (activation rows per tile, at least min_nt) of a tensor-core
+// matmul: the one that needs the fewest waves of tiles over the SMs, on a tie
+// the narrowest, whose tiles finish soonest; persistent CTAs, one per SM.
+static void tc_shape(const Matrix &W, int rows, int sms, int min_nt, int &nt, int &grid) {
     const int row_tiles = W.Np / 128;
+    long best = 0;
     nt = 0;
-    if (fused) {
-        // one token tile per CTA: narrower tiles until every SM has one (or the
-        // narrowest whose activations fit)
-        for (int cand : {64, 32, 16, 8}) {
-            if (cand < min_nt && nt) break;
-            if (tc_smem(W.type, cand, true, W.nb) > smem_limit) continue;
+    for (int cand : {8, 16, 32, 64}) {
+        if (cand < min_nt && cand != 64) continue;
+        const long waves = ((long)row_tiles * ((rows + cand - 1) / cand) + sms - 1) / sms;
+        if (!nt || waves < best) {
             nt = cand;
-            if ((long)row_tiles * ((rows + cand - 1) / cand) >= sms) break;
-        }
-    } else {
-        // the token tile (of at least min_nt rows) that needs the fewest waves
-        // of tiles over the SMs; on a tie the narrowest, whose tiles finish soonest
-        long best = 0;
-        for (int cand : {8, 16, 32, 64}) {
-            if (cand < min_nt && cand != 64) continue;
-            const long waves = ((long)row_tiles * ((rows + cand - 1) / cand) + sms - 1) / sms;
-            if (!nt || waves < best) {
-                nt = cand;
-                best = waves;
-            }
+            best = waves;
         }
     }
-    if (!nt) return false;
-    const int tok_tiles = (rows + nt - 1) / nt;
-    if (fused) {
-        const int per = std::max(1, std::min(row_tiles, sms / tok_tiles));
-        grid = per * tok_tiles;
-    } else {
-        grid = (int)std::min<long>((long)row_tiles * tok_tiles, sms);
-    }
-    return true;
+    grid = (int)std::min<long>((long)row_tiles * ((rows + nt - 1) / nt), sms);
 }
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
@@ -931,9 +838,8 @@ static mgb_status tmap(CUtensorMap *m, const void *base, int rank, const uint64_
     return MGB_OK;
 }
 
-// The launch's tensor maps (layouts: engine.h Matrix, gemm_tc.cuh tc::Maps);
-// x = null when the kernel builds its activations.
-static mgb_status make_maps(const Matrix &W, const QAct *x, int nt, tc::Maps &m) {
+// The launch's tensor maps (layouts: engine.h Matrix and QAct, gemm_tc.cuh tc::Maps).
+static mgb_status make_maps(const Matrix &W, const QAct &x, int nt, tc::Maps &m) {
     memset(&m, 0, sizeof m);
     const uint64_t G = (uint64_t)W.Np / 32, nb = W.nb, nsb = W.nsb;
     // one weight region: X words per (group, block-or-super-block) slice, n slices, boxes of k slices
@@ -960,52 +866,47 @@ static mgb_status make_maps(const Matrix &W, const QAct *x, int nt, tc::Maps &m)
         default:
             return set_err(MGB_ERR_UNSUPPORTED, "tensor-core matmul of type %d", W.type);
     }
-    if (!x) return MGB_OK;  // activations built in the kernel
-    const uint64_t rs = (uint64_t)x->rs;
+    const uint64_t rs = (uint64_t)x.rs;
     {
         const uint64_t dims[3] = {32, rs / 8, nb}, str[2] = {256, rs * 32};
         const uint32_t box[3] = {32, (uint32_t)nt / 8, 8};
-        TRY(tmap(&m.xq, x->tq, 3, dims, str, box, false));
+        TRY(tmap(&m.xq, x.tq, 3, dims, str, box, false));
     }
-    if (W.type == T_Q4_K) {
-        const uint64_t dims[2] = {rs * 4, nsb}, str[1] = {rs * 32};
-        const uint32_t box[2] = {(uint32_t)nt * 4, 1};
-        TRY(tmap(&m.xr, x->trec, 2, dims, str, box, false));
-    } else {
-        const uint64_t units = W.type == T_Q6_K ? nsb : nb;
-        const uint64_t dims[2] = {rs / 2, units}, str[1] = {rs * 4};
-        const uint32_t box[2] = {(uint32_t)nt / 2, W.type == T_Q6_K ? 1u : 8u};
-        TRY(tmap(&m.xr, x->trec, 2, dims, str, box, false));
+    {
+        // records: one float2 (8-byte word) per (block, row)
+        const uint64_t dims[2] = {rs, nb}, str[1] = {rs * 8};
+        const uint32_t box[2] = {(uint32_t)nt, 8};
+        TRY(tmap(&m.xr, x.trec, 2, dims, str, box, false));
     }
     return MGB_OK;
 }
 
-template <int TYPE, int EPI, int XM>
+template <int TYPE, int EPI>
 static mgb_status gemm_tc_t(mgb_ctx *c, const tc::Args &a, int nt, int grid) {
-    const size_t sh = tc_smem(TYPE, nt, XM >= 0, a.W.nb);
+    const size_t sh = tc_smem(TYPE, nt);
     auto go = [&](auto kern) -> cudaError_t {
         cudaError_t e = allow_smem(kern, sh);
         return e == cudaSuccess ? launch_pdl(kern, dim3(grid), dim3(tc::kThreads), sh, c->stream, a) : e;
     };
     cudaError_t e;
     switch (nt) {
-        case 8: e = go(gemm_tc_kernel<TYPE, EPI, 8, XM>); break;
-        case 16: e = go(gemm_tc_kernel<TYPE, EPI, 16, XM>); break;
-        case 32: e = go(gemm_tc_kernel<TYPE, EPI, 32, XM>); break;
-        default: e = go(gemm_tc_kernel<TYPE, EPI, 64, XM>); break;
+        case 8: e = go(gemm_tc_kernel<TYPE, EPI, 8>); break;
+        case 16: e = go(gemm_tc_kernel<TYPE, EPI, 16>); break;
+        case 32: e = go(gemm_tc_kernel<TYPE, EPI, 32>); break;
+        default: e = go(gemm_tc_kernel<TYPE, EPI, 64>); break;
     }
     ++c->launches;
     return e == cudaSuccess ? MGB_OK : cuda_err(e, "tensor-core matmul launch");
 }
 
-// y = W . x for `rows` activation rows on the tensor cores, epilogue EPI.
-// XM < 0: x was written by qprep_row (act); otherwise the kernel builds it from
-// p in mode XM. The LM head (ARGMAX) runs in launches of at most 64 rows (one
+// y = W . x for `rows` activation rows (q8_1 in `act`, written by qprep_row or
+// the attention kernel) on the tensor cores, epilogue EPI, the reference's MMQ
+// arithmetic. The LM head (ARGMAX) runs in launches of at most 64 rows (one
 // token tile each); *ctas returns its CTA count, the partial count per row.
-template <int EPI, int XM>
-static mgb_status gemm_tc(mgb_ctx *c, const Matrix &W, const QAct *act, const PrepArgs *p, int rows,
-                          const GemvArgs &g, int *ctas = nullptr, const tc::Post *post = nullptr,
-                          const SplitBufs *split = nullptr) {
+template <int EPI>
+static mgb_status gemm_tc(mgb_ctx *c, const Matrix &W, const QAct &act, int rows, const GemvArgs &g,
+                          int *ctas = nullptr, const SplitBufs *split = nullptr) {
+    if (!tc_ok(W)) return set_err(MGB_ERR_UNSUPPORTED, "tensor-core matmul of type %d", W.type);
     const int chunk = EPI == EPI_ARGMAX ? 64 : rows;
     for (int t0 = 0; t0 < rows; t0 += chunk) {
         const int n = std::min(chunk, rows - t0);
@@ -1018,15 +919,8 @@ static mgb_status gemm_tc(mgb_ctx *c, const Matrix &W, const QAct *act, const Pr
         a.g.W = W;
         a.g.rows = n;
         a.err = c->d_err;
-        a.post = post ? *post : tc::Post{};  // (after the memset: mode -1 = no post step)
-        if (p) {
-            a.p = *p;
-            a.p.K = W.K;
-            if (a.p.x) a.p.x += (size_t)t0 * W.K;
-        }
         int nt, grid;
-        if (!tc_shape(W, n, c->sms, XM >= 0, c->smem_optin, c->tc_min_nt, nt, grid))
-            return set_err(MGB_ERR_UNSUPPORTED, "no tensor-core tile fits a %d-value row", W.K);
+        tc_shape(W, n, c->sms, c->tc_min_nt, nt, grid);
         if (EPI == EPI_ARGMAX) {
             if (a.g.logits) a.g.logits += (size_t)t0 * W.N;
             a.g.part_v += (size_t)t0 * grid;
@@ -1034,13 +928,13 @@ static mgb_status gemm_tc(mgb_ctx *c, const Matrix &W, const QAct *act, const Pr
         }
         a.row_tiles = W.Np / 128;
         a.splits = 1;
-        if (split && split->part && XM < 0 && EPI != EPI_ARGMAX) {
+        if (split && split->part && EPI != EPI_ARGMAX) {
             // Too few tiles for the SMs: split the stages (2 or 4 ways) where they divide, each split keeping
             // tc_split_stages or more. Token tile and split count together: the fewest stages per CTA times
             // waves over the SMs (on a tie the narrowest tile), e.g. the 16-stage FFN down at batch 64 runs as
             // 16-token tiles split 4 ways (4 stages a CTA) rather than 8-token tiles split 2 ways (8).
             const int ns = (W.nb + 7) / 8;
-            const int nu = W.type == T_Q8_0 ? W.nb : W.nsb;
+            const int nu = W.type == T_Q8_0 ? W.nb : W.nb / 2;
             long best = 0;
             int best_nt = nt, best_splits = 1;
             for (int cand : {8, 16, 32, 64}) {
@@ -1050,7 +944,7 @@ static mgb_status gemm_tc(mgb_ctx *c, const Matrix &W, const QAct *act, const Pr
                 while (sp * 2 <= c->tc_split_max && tiles * sp * 2 <= c->sms && ns % (sp * 2) == 0 &&
                        ns / (sp * 2) >= c->tc_split_stages)
                     sp *= 2;
-                if (sp > 1 && (size_t)tt * cand * W.Np * nu > split->part_floats) sp = 1;
+                if (sp > 1 && (size_t)tt * cand * W.Np * nu > split->part_units) sp = 1;
                 const long waves = ((long)tiles * sp + c->sms - 1) / c->sms;
                 const long cost = waves * (ns / sp);
                 if (best == 0 || cost < best) {
@@ -1070,22 +964,18 @@ static mgb_status gemm_tc(mgb_ctx *c, const Matrix &W, const QAct *act, const Pr
         }
         a.tok_tiles = (n + nt - 1) / nt;
         if (ctas) *ctas = grid;
-        TRY(make_maps(W, XM >= 0 ? nullptr : act, nt, a.m));
+        TRY(make_maps(W, act, nt, a.m));
         switch (W.type) {
-            case T_Q8_0: TRY((gemm_tc_t<T_Q8_0, EPI, XM>(c, a, nt, grid))); break;
-            case T_Q4_K: TRY((gemm_tc_t<T_Q4_K, EPI, XM>(c, a, nt, grid))); break;
-            case T_Q6_K: TRY((gemm_tc_t<T_Q6_K, EPI, XM>(c, a, nt, grid))); break;
-            default: return set_err(MGB_ERR_UNSUPPORTED, "tensor-core matmul of type %d", W.type);
+            case T_Q8_0: TRY((gemm_tc_t<T_Q8_0, EPI>(c, a, nt, grid))); break;
+            case T_Q4_K: TRY((gemm_tc_t<T_Q4_K, EPI>(c, a, nt, grid))); break;
+            default: TRY((gemm_tc_t<T_Q6_K, EPI>(c, a, nt, grid))); break;
         }
     }
     return MGB_OK;
 }
 
-static bool tc_ok(const Matrix &W) { return W.type == T_Q8_0 || W.type == T_Q4_K || W.type == T_Q6_K; }
-
-// Activation buffers: the tensor-core layout (rows padded to 64; tiles for up
-// to two copies per block for Q6_K consumers, records for the largest unit
-// count) and the row-major q8 arrays of the other matmul kernels.
+// q8_1 activation buffers of the tensor-core path: tiles and records for rows
+// padded to 64 and rows of up to kmax values.
 static mgb_status alloc_tc_act(mgb_ctx *c, int rows, int kmax, QAct &a, std::vector<void *> &allocs, size_t *bytes) {
     const int rp = (rows + 63) / 64 * 64, nbm = kmax / 32;
     auto A = [&](void **p, size_t n) -> mgb_status {
@@ -1095,15 +985,9 @@ static mgb_status alloc_tc_act(mgb_ctx *c, int rows, int kmax, QAct &a, std::vec
         CK(cudaMemsetAsync(*p, 0, n, c->stream));
         return MGB_OK;
     };
-    const size_t rec = std::max((size_t)(nbm / 8) * rp * 32, (size_t)nbm * rp * 4);
-    TRY(A((void **)&a.tq, (size_t)nbm * 2 * rp * 32));
-    TRY(A((void **)&a.trec, rec));
+    TRY(A((void **)&a.tq, (size_t)nbm * rp * 32));
+    TRY(A((void **)&a.trec, (size_t)nbm * rp * 8));
     a.rs = rp;
-    // row-major q8 activations of the other matmul kernels (F32 and encoder fallbacks)
-    TRY(A((void **)&a.q, (size_t)rp * kmax));
-    TRY(A((void **)&a.d, (size_t)4 * rp * nbm));
-    TRY(A((void **)&a.s32, (size_t)4 * rp * nbm));
-    TRY(A((void **)&a.s16, (size_t)8 * rp * nbm));
     return MGB_OK;
 }
 
@@ -1154,20 +1038,15 @@ static mgb_status new_state(mgb_ctx *c, int b, int s, int m, StaticState **out) 
     }
     TRY(A((void **)&st->part_v, (size_t)4 * b * kLmParts));
     TRY(A((void **)&st->part_i, (size_t)4 * b * kLmParts));
-    if (b >= c->tc_min_rows) {
+    if (b > kSmallRows && tc_ok(c->dec[0].qkv)) {
         TRY(alloc_tc_act(c, b, std::max(d, g.dec_ffn), st->act, st->allocs, &st->bytes));
-        TRY(alloc_tc_act(c, b, std::max(d, g.dec_ffn), st->act2, st->allocs, &st->bytes));
-        // one counter per (token tile of 8 rows, 256-row super-block) covers every post step
-        st->counter_bytes = (size_t)4 * ((b + 7) / 8) * std::max(1, std::max(d, g.dec_ffn) / 256);
-        TRY(A((void **)&st->counters, st->counter_bytes));
-        CK(cudaMemsetAsync(st->counters, 0, st->counter_bytes, c->stream));
         // split-K: the largest (rows x units) of the step's matrices, rows padded to 64
-        size_t pf = 0;
+        size_t pu = 0;
         for (const DecLayer &L : c->dec)
             for (const Matrix *M : {&L.qkv, &L.out, &L.cq, &L.co, &L.up, &L.down})
-                pf = std::max(pf, (size_t)M->Np * ((b + 63) / 64 * 64) * (M->type == T_Q8_0 ? M->nb : std::max(1, M->nsb)));
-        st->split.part_floats = pf;
-        TRY(A((void **)&st->split.part, 4 * pf));
+                pu = std::max(pu, (size_t)M->Np * ((b + 63) / 64 * 64) * (M->type == T_Q8_0 ? M->nb : M->nb / 2));
+        st->split.part_units = pu;
+        TRY(A((void **)&st->split.part, 8 * pu));
         TRY(A((void **)&st->split.count, 4 * 4096));
         CK(cudaMemsetAsync(st->split.count, 0, 4 * 4096, c->stream));
     }
@@ -1175,211 +1054,43 @@ static mgb_status new_state(mgb_ctx *c, int b, int s, int m, StaticState **out) 
     return MGB_OK;
 }
 
-// Whether the small-batch out / cross-out matmul computes the attention itself
-// (prologue of the staged matmul: every CTA recomputes all heads of its rows,
-// which costs little at 1-2 rows and saves the attention launch).
-static bool attn_in_matmul(const mgb_ctx *c, const Matrix &W, int b, const AttnArgs &a) {
-    if (b > c->attn_fuse_rows || b >= c->tc_min_rows) return false;
-    if (W.type != T_Q8_0 && W.type != T_Q4_K && W.type != T_Q6_K) return false;
-    if (a.queries != 1 || (a.hd != 64 && a.hd != 128)) return false;
-    const size_t sh = staged_bytes(W.type, W.nb, W.nsb) + smact_bytes(b, W.K, false) +
-                      staged_partial_bytes(W.type, b, W.nb) + attn_prologue_bytes(a.max_keys, a.hd);
-    return sh <= 200 * 1024 && (size_t)b * W.K * 4 <= staged_partial_bytes(W.type, b, W.nb);
+static PrepArgs prep_src(const float *x, const Norm *n) {
+    PrepArgs p{};
+    p.x = x;
+    if (n) {
+        p.gamma = n->g;
+        p.beta = n->b;
+    }
+    return p;
 }
 
-// One matmul of the step: from tc_min_rows rows the tcgen05 matmul, which
-// builds its LayerNorm / embedding / plain activations itself (rows of at most
-// 2048 values under LayerNorm, token tiles that fit in shared memory; others go
-// through qprep_row first); otherwise the fused small-batch kernel.
+static GemvArgs mm_out(const Matrix &W, int rows) {
+    GemvArgs g{};
+    g.W = W;
+    g.rows = rows;
+    return g;
+}
+
+// A matmul of the decode step or the encoder: the reference's MMVQ arithmetic
+// (small-batch kernel) for at most 8 rows or F32 weights, else MMQ on the tensor
+// cores with the activations prepared by qprep_row into `act`.
 template <int EPI, int MODE>
-static mgb_status step_op(mgb_ctx *c, StaticState *st, const FusedArgs &f, int *ctas = nullptr) {
-    const int b = f.g.rows;
-    if constexpr (MODE == PREP_ATTN) return fused<EPI, MODE>(c, f);  // staged small-batch matmul only
-    if (b >= c->tc_min_rows && tc_ok(f.g.W)) {
-        PrepArgs p = f.p;
-        p.rows = b;
-        p.K = f.g.W.K;
-        int nt, grid;
-        if (c->tc_fused && (MODE == PREP_PLAIN || f.g.W.K <= 2048) &&
-            tc_shape(f.g.W, std::min(b, EPI == EPI_ARGMAX ? 64 : b), c->sms, true, c->smem_optin, c->tc_min_nt, nt,
-                     grid))
-            return gemm_tc<EPI, MODE>(c, f.g.W, nullptr, &p, b, f.g, ctas);
-        if (!st->act.tq) return set_err(MGB_ERR_INVALID, "tensor-core activation buffers missing");
-        TRY(qprep_row<MODE>(c, p, st->act, f.g.W));
-        return gemm_tc<EPI, -1>(c, f.g.W, &st->act, nullptr, b, f.g, ctas);
-    }
-    if (ctas) *ctas = kLmParts;
-    return fused<EPI, MODE>(c, f);
+static mgb_status matmul(mgb_ctx *c, const GemvArgs &g, const PrepArgs &p, const QAct *act, int *ctas = nullptr,
+                         const SplitBufs *split = nullptr) {
+    if (g.rows <= kSmallRows || !tc_ok(g.W)) return small_mm<EPI, MODE>(c, g, p, ctas);
+    if (!act || !act->tq) return set_err(MGB_ERR_INVALID, "tensor-core activation buffers missing");
+    PrepArgs pp = p;
+    pp.rows = g.rows;
+    pp.K = g.W.K;
+    TRY(qprep_row<MODE>(c, pp, *act));
+    return gemm_tc<EPI>(c, g.W, *act, g.rows, g, ctas, split);
 }
 
-// The decode step on the tensor cores (batches of tc_min_rows rows or more).
-// Every matmul reads activations in the tensor-core layout from one of two
-// buffers and the producer of its input writes them there: the LayerNorm
-// inputs by the previous matmul's last CTA per token tile (post step), the
-// attention outputs by the attention kernel, the FFN hidden layer by the up
-// projection per super-block; layer 0's embedding input by qprep_row. Where a
-// shape does not allow that, qprep_row prepares the input instead.
-static mgb_status launch_step_tc(mgb_ctx *c, StaticState *st, float *logits, int force, cudaEvent_t lm0,
-                                 cudaEvent_t lm1, bool finalize) {
+static mgb_status finalize(mgb_ctx *c, StaticState *st, int parts, int force) {
     const Config &g = c->cfg;
-    const int b = st->b, d = g.d, H = g.dec_heads, hd = d / H;
-    QAct *X = &st->act, *Y = &st->act2;  // X: input of the next matmul in program order
-    const SplitBufs *sp = c->tc_split ? &st->split : nullptr;
-    auto plain = [&](const float *x, int K) {
-        PrepArgs p{};
-        p.x = x;
-        p.rows = b;
-        p.K = K;
-        return p;
-    };
-    auto gemv = [&](const Matrix &W) {
-        GemvArgs gg{};
-        gg.W = W;
-        gg.rows = b;
-        return gg;
-    };
-    // post step of a matmul whose output (rows of width W.N) feeds `next`
-    auto post_for = [&](int mode, const Matrix &W, const Norm *nrm, const Matrix &next, QAct *dst, tc::Post &po) {
-        po = tc::Post{};
-        if (!MGB_TC_POST_STEPS || !c->tc_post || !tc_ok(next)) return false;
-        if (mode == PREP_LN && W.N > 2048) return false;
-        if (mode == PREP_PLAIN && (W.N % 256 || (W.Np / 128) % 2)) return false;
-        po.mode = mode;
-        if (nrm) {
-            po.gamma = nrm->g;
-            po.beta = nrm->b;
-        }
-        po.group = act_group(next.type);
-        po.ctype = next.type;
-        po.out = *dst;
-        po.counters = st->counters;
-        return true;
-    };
-    // prepare `next`'s input from f32 rows when no producer did it
-    auto prep = [&](int mode, const float *x, int K, const Norm *nrm, const Matrix &next, QAct *dst) -> mgb_status {
-        PrepArgs p = plain(x, K);
-        if (nrm) {
-            p.gamma = nrm->g;
-            p.beta = nrm->b;
-        }
-        return mode == PREP_LN ? qprep_row<PREP_LN>(c, p, *dst, next) : qprep_row<PREP_PLAIN>(c, p, *dst, next);
-    };
-    // attention that also quantizes its outputs for `next` when the shape allows
-    auto attn_q = [&](AttnArgs aa, const Matrix &next, QAct *dst) -> mgb_status {
-        const int G = act_group(next.type);
-        const bool ok = c->tc_attn_q && tc_ok(next) && aa.queries == 1 && H % 4 == 0 && hd <= 128 &&
-                        (4 * hd) % (32 * G) == 0;
-        if (ok) {
-            aa.qo = *dst;
-            aa.qo_ctype = next.type;
-        }
-        TRY(attend<__half>(c, aa));
-        if (!ok) TRY(prep(PREP_PLAIN, aa.out, d, nullptr, next, dst));
-        return MGB_OK;
-    };
-    for (int l = 0; l < g.dec_layers; ++l) {
-        const DecLayer &L = c->dec[l];
-        if (l == 0) {
-            PrepArgs p = plain(st->x, d);
-            p.gamma = L.attn_norm.g;
-            p.beta = L.attn_norm.b;
-            p.x_out = st->x;
-            p.embed = c->embed;
-            p.ids = st->ids;
-            p.step = st->step;
-            p.pos_table = c->pos;
-            p.pos_base = (uint32_t)g.pad + 1;
-            p.scale = c->embed_scale;
-            TRY(qprep_row<PREP_EMBED_LN>(c, p, *X, L.qkv));
-        }
-        // (X holds attn_norm(x) for qkv)
-        GemvArgs gq = gemv(L.qkv);
-        gq.q = st->q;
-        gq.kc = st->kc[l];
-        gq.vc = st->vc[l];
-        gq.step = st->step;
-        gq.H = H;
-        gq.hd = hd;
-        gq.m = st->m;
-        TRY((gemm_tc<EPI_QKV, -1>(c, L.qkv, X, nullptr, b, gq, nullptr, nullptr, sp)));
-        AttnArgs sa{};
-        sa.q = st->q;
-        sa.q_row = d;
-        sa.K = st->kc[l];
-        sa.V = st->vc[l];
-        sa.kv_row = hd;
-        sa.kv_head = (long)st->m * hd;
-        sa.kv_batch = (long)H * st->m * hd;
-        sa.step = st->step;
-        sa.out = st->a;
-        sa.out_row = d;
-        sa.H = H;
-        sa.hd = hd;
-        sa.rows = b;
-        sa.queries = 1;
-        sa.max_keys = st->m;
-        TRY(attn_q(sa, L.out, Y));
-        std::swap(X, Y);
-        // out projection + residual; its post step: cross_norm(x) for cross_q
-        tc::Post po;
-        GemvArgs go = gemv(L.out);
-        go.y = st->x;
-        bool posted = post_for(PREP_LN, L.out, &L.cross_norm, L.cq, Y, po);
-        TRY((gemm_tc<EPI_RESID, -1>(c, L.out, X, nullptr, b, go, nullptr, posted ? &po : nullptr, sp)));
-        if (!posted) TRY(prep(PREP_LN, st->x, d, &L.cross_norm, L.cq, Y));
-        std::swap(X, Y);
-        GemvArgs gc = gemv(L.cq);
-        gc.y = st->q;
-        TRY((gemm_tc<EPI_STORE, -1>(c, L.cq, X, nullptr, b, gc, nullptr, nullptr, sp)));
-        AttnArgs ca = sa;
-        ca.K = st->ck[l];
-        ca.V = st->cv[l];
-        ca.kv_head = (long)st->s * hd;
-        ca.kv_batch = (long)H * st->s * hd;
-        ca.step = nullptr;
-        ca.lens = st->lens;
-        ca.max_keys = st->s;
-        TRY(attn_q(ca, L.co, Y));
-        std::swap(X, Y);
-        // cross out + residual; post: ffn_norm(x) for up
-        GemvArgs gco = gemv(L.co);
-        gco.y = st->x;
-        posted = post_for(PREP_LN, L.co, &L.ffn_norm, L.up, Y, po);
-        TRY((gemm_tc<EPI_RESID, -1>(c, L.co, X, nullptr, b, gco, nullptr, posted ? &po : nullptr, sp)));
-        if (!posted) TRY(prep(PREP_LN, st->x, d, &L.ffn_norm, L.up, Y));
-        std::swap(X, Y);
-        // up + ReLU; post: the hidden layer per super-block for down
-        GemvArgs gu = gemv(L.up);
-        gu.y = st->u;
-        posted = post_for(PREP_PLAIN, L.up, nullptr, L.down, Y, po);
-        TRY((gemm_tc<EPI_RELU, -1>(c, L.up, X, nullptr, b, gu, nullptr, posted ? &po : nullptr, sp)));
-        if (!posted) TRY(prep(PREP_PLAIN, st->u, g.dec_ffn, nullptr, L.down, Y));
-        std::swap(X, Y);
-        // down + residual; post: the next layer's attn_norm(x), or dec_norm(x) for the LM head
-        const bool last = l + 1 == g.dec_layers;
-        const Norm &nn = last ? c->dec_norm : c->dec[l + 1].attn_norm;
-        const Matrix &nm = last ? c->embed : c->dec[l + 1].qkv;
-        GemvArgs gd = gemv(L.down);
-        gd.y = st->x;
-        posted = post_for(PREP_LN, L.down, &nn, nm, Y, po);
-        TRY((gemm_tc<EPI_RESID, -1>(c, L.down, X, nullptr, b, gd, nullptr, posted ? &po : nullptr, sp)));
-        if (!posted) TRY(prep(PREP_LN, st->x, d, &nn, nm, Y));
-        std::swap(X, Y);
-    }
-    // tied LM head fused with the first argmax pass, then greedy bookkeeping
-    GemvArgs gl = gemv(c->embed);
-    gl.part_v = st->part_v;
-    gl.part_i = st->part_i;
-    gl.logits = logits;
-    if (lm0) CK(cudaEventRecord(lm0, c->stream));
-    int parts = kLmParts;
-    TRY((gemm_tc<EPI_ARGMAX, -1>(c, c->embed, X, nullptr, b, gl, &parts)));
-    st->lm_parts = parts;
-    if (lm1) CK(cudaEventRecord(lm1, c->stream));
-    if (!finalize) return MGB_OK;
-    const int threads = std::min(1024, std::max(32, 32 * b));
+    const int threads = std::min(1024, std::max(32, 32 * st->b));
     cudaError_t e = launch_pdl(greedy_finalize_kernel, dim3(1), dim3(threads), 0, c->stream,
-                               (const float *)st->part_v, (const uint32_t *)st->part_i, parts, b,
+                               (const float *)st->part_v, (const uint32_t *)st->part_i, parts, st->b,
                                st->finished, st->ids, st->out, st->m, st->step, (uint32_t)g.eos, (uint32_t)g.pad,
                                force);
     ++c->launches;
@@ -1388,53 +1099,45 @@ static mgb_status launch_step_tc(mgb_ctx *c, StaticState *st, float *logits, int
 }
 
 // One greedy decoder step on the state's fixed buffers (model.rs:552-612):
-// 6 fused matmuls + 2 attentions per layer, the LM head with argmax, finalize.
+// per layer fused QKV (+ f16 K/V cache write), self-attention, out-proj +
+// residual, cross-q, cross-attention, cross-out + residual, FFN up + ReLU,
+// down + residual, every LayerNorm folded into the next matmul's activation
+// prologue; then the tied LM head fused with the first argmax pass, finalize.
+// Up to 8 rows the matmuls are the small-batch kernel (MMVQ); above, the
+// tensor-core kernel (MMQ) reads q8_1 activations that qprep_row, or for the
+// out projections the attention kernel itself, writes into one of two buffers.
 static mgb_status launch_step(mgb_ctx *c, StaticState *st, float *logits, int force,
-                              cudaEvent_t lm0 = nullptr, cudaEvent_t lm1 = nullptr, bool finalize = true) {
-    if (st->b >= c->tc_min_rows && st->act.tq && !c->tc_fused && tc_ok(c->embed) && tc_ok(c->dec[0].qkv))
-        return launch_step_tc(c, st, logits, force, lm0, lm1, finalize);
+                              cudaEvent_t lm0 = nullptr, cudaEvent_t lm1 = nullptr, bool finalize_step = true) {
     const Config &g = c->cfg;
     const int b = st->b, d = g.d, H = g.dec_heads, hd = d / H;
-    auto src = [&](const float *x, int K, const Norm *n) {
-        PrepArgs p{};
-        p.x = x;
-        p.rows = b;
-        p.K = K;
-        if (n) {
-            p.gamma = n->g;
-            p.beta = n->b;
-        }
-        return p;
-    };
-    auto mm = [&](const Matrix &W) {
-        FusedArgs f{};
-        f.g.W = W;
-        f.g.rows = b;
-        return f;
-    };
+    const bool tc = b > kSmallRows;
+    const SplitBufs *sp = tc && c->tc_split ? &st->split : nullptr;
+    QAct *X = &st->act;  // tensor-core activations of the next matmul
+    // attention whose outputs also go, as q8_1, into the next matmul's input
+    const bool attn_q = tc && hd % 32 == 0;
     for (int l = 0; l < g.dec_layers; ++l) {
         const DecLayer &L = c->dec[l];
         // attn_norm(x) (layer 0: x = E[id]*scale + pos) -> fused QKV -> q, K/V cache slot *step
-        FusedArgs fq = mm(L.qkv);
-        fq.p = src(st->x, d, &L.attn_norm);
-        fq.g.q = st->q;
-        fq.g.kc = st->kc[l];
-        fq.g.vc = st->vc[l];
-        fq.g.step = st->step;
-        fq.g.H = H;
-        fq.g.hd = hd;
-        fq.g.m = st->m;
+        GemvArgs gq = mm_out(L.qkv, b);
+        gq.q = st->q;
+        gq.kc = st->kc[l];
+        gq.vc = st->vc[l];
+        gq.step = st->step;
+        gq.H = H;
+        gq.hd = hd;
+        gq.m = st->m;
+        PrepArgs pq = prep_src(st->x, &L.attn_norm);
         if (l == 0) {
-            fq.p.x_out = st->x;
-            fq.p.embed = c->embed;
-            fq.p.ids = st->ids;
-            fq.p.step = st->step;
-            fq.p.pos_table = c->pos;
-            fq.p.pos_base = (uint32_t)g.pad + 1;
-            fq.p.scale = c->embed_scale;
-            TRY((step_op<EPI_QKV, PREP_EMBED_LN>(c, st, fq)));
+            pq.x_out = st->x;
+            pq.embed = c->embed;
+            pq.ids = st->ids;
+            pq.step = st->step;
+            pq.pos_table = c->pos;
+            pq.pos_base = (uint32_t)g.pad + 1;
+            pq.scale = c->embed_scale;
+            TRY((matmul<EPI_QKV, PREP_EMBED_LN>(c, gq, pq, X, nullptr, sp)));
         } else {
-            TRY((step_op<EPI_QKV, PREP_LN>(c, st, fq)));
+            TRY((matmul<EPI_QKV, PREP_LN>(c, gq, pq, X, nullptr, sp)));
         }
         AttnArgs sa{};
         sa.q = st->q;
@@ -1452,21 +1155,16 @@ static mgb_status launch_step(mgb_ctx *c, StaticState *st, float *logits, int fo
         sa.rows = b;
         sa.queries = 1;
         sa.max_keys = st->m;
-        FusedArgs fo = mm(L.out);
-        fo.p = src(st->a, d, nullptr);
-        fo.g.y = st->x;
-        if (attn_in_matmul(c, L.out, b, sa)) {
-            fo.at = sa;
-            TRY((step_op<EPI_RESID, PREP_ATTN>(c, st, fo)));
-        } else {
-            TRY(attend<__half>(c, sa));
-            TRY((step_op<EPI_RESID, PREP_PLAIN>(c, st, fo)));
-        }
+        if (attn_q) sa.qo = *X;
+        TRY(attend<__half>(c, sa));
+        GemvArgs go = mm_out(L.out, b);
+        go.y = st->x;
+        if (attn_q) TRY(gemm_tc<EPI_RESID>(c, L.out, *X, b, go, nullptr, sp));
+        else TRY((matmul<EPI_RESID, PREP_PLAIN>(c, go, prep_src(st->a, nullptr), X, nullptr, sp)));
         // cross_norm -> cross_q -> cross attention -> cross_out + residual
-        FusedArgs fc = mm(L.cq);
-        fc.p = src(st->x, d, &L.cross_norm);
-        fc.g.y = st->q;
-        TRY((step_op<EPI_STORE, PREP_LN>(c, st, fc)));
+        GemvArgs gc = mm_out(L.cq, b);
+        gc.y = st->q;
+        TRY((matmul<EPI_STORE, PREP_LN>(c, gc, prep_src(st->x, &L.cross_norm), X, nullptr, sp)));
         AttnArgs ca = sa;
         ca.K = st->ck[l];
         ca.V = st->cv[l];
@@ -1475,67 +1173,51 @@ static mgb_status launch_step(mgb_ctx *c, StaticState *st, float *logits, int fo
         ca.step = nullptr;
         ca.lens = st->lens;
         ca.max_keys = st->s;
-        FusedArgs fco = mm(L.co);
-        fco.p = src(st->a, d, nullptr);
-        fco.g.y = st->x;
-        if (attn_in_matmul(c, L.co, b, ca)) {
-            fco.at = ca;
-            TRY((step_op<EPI_RESID, PREP_ATTN>(c, st, fco)));
-        } else {
-            TRY(attend<__half>(c, ca));
-            TRY((step_op<EPI_RESID, PREP_PLAIN>(c, st, fco)));
-        }
+        TRY(attend<__half>(c, ca));
+        GemvArgs gco = mm_out(L.co, b);
+        gco.y = st->x;
+        if (attn_q) TRY(gemm_tc<EPI_RESID>(c, L.co, *X, b, gco, nullptr, sp));
+        else TRY((matmul<EPI_RESID, PREP_PLAIN>(c, gco, prep_src(st->a, nullptr), X, nullptr, sp)));
         // ffn_norm -> up + ReLU -> down + residual
-        FusedArgs fu = mm(L.up);
-        fu.p = src(st->x, d, &L.ffn_norm);
-        fu.g.y = st->u;
-        TRY((step_op<EPI_RELU, PREP_LN>(c, st, fu)));
-        FusedArgs fd = mm(L.down);
-        fd.p = src(st->u, g.dec_ffn, nullptr);
-        fd.g.y = st->x;
-        TRY((step_op<EPI_RESID, PREP_PLAIN>(c, st, fd)));
+        GemvArgs gu = mm_out(L.up, b);
+        gu.y = st->u;
+        TRY((matmul<EPI_RELU, PREP_LN>(c, gu, prep_src(st->x, &L.ffn_norm), X, nullptr, sp)));
+        GemvArgs gd = mm_out(L.down, b);
+        gd.y = st->x;
+        TRY((matmul<EPI_RESID, PREP_PLAIN>(c, gd, prep_src(st->u, nullptr), X, nullptr, sp)));
     }
     // dec_norm -> tied LM head fused with the first argmax pass -> greedy bookkeeping
-    FusedArgs fl = mm(c->embed);
-    fl.p = src(st->x, d, &c->dec_norm);
-    fl.g.part_v = st->part_v;
-    fl.g.part_i = st->part_i;
-    fl.g.logits = logits;
+    GemvArgs gl = mm_out(c->embed, b);
+    gl.part_v = st->part_v;
+    gl.part_i = st->part_i;
+    gl.logits = logits;
     if (lm0) CK(cudaEventRecord(lm0, c->stream));
     int parts = kLmParts;
-    TRY((step_op<EPI_ARGMAX, PREP_LN>(c, st, fl, &parts)));
+    TRY((matmul<EPI_ARGMAX, PREP_LN>(c, gl, prep_src(st->x, &c->dec_norm), X, &parts)));
     st->lm_parts = parts;
     if (lm1) CK(cudaEventRecord(lm1, c->stream));
-    if (!finalize) return MGB_OK;
-    const int threads = std::min(1024, std::max(32, 32 * b));
-    cudaError_t e = launch_pdl(greedy_finalize_kernel, dim3(1), dim3(threads), 0, c->stream,
-                               (const float *)st->part_v, (const uint32_t *)st->part_i, parts, b,
-                               st->finished, st->ids, st->out, st->m, st->step, (uint32_t)g.eos, (uint32_t)g.pad,
-                               force);
-    ++c->launches;
-    if (e != cudaSuccess) return cuda_err(e, "finalize launch");
-    return MGB_OK;
+    if (!finalize_step) return MGB_OK;
+    return finalize(c, st, parts, force);
 }
 
 // ---------------------------------------------------------------------------
 // Encoder (model.rs:463-500)
 
+// ids: [b][S] right-padded, S = the longest sentence (pad_batch, model.rs:480-500;
+// the matmuls then see b*S rows, as the reference's).
 static mgb_status encode(mgb_ctx *c, const uint32_t *ids, const uint32_t *lens, int b, int S, mgb_batch **out) {
     const Config &g = c->cfg;
     const int d = g.d, H = g.enc_heads, hd = d / H, rows = b * S, ffn = g.enc_ffn, kmax = std::max(d, ffn);
     uint32_t *d_ids, *d_lens;
-    float *x, *qkv, *a, *u, *xf = nullptr;
+    float *x, *qkv, *a, *u;
     QAct act;
-    const bool f32 = any_f32(c);
     // temporaries carved from the context's encoder workspace (grown, never
     // shrunk, released by mgb_clear_cache / mgb_close): no allocation per call
     {
         const int rp = (rows + 63) / 64 * 64, nbm = kmax / 32;
         const size_t sz[] = {(size_t)4 * rows, (size_t)4 * b, (size_t)4 * rows * d, (size_t)4 * rows * 3 * d,
-                             (size_t)4 * rows * d, (size_t)4 * rows * ffn, f32 ? (size_t)4 * rows * kmax : 0,
-                             (size_t)nbm * 2 * rp * 32,
-                             std::max((size_t)(nbm / 8) * rp * 32, (size_t)nbm * rp * 4),
-                             (size_t)rp * kmax, (size_t)4 * rp * nbm, (size_t)4 * rp * nbm, (size_t)8 * rp * nbm};
+                             (size_t)4 * rows * d, (size_t)4 * rows * ffn, (size_t)nbm * rp * 32, (size_t)nbm * rp * 8};
+        constexpr int NP = sizeof sz / sizeof sz[0];
         size_t total = 0;
         for (size_t n : sz) total += (n + 255) / 256 * 256;
         if (total > c->enc_ws_bytes) {
@@ -1546,9 +1228,9 @@ static mgb_status encode(mgb_ctx *c, const uint32_t *ids, const uint32_t *lens, 
             c->enc_ws_bytes = total;
         }
         uint8_t *w = reinterpret_cast<uint8_t *>(c->enc_ws);
-        void *ptrs[13];
-        for (int i = 0; i < 13; ++i) {
-            ptrs[i] = sz[i] ? w : nullptr;
+        void *ptrs[NP];
+        for (int i = 0; i < NP; ++i) {
+            ptrs[i] = w;
             w += (sz[i] + 255) / 256 * 256;
         }
         d_ids = (uint32_t *)ptrs[0];
@@ -1557,13 +1239,8 @@ static mgb_status encode(mgb_ctx *c, const uint32_t *ids, const uint32_t *lens, 
         qkv = (float *)ptrs[3];
         a = (float *)ptrs[4];
         u = (float *)ptrs[5];
-        xf = (float *)ptrs[6];
-        act.tq = (uint8_t *)ptrs[7];
-        act.trec = (uint8_t *)ptrs[8];
-        act.q = (int8_t *)ptrs[9];
-        act.d = (float *)ptrs[10];
-        act.s32 = (int *)ptrs[11];
-        act.s16 = (int *)ptrs[12];
+        act.tq = (uint8_t *)ptrs[6];
+        act.trec = (float2 *)ptrs[7];
         act.rs = rp;
     }
     CK(cudaMemcpyAsync(d_ids, ids, (size_t)4 * rows, cudaMemcpyHostToDevice, c->stream));
@@ -1572,32 +1249,11 @@ static mgb_status encode(mgb_ctx *c, const uint32_t *ids, const uint32_t *lens, 
         embed_tokens_kernel<<<(rows + 7) / 8, 256, 0, c->stream>>>(c->embed, d_ids, d_lens, S, rows, c->pos,
                                                                    (uint32_t)g.pad, c->embed_scale, x);
     }));
-    // One encoder matmul: tensor cores for quantized weights, else the
-    // row-per-lane kernel over activations quantized in global memory.
-    auto enc_mm = [&](int epi, int mode, const Matrix &W, const float *in, const Norm *nrm, GemvArgs gg) -> mgb_status {
-        PrepArgs p = prep_args(act, xf, f32, in, rows, W.K);
-        if (nrm) {
-            p.gamma = nrm->g;
-            p.beta = nrm->b;
-        }
-        if (tc_ok(W)) {
-            TRY(mode == PREP_LN ? qprep_row<PREP_LN>(c, p, act, W) : qprep_row<PREP_PLAIN>(c, p, act, W));
-            switch (epi) {
-                case EPI_STORE: return gemm_tc<EPI_STORE, -1>(c, W, &act, nullptr, rows, gg);
-                case EPI_RELU: return gemm_tc<EPI_RELU, -1>(c, W, &act, nullptr, rows, gg);
-                case EPI_RESID: return gemm_tc<EPI_RESID, -1>(c, W, &act, nullptr, rows, gg);
-                default: return gemm_tc<EPI_CROSSKV, -1>(c, W, &act, nullptr, rows, gg);
-            }
-        }
-        p.group = act_group(W.type);
-        TRY(qprep(c, mode, p));
-        return gemv(c, epi, gg);
-    };
     for (int l = 0; l < g.enc_layers; ++l) {
         const EncLayer &L = c->enc[l];
-        GemvArgs gq = gemv_args(L.qkv, act, xf, rows);
+        GemvArgs gq = mm_out(L.qkv, rows);
         gq.y = qkv;
-        TRY(enc_mm(EPI_STORE, PREP_LN, L.qkv, x, &L.attn_norm, gq));
+        TRY((matmul<EPI_STORE, PREP_LN>(c, gq, prep_src(x, &L.attn_norm), &act)));
         AttnArgs at{};
         at.q = qkv;
         at.q_row = 3 * d;
@@ -1615,23 +1271,16 @@ static mgb_status encode(mgb_ctx *c, const uint32_t *ids, const uint32_t *lens, 
         at.queries = S;
         at.max_keys = S;
         TRY(attend<float>(c, at));
-        GemvArgs go = gemv_args(L.out, act, xf, rows);
+        GemvArgs go = mm_out(L.out, rows);
         go.y = x;
-        TRY(enc_mm(EPI_RESID, PREP_PLAIN, L.out, a, nullptr, go));
-        GemvArgs gu = gemv_args(L.up, act, xf, rows);
+        TRY((matmul<EPI_RESID, PREP_PLAIN>(c, go, prep_src(a, nullptr), &act)));
+        GemvArgs gu = mm_out(L.up, rows);
         gu.y = u;
-        TRY(enc_mm(EPI_RELU, PREP_LN, L.up, x, &L.ffn_norm, gu));
-        GemvArgs gd = gemv_args(L.down, act, xf, rows);
+        TRY((matmul<EPI_RELU, PREP_LN>(c, gu, prep_src(x, &L.ffn_norm), &act)));
+        GemvArgs gd = mm_out(L.down, rows);
         gd.y = x;
-        TRY(enc_mm(EPI_RESID, PREP_PLAIN, L.down, u, nullptr, gd));
+        TRY((matmul<EPI_RESID, PREP_PLAIN>(c, gd, prep_src(u, nullptr), &act)));
     }
-    // enc_norm(x) is the input of every decoder layer's cross K/V projection
-    PrepArgs pn = prep_args(act, xf, f32, x, rows, d);
-    pn.gamma = c->enc_norm.g;
-    pn.beta = c->enc_norm.b;
-    const bool kv_tc = tc_ok(c->dec[0].ckv);
-    pn.group = act_group(c->dec[0].ckv.type);
-    TRY(kv_tc ? qprep_row<PREP_LN>(c, pn, act, c->dec[0].ckv) : qprep(c, PREP_LN, pn));
     auto B = std::make_unique<mgb_batch>();
     B->b = b;
     B->s = S;
@@ -1649,20 +1298,30 @@ static mgb_status encode(mgb_ctx *c, const uint32_t *ids, const uint32_t *lens, 
     }
     B->d_lens = (uint32_t *)dl;
     CK(cudaMemcpyAsync(B->d_lens, lens, (size_t)4 * b, cudaMemcpyHostToDevice, c->stream));
-    for (int l = 0; l < g.dec_layers; ++l) {
-        GemvArgs gk = gemv_args(c->dec[l].ckv, act, xf, rows);
+    // enc_norm(x) is the input of every decoder layer's cross K/V projection
+    // (model.rs:471-475); its q8_1 activations are prepared once
+    const PrepArgs pn = prep_src(x, &c->enc_norm);
+    const bool tc = rows > kSmallRows && tc_ok(c->dec[0].ckv);
+    if (tc) {
+        PrepArgs pp = pn;
+        pp.rows = rows;
+        pp.K = d;
+        s = qprep_row<PREP_LN>(c, pp, act);
+    }
+    for (int l = 0; l < g.dec_layers && s == MGB_OK; ++l) {
+        GemvArgs gk = mm_out(c->dec[l].ckv, rows);
         gk.kc = B->cross + per * (2 * l);
         gk.vc = B->cross + per * (2 * l + 1);
         gk.H = Hd;
         gk.hd = hdd;
         gk.S = S;
-        mgb_status s2 = tc_ok(c->dec[l].ckv) ? gemm_tc<EPI_CROSSKV, -1>(c, c->dec[l].ckv, &act, nullptr, rows, gk)
-                                             : gemv(c, EPI_CROSSKV, gk);
-        if (s2 != MGB_OK) {
-            cudaFree(B->cross);
-            cudaFree(B->d_lens);
-            return s2;
-        }
+        s = tc && tc_ok(c->dec[l].ckv) ? gemm_tc<EPI_CROSSKV>(c, c->dec[l].ckv, act, rows, gk)
+                                       : small_mm<EPI_CROSSKV, PREP_LN>(c, gk, pn);
+    }
+    if (s != MGB_OK) {
+        cudaFree(B->cross);
+        cudaFree(B->d_lens);
+        return s;
     }
     uint32_t derr = 0;
     CK(cudaMemcpyAsync(&derr, c->d_err, 4, cudaMemcpyDeviceToHost, c->stream));
@@ -1762,7 +1421,6 @@ static mgb_status acquire_state(mgb_ctx *c, const mgb_batch *B, int max_new, boo
     for (int i = 0; i < n; ++i) lens[i] = B->lens[i / rep];
     CK(cudaMemcpyAsync(st->lens, lens.data(), 4 * b, cudaMemcpyHostToDevice, c->stream));
     CK(cudaMemsetAsync(st->step, 0, 4, c->stream));
-    if (st->counters) CK(cudaMemsetAsync(st->counters, 0, st->counter_bytes, c->stream));
     if (st->split.count) CK(cudaMemsetAsync(st->split.count, 0, 4 * 4096, c->stream));
     TRY(set_ids(c, st, (uint32_t)g.start));
     TRY(reset_finished(c, st, n));
@@ -2111,15 +1769,10 @@ mgb_status mgb_open(const char *path, int device, const mgb_options *opts, mgb_c
     if (opts) c->opts = *opts;
     else mgb_default_options(&c->opts);
     CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
-    if (const char *v = getenv("MGB_TC_MIN_ROWS")) c->tc_min_rows = std::max(1, atoi(v));
     if (const char *v = getenv("MGB_TC_MIN_NT")) c->tc_min_nt = atoi(v);
-    if (const char *v = getenv("MGB_TC_FUSED")) c->tc_fused = atoi(v) != 0;
-    if (const char *v = getenv("MGB_TC_POST")) c->tc_post = atoi(v) != 0;
-    if (const char *v = getenv("MGB_TC_ATTN_Q")) c->tc_attn_q = atoi(v) != 0;
     if (const char *v = getenv("MGB_TC_SPLIT")) c->tc_split = atoi(v) != 0;
     if (const char *v = getenv("MGB_TC_SPLIT_STAGES")) c->tc_split_stages = std::max(1, atoi(v));
     if (const char *v = getenv("MGB_TC_SPLIT_MAX")) c->tc_split_max = std::max(1, atoi(v));
-    if (const char *v = getenv("MGB_ATTN_FUSE_ROWS")) c->attn_fuse_rows = atoi(v);
     cudaDeviceGetAttribute(&c->sms, cudaDevAttrMultiProcessorCount, device);
     if (c->sms <= 0) c->sms = 148;
     {
@@ -2195,7 +1848,14 @@ mgb_status mgb_encode(mgb_ctx *c, const uint32_t *ids, const uint32_t *lens, uin
                 return set_err(MGB_ERR_INVALID, "token id %u >= vocab %d", ids[(size_t)i * s + j], c->cfg.V);
     }
     CK(cudaSetDevice(c->device));
-    return encode(c, ids, lens, (int)b, (int)s, out);
+    // the reference pads a batch to its longest sentence (pad_batch,
+    // model.rs:480-500): repack a wider stride
+    uint32_t smax = 0;
+    for (uint32_t i = 0; i < b; ++i) smax = std::max(smax, lens[i]);
+    if (smax == s) return encode(c, ids, lens, (int)b, (int)s, out);
+    std::vector<uint32_t> packed((size_t)b * smax);
+    for (uint32_t i = 0; i < b; ++i) memcpy(&packed[(size_t)i * smax], ids + (size_t)i * s, 4 * (size_t)smax);
+    return encode(c, packed.data(), lens, (int)b, (int)smax, out);
 }
 
 void mgb_batch_free(mgb_batch *B) {

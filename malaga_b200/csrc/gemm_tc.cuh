@@ -1,20 +1,23 @@
 // Batched quantized matmul on the 5th-generation tensor cores (tcgen05, sm_100a).
 //
 // Replaces candle's MMQ path (QMatMul::forward for more than 8 activation rows,
-// model.rs:571-607, and the encoder's projections model.rs:137-154 / 463-477).
-// The arithmetic is the engine's (kernels.cuh, BlockW): per 32-block the
-// integer dot of weight and activation values is exact, so the tensor core
-// computes it (tcgen05.mma kind::i8, M = 128 weight rows x N = NT activation
-// rows x K = 32), each block into its own TMEM columns; the epilogue adds the
-// blocks of a unit (a 256-value super-block for Q4_K / Q6_K, one block for
-// Q8_0) in int32, applies the unit's float scales and sums the units left to
-// right, so the results are bit-identical to the small-batch kernels.
+// model.rs:571-607, and the encoder's projections model.rs:137-154 / 463-477;
+// candle-kernels 0.11.0 src/quantized.cu mul_mat_q). The arithmetic is MMQ's:
+// activations are q8_1 blocks (qprep_row_kernel, or the attention kernel), the
+// integer dot of weight and activation values per 32-block is exact, so the
+// tensor core computes it (tcgen05.mma kind::i8, M = 128 weight rows x N = NT
+// activation rows x K = 32, each block into its own TMEM columns; Q6_K twice,
+// once per 16-value half), and the epilogue forms MMQ's units -- Q8_0: one
+// block, fma(dw*dx, float(I), acc); Q4_K: a pair of sub-blocks,
+// acc + fma(d, sum dx*float(sc*I), -(dmin * sum sx*float(m))); Q6_K: a pair of
+// blocks, fma(d, sum dx*float(sa*Ia + sb*Ib), acc) -- summed from 0 in row
+// order, as each MMQ thread sums its outputs.
 //
 // One persistent CTA per SM walks its (128-row x NT-token) tiles in stages of
 // 8 blocks (256 values) with warp-specialized roles linked by mbarriers:
-//   warp 10     producer: one TMA tensor copy per weight region (and, when the
-//               activations come from global memory, one for their tiles and
-//               one for their scale records) into a ring of RS stages;
+//   warp 10     producer: one TMA tensor copy per weight region, one for the
+//               activation tiles and one for their {d, s} records, into a ring
+//               of RS stages;
 //   warps EW-9  converters (EW = 4 for tiles of at most 16 tokens, else 8):
 //               they unpack each block's 128 weight rows (Q4_K nibbles, Q6_K
 //               6-bit values minus 32, Q8_0 bytes), loads batched ahead of stores,
@@ -28,13 +31,8 @@
 //               stage to free the stage;
 //   warps 0..EW-1 epilogue: warp w reads TMEM lanes 32(w%4).. (its weight
 //               rows) for all (EW = 4) or half (EW = 8) of the tile's tokens,
-//               accumulates, and stores.
+//               forms the units, accumulates, and stores.
 // (12 warps: three per scheduler leave 168 registers per thread.)
-// Activations either arrive by TMA in the layout qprep_row_kernel writes (XM <
-// 0: the encoder's long inputs), or (XM = a PrepMode: the decode step) the
-// epilogue warps build the CTA's whole token tile in shared memory first
-// (LayerNorm / embedding / plain input, quantized in the engine's order), so
-// no separate activation kernel runs. A CTA then serves one token tile.
 // Roles hand over groups of BG blocks (2-8), one mbarrier operation per group.
 // Every mbarrier wait is bounded in time; when one runs out the CTA records an
 // error flag, every role stops, and the CTA waits for its own MMAs before it
@@ -42,7 +40,7 @@
 #pragma once
 #include <cuda.h>
 
-#include "fused.cuh"
+#include "kernels.cuh"
 
 namespace mgb {
 
@@ -127,40 +125,20 @@ struct Maps {
     CUtensorMap xq, xr;
 };
 
-// The next matmul's activations, written by the CTA that completes them
-// (RESID / RELU launches of the decode step): mode PREP_LN = LayerNorm of the
-// finished output rows, once every row tile of a token tile is done (the last
-// CTA of the token tile, found with an atomic counter); mode PREP_PLAIN = the
-// output quantized per 256-row super-block, once both row tiles of it are done.
-// mode < 0: none. Compiled only with MGB_TC_POST_STEPS=1: the decode step
-// measured slower with them, and their registers make the RESID / RELU
-// epilogues spill.
-#ifndef MGB_TC_POST_STEPS
-#define MGB_TC_POST_STEPS 0
-#endif
-struct Post {
-    int mode = -1;
-    const float *gamma = nullptr, *beta = nullptr;
-    int group = 1, ctype = 0;   // the consumer's activation format
-    QAct out;                   // the consumer's tensor-core layout (tq, trec, rs)
-    uint32_t *counters = nullptr;  // one per token tile (LN) or (token tile, super-block); zero between launches
-};
-
 struct Args {
     Maps m;
-    Post post;
     Matrix W;
     int rows;        // activation rows
     int row_tiles;   // Np / 128
     int tok_tiles;   // ceil(rows / NT)
     int tok0;        // first activation row (a multiple of 64) of this launch (TMA activations)
     GemvArgs g;      // epilogue outputs
-    PrepArgs p;      // activation source (activations built in the kernel)
-    // split-K (TMA activations): `splits` CTAs share a tile's stages; split 0
-    // keeps the running row sum, the others store their unit partials in kpart,
-    // and the last of them (kcount) continues the sum in unit order
+    // split-K: `splits` CTAs share a tile's stages; split 0 keeps the running
+    // row sum, the others store their units in kpart (Q8_0 / Q6_K: the two
+    // factors of the unit's fused multiply-add; Q4_K: its value), and the last
+    // of them (kcount) continues the sum in unit order
     int splits;
-    float *kpart;
+    float2 *kpart;
     uint32_t *kcount;
     uint32_t *err;
 };
@@ -178,8 +156,8 @@ struct MmaN {
     static_assert(N == NT || NT == 8, "narrow tile");
 };
 
-// Stage geometry per weight type, tile width and activation source.
-template <int TYPE, int NT, bool FX>
+// Stage geometry per weight type and tile width.
+template <int TYPE, int NT>
 struct Geo {
     static constexpr bool Q6 = TYPE == T_Q6_K, Q4 = TYPE == T_Q4_K, Q8 = TYPE == T_Q8_0;
     static constexpr int MN = MmaN<NT>::N;            // MMA columns per block (half)
@@ -190,13 +168,11 @@ struct Geo {
     static constexpr int WB = Q8 ? 4 * KB * 64 : (Q4 ? 4 * 512 : 4 * KB * 256);    // d / header / qh
     static constexpr int WC = Q6 ? 4 * KB * 64 : 0;                                // Q6_K scales
     static constexpr int WE = Q6 ? 4 * 64 : 0;                                     // Q6_K d
-    static constexpr int RB = Q4 ? 32 : 4;                                         // record bytes
-    static constexpr int UPS = Q8 ? KB : 1;                                        // units per stage
     static constexpr int oB = WA, oC = oB + WB, oE = oC + WC;
     static constexpr int oXQ = (oE + WE + 1023) / 1024 * 1024;
-    static constexpr int oXR = oXQ + (FX ? 0 : KB * NT * 32);
-    static constexpr int STAGE = (oXR + (FX ? 0 : UPS * NT * RB) + 1023) / 1024 * 1024;
-    static constexpr uint32_t TX = WA + WB + WC + WE + (FX ? 0 : KB * NT * 32 + UPS * NT * RB);
+    static constexpr int oXR = oXQ + KB * NT * 32;                                 // float2 records [KB][NT]
+    static constexpr int STAGE = (oXR + KB * NT * 8 + 1023) / 1024 * 1024;
+    static constexpr uint32_t TX = WA + WB + WC + WE + KB * NT * 32 + KB * NT * 8;
     // Handoffs between roles move groups of BG blocks (one mbarrier operation
     // per group, not per block). TMEM holds TG groups of BG * COLS columns; the
     // converted tiles AG groups of BG tiles.
@@ -204,19 +180,17 @@ struct Geo {
     static constexpr int GCOLS = BG * COLS;
     static constexpr int TG = 512 / GCOLS >= 4 ? 4 : 512 / GCOLS;
     static constexpr int AGB = BG * ABYTES;   // bytes of one converted group
-    // resident activations (fused: room for 4096-value rows, at most 66 KB)
-    static constexpr int RES = NT * 32 * 128 + 2048 < 66 * 1024 ? NT * 32 * 128 + 2048 : 66 * 1024;
     // converted groups: 3 when two stages still fit beside them, else 2
-    static constexpr int AG = 220 * 1024 - (FX ? RES : 0) - 2 * STAGE >= 3 * AGB ? 3 : 2;
+    static constexpr int AG = 220 * 1024 - 2 * STAGE >= 3 * AGB ? 3 : 2;
     // raw stages: as many as fit (2 to 4) beside the rest
-    static constexpr int BUDGET = 220 * 1024 - AG * AGB - (FX ? RES : 0);
+    static constexpr int BUDGET = 220 * 1024 - AG * AGB;
     static constexpr int RS = BUDGET / STAGE >= 4 ? 4 : (BUDGET / STAGE >= 3 ? 3 : 2);
     static_assert(2 * STAGE <= BUDGET, "stage ring does not fit");
-    static_assert(8 % BG == 0 && TG >= 2, "group geometry");
+    static_assert(8 % BG == 0 && TG >= 2 && BG % 2 == 0, "group geometry");
     static constexpr int TCOLS_RAW = TG * GCOLS;
     static constexpr int TCOLS = TCOLS_RAW <= 32 ? 32 : (TCOLS_RAW <= 64 ? 64 : (TCOLS_RAW <= 128 ? 128 :
                                  (TCOLS_RAW <= 256 ? 256 : 512)));
-    static constexpr int oRES = RS * STAGE + AG * AGB;   // resident activations (fused)
+    static constexpr int oEND = RS * STAGE + AG * AGB;
 };
 
 constexpr int kThreads = 384;  // 12 warps
@@ -231,18 +205,11 @@ struct Roles {
     static constexpr int CW = kProducerWarp - EW;
 };
 
-// Resident activation bytes of a fused launch: tiles of every block, then the
-// scale records of every unit.
-__host__ __device__ inline size_t fused_act_bytes(int type, int nt, int nb) {
-    const int units = type == T_Q8_0 ? nb : nb / 8, rb = type == T_Q4_K ? 32 : 4;
-    return (size_t)nb * nt * 32 + (size_t)units * nt * rb;
-}
-
 }  // namespace tc
 
-template <int TYPE, int NT, bool FX>
-__host__ __device__ constexpr size_t gemm_tc_smem_base() {
-    return 1024 + (size_t)tc::Geo<TYPE, NT, FX>::oRES;
+template <int TYPE, int NT>
+__host__ __device__ constexpr size_t gemm_tc_smem() {
+    return 1024 + (size_t)tc::Geo<TYPE, NT>::oEND;
 }
 
 // Argmax over the 32 lanes of NH tokens at once: halving steps hand half of the
@@ -284,253 +251,34 @@ __device__ __forceinline__ void argmax_scatter(float (&v)[NH], uint32_t (&ix)[NH
     }
 }
 
-// Builds the q8 activations of token tile `tt` in shared memory (fused mode):
-// tiles [block][NT rows][32] in the UMMA K-major layout and the unit records.
-// One warp per token (warps w, w+nw, ...); same arithmetic as the activation
-// kernels: SUM32 LayerNorm statistics, then one scale per unit (the consumer's
-// groups). Units are handled UC at a time so that their loads and their amax
-// reductions overlap; Q4_K's per-block sums are added afterwards from the bytes.
-template <int TYPE, int NT, int MODE>
-__device__ void fused_prologue(const PrepArgs &p, int rows, int tt, bool write_x, uint8_t *xt, uint8_t *xr, int w,
-                               int nw, int lane) {
-    constexpr int G = act_group(TYPE), MAXV = 64;  // LayerNorm rows up to 2048 values
-    constexpr int UC = G == 8 ? 4 : 16;            // units per batch (32 or 16 values per lane)
-    const int K = p.K, T = K >> 5, nb = T, nu = nb / G;
-    for (int n = w; n < NT; n += nw) {
-        const int tok = tt * NT + n;
-        if (tok >= rows) break;  // uniform across the warp
-        uint32_t id = 0;
-        const float *pos = nullptr;
-        if constexpr (MODE == PREP_EMBED_LN) {
-            id = p.ids[tok];
-            pos = p.pos_table + (size_t)(*p.step + p.pos_base) * K;
-        }
-        auto input = [&](int i) -> float {
-            if constexpr (MODE == PREP_EMBED_LN) {
-                const float v = __fadd_rn(__fmul_rn(deq_elem(p.embed, (int)id, i), p.scale), pos[i]);
-                if (write_x) p.x_out[(size_t)tok * K + i] = v;
-                return v;
-            } else {
-                return p.x[(size_t)tok * K + i];
-            }
-        };
-        float vals[MAXV];
-        float mean = 0.f, rstd = 0.f;
-        if constexpr (MODE != PREP_PLAIN) {
-            // the whole row in registers: element 32t + lane in vals[t]
-#pragma unroll
-            for (int t = 0; t < MAXV; ++t)
-                if (t < T) vals[t] = input(32 * t + lane);
-            float sum = 0.0f;
-#pragma unroll
-            for (int t = 0; t < MAXV; ++t)
-                if (t < T) sum = t == 0 ? vals[t] : __fadd_rn(sum, vals[t]);
-            mean = __fdiv_rn(warp_tree(sum), (float)K);
-            float s2 = 0.0f;
-#pragma unroll
-            for (int t = 0; t < MAXV; ++t)
-                if (t < T) {
-                    const float c = __fsub_rn(vals[t], mean);
-                    const float c2 = __fmul_rn(c, c);
-                    s2 = t == 0 ? c2 : __fadd_rn(s2, c2);
-                }
-            const float var = __fdiv_rn(warp_tree(s2), (float)K);
-            rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
-            // normalized values in place
-#pragma unroll
-            for (int t = 0; t < MAXV; ++t)
-                if (t < T) {
-                    const int i = 32 * t + lane;
-                    vals[t] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(vals[t], mean), rstd), p.gamma[i]), p.beta[i]);
-                }
-        }
-        // a batch of UC units: amax of each (interleaved reductions), then the bytes
-        auto batch = [&](int u0, float (&y)[UC][G]) {
-            float m[UC];
-#pragma unroll
-            for (int c = 0; c < UC; ++c) {
-                m[c] = fabsf(y[c][0]);
-#pragma unroll
-                for (int g = 1; g < G; ++g) m[c] = fmaxf(m[c], fabsf(y[c][g]));
-            }
-#pragma unroll
-            for (int c = 0; c < UC; ++c) m[c] = warp_max_nonneg(m[c]);
-#pragma unroll
-            for (int c = 0; c < UC; ++c) {
-                const int u = u0 + c;
-                if (u >= nu) break;
-                const float dd = __fdiv_rn(m[c], 127.0f), id = __fdiv_rn(127.0f, m[c]);
-#pragma unroll
-                for (int g = 0; g < G; ++g) {
-                    const int t = u * G + g;
-                    const int q = m[c] == 0.0f ? 0 : (int)roundf(__fmul_rn(y[c][g], id));
-                    xt[(size_t)t * NT * 32 + tile_off(n, lane >> 4) + (lane & 15)] = (uint8_t)(int8_t)q;
-                }
-                if (lane == 0) {
-                    if constexpr (TYPE == T_Q4_K) reinterpret_cast<float *>(xr)[((size_t)u * NT + n) * 8] = dd;
-                    else reinterpret_cast<float *>(xr)[(size_t)u * NT + n] = G == 1 ? round_h(dd) : dd;
-                }
-            }
-        };
-        if constexpr (MODE != PREP_PLAIN) {
-#pragma unroll
-            for (int u0 = 0; u0 < MAXV / G; u0 += UC) {
-                if (u0 >= nu) break;
-                float y[UC][G];
-#pragma unroll
-                for (int c = 0; c < UC; ++c)
-#pragma unroll
-                    for (int g = 0; g < G; ++g) {
-                        const int t = (u0 + c) * G + g;
-                        y[c][g] = t < MAXV ? vals[t < MAXV ? t : 0] : 0.0f;
-                    }
-                batch(u0, y);
-            }
-        } else {
-            // next batch's loads are issued before this batch is quantized
-            float y[2][UC][G];
-            auto load = [&](int u0, float (&yy)[UC][G]) {
-#pragma unroll
-                for (int c = 0; c < UC; ++c)
-#pragma unroll
-                    for (int g = 0; g < G; ++g)
-                        yy[c][g] = u0 + c < nu ? input(32 * ((u0 + c) * G + g) + lane) : 0.0f;
-            };
-            load(0, y[0]);
-            for (int u0 = 0, k = 0; u0 < nu; u0 += UC, k ^= 1) {
-                if (u0 + UC < nu) {
-                    if (k == 0) load(u0 + UC, y[1]);
-                    else load(u0 + UC, y[0]);
-                }
-                if (k == 0) batch(u0, y[0]);
-                else batch(u0, y[1]);
-            }
-        }
-    }
-}
-
-// Per-block sums of the quantized activations into the Q4_K records (after the
-// tiles are complete): thread i handles (token, block) pairs i, i+nthreads, ...
-template <int NT>
-__device__ void fused_block_sums(int nb, int rows_here, const uint8_t *xt, uint8_t *xr, int i0, int nthreads) {
-    for (int i = i0; i < rows_here * nb; i += nthreads) {
-        const int n = i % rows_here, t = i / rows_here;
-        const uint8_t *row = xt + (size_t)t * NT * 32;
-        const int4 a = *reinterpret_cast<const int4 *>(row + tile_off(n, 0));
-        const int4 b = *reinterpret_cast<const int4 *>(row + tile_off(n, 1));
-        int s = 0;
-        s = __dp4a(a.x, 0x01010101, s);
-        s = __dp4a(a.y, 0x01010101, s);
-        s = __dp4a(a.z, 0x01010101, s);
-        s = __dp4a(a.w, 0x01010101, s);
-        s = __dp4a(b.x, 0x01010101, s);
-        s = __dp4a(b.y, 0x01010101, s);
-        s = __dp4a(b.z, 0x01010101, s);
-        s = __dp4a(b.w, 0x01010101, s);
-        // record of unit t/8: {f32 scale, int16 sums of its 8 blocks}
-        reinterpret_cast<int16_t *>(xr + ((size_t)(t >> 3) * NT + n) * 32 + 4)[t & 7] = (int16_t)s;
-    }
-}
-
-// LayerNorm of finished rows y[tok][0..K) (K <= 2048) into the consumer's
-// layout: one warp per token, SUM32 statistics in the engine's order.
-template <int G>
-__device__ void post_ln(const tc::Post &P, const float *y, int K, int t0, int t1, int w, int nw, int lane) {
-    constexpr int MAXV = 64;
-    const int T = K >> 5;
-    for (int tok = t0 + w; tok < t1; tok += nw) {
-        float vals[MAXV];
-#pragma unroll
-        for (int t = 0; t < MAXV; ++t)
-            if (t < T) vals[t] = __ldcg(y + (size_t)tok * K + 32 * t + lane);
-        float sum = 0.0f;
-#pragma unroll
-        for (int t = 0; t < MAXV; ++t)
-            if (t < T) sum = t == 0 ? vals[t] : __fadd_rn(sum, vals[t]);
-        const float mean = __fdiv_rn(warp_tree(sum), (float)K);
-        float s2 = 0.0f;
-#pragma unroll
-        for (int t = 0; t < MAXV; ++t)
-            if (t < T) {
-                const float c = __fsub_rn(vals[t], mean);
-                const float c2 = __fmul_rn(c, c);
-                s2 = t == 0 ? c2 : __fadd_rn(s2, c2);
-            }
-        const float var = __fdiv_rn(warp_tree(s2), (float)K);
-        const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
-#pragma unroll
-        for (int u = 0; u < MAXV / G; ++u) {
-            if (u * G >= T) break;
-            float v[G];
-#pragma unroll
-            for (int g = 0; g < G; ++g) {
-                const int t = u * G + g;
-                v[g] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(vals[t], mean), rstd), __ldg(P.gamma + 32 * t + lane)),
-                                 __ldg(P.beta + 32 * t + lane));
-            }
-            store_unit<G>(P.out, P.ctype, tok, u * G, v, lane);
-        }
-    }
-}
-
-// Super-block `sb` (256 values) of finished rows y[tok][0..K) into the
-// consumer's layout: one warp per token.
-template <int G>
-__device__ void post_plain(const tc::Post &P, const float *y, int K, int sb, int t0, int t1, int w, int nw, int lane) {
-    for (int tok = t0 + w; tok < t1; tok += nw) {
-        float v[8];
-#pragma unroll
-        for (int g = 0; g < 8; ++g) v[g] = __ldcg(y + (size_t)tok * K + 256 * sb + 32 * g + lane);
-        if constexpr (G == 8) {
-            store_unit<8>(P.out, P.ctype, tok, 8 * sb, v, lane);
-        } else {
-#pragma unroll
-            for (int g = 0; g < 8; ++g) {
-                const float one[1] = {v[g]};
-                store_unit<1>(P.out, P.ctype, tok, 8 * sb + g, one, lane);
-            }
-        }
-    }
-}
-
-// XM < 0: activations by TMA from the qprep_row_kernel layout; otherwise the
-// PrepMode of the activations the CTA builds itself.
-template <int TYPE, int EPI, int NT, int XM>
+template <int TYPE, int EPI, int NT>
 __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_constant__ tc::Args A) {
     using namespace tc;
-    constexpr bool FX = XM >= 0;
-    using G = Geo<TYPE, NT, FX>;
+    using G = Geo<TYPE, NT>;
     constexpr int RS = G::RS, AG = G::AG, TG = G::TG, BG = G::BG, COLS = G::COLS;
     constexpr int EW = Roles<NT>::EW, CW = Roles<NT>::CW;
     constexpr int NH = NT * 4 / EW;  // tokens per epilogue warp
     constexpr uint32_t IDESC = idesc_i8(128, G::MN);
     extern __shared__ __align__(16) uint8_t smem_raw[];
-    __shared__ __align__(8) uint64_t full[RS], empty[RS], afull[AG], aempty[AG], tfull[TG], tempty[TG], fin, xready,
-        ebar;
+    __shared__ __align__(8) uint64_t full[RS], empty[RS], afull[AG], aempty[AG], tfull[TG], tempty[TG], fin, ebar;
     __shared__ uint32_t tmem_base_sh;
     __shared__ volatile int abort_sh;
     __shared__ float best_v[4][64];
     __shared__ uint32_t best_i[4][64];
-    __shared__ int post_last;
+    __shared__ int split_last;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const Matrix &W = A.W;
     const int NS = (W.nb + 7) / 8;  // stages per tile (Q8_0: the last may hold fewer blocks)
-    // tiles of this CTA: TMA activations walk all tiles; fused activations keep
-    // one token tile per CTA (gridDim.x is then a multiple of tok_tiles)
-    const int splits = FX ? 1 : max(1, A.splits), NSS = NS / splits;  // stages per split
-    const int NU = G::Q8 ? W.nb : W.nsb;                                 // units of a row
+    // tiles of this CTA: (row tile, token tile, split) in turn
+    const int splits = max(1, A.splits), NSS = NS / splits;  // stages per split
+    const int NU = G::Q8 ? W.nb : W.nb / 2;                  // MMQ units of a row
     const int tiles = A.row_tiles * A.tok_tiles * splits;
-    const int my_tt = FX ? (int)blockIdx.x % A.tok_tiles : 0;
-    const int first = FX ? (int)blockIdx.x / A.tok_tiles : (int)blockIdx.x;
-    const int stride = FX ? (int)gridDim.x / A.tok_tiles : (int)gridDim.x;
-    const int count = FX ? A.row_tiles : tiles;
-    const int my_tiles = first < count ? (count - first + stride - 1) / stride : 0;
+    const int first = (int)blockIdx.x, stride = (int)gridDim.x;
+    const int my_tiles = first < tiles ? (tiles - first + stride - 1) / stride : 0;
     uint8_t *base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     uint8_t *ring = base;                                 // RS x STAGE
     uint8_t *atile = base + (size_t)RS * G::STAGE;        // AG x BG x ABYTES
-    uint8_t *xt = base + G::oRES;                         // fused: [nb][NT x 32]
-    uint8_t *xr = xt + (size_t)W.nb * NT * 32;            // fused: [units][NT x RB]
 
     if (tid == 0) {
         for (int i = 0; i < RS; ++i) {
@@ -546,7 +294,6 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
             mbar_init(&tempty[i], EW);
         }
         mbar_init(&fin, 1);
-        mbar_init(&xready, EW);
         mbar_init(&ebar, EW);
         abort_sh = 0;
     }
@@ -587,9 +334,9 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
         if (!ok && lane == 0) fail(code);
         return ok && !abort_sh;
     };
-    auto tile_rt = [&](int k) { return FX ? first + k * stride : (first + k * stride) % A.row_tiles; };
-    auto tile_tt = [&](int k) { return FX ? my_tt : ((first + k * stride) / A.row_tiles) % A.tok_tiles; };
-    auto tile_s0 = [&](int k) { return FX ? 0 : (first + k * stride) / (A.row_tiles * A.tok_tiles) * NSS; };
+    auto tile_rt = [&](int k) { return (first + k * stride) % A.row_tiles; };
+    auto tile_tt = [&](int k) { return ((first + k * stride) / A.row_tiles) % A.tok_tiles; };
+    auto tile_s0 = [&](int k) { return (first + k * stride) / (A.row_tiles * A.tok_tiles) * NSS; };
 
     // Ring position: slot and phase parity, advanced by next().
     struct Pos {
@@ -621,13 +368,9 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
                 }
             };
             auto acts = [&](int tt, int s, uint8_t *dst, uint64_t *bar) {
-                if constexpr (!FX) {
-                    const int t0 = A.tok0 + tt * NT;
-                    tma3(dst + G::oXQ, &A.m.xq, 0, t0 / 8, 8 * s, bar);
-                    if constexpr (G::Q4) tma2(dst + G::oXR, &A.m.xr, t0 * 4, s, bar);
-                    else if constexpr (G::Q6) tma2(dst + G::oXR, &A.m.xr, t0 / 2, s, bar);
-                    else tma2(dst + G::oXR, &A.m.xr, t0 / 2, 8 * s, bar);
-                }
+                const int t0 = A.tok0 + tt * NT;
+                tma3(dst + G::oXQ, &A.m.xq, 0, t0 / 8, 8 * s, bar);
+                tma2(dst + G::oXR, &A.m.xr, t0, 8 * s, bar);
             };
             // weights of the first stages do not depend on the previous kernel
             for (int s = 0; s < first_stages; ++s) {
@@ -657,15 +400,14 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
         // ----------------------------------------------------------------- MMA
         // (nothing to do before the predecessor's outputs exist: waiting here
         // keeps this warp off the issue slots of the predecessor's warps)
-        if constexpr (!FX) pdl_wait();
+        pdl_wait();
         if (lane == 0) {
             Pos st, ag, tg;
             // Descriptors are formed once and advanced by constant 16-byte
             // steps (shared-memory offsets stay below 256 KB, so the 14-bit
             // address field never carries): the issue loop is the MMAs alone.
             const uint64_t a_base = sdesc(atile, 128, 256);
-            const uint64_t x_base = sdesc(FX ? xt : ring + G::oXQ, 128, MmaN<NT>::SBO);
-            if (FX && my_tiles > 0 && !mbar_wait(&xready, 0)) fail(16u);
+            const uint64_t x_base = sdesc(ring + G::oXQ, 128, MmaN<NT>::SBO);
             for (int k = 0; k < my_tiles && !abort_sh; ++k) {
                 const int s0 = tile_s0(k);
                 for (int s = s0; s < s0 + NSS && !abort_sh; ++s, st.next(RS)) {
@@ -673,8 +415,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
                         fail(16u);
                         break;
                     }
-                    const uint64_t xs =
-                        x_base + (uint64_t)(FX ? (8 * s * NT * 32) >> 4 : (st.slot * G::STAGE) >> 4);
+                    const uint64_t xs = x_base + (uint64_t)((st.slot * G::STAGE) >> 4);
                     const int nbs = min(8, W.nb - 8 * s);
                     for (int g = 0; g * BG < nbs; ++g, ag.next(AG), tg.next(TG)) {
                         if (!mbar_wait(&afull[ag.slot], ag.phase) ||
@@ -708,7 +449,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
         }
     } else if (warp >= EW) {
         // ---------------------------------------------------------- converters
-        if constexpr (!FX) pdl_wait();  // (as the MMA warp)
+        pdl_wait();  // (as the MMA warp)
         // items of a group: (weight row r, block bb) = (i % 128, i / 128) for
         // i = ct, ct + CT, ...; a warp's 32 items are 32 consecutive rows of one
         // block. Each batch of LB items is loaded before any of it is stored.
@@ -804,19 +545,6 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
         pdl_wait();
         // the decode step (QKV cache position), written by the previous step's kernels
         const int qkv_step = EPI == EPI_QKV ? (int)*A.g.step : 0;
-        if constexpr (FX) {
-            // this CTA's token tile, built once; the first row tile writes x (embedding)
-            if (my_tiles > 0) {
-                fused_prologue<TYPE, NT, (FX ? XM : 0)>(A.p, A.rows, my_tt, first == 0, xt, xr, warp, EW, lane);
-                if constexpr (G::Q4) {
-                    asm volatile("bar.sync 1, %0;" ::"r"(32 * EW) : "memory");  // the epilogue warps
-                    fused_block_sums<NT>(W.nb, min(NT, A.rows - my_tt * NT), xt, xr, tid, 32 * EW);
-                }
-            }
-            fence_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&xready);
-        }
         Pos st, tg;
         uint32_t ephase = 0;
         bool ok = true;
@@ -824,8 +552,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
             const int rt = tile_rt(k), tt = tile_tt(k), s0 = tile_s0(k);
             const int row = rt * 128 + r;
             const bool live = row < W.N;
-            // split-K partials of this tile: [unit][NT tokens][128 rows]
-            float *kp = splits > 1 ? A.kpart + (size_t)(tt * A.row_tiles + rt) * NU * NT * 128 : nullptr;
+            // split-K units of this tile: [unit][NT tokens][128 rows]
+            float2 *kp = splits > 1 ? A.kpart + (size_t)(tt * A.row_tiles + rt) * NU * NT * 128 : nullptr;
             float acc[NH];
 #pragma unroll
             for (int n = 0; n < NH; ++n) acc[n] = 0.0f;
@@ -856,11 +584,20 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
                     qkv_tok = (size_t)A.g.H * A.g.m * A.g.hd;
                 }
             }
+            // add one unit to the running sum (split 0) or store it (later splits):
+            // Q8_0 / Q6_K units are fused multiply-adds fma(x, y, acc), Q4_K values
+            auto unit = [&](int n, int u, float x, float y) {
+                if (s0 == 0) {
+                    acc[n] = G::Q4 ? __fadd_rn(acc[n], x) : __fmaf_rn(x, y, acc[n]);
+                } else {
+                    kp[((size_t)u * NT + n0 + n) * 128 + r] = make_float2(x, y);
+                }
+            };
             for (int s = s0; s < s0 + NSS && ok; ++s, st.next(RS)) {
                 if (!(ok = wwait(&full[st.slot], st.phase, 64u))) break;
                 const uint8_t *stg = ring + (size_t)st.slot * G::STAGE;
-                // records of this stage's units: [unit][NT x RB]
-                const uint8_t *rec = FX ? xr + (size_t)(G::Q8 ? 8 * s : s) * NT * G::RB : stg + G::oXR;
+                // the stage's activation records: {d, s} per [block][token]
+                const float2 *rec = reinterpret_cast<const float2 *>(stg + G::oXR);
                 // this row's scales for the stage
                 float d = 0.f, dm = 0.f;
                 uint32_t mpk0 = 0, mpk1 = 0, scpk0 = 0, scpk1 = 0;
@@ -893,94 +630,83 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
                 } else if constexpr (G::Q6) {
                     d = h2f(*reinterpret_cast<const unsigned short *>(stg + G::oE + gi * 64 + l * 2));
                 }
-                int S[NH];
-#pragma unroll
-                for (int n = 0; n < NH; ++n) S[n] = 0;
                 const int nbs = min(8, W.nb - 8 * s);
                 for (int g = 0; g * BG < nbs && ok; ++g, tg.next(TG)) {
                     if (!(ok = wwait(&tfull[tg.slot], tg.phase, 64u))) break;
                     fence_after();
-                    for (int bb = 0; bb < group_blocks(g, nbs); ++bb) {
-                    const int b = g * BG + bb;
-                    const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + tg.slot * G::GCOLS + bb * COLS + n0;
-                    int sa = 0, sb = 0;
-                    float db = 0.f;
-                    if constexpr (G::Q4) {
-                        sa = (int)(((b < 4 ? scpk0 : scpk1) >> (8 * (b & 3))) & 0xff);
-                    } else if constexpr (G::Q6) {
-                        const unsigned short sc2 =
-                            *reinterpret_cast<const unsigned short *>(stg + G::oC + (gi * 8 + b) * 64 + l * 2);
-                        sa = (int8_t)(sc2 & 0xff);
-                        sb = (int8_t)(sc2 >> 8);
-                    } else {
-                        db = h2f(*reinterpret_cast<const unsigned short *>(stg + G::oB + (gi * 8 + b) * 64 + l * 2));
-                    }
-                    // TMEM -> registers in chunks of up to 16 tokens; the next chunk's
-                    // load is in flight while the current one is accumulated
-                    constexpr int CH = NH < 16 ? NH : 16, NC = NH / CH;
-                    int va[2][CH], vb[2][CH];
-                    auto ld = [&](int c, int (&a)[CH], int (&bv)[CH]) {
-                        if constexpr (CH == 16) {
-                            tmem_ld16(ta + c * CH, a);
-                            if constexpr (G::Q6) tmem_ld16(ta + G::MN + c * CH, bv);
-                        } else if constexpr (CH == 8) {
-                            tmem_ld8(ta + c * CH, a);
-                            if constexpr (G::Q6) tmem_ld8(ta + G::MN + c * CH, bv);
+                    const int gb = group_blocks(g, nbs);
+                    // units of the group: Q8_0 one block each, Q4_K / Q6_K pairs of blocks
+                    constexpr int UB = G::Q8 ? 1 : 2;
+                    for (int bb = 0; bb < gb; bb += UB) {
+                        const int b = g * BG + bb;
+                        const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + tg.slot * G::GCOLS + bb * COLS + n0;
+                        int sa0 = 0, sb0 = 0, sa1 = 0, sb1 = 0;
+                        float mf0 = 0.f, mf1 = 0.f, db = 0.f;
+                        if constexpr (G::Q4) {
+                            sa0 = (int)(((b < 4 ? scpk0 : scpk1) >> (8 * (b & 3))) & 0xff);
+                            sa1 = (int)(((b + 1 < 4 ? scpk0 : scpk1) >> (8 * ((b + 1) & 3))) & 0xff);
+                            mf0 = (float)(((b < 4 ? mpk0 : mpk1) >> (8 * (b & 3))) & 0xff);
+                            mf1 = (float)(((b + 1 < 4 ? mpk0 : mpk1) >> (8 * ((b + 1) & 3))) & 0xff);
+                        } else if constexpr (G::Q6) {
+                            const unsigned short c0 =
+                                *reinterpret_cast<const unsigned short *>(stg + G::oC + (gi * 8 + b) * 64 + l * 2);
+                            const unsigned short c1 =
+                                *reinterpret_cast<const unsigned short *>(stg + G::oC + (gi * 8 + b + 1) * 64 + l * 2);
+                            sa0 = (int8_t)(c0 & 0xff);
+                            sb0 = (int8_t)(c0 >> 8);
+                            sa1 = (int8_t)(c1 & 0xff);
+                            sb1 = (int8_t)(c1 >> 8);
                         } else {
-                            static_assert(CH == 4, "token chunk");
-                            tmem_ld4(ta + c * CH, a);
-                            if constexpr (G::Q6) tmem_ld4(ta + G::MN + c * CH, bv);
+                            db = h2f(*reinterpret_cast<const unsigned short *>(stg + G::oB + (gi * 8 + b) * 64 + l * 2));
                         }
-                    };
-                    ld(0, va[0], vb[0]);
+                        const int u = G::Q8 ? 8 * s + b : 4 * s + b / 2;  // unit index in the row
+                        // TMEM -> registers in chunks of up to 16 tokens: the unit's
+                        // blocks (and Q6_K halves) loaded together, then one wait
+                        constexpr int CH = NH < 16 ? NH : 16, NC = NH / CH;
 #pragma unroll
-                    for (int c = 0; c < NC; ++c) {
-                        tmem_wait_ld();
-                        if (c + 1 < NC) ld(c + 1, va[(c + 1) & 1], vb[(c + 1) & 1]);
+                        for (int c = 0; c < NC; ++c) {
+                            int va0[CH], vb0[CH], va1[CH], vb1[CH];
+                            auto ld = [&](uint32_t t, int (&v)[CH]) {
+                                if constexpr (CH == 16) tmem_ld16(t, v);
+                                else if constexpr (CH == 8) tmem_ld8(t, v);
+                                else {
+                                    static_assert(CH == 4, "token chunk");
+                                    tmem_ld4(t, v);
+                                }
+                            };
+                            ld(ta + c * CH, va0);
+                            if constexpr (G::Q6) ld(ta + G::MN + c * CH, vb0);
+                            if constexpr (!G::Q8) ld(ta + COLS + c * CH, va1);
+                            if constexpr (G::Q6) ld(ta + COLS + G::MN + c * CH, vb1);
+                            tmem_wait_ld();
 #pragma unroll
-                        for (int i = 0; i < CH; ++i) {
-                            const int n = c * CH + i;
-                            const int I = va[c & 1][i];
-                            if constexpr (G::Q4) {
-                                S[n] += sa * I;
-                            } else if constexpr (G::Q6) {
-                                S[n] += sa * I + sb * vb[c & 1][i];
-                            } else {
-                                const float xd = reinterpret_cast<const float *>(rec)[b * NT + n0 + n];
-                                const float p = __fmul_rn(__fmul_rn(db, xd), (float)I);
-                                if (s0 == 0) acc[n] = (s == 0 && b == 0) ? p : __fadd_rn(acc[n], p);
-                                else kp[((size_t)(8 * s + b) * NT + n0 + n) * 128 + r] = p;
+                            for (int i = 0; i < CH; ++i) {
+                                const int n = c * CH + i;
+                                const float2 x0 = rec[b * NT + n0 + n];
+                                if constexpr (G::Q8) {
+                                    unit(n, u, __fmul_rn(db, x0.x), (float)va0[i]);
+                                } else {
+                                    const float2 x1 = rec[(b + 1) * NT + n0 + n];
+                                    if constexpr (G::Q4) {
+                                        const float sd = __fmaf_rn(x1.x, (float)(sa1 * va1[i]),
+                                                                   __fmaf_rn(x0.x, (float)(sa0 * va0[i]), 0.0f));
+                                        const float sm = __fmaf_rn(x1.y, mf1, __fmaf_rn(x0.y, mf0, 0.0f));
+                                        unit(n, u, __fmaf_rn(d, sd, -__fmul_rn(dm, sm)), 0.0f);
+                                    } else {
+                                        const float sf =
+                                            __fmaf_rn(x1.x, (float)(sa1 * va1[i] + sb1 * vb1[i]),
+                                                      __fmaf_rn(x0.x, (float)(sa0 * va0[i] + sb0 * vb0[i]), 0.0f));
+                                        unit(n, u, d, sf);
+                                    }
+                                }
                             }
                         }
-                    }
                     }
                     fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&tempty[tg.slot]);
                 }
                 if (!ok) break;
-                if constexpr (!G::Q8) {
-                    // finish the super-block: float scales once, then the row sum
-#pragma unroll
-                    for (int n = 0; n < NH; ++n) {
-                        float p;
-                        if constexpr (G::Q4) {
-                            const int4 rv = *reinterpret_cast<const int4 *>(rec + (n0 + n) * 32);
-                            const float xd = __int_as_float(rv.x);
-                            // S2 = sum_j m_j * s32_j (s32 pairs as int16x2, m_j as bytes)
-                            int S2 = __dp2a_lo(rv.y, (int)mpk0, 0);
-                            S2 = __dp2a_hi(rv.z, (int)mpk0, S2);
-                            S2 = __dp2a_lo(rv.w, (int)mpk1, S2);
-                            S2 = __dp2a_hi(*reinterpret_cast<const int *>(rec + (n0 + n) * 32 + 16), (int)mpk1, S2);
-                            p = __fmul_rn(xd, __fsub_rn(__fmul_rn(d, (float)S[n]), __fmul_rn(dm, (float)S2)));
-                        } else {
-                            const float xd = reinterpret_cast<const float *>(rec)[n0 + n];
-                            p = __fmul_rn(__fmul_rn(d, xd), (float)S[n]);
-                        }
-                        if (s0 == 0) acc[n] = s == 0 ? p : __fadd_rn(acc[n], p);
-                        else kp[((size_t)s * NT + n0 + n) * 128 + r] = p;
-                    }
-                }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[st.slot]);
             }
@@ -989,7 +715,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
                 // split 0 leaves its running sum in unit slot 0 (a unit it summed itself)
                 if (s0 == 0)
 #pragma unroll
-                    for (int n = 0; n < NH; ++n) kp[(size_t)(n0 + n) * 128 + r] = acc[n];
+                    for (int n = 0; n < NH; ++n) kp[(size_t)(n0 + n) * 128 + r] = make_float2(acc[n], 0.0f);
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&ebar);
                 if (!(ok = wwait(&ebar, ephase, 128u))) break;
@@ -997,8 +723,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
                 if (tid == 0) {
                     __threadfence();
                     const uint32_t old = atomicAdd(&A.kcount[tt * A.row_tiles + rt], 1u);
-                    post_last = old + 1 == (uint32_t)splits;
-                    if (post_last) {
+                    split_last = old + 1 == (uint32_t)splits;
+                    if (split_last) {
                         A.kcount[tt * A.row_tiles + rt] = 0;  // every split of this launch has counted
                         __threadfence();
                     }
@@ -1007,25 +733,27 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
                 if (lane == 0) mbar_arrive(&ebar);
                 if (!(ok = wwait(&ebar, ephase, 128u))) break;
                 ephase ^= 1;
-                if (!post_last) continue;  // another split finishes this tile
-                // the row sum continued in unit order from the stored partials,
-                // UB units x NH tokens of loads in flight per batch
-                const int u1 = G::Q8 ? 8 * NSS : NSS;  // first unit of split 1
-                constexpr int UB = NH <= 8 ? 8 : (NH <= 16 ? 4 : 2);
+                if (!split_last) continue;  // another split finishes this tile
+                // the row sum continued in unit order from the stored units,
+                // UL units x NH tokens of loads in flight per batch
+                const int u1 = G::Q8 ? 8 * NSS : 4 * NSS;  // first unit of split 1
+                constexpr int UL = NH <= 8 ? 8 : (NH <= 16 ? 4 : 2);
 #pragma unroll
-                for (int n = 0; n < NH; ++n) acc[n] = __ldcg(kp + (size_t)(n0 + n) * 128 + r);
-                for (int u0 = u1; u0 < NU; u0 += UB) {
-                    float v[UB][NH];
+                for (int n = 0; n < NH; ++n) acc[n] = __ldcg(&kp[(size_t)(n0 + n) * 128 + r].x);
+                for (int u0 = u1; u0 < NU; u0 += UL) {
+                    float2 v[UL][NH];
 #pragma unroll
-                    for (int j = 0; j < UB; ++j)
+                    for (int j = 0; j < UL; ++j)
 #pragma unroll
                         for (int n = 0; n < NH; ++n)
-                            v[j][n] = u0 + j < NU ? __ldcg(kp + ((size_t)(u0 + j) * NT + n0 + n) * 128 + r) : 0.0f;
+                            v[j][n] = u0 + j < NU ? __ldcg(kp + ((size_t)(u0 + j) * NT + n0 + n) * 128 + r)
+                                                  : make_float2(0.0f, 0.0f);
 #pragma unroll
-                    for (int j = 0; j < UB; ++j) {
+                    for (int j = 0; j < UL; ++j) {
                         if (u0 + j >= NU) break;
 #pragma unroll
-                        for (int n = 0; n < NH; ++n) acc[n] = __fadd_rn(acc[n], v[j][n]);
+                        for (int n = 0; n < NH; ++n)
+                            acc[n] = G::Q4 ? __fadd_rn(acc[n], v[j][n].x) : __fmaf_rn(v[j][n].x, v[j][n].y, acc[n]);
                     }
                 }
             }
@@ -1066,43 +794,6 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
                         epilogue_store<EPI>(A.g, row, tok, acc[n]);
                     }
                 }
-                if constexpr (MGB_TC_POST_STEPS && (EPI == EPI_RESID || EPI == EPI_RELU)) {
-                    if (A.post.mode >= 0) {
-                        // the tile's outputs are stored; count it, and the CTA that
-                        // completes a token tile (LN) / super-block (PLAIN) prepares it
-                        const bool ln = A.post.mode == PREP_LN;
-                        // the 8 epilogue warps meet on a bounded mbarrier (a warp that
-                        // stopped on an error makes the others time out, not hang)
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&ebar);
-                        if (!(ok = wwait(&ebar, ephase, 128u))) break;
-                        ephase ^= 1;
-                        if (tid == 0) {
-                            __threadfence();
-                            const int idx = ln ? tt : tt * (A.row_tiles / 2) + rt / 2;
-                            const uint32_t old = atomicAdd(&A.post.counters[idx], 1u);
-                            post_last = old + 1 == (ln ? (uint32_t)A.row_tiles : 2u);
-                            if (post_last) {
-                                A.post.counters[idx] = 0;  // every CTA of this launch has counted
-                                __threadfence();
-                            }
-                        }
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&ebar);
-                        if (!(ok = wwait(&ebar, ephase, 128u))) break;
-                        ephase ^= 1;
-                        if (post_last) {
-                            const int t0 = tt * NT, t1 = min(A.rows, t0 + NT);
-                            if (ln) {
-                                if (A.post.group == 8) post_ln<8>(A.post, A.g.y, W.N, t0, t1, warp, EW, lane);
-                                else post_ln<1>(A.post, A.g.y, W.N, t0, t1, warp, EW, lane);
-                            } else {
-                                if (A.post.group == 8) post_plain<8>(A.post, A.g.y, W.N, rt / 2, t0, t1, warp, EW, lane);
-                                else post_plain<1>(A.post, A.g.y, W.N, rt / 2, t0, t1, warp, EW, lane);
-                            }
-                        }
-                    }
-                }
             }
         }
     }
@@ -1126,24 +817,22 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
     }
 }
 
-// Tensor-core layout of one activation row (one CTA per row): the row is staged
-// in shared memory (embedding rows dequantized once), LayerNorm statistics by
-// one warp in the fixed order, quantized with the consumer's scale groups, then
-// written as
-//   tq : per block j, 8-row core groups of 256 bytes [j][row/8][k16][row%8][16 B]
-//        (the UMMA K-major no-swizzle layout);
-//   trec: per unit u (super-block, or block for Q8_0 consumers) and row:
-//        Q4_K: {f32 scale, int16 block sums x 8, 12 zero bytes} (32 B);
-//        Q6_K: f32 scale; Q8_0: f32 (f16-rounded) scale.
+// Tensor-core layout of one activation row (one CTA per row): the row is
+// staged in shared memory (embedding rows dequantized once), LayerNorm
+// statistics by one warp in the engine's fixed order, then every 32-value
+// block is quantized to q8_1 (store_block_tc) as
+//   tq  : per block j, 8-row core groups of 256 bytes [j][row/8][k16][row%8][16 B]
+//         (the UMMA K-major no-swizzle layout);
+//   trec: per block j and row, float2 {d, s}.
 template <int MODE>
 __global__ void __launch_bounds__(256) qprep_row_kernel(PrepArgs p, QAct out) {
-    extern __shared__ __align__(16) uint8_t qsm[];
+    extern __shared__ __align__(16) float qsm[];
     __shared__ float st[2];
-    __shared__ uint32_t id_sh[1];
-    const int r = blockIdx.x, K = p.K, nb = K >> 5;
+    const int r = blockIdx.x, K = p.K, T = K >> 5;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float *xs = qsm, *gb = qsm + K;  // row [K]; gamma [K], beta [K]
     // LayerNorm parameters into shared memory before the dependency wait (they
     // are weights, not the predecessor's output)
-    float *gb = reinterpret_cast<float *>(qsm + (size_t)K * 5 + (size_t)nb * 16);  // gamma[K], beta[K]
     if constexpr (MODE != PREP_PLAIN) {
         for (int i = threadIdx.x; i < K / 4; i += blockDim.x) {
             reinterpret_cast<float4 *>(gb)[i] = __ldg(reinterpret_cast<const float4 *>(p.gamma) + i);
@@ -1151,20 +840,11 @@ __global__ void __launch_bounds__(256) qprep_row_kernel(PrepArgs p, QAct out) {
         }
     }
     pdl_wait();
-    float *xs = reinterpret_cast<float *>(qsm);                 // K floats
-    SmAct s;
-    s.q = reinterpret_cast<int8_t *>(qsm + (size_t)K * 4);      // K bytes
-    s.d = reinterpret_cast<float *>(qsm + (size_t)K * 5);       // nb
-    s.s32 = reinterpret_cast<int *>(s.d + nb);                  // nb
-    s.s16 = s.s32 + nb;                                         // 2 nb
-    s.st = st;
-    s.xf = nullptr;
-    PrepArgs pa = p;
+    const float *pos = nullptr;
+    uint32_t id = 0;
     if constexpr (MODE == PREP_EMBED_LN) {
-        if (threadIdx.x == 0) id_sh[0] = p.ids[r];
-        pa.pos_table += (size_t)(*p.step + p.pos_base) * K;
-        pa.ids = id_sh;
-        __syncthreads();
+        pos = p.pos_table + (size_t)(*p.step + p.pos_base) * K;
+        id = p.ids[r];
     }
     // 8 loads in flight per thread before their stores (one memory round trip)
     for (int base = threadIdx.x; base < K; base += 8 * blockDim.x) {
@@ -1172,7 +852,12 @@ __global__ void __launch_bounds__(256) qprep_row_kernel(PrepArgs p, QAct out) {
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
             const int i = base + u * blockDim.x;
-            v[u] = i < K ? act_input<MODE>(pa, MODE == PREP_EMBED_LN ? 0 : r, i) : 0.0f;
+            if (i < K) {
+                if constexpr (MODE == PREP_EMBED_LN)
+                    v[u] = __fadd_rn(__fmul_rn(deq_elem(p.embed, (int)id, i), p.scale), pos[i]);
+                else
+                    v[u] = p.x[(size_t)r * K + i];
+            }
         }
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
@@ -1183,42 +868,32 @@ __global__ void __launch_bounds__(256) qprep_row_kernel(PrepArgs p, QAct out) {
         }
     }
     __syncthreads();
-    PrepArgs q = p;
-    q.x = xs;
-    q.rows = 1;
     if constexpr (MODE != PREP_PLAIN) {
-        q.gamma = gb;
-        q.beta = gb + K;
-    }
-    constexpr int M2 = MODE == PREP_PLAIN ? PREP_PLAIN : PREP_LN;
-    if (p.group == 8) build_activations_impl<M2, 8>(q, s, 1, false);
-    else build_activations_impl<M2, 1>(q, s, 1, false);
-    // build_activations_impl ends with __syncthreads
-    // the next matmul is released once the activations are built (measured
-    // slightly faster than releasing it at the start)
-    pdl_launch_dependents();
-    const int rs = out.rs;
-    for (int c = threadIdx.x; c < nb * 2; c += blockDim.x) {
-        const int j = c >> 1, k16 = c & 1;
-        *reinterpret_cast<int4 *>(out.tq + ((size_t)j * (rs / 8) + (r >> 3)) * 256 + tile_off(r & 7, k16)) =
-            *reinterpret_cast<const int4 *>(s.q + 32 * j + 16 * k16);
-    }
-    if (p.ctype == T_Q4_K) {
-        for (int u = threadIdx.x; u < nb / 8; u += blockDim.x) {
-            int w[8];
-            w[0] = __float_as_int(s.d[8 * u]);
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-                w[1 + k] = (s.s32[8 * u + 2 * k] & 0xffff) | (s.s32[8 * u + 2 * k + 1] << 16);
-            w[5] = w[6] = w[7] = 0;
-            int4 *dst = reinterpret_cast<int4 *>(out.trec + ((size_t)u * rs + r) * 32);
-            dst[0] = make_int4(w[0], w[1], w[2], w[3]);
-            dst[1] = make_int4(w[4], w[5], w[6], w[7]);
+        if (warp == 0) {
+            float sum = 0.0f;
+            for (int t = 0; t < T; ++t) sum = t == 0 ? xs[lane] : __fadd_rn(sum, xs[32 * t + lane]);
+            const float mean = __fdiv_rn(warp_tree(sum), (float)K);
+            float s2 = 0.0f;
+            for (int t = 0; t < T; ++t) {
+                const float c = __fsub_rn(xs[32 * t + lane], mean);
+                const float c2 = __fmul_rn(c, c);
+                s2 = t == 0 ? c2 : __fadd_rn(s2, c2);
+            }
+            const float var = __fdiv_rn(warp_tree(s2), (float)K);
+            if (lane == 0) {
+                st[0] = mean;
+                st[1] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
+            }
         }
-    } else {
-        const int units = p.ctype == T_Q6_K ? nb / 8 : nb, step = p.ctype == T_Q6_K ? 8 : 1;
-        for (int u = threadIdx.x; u < units; u += blockDim.x)
-            reinterpret_cast<float *>(out.trec)[(size_t)u * rs + r] = s.d[u * step];
+        __syncthreads();
+    }
+    // the next matmul is released once the activations are about to be written
+    pdl_launch_dependents();
+    for (int j = warp; j < T; j += blockDim.x >> 5) {
+        const int i = 32 * j + lane;
+        float v = xs[i];
+        if constexpr (MODE != PREP_PLAIN) v = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v, st[0]), st[1]), gb[i]), gb[K + i]);
+        store_block_tc(out, r, j, v, lane);
     }
 }
 

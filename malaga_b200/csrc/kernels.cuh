@@ -1,69 +1,64 @@
-// Decode-step kernels of the engine (sm_100a).
+// Decode-step kernels of the engine (sm_100a): shared structures, the
+// attention, greedy bookkeeping and the encoder's embedding gather.
 //
 // Reference kernels they replace (crates/malaga-core/kernels/malaga.cu, launched
 // by crates/malaga-core/src/kernels.rs) and candle ops (model.rs:552-612):
-//   qprep_*         embed_pos_ln (malaga.cu:110-130) + bias_residual_ln's LayerNorm
-//                   (malaga.cu:89-105) + candle's q8_1 activation quantization
-//   gemv            candle QMatMul::forward (MMVQ) + the bias/residual/ReLU/K-V
-//                   epilogues of bias_residual_ln, bias_relu (malaga.cu:133-138)
-//                   and qkv_decode (malaga.cu:142-154)
 //   attend          attn_decode (malaga.cu:165-227), also the encoder's masked
 //                   softmax attention (model.rs:101-109)
-//   lm head argmax  QMatMul::forward(token_embd) (model.rs:607) fused with
-//                   argmax_partial (malaga.cu:247-280): logits never reach HBM
 //   greedy_finalize greedy_finalize (malaga.cu:290-326)
+//   embed_tokens    the encoder's embedding + position input (model.rs:270-273,
+//                   455-458), gathered on the device
+// The matmuls live in smallmm.cuh (at most 8 rows) and gemm_tc.cuh (more).
 #pragma once
 #include "engine.h"
 #include "numerics.cuh"
+#include "sync.cuh"
 
 namespace mgb {
 
 // ---------------------------------------------------------------------------
-// Weight access
+// Weight access (row layout, engine.h)
 
-__device__ __forceinline__ size_t wslot(const Matrix &W, int row, int j) {
-    return ((size_t)(row >> 5) * W.nb + j) * 32 + (row & 31);
-}
-__device__ __forceinline__ size_t wsslot(const Matrix &W, int row, int sb) {
-    return ((size_t)(row >> 5) * W.nsb + sb) * 32 + (row & 31);
-}
-
-// Dequantized element i of row `row` (every product below is exact in f32).
+// Dequantized element i of row `row` (exact: every product below is exactly
+// representable in f32, so the order of the factors does not matter).
 __device__ __forceinline__ float deq_elem(const Matrix &W, int row, int i) {
-    const int j = i >> 5, k = i & 31;
-    const size_t bi = wslot(W, row, j);
     switch (W.type) {
-        case T_F32: return reinterpret_cast<const float *>(W.a)[bi * 32 + k];
+        case T_F32: return reinterpret_cast<const float *>(W.ra)[(size_t)row * W.K + i];
         case T_Q8_0: {
-            const float d = h2f(reinterpret_cast<const uint16_t *>(W.b)[bi]);
-            return __fmul_rn(d, (float)(int8_t)W.a[bi * 32 + k]);
+            const size_t bi = (size_t)row * W.nb + (i >> 5);
+            const float d = h2f(reinterpret_cast<const uint16_t *>(W.rb)[bi]);
+            return __fmul_rn(d, (float)(int8_t)W.ra[bi * 32 + (i & 31)]);
         }
         case T_Q4_K: {
-            const uint8_t byte = W.a[bi * 16 + (k & 15)];
-            const int q = k < 16 ? (byte & 15) : (byte >> 4);
-            const uint8_t *h = W.b + wsslot(W, row, j >> 3) * 16;
-            const int sb = j & 7;
-            const uint8_t *s = h + 4;
+            const uint8_t *sb = W.ra + ((size_t)row * W.nsb + (i >> 8)) * 144;
+            const int k = i & 255, j = k >> 5, l = k & 31;
+            const uint8_t *s = sb + 4;
             int sc, m;
-            if (sb < 4) {
-                sc = s[sb] & 63;
-                m = s[sb + 4] & 63;
+            if (j < 4) {
+                sc = s[j] & 63;
+                m = s[j + 4] & 63;
             } else {
-                sc = (s[sb + 4] & 0xf) | ((s[sb - 4] >> 6) << 4);
-                m = (s[sb + 4] >> 4) | ((s[sb] >> 6) << 4);
+                sc = (s[j + 4] & 0xf) | ((s[j - 4] >> 6) << 4);
+                m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
             }
-            const float d = h2f(h[0] | (h[1] << 8)), dm = h2f(h[2] | (h[3] << 8));
+            const uint8_t byte = sb[16 + 32 * (j >> 1) + l];
+            const int q = (j & 1) ? (byte >> 4) : (byte & 15);
+            const float d = h2f(sb[0] | (sb[1] << 8)), dm = h2f(sb[2] | (sb[3] << 8));
             return __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)q), __fmul_rn(dm, (float)m));
         }
         case T_Q6_K: {
-            const uint8_t byte = W.a[bi * 16 + (k & 15)];
-            const int lo = k < 16 ? (byte & 15) : (byte >> 4);
-            const uint32_t word = reinterpret_cast<const uint32_t *>(W.b)[bi * 2 + (k >> 4)];
-            const int kk = k & 15;
-            const int hi = (word >> (8 * (kk & 3) + 2 * (kk >> 2))) & 3;
-            const int q = lo | (hi << 4);
-            const int sc = (int8_t)W.c[bi * 2 + (k >> 4)];
-            const float d = h2f(reinterpret_cast<const uint16_t *>(W.e)[wsslot(W, row, j >> 3)]);
+            const size_t u = (size_t)row * W.nsb + (i >> 8);
+            const int k = i & 255, n = k >> 7, g = (k & 127) >> 5, l = k & 31;
+            const uint8_t *ql = W.ra + u * 128 + 64 * n, *qh = W.rb + u * 64 + 32 * n;
+            int q;
+            switch (g) {
+                case 0: q = (ql[l] & 0xf) | ((qh[l] & 3) << 4); break;
+                case 1: q = (ql[l + 32] & 0xf) | (((qh[l] >> 2) & 3) << 4); break;
+                case 2: q = (ql[l] >> 4) | (((qh[l] >> 4) & 3) << 4); break;
+                default: q = (ql[l + 32] >> 4) | (((qh[l] >> 6) & 3) << 4); break;
+            }
+            const int sc = (int8_t)W.rc[u * 16 + (k >> 4)];
+            const float d = h2f(reinterpret_cast<const uint16_t *>(W.re)[u]);
             return __fmul_rn(__fmul_rn(d, (float)sc), (float)(q - 32));
         }
     }
@@ -71,16 +66,15 @@ __device__ __forceinline__ float deq_elem(const Matrix &W, int row, int i) {
 }
 
 // ---------------------------------------------------------------------------
-// Activation preparation: one warp per row. Lane l owns elements l + 32 t, so
-// block t of the q8_1 activation is exactly "element t of every lane".
+// Activation sources and matmul outputs
 
-enum PrepMode { PREP_PLAIN = 0, PREP_LN = 1, PREP_EMBED_LN = 2, PREP_ATTN = 3 };
+enum PrepMode { PREP_PLAIN = 0, PREP_LN = 1, PREP_EMBED_LN = 2 };
 
 struct PrepArgs {
     const float *x;       // input rows [rows][K] (PLAIN, LN)
     float *x_out;         // EMBED_LN: residual stream written here
     const float *gamma, *beta;
-    // EMBED_LN
+    // EMBED_LN: x = E[id] * scale + pos_table[*step + pos_base]
     Matrix embed;
     const uint32_t *ids;
     const uint32_t *step;
@@ -88,284 +82,32 @@ struct PrepArgs {
     uint32_t pos_base;
     float scale;
     int rows, K;
-    QAct out;
-    int keep_f32;  // also store the (normalised) f32 values (for F32 weights)
-    float *xf;     // [rows][K]
-    int group;     // blocks per activation scale: 1 (Q8_0 consumers) or 8 (Q4_K / Q6_K)
-    int ctype;     // weight type of the consuming matrix (tensor-core layout)
 };
-
-// Activation scale group of a consumer weight type: k-quants take one f32 scale
-// per 256-value super-block (Q8_K style), Q8_0 one f16-rounded scale per block.
-__host__ __device__ constexpr int act_group(int type) { return type == T_Q4_K || type == T_Q6_K ? 8 : 1; }
-
-// Quantizes G consecutive blocks (y[u] = element lane of block t0+u of `row`)
-// with one scale: d = amax/127 over the G*32 values, q = round(y * (127/amax)).
-// G = 1 stores the scale f16-rounded (q8_1 / Q8_0 style), G = 8 as f32 (Q8_K).
-template <int G>
-__device__ __forceinline__ void quantize_group(const float (&y)[G], int8_t *q, float *d, int *s32, int *s16, int t0,
-                                               int lane) {
-    float m = fabsf(y[0]);
-#pragma unroll
-    for (int u = 1; u < G; ++u) m = fmaxf(m, fabsf(y[u]));
-    const float amax = warp_max_nonneg(m);
-    const float dd = __fdiv_rn(amax, 127.0f), id = __fdiv_rn(127.0f, amax);
-    // every block's values first, then the half sums as independent full-warp
-    // reductions (no divergent branch between them), then one lane's stores
-    int v[G], lo[G], hi[G];
-#pragma unroll
-    for (int u = 0; u < G; ++u) {
-        v[u] = amax == 0.0f ? 0 : (int)roundf(__fmul_rn(y[u], id));
-        q[32 * (t0 + u) + lane] = (int8_t)v[u];
-    }
-#pragma unroll
-    for (int u = 0; u < G; ++u) {
-        lo[u] = warp_isum_redux(lane < 16 ? v[u] : 0);
-        hi[u] = warp_isum_redux(lane < 16 ? 0 : v[u]);
-    }
-    if (lane == 0) {
-#pragma unroll
-        for (int u = 0; u < G; ++u) {
-            const int t = t0 + u;
-            d[t] = G == 1 ? round_h(dd) : dd;
-            s16[2 * t] = lo[u];
-            s16[2 * t + 1] = hi[u];
-            s32[t] = lo[u] + hi[u];
-        }
-    }
-}
-
-// Row `row` of a global QAct as quantize_group destinations.
-#define QACT_ROW(o, row) (o).q + (size_t)(row) * (o).K, (o).d + (size_t)(row) * ((o).K >> 5), \
-                         (o).s32 + (size_t)(row) * ((o).K >> 5), (o).s16 + (size_t)(row) * ((o).K >> 4)
-
-template <int MODE>
-__global__ void __launch_bounds__(256) qprep_kernel(PrepArgs p) {
-    const int lane = threadIdx.x & 31;
-    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
-    if (row >= p.rows) return;
-    const int K = p.K, T = K >> 5, G = p.group == 8 ? 8 : 1;
-    const float *x = p.x + (size_t)row * K;
-    if constexpr (MODE == PREP_EMBED_LN) {
-        const uint32_t id = p.ids[row];
-        const float *pos = p.pos_table + (size_t)(*p.step + p.pos_base) * K;
-        float *xo = p.x_out + (size_t)row * K;
-        for (int t = 0; t < T; ++t) {
-            const int i = 32 * t + lane;
-            xo[i] = __fadd_rn(__fmul_rn(deq_elem(p.embed, (int)id, i), p.scale), pos[i]);
-        }
-        x = xo;
-        __syncwarp();
-    }
-    if constexpr (MODE == PREP_PLAIN) {
-        for (int t = 0; t < T; t += G) {
-            float v[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                v[u] = u < G ? x[32 * (t + u) + lane] : 0.0f;
-                if (u < G && p.keep_f32) p.xf[(size_t)row * K + 32 * (t + u) + lane] = v[u];
-            }
-            if (G == 8) quantize_group<8>(v, QACT_ROW(p.out, row), t, lane);
-            else quantize_group<1>(reinterpret_cast<const float(&)[1]>(v[0]), QACT_ROW(p.out, row), t, lane);
-        }
-        return;
-    }
-    // LayerNorm (eps 1e-5): mean and variance with the lane-ordered pairwise sum.
-    float s = 0.0f;
-    for (int t = 0; t < T; ++t) s = t == 0 ? x[lane] : __fadd_rn(s, x[32 * t + lane]);
-    const float mean = __fdiv_rn(warp_tree(s), (float)K);
-    float s2 = 0.0f;
-    for (int t = 0; t < T; ++t) {
-        const float c = __fsub_rn(x[32 * t + lane], mean);
-        const float c2 = __fmul_rn(c, c);
-        s2 = t == 0 ? c2 : __fadd_rn(s2, c2);
-    }
-    const float var = __fdiv_rn(warp_tree(s2), (float)K);
-    const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
-    for (int t = 0; t < T; t += G) {
-        float v[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const int i = 32 * (t + u) + lane;
-            v[u] = 0.0f;
-            if (u < G) {
-                v[u] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(x[i], mean), rstd), p.gamma[i]), p.beta[i]);
-                if (p.keep_f32) p.xf[(size_t)row * K + i] = v[u];
-            }
-        }
-        if (G == 8) quantize_group<8>(v, QACT_ROW(p.out, row), t, lane);
-        else quantize_group<1>(reinterpret_cast<const float(&)[1]>(v[0]), QACT_ROW(p.out, row), t, lane);
-    }
-}
-
-// ---------------------------------------------------------------------------
-// Matmul rows: one warp per weight row, lane l owns blocks [l*G, l*G+G).
 
 enum Epi { EPI_STORE = 0, EPI_RELU = 1, EPI_RESID = 2, EPI_QKV = 3, EPI_CROSSKV = 4, EPI_ARGMAX = 5 };
 
+// Where a matmul's outputs go (epilogue parameters).
 struct GemvArgs {
     Matrix W;
-    QAct x;           // quantized activations [rows][K]
-    const float *xf;  // f32 activations (F32 weights)
-    int rows;         // activation rows (batch)
+    int rows;         // activation rows
     float *y;         // [rows][N] (STORE, RELU, RESID in place)
-    // QKV: q out [rows][d]; caches [rows][H][m][hd]
+    // QKV: q out [rows][d]; caches [rows][H][m][hd] at slot *step
     float *q;
     __half *kc, *vc;
     const uint32_t *step;
     int H, hd, m;
     // CROSSKV: caches [b][H][S][hd], token row = bi * S + j
     int S;
-    // ARGMAX
+    // ARGMAX: per (row, CTA) best (value, index); optional logits [rows][N]
     float *part_v;
     uint32_t *part_i;
-    float *logits;  // optional [rows][N]
+    float *logits;
 };
 
-// Weight loads: read-only global loads, or plain loads when the weights were
-// staged in shared memory (GLOBAL = false).
-template <bool GLOBAL, typename T>
-__device__ __forceinline__ T ldw(const T *p) {
-    if constexpr (GLOBAL) return __ldg(p);
-    else return *p;
-}
-
-// One 32-block of a weight row against one activation row. The integer part
-// of the block is accumulated exactly into (S1, S2) by accum(); finish() turns
-// the sums of a whole unit into its float partial. A unit is one block for
-// Q8_0 and one 256-value super-block (8 blocks) for Q4_K / Q6_K:
-//   Q8_0: S1 = I;                          p = (d*xd) * float(S1)
-//   Q4_K: S1 += sc*I, S2 += m*sum(xq);     p = xd * (d*float(S1) - dmin*float(S2))
-//   Q6_K: S1 += sc_a*I_a + sc_b*I_b;       p = (d*xd) * float(S1)
-// (I = sum of weight x activation integers over the block, I_a / I_b over its
-// 16-value halves with the 6-bit values offset by -32.)
-template <int TYPE>
-struct BlockW;
-
-template <int TYPE>
-__host__ __device__ constexpr int unit_blocks() { return TYPE == T_Q4_K || TYPE == T_Q6_K ? 8 : 1; }
-
-template <>
-struct BlockW<T_Q8_0> {
-    int w[8];
-    float d;
-    template <bool GLOBAL = true>
-    __device__ __forceinline__ void load(const Matrix &W, int row, int j) {
-        const size_t bi = wslot(W, row, j);
-        const int4 *src = reinterpret_cast<const int4 *>(W.a + bi * 32);
-        const int4 a0 = ldw<GLOBAL>(src), a1 = ldw<GLOBAL>(src + 1);
-        w[0] = a0.x; w[1] = a0.y; w[2] = a0.z; w[3] = a0.w;
-        w[4] = a1.x; w[5] = a1.y; w[6] = a1.z; w[7] = a1.w;
-        d = h2f(ldw<GLOBAL>(reinterpret_cast<const unsigned short *>(W.b) + bi));
-    }
-    __device__ __forceinline__ void accum(const int *x, int, int, int, int &S1, int &) const {
-        int s = 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) s = __dp4a(w[i], x[i], s);
-        S1 += s;
-    }
-    __device__ __forceinline__ float finish(int S1, int, float xd) const {
-        return __fmul_rn(__fmul_rn(d, xd), (float)S1);
-    }
-};
-
-template <>
-struct BlockW<T_Q4_K> {
-    int q[4];
-    float d, dm;
-    int sc, m;
-    template <bool GLOBAL = true>
-    __device__ __forceinline__ void load(const Matrix &W, int row, int j) {
-        const size_t bi = wslot(W, row, j);
-        const int4 a = ldw<GLOBAL>(reinterpret_cast<const int4 *>(W.a + bi * 16));
-        q[0] = a.x; q[1] = a.y; q[2] = a.z; q[3] = a.w;
-        const uint4 h = ldw<GLOBAL>(reinterpret_cast<const uint4 *>(W.b + wsslot(W, row, j >> 3) * 16));
-        d = h2f(h.x & 0xffff);
-        dm = h2f(h.x >> 16);
-        const uint32_t s0 = h.y, s1 = h.z, s2 = h.w;  // scales bytes 0-3, 4-7, 8-11
-        const int sb = j & 7;
-        auto byte = [&](int k) -> int {
-            const uint32_t w = k < 4 ? s0 : (k < 8 ? s1 : s2);
-            return (w >> (8 * (k & 3))) & 0xff;
-        };
-        if (sb < 4) {
-            sc = byte(sb) & 63;
-            m = byte(sb + 4) & 63;
-        } else {
-            sc = (byte(sb + 4) & 0xf) | ((byte(sb - 4) >> 6) << 4);
-            m = (byte(sb + 4) >> 4) | ((byte(sb) >> 6) << 4);
-        }
-    }
-    __device__ __forceinline__ void accum(const int *x, int s8, int, int, int &S1, int &S2) const {
-        int s = 0;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            s = __dp4a(q[i] & 0x0f0f0f0f, x[i], s);
-            s = __dp4a((q[i] >> 4) & 0x0f0f0f0f, x[4 + i], s);
-        }
-        S1 += sc * s;
-        S2 += m * s8;
-    }
-    __device__ __forceinline__ float finish(int S1, int S2, float xd) const {
-        return __fmul_rn(xd, __fsub_rn(__fmul_rn(d, (float)S1), __fmul_rn(dm, (float)S2)));
-    }
-};
-
-template <>
-struct BlockW<T_Q6_K> {
-    int w[8];
-    int sa, sb;
-    float d;
-    template <bool GLOBAL = true>
-    __device__ __forceinline__ void load(const Matrix &W, int row, int j) {
-        const size_t bi = wslot(W, row, j);
-        const int4 l = ldw<GLOBAL>(reinterpret_cast<const int4 *>(W.a + bi * 16));
-        const uint2 h = ldw<GLOBAL>(reinterpret_cast<const uint2 *>(W.b + bi * 8));
-        const int ql[4] = {l.x, l.y, l.z, l.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            w[i] = (ql[i] & 0x0f0f0f0f) | (int)(((h.x >> (2 * i)) & 0x03030303u) << 4);
-            w[4 + i] = ((ql[i] >> 4) & 0x0f0f0f0f) | (int)(((h.y >> (2 * i)) & 0x03030303u) << 4);
-        }
-        const unsigned short s = ldw<GLOBAL>(reinterpret_cast<const unsigned short *>(W.c) + bi);
-        sa = (int8_t)(s & 0xff);
-        sb = (int8_t)(s >> 8);
-        d = h2f(ldw<GLOBAL>(reinterpret_cast<const unsigned short *>(W.e) + wsslot(W, row, j >> 3)));
-    }
-    __device__ __forceinline__ void accum(const int *x, int, int s16a, int s16b, int &S1, int &) const {
-        int da = 0, db = 0;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            da = __dp4a(w[i], x[i], da);
-            db = __dp4a(w[4 + i], x[4 + i], db);
-        }
-        da -= 32 * s16a;
-        db -= 32 * s16b;
-        S1 += sa * da + sb * db;
-    }
-    __device__ __forceinline__ float finish(int S1, int, float xd) const {
-        return __fmul_rn(__fmul_rn(d, xd), (float)S1);
-    }
-};
-
-// Block partial p_j of row `row` against activation row n, for F32 weights:
-// an FMA chain over the block's 32 values.
-__device__ __forceinline__ float f32_block(const Matrix &W, int row, int j, const float *x) {
-    const float4 *w = reinterpret_cast<const float4 *>(W.a + wslot(W, row, j) * 128);
-    float p = 0.0f;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-        const float4 v = __ldg(w + c);
-        p = __fmaf_rn(v.x, x[4 * c], p);
-        p = __fmaf_rn(v.y, x[4 * c + 1], p);
-        p = __fmaf_rn(v.z, x[4 * c + 2], p);
-        p = __fmaf_rn(v.w, x[4 * c + 3], p);
-    }
-    return p;
-}
-
-// Epilogue of one output element (row of W, activation row n); v = the
-// row sum in block order.
+// Epilogue of one output element (row of W, activation row n); v = the dot
+// product. Bias, then the residual / ReLU / cache write of malaga.cu's fused
+// kernels (bias_residual_ln: (y + bias) + resid, malaga.cu:100; bias_relu;
+// qkv_decode's f16 K/V cache slot, malaga.cu:142-154).
 template <int EPI>
 __device__ __forceinline__ void epilogue_store(const GemvArgs &g, int row, int n, float v) {
     const Matrix &W = g.W;
@@ -397,113 +139,21 @@ __device__ __forceinline__ void epilogue_store(const GemvArgs &g, int row, int n
     }
 }
 
-// Matmul over activations already quantized in global memory: one warp per
-// group of 32 weight rows, lane = row, unit partials accumulated left to right;
-// NB activation rows per pass.
-template <int TYPE, int EPI>
-__global__ void __launch_bounds__(256) gemv_kernel(GemvArgs g) {
-    constexpr int NB = 8;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const Matrix &W = g.W;
-    const int nb = W.nb, groups = W.Np >> 5;
-    for (int grp = blockIdx.x * 8 + warp; grp < groups; grp += gridDim.x * 8) {
-        const int row = grp * 32 + lane;
-        for (int n0 = 0; n0 < g.rows; n0 += NB) {
-            float acc[NB];
-#pragma unroll
-            for (int i = 0; i < NB; ++i) acc[i] = 0.0f;
-            if constexpr (TYPE == T_F32) {
-                for (int j = 0; j < nb; ++j)
-#pragma unroll
-                    for (int i = 0; i < NB; ++i) {
-                        if (n0 + i >= g.rows) break;
-                        const float p = f32_block(W, row, j, g.xf + (size_t)(n0 + i) * W.K + 32 * j);
-                        acc[i] = j == 0 ? p : __fadd_rn(acc[i], p);
-                    }
-            } else {
-                constexpr int UB = unit_blocks<TYPE>();
-                for (int u = 0; u < nb; u += UB) {
-                    int S1[NB], S2[NB];
-#pragma unroll
-                    for (int i = 0; i < NB; ++i) S1[i] = S2[i] = 0;
-                    BlockW<TYPE> bw;
-#pragma unroll 2
-                    for (int j = u; j < u + UB; ++j) {
-                        bw.load(W, row, j);
-#pragma unroll
-                        for (int i = 0; i < NB; ++i) {
-                            const int n = n0 + i;
-                            if (n >= g.rows) break;
-                            const int4 *xs = reinterpret_cast<const int4 *>(g.x.q + (size_t)n * W.K + 32 * j);
-                            const int4 x0 = xs[0], x1 = xs[1];
-                            const int xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-                            int s32 = 0, s16a = 0, s16b = 0;
-                            if constexpr (TYPE == T_Q4_K) s32 = g.x.s32[(size_t)n * nb + j];
-                            if constexpr (TYPE == T_Q6_K) {
-                                s16a = g.x.s16[(size_t)n * 2 * nb + 2 * j];
-                                s16b = g.x.s16[(size_t)n * 2 * nb + 2 * j + 1];
-                            }
-                            bw.accum(xv, s32, s16a, s16b, S1[i], S2[i]);
-                        }
-                    }
-#pragma unroll
-                    for (int i = 0; i < NB; ++i) {
-                        const int n = n0 + i;
-                        if (n >= g.rows) break;
-                        const float p = bw.finish(S1[i], S2[i], g.x.d[(size_t)n * nb + u]);
-                        acc[i] = u == 0 ? p : __fadd_rn(acc[i], p);
-                    }
-                }
-            }
-            if (row < W.N)
-#pragma unroll
-                for (int i = 0; i < NB; ++i) {
-                    if (n0 + i >= g.rows) break;
-                    epilogue_store<EPI>(g, row, n0 + i, acc[i]);
-                }
-        }
-    }
-}
-
 // ---------------------------------------------------------------------------
-// Tensor-core activation layout (QAct tq / trec, written for one consumer)
+// Tensor-core activation layout (QAct, written for the tensor-core matmul)
 
 // Byte offset of (row r, 16-byte K chunk k16) of a K=32 int8 operand tile in
 // the UMMA K-major no-swizzle layout: 8-row core groups of 256 bytes.
 __host__ __device__ __forceinline__ int tile_off(int r, int k16) { return (r >> 3) * 256 + k16 * 128 + (r & 7) * 16; }
 
-// One unit (G blocks of 32 values, y[g] = value lane of block j0+g of token
-// `tok`) into a tensor-core activation buffer: one scale, the bytes in the UMMA
-// layout, the unit record (same arithmetic as qprep_row_kernel).
-template <int G>
-__device__ __forceinline__ void store_unit(const QAct &o, int ctype, int tok, int j0, const float (&y)[G], int lane) {
-    float m = fabsf(y[0]);
-#pragma unroll
-    for (int g = 1; g < G; ++g) m = fmaxf(m, fabsf(y[g]));
-    const float amax = warp_max_nonneg(m);
-    const float dd = __fdiv_rn(amax, 127.0f), id = __fdiv_rn(127.0f, amax);
-    const int rs = o.rs;
-    const bool sums = ctype == T_Q4_K && G == 8;  // only Q4_K records carry block sums
-    int s32[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-        const int q = amax == 0.0f ? 0 : (int)roundf(__fmul_rn(y[g], id));
-        o.tq[((size_t)(j0 + g) * (rs / 8) + (tok >> 3)) * 256 + tile_off(tok & 7, lane >> 4) + (lane & 15)] =
-            (uint8_t)(int8_t)q;
-        s32[g] = sums ? warp_isum_redux(q) : 0;
-    }
-    if (lane == 0) {
-        if (sums) {
-            int4 *rec = reinterpret_cast<int4 *>(o.trec + ((size_t)(j0 / 8) * rs + tok) * 32);
-            rec[0] = make_int4(__float_as_int(dd), (s32[0] & 0xffff) | (s32[1 % G] << 16),
-                               (s32[2 % G] & 0xffff) | (s32[3 % G] << 16), (s32[4 % G] & 0xffff) | (s32[5 % G] << 16));
-            rec[1] = make_int4((s32[6 % G] & 0xffff) | (s32[7 % G] << 16), 0, 0, 0);
-        } else if (G == 8) {
-            reinterpret_cast<float *>(o.trec)[(size_t)(j0 / 8) * rs + tok] = dd;
-        } else {
-            reinterpret_cast<float *>(o.trec)[(size_t)j0 * rs + tok] = round_h(dd);
-        }
-    }
+// Block j of activation row `tok` (value y at position lane) quantized to q8_1
+// into the tensor-core layout: the byte into the tile, lane 0 the record.
+__device__ __forceinline__ void store_block_tc(const QAct &o, int tok, int j, float y, int lane) {
+    float d, s;
+    const int q = q81_block(y, d, s);
+    o.tq[((size_t)j * (o.rs / 8) + (tok >> 3)) * 256 + tile_off(tok & 7, lane >> 4) + (lane & 15)] =
+        (uint8_t)(int8_t)q;
+    if (lane == 0) o.trec[(size_t)j * o.rs + tok] = make_float2(d, s);
 }
 
 // ---------------------------------------------------------------------------
@@ -522,11 +172,9 @@ struct AttnArgs {
     long out_row;
     int H, hd, rows, queries;  // queries per batch row (encoder: S)
     int max_keys;
-    // Optional: the outputs also quantized into the next matmul's tensor-core
-    // layout (qo.tq != null; single queries, 4 heads of one row per CTA whose
-    // 4*hd values are whole units of the consumer qo_ctype).
+    // Optional: the outputs also quantized to q8_1 in the next matmul's
+    // tensor-core layout (qo.tq != null; single queries, hd a multiple of 32).
     QAct qo;
-    int qo_ctype;
 };
 
 // Programmatic dependent launch: a kernel may start while its predecessor in
@@ -684,7 +332,7 @@ __global__ void __launch_bounds__(128) attend_kernel(AttnArgs a) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const long task = (long)blockIdx.x * 4 + warp;
     const long total = (long)a.rows * a.H * a.queries;
-    if (task >= total) return;  // (never with qo: the host launches whole CTAs then)
+    if (task >= total) return;
     const int qi = (int)(task % a.queries), h = (int)((task / a.queries) % a.H), n = (int)(task / ((long)a.queries * a.H));
     constexpr int PER = HD >= 32 ? HD / 32 : 1;
     constexpr int KC = 64;
@@ -698,27 +346,11 @@ __global__ void __launch_bounds__(128) attend_kernel(AttnArgs a) {
 #pragma unroll
         for (int c = 0; c < PER; ++c) o[lane + 32 * c] = res[c];
     }
-    if (a.qo.tq) {
-        // the CTA's 4 heads (4*HD consecutive values of row n) as units of the consumer
-        __shared__ float ov[4 * 128];
-        if (live)
+    if (a.qo.tq && live) {
+        // the head's outputs as q8_1 blocks of the next matmul's input: lane l
+        // holds value 32c + l of the head, i.e. position l of block c
 #pragma unroll
-            for (int c = 0; c < PER; ++c) ov[warp * HD + lane + 32 * c] = res[c];
-        __syncthreads();
-        const int j0 = (h - warp) * HD / 32;  // first block of the CTA's values
-        if (a.qo_ctype == T_Q4_K || a.qo_ctype == T_Q6_K) {
-            for (int u = warp; u < 4 * HD / 256; u += 4) {
-                float y[8];
-#pragma unroll
-                for (int g = 0; g < 8; ++g) y[g] = ov[256 * u + 32 * g + lane];
-                store_unit<8>(a.qo, a.qo_ctype, n, j0 + 8 * u, y, lane);
-            }
-        } else {
-            for (int t = warp; t < 4 * HD / 32; t += 4) {
-                const float y[1] = {ov[32 * t + lane]};
-                store_unit<1>(a.qo, a.qo_ctype, n, j0 + t, y, lane);
-            }
-        }
+        for (int c = 0; c < PER; ++c) store_block_tc(a.qo, n, h * (HD / 32) + c, res[c], lane);
     }
 }
 

@@ -1,12 +1,13 @@
 // Allocation-free greedy token choice over logits already in device memory.
 //
-// This is a variant of the two-pass argmax that the fused LM-head kernel uses
-// (gemv_kernel<..., EPI_ARGMAX> writes per-CTA (value, index) partials to
-// scratch, greedy_finalize_kernel merges them). Here the partials live in a
-// file-scope __device__ array instead of memory the context allocated, so the
-// entry point never calls cudaMalloc / cudaFree.
+// This is a variant of the two-pass argmax of the engine's LM head (the fused
+// matmul kernels, small_mm_kernel / gemm_tc_kernel with EPI_ARGMAX, write
+// per-CTA (value, index) partials to buffers the context allocated, and
+// greedy_finalize_kernel merges them). Here the partials live in a file-scope
+// __device__ array instead, so the entry point never calls cudaMalloc /
+// cudaFree.
 //
-// Who needs it: callers that must not allocate device memory at this point —
+// Who needs it: callers that must not allocate device memory at this point --
 // code running while another framework's stream capture is active (an
 // allocation there either fails or is baked into the graph), hosts whose
 // caching allocator has already reserved the GPU's memory (candle, PyTorch),
@@ -70,7 +71,9 @@ __global__ void argmax_final_noalloc(const Partial *part, uint32_t rows, uint32_
         for (int p = lane; p < kParts; p += 32) mgb::argmax_merge(best, bi, part[row * kParts + p].v, part[row * kParts + p].i);
         mgb::warp_argmax(best, bi);
         if (lane == 0) {
-            ids[row] = bi;
+            // NaN logits never win a comparison: a row of only NaNs keeps no
+            // index and gets id 0 (value -inf), so the id is always < vocab
+            ids[row] = bi == 0xffffffffu ? 0u : bi;
             if (vals) vals[row] = best;
         }
     }

@@ -85,6 +85,14 @@ __device__ __forceinline__ float warp_tree(float v) {
     return v;
 }
 
+// The reference kernels' warp sum (llama.cpp / candle warp_reduce_sum):
+// x += shfl_xor(x, m) for m = 16, 8, 4, 2, 1; every lane ends with the result.
+__device__ __forceinline__ float warp_sum_bf(float v) {
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, m));
+    return v;
+}
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -95,6 +103,19 @@ __device__ __forceinline__ float warp_max(float v) {
 // (their bit patterns order like the values).
 __device__ __forceinline__ float warp_max_nonneg(float v) {
     return __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(v)));
+}
+
+// q8_1 quantization of one 32-value block held one value per lane (lane =
+// position), as candle-kernels' quantize_q8_1: amax = max |x|, s = warp sum of
+// x (warp_sum_bf), d = amax / 127, q = amax == 0 ? 0 : roundf(x / d) (IEEE
+// division, halves away from zero). Returns q; d and s come back rounded to
+// f16 (the values the matmuls read), identical in every lane.
+__device__ __forceinline__ int q81_block(float x, float &d, float &s) {
+    const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(x))));
+    s = round_h(warp_sum_bf(x));
+    const float dd = __fdiv_rn(amax, 127.0f);
+    d = round_h(dd);
+    return amax == 0.0f ? 0 : (int)roundf(__fdiv_rn(x, dd));
 }
 
 // Integer sum across the warp, one reduction instruction.

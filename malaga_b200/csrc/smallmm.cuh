@@ -1,0 +1,437 @@
+// Small-batch quantized matmul (at most 8 activation rows) with the
+// reference's MMVQ arithmetic, fused with its activation prologue and
+// epilogue (sm_100a).
+//
+// One launch replaces the reference's chain "bias_residual_ln / embed_pos_ln
+// (malaga.cu:89-130) -> candle quantize_q8_1 -> QMatMul MMVQ (candle-core
+// 0.11.0 src/quantized/cuda.rs, candle-kernels 0.11.0 src/quantized.cu) ->
+// bias / ReLU / residual / qkv_decode epilogue (malaga.cu:133-154)".
+//
+// Data flow of one CTA (a contiguous range of weight rows):
+//   1. thread 0 starts 1-D bulk copies (TMA) of the first chunks of its rows
+//      (row layout, engine.h) into a ring of shared-memory stages; weights do
+//      not depend on the previous kernel, so this overlaps its tail (PDL);
+//   2. after griddepcontrol.wait the warps build the q8_1 activations of the
+//      NC batch rows in shared memory (LayerNorm / embedding + position +
+//      LayerNorm / plain input, the engine's fixed LayerNorm order);
+//   3. per chunk, warp w takes rows w, w+8, ...: the 32 lanes play MMVQ's
+//      NW x 32 threads for that row -- lane l computes, for virtual warp v,
+//      thread 32v + l's vec_dot sum over its blocks, adds the virtual warps in
+//      order, and a butterfly sum over the lanes gives the output (identical in
+//      every lane); lane n stores column n;
+//   4. the freed stage is refilled with the chunk RS ahead.
+// Every mbarrier wait is bounded; on a timeout the CTA records an error flag,
+// waits (bounded) for its own copies in flight and returns.
+#pragma once
+#include "kernels.cuh"
+
+namespace mgb {
+
+// q8_1 activations of NC batch rows in shared memory (F32 weights: the f32
+// values instead).
+struct SmAct {
+    int8_t *q;   // [NC][K]
+    float *d;    // [NC][K/32] block scales (f16 values)
+    float *xf;   // [NC][K] (F32 weights only)
+};
+
+// Bytes of one weight row in the row layout (= its GGUF bytes; F32: 4K).
+__host__ __device__ inline int row_bytes_of(int type, int K) {
+    switch (type) {
+        case T_Q8_0: return K / 32 * 34;
+        case T_Q4_K: return K / 256 * 144;
+        case T_Q6_K: return K / 256 * 210;
+        default: return 4 * K;
+    }
+}
+
+// Per-row bytes of the row layout's regions ra, rb, rc, re.
+__host__ __device__ inline void row_regions(int type, int K, int (&rb)[4]) {
+    rb[1] = rb[2] = rb[3] = 0;
+    switch (type) {
+        case T_Q8_0: rb[0] = K; rb[1] = K / 16; break;
+        case T_Q4_K: rb[0] = K / 256 * 144; break;
+        case T_Q6_K: rb[0] = K / 2; rb[1] = K / 4; rb[2] = K / 16; rb[3] = K / 128; break;
+        default: rb[0] = 4 * K; break;
+    }
+}
+
+struct SmallArgs {
+    GemvArgs g;        // matrix and outputs (g.rows: activation rows of the whole matmul)
+    PrepArgs p;        // activation source
+    int n0;            // first activation row of this launch (launches cover at most 8 rows)
+    int rows_per_cta;  // weight rows per CTA (a multiple of 8)
+    int chunk;         // weight rows per stage (a multiple of 8)
+    int stages;        // ring depth (1..4); 0 for F32 weights (read from global memory)
+    uint32_t *err;
+};
+
+__host__ __device__ inline size_t small_act_bytes(int NC, int K, int type, int mode) {
+    size_t n = (size_t)NC * K + (size_t)NC * (K / 32) * 4;        // q, d
+    if (type == T_F32) n += (size_t)NC * K * 4;                   // xf
+    if (mode != PREP_PLAIN) n += (size_t)NC * K * 4 + (size_t)8 * K + (size_t)NC * 8;  // rows, gamma/beta, stats
+    return (n + 15) / 16 * 16;
+}
+
+__device__ __forceinline__ int lds32(const void *p) { return *reinterpret_cast<const int *>(p); }
+
+// ---------------------------------------------------------------------------
+// MMVQ per type. Row data in shared memory; out[n] = the output of column n.
+
+// Q6_K (candle vec_dot_q6_K_q8_1, qi 32, vdr 1): thread t handles super-blocks
+// t/32 + i*NW; lane l reads ql int l, 4 values of blocks A and A+2 of the
+// super-block (A = 4(l/16) + (l%16)/8) at positions 4(l%8)..+3:
+//   sf = dx_{A+2}*float(I_1*sc_1) + dx_A*float(I_0*sc_0) (two FMAs from 0), P = fma(d, sf, P).
+template <int NC, int NW>
+__device__ __forceinline__ void mmvq_q6k(const uint8_t *ql, const uint8_t *qh, const int8_t *sc, const __half *dd,
+                                         int nsb, const SmAct &s, int K, int lane, float (&out)[NC]) {
+    const int nb = K >> 5;
+    const int A = 4 * (lane >> 4) + ((lane & 15) >> 3), p0 = 4 * (lane & 7);
+    const int hoff = 4 * (8 * (lane >> 4) + (lane & 7)), hsh = 2 * ((lane & 15) >> 3);
+    const int so = 8 * (lane >> 4) + ((lane & 15) >> 2);
+    float leaf[NC];
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+        float P[NC];
+#pragma unroll
+        for (int n = 0; n < NC; ++n) P[n] = 0.0f;
+        for (int kb = w; kb < nsb; kb += NW) {
+            const int vl = lds32(ql + kb * 128 + 4 * lane);
+            const int vh = lds32(qh + kb * 64 + hoff) >> hsh;
+            const int sc0 = sc[kb * 16 + so], sc1 = sc[kb * 16 + so + 4];
+            const float d6 = __half2float(dd[kb]);
+            const int vi0 = __vsubss4((vl & 0x0F0F0F0F) | ((vh << 4) & 0x30303030), 0x20202020);
+            const int vi1 = __vsubss4(((vl >> 4) & 0x0F0F0F0F) | (vh & 0x30303030), 0x20202020);
+            const int j0 = 8 * kb + A;
+#pragma unroll
+            for (int n = 0; n < NC; ++n) {
+                const int8_t *xq = s.q + (size_t)n * K;
+                const int u0 = lds32(xq + 32 * j0 + p0), u1 = lds32(xq + 32 * (j0 + 2) + p0);
+                const float d0 = s.d[n * nb + j0], d1 = s.d[n * nb + j0 + 2];
+                const float sf = __fmaf_rn(d1, (float)(__dp4a(vi1, u1, 0) * sc1),
+                                           __fmaf_rn(d0, (float)(__dp4a(vi0, u0, 0) * sc0), 0.0f));
+                P[n] = __fmaf_rn(d6, sf, P[n]);
+            }
+        }
+#pragma unroll
+        for (int n = 0; n < NC; ++n) leaf[n] = w == 0 ? P[n] : __fadd_rn(leaf[n], P[n]);
+    }
+#pragma unroll
+    for (int n = 0; n < NC; ++n) out[n] = warp_sum_bf(leaf[n]);
+}
+
+// Q4_K (candle vec_dot_q4_K_q8_1, qi 32, vdr 2): 16 threads per super-block;
+// thread t handles super-blocks t/16 + i*2NW, sub-blocks 2c (low nibbles) and
+// 2c+1 (high) with c = (t%16)/4, positions 4o..4o+3 and 16+4o..+3 (o = t%4):
+//   sumf_d = sum_i dx_i*float(I_i*sc_i), sumf_m = sum_i dx_i*float(Q_i*m_i)
+//   P += fma(d, sumf_d, -(dmin*sumf_m))   (Q_i = sum of the 8 activation bytes)
+template <int NC, int NW>
+__device__ __forceinline__ void mmvq_q4k(const uint8_t *row, int nsb, const SmAct &s, int K, int lane,
+                                         float (&out)[NC]) {
+    const int nb = K >> 5;
+    const int c = (lane & 15) >> 2, o = lane & 3;
+    float leaf[NC];
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+        float P[NC];
+#pragma unroll
+        for (int n = 0; n < NC; ++n) P[n] = 0.0f;
+        for (int kb = 2 * w + (lane >> 4); kb < nsb; kb += 2 * NW) {
+            const uint8_t *sb = row + kb * 144;
+            const uint32_t dmw = (uint32_t)lds32(sb);
+            const float dall = h2f((uint16_t)(dmw & 0xffff)), dmin = h2f((uint16_t)(dmw >> 16));
+            const uint8_t *sp = sb + 4;
+            int sca, scb, ma, mb;
+            if (c < 2) {
+                sca = sp[2 * c] & 63;
+                scb = sp[2 * c + 1] & 63;
+                ma = sp[2 * c + 4] & 63;
+                mb = sp[2 * c + 5] & 63;
+            } else {
+                const int ja = 2 * c, jb = 2 * c + 1;
+                sca = (sp[ja + 4] & 0xf) | ((sp[ja - 4] >> 6) << 4);
+                ma = (sp[ja + 4] >> 4) | ((sp[ja] >> 6) << 4);
+                scb = (sp[jb + 4] & 0xf) | ((sp[jb - 4] >> 6) << 4);
+                mb = (sp[jb + 4] >> 4) | ((sp[jb] >> 6) << 4);
+            }
+            const int v0 = lds32(sb + 16 + 32 * c + 4 * o), v1 = lds32(sb + 32 + 32 * c + 4 * o);
+            const int ja = 8 * kb + 2 * c;
+#pragma unroll
+            for (int n = 0; n < NC; ++n) {
+                const int8_t *xq = s.q + (size_t)n * K + 32 * ja + 4 * o;
+                const int ua0 = lds32(xq), ua1 = lds32(xq + 16), ub0 = lds32(xq + 32), ub1 = lds32(xq + 48);
+                const float d8a = s.d[n * nb + ja], d8b = s.d[n * nb + ja + 1];
+                const int dot1a = __dp4a(v1 & 0x0F0F0F0F, ua1, __dp4a(v0 & 0x0F0F0F0F, ua0, 0));
+                const int dot1b = __dp4a((v1 >> 4) & 0x0F0F0F0F, ub1, __dp4a((v0 >> 4) & 0x0F0F0F0F, ub0, 0));
+                const int dot2a = __dp4a(0x01010101, ua1, __dp4a(0x01010101, ua0, 0));
+                const int dot2b = __dp4a(0x01010101, ub1, __dp4a(0x01010101, ub0, 0));
+                const float sd = __fmaf_rn(d8b, (float)(dot1b * scb), __fmaf_rn(d8a, (float)(dot1a * sca), 0.0f));
+                const float sm = __fmaf_rn(d8b, (float)(dot2b * mb), __fmaf_rn(d8a, (float)(dot2a * ma), 0.0f));
+                P[n] = __fadd_rn(P[n], __fmaf_rn(dall, sd, -__fmul_rn(dmin, sm)));
+            }
+        }
+#pragma unroll
+        for (int n = 0; n < NC; ++n) leaf[n] = w == 0 ? P[n] : __fadd_rn(leaf[n], P[n]);
+    }
+#pragma unroll
+    for (int n = 0; n < NC; ++n) out[n] = warp_sum_bf(leaf[n]);
+}
+
+// Q8_0 (candle vec_dot_q8_0_q8_1, qi 8, vdr 2): 4 threads per block; thread t
+// handles blocks t/4 + i*8NW, values 8o..8o+7 (o = t%4): P = fma(dw*dx, float(I), P).
+template <int NC, int NW>
+__device__ __forceinline__ void mmvq_q80(const uint8_t *qs, const __half *dd, int nb, const SmAct &s, int K, int lane,
+                                         float (&out)[NC]) {
+    const int o = lane & 3;
+    float leaf[NC];
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+        float P[NC];
+#pragma unroll
+        for (int n = 0; n < NC; ++n) P[n] = 0.0f;
+        for (int kb = 8 * w + (lane >> 2); kb < nb; kb += 8 * NW) {
+            const int v0 = lds32(qs + kb * 32 + 8 * o), v1 = lds32(qs + kb * 32 + 8 * o + 4);
+            const float dw = __half2float(dd[kb]);
+#pragma unroll
+            for (int n = 0; n < NC; ++n) {
+                const int8_t *xq = s.q + (size_t)n * K + 32 * kb + 8 * o;
+                const int sumi = __dp4a(v1, lds32(xq + 4), __dp4a(v0, lds32(xq), 0));
+                P[n] = __fmaf_rn(__fmul_rn(dw, s.d[n * nb + kb]), (float)sumi, P[n]);
+            }
+        }
+#pragma unroll
+        for (int n = 0; n < NC; ++n) leaf[n] = w == 0 ? P[n] : __fadd_rn(leaf[n], P[n]);
+    }
+#pragma unroll
+    for (int n = 0; n < NC; ++n) out[n] = warp_sum_bf(leaf[n]);
+}
+
+// F32 weights (candle: a cuBLAS matmul; this project's order): lane l's FMA
+// chain over elements l, l+32, ..., then the butterfly sum.
+template <int NC>
+__device__ __forceinline__ void mm_f32(const float *w, const SmAct &s, int K, int lane, float (&out)[NC]) {
+#pragma unroll
+    for (int n = 0; n < NC; ++n) {
+        const float *x = s.xf + (size_t)n * K;
+        float acc = 0.0f;
+        for (int i = lane; i < K; i += 32) acc = __fmaf_rn(w[i], x[i], acc);
+        out[n] = warp_sum_bf(acc);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Activation prologue: the NC rows' inputs (rows >= p.rows are zero), the
+// LayerNorm statistics (warp per row: lane-ordered sums, SUM32 tree), then
+// (row, block) tasks over the warps: normalise and quantize to q8_1.
+
+template <int MODE>
+__device__ __forceinline__ float small_input(const PrepArgs &p, const float *pos, int n, int i) {  // n: global row
+    if constexpr (MODE == PREP_EMBED_LN)
+        return __fadd_rn(__fmul_rn(deq_elem(p.embed, (int)p.ids[n], i), p.scale), pos[i]);
+    else
+        return p.x[(size_t)n * p.K + i];
+}
+
+template <int MODE, bool F32W>
+__device__ void small_prologue(const PrepArgs &p, int n0, const SmAct &s, int NC, uint8_t *lnbuf, bool write_x) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int K = p.K, T = K >> 5, rows = min(NC, p.rows - n0);
+    const float *pos = nullptr;
+    float *xs = nullptr, *gb = nullptr, *st = nullptr;
+    if constexpr (MODE != PREP_PLAIN) {
+        xs = reinterpret_cast<float *>(lnbuf);     // [NC][K] input rows
+        gb = xs + (size_t)NC * K;                  // gamma[K], beta[K]
+        st = gb + 2 * K;                           // [NC] mean, rstd
+        if constexpr (MODE == PREP_EMBED_LN) pos = p.pos_table + (size_t)(*p.step + p.pos_base) * K;
+        for (int i = threadIdx.x; i < K; i += blockDim.x) {
+            gb[i] = __ldg(p.gamma + i);
+            gb[K + i] = __ldg(p.beta + i);
+        }
+        for (int n = warp; n < rows; n += nw) {
+            float sum = 0.0f;
+            for (int t = 0; t < T; ++t) {
+                const int i = 32 * t + lane;
+                const float v = small_input<MODE>(p, pos, n0 + n, i);
+                xs[(size_t)n * K + i] = v;
+                if constexpr (MODE == PREP_EMBED_LN)
+                    if (write_x) p.x_out[(size_t)(n0 + n) * K + i] = v;
+                sum = t == 0 ? v : __fadd_rn(sum, v);
+            }
+            const float mean = __fdiv_rn(warp_tree(sum), (float)K);
+            float s2 = 0.0f;
+            for (int t = 0; t < T; ++t) {
+                const float c = __fsub_rn(xs[(size_t)n * K + 32 * t + lane], mean);
+                const float c2 = __fmul_rn(c, c);
+                s2 = t == 0 ? c2 : __fadd_rn(s2, c2);
+            }
+            const float var = __fdiv_rn(warp_tree(s2), (float)K);
+            if (lane == 0) {
+                st[2 * n] = mean;
+                st[2 * n + 1] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
+            }
+        }
+        __syncthreads();
+    }
+    // (row, block) tasks; loads of 8 tasks in flight per warp
+    constexpr int PIPE = 8;
+    const int tasks = NC * T;
+    for (int base = warp; base < tasks; base += nw * PIPE) {
+        float y[PIPE];
+#pragma unroll
+        for (int u = 0; u < PIPE; ++u) {
+            const int task = base + u * nw, n = task / T, i = 32 * (task % T) + lane;
+            y[u] = 0.0f;
+            if (task < tasks && n < rows) {
+                if constexpr (MODE == PREP_PLAIN) y[u] = p.x[(size_t)(n0 + n) * K + i];
+                else y[u] = xs[(size_t)n * K + i];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < PIPE; ++u) {
+            const int task = base + u * nw;
+            if (task >= tasks) break;  // uniform across the warp
+            const int n = task / T, t = task % T, i = 32 * t + lane;
+            float v = y[u];
+            if constexpr (MODE != PREP_PLAIN)
+                if (n < rows)
+                    v = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v, st[2 * n]), st[2 * n + 1]), gb[i]), gb[K + i]);
+            if constexpr (F32W) {
+                s.xf[(size_t)n * K + i] = v;
+            } else {
+                float d, sm;
+                const int q = q81_block(v, d, sm);
+                s.q[(size_t)n * K + i] = (int8_t)q;
+                if (lane == 0) s.d[n * T + t] = d;
+            }
+        }
+    }
+    __syncthreads();
+}
+
+// ---------------------------------------------------------------------------
+
+template <int TYPE, int EPI, int MODE, int NC, int NW>
+__global__ void __launch_bounds__(256) small_mm_kernel(const __grid_constant__ SmallArgs A) {
+    extern __shared__ __align__(16) uint8_t sm_raw[];
+    __shared__ __align__(8) uint64_t full[4];
+    __shared__ float best_v[8][NC];
+    __shared__ uint32_t best_i[8][NC];
+    const GemvArgs &g = A.g;
+    const Matrix &W = g.W;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr bool STAGED = TYPE != T_F32;  // F32 rows are read from global memory
+    const int K = W.K, RS = STAGED ? A.stages : 1, CR = A.chunk, n0 = A.n0;
+    const int r0 = blockIdx.x * A.rows_per_cta, r1 = min(W.Np, r0 + A.rows_per_cta);
+    const int nchunks = r0 < r1 ? (r1 - r0 + CR - 1) / CR : 0;
+    int rb[4];
+    row_regions(TYPE, K, rb);
+    const int RB = rb[0] + rb[1] + rb[2] + rb[3];
+    const size_t stage_bytes = (size_t)CR * RB;
+    const uint8_t *src[4] = {W.ra, W.rb, W.rc, W.re};
+    // shared layout: [RS stages][activations]
+    uint8_t *stages = sm_raw;
+    uint8_t *act = sm_raw + (STAGED ? (size_t)RS * stage_bytes : 0);
+    auto issue = [&](int ci) {  // thread 0: chunk ci into stage ci % RS
+        const int c0 = r0 + ci * CR, cr = min(CR, r1 - c0);
+        uint64_t *bar = &full[ci % RS];
+        uint8_t *dst = stages + (size_t)(ci % RS) * stage_bytes;
+        mbar_expect_tx(bar, (uint32_t)(cr * RB));
+        for (int k = 0; k < 4; ++k) {
+            if (!rb[k]) continue;
+            bulk_g2s(dst, src[k] + (size_t)c0 * rb[k], (uint32_t)(cr * rb[k]), bar);
+            dst += (size_t)CR * rb[k];
+        }
+    };
+    if (STAGED && tid == 0) {
+        for (int i = 0; i < RS; ++i) mbar_init(&full[i], 1);
+        for (int i = 0; i < min(RS, nchunks); ++i) issue(i);
+    }
+    if constexpr (EPI == EPI_ARGMAX)
+        if (lane < NC) {
+            best_v[warp][lane] = kNegInf;
+            best_i[warp][lane] = 0xffffffffu;
+        }
+    pdl_launch_dependents();
+    pdl_wait();
+    SmAct s;
+    s.q = reinterpret_cast<int8_t *>(act);
+    s.d = reinterpret_cast<float *>(act + (size_t)NC * K);
+    s.xf = reinterpret_cast<float *>(act + (size_t)NC * K + (size_t)NC * (K / 32) * 4);
+    uint8_t *lnbuf = reinterpret_cast<uint8_t *>(s.xf) + (TYPE == T_F32 ? (size_t)NC * K * 4 : 0);
+    small_prologue<MODE, TYPE == T_F32>(A.p, n0, s, NC, lnbuf, blockIdx.x == 0);
+
+    float bv = kNegInf;
+    uint32_t bi = 0xffffffffu;
+    int ci = 0;
+    bool ok = true;
+    for (; ci < nchunks; ++ci) {
+        if constexpr (STAGED) {
+            ok = mbar_wait(&full[ci % RS], (uint32_t)((ci / RS) & 1));
+            ok = __syncthreads_and(ok);
+            if (!ok) break;
+        }
+        const int c0 = r0 + ci * CR, cr = min(CR, r1 - c0);
+        const uint8_t *st = STAGED ? stages + (size_t)(ci % RS) * stage_bytes : W.ra + (size_t)c0 * RB;
+        for (int lr = warp; lr < cr; lr += 8) {
+            const int row = c0 + lr;
+            float out[NC];
+            if constexpr (TYPE == T_Q6_K) {
+                const uint8_t *ql = st + (size_t)lr * rb[0];
+                const uint8_t *qh = st + (size_t)CR * rb[0] + (size_t)lr * rb[1];
+                const int8_t *sc = reinterpret_cast<const int8_t *>(st + (size_t)CR * (rb[0] + rb[1]) + (size_t)lr * rb[2]);
+                const __half *dd =
+                    reinterpret_cast<const __half *>(st + (size_t)CR * (rb[0] + rb[1] + rb[2]) + (size_t)lr * rb[3]);
+                mmvq_q6k<NC, NW>(ql, qh, sc, dd, W.nsb, s, K, lane, out);
+            } else if constexpr (TYPE == T_Q4_K) {
+                mmvq_q4k<NC, NW>(st + (size_t)lr * rb[0], W.nsb, s, K, lane, out);
+            } else if constexpr (TYPE == T_Q8_0) {
+                const __half *dd = reinterpret_cast<const __half *>(st + (size_t)CR * rb[0] + (size_t)lr * rb[1]);
+                mmvq_q80<NC, NW>(st + (size_t)lr * rb[0], dd, W.nb, s, K, lane, out);
+            } else {
+                mm_f32<NC>(reinterpret_cast<const float *>(st + (size_t)lr * rb[0]), s, K, lane, out);
+            }
+            if (row < W.N) {
+                // lane n handles column n (every lane holds every output)
+#pragma unroll
+                for (int n = 0; n < NC; ++n) {
+                    if (n != lane || n0 + n >= g.rows) continue;
+                    if constexpr (EPI == EPI_ARGMAX) {
+                        if (g.logits) g.logits[(size_t)(n0 + n) * W.N + row] = out[n];
+                        argmax_merge(bv, bi, out[n], (uint32_t)row);
+                    } else {
+                        epilogue_store<EPI>(g, row, n0 + n, out[n]);
+                    }
+                }
+            }
+        }
+        if constexpr (STAGED) {
+            __syncthreads();  // the stage is free
+            if (tid == 0 && ci + RS < nchunks) issue(ci + RS);
+        }
+    }
+    if (!ok) {
+        // a copy never completed: report, wait (bounded) for this CTA's copies
+        // still in flight, produce nothing more
+        if (tid == 0) {
+            atomicOr(A.err, 2u);
+            for (int k = ci; k < min(nchunks, ci + RS); ++k) mbar_wait(&full[k % RS], (uint32_t)((k / RS) & 1));
+        }
+        return;
+    }
+    if constexpr (EPI == EPI_ARGMAX) {
+        if (lane < NC) {
+            best_v[warp][lane] = bv;
+            best_i[warp][lane] = bi;
+        }
+        __syncthreads();
+        if (tid < NC && n0 + tid < g.rows) {
+            float v = best_v[0][tid];
+            uint32_t i = best_i[0][tid];
+            for (int w = 1; w < 8; ++w) argmax_merge(v, i, best_v[w][tid], best_i[w][tid]);
+            g.part_v[(size_t)(n0 + tid) * gridDim.x + blockIdx.x] = v;
+            g.part_i[(size_t)(n0 + tid) * gridDim.x + blockIdx.x] = i;
+        }
+    }
+}
+
+}  // namespace mgb

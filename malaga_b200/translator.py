@@ -106,7 +106,8 @@ class Engine:
         h = ctypes.c_void_p()
         check(_lib.load().mgb_encode(self.h, ids.ctypes.data, lens.ctypes.data, ids.shape[0], ids.shape[1],
                                      ctypes.byref(h)))
-        return Batch(self, h.value, [int(x) for x in lens], int(ids.shape[1]))
+        # the engine pads the batch to its longest sentence (pad_batch, model.rs:480-500)
+        return Batch(self, h.value, [int(x) for x in lens], int(lens.max()))
 
     def greedy(self, batch: Batch, tgt_lang: int, max_new: int, sync_every: int = 4, force: bool = False,
                out: np.ndarray | None = None) -> tuple[np.ndarray, np.ndarray]:

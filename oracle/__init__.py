@@ -55,6 +55,9 @@ def lib():
         L.orc_log.argtypes = [f]
         L.orc_log.restype = f
         L.orc_threads.restype = i
+        L.orc_matmul.argtypes = [i, vp, ctypes.c_long, ctypes.c_long, vp, i, i, i, vp]
+        L.orc_matmul.restype = i
+        L.orc_quantize_q81.argtypes = [vp, i, i, vp, vp, vp]
         _lib = L
     return _lib
 
@@ -136,6 +139,29 @@ class _Enc:
         if self.h:
             lib().orc_enc_free(self.h)
             self.h = None
+
+
+def matmul(ggml_type: int, w: np.ndarray, n_rows: int, k: int, x: np.ndarray, mode: str, nw: int = 4) -> np.ndarray:
+    """y = x . W^T for raw GGUF rows w ([n_rows, row_bytes] uint8): mode "mmvq"
+    (the reference's vector kernel with nw warps) or "mmq"."""
+    w = np.ascontiguousarray(w, np.uint8)
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.zeros((x.shape[0], n_rows), np.float32)
+    if lib().orc_matmul(ggml_type, w.ctypes.data, n_rows, k, x.ctypes.data, x.shape[0],
+                        0 if mode == "mmvq" else 1, nw, y.ctypes.data) != 0:
+        raise ValueError("unsupported matmul shape")
+    return y
+
+
+def quantize_q81(x: np.ndarray):
+    """q8_1 blocks of rows x: (q int8 [rows, K], d [rows, K/32], s [rows, K/32])."""
+    x = np.ascontiguousarray(x, np.float32)
+    rows, k = x.shape
+    q = np.zeros((rows, k), np.int8)
+    d = np.zeros((rows, k // 32), np.float32)
+    s = np.zeros((rows, k // 32), np.float32)
+    lib().orc_quantize_q81(x.ctypes.data, rows, k, q.ctypes.data, d.ctypes.data, s.ctypes.data)
+    return q, d, s
 
 
 def strip_eos(row, eos: int) -> list[int]:

@@ -17,25 +17,20 @@
  *     pad-after-finish bookkeeping), driven as graph.rs:262-297 does (step 0
  *     consumes </s> and is discarded, the target-language token is forced).
  *   - beam search: translator.rs:250-335 and topk 343-358.
- *   - quantized matmuls: candle-core 0.11.0's QMatMul (not in the reference
- *     tree) quantizes activations and takes integer block dot products against
- *     the GGUF blocks. Restated below: Q8_0 weights against 32-value
- *     activation blocks with f16 scales (per-block float scale, as candle's
- *     q8_0 vec_dot and MMVQ); Q4_K / Q6_K weights against Q8_K-style
- *     activations (one f32 scale per 256 values) with integer sums over each
- *     super-block and the float scales applied once per super-block, as
- *     candle's CPU k-quant vec_dot does (ggml's published algorithm).
+ *   - quantized matmuls: candle-core 0.11.0's CUDA QMatMul (not in the
+ *     reference tree; kernels in candle-kernels 0.11.0 src/quantized.cu):
+ *     q8_1 activations, MMVQ for at most 8 rows, MMQ above, restated
+ *     operation by operation in the section "Activation quantization and the
+ *     quantized matmul" below.
  *
- * Reduction orders are not specified by the reference (candle leaves them to
- * its kernels). This oracle FIXES one order for every float reduction, and the
- * CUDA kernels follow the same order, so the two agree bit for bit:
+ * Outside the matmuls the reference's kernels are built with --use_fast_math
+ * (rsqrtf, __expf, approximate division), whose hardware results cannot be
+ * restated on a CPU; there this oracle FIXES one IEEE order for every float
+ * reduction, and the CUDA kernels follow the same order, so the two agree bit
+ * for bit:
  *   SUM32(v[0..n))  lane l (0..31) sums v[l], v[l+32], ... left to right
  *                   (empty lane = 0), then pairs are added at distances
  *                   1,2,4,8,16 (acc[l] + acc[l^o]); the result is acc[0].
- *   ROW(p[0..n))    per-unit partials of a matmul row (32-blocks, or 256-value
- *                   super-blocks for k-quants), summed left to right (one
- *                   accumulator per output: the shape a tensor-core epilogue
- *                   can keep per (row, column)).
  *   exp             own implementation (Cody-Waite reduction with a 2-term
  *                   ln2 split, degree-7 Taylor polynomial in fmaf, exact 2^k
  *                   scaling); see mgb_exp.
@@ -154,12 +149,6 @@ static float sum32(const float *v, int n, int st) {
     return a[0];
 }
 
-/* ROW reduction of nb per-block partials: left to right in block order. */
-static float row_reduce(const float *p, int nb) {
-    float acc = p[0];
-    for (int j = 1; j < nb; ++j) acc = acc + p[j];
-    return acc;
-}
 
 /* ------------------------------------------------------------------------ */
 /* GGUF reading                                                              */
@@ -425,38 +414,83 @@ ORC_EXPORT int orc_config(orc_model *m, int *out) {
 }
 
 /* ------------------------------------------------------------------------ */
-/* Activation quantization and the matmul spec                                */
+/* Activation quantization and the quantized matmul                          */
+/*
+ * The reference's GPU decode runs every quantized projection through candle's
+ * QMatMul::forward (model.rs:79-81, 571-607), i.e. candle-core 0.11.0
+ * src/quantized/cuda.rs with the kernels of candle-kernels 0.11.0
+ * src/quantized.cu (vendored from llama.cpp's ggml-cuda). The reference
+ * documents the consequence: activations are quantized to q8_1, MMVQ runs up
+ * to 8 rows and MMQ above, and outputs depend on the batch size
+ * (docs/performance.md:51-54). This section restates that published
+ * arithmetic for the three weight types the presets use:
+ *
+ *   q8_1 (quantize_q8_1): per 32-value block, amax = max|x|, s = warp sum of x
+ *     (xor butterfly 16,8,4,2,1), d = amax/127, q = amax == 0 ? 0 : roundf(x/d);
+ *     d and s are stored as f16.
+ *   MMVQ (mul_mat_vec_q, b_size <= 8 rows): nw = 4 warps for 1-4 rows, 2 for
+ *     5-8 (candle's launch table). Thread t of nw*32 owns slices of blocks
+ *     kbx = t/(qi/vdr) + i*blocks_per_iter and sums its vec_dot results in
+ *     that order; warps 1.. add theirs to warp 0's in warp order; a butterfly
+ *     sum over the 32 lanes gives the output. vec_dot per type:
+ *       Q8_0 (8 values): (dw*dx) * float(I)
+ *       Q4_K (8 values of 2 sub-blocks): dall*sumf_d - dmin*sumf_m with
+ *             sumf_d = sum_i dx_i*float(I_i*sc_i), sumf_m = sum_i dx_i*float(Q_i*m_i)
+ *             (Q_i = sum of the 8 activation integers)
+ *       Q6_K (4 values of 2 blocks 64 apart): d * sum_i dx_i*float(I_i*sc_i)
+ *   MMQ (mul_mat_q, more rows): every output is one thread's running sum over
+ *     units in row order, starting at 0:
+ *       Q8_0 unit = one block: (dw*dx) * float(I)
+ *       Q4_K unit = 2 sub-blocks: dall*sumf_d - dmin*sumf_m, sumf_d = sum dx*float(sc*I),
+ *             sumf_m = sum sx*float(m) (sx = the f16 block sum of the f32 inputs)
+ *       Q6_K unit = 2 blocks: d * sum dx*float(sc_a*I_a + sc_b*I_b) (16-value halves)
+ * Integer sums are exact. Every float "a += b*c" / "a*b - c*d" of those
+ * kernels is written below as nvcc's default contraction computes it
+ * (fmaf(b, c, a); fmaf(a, b, -(c*d))); all other operations round on their own.
+ * F32 weights (candle: a cuBLAS matmul, not restated) use this project's order:
+ * lane l's FMA chain over elements l, l+32, ..., then the butterfly sum.
+ */
 
 typedef struct {
     int8_t *q;  /* [rows, K] */
-    float *d;   /* [rows, K/32]: the scale of the group holding each 32-block */
-} qact_t;
+    float *d;   /* [rows, K/32]: block scale (f16 value) */
+    float *s;   /* [rows, K/32]: block sum of the inputs (f16 value) */
+} q81_t;
 
-/* group = 1: blocks of 32 values with an f16-rounded scale (q8_1 / Q8_0 style,
- * consumed by Q8_0 weights). group = 8: one f32 scale per 256-value
- * super-block (Q8_K style, consumed by Q4_K and Q6_K weights, as candle's
- * k-quant vec_dot does). Both: d = amax/127 (the scale), q = round(v * (127/amax))
- * (one reciprocal per group, as ggml's Q8_K quantizer), q = 0 if amax = 0. */
-static void quantize_act(const float *x, int rows, int K, int group, qact_t *out) {
-    int nb = K / 32, gv = 32 * group;
-    for (int r = 0; r < rows; ++r) {
-        for (int u = 0; u < K / gv; ++u) {
-            const float *v = x + (size_t)r * K + (size_t)gv * u;
-            float amax = 0.0f;
-            for (int i = 0; i < gv; ++i) amax = fmaxf(amax, fabsf(v[i]));
-            float dd = amax / 127.0f, id = 127.0f / amax;
-            for (int i = 0; i < gv; ++i)
-                out->q[(size_t)r * K + (size_t)gv * u + i] = amax == 0.0f ? 0 : (int8_t)roundf(v[i] * id);
-            for (int j = 0; j < group; ++j) out->d[(size_t)r * nb + group * u + j] = group == 1 ? rnd_h(dd) : dd;
-        }
+/* The reference's warp_reduce_sum over 32 lane values: x += shfl_xor(x, m), m = 16..1. */
+static float bfly32(const float *v) {
+    float a[32], b[32];
+    memcpy(a, v, sizeof a);
+    for (int m = 16; m > 0; m >>= 1) {
+        for (int l = 0; l < 32; ++l) b[l] = a[l] + a[l ^ m];
+        memcpy(a, b, sizeof a);
     }
+    return a[0];
 }
 
-/* Unpacked weight row: integer values and per-block scale data. */
+/* quantize_q8_1 of `rows` rows of K values (candle-kernels src/quantized.cu). */
+static void quantize_q81(const float *x, int rows, int K, q81_t *o) {
+    const int nb = K / 32;
+    for (int r = 0; r < rows; ++r)
+        for (int j = 0; j < nb; ++j) {
+            const float *v = x + (size_t)r * K + 32 * j;
+            float amax = 0.0f;
+            for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+            const float sum = bfly32(v), d = amax / 127.0f;
+            int8_t *q = o->q + (size_t)r * K + 32 * j;
+            for (int i = 0; i < 32; ++i) q[i] = amax == 0.0f ? 0 : (int8_t)roundf(v[i] / d);
+            o->d[(size_t)r * nb + j] = rnd_h(d);
+            o->s[(size_t)r * nb + j] = rnd_h(sum);
+        }
+}
+
+/* Unpacked weight row: integer values and scale data. */
 typedef struct {
-    int8_t *q;         /* [K]: Q8_0 int8; Q4_K 0..15; Q6_K q-32 */
-    float *s0, *s1;    /* per 32-block: Q8_0 d; Q4_K d, dmin; Q6_K d */
-    int16_t *sc0, *sc1;/* per 32-block: Q4_K sc, m; Q6_K sc of the two 16-halves */
+    int8_t *q;    /* [K]: Q8_0 int8; Q4_K 0..15; Q6_K q-32 */
+    float *dw;    /* Q8_0: per block d; Q4_K: per super-block d; Q6_K: per super-block d */
+    float *dm;    /* Q4_K: per super-block dmin */
+    int *sc;      /* Q4_K: per block 6-bit scale; Q6_K: per 16 values int8 scale */
+    int *mn;      /* Q4_K: per block 6-bit min */
 } wrow_t;
 
 static void unpack_row(const tensor_t *t, long r, wrow_t *w) {
@@ -465,23 +499,25 @@ static void unpack_row(const tensor_t *t, long r, wrow_t *w) {
     if (t->type == GT_Q8_0) {
         for (long j = 0; j < K / 32; ++j) {
             uint16_t h; memcpy(&h, row + 34 * j, 2);
-            w->s0[j] = h2f(h);
+            w->dw[j] = h2f(h);
             for (int i = 0; i < 32; ++i) w->q[32 * j + i] = (int8_t)row[34 * j + 2 + i];
         }
     } else if (t->type == GT_Q4_K) {
         for (long sbk = 0; sbk < K / 256; ++sbk) {
             const uint8_t *b = row + 144 * sbk, *s = b + 4;
             uint16_t hd, hm; memcpy(&hd, b, 2); memcpy(&hm, b + 2, 2);
+            w->dw[sbk] = h2f(hd);
+            w->dm[sbk] = h2f(hm);
             for (int sb = 0; sb < 8; ++sb) {
                 int sc, mn;
                 if (sb < 4) { sc = s[sb] & 63; mn = s[sb + 4] & 63; }
                 else { sc = (s[sb + 4] & 0xf) | ((s[sb - 4] >> 6) << 4); mn = (s[sb + 4] >> 4) | ((s[sb] >> 6) << 4); }
                 long j = sbk * 8 + sb;
-                w->s0[j] = h2f(hd); w->s1[j] = h2f(hm); w->sc0[j] = (int16_t)sc; w->sc1[j] = (int16_t)mn;
+                w->sc[j] = sc;
+                w->mn[j] = mn;
                 for (int i = 0; i < 32; ++i) {
-                    int c = sb / 2, hi = sb & 1;
-                    uint8_t byte = b[16 + 32 * c + i];
-                    w->q[256 * sbk + 32 * sb + i] = (int8_t)(hi ? byte >> 4 : byte & 0xf);
+                    uint8_t byte = b[16 + 32 * (sb / 2) + i];
+                    w->q[256 * sbk + 32 * sb + i] = (int8_t)((sb & 1) ? byte >> 4 : byte & 0xf);
                 }
             }
         }
@@ -489,6 +525,7 @@ static void unpack_row(const tensor_t *t, long r, wrow_t *w) {
         for (long sbk = 0; sbk < K / 256; ++sbk) {
             const uint8_t *b = row + 210 * sbk;
             uint16_t hd; memcpy(&hd, b + 208, 2);
+            w->dw[sbk] = h2f(hd);
             for (int i = 0; i < 256; ++i) {
                 int n = i / 128, g = (i % 128) / 32, l = i % 32, q;
                 const uint8_t *ql = b + 64 * n, *qh = b + 128 + 32 * n;
@@ -500,104 +537,197 @@ static void unpack_row(const tensor_t *t, long r, wrow_t *w) {
                 }
                 w->q[256 * sbk + i] = (int8_t)(q - 32);
             }
-            for (int j8 = 0; j8 < 8; ++j8) {
-                long j = sbk * 8 + j8;
-                w->s0[j] = h2f(hd);
-                w->sc0[j] = (int8_t)b[192 + 2 * j8];
-                w->sc1[j] = (int8_t)b[192 + 2 * j8 + 1];
-            }
+            for (int g = 0; g < 16; ++g) w->sc[sbk * 16 + g] = (int8_t)b[192 + g];
         }
     }
 }
 
+/* MMVQ: thread t's sum of its vec_dot results (mul_mat_vec_q's tmp). */
+static float mmvq_thread(int type, const wrow_t *w, const int8_t *xq, const float *xd, int K, int nw, int t) {
+    float P = 0.0f;
+    if (type == GT_Q8_0) { /* qi 8, vdr 2: 4 threads per block, values 8o..8o+7 */
+        const int nb = K / 32, bpi = nw * 8, o = t % 4;
+        for (int kb = t / 4; kb < nb; kb += bpi) {
+            int s = 0;
+            for (int i = 8 * o; i < 8 * o + 8; ++i) s += w->q[32 * kb + i] * xq[32 * kb + i];
+            P = fmaf(w->dw[kb] * xd[kb], (float)s, P);
+        }
+    } else if (type == GT_Q4_K) { /* qi 32, vdr 2: 16 threads per super-block */
+        const int nsb = K / 256, bpi = nw * 2, c = (t % 16) / 4, o = t % 4;
+        for (int kb = t / 16; kb < nsb; kb += bpi) {
+            float sd = 0.0f, sm = 0.0f;
+            for (int i = 0; i < 2; ++i) { /* sub-blocks 2c (low nibbles) and 2c+1 (high) */
+                const int j = 8 * kb + 2 * c + i;
+                int dot1 = 0, dot2 = 0;
+                for (int h = 0; h < 2; ++h)
+                    for (int p = 16 * h + 4 * o; p < 16 * h + 4 * o + 4; ++p) {
+                        dot1 += w->q[32 * j + p] * xq[32 * j + p];
+                        dot2 += xq[32 * j + p];
+                    }
+                sd = fmaf(xd[j], (float)(dot1 * w->sc[j]), sd);
+                sm = fmaf(xd[j], (float)(dot2 * w->mn[j]), sm);
+            }
+            P = P + fmaf(w->dw[kb], sd, -(w->dm[kb] * sm));
+        }
+    } else { /* Q6_K: qi 32, vdr 1: 32 threads per super-block */
+        const int nsb = K / 256, bpi = nw, l = t % 32;
+        const int A = 4 * (l / 16) + (l % 16) / 8, p0 = 4 * (l % 8);
+        for (int kb = t / 32; kb < nsb; kb += bpi) {
+            float sf = 0.0f;
+            for (int i = 0; i < 2; ++i) { /* blocks A and A+2 of the super-block */
+                const int j = 8 * kb + A + 2 * i;
+                int dot = 0;
+                for (int p = p0; p < p0 + 4; ++p) dot += w->q[32 * j + p] * xq[32 * j + p];
+                sf = fmaf(xd[j], (float)(dot * w->sc[(32 * j + p0) / 16]), sf);
+            }
+            P = fmaf(w->dw[kb], sf, P);
+        }
+    }
+    return P;
+}
+
+/* One MMVQ output with nw warps. */
+static float mmvq_out(int type, const wrow_t *w, const int8_t *xq, const float *xd, int K, int nw) {
+    float leaf[32];
+    for (int l = 0; l < 32; ++l) {
+        float v = 0.0f;
+        for (int wv = 0; wv < nw; ++wv) {
+            const float P = mmvq_thread(type, w, xq, xd, K, nw, 32 * wv + l);
+            v = wv == 0 ? P : v + P;
+        }
+        leaf[l] = v;
+    }
+    return bfly32(leaf);
+}
+
+/* One MMQ output: the running sum over units in row order. */
+static float mmq_out(int type, const wrow_t *w, const int8_t *xq, const float *xd, const float *xs, int K) {
+    const int nb = K / 32;
+    float acc = 0.0f;
+    if (type == GT_Q8_0) {
+        for (int j = 0; j < nb; ++j) {
+            int s = 0;
+            for (int i = 0; i < 32; ++i) s += w->q[32 * j + i] * xq[32 * j + i];
+            acc = fmaf(w->dw[j] * xd[j], (float)s, acc);
+        }
+    } else if (type == GT_Q4_K) {
+        for (int j = 0; j < nb; j += 2) {
+            int I[2];
+            for (int i = 0; i < 2; ++i) {
+                int s = 0;
+                for (int p = 0; p < 32; ++p) s += w->q[32 * (j + i) + p] * xq[32 * (j + i) + p];
+                I[i] = s;
+            }
+            const float sd = fmaf(xd[j + 1], (float)(w->sc[j + 1] * I[1]), fmaf(xd[j], (float)(w->sc[j] * I[0]), 0.0f));
+            const float sm = fmaf(xs[j + 1], (float)w->mn[j + 1], fmaf(xs[j], (float)w->mn[j], 0.0f));
+            acc = acc + fmaf(w->dw[j / 8], sd, -(w->dm[j / 8] * sm));
+        }
+    } else {
+        for (int j = 0; j < nb; j += 2) {
+            int X[2];
+            for (int i = 0; i < 2; ++i) {
+                int a = 0, b = 0;
+                for (int p = 0; p < 16; ++p) {
+                    a += w->q[32 * (j + i) + p] * xq[32 * (j + i) + p];
+                    b += w->q[32 * (j + i) + 16 + p] * xq[32 * (j + i) + 16 + p];
+                }
+                X[i] = w->sc[2 * (j + i)] * a + w->sc[2 * (j + i) + 1] * b;
+            }
+            const float sf = fmaf(xd[j + 1], (float)X[1], fmaf(xd[j], (float)X[0], 0.0f));
+            acc = fmaf(w->dw[j / 8], sf, acc);
+        }
+    }
+    return acc;
+}
+
+/* F32 weights: lane l's FMA chain over elements l, l+32, ..., then the butterfly. */
+static float f32_out(const float *wr, const float *x, int K) {
+    float leaf[32];
+    for (int l = 0; l < 32; ++l) {
+        float acc = 0.0f;
+        for (int i = l; i < K; i += 32) acc = fmaf(wr[i], x[i], acc);
+        leaf[l] = acc;
+    }
+    return bfly32(leaf);
+}
+
 /*
- * y[n, r] = ROW(p_u) + bias[r] for every activation row n and weight row r,
- * over the row's units u: 32-blocks for F32 / Q8_0, 256-value super-blocks for
- * Q4_K / Q6_K. xq = activation values, xd = the unit's activation scale;
- * integer sums are exact (int32), float operations as written:
- *   F32  : p = fmaf chain of w*x over the block (activations not quantized)
- *   Q8_0 : p = (d*xd) * float(sum w*xq)
- *   Q4_K : S1 = sum_j sc_j * (sum_{i in j} q*xq), S2 = sum_j m_j * (sum_{i in j} xq)
- *          p = xd * (d*float(S1) - dmin*float(S2))
- *   Q6_K : S = sum over the 16 halves h of sc_h * (sum_{i in h} (q-32)*xq)
- *          p = (d*xd) * float(S)
- * This is the arithmetic of candle's CPU k-quant dot products against Q8_K
- * activations (ggml's vec_dot_q4_K_q8_K / vec_dot_q6_K_q8_K: integer sums per
- * super-block, float scales once per super-block).
+ * y[n, r] = dot(row r, x[n]) + bias[r] (then ReLU) for the `rows` activation
+ * rows. `cls` is the row count candle's QMatMul sees (the b_size of its kernel
+ * choice): the decode step's padded batch, beam rows, or batch x tokens.
  */
-static void linear(const linear_t *L, const float *x, int rows, float *y, int relu) {
+static void linear_k(const linear_t *L, const float *x, int rows, int vec, int nw, float *y, int relu);
+
+static void linear(const linear_t *L, const float *x, int rows, int cls, float *y, int relu) {
+    linear_k(L, x, rows, cls <= 8, cls <= 4 ? 4 : 2, y, relu);
+}
+
+/* The same with the kernel choice explicit: vec = MMVQ with nw warps, else MMQ. */
+static void linear_k(const linear_t *L, const float *x, int rows, int vec, int nw, float *y, int relu) {
     const tensor_t *t = L->w;
-    int K = (int)t->cols, N = (int)t->rows, nb = K / 32;
-    const int kq = t->type == GT_Q4_K || t->type == GT_Q6_K;
-    qact_t xa = {0};
+    const int K = (int)t->cols, N = (int)t->rows, nb = K / 32;
+    q81_t xa = {0};
     if (t->type != GT_F32) {
         xa.q = malloc((size_t)rows * K);
         xa.d = malloc((size_t)rows * nb * sizeof(float));
-        quantize_act(x, rows, K, kq ? 8 : 1, &xa);
+        xa.s = malloc((size_t)rows * nb * sizeof(float));
+        quantize_q81(x, rows, K, &xa);
     }
 #pragma omp parallel
     {
         wrow_t w;
         w.q = malloc((size_t)K);
-        w.s0 = malloc(nb * sizeof(float)); w.s1 = malloc(nb * sizeof(float));
-        w.sc0 = malloc(nb * sizeof(int16_t)); w.sc1 = malloc(nb * sizeof(int16_t));
-        float *p = malloc(nb * sizeof(float));
+        w.dw = malloc(nb * sizeof(float));
+        w.dm = malloc(nb * sizeof(float));
+        w.sc = malloc(2 * nb * sizeof(int));
+        w.mn = malloc(nb * sizeof(int));
 #pragma omp for schedule(dynamic, 16)
         for (int r = 0; r < N; ++r) {
             const float *wr32 = NULL;
             if (t->type == GT_F32) wr32 = (const float *)(t->data + (size_t)r * 4 * K);
             else unpack_row(t, r, &w);
             for (int n = 0; n < rows; ++n) {
-                if (kq) {
-                    for (int u = 0; u < nb / 8; ++u) {
-                        int S1 = 0, S2 = 0;
-                        for (int j = 8 * u; j < 8 * u + 8; ++j) {
-                            const int8_t *xq = xa.q + (size_t)n * K + 32 * j, *wq = w.q + 32 * j;
-                            if (t->type == GT_Q4_K) {
-                                int dot = 0, s8 = 0;
-                                for (int i = 0; i < 32; ++i) { dot += wq[i] * xq[i]; s8 += xq[i]; }
-                                S1 += w.sc0[j] * dot;
-                                S2 += w.sc1[j] * s8;
-                            } else {
-                                int da = 0, db = 0;
-                                for (int i = 0; i < 16; ++i) { da += wq[i] * xq[i]; db += wq[16 + i] * xq[16 + i]; }
-                                S1 += w.sc0[j] * da + w.sc1[j] * db;
-                            }
-                        }
-                        float xd = xa.d[(size_t)n * nb + 8 * u];
-                        if (t->type == GT_Q4_K) p[u] = xd * (w.s0[8 * u] * (float)S1 - w.s1[8 * u] * (float)S2);
-                        else p[u] = (w.s0[8 * u] * xd) * (float)S1;
-                    }
-                    float v = row_reduce(p, nb / 8);
-                    if (L->b) v = v + L->b[r];
-                    if (relu) v = v > 0.0f ? v : 0.0f;
-                    y[(size_t)n * N + r] = v;
-                    continue;
+                float v;
+                if (t->type == GT_F32) {
+                    v = f32_out(wr32, x + (size_t)n * K, K);
+                } else {
+                    const int8_t *xq = xa.q + (size_t)n * K;
+                    const float *xd = xa.d + (size_t)n * nb, *xs = xa.s + (size_t)n * nb;
+                    v = vec ? mmvq_out(t->type, &w, xq, xd, K, nw) : mmq_out(t->type, &w, xq, xd, xs, K);
                 }
-                for (int j = 0; j < nb; ++j) {
-                    if (t->type == GT_F32) {
-                        const float *xv = x + (size_t)n * K + 32 * j;
-                        float acc = 0.0f;
-                        for (int i = 0; i < 32; ++i) acc = fmaf(wr32[32 * j + i], xv[i], acc);
-                        p[j] = acc;
-                        continue;
-                    }
-                    const int8_t *xq = xa.q + (size_t)n * K + 32 * j, *wq = w.q + 32 * j;
-                    float xd = xa.d[(size_t)n * nb + j];
-                    int s = 0;
-                    for (int i = 0; i < 32; ++i) s += wq[i] * xq[i];
-                    p[j] = (w.s0[j] * xd) * (float)s;
-                }
-                float v = row_reduce(p, nb);
                 if (L->b) v = v + L->b[r];
                 if (relu) v = v > 0.0f ? v : 0.0f;
                 y[(size_t)n * N + r] = v;
             }
         }
-        free(w.q); free(w.s0); free(w.s1); free(w.sc0); free(w.sc1); free(p);
+        free(w.q); free(w.dw); free(w.dm); free(w.sc); free(w.mn);
     }
     free(xa.q);
     free(xa.d);
+    free(xa.s);
+}
+
+/* y[rows, N] = x[rows, K] . W^T for a raw GGUF matrix (type, N rows of K values):
+ * mode 0 = MMVQ with nw warps, 1 = MMQ. Test entry point (pins against other
+ * builds of the same published kernels). */
+ORC_EXPORT int orc_matmul(int type, const uint8_t *w, long N, long K, const float *x, int rows, int mode, int nw,
+                          float *y) {
+    if (K % 256 && type != GT_Q8_0 && type != GT_F32) return -1;
+    tensor_t t;
+    memset(&t, 0, sizeof t);
+    t.type = type;
+    t.rows = N;
+    t.cols = K;
+    t.data = w;
+    linear_t L = {&t, NULL};
+    linear_k(&L, x, rows, mode == 0, nw, y, 0);
+    return 0;
+}
+
+/* q8_1 quantization of rows x K values: q [rows, K], d and s [rows, K/32]. */
+ORC_EXPORT void orc_quantize_q81(const float *x, int rows, int K, int8_t *q, float *d, float *s) {
+    q81_t o = {q, d, s};
+    quantize_q81(x, rows, K, &o);
 }
 
 /* LayerNorm (eps 1e-5, config.rs:58): mean and variance by SUM32. */
@@ -662,7 +792,7 @@ ORC_EXPORT orc_enc *orc_encode(orc_model *m, const uint32_t *ids, const uint32_t
     for (int l = 0; l < c->enc_layers; ++l) {
         const layer_t *L = &m->enc[l];
         layer_norm(x, &L->attn_norm, rows, d, h);
-        linear(&L->qkv, h, rows, qkv, 0);
+        linear(&L->qkv, h, rows, rows, qkv, 0);
 #pragma omp parallel
         {
             float *e = malloc((size_t)s * sizeof(float));
@@ -676,11 +806,11 @@ ORC_EXPORT orc_enc *orc_encode(orc_model *m, const uint32_t *ids, const uint32_t
                     }
             free(e);
         }
-        linear(&L->out, a, rows, y, 0);
+        linear(&L->out, a, rows, rows, y, 0);
         for (size_t i = 0; i < (size_t)rows * d; ++i) x[i] = y[i] + x[i];
         layer_norm(x, &L->ffn_norm, rows, d, h);
-        linear(&L->up, h, rows, u, 1);
-        linear(&L->down, u, rows, y, 0);
+        linear(&L->up, h, rows, rows, u, 1);
+        linear(&L->down, u, rows, rows, y, 0);
         for (size_t i = 0; i < (size_t)rows * d; ++i) x[i] = y[i] + x[i];
     }
     layer_norm(x, &m->enc_norm, rows, d, h);
@@ -695,7 +825,7 @@ ORC_EXPORT orc_enc *orc_encode(orc_model *m, const uint32_t *ids, const uint32_t
     E->cv = malloc(per * c->dec_layers * sizeof(float));
     float *kv = malloc((size_t)rows * 2 * d * sizeof(float));
     for (int l = 0; l < c->dec_layers; ++l) {
-        linear(&m->dec[l].ckv, h, rows, kv, 0);
+        linear(&m->dec[l].ckv, h, rows, rows, kv, 0);
         for (int bi = 0; bi < b; ++bi)
             for (int hh = 0; hh < Hd; ++hh)
                 for (int j = 0; j < s; ++j)
@@ -747,15 +877,17 @@ ORC_EXPORT void orc_enc_cross(orc_model *m, orc_enc *E, int l, int which, float 
 /* Decoder state and the fused greedy step (model.rs:552-612)                */
 
 typedef struct {
-    int b, m; /* rows, self-KV capacity */
+    int b, m;  /* rows, self-KV capacity */
+    int cls;   /* rows of the reference's matmul calls (graph.rs:242: the batch padded to a power of two) */
     float *kc, *vc; /* per layer [b, H, m, hd] (f16-exact values) */
     float *x, *h, *qkv, *a, *y, *u, *logits;
 } dstate_t;
 
-static void dstate_init(orc_model *M, dstate_t *S, int b, int m) {
+static void dstate_init(orc_model *M, dstate_t *S, int b, int m, int cls) {
     const cfg_t *c = &M->c;
     int d = c->d;
     S->b = b;
+    S->cls = cls;
     S->m = m;
     size_t kv = (size_t)c->dec_layers * b * d * m;
     S->kc = calloc(kv, sizeof(float));
@@ -785,7 +917,7 @@ static void dec_step(orc_model *M, orc_enc *E, dstate_t *S, const uint32_t *ids,
         const layer_t *L = &M->dec[l];
         float *kc = S->kc + (size_t)l * b * d * S->m, *vc = S->vc + (size_t)l * b * d * S->m;
         layer_norm(S->x, &L->attn_norm, b, d, S->h);
-        linear(&L->qkv, S->h, b, S->qkv, 0);
+        linear(&L->qkv, S->h, b, S->cls, S->qkv, 0);
         for (int r = 0; r < b; ++r)
             for (int hh = 0; hh < H; ++hh)
                 for (int t = 0; t < hd; ++t) {
@@ -805,10 +937,10 @@ static void dec_step(orc_model *M, orc_enc *E, dstate_t *S, const uint32_t *ids,
                 }
             free(e);
         }
-        linear(&L->out, S->a, b, S->y, 0);
+        linear(&L->out, S->a, b, S->cls, S->y, 0);
         for (size_t i = 0; i < (size_t)b * d; ++i) S->x[i] = S->y[i] + S->x[i];
         layer_norm(S->x, &L->cross_norm, b, d, S->h);
-        linear(&L->cq, S->h, b, S->y, 0);
+        linear(&L->cq, S->h, b, S->cls, S->y, 0);
 #pragma omp parallel
         {
             float *e = malloc((size_t)E->s * sizeof(float));
@@ -822,16 +954,16 @@ static void dec_step(orc_model *M, orc_enc *E, dstate_t *S, const uint32_t *ids,
                 }
             free(e);
         }
-        linear(&L->co, S->a, b, S->y, 0);
+        linear(&L->co, S->a, b, S->cls, S->y, 0);
         for (size_t i = 0; i < (size_t)b * d; ++i) S->x[i] = S->y[i] + S->x[i];
         layer_norm(S->x, &L->ffn_norm, b, d, S->h);
-        linear(&L->up, S->h, b, S->u, 1);
-        linear(&L->down, S->u, b, S->y, 0);
+        linear(&L->up, S->h, b, S->cls, S->u, 1);
+        linear(&L->down, S->u, b, S->cls, S->y, 0);
         for (size_t i = 0; i < (size_t)b * d; ++i) S->x[i] = S->y[i] + S->x[i];
     }
     layer_norm(S->x, &M->dec_norm, b, d, S->h);
     linear_t head = {M->embed, NULL};
-    linear(&head, S->h, b, S->logits, 0);
+    linear(&head, S->h, b, S->cls, S->logits, 0);
 }
 
 static uint32_t argmax_row(const float *v, int n) {
@@ -854,7 +986,9 @@ ORC_EXPORT int orc_greedy(orc_model *M, orc_enc *E, uint32_t tgt, int max_new, i
     const cfg_t *c = &M->c;
     int b = E->b, m = max_new + 2;
     dstate_t S;
-    dstate_init(M, &S, b, m);
+    int cls = 1;
+    while (cls < b) cls <<= 1; /* graph.rs:242 */
+    dstate_init(M, &S, b, m, cls);
     uint32_t *ids = malloc(b * sizeof(uint32_t));
     uint8_t *fin = calloc(b, 1);
     for (int r = 0; r < b; ++r) ids[r] = (uint32_t)c->start;
@@ -954,7 +1088,7 @@ ORC_EXPORT int orc_beam(orc_model *M, orc_enc *E, uint32_t tgt, int k, float lp,
     int b = E->b, V = c->V, rows = b * k, m = max_new + 2;
     uint32_t eos = (uint32_t)c->eos;
     dstate_t S;
-    dstate_init(M, &S, rows, m);
+    dstate_init(M, &S, rows, m, rows);
     int *src_row = malloc(rows * sizeof(int));
     for (int r = 0; r < rows; ++r) src_row[r] = r / k;
     uint32_t *ids = malloc(rows * sizeof(uint32_t));

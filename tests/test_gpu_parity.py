@@ -101,15 +101,16 @@ def test_graph_replay_matches_eager_and_oracle(gpu, model, preset):
 
 
 def test_batching_does_not_change_outputs(gpu, model):
-    """pipeline.rs:45-57 (batch == single), bit-exact for the quantized preset too."""
-    path = model("mid", "q4_k_m")
-    V = models.config_of("mid").vocab_size
-    src = mid_sentences(V, n=7, seed=5)
+    """pipeline.rs:45-57 (batch == single) on the f32 preset, as the reference
+    tests it: quantized presets depend on the batch size in the reference
+    (docs/performance.md:51-54) and here alike."""
+    path = model("tiny", "f32")
+    src = tiny_sentences()
     t = Translator(Engine(path))
     opts = GenOptions(max_new_tokens=10, force_steps=True)
-    batched = t.generate(src, V - 2, opts)
+    batched = t.generate(src, TINY_TGT, opts)
     for s, row in zip(src, batched):
-        assert t.generate([s], V - 2, opts)[0] == row
+        assert t.generate([s], TINY_TGT, opts)[0] == row
 
 
 def test_idle_rows_sync_every_and_eos(gpu, model):
@@ -196,24 +197,6 @@ def test_tensor_core_batches_bit_exact(gpu, model, name, preset, b):
         f"max |diff| {np.abs(got_logits - want_logits).max()}"
 
 
-@pytest.mark.parametrize("preset", ["q4_k_m", "q8_0"])
-def test_tensor_core_equals_small_batch_kernels(gpu, model, preset, monkeypatch):
-    """The same small batch through the tcgen05 path (forced from 1 row) and the
-    small-batch kernels: identical logits, graph replay included."""
-    path = model("mid", preset)
-    V = models.config_of("mid").vocab_size
-    src = models.random_sources(5, 3, 14, V, 12, src_tag=V - 1)
-    eng = Engine(path)
-    ids_a, lg_a = eng.greedy_logits(eng.encode(src), V - 2, 4, force=True)
-    monkeypatch.setenv("MGB_TC_MIN_ROWS", "1")
-    eng_tc = Engine(path)
-    ids_b, lg_b = eng_tc.greedy_logits(eng_tc.encode(src), V - 2, 4, force=True)
-    np.testing.assert_array_equal(ids_a, ids_b)
-    assert np.array_equal(lg_a.view(np.uint32), lg_b.view(np.uint32))
-    out, _ = eng_tc.greedy(eng_tc.encode(src), V - 2, 4, force=True)
-    np.testing.assert_array_equal(out, ids_a)
-
-
 @pytest.mark.parametrize("name,preset,n,k", [("tiny", "q8_0", 6, 3), ("tiny", "f32", 4, 2), ("mid", "q4_k_m", 4, 4),
                                              ("mid", "q8_0", 3, 5)])
 def test_beam_search_matches_oracle(gpu, model, name, preset, n, k):
@@ -243,10 +226,12 @@ def test_beam_one_equals_greedy_on_device(gpu, model):
     assert [[int(x) for x in out[i, : lens[i]]] for i in range(len(src))] == greedy
 
 
-@pytest.mark.parametrize("preset,n", [("q4_k_m", 1), ("q8_0", 2)])
-def test_attention_in_matmul_prologue_bit_exact(gpu, model, preset, n):
-    """At 1-2 rows the out / cross-out matmuls compute the attention in their
-    prologue (no attention launch): logits still equal the oracle's bit for bit."""
+@pytest.mark.parametrize("preset", ["q4_k_m", "q8_0"])
+@pytest.mark.parametrize("n", [1, 2, 3, 5, 8])
+def test_small_batches_bit_exact(gpu, model, preset, n):
+    """1-8 rows run the small-batch kernel with the reference's MMVQ arithmetic:
+    the padded batch (1, 2, 4 or 8 rows) picks candle's warp count (4 warps up to
+    4 rows, 2 for 5-8); tokens and logits equal the oracle's bit for bit."""
     path = model("mid", preset)
     V = models.config_of("mid").vocab_size
     src = mid_sentences(V, n=n, seed=21)
@@ -254,4 +239,5 @@ def test_attention_in_matmul_prologue_bit_exact(gpu, model, preset, n):
     eng = Engine(path)
     got_ids, got_logits = eng.greedy_logits(eng.encode(src), V - 2, 6, force=True)
     np.testing.assert_array_equal(got_ids, want_ids)
-    assert np.array_equal(got_logits.view(np.uint32), want_logits.view(np.uint32))
+    assert np.array_equal(got_logits.view(np.uint32), want_logits.view(np.uint32)), \
+        f"max |diff| {np.abs(got_logits - want_logits).max()}"

@@ -10,8 +10,6 @@ token ids are the engine's fused argmax of the very logits it returns: two calls
 in a row (sharing the static scratch) must give the same ids and maxima. The
 file name makes pytest collect it last.
 """
-import ctypes
-
 import numpy as np
 import pytest
 
@@ -23,11 +21,7 @@ pytestmark = pytest.mark.gpu
 def _entry():
     from malaga_b200 import _lib
 
-    fn = _lib.load().mgb_argmax_noalloc
-    fn.restype = ctypes.c_int
-    fn.argtypes = [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p,
-                   ctypes.c_void_p]
-    return fn
+    return _lib.load().mgb_argmax_noalloc  # typed by _lib.SIGNATURES
 
 
 def test_argmax_noalloc_matches_greedy_ids_on_two_calls(gpu, model):
@@ -67,3 +61,35 @@ def test_argmax_noalloc_rejects_more_rows_than_its_scratch(gpu):
     rc = fn(x.data_ptr(), 65, 8, out.data_ptr(), None, None)
     assert rc == _lib.MGB_ERR_INVALID
     assert b"64 rows" in _lib.load().mgb_last_error()
+
+
+def test_argmax_noalloc_edge_rows(gpu):
+    """64 rows (the warps of the second pass loop over rows) of 100 logits (most
+    first-pass CTAs get an empty range), with a row of only -inf, a row whose
+    maximum repeats (the lowest index wins, as numpy's argmax), and a row of only
+    NaN (id 0): two calls in a row against numpy."""
+    import torch
+
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((64, 100)).astype(np.float32)
+    x[3, :] = -np.inf
+    x[7, :] = 1.0
+    x[7, [11, 40, 77]] = 2.5
+    x[9, :] = np.nan
+    want = x.argmax(axis=1)
+    want[9] = 0
+    fn = _entry()
+    stream = torch.cuda.current_stream()
+    for _ in range(2):
+        d_x = torch.from_numpy(x).cuda()
+        d_ids = torch.full((64,), -1, dtype=torch.int32, device="cuda")
+        d_vals = torch.zeros(64, dtype=torch.float32, device="cuda")
+        assert fn(d_x.data_ptr(), 64, 100, d_ids.data_ptr(), d_vals.data_ptr(), stream.cuda_stream) == 0
+        torch.cuda.synchronize()
+        got = d_ids.cpu().numpy()
+        np.testing.assert_array_equal(got, want)
+        vals = d_vals.cpu().numpy()
+        ok = np.ones(64, bool)
+        ok[9] = False
+        np.testing.assert_array_equal(vals[ok], x[ok].max(axis=1))
+        assert vals[9] == -np.inf and got[7] == 11 and got[3] == 0
