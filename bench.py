@@ -1,21 +1,36 @@
 """Benchmark of the NLLB decoder token loop (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2q4|c2|c1] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload dp600|c2q4|c2|c1] [--impl ours|reference]
 
-Metric: decoded tokens/s, NLLB-600M, batch 64, on 1/2/4/8 B200.
-One bench step = one pass of the hot path over one batch: the greedy decode of
-an encoded batch of 64 sentences, forced to 64 steps (EOS ignored), through
-mgb_greedy (CUDA-graph replay of the fused step). Inputs are synthetic: a
-random-init NLLB-600M converted to GGUF, and seeded token ids (config 2's
-batch: lengths uniform in [8, 64]). Each rank decodes its own batch ("weak"
-scaling, no collective on the data path); `value` = tokens of all ranks / the
-slowest rank's device time.
+Metric: decoded tokens/s, NLLB-600M q4_k_m, batch 64, on
+1/2/4/8 B200; p50 ms/sentence at batch 1.
+
+Headline (default workload dp600): a fixed set of 1024 synthetic sentences
+(config 2's lengths, uniform in [8, 64]) cut into 16 length-sorted batches of
+64 (translator.rs:140-147) and placed on the ranks longest-processing-time
+first (malaga_b200/dp.py): one process per GPU, no collective on the data
+path, strong scaling (the total work is fixed as N grows). One bench step = one
+pass of the hot path over every batch of the rank's share: the greedy decode
+of each encoded batch, forced to 64 tokens per row (EOS ignored), through
+mgb_greedy (CUDA-graph replay of the fused step). `value` = tokens of all
+ranks / the slowest rank's device time (CUDA events on the engine's stream,
+max over ranks).
 
 `e2e`: the same metric through the public API from host buffers (token ids in
-host memory -> mgb_encode -> mgb_greedy -> token ids back in host memory) per
-step. `--impl reference`: the CPU restatement of the reference's algorithm
-(oracle/, compiled C with OpenMP on every host core) on a bounded sample of the
-same workload; the reference's own Rust/candle build cannot be compiled here.
+host memory -> mgb_encode -> mgb_greedy -> token ids back in host memory), per
+step, for every batch of the share. `b1` (rank 0, N = 1): config 1 (batch 1,
+34-token source, 32 forced steps) timed as the reference's `malaga bench`
+(crates/malaga/src/main.rs:409-436: 3 warm-ups, p50 over 20 runs of a whole
+sentence: encode + decode from host ids).
+
+`roofline`: the dominant kernel (the fused LM head + argmax), its algorithmic
+bytes over its launch time measured live (CUDA events, mgb_profile_step);
+`step_roofline`: weight + KV bytes actually read per decode over the decode's
+device time (north_star's definition).
+
+`--impl reference`: the CPU restatement of the reference's algorithm (oracle/,
+compiled C with OpenMP on every host core) on a bounded sample of the same
+workload; the reference's own Rust/candle build cannot be compiled here.
 """
 from __future__ import annotations
 
@@ -33,7 +48,7 @@ sys.path.insert(0, ROOT)
 
 import numpy as np  # noqa: E402
 
-from malaga_b200 import models  # noqa: E402
+from malaga_b200 import dp, models  # noqa: E402
 
 METRIC = "decoded tokens/s NLLB-600M q4_k_m b64 @1/2/4/8 B200; p50 ms/sentence b1"
 
@@ -94,49 +109,67 @@ class ClockSampler:
 
 
 DESCRIBE = {
+    "dp600": "1024 sentences (source lengths U[8,64]) in 16 length-sorted batches of 64, "
+             "64 forced greedy steps per batch, batches placed on the ranks by LPT",
     "c1": "batch 1, source 32 random ids + language tag + </s>, 32 forced greedy steps",
     "c2": "batch 64 (q8_0 weights), source lengths U[8,64], 64 forced greedy steps",
     "c2q4": "batch 64, source lengths U[8,64], 64 forced greedy steps",
 }
 
-# The LM-head kernel each workload runs (the roofline's dominant kernel).
-LM_KERNEL = {
-    "c1": "gemv_fused_kernel<Q6_K, ARGMAX, LN, 1> (small-batch LM head + argmax)",
-    "c2": "gemm_tc_kernel<Q8_0, ARGMAX, 64> (tcgen05 LM head + argmax)",
-    "c2q4": "gemm_tc_kernel<Q6_K, ARGMAX, 64> (tcgen05 LM head + argmax)",
-}
+# The LM-head kernel each batch size runs (the roofline's dominant kernel).
+def lm_kernel(rows: int, preset: str) -> str:
+    t = "Q6_K" if preset == "q4_k_m" else "Q8_0"
+    if rows <= 8:
+        return f"small_mm_kernel<{t}, ARGMAX, LN> (MMVQ LM head + argmax, {rows} row(s))"
+    return f"gemm_tc_kernel<{t}, ARGMAX, 64> (tcgen05 MMQ LM head + argmax)"
 
 
-def measured_traffic(workload: str):
-    """DRAM bytes per launch of the workload's LM-head kernel from the ncu capture
-    summarized in profiles/traffic.txt (lines: workload bytes_per_launch)."""
+def measured_traffic(key: str):
+    """DRAM bytes per launch of a workload's LM-head kernel from the ncu capture
+    summarized in profiles/traffic.txt (lines: key bytes_per_launch)."""
     try:
         with open(os.path.join(ROOT, "profiles", "traffic.txt")) as f:
             for line in f:
                 parts = line.split()
-                if len(parts) >= 2 and parts[0] == workload and not line.startswith("#"):
+                if len(parts) >= 2 and parts[0] == key and not line.startswith("#"):
                     return int(parts[1])
     except OSError:
         pass
     return None
 
 
-def cpu_baseline(w, max_seconds: float = 20.0):
-    """The oracle (CPU restatement, OpenMP on every host core) on a bounded sample:
-    the workload's full batch decoding 2 steps from synthetic cross K/V."""
+def kv_bytes(info: dict, src_lens: list[int], steps: int) -> int:
+    """K/V bytes the attention reads in one decode of a batch (f16 caches): at
+    step t (0..steps, the start step included) every layer reads t+1 self-attention
+    keys and values and the row's source-length cross keys and values."""
+    per_key = info["decoder_layers"] * 2 * info["d_model"] * 2
+    self_keys = (steps + 1) * (steps + 2) // 2
+    return per_key * sum(self_keys + (steps + 1) * s for s in src_lens)
+
+
+def cpu_sample(w) -> tuple[int, int]:
+    """Rows and forced steps of the CPU baseline's bounded sample (seconds of work)."""
+    rows = min(w.batch, len(w.sources))
+    return rows, (2 if rows > 8 else 8)
+
+
+def cpu_baseline(w):
+    """The oracle (CPU restatement, OpenMP on every host core) on a bounded
+    sample of the workload: one batch of it decoding a few forced steps (plus
+    the start step) from synthetic cross K/V."""
     import oracle
 
     path = models.model_path(w.model, w.preset, w.seed)
     orc = oracle.Oracle(path)
-    sample_steps = 4
+    rows, sample_steps = cpu_sample(w)
+    src = sorted(w.sources, key=len, reverse=True)[:rows]
     t0 = time.perf_counter()
-    orc.decode_timing_sample(w.sources, models.TGT_TAG, sample_steps)
+    orc.decode_timing_sample(src, models.TGT_TAG, sample_steps)
     dt = time.perf_counter() - t0
-    # the discarded decoder-start step is timed too, as on the GPU path; count generated tokens
-    toks = len(w.sources) * sample_steps
+    toks = len(src) * sample_steps
     return {"value": toks / dt, "unit": "tokens/s", "cores": oracle.lib().orc_threads(), "kind": "port",
-            "sample": f"{len(w.sources)} rows x {sample_steps} decode steps (+1 start step) of {w.name} "
-                      f"from synthetic cross K/V, {dt:.1f} s"}
+            "sample": f"{len(src)} rows x {sample_steps} forced decode steps (+1 start step) of {w.name} "
+                      f"from synthetic cross K/V, {dt:.1f} s", "seconds": dt}
 
 
 def run_reference(args, w):
@@ -148,14 +181,68 @@ def run_reference(args, w):
     v = statistics.median(vals)
     cb = dict(results[-1])
     cb["value"] = v
+    rows, sample_steps = cpu_sample(w)
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * len(w.sources) * 4 / v,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 dot / f32",
-            "data": "synthetic", "config": {"workload": w.name, "model": f"nllb-600m-{w.preset} (random init)",
-                                            "batch": len(w.sources), "decode_steps_sampled": 4},
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * rows * sample_steps / v,
+            "higher_is_better": True, "scaling": "strong" if w.name == "dp600" else "weak", "vs_baseline": None,
+            "dtype": "int8 dot / f32", "data": "synthetic",
+            "config": {"workload": w.name, "model": f"nllb-600m-{w.preset} (random init)", "sample_rows": rows,
+                       "decode_steps_sampled": sample_steps},
             "cpu_baseline": cb, "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                                         "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def bench_b1(eng, torch, stream, info, hbm):
+    """Config 1 as the reference's bench: p50 over 20 whole sentences (host ids ->
+    encode -> 32 forced steps -> host ids) after 3 warm-ups; also the device time."""
+    w = models.workload("c1")
+    src = w.sources
+    ids = np.array(src, np.uint32)
+    lens = np.array([len(s) for s in src], np.uint32)
+    out = np.empty((1, w.steps), np.uint32)
+    wall, dev = [], []
+    for it in range(3 + 20):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        e0.record(stream)
+        b = eng.encode_array(ids, lens)
+        eng.greedy(b, models.TGT_TAG, w.steps, sync_every=4, force=True, out=out)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        t1 = time.perf_counter()
+        b.free()
+        if it >= 3:
+            wall.append((t1 - t0) * 1e3)
+            dev.append(e0.elapsed_time(e1))
+    # the decode alone (graph replay), for the per-step roofline
+    b = eng.encode_array(ids, lens)
+    eng.greedy(b, models.TGT_TAG, w.steps, sync_every=4, force=True, out=out)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(5):
+        eng.greedy(b, models.TGT_TAG, w.steps, sync_every=4, force=True, out=out)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    dec_ms = e0.elapsed_time(e1) / 5
+    lm_ms, _ = eng.profile_step(b, models.TGT_TAG, 8)
+    b.free()
+    steps = w.steps + 1  # the start step runs the whole decoder too
+    by = steps * info["decoder_step_bytes"] + kv_bytes(info, [len(s) for s in src], w.steps)
+    lm_bytes = info["lm_head_bytes"]
+    return {
+        "workload": f"c1: NLLB-600M q4_k_m (random init, seed 0), {DESCRIBE['c1']}",
+        "p50_ms_per_sentence": statistics.median(wall), "p90_ms_per_sentence": float(np.percentile(wall, 90)),
+        "p50_device_ms_per_sentence": statistics.median(dev), "iterations": len(wall), "warmup": 3,
+        "decode_ms": dec_ms, "ms_per_decoder_step": dec_ms / steps, "tokens_per_s": w.steps / (dec_ms / 1e3),
+        "step_roofline": {"bytes_per_decode": by, "achieved_gbs": by / (dec_ms / 1e3) / 1e9, "peak": hbm,
+                          "frac": by / (dec_ms / 1e3) / 1e9 / hbm},
+        "lm_head": {"kernel": lm_kernel(1, "q4_k_m"), "launch_ms": lm_ms, "algorithmic_bytes": lm_bytes,
+                    "achieved_gbs": lm_bytes / (lm_ms / 1e3) / 1e9,
+                    "frac": lm_bytes / (lm_ms / 1e3) / 1e9 / hbm, "traffic": measured_traffic("b1")},
+    }
 
 
 def main():
@@ -163,9 +250,10 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="c2q4", choices=["c2q4", "c2", "c1"])
+    ap.add_argument("--workload", default="dp600", choices=["dp600", "c2q4", "c2", "c1"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-b1", action="store_true")
     args = ap.parse_args()
     w = models.workload(args.workload)
     if args.impl == "reference":
@@ -189,16 +277,27 @@ def main():
     from malaga_b200 import Engine
 
     eng = Engine(path, device=local)
+    info = eng.info
     stream = torch.cuda.ExternalStream(eng.stream, device=torch.device("cuda", local))
-    tgt = models.TGT_TAG
-    src = w.sources
-    batch = eng.encode(src)
-    rows, steps = len(src), w.steps
-    tokens_per_step = rows * steps
-    out = np.empty((rows, steps), np.uint32)
+    tgt, steps = models.TGT_TAG, w.steps
+    # this rank's share: length-sorted batches of w.batch placed by LPT (a
+    # single-batch workload is replicated on every rank instead)
+    lens_all = [len(s) for s in w.sources]
+    if w.name == "dp600":
+        share = dp.shard(lens_all, world, rank, w.batch, lambda b: steps)
+        scaling = "strong"
+    else:
+        share = [list(range(len(w.sources)))]
+        scaling = "weak"
+    srcs = [[w.sources[i] for i in b] for b in share]
+    batches = [eng.encode(s) for s in srcs]
+    outs = [np.empty((len(s), steps), np.uint32) for s in srcs]
+    my_tokens = sum(len(s) for s in srcs) * steps
+    total_tokens = (len(w.sources) if scaling == "strong" else world * len(w.sources)) * steps
 
     def decode_step():
-        eng.greedy(batch, tgt, steps, sync_every=4, force=True, out=out)
+        for b, o in zip(batches, outs):
+            eng.greedy(b, tgt, steps, sync_every=4, force=True, out=o)
 
     for _ in range(max(3, args.warmup)):
         decode_step()
@@ -225,57 +324,78 @@ def main():
         ms = timed(decode_step, args.steps)
     launches = eng.kernel_launches - l0
     ms_step = ms / args.steps
-    value = world * tokens_per_step / (ms_step / 1e3)
+    value = total_tokens / (ms_step / 1e3)
 
-    # e2e: host ids -> encode -> greedy -> host ids, every step
-    ids_host = np.full((rows, max(len(s) for s in src)), 1, np.uint32)
-    for i, s in enumerate(src):
-        ids_host[i, : len(s)] = s
-    lens_host = np.array([len(s) for s in src], np.uint32)
+    # e2e: host ids -> encode -> greedy -> host ids, every batch of the share, every step
+    hosts = []
+    for s in srcs:
+        ids_host = np.full((len(s), max(len(r) for r in s)), 1, np.uint32)
+        for i, r in enumerate(s):
+            ids_host[i, : len(r)] = r
+        hosts.append((ids_host, np.array([len(r) for r in s], np.uint32)))
 
     def e2e_step():
-        b = eng.encode_array(ids_host, lens_host)
-        eng.greedy(b, tgt, steps, sync_every=4, force=True, out=out)
-        b.free()
+        for (ih, lh), o in zip(hosts, outs):
+            b = eng.encode_array(ih, lh)
+            eng.greedy(b, tgt, steps, sync_every=4, force=True, out=o)
+            b.free()
 
     e2e_step()
-    ms_e2e = timed(e2e_step, max(1, min(args.steps, 3)))
-    e2e_value = world * tokens_per_step / (ms_e2e / max(1, min(args.steps, 3)) / 1e3)
+    k_e2e = max(1, min(args.steps, 3))
+    ms_e2e = timed(e2e_step, k_e2e)
+    e2e_value = total_tokens / (ms_e2e / k_e2e / 1e3)
 
     # roofline of the dominant kernel (fused LM head + argmax), timed live with events
-    lm_ms, step_ms = eng.profile_step(batch, tgt, 8)
-    lm_bytes = eng.info["lm_head_bytes"]
     hbm, peak_kind = peaks()
+    lm_ms, eager_step_ms = eng.profile_step(batches[0], tgt, 8)
+    lm_bytes = info["lm_head_bytes"]
     achieved = lm_bytes / (lm_ms / 1e3) / 1e9
-    step_bytes = eng.info["decoder_step_bytes"]
+    step_bytes = info["decoder_step_bytes"]
+    # weight + KV bytes of this rank's decodes per bench step
+    rank_bytes = sum((steps + 1) * step_bytes + kv_bytes(info, [len(r) for r in s], steps) for s in srcs)
+    rank_dev_ms = ms_step  # (max over ranks: the slowest rank's time)
+
+    b1 = None
+    if rank == 0 and world == 1 and not args.no_b1:
+        if w.model == "600m" and w.preset == "q4_k_m":
+            b1 = bench_b1(eng, torch, stream, info, hbm)
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "int8 dot / f32 (q8 activations x GGUF blocks)", "data": "synthetic",
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": scaling,
+            "vs_baseline": None, "dtype": "int8 dot / f32 (q8_1 activations x GGUF blocks)", "data": "synthetic",
             "config": {"workload": f"{w.name}: NLLB-600M {w.preset} (random init, seed {w.seed}), {DESCRIBE[w.name]}",
-                       "global_batch": rows * world, "decode_steps": steps, "parallelism": f"dp{world}",
-                       "l2": "weights (%.0f MB/step) exceed the 126 MB L2" % (step_bytes / 1e6)},
+                       "global_batch": w.batch, "sentences": len(w.sources) * (1 if scaling == "strong" else world),
+                       "decode_steps": steps, "parallelism": f"dp{world}",
+                       "step": "ms_per_step = one pass over the rank's batches (each a whole forced decode)",
+                       "batches_this_rank": len(srcs),
+                       "l2": "weights (%.0f MB per decoder step) exceed the 126 MB L2" % (step_bytes / 1e6)},
             "gpu_launches": launches,
-            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": int(ids_host.nbytes + lens_host.nbytes),
-                    "d2h_bytes_per_step": int(out.nbytes)},
-            "roofline": {"bound": "hbm", "kernel": LM_KERNEL[w.name],
+            "e2e": {"value": e2e_value, "unit": "tokens/s",
+                    "h2d_bytes_per_step": int(sum(ih.nbytes + lh.nbytes for ih, lh in hosts)),
+                    "d2h_bytes_per_step": int(sum(o.nbytes for o in outs))},
+            "roofline": {"bound": "hbm", "kernel": lm_kernel(len(srcs[0]), w.preset),
                          "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                         "peak_source": peak_kind, "traffic": measured_traffic(w.name),
+                         "peak_source": peak_kind, "traffic": measured_traffic(f"b{len(srcs[0])}"),
                          "algorithmic_bytes": lm_bytes, "launch_ms": lm_ms},
-            "step_roofline": {"weight_bytes_per_step": step_bytes, "eager_step_ms": step_ms,
-                              "graph_step_ms": ms_step / steps,
-                              "frac_of_hbm": step_bytes / (ms_step / steps / 1e3) / 1e9 / hbm},
+            "step_roofline": {"bytes_per_step_rank0": rank_bytes, "weight_bytes_per_decoder_step": step_bytes,
+                              "achieved_gbs": rank_bytes / (rank_dev_ms / 1e3) / 1e9,
+                              "frac": rank_bytes / (rank_dev_ms / 1e3) / 1e9 / hbm,
+                              "ms_per_decoder_step": ms_step / len(srcs) / (steps + 1),
+                              "eager_step_ms": eager_step_ms},
             "clocks": clk.summary(),
         }
+        if b1:
+            line["b1"] = b1
         if not args.no_cpu_baseline and world == 1:
             try:
                 line["cpu_baseline"] = cpu_baseline(w)
             except Exception as e:  # reported, never fatal
                 line["cpu_baseline"] = {"error": str(e)}
         print(json.dumps(line), flush=True)
-    batch.free()
+    for b in batches:
+        b.free()
     eng.close()
     if world > 1:
         dist.destroy_process_group()

@@ -52,7 +52,10 @@ typedef struct {
      * (graph.rs:273-294). 0 runs the same kernels eagerly (MALAGA_NO_CUDA_GRAPH). */
     int use_graphs;
     /* Byte budget of cached static states + graphs, LRU-evicted (graph.rs:183, 302-323;
-     * MALAGA_GRAPH_CACHE_MB, default 512 MiB). */
+     * MALAGA_GRAPH_CACHE_MB). Default 8 GiB: the reference's 512 MiB default is
+     * sized for a 24 GB card, while one batch-64 state here (K/V caches of 128
+     * positions, 128-key cross K/V, split-K buffers) takes about 0.85 GB and a
+     * length-sorted batch set touches up to four source buckets. */
     uint64_t graph_cache_bytes;
     /* Test hook: when >= 0, the n-th device allocation made after mgb_open returns
      * MGB_ERR_OOM, without touching the GPU's memory. -1 = off. */
@@ -68,7 +71,7 @@ typedef struct {
     uint64_t lm_head_bytes;       /* bytes of the tied LM head (token embedding) */
 } mgb_model_info;
 
-/* Fills `o` with the defaults (graphs on, 512 MiB cache, no fault injection). */
+/* Fills `o` with the defaults (graphs on, 8 GiB cache, no fault injection). */
 MGB_API void mgb_default_options(mgb_options *o);
 
 /* Loads a GGUF written by malaga's converter onto GPU `device`.

@@ -688,18 +688,26 @@ static mgb_status attend(mgb_ctx *c, AttnArgs a) {
 // Small-batch matmul (smallmm.cuh). NC = the launch's rows rounded up to a
 // power of two; the MMVQ warp count follows from it as in candle's launch
 // table (4 warps for 1-4 rows, 2 for 5-8). At least 8 weight rows per CTA, at
-// most two CTAs per SM, stages of about 24 KB.
-template <int TYPE, int EPI, int MODE, int NC>
+// most two CTAs per SM; stages of 32 rows (R = 4 rows per warp) while that
+// stays within 32 KB, else 8 rows.
+template <int TYPE, int EPI, int MODE, int NC, int R>
 static cudaError_t small_launch(mgb_ctx *c, const SmallArgs &a, int grid, size_t smem) {
-    auto kern = small_mm_kernel<TYPE, EPI, MODE, NC, NC <= 4 ? 4 : 2>;
+    auto kern = small_mm_kernel<TYPE, EPI, MODE, NC, NC <= 4 ? 4 : 2, R>;
     cudaError_t e = allow_smem(kern, smem);
     return e == cudaSuccess ? launch_pdl(kern, dim3(grid), dim3(256), smem, c->stream, a) : e;
+}
+
+template <int TYPE, int EPI, int MODE, int NC>
+static cudaError_t small_launch_r(mgb_ctx *c, const SmallArgs &a, int grid, size_t smem, int R) {
+    return R == 4 ? small_launch<TYPE, EPI, MODE, NC, 4>(c, a, grid, smem)
+                  : small_launch<TYPE, EPI, MODE, NC, 1>(c, a, grid, smem);
 }
 
 template <int TYPE, int EPI, int MODE>
 static mgb_status small_t(mgb_ctx *c, const GemvArgs &g, const PrepArgs &p, int *ctas) {
     const Matrix &W = g.W;
     const int RB = row_bytes_of(TYPE, W.K), groups = W.Np / 8;
+    const int R = TYPE != T_F32 && 32 * RB <= 32 * 1024 ? 4 : 1;
     int grid = std::min(groups, 2 * c->sms);
     const int rpc = (groups + grid - 1) / grid * 8;
     grid = (W.Np + rpc - 1) / rpc;
@@ -713,21 +721,21 @@ static mgb_status small_t(mgb_ctx *c, const GemvArgs &g, const PrepArgs &p, int 
         a.p = p;
         a.n0 = n0;
         a.rows_per_cta = rpc;
-        a.chunk = std::max(1, std::min(rpc / 8, 24 * 1024 / (8 * RB))) * 8;
-        a.stages = TYPE == T_F32 ? 0 : std::min(3, (rpc + a.chunk - 1) / a.chunk);
+        const int nch = (rpc + 8 * R - 1) / (8 * R);
+        a.stages = TYPE == T_F32 ? 0 : std::min(3, nch);
         a.err = c->d_err;
-        const size_t act = small_act_bytes(NC, W.K, TYPE, MODE);
-        while (a.stages > 1 && (size_t)a.stages * a.chunk * RB + act > c->smem_optin) --a.stages;
-        const size_t smem = (size_t)a.stages * a.chunk * RB + act;
+        const size_t act = small_act_bytes(NC, W.K, TYPE, MODE), sb = (size_t)8 * R * RB;
+        while (a.stages > 1 && (size_t)a.stages * sb + act > c->smem_optin) --a.stages;
+        const size_t smem = (size_t)a.stages * sb + act;
         if (smem > c->smem_optin)
             return set_err(MGB_ERR_UNSUPPORTED, "small-batch matmul of a %d-value row needs %zu B of shared memory",
                            W.K, smem);
         cudaError_t e;
         switch (NC) {
-            case 1: e = small_launch<TYPE, EPI, MODE, 1>(c, a, grid, smem); break;
-            case 2: e = small_launch<TYPE, EPI, MODE, 2>(c, a, grid, smem); break;
-            case 4: e = small_launch<TYPE, EPI, MODE, 4>(c, a, grid, smem); break;
-            default: e = small_launch<TYPE, EPI, MODE, 8>(c, a, grid, smem); break;
+            case 1: e = small_launch_r<TYPE, EPI, MODE, 1>(c, a, grid, smem, R); break;
+            case 2: e = small_launch_r<TYPE, EPI, MODE, 2>(c, a, grid, smem, R); break;
+            case 4: e = small_launch_r<TYPE, EPI, MODE, 4>(c, a, grid, smem, R); break;
+            default: e = small_launch_r<TYPE, EPI, MODE, 8>(c, a, grid, smem, R); break;
         }
         ++c->launches;
         if (e != cudaSuccess) return cuda_err(e, "small-batch matmul launch");
@@ -1750,7 +1758,7 @@ extern "C" {
 
 void mgb_default_options(mgb_options *o) {
     o->use_graphs = 1;
-    o->graph_cache_bytes = (uint64_t)512 << 20;
+    o->graph_cache_bytes = (uint64_t)8 << 30;
     o->fail_alloc_after = -1;
 }
 

@@ -61,7 +61,6 @@ struct SmallArgs {
     PrepArgs p;        // activation source
     int n0;            // first activation row of this launch (launches cover at most 8 rows)
     int rows_per_cta;  // weight rows per CTA (a multiple of 8)
-    int chunk;         // weight rows per stage (a multiple of 8)
     int stages;        // ring depth (1..4); 0 for F32 weights (read from global memory)
     uint32_t *err;
 };
@@ -76,48 +75,82 @@ __host__ __device__ inline size_t small_act_bytes(int NC, int K, int type, int m
 __device__ __forceinline__ int lds32(const void *p) { return *reinterpret_cast<const int *>(p); }
 
 // ---------------------------------------------------------------------------
-// MMVQ per type. Row data in shared memory; out[n] = the output of column n.
+// MMVQ per type. A warp computes R weight rows at once (local rows lr0,
+// lr0 + 8, ... of the stage; region k of local row r at st + CR*off_k + r*rb[k]),
+// the activation operands of each unit loaded once for all R rows.
+// out[r][n] = the output of row r, column n, in every lane.
+
+// Exact int -> float for |x| < 2^22: two full-rate instructions instead of one
+// conversion on the quarter-rate pipe (1.5 * 2^23 + x has x in its mantissa).
+__device__ __forceinline__ float i2f_exact(int x) { return __fsub_rn(__int_as_float(x + 0x4B400000), 12582912.0f); }
+
+struct StageRows {
+    const uint8_t *base[4];  // region k of local row 0
+    int rb[4];               // bytes per row of region k
+    __device__ __forceinline__ const uint8_t *row(int k, int lr) const { return base[k] + (size_t)lr * rb[k]; }
+};
 
 // Q6_K (candle vec_dot_q6_K_q8_1, qi 32, vdr 1): thread t handles super-blocks
 // t/32 + i*NW; lane l reads ql int l, 4 values of blocks A and A+2 of the
 // super-block (A = 4(l/16) + (l%16)/8) at positions 4(l%8)..+3:
-//   sf = dx_{A+2}*float(I_1*sc_1) + dx_A*float(I_0*sc_0) (two FMAs from 0), P = fma(d, sf, P).
-template <int NC, int NW>
-__device__ __forceinline__ void mmvq_q6k(const uint8_t *ql, const uint8_t *qh, const int8_t *sc, const __half *dd,
-                                         int nsb, const SmAct &s, int K, int lane, float (&out)[NC]) {
+//   sf = fma(dx_{A+2}, float(I_1*sc_1), fma(dx_A, float(I_0*sc_0), 0)), P = fma(d, sf, P)
+// with I = sum (q - 32) * u, formed as dp4a(q, u, dp4a(-32 x 4, u, 0)).
+template <int NC, int NW, int R>
+__device__ __forceinline__ void mmvq_q6k(const StageRows &S, int lr0, int nsb, const SmAct &s, int K, int lane,
+                                         float (&out)[R][NC]) {
     const int nb = K >> 5;
     const int A = 4 * (lane >> 4) + ((lane & 15) >> 3), p0 = 4 * (lane & 7);
     const int hoff = 4 * (8 * (lane >> 4) + (lane & 7)), hsh = 2 * ((lane & 15) >> 3);
     const int so = 8 * (lane >> 4) + ((lane & 15) >> 2);
-    float leaf[NC];
+    float leaf[R][NC];
 #pragma unroll
     for (int w = 0; w < NW; ++w) {
-        float P[NC];
+        float P[R][NC];
 #pragma unroll
-        for (int n = 0; n < NC; ++n) P[n] = 0.0f;
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int n = 0; n < NC; ++n) P[r][n] = 0.0f;
         for (int kb = w; kb < nsb; kb += NW) {
-            const int vl = lds32(ql + kb * 128 + 4 * lane);
-            const int vh = lds32(qh + kb * 64 + hoff) >> hsh;
-            const int sc0 = sc[kb * 16 + so], sc1 = sc[kb * 16 + so + 4];
-            const float d6 = __half2float(dd[kb]);
-            const int vi0 = __vsubss4((vl & 0x0F0F0F0F) | ((vh << 4) & 0x30303030), 0x20202020);
-            const int vi1 = __vsubss4(((vl >> 4) & 0x0F0F0F0F) | (vh & 0x30303030), 0x20202020);
             const int j0 = 8 * kb + A;
+            int u0[NC], u1[NC], c0[NC], c1[NC];
+            float d0[NC], d1[NC];
 #pragma unroll
             for (int n = 0; n < NC; ++n) {
                 const int8_t *xq = s.q + (size_t)n * K;
-                const int u0 = lds32(xq + 32 * j0 + p0), u1 = lds32(xq + 32 * (j0 + 2) + p0);
-                const float d0 = s.d[n * nb + j0], d1 = s.d[n * nb + j0 + 2];
-                const float sf = __fmaf_rn(d1, (float)(__dp4a(vi1, u1, 0) * sc1),
-                                           __fmaf_rn(d0, (float)(__dp4a(vi0, u0, 0) * sc0), 0.0f));
-                P[n] = __fmaf_rn(d6, sf, P[n]);
+                u0[n] = lds32(xq + 32 * j0 + p0);
+                u1[n] = lds32(xq + 32 * (j0 + 2) + p0);
+                c0[n] = __dp4a((int)0xE0E0E0E0, u0[n], 0);
+                c1[n] = __dp4a((int)0xE0E0E0E0, u1[n], 0);
+                d0[n] = s.d[n * nb + j0];
+                d1[n] = s.d[n * nb + j0 + 2];
+            }
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const int lr = lr0 + 8 * r;
+                const int vl = lds32(S.row(0, lr) + kb * 128 + 4 * lane);
+                const int vh = lds32(S.row(1, lr) + kb * 64 + hoff) >> hsh;
+                const int8_t *sc = reinterpret_cast<const int8_t *>(S.row(2, lr)) + kb * 16 + so;
+                const int sc0 = sc[0], sc1 = sc[4];
+                const float d6 = __half2float(reinterpret_cast<const __half *>(S.row(3, lr))[kb]);
+                const int q0 = (vl & 0x0F0F0F0F) | ((vh << 4) & 0x30303030);
+                const int q1 = ((vl >> 4) & 0x0F0F0F0F) | (vh & 0x30303030);
+#pragma unroll
+                for (int n = 0; n < NC; ++n) {
+                    const float sf = __fmaf_rn(d1[n], i2f_exact(__dp4a(q1, u1[n], c1[n]) * sc1),
+                                               __fmaf_rn(d0[n], i2f_exact(__dp4a(q0, u0[n], c0[n]) * sc0), 0.0f));
+                    P[r][n] = __fmaf_rn(d6, sf, P[r][n]);
+                }
             }
         }
 #pragma unroll
-        for (int n = 0; n < NC; ++n) leaf[n] = w == 0 ? P[n] : __fadd_rn(leaf[n], P[n]);
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int n = 0; n < NC; ++n) leaf[r][n] = w == 0 ? P[r][n] : __fadd_rn(leaf[r][n], P[r][n]);
     }
 #pragma unroll
-    for (int n = 0; n < NC; ++n) out[n] = warp_sum_bf(leaf[n]);
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int n = 0; n < NC; ++n) out[r][n] = warp_sum_bf(leaf[r][n]);
 }
 
 // Q4_K (candle vec_dot_q4_K_q8_1, qi 32, vdr 2): 16 threads per super-block;
@@ -125,97 +158,137 @@ __device__ __forceinline__ void mmvq_q6k(const uint8_t *ql, const uint8_t *qh, c
 // 2c+1 (high) with c = (t%16)/4, positions 4o..4o+3 and 16+4o..+3 (o = t%4):
 //   sumf_d = sum_i dx_i*float(I_i*sc_i), sumf_m = sum_i dx_i*float(Q_i*m_i)
 //   P += fma(d, sumf_d, -(dmin*sumf_m))   (Q_i = sum of the 8 activation bytes)
-template <int NC, int NW>
-__device__ __forceinline__ void mmvq_q4k(const uint8_t *row, int nsb, const SmAct &s, int K, int lane,
-                                         float (&out)[NC]) {
+template <int NC, int NW, int R>
+__device__ __forceinline__ void mmvq_q4k(const StageRows &S, int lr0, int nsb, const SmAct &s, int K, int lane,
+                                         float (&out)[R][NC]) {
     const int nb = K >> 5;
     const int c = (lane & 15) >> 2, o = lane & 3;
-    float leaf[NC];
+    float leaf[R][NC];
 #pragma unroll
     for (int w = 0; w < NW; ++w) {
-        float P[NC];
+        float P[R][NC];
 #pragma unroll
-        for (int n = 0; n < NC; ++n) P[n] = 0.0f;
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int n = 0; n < NC; ++n) P[r][n] = 0.0f;
         for (int kb = 2 * w + (lane >> 4); kb < nsb; kb += 2 * NW) {
-            const uint8_t *sb = row + kb * 144;
-            const uint32_t dmw = (uint32_t)lds32(sb);
-            const float dall = h2f((uint16_t)(dmw & 0xffff)), dmin = h2f((uint16_t)(dmw >> 16));
-            const uint8_t *sp = sb + 4;
-            int sca, scb, ma, mb;
-            if (c < 2) {
-                sca = sp[2 * c] & 63;
-                scb = sp[2 * c + 1] & 63;
-                ma = sp[2 * c + 4] & 63;
-                mb = sp[2 * c + 5] & 63;
-            } else {
-                const int ja = 2 * c, jb = 2 * c + 1;
-                sca = (sp[ja + 4] & 0xf) | ((sp[ja - 4] >> 6) << 4);
-                ma = (sp[ja + 4] >> 4) | ((sp[ja] >> 6) << 4);
-                scb = (sp[jb + 4] & 0xf) | ((sp[jb - 4] >> 6) << 4);
-                mb = (sp[jb + 4] >> 4) | ((sp[jb] >> 6) << 4);
-            }
-            const int v0 = lds32(sb + 16 + 32 * c + 4 * o), v1 = lds32(sb + 32 + 32 * c + 4 * o);
             const int ja = 8 * kb + 2 * c;
+            int ua0[NC], ua1[NC], ub0[NC], ub1[NC], qa[NC], qb[NC];
+            float d8a[NC], d8b[NC];
 #pragma unroll
             for (int n = 0; n < NC; ++n) {
                 const int8_t *xq = s.q + (size_t)n * K + 32 * ja + 4 * o;
-                const int ua0 = lds32(xq), ua1 = lds32(xq + 16), ub0 = lds32(xq + 32), ub1 = lds32(xq + 48);
-                const float d8a = s.d[n * nb + ja], d8b = s.d[n * nb + ja + 1];
-                const int dot1a = __dp4a(v1 & 0x0F0F0F0F, ua1, __dp4a(v0 & 0x0F0F0F0F, ua0, 0));
-                const int dot1b = __dp4a((v1 >> 4) & 0x0F0F0F0F, ub1, __dp4a((v0 >> 4) & 0x0F0F0F0F, ub0, 0));
-                const int dot2a = __dp4a(0x01010101, ua1, __dp4a(0x01010101, ua0, 0));
-                const int dot2b = __dp4a(0x01010101, ub1, __dp4a(0x01010101, ub0, 0));
-                const float sd = __fmaf_rn(d8b, (float)(dot1b * scb), __fmaf_rn(d8a, (float)(dot1a * sca), 0.0f));
-                const float sm = __fmaf_rn(d8b, (float)(dot2b * mb), __fmaf_rn(d8a, (float)(dot2a * ma), 0.0f));
-                P[n] = __fadd_rn(P[n], __fmaf_rn(dall, sd, -__fmul_rn(dmin, sm)));
+                ua0[n] = lds32(xq);
+                ua1[n] = lds32(xq + 16);
+                ub0[n] = lds32(xq + 32);
+                ub1[n] = lds32(xq + 48);
+                qa[n] = __dp4a(0x01010101, ua1[n], __dp4a(0x01010101, ua0[n], 0));
+                qb[n] = __dp4a(0x01010101, ub1[n], __dp4a(0x01010101, ub0[n], 0));
+                d8a[n] = s.d[n * nb + ja];
+                d8b[n] = s.d[n * nb + ja + 1];
+            }
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const uint8_t *sb = S.row(0, lr0 + 8 * r) + kb * 144;
+                const uint32_t dmw = (uint32_t)lds32(sb);
+                const float dall = h2f((uint16_t)(dmw & 0xffff)), dmin = h2f((uint16_t)(dmw >> 16));
+                // 6-bit scale / min of sub-blocks 2c, 2c+1 (GGUF packing)
+                const uint32_t s0 = (uint32_t)lds32(sb + 4), s1 = (uint32_t)lds32(sb + 8), s2 = (uint32_t)lds32(sb + 12);
+                uint32_t scw, mw;  // bytes: scale of 2c, 2c+1 / min of 2c, 2c+1 in the low 16 bits
+                if (c < 2) {
+                    scw = (s0 >> (16 * c)) & 0x3f3f;
+                    mw = (s1 >> (16 * c)) & 0x3f3f;
+                } else {
+                    const int h = 16 * (c - 2);
+                    scw = ((s2 >> h) & 0x0f0f) | (((s0 >> h) & 0xc0c0) >> 2);
+                    mw = (((s2 >> h) >> 4) & 0x0f0f) | (((s1 >> h) & 0xc0c0) >> 2);
+                }
+                const int sca = scw & 0xff, scb = scw >> 8, ma = mw & 0xff, mb = mw >> 8;
+                const int v0 = lds32(sb + 16 + 32 * c + 4 * o), v1 = lds32(sb + 32 + 32 * c + 4 * o);
+                const int la0 = v0 & 0x0F0F0F0F, la1 = v1 & 0x0F0F0F0F;
+                const int hb0 = (v0 >> 4) & 0x0F0F0F0F, hb1 = (v1 >> 4) & 0x0F0F0F0F;
+#pragma unroll
+                for (int n = 0; n < NC; ++n) {
+                    const int dot1a = __dp4a(la1, ua1[n], __dp4a(la0, ua0[n], 0));
+                    const int dot1b = __dp4a(hb1, ub1[n], __dp4a(hb0, ub0[n], 0));
+                    const float sd = __fmaf_rn(d8b[n], i2f_exact(dot1b * scb), __fmaf_rn(d8a[n], i2f_exact(dot1a * sca), 0.0f));
+                    const float sm = __fmaf_rn(d8b[n], i2f_exact(qb[n] * mb), __fmaf_rn(d8a[n], i2f_exact(qa[n] * ma), 0.0f));
+                    P[r][n] = __fadd_rn(P[r][n], __fmaf_rn(dall, sd, -__fmul_rn(dmin, sm)));
+                }
             }
         }
 #pragma unroll
-        for (int n = 0; n < NC; ++n) leaf[n] = w == 0 ? P[n] : __fadd_rn(leaf[n], P[n]);
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int n = 0; n < NC; ++n) leaf[r][n] = w == 0 ? P[r][n] : __fadd_rn(leaf[r][n], P[r][n]);
     }
 #pragma unroll
-    for (int n = 0; n < NC; ++n) out[n] = warp_sum_bf(leaf[n]);
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int n = 0; n < NC; ++n) out[r][n] = warp_sum_bf(leaf[r][n]);
 }
 
 // Q8_0 (candle vec_dot_q8_0_q8_1, qi 8, vdr 2): 4 threads per block; thread t
 // handles blocks t/4 + i*8NW, values 8o..8o+7 (o = t%4): P = fma(dw*dx, float(I), P).
-template <int NC, int NW>
-__device__ __forceinline__ void mmvq_q80(const uint8_t *qs, const __half *dd, int nb, const SmAct &s, int K, int lane,
-                                         float (&out)[NC]) {
+template <int NC, int NW, int R>
+__device__ __forceinline__ void mmvq_q80(const StageRows &S, int lr0, int nb, const SmAct &s, int K, int lane,
+                                         float (&out)[R][NC]) {
     const int o = lane & 3;
-    float leaf[NC];
+    float leaf[R][NC];
 #pragma unroll
     for (int w = 0; w < NW; ++w) {
-        float P[NC];
+        float P[R][NC];
 #pragma unroll
-        for (int n = 0; n < NC; ++n) P[n] = 0.0f;
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int n = 0; n < NC; ++n) P[r][n] = 0.0f;
         for (int kb = 8 * w + (lane >> 2); kb < nb; kb += 8 * NW) {
-            const int v0 = lds32(qs + kb * 32 + 8 * o), v1 = lds32(qs + kb * 32 + 8 * o + 4);
-            const float dw = __half2float(dd[kb]);
+            int x0[NC], x1[NC];
+            float dx[NC];
 #pragma unroll
             for (int n = 0; n < NC; ++n) {
                 const int8_t *xq = s.q + (size_t)n * K + 32 * kb + 8 * o;
-                const int sumi = __dp4a(v1, lds32(xq + 4), __dp4a(v0, lds32(xq), 0));
-                P[n] = __fmaf_rn(__fmul_rn(dw, s.d[n * nb + kb]), (float)sumi, P[n]);
+                x0[n] = lds32(xq);
+                x1[n] = lds32(xq + 4);
+                dx[n] = s.d[n * nb + kb];
+            }
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const int lr = lr0 + 8 * r;
+                const uint8_t *qs = S.row(0, lr) + kb * 32 + 8 * o;
+                const int v0 = lds32(qs), v1 = lds32(qs + 4);
+                const float dw = __half2float(reinterpret_cast<const __half *>(S.row(1, lr))[kb]);
+#pragma unroll
+                for (int n = 0; n < NC; ++n)
+                    P[r][n] = __fmaf_rn(__fmul_rn(dw, dx[n]), i2f_exact(__dp4a(v1, x1[n], __dp4a(v0, x0[n], 0))), P[r][n]);
             }
         }
 #pragma unroll
-        for (int n = 0; n < NC; ++n) leaf[n] = w == 0 ? P[n] : __fadd_rn(leaf[n], P[n]);
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int n = 0; n < NC; ++n) leaf[r][n] = w == 0 ? P[r][n] : __fadd_rn(leaf[r][n], P[r][n]);
     }
 #pragma unroll
-    for (int n = 0; n < NC; ++n) out[n] = warp_sum_bf(leaf[n]);
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int n = 0; n < NC; ++n) out[r][n] = warp_sum_bf(leaf[r][n]);
 }
 
 // F32 weights (candle: a cuBLAS matmul; this project's order): lane l's FMA
-// chain over elements l, l+32, ..., then the butterfly sum.
-template <int NC>
-__device__ __forceinline__ void mm_f32(const float *w, const SmAct &s, int K, int lane, float (&out)[NC]) {
+// chain over elements l, l+32, ..., then the butterfly sum. Rows from global memory.
+template <int NC, int R>
+__device__ __forceinline__ void mm_f32(const StageRows &S, int lr0, const SmAct &s, int K, int lane,
+                                       float (&out)[R][NC]) {
 #pragma unroll
-    for (int n = 0; n < NC; ++n) {
-        const float *x = s.xf + (size_t)n * K;
-        float acc = 0.0f;
-        for (int i = lane; i < K; i += 32) acc = __fmaf_rn(w[i], x[i], acc);
-        out[n] = warp_sum_bf(acc);
+    for (int r = 0; r < R; ++r) {
+        const float *w = reinterpret_cast<const float *>(S.row(0, lr0 + 8 * r));
+#pragma unroll
+        for (int n = 0; n < NC; ++n) {
+            const float *x = s.xf + (size_t)n * K;
+            float acc = 0.0f;
+            for (int i = lane; i < K; i += 32) acc = __fmaf_rn(w[i], x[i], acc);
+            out[r][n] = warp_sum_bf(acc);
+        }
     }
 }
 
@@ -247,20 +320,33 @@ __device__ void small_prologue(const PrepArgs &p, int n0, const SmAct &s, int NC
             gb[i] = __ldg(p.gamma + i);
             gb[K + i] = __ldg(p.beta + i);
         }
-        for (int n = warp; n < rows; n += nw) {
-            float sum = 0.0f;
-            for (int t = 0; t < T; ++t) {
-                const int i = 32 * t + lane;
-                const float v = small_input<MODE>(p, pos, n0 + n, i);
-                xs[(size_t)n * K + i] = v;
-                if constexpr (MODE == PREP_EMBED_LN)
-                    if (write_x) p.x_out[(size_t)(n0 + n) * K + i] = v;
-                sum = t == 0 ? v : __fadd_rn(sum, v);
+        // the rows' inputs into shared memory by every thread, 8 loads in flight
+        // each (one memory round trip), then the statistics from there
+        for (int base = threadIdx.x; base < rows * K; base += 8 * blockDim.x) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int idx = base + u * blockDim.x;
+                v[u] = idx < rows * K ? small_input<MODE>(p, pos, n0 + idx / K, idx % K) : 0.0f;
             }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int idx = base + u * blockDim.x;
+                if (idx >= rows * K) break;
+                xs[idx] = v[u];
+                if constexpr (MODE == PREP_EMBED_LN)
+                    if (write_x) p.x_out[(size_t)n0 * K + idx] = v[u];
+            }
+        }
+        __syncthreads();
+        for (int n = warp; n < rows; n += nw) {
+            const float *xr = xs + (size_t)n * K;
+            float sum = 0.0f;
+            for (int t = 0; t < T; ++t) sum = t == 0 ? xr[lane] : __fadd_rn(sum, xr[32 * t + lane]);
             const float mean = __fdiv_rn(warp_tree(sum), (float)K);
             float s2 = 0.0f;
             for (int t = 0; t < T; ++t) {
-                const float c = __fsub_rn(xs[(size_t)n * K + 32 * t + lane], mean);
+                const float c = __fsub_rn(xr[32 * t + lane], mean);
                 const float c2 = __fmul_rn(c, c);
                 s2 = t == 0 ? c2 : __fadd_rn(s2, c2);
             }
@@ -310,7 +396,8 @@ __device__ void small_prologue(const PrepArgs &p, int n0, const SmAct &s, int NC
 
 // ---------------------------------------------------------------------------
 
-template <int TYPE, int EPI, int MODE, int NC, int NW>
+// R: weight rows per warp per stage (a stage holds 8R rows).
+template <int TYPE, int EPI, int MODE, int NC, int NW, int R>
 __global__ void __launch_bounds__(256) small_mm_kernel(const __grid_constant__ SmallArgs A) {
     extern __shared__ __align__(16) uint8_t sm_raw[];
     __shared__ __align__(8) uint64_t full[4];
@@ -320,7 +407,8 @@ __global__ void __launch_bounds__(256) small_mm_kernel(const __grid_constant__ S
     const Matrix &W = g.W;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr bool STAGED = TYPE != T_F32;  // F32 rows are read from global memory
-    const int K = W.K, RS = STAGED ? A.stages : 1, CR = A.chunk, n0 = A.n0;
+    constexpr int CR = 8 * R;               // weight rows per stage
+    const int K = W.K, RS = STAGED ? A.stages : 1, n0 = A.n0;
     const int r0 = blockIdx.x * A.rows_per_cta, r1 = min(W.Np, r0 + A.rows_per_cta);
     const int nchunks = r0 < r1 ? (r1 - r0 + CR - 1) / CR : 0;
     int rb[4];
@@ -371,36 +459,36 @@ __global__ void __launch_bounds__(256) small_mm_kernel(const __grid_constant__ S
             if (!ok) break;
         }
         const int c0 = r0 + ci * CR, cr = min(CR, r1 - c0);
-        const uint8_t *st = STAGED ? stages + (size_t)(ci % RS) * stage_bytes : W.ra + (size_t)c0 * RB;
-        for (int lr = warp; lr < cr; lr += 8) {
-            const int row = c0 + lr;
-            float out[NC];
-            if constexpr (TYPE == T_Q6_K) {
-                const uint8_t *ql = st + (size_t)lr * rb[0];
-                const uint8_t *qh = st + (size_t)CR * rb[0] + (size_t)lr * rb[1];
-                const int8_t *sc = reinterpret_cast<const int8_t *>(st + (size_t)CR * (rb[0] + rb[1]) + (size_t)lr * rb[2]);
-                const __half *dd =
-                    reinterpret_cast<const __half *>(st + (size_t)CR * (rb[0] + rb[1] + rb[2]) + (size_t)lr * rb[3]);
-                mmvq_q6k<NC, NW>(ql, qh, sc, dd, W.nsb, s, K, lane, out);
-            } else if constexpr (TYPE == T_Q4_K) {
-                mmvq_q4k<NC, NW>(st + (size_t)lr * rb[0], W.nsb, s, K, lane, out);
-            } else if constexpr (TYPE == T_Q8_0) {
-                const __half *dd = reinterpret_cast<const __half *>(st + (size_t)CR * rb[0] + (size_t)lr * rb[1]);
-                mmvq_q80<NC, NW>(st + (size_t)lr * rb[0], dd, W.nb, s, K, lane, out);
-            } else {
-                mm_f32<NC>(reinterpret_cast<const float *>(st + (size_t)lr * rb[0]), s, K, lane, out);
+        StageRows S;
+        {
+            const uint8_t *st = STAGED ? stages + (size_t)(ci % RS) * stage_bytes : W.ra + (size_t)c0 * RB;
+            size_t off = 0;
+            for (int k = 0; k < 4; ++k) {
+                S.base[k] = st + off;
+                S.rb[k] = rb[k];
+                off += (size_t)CR * rb[k];
             }
-            if (row < W.N) {
-                // lane n handles column n (every lane holds every output)
+        }
+        // warp w: local rows w, w+8, ..., w+8(R-1); rows past the chunk compute on
+        // stale stage bytes and are not stored
+        float out[R][NC];
+        if constexpr (TYPE == T_Q6_K) mmvq_q6k<NC, NW, R>(S, warp, W.nsb, s, K, lane, out);
+        else if constexpr (TYPE == T_Q4_K) mmvq_q4k<NC, NW, R>(S, warp, W.nsb, s, K, lane, out);
+        else if constexpr (TYPE == T_Q8_0) mmvq_q80<NC, NW, R>(S, warp, W.nb, s, K, lane, out);
+        else mm_f32<NC, R>(S, warp, s, K, lane, out);
 #pragma unroll
-                for (int n = 0; n < NC; ++n) {
-                    if (n != lane || n0 + n >= g.rows) continue;
-                    if constexpr (EPI == EPI_ARGMAX) {
-                        if (g.logits) g.logits[(size_t)(n0 + n) * W.N + row] = out[n];
-                        argmax_merge(bv, bi, out[n], (uint32_t)row);
-                    } else {
-                        epilogue_store<EPI>(g, row, n0 + n, out[n]);
-                    }
+        for (int r = 0; r < R; ++r) {
+            const int lr = warp + 8 * r, row = c0 + lr;
+            if (lr >= cr || row >= W.N) continue;
+            // lane n handles column n (every lane holds every output)
+#pragma unroll
+            for (int n = 0; n < NC; ++n) {
+                if (n != lane || n0 + n >= g.rows) continue;
+                if constexpr (EPI == EPI_ARGMAX) {
+                    if (g.logits) g.logits[(size_t)(n0 + n) * W.N + row] = out[r][n];
+                    argmax_merge(bv, bi, out[r][n], (uint32_t)row);
+                } else {
+                    epilogue_store<EPI>(g, row, n0 + n, out[r][n]);
                 }
             }
         }

@@ -102,4 +102,7 @@ def workload(key: str) -> Workload:
     if key == "c2q4":  # the headline metric's q4_k_m weights on config 2's batch
         src = sorted(random_sources(64, 8, 64, V, 1), key=len, reverse=True)
         return Workload("c2q4", "600m", "q4_k_m", 0, 64, 64, src)
+    if key == "dp600":  # the headline set: 1024 sentences (config 2's lengths) in batches of 64,
+        # partitioned over the GPUs (translator.rs:140-147 batching, LPT placement)
+        return Workload("dp600", "600m", "q4_k_m", 0, 64, 64, random_sources(1024, 8, 64, V, 1))
     raise KeyError(key)

@@ -57,7 +57,7 @@ class Batch:
 class Engine:
     """One decode context on one GPU (mgb_open)."""
 
-    def __init__(self, gguf_path: str, device: int = 0, use_graphs: bool = True, graph_cache_mb: int = 512,
+    def __init__(self, gguf_path: str, device: int = 0, use_graphs: bool = True, graph_cache_mb: int = 8192,
                  fail_alloc_after: int = -1):
         L = _lib.load()
         opts = _lib.Options()
