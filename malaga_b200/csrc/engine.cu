@@ -290,6 +290,12 @@ struct mgb_ctx {
     int tc_split = 1;
     int tc_split_stages = 4;  // fewest stages per split (MGB_TC_SPLIT_STAGES)
     int tc_split_max = 4;     // most splits of a tile (MGB_TC_SPLIT_MAX)
+    // Failure-path test hooks of the small-batch kernel (MGB_TEST_WAIT_NS,
+    // MGB_TEST_WITHHOLD_CHUNK): a shorter limit for its bounded waits, and one
+    // weight chunk of its first CTA that is never copied, so that a wait runs
+    // out and the error word reports it. Off unless the variables are set.
+    uint64_t test_wait_ns = kWaitNs;
+    int test_withhold_chunk = -1;
     int sms = 148;  // multiprocessor count of the device (one tensor-core CTA each)
     void *enc_ws = nullptr;  // encoder temporaries (grown on demand)
     size_t enc_ws_bytes = 0;
@@ -724,6 +730,8 @@ static mgb_status small_t(mgb_ctx *c, const GemvArgs &g, const PrepArgs &p, int 
         const int nch = (rpc + 8 * R - 1) / (8 * R);
         a.stages = TYPE == T_F32 ? 0 : std::min(3, nch);
         a.err = c->d_err;
+        a.wait_ns = c->test_wait_ns;
+        a.withhold_chunk = c->test_withhold_chunk;
         const size_t act = small_act_bytes(NC, W.K, TYPE, MODE), sb = (size_t)8 * R * RB;
         while (a.stages > 1 && (size_t)a.stages * sb + act > c->smem_optin) --a.stages;
         const size_t smem = (size_t)a.stages * sb + act;
@@ -1781,6 +1789,8 @@ mgb_status mgb_open(const char *path, int device, const mgb_options *opts, mgb_c
     if (const char *v = getenv("MGB_TC_SPLIT")) c->tc_split = atoi(v) != 0;
     if (const char *v = getenv("MGB_TC_SPLIT_STAGES")) c->tc_split_stages = std::max(1, atoi(v));
     if (const char *v = getenv("MGB_TC_SPLIT_MAX")) c->tc_split_max = std::max(1, atoi(v));
+    if (const char *v = getenv("MGB_TEST_WAIT_NS")) c->test_wait_ns = std::max<uint64_t>(1000, strtoull(v, nullptr, 10));
+    if (const char *v = getenv("MGB_TEST_WITHHOLD_CHUNK")) c->test_withhold_chunk = atoi(v);
     cudaDeviceGetAttribute(&c->sms, cudaDevAttrMultiProcessorCount, device);
     if (c->sms <= 0) c->sms = 148;
     {

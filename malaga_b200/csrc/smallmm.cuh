@@ -63,6 +63,11 @@ struct SmallArgs {
     int rows_per_cta;  // weight rows per CTA (a multiple of 8)
     int stages;        // ring depth (1..4); 0 for F32 weights (read from global memory)
     uint32_t *err;
+    // Failure-path test hooks (mgb_ctx, set from MGB_TEST_* at mgb_open; off by
+    // default): the limit of every mbarrier wait, and one chunk of CTA 0 whose
+    // copy is withheld (-1: none), so that a bounded wait runs out.
+    uint64_t wait_ns;
+    int withhold_chunk;
 };
 
 __host__ __device__ inline size_t small_act_bytes(int NC, int K, int type, int mode) {
@@ -432,7 +437,8 @@ __global__ void __launch_bounds__(256) small_mm_kernel(const __grid_constant__ S
     };
     if (STAGED && tid == 0) {
         for (int i = 0; i < RS; ++i) mbar_init(&full[i], 1);
-        for (int i = 0; i < min(RS, nchunks); ++i) issue(i);
+        for (int i = 0; i < min(RS, nchunks); ++i)
+            if (!(blockIdx.x == 0 && i == A.withhold_chunk)) issue(i);
     }
     if constexpr (EPI == EPI_ARGMAX)
         if (lane < NC) {
@@ -454,7 +460,7 @@ __global__ void __launch_bounds__(256) small_mm_kernel(const __grid_constant__ S
     bool ok = true;
     for (; ci < nchunks; ++ci) {
         if constexpr (STAGED) {
-            ok = mbar_wait(&full[ci % RS], (uint32_t)((ci / RS) & 1));
+            ok = mbar_wait(&full[ci % RS], (uint32_t)((ci / RS) & 1), A.wait_ns);
             ok = __syncthreads_and(ok);
             if (!ok) break;
         }
@@ -494,7 +500,7 @@ __global__ void __launch_bounds__(256) small_mm_kernel(const __grid_constant__ S
         }
         if constexpr (STAGED) {
             __syncthreads();  // the stage is free
-            if (tid == 0 && ci + RS < nchunks) issue(ci + RS);
+            if (tid == 0 && ci + RS < nchunks && !(blockIdx.x == 0 && ci + RS == A.withhold_chunk)) issue(ci + RS);
         }
     }
     if (!ok) {
@@ -502,7 +508,9 @@ __global__ void __launch_bounds__(256) small_mm_kernel(const __grid_constant__ S
         // still in flight, produce nothing more
         if (tid == 0) {
             atomicOr(A.err, 2u);
-            for (int k = ci; k < min(nchunks, ci + RS); ++k) mbar_wait(&full[k % RS], (uint32_t)((k / RS) & 1));
+            for (int k = ci; k < min(nchunks, ci + RS); ++k)
+                if (!(blockIdx.x == 0 && k == A.withhold_chunk))
+                    mbar_wait(&full[k % RS], (uint32_t)((k / RS) & 1), A.wait_ns);
         }
         return;
     }

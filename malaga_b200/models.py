@@ -34,6 +34,9 @@ SPECS = {
     # name: (config, preset, seed, std)
     "mid": (_mid(), 0.05),
     "wide": (_mid(vocab=8192, d=1024, heads=16, ffn=4096, layers=2, max_pos=1024), 0.02),
+    # the 3.3B layer shapes (d_model 2048, 16 heads of 128, FFN 8192) with 2+2 layers
+    # and a smaller vocabulary, so that the CPU oracle checks them in seconds
+    "3.3b-lite": (_mid(vocab=16384, d=2048, heads=16, ffn=8192, layers=2, max_pos=256), 0.02),
     "600m": (C.NLLB_600M, 0.02),
     "1.3b": (C.NLLB_1_3B, 0.02),
     "3.3b": (C.NLLB_3_3B, 0.02),

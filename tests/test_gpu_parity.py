@@ -167,17 +167,71 @@ def test_invalid_arguments_fail_cleanly(gpu, model):
 
 
 @pytest.mark.slow
-def test_600m_q4_k_m_b1_config1_prefix_bit_exact(gpu, model):
-    """Config 1 at full size (NLLB-600M q4_k_m, 34-token source), first 3 forced
-    steps against the oracle (the oracle takes seconds per step at this size)."""
+def test_600m_q4_k_m_b1_config1_all_steps_bit_exact(gpu, model):
+    """Config 1 at full size (NLLB-600M q4_k_m, 34-token source, batch 1): all
+    32 forced steps, tokens and logits, against the oracle."""
     path = model("600m", "q4_k_m")
     w = models.workload("c1")
+    orc = oracle.Oracle(path)
+    want_ids, want_logits = orc.greedy(w.sources, models.TGT_TAG, w.steps, force=True, logits=True)
+    eng = Engine(path)
+    got_ids, got_logits = eng.greedy_logits(eng.encode(w.sources), models.TGT_TAG, w.steps, force=True)
+    np.testing.assert_array_equal(got_ids, want_ids)
+    assert np.array_equal(got_logits.view(np.uint32), want_logits.view(np.uint32))
+
+
+@pytest.mark.slow
+def test_600m_q8_0_b64_config2_prefix_bit_exact(gpu, model):
+    """Config 2 at full size (NLLB-600M q8_0, 64 sentences of 8-64 tokens): the
+    encoder and 3 forced steps on the tensor-core path, against the oracle."""
+    w = models.workload("c2")
+    path = model(w.model, w.preset, w.seed)
     orc = oracle.Oracle(path)
     want_ids, want_logits = orc.greedy(w.sources, models.TGT_TAG, 3, force=True, logits=True)
     eng = Engine(path)
     got_ids, got_logits = eng.greedy_logits(eng.encode(w.sources), models.TGT_TAG, 3, force=True)
     np.testing.assert_array_equal(got_ids, want_ids)
     assert np.array_equal(got_logits.view(np.uint32), want_logits.view(np.uint32))
+
+
+@pytest.mark.parametrize("preset", ["q4_k_m", "q8_0"])
+@pytest.mark.parametrize("n", [3, 20])
+def test_3_3b_layer_shapes_bit_exact(gpu, model, preset, n):
+    """The 3.3B layer shapes (d_model 2048, 16 heads of 128, FFN 8192; 2+2 layers,
+    16k vocabulary): 3 rows on the small-batch kernels, 20 rows (a 32-row bucket)
+    on the tensor cores, encoder included; tokens and logits bit-exact."""
+    path = model("3.3b-lite", preset)
+    V = models.config_of("3.3b-lite").vocab_size
+    src = models.random_sources(n, 3, 14, V, 31, src_tag=V - 1)
+    want_ids, want_logits = oracle.Oracle(path).greedy(src, V - 2, 3, force=True, logits=True)
+    eng = Engine(path)
+    got_ids, got_logits = eng.greedy_logits(eng.encode(src), V - 2, 3, force=True)
+    np.testing.assert_array_equal(got_ids, want_ids)
+    assert np.array_equal(got_logits.view(np.uint32), want_logits.view(np.uint32)), \
+        f"max |diff| {np.abs(got_logits - want_logits).max()}"
+
+
+def test_bounded_wait_that_runs_out_is_reported(gpu, model, monkeypatch):
+    """A bounded mbarrier wait that runs out: the test hook withholds one weight
+    copy of the small-batch kernel's first CTA and shortens the limit to 20 ms;
+    the kernel records the error word and returns (no hang, no fault), the call
+    fails with MGB_ERR_CUDA, and a context opened afterwards decodes correctly."""
+    from malaga_b200 import _lib
+
+    path = model("tiny", "q8_0")
+    src = tiny_sentences()[:1]  # 1 sentence: the encoder's matmuls run the small-batch kernel
+    monkeypatch.setenv("MGB_TEST_WAIT_NS", "20000000")
+    monkeypatch.setenv("MGB_TEST_WITHHOLD_CHUNK", "0")
+    eng = Engine(path)
+    with pytest.raises(MgbError) as e:
+        eng.encode(src)
+    assert e.value.code == _lib.MGB_ERR_CUDA
+    assert "ran out of time" in str(e.value)
+    eng.close()
+    monkeypatch.delenv("MGB_TEST_WAIT_NS")
+    monkeypatch.delenv("MGB_TEST_WITHHOLD_CHUNK")
+    want = [oracle.strip_eos(r, 2) for r in oracle.Oracle(path).greedy(src, TINY_TGT, 8)]
+    assert Translator(Engine(path)).generate(src, TINY_TGT, GenOptions(max_new_tokens=8)) == want
 
 
 @pytest.mark.parametrize("name,preset,b", [("mid", "q4_k_m", 64), ("mid", "q8_0", 24), ("wide", "q8_0", 64),
