@@ -108,14 +108,18 @@ __global__ void __launch_bounds__(256) beam_topk_kernel(const float *logits, int
 // (DecoderState::reorder, model.rs:209-226): dst[r] = src[from[r]] for the first
 // `npos` positions. Caches of up to 64 layers x {K, V}.
 struct KvGather {
-    const __half *src[128];
-    __half *dst[128];
+    const void *src[128];
+    void *dst[128];
     int n;  // caches (2 per layer)
 };
 
+// Beam reorder (DecoderState::reorder, model.rs:209-226): row r of every cache
+// takes the first npos positions of row from[r]; esz = element bytes (2: f16,
+// 4: f32), moved as 16-byte words.
 __global__ void __launch_bounds__(256) kv_gather_kernel(KvGather g, const int *from, int rows, int H, int m, int hd,
-                                                        int npos) {
-    const int per = npos * hd / 8;  // 16-byte words per (row, head)
+                                                        int npos, int esz) {
+    const int wpp = hd * esz / 16;  // words per position
+    const int per = npos * wpp;     // words per (row, head)
     const long total = (long)g.n * rows * H * per;
     for (long w = blockIdx.x * (long)blockDim.x + threadIdx.x; w < total; w += (long)gridDim.x * blockDim.x) {
         const int c = (int)(w / ((long)rows * H * per));
@@ -123,24 +127,29 @@ __global__ void __launch_bounds__(256) kv_gather_kernel(KvGather g, const int *f
         const int r = (int)(rem / ((long)H * per));
         rem %= (long)H * per;
         const int h = (int)(rem / per), o = (int)(rem % per);
-        const size_t src = (((size_t)from[r] * H + h) * m) * hd / 8 + o;
-        const size_t dst = (((size_t)r * H + h) * m) * hd / 8 + o;
+        const size_t src = (((size_t)from[r] * H + h) * m) * wpp + o;
+        const size_t dst = (((size_t)r * H + h) * m) * wpp + o;
         reinterpret_cast<uint4 *>(g.dst[c])[dst] = reinterpret_cast<const uint4 *>(g.src[c])[src];
     }
 }
 
-// Cross K/V of sentence r/rep (the batch, [n][H][S][hd]) into row r of the
-// state's caches ([rows][H][s][hd]), for one layer's K or V.
-__global__ void __launch_bounds__(256) cross_replicate_kernel(const __half *src, __half *dst, int rows, int rep, int H,
-                                                              int S, int s, int hd) {
-    const int per = S * hd / 8;
-    const long total = (long)rows * H * per;
-    for (long w = blockIdx.x * (long)blockDim.x + threadIdx.x; w < total; w += (long)gridDim.x * blockDim.x) {
-        const int r = (int)(w / ((long)H * per));
-        const long rem = w % ((long)H * per);
-        const int h = (int)(rem / per), o = (int)(rem % per);
-        reinterpret_cast<uint4 *>(dst)[(((size_t)r * H + h) * s) * hd / 8 + o] =
-            reinterpret_cast<const uint4 *>(src)[(((size_t)(r / rep) * H + h) * S) * hd / 8 + o];
+// A batch's f32 cross K/V [b][H][S][hd] into a decode state's buffers
+// [b*rep][H][s][hd]: every sentence to its rep consecutive rows, as f16 (the
+// fused greedy step's copy, graph.rs:95-96) or f32 (beam search's generic
+// decode, model.rs:209-226).
+__global__ void __launch_bounds__(256) cross_load_kernel(const float *src, void *dst, int to_f16, int rows, int rep,
+                                                         int H, int S, int s, int hd) {
+    const long total = (long)rows * H * S * hd;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        const int t = (int)(i % hd);
+        long rem = i / hd;
+        const int j = (int)(rem % S);
+        rem /= S;
+        const int h = (int)(rem % H), r = (int)(rem / H);
+        const float v = src[(((size_t)(r / rep) * H + h) * S + j) * hd + t];
+        const size_t at = (((size_t)r * H + h) * s + j) * hd + t;
+        if (to_f16) reinterpret_cast<__half *>(dst)[at] = __float2half_rn(v);
+        else reinterpret_cast<float *>(dst)[at] = v;
     }
 }
 

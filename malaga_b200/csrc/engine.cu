@@ -231,12 +231,13 @@ struct StaticState {
     float *x = nullptr, *q = nullptr, *a = nullptr, *u = nullptr, *xf = nullptr;
     QAct act;                        // q8_1 tensor-core activations of the next matmul
     SplitBufs split;                 // split-K partials and tile counters
-    // beam search (allocated on first use): step logits, top-k, row sources and a
-    // second set of self-attention caches to gather into
+    // beam search (allocated on first use): step logits, top-k, row sources, and
+    // the generic decode's f32 caches (model.rs:124-133: self K/V, with a second
+    // set to gather into; the sentences' cross K/V per beam row)
     float *beam_logits = nullptr, *beam_vals = nullptr;
     uint32_t *beam_idx = nullptr;
     int *beam_from = nullptr;
-    std::vector<__half *> kc2, vc2;
+    std::vector<float *> kc32, vc32, kc32b, vc32b, ck32, cv32;
     std::vector<__half *> kc, vc, ck, cv;
     float *part_v = nullptr;
     uint32_t *part_i = nullptr;
@@ -253,7 +254,7 @@ struct mgb_batch {
     int b = 0, s = 0;
     std::vector<uint32_t> lens;
     uint32_t *d_lens = nullptr;
-    __half *cross = nullptr;  // [L][2][b][H][s][hd]
+    float *cross = nullptr;  // f32 [L][2][b][H][s][hd], as encode_cross returns it (model.rs:463-477)
     size_t cross_bytes = 0;
     mgb_ctx *owner = nullptr;
 };
@@ -710,7 +711,7 @@ static cudaError_t small_launch_r(mgb_ctx *c, const SmallArgs &a, int grid, size
 }
 
 template <int TYPE, int EPI, int MODE>
-static mgb_status small_t(mgb_ctx *c, const GemvArgs &g, const PrepArgs &p, int *ctas) {
+static mgb_status small_t(mgb_ctx *c, const GemvArgs &g, const PrepArgs &p, int *ctas, int cls) {
     const Matrix &W = g.W;
     const int RB = row_bytes_of(TYPE, W.K), groups = W.Np / 8;
     const int R = TYPE != T_F32 && 32 * RB <= 32 * 1024 ? 4 : 1;
@@ -721,7 +722,8 @@ static mgb_status small_t(mgb_ctx *c, const GemvArgs &g, const PrepArgs &p, int 
     // launches of at most 8 activation rows (more only for F32 weights)
     for (int n0 = 0; n0 < g.rows; n0 += kSmallRows) {
         const int here = std::min(kSmallRows, g.rows - n0);
-        const int NC = here <= 1 ? 1 : here <= 2 ? 2 : here <= 4 ? 4 : 8;
+        // (5-8 rows of the reference's call: 2 warps, the 8-column variant)
+        const int NC = cls > 4 ? 8 : here <= 1 ? 1 : here <= 2 ? 2 : here <= 4 ? 4 : 8;
         SmallArgs a{};
         a.g = g;
         a.p = p;
@@ -752,16 +754,18 @@ static mgb_status small_t(mgb_ctx *c, const GemvArgs &g, const PrepArgs &p, int 
 }
 
 // y = W . act(p) with the reference's MMVQ arithmetic (at most 8 rows; F32
-// weights any number). *ctas: CTAs of the launch (argmax partials per row).
+// weights any number). cls: the rows of the reference's call (the MMVQ warp
+// count; 0 = g.rows). *ctas: CTAs of the launch (argmax partials per row).
 template <int EPI, int MODE>
-static mgb_status small_mm(mgb_ctx *c, GemvArgs g, PrepArgs p, int *ctas = nullptr) {
+static mgb_status small_mm(mgb_ctx *c, GemvArgs g, PrepArgs p, int *ctas = nullptr, int cls = 0) {
     p.rows = g.rows;
     p.K = g.W.K;
+    if (!cls) cls = g.rows;
     switch (g.W.type) {
-        case T_F32: return small_t<T_F32, EPI, MODE>(c, g, p, ctas);
-        case T_Q8_0: return small_t<T_Q8_0, EPI, MODE>(c, g, p, ctas);
-        case T_Q4_K: return small_t<T_Q4_K, EPI, MODE>(c, g, p, ctas);
-        case T_Q6_K: return small_t<T_Q6_K, EPI, MODE>(c, g, p, ctas);
+        case T_F32: return small_t<T_F32, EPI, MODE>(c, g, p, ctas, cls);
+        case T_Q8_0: return small_t<T_Q8_0, EPI, MODE>(c, g, p, ctas, cls);
+        case T_Q4_K: return small_t<T_Q4_K, EPI, MODE>(c, g, p, ctas, cls);
+        case T_Q6_K: return small_t<T_Q6_K, EPI, MODE>(c, g, p, ctas, cls);
     }
     return set_err(MGB_ERR_UNSUPPORTED, "matrix type %d", g.W.type);
 }
@@ -1054,8 +1058,9 @@ static mgb_status new_state(mgb_ctx *c, int b, int s, int m, StaticState **out) 
     }
     TRY(A((void **)&st->part_v, (size_t)4 * b * kLmParts));
     TRY(A((void **)&st->part_i, (size_t)4 * b * kLmParts));
-    if (b > kSmallRows && tc_ok(c->dec[0].qkv)) {
+    if (tc_ok(c->dec[0].qkv))  // (small batches too: beam prefills can take the MMQ path)
         TRY(alloc_tc_act(c, b, std::max(d, g.dec_ffn), st->act, st->allocs, &st->bytes));
+    if (b > kSmallRows && tc_ok(c->dec[0].qkv)) {
         // split-K: the largest (rows x units) of the step's matrices, rows padded to 64
         size_t pu = 0;
         for (const DecLayer &L : c->dec)
@@ -1088,12 +1093,14 @@ static GemvArgs mm_out(const Matrix &W, int rows) {
 }
 
 // A matmul of the decode step or the encoder: the reference's MMVQ arithmetic
-// (small-batch kernel) for at most 8 rows or F32 weights, else MMQ on the tensor
-// cores with the activations prepared by qprep_row into `act`.
+// (small-batch kernel) when its call has at most 8 rows (cls, default the
+// rows computed here) or for F32 weights, else MMQ on the tensor cores with the
+// activations prepared by qprep_row into `act`.
 template <int EPI, int MODE>
 static mgb_status matmul(mgb_ctx *c, const GemvArgs &g, const PrepArgs &p, const QAct *act, int *ctas = nullptr,
-                         const SplitBufs *split = nullptr) {
-    if (g.rows <= kSmallRows || !tc_ok(g.W)) return small_mm<EPI, MODE>(c, g, p, ctas);
+                         const SplitBufs *split = nullptr, int cls = 0) {
+    if (!cls) cls = g.rows;
+    if (cls <= kSmallRows || !tc_ok(g.W)) return small_mm<EPI, MODE>(c, g, p, ctas, cls);
     if (!act || !act->tq) return set_err(MGB_ERR_INVALID, "tensor-core activation buffers missing");
     PrepArgs pp = p;
     pp.rows = g.rows;
@@ -1114,30 +1121,45 @@ static mgb_status finalize(mgb_ctx *c, StaticState *st, int parts, int force) {
     return MGB_OK;
 }
 
-// One greedy decoder step on the state's fixed buffers (model.rs:552-612):
-// per layer fused QKV (+ f16 K/V cache write), self-attention, out-proj +
+// How a decoder step runs: the K/V element type and the rows of the
+// reference's matmul calls (candle picks MMVQ or MMQ, and MMVQ's warp count,
+// from them).
+struct StepMode {
+    bool kv32 = false;  // the generic decode's f32 self / cross K/V (beam search, model.rs:124-133)
+    int cls = 0;        // rows of the decoder-layer matmul calls (0: the state's rows)
+    int lm_cls = 0;     // rows of the LM head call (0: the state's rows)
+    bool lm = true;     // run the LM head (a prefill position whose logits are not used has none)
+};
+
+// One decoder step on the state's fixed buffers (model.rs:552-612):
+// per layer fused QKV (+ K/V cache write), self-attention, out-proj +
 // residual, cross-q, cross-attention, cross-out + residual, FFN up + ReLU,
 // down + residual, every LayerNorm folded into the next matmul's activation
 // prologue; then the tied LM head fused with the first argmax pass, finalize.
-// Up to 8 rows the matmuls are the small-batch kernel (MMVQ); above, the
-// tensor-core kernel (MMQ) reads q8_1 activations that qprep_row, or for the
-// out projections the attention kernel itself, writes into one of two buffers.
+// Calls of up to 8 rows run the small-batch kernel (MMVQ); larger ones the
+// tensor-core kernel (MMQ), which reads q8_1 activations that qprep_row, or for
+// the out projections the attention kernel itself, writes.
 static mgb_status launch_step(mgb_ctx *c, StaticState *st, float *logits, int force,
-                              cudaEvent_t lm0 = nullptr, cudaEvent_t lm1 = nullptr, bool finalize_step = true) {
+                              cudaEvent_t lm0 = nullptr, cudaEvent_t lm1 = nullptr, bool finalize_step = true,
+                              const StepMode &mode = StepMode{}) {
     const Config &g = c->cfg;
     const int b = st->b, d = g.d, H = g.dec_heads, hd = d / H;
-    const bool tc = b > kSmallRows;
-    const SplitBufs *sp = tc && c->tc_split ? &st->split : nullptr;
+    const int cls = mode.cls ? mode.cls : b, lm_cls = mode.lm_cls ? mode.lm_cls : b;
+    const bool tc = cls > kSmallRows && tc_ok(c->dec[0].qkv);
+    const SplitBufs *sp = tc && c->tc_split && st->split.part ? &st->split : nullptr;
+    const bool kv32 = mode.kv32;
     QAct *X = &st->act;  // tensor-core activations of the next matmul
     // attention whose outputs also go, as q8_1, into the next matmul's input
     const bool attn_q = tc && hd % 32 == 0;
+    auto attn = [&](const AttnArgs &a) { return kv32 ? attend<float>(c, a) : attend<__half>(c, a); };
     for (int l = 0; l < g.dec_layers; ++l) {
         const DecLayer &L = c->dec[l];
         // attn_norm(x) (layer 0: x = E[id]*scale + pos) -> fused QKV -> q, K/V cache slot *step
         GemvArgs gq = mm_out(L.qkv, b);
         gq.q = st->q;
-        gq.kc = st->kc[l];
-        gq.vc = st->vc[l];
+        gq.kc = kv32 ? (void *)st->kc32[l] : (void *)st->kc[l];
+        gq.vc = kv32 ? (void *)st->vc32[l] : (void *)st->vc[l];
+        gq.kv_f32 = kv32;
         gq.step = st->step;
         gq.H = H;
         gq.hd = hd;
@@ -1151,15 +1173,15 @@ static mgb_status launch_step(mgb_ctx *c, StaticState *st, float *logits, int fo
             pq.pos_table = c->pos;
             pq.pos_base = (uint32_t)g.pad + 1;
             pq.scale = c->embed_scale;
-            TRY((matmul<EPI_QKV, PREP_EMBED_LN>(c, gq, pq, X, nullptr, sp)));
+            TRY((matmul<EPI_QKV, PREP_EMBED_LN>(c, gq, pq, X, nullptr, sp, cls)));
         } else {
-            TRY((matmul<EPI_QKV, PREP_LN>(c, gq, pq, X, nullptr, sp)));
+            TRY((matmul<EPI_QKV, PREP_LN>(c, gq, pq, X, nullptr, sp, cls)));
         }
         AttnArgs sa{};
         sa.q = st->q;
         sa.q_row = d;
-        sa.K = st->kc[l];
-        sa.V = st->vc[l];
+        sa.K = gq.kc;
+        sa.V = gq.vc;
         sa.kv_row = hd;
         sa.kv_head = (long)st->m * hd;
         sa.kv_batch = (long)H * st->m * hd;
@@ -1172,36 +1194,37 @@ static mgb_status launch_step(mgb_ctx *c, StaticState *st, float *logits, int fo
         sa.queries = 1;
         sa.max_keys = st->m;
         if (attn_q) sa.qo = *X;
-        TRY(attend<__half>(c, sa));
+        TRY(attn(sa));
         GemvArgs go = mm_out(L.out, b);
         go.y = st->x;
         if (attn_q) TRY(gemm_tc<EPI_RESID>(c, L.out, *X, b, go, nullptr, sp));
-        else TRY((matmul<EPI_RESID, PREP_PLAIN>(c, go, prep_src(st->a, nullptr), X, nullptr, sp)));
+        else TRY((matmul<EPI_RESID, PREP_PLAIN>(c, go, prep_src(st->a, nullptr), X, nullptr, sp, cls)));
         // cross_norm -> cross_q -> cross attention -> cross_out + residual
         GemvArgs gc = mm_out(L.cq, b);
         gc.y = st->q;
-        TRY((matmul<EPI_STORE, PREP_LN>(c, gc, prep_src(st->x, &L.cross_norm), X, nullptr, sp)));
+        TRY((matmul<EPI_STORE, PREP_LN>(c, gc, prep_src(st->x, &L.cross_norm), X, nullptr, sp, cls)));
         AttnArgs ca = sa;
-        ca.K = st->ck[l];
-        ca.V = st->cv[l];
+        ca.K = kv32 ? (const void *)st->ck32[l] : (const void *)st->ck[l];
+        ca.V = kv32 ? (const void *)st->cv32[l] : (const void *)st->cv[l];
         ca.kv_head = (long)st->s * hd;
         ca.kv_batch = (long)H * st->s * hd;
         ca.step = nullptr;
         ca.lens = st->lens;
         ca.max_keys = st->s;
-        TRY(attend<__half>(c, ca));
+        TRY(attn(ca));
         GemvArgs gco = mm_out(L.co, b);
         gco.y = st->x;
         if (attn_q) TRY(gemm_tc<EPI_RESID>(c, L.co, *X, b, gco, nullptr, sp));
-        else TRY((matmul<EPI_RESID, PREP_PLAIN>(c, gco, prep_src(st->a, nullptr), X, nullptr, sp)));
+        else TRY((matmul<EPI_RESID, PREP_PLAIN>(c, gco, prep_src(st->a, nullptr), X, nullptr, sp, cls)));
         // ffn_norm -> up + ReLU -> down + residual
         GemvArgs gu = mm_out(L.up, b);
         gu.y = st->u;
-        TRY((matmul<EPI_RELU, PREP_LN>(c, gu, prep_src(st->x, &L.ffn_norm), X, nullptr, sp)));
+        TRY((matmul<EPI_RELU, PREP_LN>(c, gu, prep_src(st->x, &L.ffn_norm), X, nullptr, sp, cls)));
         GemvArgs gd = mm_out(L.down, b);
         gd.y = st->x;
-        TRY((matmul<EPI_RESID, PREP_PLAIN>(c, gd, prep_src(st->u, nullptr), X, nullptr, sp)));
+        TRY((matmul<EPI_RESID, PREP_PLAIN>(c, gd, prep_src(st->u, nullptr), X, nullptr, sp, cls)));
     }
+    if (!mode.lm) return MGB_OK;
     // dec_norm -> tied LM head fused with the first argmax pass -> greedy bookkeeping
     GemvArgs gl = mm_out(c->embed, b);
     gl.part_v = st->part_v;
@@ -1209,7 +1232,7 @@ static mgb_status launch_step(mgb_ctx *c, StaticState *st, float *logits, int fo
     gl.logits = logits;
     if (lm0) CK(cudaEventRecord(lm0, c->stream));
     int parts = kLmParts;
-    TRY((matmul<EPI_ARGMAX, PREP_LN>(c, gl, prep_src(st->x, &c->dec_norm), X, &parts)));
+    TRY((matmul<EPI_ARGMAX, PREP_LN>(c, gl, prep_src(st->x, &c->dec_norm), X, &parts, nullptr, lm_cls)));
     st->lm_parts = parts;
     if (lm1) CK(cudaEventRecord(lm1, c->stream));
     if (!finalize_step) return MGB_OK;
@@ -1304,7 +1327,7 @@ static mgb_status encode(mgb_ctx *c, const uint32_t *ids, const uint32_t *lens, 
     B->lens.assign(lens, lens + b);
     const int Hd = g.dec_heads, hdd = d / Hd;
     const size_t per = (size_t)b * Hd * S * hdd;
-    B->cross_bytes = per * 2 * 2 * g.dec_layers;
+    B->cross_bytes = per * 4 * 2 * g.dec_layers;
     TRY(c->dalloc((void **)&B->cross, B->cross_bytes));
     void *dl = nullptr;
     mgb_status s = c->dalloc(&dl, (size_t)4 * b);
@@ -1416,22 +1439,16 @@ static mgb_status acquire_state(mgb_ctx *c, const mgb_batch *B, int max_new, boo
         evict(c, st);
     }
     st->last_used = ++c->clock;
-    // reset (graph.rs:91-113): cross K/V, lens, start token, step, finished
+    // reset (graph.rs:91-113): cross K/V (converted to f16, graph.rs:95-96), lens,
+    // start token, step, finished
     const size_t per = (size_t)B->b * H * B->s * hd;
     for (int l = 0; l < g.dec_layers; ++l) {
-        if (rep == 1) {
-            CK(cudaMemcpy2DAsync(st->ck[l], (size_t)s * hd * 2, B->cross + per * 2 * l, (size_t)B->s * hd * 2,
-                                 (size_t)B->s * hd * 2, (size_t)n * H, cudaMemcpyDeviceToDevice, c->stream));
-            CK(cudaMemcpy2DAsync(st->cv[l], (size_t)s * hd * 2, B->cross + per * (2 * l + 1), (size_t)B->s * hd * 2,
-                                 (size_t)B->s * hd * 2, (size_t)n * H, cudaMemcpyDeviceToDevice, c->stream));
-        } else {
-            TRY(launch_check(c, [&] {
-                cross_replicate_kernel<<<c->sms * 4, 256, 0, c->stream>>>(B->cross + per * 2 * l, st->ck[l], n, rep, H,
-                                                                          B->s, s, hd);
-                cross_replicate_kernel<<<c->sms * 4, 256, 0, c->stream>>>(B->cross + per * (2 * l + 1), st->cv[l], n,
-                                                                          rep, H, B->s, s, hd);
-            }));
-        }
+        TRY(launch_check(c, [&] {
+            cross_load_kernel<<<c->sms * 4, 256, 0, c->stream>>>(B->cross + per * 2 * l, st->ck[l], 1, n, rep, H, B->s,
+                                                                 s, hd);
+            cross_load_kernel<<<c->sms * 4, 256, 0, c->stream>>>(B->cross + per * (2 * l + 1), st->cv[l], 1, n, rep,
+                                                                 H, B->s, s, hd);
+        }));
     }
     std::vector<uint32_t> lens(b, 1);
     for (int i = 0; i < n; ++i) lens[i] = B->lens[i / rep];
@@ -1459,11 +1476,12 @@ static mgb_status ensure_beam(mgb_ctx *c, StaticState *st) {
     TRY(A((void **)&st->beam_vals, (size_t)4 * b * 8));
     TRY(A((void **)&st->beam_idx, (size_t)4 * b * 8));
     TRY(A((void **)&st->beam_from, (size_t)4 * b));
-    st->kc2.resize(g.dec_layers);
-    st->vc2.resize(g.dec_layers);
+    for (auto *v : {&st->kc32, &st->vc32, &st->kc32b, &st->vc32b, &st->ck32, &st->cv32}) v->resize(g.dec_layers);
     for (int l = 0; l < g.dec_layers; ++l) {
-        TRY(A((void **)&st->kc2[l], (size_t)2 * b * H * st->m * hd));
-        TRY(A((void **)&st->vc2[l], (size_t)2 * b * H * st->m * hd));
+        for (auto *v : {&st->kc32, &st->vc32, &st->kc32b, &st->vc32b})
+            TRY(A((void **)&(*v)[l], (size_t)4 * b * H * st->m * hd));
+        TRY(A((void **)&st->ck32[l], (size_t)4 * b * H * st->s * hd));
+        TRY(A((void **)&st->cv32[l], (size_t)4 * b * H * st->s * hd));
     }
     return MGB_OK;
 }
@@ -1475,13 +1493,19 @@ static int32_t total_key(float f) {
     return v ^ (int32_t)(((uint32_t)(v >> 31)) >> 1);
 }
 
-// Beam search (translator.rs:250-335; top-k 343-358): rows = sentences x k on
-// the device; per step the engine's decode step writes every row's logits, the
-// device computes log_softmax statistics and each row's top k, and the host
-// merges the k*k candidates of every sentence (score descending, ties in
-// insertion order, beam-major then rank), retires hypotheses that end in eos
-// or at max_new with score / (len+1)^lp, and reorders the self-attention
-// caches by source row. Prefill [</s>, tgt] as two single-token steps.
+// Beam search (translator.rs:250-335; top-k 343-358) with the reference's
+// generic decode (Nllb::decode, model.rs:515-540): rows = sentences x k on the
+// device with f32 self and cross K/V (KvCache, model.rs:124-133); the prefill
+// [</s>, tgt] is one call of 2 tokens per row in the reference (its matmuls see
+// 2*rows rows, its LM head rows rows), run here as two single-token passes with
+// that row class -- each output of those matmuls depends only on its own row and
+// the class, so the values are the same; per step the LM head writes every
+// row's logits, the device computes log_softmax statistics and each row's top
+// k, the host merges the k*k candidates of every sentence (score descending,
+// ties in insertion order, beam-major then rank), retires hypotheses that end in
+// eos or at max_new with score / (len+1)^lp, and the self-attention caches are
+// gathered by source row (DecoderState::reorder; a row's cross K/V stays its
+// sentence's).
 static mgb_status run_beam(mgb_ctx *c, const mgb_batch *B, uint32_t tgt, int k, float lp, int max_new,
                            uint32_t *out_ids, uint32_t *out_lens) {
     const Config &g = c->cfg;
@@ -1490,26 +1514,28 @@ static mgb_status run_beam(mgb_ctx *c, const mgb_batch *B, uint32_t tgt, int k, 
     StaticState *st = nullptr;
     TRY(acquire_state(c, B, max_new, false, &st, k));
     TRY(ensure_beam(c, st));
-    const std::vector<__half *> kc0 = st->kc, vc0 = st->vc;
-    struct Restore {  // the state's cache pointers back as they were (graphs of other runs hold them)
-        StaticState *st;
-        const std::vector<__half *> &k, &v;
-        ~Restore() {
-            if (st->kc != k) {
-                std::swap(st->kc, st->kc2);
-                std::swap(st->vc, st->vc2);
-            }
-        }
-    } restore{st, kc0, vc0};
+    const size_t per = (size_t)B->b * H * B->s * hd;
+    for (int l = 0; l < g.dec_layers; ++l) {
+        TRY(launch_check(c, [&] {
+            cross_load_kernel<<<c->sms * 4, 256, 0, c->stream>>>(B->cross + per * 2 * l, st->ck32[l], 0, rows, k, H,
+                                                                 B->s, st->s, hd);
+            cross_load_kernel<<<c->sms * 4, 256, 0, c->stream>>>(B->cross + per * (2 * l + 1), st->cv32[l], 0, rows,
+                                                                 k, H, B->s, st->s, hd);
+        }));
+    }
     auto set_step = [&](uint32_t v) -> mgb_status {
         CK(cudaMemcpyAsync(st->step, &v, 4, cudaMemcpyHostToDevice, c->stream));
         return cudaStreamSynchronize(c->stream) == cudaSuccess ? MGB_OK : cuda_err(cudaGetLastError(), "beam step");
     };
+    StepMode prefill0, prefill1, stepm;
+    prefill0.kv32 = prefill1.kv32 = stepm.kv32 = true;
+    prefill0.cls = prefill1.cls = 2 * rows;
+    prefill0.lm = false;  // the first position's logits are not used (model.rs:535)
     TRY(set_step(0));
-    TRY(launch_step(c, st, st->beam_logits, 1, nullptr, nullptr, false));
+    TRY(launch_step(c, st, nullptr, 1, nullptr, nullptr, false, prefill0));
     TRY(set_ids(c, st, tgt));
     TRY(set_step(1));
-    TRY(launch_step(c, st, st->beam_logits, 1, nullptr, nullptr, false));
+    TRY(launch_step(c, st, st->beam_logits, 1, nullptr, nullptr, false, prefill1));
     const int L = max_new + 1;
     std::vector<float> alive_score(rows, 0.0f), nscore(rows), vals((size_t)rows * k);
     std::vector<uint32_t> alive_tok((size_t)rows * L, 0), ntok((size_t)rows * L, 0), idx((size_t)rows * k);
@@ -1617,19 +1643,19 @@ static mgb_status run_beam(mgb_ctx *c, const mgb_batch *B, uint32_t tgt, int k, 
             KvGather kg{};
             kg.n = 0;
             for (int l = l0; l < std::min(g.dec_layers, l0 + 64); ++l) {
-                kg.src[kg.n] = st->kc[l];
-                kg.dst[kg.n++] = st->kc2[l];
-                kg.src[kg.n] = st->vc[l];
-                kg.dst[kg.n++] = st->vc2[l];
+                kg.src[kg.n] = st->kc32[l];
+                kg.dst[kg.n++] = st->kc32b[l];
+                kg.src[kg.n] = st->vc32[l];
+                kg.dst[kg.n++] = st->vc32b[l];
             }
             TRY(launch_check(c, [&] {
-                kv_gather_kernel<<<c->sms * 4, 256, 0, c->stream>>>(kg, st->beam_from, rows, H, st->m, hd, step + 1);
+                kv_gather_kernel<<<c->sms * 4, 256, 0, c->stream>>>(kg, st->beam_from, rows, H, st->m, hd, step + 1, 4);
             }));
         }
-        std::swap(st->kc, st->kc2);
-        std::swap(st->vc, st->vc2);
+        std::swap(st->kc32, st->kc32b);
+        std::swap(st->vc32, st->vc32b);
         TRY(set_step((uint32_t)step + 1));
-        TRY(launch_step(c, st, st->beam_logits, 1, nullptr, nullptr, false));
+        TRY(launch_step(c, st, st->beam_logits, 1, nullptr, nullptr, false, stepm));
     }
     uint32_t derr = 0;
     CK(cudaMemcpyAsync(&derr, c->d_err, 4, cudaMemcpyDeviceToHost, c->stream));
@@ -1885,10 +1911,11 @@ void mgb_batch_free(mgb_batch *B) {
 }
 
 mgb_status mgb_batch_cross(mgb_ctx *c, const mgb_batch *B, uint32_t layer, int which, uint16_t *out) {
-    if (!c || !B || !out || layer >= (uint32_t)c->cfg.dec_layers || (which != 0 && which != 1))
-        return set_err(MGB_ERR_INVALID, "bad argument");
+    if (!c || !B || !out || layer >= (uint32_t)c->cfg.dec_layers) return set_err(MGB_ERR_INVALID, "bad argument");
     const size_t per = (size_t)B->b * c->cfg.d * B->s;
-    CK(cudaMemcpy(out, B->cross + per * (2 * layer + which), per * 2, cudaMemcpyDeviceToHost));
+    std::vector<float> f(per);
+    CK(cudaMemcpy(f.data(), B->cross + per * (2 * layer + which), per * 4, cudaMemcpyDeviceToHost));
+    for (size_t i = 0; i < per; ++i) out[i] = __half_as_ushort(__float2half_rn(f[i]));
     return MGB_OK;
 }
 

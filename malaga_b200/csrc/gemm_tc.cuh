@@ -571,7 +571,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
             }
             // QKV: q row, or this row's place in the step's K or V cache entry
             float *qkv_q = nullptr;
-            __half *qkv_c = nullptr;
+            uint8_t *qkv_c = nullptr;  // cache element of token 0 (f16 or f32: A.g.kv_f32)
             size_t qkv_tok = 0;
             if constexpr (EPI == EPI_QKV) {
                 const int dm = A.g.H * A.g.hd;
@@ -580,7 +580,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
                     qkv_tok = dm;
                 } else if (live) {
                     const int c = row - dm, which = c / dm, h = (c % dm) / A.g.hd, t = c % A.g.hd;
-                    qkv_c = (which == 0 ? A.g.kc : A.g.vc) + ((size_t)h * A.g.m + qkv_step) * A.g.hd + t;
+                    qkv_c = reinterpret_cast<uint8_t *>(which == 0 ? A.g.kc : A.g.vc) +
+                            (((size_t)h * A.g.m + qkv_step) * A.g.hd + t) * (A.g.kv_f32 ? 4 : 2);
                     qkv_tok = (size_t)A.g.H * A.g.m * A.g.hd;
                 }
             }
@@ -789,7 +790,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
                     } else if constexpr (EPI == EPI_QKV) {
                         const float y = __fadd_rn(acc[n], bias);
                         if (qkv_q) qkv_q[tok * qkv_tok] = y;
-                        else qkv_c[tok * qkv_tok] = __float2half_rn(y);
+                        else if (A.g.kv_f32) reinterpret_cast<float *>(qkv_c)[tok * qkv_tok] = y;
+                        else reinterpret_cast<__half *>(qkv_c)[tok * qkv_tok] = __float2half_rn(y);
                     } else {
                         epilogue_store<EPI>(A.g, row, tok, acc[n]);
                     }

@@ -91,12 +91,15 @@ struct GemvArgs {
     Matrix W;
     int rows;         // activation rows
     float *y;         // [rows][N] (STORE, RELU, RESID in place)
-    // QKV: q out [rows][d]; caches [rows][H][m][hd] at slot *step
+    // QKV: q out [rows][d]; caches [rows][H][m][hd] at slot *step, f16
+    // (the fused greedy step, graph.rs:58-63) or f32 (kv_f32: the generic
+    // decode's KvCache, model.rs:124-133)
     float *q;
-    __half *kc, *vc;
+    void *kc, *vc;
+    int kv_f32;
     const uint32_t *step;
     int H, hd, m;
-    // CROSSKV: caches [b][H][S][hd], token row = bi * S + j
+    // CROSSKV: f32 cross K/V [b][H][S][hd] (kc, vc), token row = bi * S + j
     int S;
     // ARGMAX: per (row, CTA) best (value, index); optional logits [rows][N]
     float *part_v;
@@ -127,15 +130,17 @@ __device__ __forceinline__ void epilogue_store(const GemvArgs &g, int row, int n
             g.q[(size_t)n * dm + row] = y;
         } else {
             const int c = row - dm, which = c / dm, h = (c % dm) / g.hd, t = c % g.hd;
-            __half *cache = which == 0 ? g.kc : g.vc;
-            cache[(((size_t)n * g.H + h) * g.m + *g.step) * g.hd + t] = __float2half_rn(y);
+            const size_t at = (((size_t)n * g.H + h) * g.m + *g.step) * g.hd + t;
+            void *cache = which == 0 ? g.kc : g.vc;
+            if (g.kv_f32) reinterpret_cast<float *>(cache)[at] = y;
+            else reinterpret_cast<__half *>(cache)[at] = __float2half_rn(y);
         }
     } else if constexpr (EPI == EPI_CROSSKV) {
         const float y = __fadd_rn(v, b);
         const int dm = g.H * g.hd, which = row / dm, c = row % dm, h = c / g.hd, t = c % g.hd;
         const int bi = n / g.S, jj = n % g.S;
-        __half *cache = which == 0 ? g.kc : g.vc;
-        cache[(((size_t)bi * g.H + h) * g.S + jj) * g.hd + t] = __float2half_rn(y);
+        float *cache = reinterpret_cast<float *>(which == 0 ? g.kc : g.vc);
+        cache[(((size_t)bi * g.H + h) * g.S + jj) * g.hd + t] = y;
     }
 }
 

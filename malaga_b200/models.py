@@ -37,6 +37,10 @@ SPECS = {
     # the 3.3B layer shapes (d_model 2048, 16 heads of 128, FFN 8192) with 2+2 layers
     # and a smaller vocabulary, so that the CPU oracle checks them in seconds
     "3.3b-lite": (_mid(vocab=16384, d=2048, heads=16, ffn=8192, layers=2, max_pos=256), 0.02),
+    # config 3's layer shapes (d_model 1024, FFN 8192, the full 256206 vocabulary) with 2+2 layers
+    "1.3b-lite": (C.NllbConfig(vocab_size=256206, d_model=1024, encoder_layers=2, decoder_layers=2,
+                               encoder_attention_heads=16, decoder_attention_heads=16, encoder_ffn_dim=8192,
+                               decoder_ffn_dim=8192, max_position_embeddings=1024), 0.02),
     "600m": (C.NLLB_600M, 0.02),
     "1.3b": (C.NLLB_1_3B, 0.02),
     "3.3b": (C.NLLB_3_3B, 0.02),

@@ -771,7 +771,8 @@ static void attend(const float *q, const float *K, const float *Vv, int n, int h
 typedef struct orc_enc {
     int b, s;
     uint32_t *lens;
-    float *ck, *cv; /* per decoder layer [b, H, s, hd], values rounded to f16 */
+    float *ck, *cv;     /* per decoder layer [b, H, s, hd], values rounded to f16 (the fused step's copy) */
+    float *ck32, *cv32; /* the same in f32, as encode_cross returns them (the generic decode's) */
 } orc_enc;
 
 ORC_EXPORT orc_enc *orc_encode(orc_model *m, const uint32_t *ids, const uint32_t *lens, int b, int s) {
@@ -823,6 +824,8 @@ ORC_EXPORT orc_enc *orc_encode(orc_model *m, const uint32_t *ids, const uint32_t
     size_t per = (size_t)b * Hd * s * hdd;
     E->ck = malloc(per * c->dec_layers * sizeof(float));
     E->cv = malloc(per * c->dec_layers * sizeof(float));
+    E->ck32 = malloc(per * c->dec_layers * sizeof(float));
+    E->cv32 = malloc(per * c->dec_layers * sizeof(float));
     float *kv = malloc((size_t)rows * 2 * d * sizeof(float));
     for (int l = 0; l < c->dec_layers; ++l) {
         linear(&m->dec[l].ckv, h, rows, rows, kv, 0);
@@ -832,6 +835,8 @@ ORC_EXPORT orc_enc *orc_encode(orc_model *m, const uint32_t *ids, const uint32_t
                     for (int t = 0; t < hdd; ++t) {
                         size_t src = ((size_t)bi * s + j) * 2 * d + hh * hdd + t;
                         size_t dst = per * l + (((size_t)bi * Hd + hh) * s + j) * hdd + t;
+                        E->ck32[dst] = kv[src];
+                        E->cv32[dst] = kv[src + d];
                         E->ck[dst] = rnd_h(kv[src]);
                         E->cv[dst] = rnd_h(kv[src + d]);
                     }
@@ -852,6 +857,8 @@ ORC_EXPORT orc_enc *orc_enc_synthetic(orc_model *m, const uint32_t *lens, int b,
     size_t n = (size_t)b * c->d * s * c->dec_layers;
     E->ck = malloc(n * sizeof(float));
     E->cv = malloc(n * sizeof(float));
+    E->ck32 = E->ck;
+    E->cv32 = E->cv;
     uint64_t x = seed * 0x9e3779b97f4a7c15ull + 1;
     for (size_t i = 0; i < n; ++i) {
         x ^= x << 13; x ^= x >> 7; x ^= x << 17;
@@ -863,6 +870,7 @@ ORC_EXPORT orc_enc *orc_enc_synthetic(orc_model *m, const uint32_t *lens, int b,
 
 ORC_EXPORT void orc_enc_free(orc_enc *E) {
     if (!E) return;
+    if (E->ck32 != E->ck) { free(E->ck32); free(E->cv32); }
     free(E->lens); free(E->ck); free(E->cv); free(E);
 }
 
@@ -878,7 +886,10 @@ ORC_EXPORT void orc_enc_cross(orc_model *m, orc_enc *E, int l, int which, float 
 
 typedef struct {
     int b, m;  /* rows, self-KV capacity */
-    int cls;   /* rows of the reference's matmul calls (graph.rs:242: the batch padded to a power of two) */
+    int cls;   /* rows of the reference's decoder-layer matmul calls (greedy: graph.rs:242, the batch
+                  padded to a power of two; beam prefill: 2 tokens per row) */
+    int lm_cls; /* rows of its LM head call */
+    int kv32;  /* 1: the generic decode's f32 self / cross K/V (beam search); 0: the fused step's f16 */
     float *kc, *vc; /* per layer [b, H, m, hd] (f16-exact values) */
     float *x, *h, *qkv, *a, *y, *u, *logits;
 } dstate_t;
@@ -888,6 +899,8 @@ static void dstate_init(orc_model *M, dstate_t *S, int b, int m, int cls) {
     int d = c->d;
     S->b = b;
     S->cls = cls;
+    S->lm_cls = cls;
+    S->kv32 = 0;
     S->m = m;
     size_t kv = (size_t)c->dec_layers * b * d * m;
     S->kc = calloc(kv, sizeof(float));
@@ -903,9 +916,11 @@ static void dstate_free(dstate_t *S) {
     free(S->logits);
 }
 
-/* One decoder step at position `step` for input tokens ids[b]; leaves logits [b, V] in S->logits.
- * `src_row[r]` maps decoder row r to its encoder row (beam search repeats sentences). */
-static void dec_step(orc_model *M, orc_enc *E, dstate_t *S, const uint32_t *ids, int step, const int *src_row) {
+/* One decoder step at position `step` for input tokens ids[b]; leaves logits [b, V] in S->logits
+ * (lm = 0: no LM head). `src_row[r]` maps decoder row r to its encoder row (beam search
+ * repeats sentences). */
+static void dec_step(orc_model *M, orc_enc *E, dstate_t *S, const uint32_t *ids, int step, const int *src_row,
+                     int lm) {
     const cfg_t *c = &M->c;
     int b = S->b, d = c->d, H = c->dec_heads, hd = d / H;
     for (int r = 0; r < b; ++r)
@@ -922,8 +937,10 @@ static void dec_step(orc_model *M, orc_enc *E, dstate_t *S, const uint32_t *ids,
             for (int hh = 0; hh < H; ++hh)
                 for (int t = 0; t < hd; ++t) {
                     size_t slot = (((size_t)r * H + hh) * S->m + step) * hd + t;
-                    kc[slot] = rnd_h(S->qkv[(size_t)r * 3 * d + d + hh * hd + t]);
-                    vc[slot] = rnd_h(S->qkv[(size_t)r * 3 * d + 2 * d + hh * hd + t]);
+                    const float kv_k = S->qkv[(size_t)r * 3 * d + d + hh * hd + t];
+                    const float kv_v = S->qkv[(size_t)r * 3 * d + 2 * d + hh * hd + t];
+                    kc[slot] = S->kv32 ? kv_k : rnd_h(kv_k);
+                    vc[slot] = S->kv32 ? kv_v : rnd_h(kv_v);
                 }
 #pragma omp parallel
         {
@@ -949,7 +966,8 @@ static void dec_step(orc_model *M, orc_enc *E, dstate_t *S, const uint32_t *ids,
                 for (int hh = 0; hh < H; ++hh) {
                     int sr = src_row ? src_row[r] : r;
                     size_t base = cper * l + ((size_t)sr * H + hh) * E->s * hd;
-                    attend(S->y + (size_t)r * d + hh * hd, E->ck + base, E->cv + base, (int)E->lens[sr], hd, hd,
+                    attend(S->y + (size_t)r * d + hh * hd, (S->kv32 ? E->ck32 : E->ck) + base,
+                           (S->kv32 ? E->cv32 : E->cv) + base, (int)E->lens[sr], hd, hd,
                            S->a + (size_t)r * d + hh * hd, e);
                 }
             free(e);
@@ -961,9 +979,10 @@ static void dec_step(orc_model *M, orc_enc *E, dstate_t *S, const uint32_t *ids,
         linear(&L->down, S->u, b, S->cls, S->y, 0);
         for (size_t i = 0; i < (size_t)b * d; ++i) S->x[i] = S->y[i] + S->x[i];
     }
+    if (!lm) return;
     layer_norm(S->x, &M->dec_norm, b, d, S->h);
     linear_t head = {M->embed, NULL};
-    linear(&head, S->h, b, S->cls, S->logits, 0);
+    linear(&head, S->h, b, S->lm_cls, S->logits, 0);
 }
 
 static uint32_t argmax_row(const float *v, int n) {
@@ -992,10 +1011,10 @@ ORC_EXPORT int orc_greedy(orc_model *M, orc_enc *E, uint32_t tgt, int max_new, i
     uint32_t *ids = malloc(b * sizeof(uint32_t));
     uint8_t *fin = calloc(b, 1);
     for (int r = 0; r < b; ++r) ids[r] = (uint32_t)c->start;
-    dec_step(M, E, &S, ids, 0, NULL);
+    dec_step(M, E, &S, ids, 0, NULL, 1);
     for (int r = 0; r < b; ++r) ids[r] = tgt;
     for (int st = 1; st <= max_new; ++st) {
-        dec_step(M, E, &S, ids, st, NULL);
+        dec_step(M, E, &S, ids, st, NULL, 1);
         if (logits) memcpy(logits + (size_t)(st - 1) * b * c->V, S.logits, (size_t)b * c->V * 4);
         for (int r = 0; r < b; ++r) {
             uint32_t tok = argmax_row(S.logits + (size_t)r * c->V, c->V);
@@ -1115,11 +1134,17 @@ ORC_EXPORT int orc_beam(orc_model *M, orc_enc *E, uint32_t tgt, int k, float lp,
     int *nlen = malloc(rows * sizeof(int));
     float *kbuf = malloc((size_t)c->dec_layers * rows * c->d * m * sizeof(float));
 
-    /* prefill [</s>, tgt] as two single-token steps (same K/V and logits as the causal prefill) */
+    /* the generic decode (model.rs:515-540): f32 K/V; the prefill [</s>, tgt] is one call of 2
+     * tokens per row (matmuls over 2*rows rows, the LM head over the last position's rows),
+     * computed as two single-token steps with those row classes */
+    S.kv32 = 1;
+    S.cls = 2 * rows;
+    S.lm_cls = rows;
     for (int r = 0; r < rows; ++r) ids[r] = (uint32_t)c->start;
-    dec_step(M, E, &S, ids, 0, src_row);
+    dec_step(M, E, &S, ids, 0, src_row, 0);
     for (int r = 0; r < rows; ++r) ids[r] = tgt;
-    dec_step(M, E, &S, ids, 1, src_row);
+    dec_step(M, E, &S, ids, 1, src_row, 1);
+    S.cls = rows;
     for (int step = 1; step <= max_new; ++step) {
         for (int r = 0; r < rows; ++r) {
             log_softmax_row(S.logits + (size_t)r * V, V, lp_row, tmp);
@@ -1218,7 +1243,7 @@ ORC_EXPORT int orc_beam(orc_model *M, orc_enc *E, uint32_t tgt, int k, float lp,
         }
         /* src_row is unchanged by reordering within a sentence */
         memcpy(ids, next, rows * sizeof(uint32_t));
-        dec_step(M, E, &S, ids, step + 1, src_row);
+        dec_step(M, E, &S, ids, step + 1, src_row, 1);
     }
     for (int s = 0; s < b; ++s) {
         int best = -1;

@@ -252,10 +252,13 @@ def test_tensor_core_batches_bit_exact(gpu, model, name, preset, b):
 
 
 @pytest.mark.parametrize("name,preset,n,k", [("tiny", "q8_0", 6, 3), ("tiny", "f32", 4, 2), ("mid", "q4_k_m", 4, 4),
-                                             ("mid", "q8_0", 3, 5)])
+                                             ("mid", "q8_0", 3, 5), ("mid", "q4_k_m", 1, 3), ("mid", "q8_0", 2, 2)])
 def test_beam_search_matches_oracle(gpu, model, name, preset, n, k):
-    """Beam search (translator.rs:250-358): device log_softmax + top-k, host merge;
-    the hypotheses equal the oracle's (mid q4_k_m: 16 rows run the tcgen05 step)."""
+    """Beam search (translator.rs:250-358) on the reference's generic decode: f32
+    self / cross K/V, the [</s>, tgt] prefill with the row class of a 2-token
+    call, device log_softmax + top-k, host merge; the hypotheses equal the
+    oracle's (mid q4_k_m 4x4: 16 rows run the tcgen05 step; 1x3: 3 rows on the
+    small kernels with a 6-row (2-warp) prefill; 2x2: 4 rows, 8-row prefill)."""
     path = model(name, preset)
     if name == "tiny":
         src, tgt = tiny_sentences()[:n], TINY_TGT
@@ -265,6 +268,21 @@ def test_beam_search_matches_oracle(gpu, model, name, preset, n, k):
     want = oracle.Oracle(path).beam(src, tgt, k, 12)
     eng = Engine(path)
     out, lens = eng.beam(eng.encode(src), tgt, k, 12)
+    got = [[int(t) for t in out[i, : lens[i]]] for i in range(len(src))]
+    assert got == [[int(t) for t in r] for r in want]
+
+
+@pytest.mark.slow
+def test_beam_config3_row_shape_full_vocabulary(gpu, model):
+    """Config 3's shape: beam 4 over 16 sources of 48 tokens (64 beam rows on the
+    tensor cores, a 128-row prefill), d_model 1024, FFN 8192 and the full 256206
+    vocabulary (2+2 layers): the hypotheses equal the oracle's."""
+    path = model("1.3b-lite", "q4_k_m", 2)
+    V = models.config_of("1.3b-lite").vocab_size
+    src = models.random_sources(16, 46, 46, V, 2, fixed_len=46)  # tag + 46 ids + </s> = 48
+    want = oracle.Oracle(path).beam(src, models.TGT_TAG, 4, 8)
+    eng = Engine(path)
+    out, lens = eng.beam(eng.encode(src), models.TGT_TAG, 4, 8)
     got = [[int(t) for t in out[i, : lens[i]]] for i in range(len(src))]
     assert got == [[int(t) for t in r] for r in want]
 
