@@ -650,21 +650,22 @@ static cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, size_t
 
 // Raises a kernel's dynamic shared-memory limit to the full 227 KB once
 // (before any graph capture: the first step of every shape runs eagerly).
+// (per device: one process may drive several GPUs, one context each)
 template <typename... KArgs>
 static cudaError_t allow_smem(void (*k)(KArgs...), size_t bytes) {
     static std::mutex mu;
-    static std::set<const void *> done;
+    static std::set<std::pair<int, const void *>> done;
     if (bytes <= 48 * 1024) return cudaSuccess;
-    std::lock_guard<std::mutex> lock(mu);
-    if (done.count((const void *)k)) return cudaSuccess;
     int dev = 0, optin = 0;
     cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (done.count({dev, (const void *)k})) return cudaSuccess;
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     cudaFuncAttributes fa{};
     cudaError_t e = cudaFuncGetAttributes(&fa, k);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes);
-    if (e == cudaSuccess) done.insert((const void *)k);
+    if (e == cudaSuccess) done.insert({dev, (const void *)k});
     return e;
 }
 

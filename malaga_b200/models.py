@@ -80,6 +80,12 @@ def random_sources(n: int, lo: int, hi: int, vocab: int, seed: int, src_tag: int
     return out
 
 
+def poisson_arrivals(n: int, rate: float, seed: int) -> np.ndarray:
+    """Arrival times (s) of a Poisson process of `rate` requests/s, seeded."""
+    u = C.seeded_uniform_u32(n, seed, 3, 1, 1 << 24).astype(np.float64) / float(1 << 24)
+    return np.cumsum(-np.log(u) / rate)
+
+
 def lognormal_sources(n: int, median: float, lo: int, hi: int, vocab: int, seed: int) -> list[list[int]]:
     """Lengths lognormal(median, sigma 0.5) clipped to [lo, hi] (configs 4 and 5)."""
     z = C.seeded_normal(n, seed, 2, 1.0).astype(np.float64)
@@ -109,6 +115,8 @@ def workload(key: str) -> Workload:
     if key == "c2q4":  # the headline metric's q4_k_m weights on config 2's batch
         src = sorted(random_sources(64, 8, 64, V, 1), key=len, reverse=True)
         return Workload("c2q4", "600m", "q4_k_m", 0, 64, 64, src)
+    if key == "c5":  # server simulation: 4096 single-sentence requests, lengths lognormal(24), 4..96
+        return Workload("c5", "600m", "q4_k_m", 0, 64, 0, lognormal_sources(4096, 24, 4, 96, V, 4))
     if key == "dp600":  # the headline set: 1024 sentences (config 2's lengths) in batches of 64,
         # partitioned over the GPUs (translator.rs:140-147 batching, LPT placement)
         return Workload("dp600", "600m", "q4_k_m", 0, 64, 64, random_sources(1024, 8, 64, V, 1))

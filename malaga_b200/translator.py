@@ -33,6 +33,11 @@ class GenOptions:
     # Decode every row to its full budget, ignoring end-of-sequence (the
     # benchmark configurations' "forced steps"). Not a reference option.
     force_steps: bool = False
+    # Per-sentence budget when max_new_tokens is None: floor(scale * len) + extra
+    # (the reference's rule is 2 * len + 16, translator.rs:179-183; config 5 of the
+    # benchmark uses 1.5 * len + 8).
+    budget_scale: float = 2.0
+    budget_extra: int = 16
 
 
 class Batch:
@@ -159,7 +164,7 @@ class Translator:
         self.cap = min(i["max_length"], i["max_position_embeddings"] - 2)
 
     def budget(self, n: int, opts: GenOptions) -> int:
-        v = opts.max_new_tokens if opts.max_new_tokens is not None else 2 * n + 16
+        v = opts.max_new_tokens if opts.max_new_tokens is not None else int(opts.budget_scale * n) + opts.budget_extra
         return max(1, min(v, self.cap))
 
     def generate(self, src: list[list[int]], tgt_lang: int, opts: GenOptions = GenOptions()) -> list[list[int]]:
