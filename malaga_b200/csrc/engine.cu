@@ -31,6 +31,7 @@
 #include "beam.cuh"
 #include "gemm_tc.cuh"
 #include "smallmm.cuh"
+#include "stepkernel.cuh"
 
 using namespace mgb;
 
@@ -231,6 +232,16 @@ struct StaticState {
     float *x = nullptr, *q = nullptr, *a = nullptr, *u = nullptr, *xf = nullptr;
     QAct act;                        // q8_1 tensor-core activations of the next matmul
     SplitBufs split;                 // split-K partials and tile counters
+    // persistent step kernel (batches of at most 8 rows): its phase table, grid
+    // barrier / abort words and shared-memory geometry
+    StepPhase *phases = nullptr;
+    int nphases = 0;
+    uint32_t *bar = nullptr;
+    unsigned long long *trace = nullptr;  // phase timing (MGB_STEP_TRACE)
+    std::vector<StepPhase> phase_host;
+    std::string trace_path;
+    int step_slots = 0, step_slot_bytes = 0, step_act_bytes = 0, step_ctas = 0;
+    size_t step_smem = 0;
     // beam search (allocated on first use): step logits, top-k, row sources, and
     // the generic decode's f32 caches (model.rs:124-133: self K/V, with a second
     // set to gather into; the sentences' cross K/V per beam row)
@@ -291,12 +302,20 @@ struct mgb_ctx {
     int tc_split = 1;
     int tc_split_stages = 4;  // fewest stages per split (MGB_TC_SPLIT_STAGES)
     int tc_split_max = 4;     // most splits of a tile (MGB_TC_SPLIT_MAX)
+    // The decoder layers of greedy steps of at most 8 rows run as one persistent
+    // kernel (1) or as one launch per operation (0, the default: measured faster
+    // on B200); MGB_STEP_KERNEL overrides.
+    int step_kernel = 0;
+    // MGB_STEP_TRACE=<file>: the persistent kernel times its phases; each state
+    // appends its per-launch averages to the file when it is freed.
+    std::string step_trace;
     // Failure-path test hooks of the small-batch kernel (MGB_TEST_WAIT_NS,
     // MGB_TEST_WITHHOLD_CHUNK): a shorter limit for its bounded waits, and one
     // weight chunk of its first CTA that is never copied, so that a wait runs
     // out and the error word reports it. Off unless the variables are set.
     uint64_t test_wait_ns = kWaitNs;
     int test_withhold_chunk = -1;
+    int test_withhold_step = -1;  // the same for the persistent step kernel (MGB_TEST_WITHHOLD_STEP)
     int sms = 148;  // multiprocessor count of the device (one tensor-core CTA each)
     void *enc_ws = nullptr;  // encoder temporaries (grown on demand)
     size_t enc_ws_bytes = 0;
@@ -1015,7 +1034,27 @@ static mgb_status alloc_tc_act(mgb_ctx *c, int rows, int kmax, QAct &a, std::vec
 // ---------------------------------------------------------------------------
 // Static state (graph.rs:23-135)
 
+// Appends a state's phase timing (per-launch averages, microseconds) to its file.
+static void dump_trace(StaticState *st) {
+    const size_t n = st->phase_host.size();
+    std::vector<unsigned long long> t(8 * n + 1);
+    if (cudaMemcpy(t.data(), st->trace, 8 * t.size(), cudaMemcpyDeviceToHost) != cudaSuccess || !t[8 * n]) return;
+    FILE *f = fopen(st->trace_path.c_str(), "a");
+    if (!f) return;
+    const double L = (double)t[8 * n], ctas = st->step_ctas > 0 ? st->step_ctas : 1;
+    fprintf(f, "# rows %d, launches %.0f: phase kind epi N K rsel | staged stats act chunk work barrier | cta_mean_us\n",
+            st->b, L);
+    for (size_t i = 0; i < n; ++i) {
+        const StepPhase &p = st->phase_host[i];
+        fprintf(f, "%zu %s %d %d %d %d |", i, p.kind == PH_MM ? "mm" : "attn", p.epi, p.W.N, p.W.K, p.rsel);
+        for (int k = 0; k < 6; ++k) fprintf(f, " %.2f", t[8 * i + k] / L / 1e3);
+        fprintf(f, " | %.2f\n", t[8 * i + 6] / L / ctas / 1e3);
+    }
+    fclose(f);
+}
+
 static void free_state(StaticState *st) {
+    if (st->trace) dump_trace(st);
     if (st->exec) cudaGraphExecDestroy(st->exec);
     for (void *p : st->allocs) cudaFree(p);
     st->allocs.clear();
@@ -1122,6 +1161,172 @@ static mgb_status finalize(mgb_ctx *c, StaticState *st, int parts, int force) {
     return MGB_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Persistent step kernel (stepkernel.cuh): batches of at most 8 rows, the
+// greedy step's f16 caches, quantized matrices.
+
+static bool step_kernel_ok(const mgb_ctx *c, int b) {
+    if (!c->step_kernel || b > kSmallRows) return false;
+    const int hd = c->cfg.d / c->cfg.dec_heads;
+    if (hd != 64 && hd != 128) return false;
+    if (!tc_ok(c->embed)) return false;
+    for (const DecLayer &L : c->dec)
+        for (const Matrix *M : {&L.qkv, &L.out, &L.cq, &L.co, &L.up, &L.down}) {
+            if (!tc_ok(*M)) return false;
+            int r0, r1;
+            cta_rows(M->Np, c->sms, 0, r0, r1);
+            if (r1 - r0 > kStepRows) return false;  // the kernel stages at most kStepRows rows' bias / residual
+        }
+    return true;
+}
+
+// The state's phase table and shared-memory geometry (first use of a state).
+static mgb_status build_step(mgb_ctx *c, StaticState *st) {
+    if (st->phases) return MGB_OK;
+    const Config &g = c->cfg;
+    const int b = st->b, d = g.d, H = g.dec_heads, hd = d / H;
+    const int NC = b <= 1 ? 1 : b <= 2 ? 2 : b <= 4 ? 4 : 8;
+    std::vector<StepPhase> ph;
+    int slot_bytes = 0;
+    size_t act = 0;
+    auto mm = [&](const Matrix &W, int epi, int mode, const float *x, const Norm *n, float *y, void *kc = nullptr,
+                  void *vc = nullptr) {
+        StepPhase p{};
+        p.kind = PH_MM;
+        p.W = W;
+        p.epi = epi;
+        p.mode = mode;
+        p.x = x;
+        if (n) {
+            p.gamma = n->g;
+            p.beta = n->b;
+        }
+        p.y = y;
+        p.kc = kc;
+        p.vc = vc;
+        const int RB = row_bytes_of(W.type, W.K);
+        const int per = (W.Np / 8 + c->sms - 1) / c->sms * 8;  // rows per CTA (stepkernel.cuh cta_rows)
+        p.rsel = per > 8 && 32 * RB <= 36 * 1024 ? 4 : 1;
+        slot_bytes = std::max(slot_bytes, 8 * p.rsel * RB);
+        act = std::max(act, small_act_bytes(NC, W.K, W.type, mode));
+        ph.push_back(p);
+    };
+    auto at = [&](bool self, int l) {
+        StepPhase p{};
+        p.kind = PH_ATTN;
+        p.aq = st->q;
+        p.K = self ? (const void *)st->kc[l] : (const void *)st->ck[l];
+        p.V = self ? (const void *)st->vc[l] : (const void *)st->cv[l];
+        p.kv_head = (long)(self ? st->m : st->s) * hd;
+        p.kv_batch = (long)H * (self ? st->m : st->s) * hd;
+        p.self = self;
+        p.aout = st->a;
+        ph.push_back(p);
+    };
+    for (int l = 0; l < g.dec_layers; ++l) {
+        const DecLayer &L = c->dec[l];
+        mm(L.qkv, EPI_QKV, l == 0 ? PREP_EMBED_LN : PREP_LN, st->x, &L.attn_norm, nullptr, st->kc[l], st->vc[l]);
+        at(true, l);
+        mm(L.out, EPI_RESID, PREP_PLAIN, st->a, nullptr, st->x);
+        mm(L.cq, EPI_STORE, PREP_LN, st->x, &L.cross_norm, st->q);
+        at(false, l);
+        mm(L.co, EPI_RESID, PREP_PLAIN, st->a, nullptr, st->x);
+        mm(L.up, EPI_RELU, PREP_LN, st->x, &L.ffn_norm, st->u);
+        mm(L.down, EPI_RESID, PREP_PLAIN, st->u, nullptr, st->x);
+    }
+    slot_bytes = (slot_bytes + 127) / 128 * 128;
+    act = (act + 127) / 128 * 128;
+    const size_t escr = (size_t)8 * std::max(st->m, st->s) * 4;
+    const int slots = (int)std::min<size_t>(8, (c->smem_optin - 8192 - act - escr) / slot_bytes);
+    if (slots < 2) return set_err(MGB_ERR_UNSUPPORTED, "persistent step: shared memory");
+    void *p = nullptr;
+    TRY(c->dalloc(&p, sizeof(StepPhase) * ph.size()));
+    st->allocs.push_back(p);
+    st->phases = (StepPhase *)p;
+    CK(cudaMemcpyAsync(st->phases, ph.data(), sizeof(StepPhase) * ph.size(), cudaMemcpyHostToDevice, c->stream));
+    TRY(c->dalloc(&p, 256));
+    st->allocs.push_back(p);
+    st->bar = (uint32_t *)p;
+    CK(cudaMemsetAsync(st->bar, 0, 256, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    if (!c->step_trace.empty()) {
+        TRY(c->dalloc(&p, 8 * (8 * ph.size() + 1)));
+        st->allocs.push_back(p);
+        st->trace = (unsigned long long *)p;
+        CK(cudaMemset(st->trace, 0, 8 * (8 * ph.size() + 1)));
+        st->phase_host = ph;
+        st->trace_path = c->step_trace;
+    }
+    st->nphases = (int)ph.size();
+    st->step_slots = slots;
+    st->step_ctas = c->sms;
+    st->step_slot_bytes = slot_bytes;
+    st->step_act_bytes = (int)act;
+    st->step_smem = (size_t)slots * slot_bytes + act + escr;
+    return MGB_OK;
+}
+
+template <int NC, int NW>
+static cudaError_t step_launch(mgb_ctx *c, const StepArgs &a, size_t smem) {
+    auto kern = step_kernel<NC, NW>;
+    cudaError_t e = allow_smem(kern, smem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(c->sms);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = c->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: the grid barriers need it
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+// The decoder layers of a greedy step as one persistent launch (stepkernel.cuh).
+static mgb_status launch_step_persistent(mgb_ctx *c, StaticState *st) {
+    TRY(build_step(c, st));
+    const Config &g = c->cfg;
+    StepArgs a{};
+    a.ph = st->phases;
+    a.nph = st->nphases;
+    a.rows = st->b;
+    a.H = g.dec_heads;
+    a.hd = g.d / g.dec_heads;
+    a.m = st->m;
+    a.max_keys = std::max(st->m, st->s);
+    a.kv_f32 = 0;
+    a.lens = st->lens;
+    a.embed = c->embed;
+    a.ids = st->ids;
+    a.step = st->step;
+    a.pos_table = c->pos;
+    a.pos_base = (uint32_t)g.pad + 1;
+    a.scale = c->embed_scale;
+    a.x = st->x;
+    a.q = st->q;
+    a.bar = st->bar;
+    a.abort_flag = st->bar + 32;
+    a.err = c->d_err;
+    a.wait_ns = c->test_wait_ns;
+    a.withhold = c->test_withhold_step;
+    a.trace = st->trace;
+    a.slots = st->step_slots;
+    a.slot_bytes = st->step_slot_bytes;
+    a.act_bytes = st->step_act_bytes;
+    CK(cudaMemsetAsync(st->bar, 0, 256, c->stream));
+    cudaError_t e;
+    switch (st->b <= 1 ? 1 : st->b <= 2 ? 2 : st->b <= 4 ? 4 : 8) {
+        case 1: e = step_launch<1, 4>(c, a, st->step_smem); break;
+        case 2: e = step_launch<2, 4>(c, a, st->step_smem); break;
+        case 4: e = step_launch<4, 4>(c, a, st->step_smem); break;
+        default: e = step_launch<8, 2>(c, a, st->step_smem); break;
+    }
+    ++c->launches;
+    return e == cudaSuccess ? MGB_OK : cuda_err(e, "persistent step launch");
+}
+
 // How a decoder step runs: the K/V element type and the rows of the
 // reference's matmul calls (candle picks MMVQ or MMQ, and MMVQ's warp count,
 // from them).
@@ -1145,6 +1350,8 @@ static mgb_status launch_step(mgb_ctx *c, StaticState *st, float *logits, int fo
                               const StepMode &mode = StepMode{}) {
     const Config &g = c->cfg;
     const int b = st->b, d = g.d, H = g.dec_heads, hd = d / H;
+    // the decoder layers of a small greedy batch: one persistent launch
+    const bool persistent = !mode.kv32 && !mode.cls && !mode.lm_cls && step_kernel_ok(c, b);
     const int cls = mode.cls ? mode.cls : b, lm_cls = mode.lm_cls ? mode.lm_cls : b;
     const bool tc = cls > kSmallRows && tc_ok(c->dec[0].qkv);
     const SplitBufs *sp = tc && c->tc_split && st->split.part ? &st->split : nullptr;
@@ -1153,7 +1360,8 @@ static mgb_status launch_step(mgb_ctx *c, StaticState *st, float *logits, int fo
     // attention whose outputs also go, as q8_1, into the next matmul's input
     const bool attn_q = tc && hd % 32 == 0;
     auto attn = [&](const AttnArgs &a) { return kv32 ? attend<float>(c, a) : attend<__half>(c, a); };
-    for (int l = 0; l < g.dec_layers; ++l) {
+    if (persistent) TRY(launch_step_persistent(c, st));
+    for (int l = 0; l < g.dec_layers && !persistent; ++l) {
         const DecLayer &L = c->dec[l];
         // attn_norm(x) (layer 0: x = E[id]*scale + pos) -> fused QKV -> q, K/V cache slot *step
         GemvArgs gq = mm_out(L.qkv, b);
@@ -1816,8 +2024,11 @@ mgb_status mgb_open(const char *path, int device, const mgb_options *opts, mgb_c
     if (const char *v = getenv("MGB_TC_SPLIT")) c->tc_split = atoi(v) != 0;
     if (const char *v = getenv("MGB_TC_SPLIT_STAGES")) c->tc_split_stages = std::max(1, atoi(v));
     if (const char *v = getenv("MGB_TC_SPLIT_MAX")) c->tc_split_max = std::max(1, atoi(v));
+    if (const char *v = getenv("MGB_STEP_KERNEL")) c->step_kernel = atoi(v) != 0;
+    if (const char *v = getenv("MGB_STEP_TRACE")) c->step_trace = v;
     if (const char *v = getenv("MGB_TEST_WAIT_NS")) c->test_wait_ns = std::max<uint64_t>(1000, strtoull(v, nullptr, 10));
     if (const char *v = getenv("MGB_TEST_WITHHOLD_CHUNK")) c->test_withhold_chunk = atoi(v);
+    if (const char *v = getenv("MGB_TEST_WITHHOLD_STEP")) c->test_withhold_step = atoi(v);
     cudaDeviceGetAttribute(&c->sms, cudaDevAttrMultiProcessorCount, device);
     if (c->sms <= 0) c->sms = 148;
     {

@@ -122,7 +122,7 @@ __device__ __forceinline__ void epilogue_store(const GemvArgs &g, int row, int n
         g.y[(size_t)n * W.N + row] = y > 0.0f ? y : 0.0f;
     } else if constexpr (EPI == EPI_RESID) {
         float *xr = g.y + (size_t)n * W.N + row;
-        *xr = __fadd_rn(__fadd_rn(v, b), *xr);
+        *xr = __fadd_rn(__fadd_rn(v, b), __ldcg(xr));
     } else if constexpr (EPI == EPI_QKV) {
         const float y = __fadd_rn(v, b);
         const int dm = g.H * g.hd;

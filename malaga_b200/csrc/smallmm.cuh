@@ -302,17 +302,36 @@ __device__ __forceinline__ void mm_f32(const StageRows &S, int lr0, const SmAct 
 // LayerNorm statistics (warp per row: lane-ordered sums, SUM32 tree), then
 // (row, block) tasks over the warps: normalise and quantize to q8_1.
 
+// (activation rows are read through L2 only: inside the persistent step kernel
+// other CTAs wrote them earlier in the same launch)
 template <int MODE>
 __device__ __forceinline__ float small_input(const PrepArgs &p, const float *pos, int n, int i) {  // n: global row
     if constexpr (MODE == PREP_EMBED_LN)
-        return __fadd_rn(__fmul_rn(deq_elem(p.embed, (int)p.ids[n], i), p.scale), pos[i]);
+        return __fadd_rn(__fmul_rn(deq_elem(p.embed, (int)__ldcg(p.ids + n), i), p.scale), pos[i]);
     else
-        return p.x[(size_t)n * p.K + i];
+        return __ldcg(p.x + (size_t)n * p.K + i);
 }
 
-template <int MODE, bool F32W>
-__device__ void small_prologue(const PrepArgs &p, int n0, const SmAct &s, int NC, uint8_t *lnbuf, bool write_x) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+// A CTA-wide barrier over the first `n` threads: __syncthreads when id is 0,
+// else named barrier `id` (the persistent step kernel's compute warps, whose
+// producer warp does not take part).
+struct CtaSync {
+    int id, n;
+    __device__ __forceinline__ void operator()() const {
+        if (id == 0) __syncthreads();
+        else asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+    }
+};
+
+struct NoMark {
+    __device__ void operator()(int) const {}
+};
+
+// `mark(k)` is called after each of its three stages (timing probes).
+template <int MODE, bool F32W, typename Mark = NoMark>
+__device__ void small_prologue(const PrepArgs &p, int n0, const SmAct &s, int NC, uint8_t *lnbuf, bool write_x,
+                               int nthr, CtaSync sync, Mark &&mark = Mark{}) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = nthr >> 5;
     const int K = p.K, T = K >> 5, rows = min(NC, p.rows - n0);
     const float *pos = nullptr;
     float *xs = nullptr, *gb = nullptr, *st = nullptr;
@@ -321,35 +340,42 @@ __device__ void small_prologue(const PrepArgs &p, int n0, const SmAct &s, int NC
         gb = xs + (size_t)NC * K;                  // gamma[K], beta[K]
         st = gb + 2 * K;                           // [NC] mean, rstd
         if constexpr (MODE == PREP_EMBED_LN) pos = p.pos_table + (size_t)(*p.step + p.pos_base) * K;
-        for (int i = threadIdx.x; i < K; i += blockDim.x) {
-            gb[i] = __ldg(p.gamma + i);
-            gb[K + i] = __ldg(p.beta + i);
-        }
-        // the rows' inputs into shared memory by every thread, 8 loads in flight
-        // each (one memory round trip), then the statistics from there
-        for (int base = threadIdx.x; base < rows * K; base += 8 * blockDim.x) {
-            float v[8];
+        // the rows' inputs, then gamma and beta, into shared memory (xs and gb
+        // are one array): 16 loads in flight per thread before their stores
+        const int nin = rows * K, nall = nin + 2 * K;
+        for (int base = threadIdx.x; base < nall; base += 16 * nthr) {
+            float v[16];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const int idx = base + u * blockDim.x;
-                v[u] = idx < rows * K ? small_input<MODE>(p, pos, n0 + idx / K, idx % K) : 0.0f;
+            for (int u = 0; u < 16; ++u) {
+                const int idx = base + u * nthr;
+                v[u] = idx < nin    ? small_input<MODE>(p, pos, n0 + idx / K, idx % K)
+                       : idx < nin + K ? __ldg(p.gamma + (idx - nin))
+                       : idx < nall    ? __ldg(p.beta + (idx - nin - K))
+                                       : 0.0f;
             }
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const int idx = base + u * blockDim.x;
-                if (idx >= rows * K) break;
-                xs[idx] = v[u];
-                if constexpr (MODE == PREP_EMBED_LN)
-                    if (write_x) p.x_out[(size_t)n0 * K + idx] = v[u];
+            for (int u = 0; u < 16; ++u) {
+                const int idx = base + u * nthr;
+                if (idx >= nall) break;
+                if (idx < nin) {
+                    xs[idx] = v[u];
+                    if constexpr (MODE == PREP_EMBED_LN)
+                        if (write_x) p.x_out[(size_t)n0 * K + idx] = v[u];
+                } else {
+                    gb[idx - nin] = v[u];
+                }
             }
         }
-        __syncthreads();
+        sync();
+        mark(1);
         for (int n = warp; n < rows; n += nw) {
             const float *xr = xs + (size_t)n * K;
             float sum = 0.0f;
+#pragma unroll 8
             for (int t = 0; t < T; ++t) sum = t == 0 ? xr[lane] : __fadd_rn(sum, xr[32 * t + lane]);
             const float mean = __fdiv_rn(warp_tree(sum), (float)K);
             float s2 = 0.0f;
+#pragma unroll 8
             for (int t = 0; t < T; ++t) {
                 const float c = __fsub_rn(xr[32 * t + lane], mean);
                 const float c2 = __fmul_rn(c, c);
@@ -361,7 +387,8 @@ __device__ void small_prologue(const PrepArgs &p, int n0, const SmAct &s, int NC
                 st[2 * n + 1] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
             }
         }
-        __syncthreads();
+        sync();
+        mark(2);
     }
     // (row, block) tasks; loads of 8 tasks in flight per warp
     constexpr int PIPE = 8;
@@ -373,7 +400,7 @@ __device__ void small_prologue(const PrepArgs &p, int n0, const SmAct &s, int NC
             const int task = base + u * nw, n = task / T, i = 32 * (task % T) + lane;
             y[u] = 0.0f;
             if (task < tasks && n < rows) {
-                if constexpr (MODE == PREP_PLAIN) y[u] = p.x[(size_t)(n0 + n) * K + i];
+                if constexpr (MODE == PREP_PLAIN) y[u] = __ldcg(p.x + (size_t)(n0 + n) * K + i);
                 else y[u] = xs[(size_t)n * K + i];
             }
         }
@@ -396,7 +423,8 @@ __device__ void small_prologue(const PrepArgs &p, int n0, const SmAct &s, int NC
             }
         }
     }
-    __syncthreads();
+    sync();
+    mark(3);
 }
 
 // ---------------------------------------------------------------------------
@@ -452,7 +480,7 @@ __global__ void __launch_bounds__(256) small_mm_kernel(const __grid_constant__ S
     s.d = reinterpret_cast<float *>(act + (size_t)NC * K);
     s.xf = reinterpret_cast<float *>(act + (size_t)NC * K + (size_t)NC * (K / 32) * 4);
     uint8_t *lnbuf = reinterpret_cast<uint8_t *>(s.xf) + (TYPE == T_F32 ? (size_t)NC * K * 4 : 0);
-    small_prologue<MODE, TYPE == T_F32>(A.p, n0, s, NC, lnbuf, blockIdx.x == 0);
+    small_prologue<MODE, TYPE == T_F32>(A.p, n0, s, NC, lnbuf, blockIdx.x == 0, blockDim.x, CtaSync{0, 0});
 
     float bv = kNegInf;
     uint32_t bi = 0xffffffffu;

@@ -38,6 +38,11 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
                  : "memory");
 }
 
+// One arrival on an mbarrier (no transaction bytes).
+__device__ __forceinline__ void mbar_arrive_cta(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 // L2 prefetch of [p, p + bytes), rounded out to 16-byte bounds.
 __device__ __forceinline__ void prefetch_l2(const void *p, size_t bytes) {
     uint64_t lo = (uint64_t)p & ~15ull, hi = ((uint64_t)p + bytes + 15) & ~15ull;

@@ -234,6 +234,37 @@ def test_bounded_wait_that_runs_out_is_reported(gpu, model, monkeypatch):
     assert Translator(Engine(path)).generate(src, TINY_TGT, GenOptions(max_new_tokens=8)) == want
 
 
+@pytest.mark.parametrize("chunk", [0, 3])
+def test_bounded_wait_in_step_kernel_is_reported(gpu, model, monkeypatch, chunk):
+    """The persistent step kernel's failure path: the test hook withholds one
+    weight copy of CTA 0 (the first chunk, or one of a later phase) and shortens
+    every wait to 20 ms; the warps that wait for it give up and raise the abort
+    flag, the other CTAs leave at their next grid barrier, every CTA waits for its
+    own copies in flight, and the call fails with MGB_ERR_CUDA instead of hanging.
+    A context opened afterwards decodes correctly."""
+    from malaga_b200 import _lib
+
+    path = model("mid", "q8_0")
+    V = models.config_of("mid").vocab_size
+    src = mid_sentences(V, n=1, seed=21)
+    monkeypatch.setenv("MGB_STEP_KERNEL", "1")
+    monkeypatch.setenv("MGB_TEST_WAIT_NS", "20000000")
+    monkeypatch.setenv("MGB_TEST_WITHHOLD_STEP", str(chunk))
+    eng = Engine(path)
+    batch = eng.encode(src)
+    with pytest.raises(MgbError) as e:
+        eng.greedy_logits(batch, V - 2, 2, force=True)
+    assert e.value.code == _lib.MGB_ERR_CUDA
+    assert "ran out of time" in str(e.value)
+    eng.close()
+    monkeypatch.delenv("MGB_TEST_WAIT_NS")
+    monkeypatch.delenv("MGB_TEST_WITHHOLD_STEP")
+    want_ids, _ = oracle.Oracle(path).greedy(src, V - 2, 4, force=True, logits=True)
+    eng = Engine(path)
+    got, _ = eng.greedy(eng.encode(src), V - 2, 4, force=True)
+    np.testing.assert_array_equal(got, want_ids)
+
+
 @pytest.mark.parametrize("name,preset,b", [("mid", "q4_k_m", 64), ("mid", "q8_0", 24), ("wide", "q8_0", 64),
                                            ("wide", "q4_k_m", 40)])
 def test_tensor_core_batches_bit_exact(gpu, model, name, preset, b):
@@ -298,12 +329,16 @@ def test_beam_one_equals_greedy_on_device(gpu, model):
     assert [[int(x) for x in out[i, : lens[i]]] for i in range(len(src))] == greedy
 
 
+@pytest.mark.parametrize("step_kernel", ["1", "0"])
 @pytest.mark.parametrize("preset", ["q4_k_m", "q8_0"])
 @pytest.mark.parametrize("n", [1, 2, 3, 5, 8])
-def test_small_batches_bit_exact(gpu, model, preset, n):
-    """1-8 rows run the small-batch kernel with the reference's MMVQ arithmetic:
-    the padded batch (1, 2, 4 or 8 rows) picks candle's warp count (4 warps up to
-    4 rows, 2 for 5-8); tokens and logits equal the oracle's bit for bit."""
+def test_small_batches_bit_exact(gpu, model, preset, n, step_kernel, monkeypatch):
+    """1-8 rows run the reference's MMVQ arithmetic: the padded batch (1, 2, 4 or
+    8 rows) picks candle's warp count (4 warps up to 4 rows, 2 for 5-8). Greedy
+    steps run as the persistent step kernel (step_kernel 1) or one launch per
+    operation (0); graph replay included; tokens and logits equal the oracle's
+    bit for bit."""
+    monkeypatch.setenv("MGB_STEP_KERNEL", step_kernel)
     path = model("mid", preset)
     V = models.config_of("mid").vocab_size
     src = mid_sentences(V, n=n, seed=21)
@@ -313,3 +348,5 @@ def test_small_batches_bit_exact(gpu, model, preset, n):
     np.testing.assert_array_equal(got_ids, want_ids)
     assert np.array_equal(got_logits.view(np.uint32), want_logits.view(np.uint32)), \
         f"max |diff| {np.abs(got_logits - want_logits).max()}"
+    out, _ = eng.greedy(eng.encode(src), V - 2, 6, force=True)  # CUDA-graph replay
+    np.testing.assert_array_equal(out, want_ids)
