@@ -301,7 +301,7 @@ struct mgb_ctx {
     // Matmuls with too few tiles for the SMs split their K stages (MGB_TC_SPLIT overrides).
     int tc_split = 1;
     int tc_split_stages = 4;  // fewest stages per split (MGB_TC_SPLIT_STAGES)
-    int tc_split_max = 4;     // most splits of a tile (MGB_TC_SPLIT_MAX)
+    int tc_split_max = 2;     // most splits of a tile (MGB_TC_SPLIT_MAX; 2 measured fastest at batch 64)
     // The decoder layers of greedy steps of at most 8 rows run as one persistent
     // kernel (1) or as one launch per operation (0, the default: measured faster
     // on B200); MGB_STEP_KERNEL overrides.

@@ -587,11 +587,16 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
             }
             // add one unit to the running sum (split 0) or store it (later splits):
             // Q8_0 / Q6_K units are fused multiply-adds fma(x, y, acc), Q4_K values
-            auto unit = [&](int n, int u, float x, float y) {
-                if (s0 == 0) {
-                    acc[n] = G::Q4 ? __fadd_rn(acc[n], x) : __fmaf_rn(x, y, acc[n]);
+            // (two tokens n, n + 1 at a time, as packed f32 pairs; ARGMAX launches never split)
+            auto unit2 = [&](int n, int u, float2 x, float2 y) {
+                if (EPI == EPI_ARGMAX || s0 == 0) {
+                    float2 a = make_float2(acc[n], acc[n + 1]);
+                    a = G::Q4 ? add2(a, x) : fma2(x, y, a);
+                    acc[n] = a.x;
+                    acc[n + 1] = a.y;
                 } else {
-                    kp[((size_t)u * NT + n0 + n) * 128 + r] = make_float2(x, y);
+                    kp[((size_t)u * NT + n0 + n) * 128 + r] = make_float2(x.x, y.x);
+                    kp[((size_t)u * NT + n0 + n + 1) * 128 + r] = make_float2(x.y, y.y);
                 }
             };
             for (int s = s0; s < s0 + NSS && ok; ++s, st.next(RS)) {
@@ -680,24 +685,37 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
                             if constexpr (!G::Q8) ld(ta + COLS + c * CH, va1);
                             if constexpr (G::Q6) ld(ta + COLS + G::MN + c * CH, vb1);
                             tmem_wait_ld();
+                            const float2 z2 = make_float2(0.0f, 0.0f);
 #pragma unroll
-                            for (int i = 0; i < CH; ++i) {
+                            for (int i = 0; i < CH; i += 2) {
                                 const int n = c * CH + i;
-                                const float2 x0 = rec[b * NT + n0 + n];
+                                // both tokens' {d, s} records of a block in one 16-byte load
+                                const float4 x0 = *reinterpret_cast<const float4 *>(rec + b * NT + n0 + n);
                                 if constexpr (G::Q8) {
-                                    unit(n, u, __fmul_rn(db, x0.x), (float)va0[i]);
+                                    unit2(n, u, mul2(make_float2(db, db), make_float2(x0.x, x0.z)),
+                                          make_float2((float)va0[i], (float)va0[i + 1]));
                                 } else {
-                                    const float2 x1 = rec[(b + 1) * NT + n0 + n];
+                                    const float4 x1 = *reinterpret_cast<const float4 *>(rec + (b + 1) * NT + n0 + n);
                                     if constexpr (G::Q4) {
-                                        const float sd = __fmaf_rn(x1.x, (float)(sa1 * va1[i]),
-                                                                   __fmaf_rn(x0.x, (float)(sa0 * va0[i]), 0.0f));
-                                        const float sm = __fmaf_rn(x1.y, mf1, __fmaf_rn(x0.y, mf0, 0.0f));
-                                        unit(n, u, __fmaf_rn(d, sd, -__fmul_rn(dm, sm)), 0.0f);
+                                        const float2 sd =
+                                            fma2(make_float2(x1.x, x1.z),
+                                                 make_float2((float)(sa1 * va1[i]), (float)(sa1 * va1[i + 1])),
+                                                 fma2(make_float2(x0.x, x0.z),
+                                                      make_float2((float)(sa0 * va0[i]), (float)(sa0 * va0[i + 1])), z2));
+                                        const float2 sm = fma2(make_float2(x1.y, x1.w), make_float2(mf1, mf1),
+                                                               fma2(make_float2(x0.y, x0.w), make_float2(mf0, mf0), z2));
+                                        const float2 t = mul2(make_float2(dm, dm), sm);  // fma(d, sd, -(dmin * sm))
+                                        unit2(n, u, fma2(make_float2(d, d), sd, make_float2(-t.x, -t.y)), z2);
                                     } else {
-                                        const float sf =
-                                            __fmaf_rn(x1.x, (float)(sa1 * va1[i] + sb1 * vb1[i]),
-                                                      __fmaf_rn(x0.x, (float)(sa0 * va0[i] + sb0 * vb0[i]), 0.0f));
-                                        unit(n, u, d, sf);
+                                        const float2 sf = fma2(
+                                            make_float2(x1.x, x1.z),
+                                            make_float2((float)(sa1 * va1[i] + sb1 * vb1[i]),
+                                                        (float)(sa1 * va1[i + 1] + sb1 * vb1[i + 1])),
+                                            fma2(make_float2(x0.x, x0.z),
+                                                 make_float2((float)(sa0 * va0[i] + sb0 * vb0[i]),
+                                                             (float)(sa0 * va0[i + 1] + sb0 * vb0[i + 1])),
+                                                 z2));
+                                        unit2(n, u, make_float2(d, d), sf);
                                     }
                                 }
                             }

@@ -118,6 +118,38 @@ __device__ __forceinline__ int q81_block(float x, float &d, float &s) {
     return amax == 0.0f ? 0 : (int)roundf(__fdiv_rn(x, dd));
 }
 
+// Packed pairs of f32 operations (sm_100 f32x2): each element is rounded
+// exactly as the scalar __fmaf_rn / __fmul_rn would round it.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 pa, pb, pc, pd;\n\t"
+        "mov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\tmov.b64 pc, {%6, %7};\n\t"
+        "fma.rn.f32x2 pd, pa, pb, pc;\n\tmov.b64 {%0, %1}, pd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 pa, pb, pd;\n\t"
+        "mov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\t"
+        "mul.rn.f32x2 pd, pa, pb;\n\tmov.b64 {%0, %1}, pd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 pa, pb, pd;\n\t"
+        "mov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\t"
+        "add.rn.f32x2 pd, pa, pb;\n\tmov.b64 {%0, %1}, pd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
 // Integer sum across the warp, one reduction instruction.
 __device__ __forceinline__ int warp_isum_redux(int v) { return __reduce_add_sync(0xffffffffu, v); }
 

@@ -240,11 +240,10 @@ __device__ void attend_warp(const StepPhase &P, int H, int n, int h, int keys, f
 
 // Thread 0's weight feed: this CTA's chunks of every matmul phase, in phase
 // order, into the ring of shared-memory slots (chunk k in slot k % slots).
-// fill() issues while the next chunk's slot is free and never waits, so thread
-// 0 calls it wherever it passes (after its rows of a chunk, before an attention
-// phase, while it polls a grid barrier); ensure(k) issues up to chunk k and may
-// wait (bounded) for a slot, which only needs warps to finish chunks that were
-// issued already.
+// fill() issues while the next chunk's slot is free and never waits: thread 0
+// calls it while it polls a grid barrier (not inside a phase, where it would
+// hold up its warp); ensure(k) issues up to chunk k and may wait (bounded) for
+// a slot, which only needs warps to finish chunks that were issued already.
 struct Feed {
     int pi, c0, r1, n;  // next chunk: rows [c0, ...) of phase pi; chunks issued
 
@@ -377,7 +376,6 @@ __global__ void __launch_bounds__(256, 1) step_kernel(const __grid_constant__ St
             for (int k = 1; k < 5; ++k) m[k] = m[0];
         }
         if (P.kind == PH_ATTN) {
-            if (tid == 0) refill();
             if (A.hd == 64) attend_phase<64>(A, P, step, lens_sh, e, qsh[warp], lane, gwarp, nwarps);
             else attend_phase<128>(A, P, step, lens_sh, e, qsh[warp], lane, gwarp, nwarps);
         } else {
@@ -497,7 +495,6 @@ __global__ void __launch_bounds__(256, 1) step_kernel(const __grid_constant__ St
                 else rows_out(std::integral_constant<int, 1>{});
                 __syncwarp();
                 if (lane == 0) mbar_arrive_cta(&empty[slot]);  // this warp is done with the slot
-                if (tid == 0) refill();
             }
         }
         target += gridDim.x;
