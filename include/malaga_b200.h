@@ -94,7 +94,10 @@ MGB_API mgb_status mgb_model_info_get(const mgb_ctx *ctx, mgb_model_info *out);
 MGB_API mgb_status mgb_encode(mgb_ctx *ctx, const uint32_t *ids, const uint32_t *lens, uint32_t b, uint32_t s_stride,
                       mgb_batch **out);
 
-/* Frees an encoded batch. */
+/* Frees an encoded batch. Its device buffer goes back to the context's pool,
+ * reused by the next mgb_encode (at most 4 GiB kept; mgb_clear_cache and
+ * mgb_close release them). A batch freed after its context was closed releases
+ * its buffer itself. */
 MGB_API void mgb_batch_free(mgb_batch *batch);
 
 /* Copies cross-attention K (which=0) or V (which=1) of decoder layer `layer`,

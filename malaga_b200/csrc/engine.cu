@@ -25,6 +25,7 @@
 #include <mutex>
 #include <set>
 #include <string>
+#include <unordered_set>
 #include <vector>
 
 #include "../../include/malaga_b200.h"
@@ -267,8 +268,20 @@ struct mgb_batch {
     uint32_t *d_lens = nullptr;
     float *cross = nullptr;  // f32 [L][2][b][H][s][hd], as encode_cross returns it (model.rs:463-477)
     size_t cross_bytes = 0;
+    void *buf = nullptr;     // one device buffer: cross, then d_lens (from the context's batch pool)
+    size_t buf_bytes = 0;
     mgb_ctx *owner = nullptr;
 };
+
+// Device buffers of freed batches, kept for the next encode: cudaFree of a few
+// hundred MB takes tens of milliseconds and waits for the device, so a stream
+// of batches (encode, decode, free, ...) reuses them instead. At most
+// kBatchPoolBytes are kept; mgb_clear_cache and mgb_close release them.
+struct PoolBuf {
+    void *p;
+    size_t bytes;
+};
+static constexpr size_t kBatchPoolBytes = 4ull << 30;
 
 static constexpr int kLmParts = 148 * 8;  // most CTAs of a fused LM-head argmax launch (partials per row)
 // Matmuls of at most this many activation rows run the reference's MMVQ
@@ -295,6 +308,9 @@ struct mgb_ctx {
     bool capture = true;
     uint64_t clock = 0;
     std::vector<std::unique_ptr<StaticState>> cache;
+    std::vector<PoolBuf> batch_pool;  // freed batches' buffers
+    size_t batch_pool_bytes = 0;
+    std::unordered_set<mgb_batch *> batches;  // live batches (detached by mgb_close)
     size_t weight_bytes = 0, step_bytes = 0;
     uint32_t *d_err = nullptr;  // device-side error flags (a bounded wait ran out)
     int tc_min_nt = 8;  // narrowest token tile of the tensor-core matmul (MGB_TC_MIN_NT)
@@ -1451,6 +1467,40 @@ static mgb_status launch_step(mgb_ctx *c, StaticState *st, float *logits, int fo
 // ---------------------------------------------------------------------------
 // Encoder (model.rs:463-500)
 
+// A batch's device buffer of at least `bytes`: the smallest pooled buffer that
+// fits, else a new allocation.
+static mgb_status batch_buf(mgb_ctx *c, size_t bytes, mgb_batch *B) {
+    int best = -1;
+    for (size_t i = 0; i < c->batch_pool.size(); ++i)
+        if (c->batch_pool[i].bytes >= bytes && (best < 0 || c->batch_pool[i].bytes < c->batch_pool[best].bytes))
+            best = (int)i;
+    if (best >= 0) {
+        B->buf = c->batch_pool[best].p;
+        B->buf_bytes = c->batch_pool[best].bytes;
+        c->batch_pool_bytes -= B->buf_bytes;
+        c->batch_pool.erase(c->batch_pool.begin() + best);
+        return MGB_OK;
+    }
+    TRY(c->dalloc(&B->buf, bytes));
+    B->buf_bytes = bytes;
+    return MGB_OK;
+}
+
+// Back to the pool (work queued on the context's stream that still reads the
+// buffer runs before any later use of it, which is queued on the same stream).
+static void batch_release(mgb_ctx *c, mgb_batch *B) {
+    if (!B->buf) return;
+    if (c->batch_pool_bytes + B->buf_bytes <= kBatchPoolBytes) {
+        c->batch_pool.push_back({B->buf, B->buf_bytes});
+        c->batch_pool_bytes += B->buf_bytes;
+    } else {
+        cudaFree(B->buf);
+    }
+    B->buf = nullptr;
+    B->cross = nullptr;
+    B->d_lens = nullptr;
+}
+
 // ids: [b][S] right-padded, S = the longest sentence (pad_batch, model.rs:480-500;
 // the matmuls then see b*S rows, as the reference's).
 static mgb_status encode(mgb_ctx *c, const uint32_t *ids, const uint32_t *lens, int b, int S, mgb_batch **out) {
@@ -1537,14 +1587,10 @@ static mgb_status encode(mgb_ctx *c, const uint32_t *ids, const uint32_t *lens, 
     const int Hd = g.dec_heads, hdd = d / Hd;
     const size_t per = (size_t)b * Hd * S * hdd;
     B->cross_bytes = per * 4 * 2 * g.dec_layers;
-    TRY(c->dalloc((void **)&B->cross, B->cross_bytes));
-    void *dl = nullptr;
-    mgb_status s = c->dalloc(&dl, (size_t)4 * b);
-    if (s != MGB_OK) {
-        cudaFree(B->cross);
-        return s;
-    }
-    B->d_lens = (uint32_t *)dl;
+    TRY(batch_buf(c, (B->cross_bytes + 255) / 256 * 256 + (size_t)4 * b, B.get()));
+    B->cross = (float *)B->buf;
+    B->d_lens = (uint32_t *)((uint8_t *)B->buf + (B->cross_bytes + 255) / 256 * 256);
+    mgb_status s = MGB_OK;
     CK(cudaMemcpyAsync(B->d_lens, lens, (size_t)4 * b, cudaMemcpyHostToDevice, c->stream));
     // enc_norm(x) is the input of every decoder layer's cross K/V projection
     // (model.rs:471-475); its q8_1 activations are prepared once
@@ -1567,8 +1613,7 @@ static mgb_status encode(mgb_ctx *c, const uint32_t *ids, const uint32_t *lens, 
                                        : small_mm<EPI_CROSSKV, PREP_LN>(c, gk, pn);
     }
     if (s != MGB_OK) {
-        cudaFree(B->cross);
-        cudaFree(B->d_lens);
+        batch_release(c, B.get());
         return s;
     }
     uint32_t derr = 0;
@@ -1576,10 +1621,10 @@ static mgb_status encode(mgb_ctx *c, const uint32_t *ids, const uint32_t *lens, 
     CK(cudaStreamSynchronize(c->stream));
     if (derr) {
         cudaMemsetAsync(c->d_err, 0, 4, c->stream);
-        cudaFree(B->cross);
-        cudaFree(B->d_lens);
+        batch_release(c, B.get());
         return set_err(MGB_ERR_CUDA, "a device-side wait ran out of time in the encoder (flags %u)", derr);
     }
+    c->batches.insert(B.get());
     *out = B.release();
     return MGB_OK;
 }
@@ -1612,6 +1657,9 @@ static void clear_cache(mgb_ctx *c) {
     if (c->enc_ws) cudaFree(c->enc_ws);
     c->enc_ws = nullptr;
     c->enc_ws_bytes = 0;
+    for (const PoolBuf &e : c->batch_pool) cudaFree(e.p);
+    c->batch_pool.clear();
+    c->batch_pool_bytes = 0;
     cudaDeviceGraphMemTrim(c->device);
 }
 
@@ -2061,6 +2109,7 @@ mgb_status mgb_open(const char *path, int device, const mgb_options *opts, mgb_c
 void mgb_close(mgb_ctx *c) {
     if (!c) return;
     cudaSetDevice(c->device);
+    for (mgb_batch *B : c->batches) B->owner = nullptr;  // they free their own buffers later
     clear_cache(c);
     if (c->arena) cudaFree(c->arena);
     if (c->d_err) cudaFree(c->d_err);
@@ -2116,9 +2165,13 @@ mgb_status mgb_encode(mgb_ctx *c, const uint32_t *ids, const uint32_t *lens, uin
 
 void mgb_batch_free(mgb_batch *B) {
     if (!B) return;
-    if (B->owner) cudaSetDevice(B->owner->device);
-    cudaFree(B->cross);
-    cudaFree(B->d_lens);
+    if (B->owner) {
+        cudaSetDevice(B->owner->device);
+        B->owner->batches.erase(B);
+        batch_release(B->owner, B);
+    } else {  // its context was closed first
+        cudaFree(B->buf);
+    }
     delete B;
 }
 

@@ -52,7 +52,11 @@ class Batch:
 
     def free(self):
         if self.h:
-            _lib.load().mgb_batch_free(self.h)
+            try:
+                L = _lib.load()
+            except Exception:  # interpreter shutdown
+                return
+            L.mgb_batch_free(self.h)
             self.h = None
 
     def __del__(self):
@@ -80,7 +84,11 @@ class Engine:
 
     def close(self):
         if getattr(self, "h", None):
-            _lib.load().mgb_close(self.h)
+            try:
+                L = _lib.load()
+            except Exception:  # interpreter shutdown: the process releases the device
+                return
+            L.mgb_close(self.h)
             self.h = None
 
     def __del__(self):

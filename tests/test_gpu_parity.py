@@ -145,7 +145,7 @@ def test_injected_oom_is_reported_and_recovered(gpu, model):
     the context stays usable (graph.rs:214-222, translator.rs:150-158)."""
     path = model("tiny", "q8_0")
     src = tiny_sentences()
-    eng = Engine(path, fail_alloc_after=2)
+    eng = Engine(path, fail_alloc_after=1)  # the batch buffer (after the encoder workspace)
     with pytest.raises(MgbError) as e:
         eng.encode(src)
     assert e.value.is_oom
@@ -153,6 +153,25 @@ def test_injected_oom_is_reported_and_recovered(gpu, model):
     want = [oracle.strip_eos(r, 2) for r in oracle.Oracle(path).greedy(src, TINY_TGT, 10)]
     got = Translator(eng).generate(src, TINY_TGT, GenOptions(max_new_tokens=10))
     assert got == want
+
+
+def test_batch_buffers_are_pooled_and_outlive_close(gpu, model):
+    """Freed batches' device buffers are reused by later encodes (a larger one
+    for a smaller batch too) with unchanged results; a batch freed after its
+    context was closed releases its own buffer."""
+    path = model("tiny", "q8_0")
+    src = tiny_sentences()
+    orc = oracle.Oracle(path)
+    eng = Engine(path)
+    for batch in (src, src[:2], src, src[:1]):
+        want = [oracle.strip_eos(r, 2) for r in orc.greedy(batch, TINY_TGT, 8)]
+        b = eng.encode(batch)
+        out, lens = eng.greedy(b, TINY_TGT, 8)
+        b.free()
+        assert [[int(x) for x in out[i, : lens[i]]] for i in range(len(batch))] == want
+    b = eng.encode(src)
+    eng.close()
+    b.free()
 
 
 def test_invalid_arguments_fail_cleanly(gpu, model):
