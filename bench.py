@@ -247,8 +247,8 @@ def bench_b1(eng, torch, stream, info, hbm):
 
 def run_c5(args):
     """Config 5: server dynamic batching (malaga_b200/server.py) on NLLB-600M
-    q4_k_m over --gpus GPUs of one process (one worker thread and engine per
-    GPU): 4096 single-sentence requests arriving as a Poisson process at 2000
+    q4_k_m over --gpus GPUs of one process (--streams worker threads, each with
+    its own engine, per GPU): 4096 single-sentence requests arriving as a Poisson process at 2000
     requests/s, source lengths lognormal (median 24, 4-96), greedy decode with a
     budget of 1.5 x source length + 8. The stream runs once to capture every
     shape's CUDA graphs, then again timed: end-to-end latency per request (host
@@ -263,7 +263,7 @@ def run_c5(args):
     path = models.model_path(w.model, w.preset, w.seed)
     arrivals = models.poisson_arrivals(len(w.sources), 2000.0, 4)
     opts = GenOptions(max_batch=64, budget_scale=1.5, budget_extra=8)
-    backends = [TranslatorBackend(path, d, opts) for d in range(args.gpus)]
+    backends = [TranslatorBackend(path, d, opts) for d in range(args.gpus) for _ in range(max(1, args.streams))]
     srv = Server(backends, cost=lambda srcs: sum(backends[0].budget(len(s)) for s in srcs))
 
     def stream():
@@ -292,7 +292,8 @@ def run_c5(args):
             "offered_rps": 2000.0, "achieved_rps": len(lat) / span,
             "config": {"workload": "c5: NLLB-600M q4_k_m (random init, seed 0), 4096 Poisson requests at 2000/s, "
                                    "lognormal lengths (median 24, 4-96), greedy, budget 1.5*len+8, max_batch 64",
-                       "dispatch": "least outstanding decode tokens; per-GPU drain-and-group (server.rs:74-89)"}}
+                       "workers_per_gpu": max(1, args.streams),
+                       "dispatch": "least outstanding decode tokens; per-worker drain-and-group (server.rs:74-89)"}}
     print(json.dumps(line), flush=True)
 
 
@@ -305,6 +306,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-b1", action="store_true")
+    ap.add_argument("--streams", type=int, default=4,
+                    help="decode contexts (CUDA streams) per GPU for independent batches (dp.StreamPool)")
     args = ap.parse_args()
     if args.workload == "c5" and args.impl == "ours":
         return run_c5(args)
@@ -327,43 +330,53 @@ def main():
         dist.barrier()
     path = models.model_path(w.model, w.preset, w.seed)
 
-    from malaga_b200 import Engine
-
-    eng = Engine(path, device=local)
-    info = eng.info
-    stream = torch.cuda.ExternalStream(eng.stream, device=torch.device("cuda", local))
-    tgt, steps = models.TGT_TAG, w.steps
     # this rank's share: length-sorted batches of w.batch placed by LPT (a
     # single-batch workload is replicated on every rank instead)
     lens_all = [len(s) for s in w.sources]
     if w.name == "dp600":
-        share = dp.shard(lens_all, world, rank, w.batch, lambda b: steps)
+        share = dp.shard(lens_all, world, rank, w.batch, lambda b: w.steps)
         scaling = "strong"
     else:
         share = [list(range(len(w.sources)))]
         scaling = "weak"
     srcs = [[w.sources[i] for i in b] for b in share]
-    batches = [eng.encode(s) for s in srcs]
+    # independent batches decode on `streams` contexts of this GPU at once
+    # (dp.StreamPool); batch i belongs to context i % streams
+    streams = max(1, min(args.streams, len(srcs)))
+    pool = dp.StreamPool(path, device=local, streams=streams)
+    eng = pool.engines[0]
+    info = eng.info
+    cur = torch.cuda.current_stream()
+    estreams = [torch.cuda.ExternalStream(e.stream, device=torch.device("cuda", local)) for e in pool.engines]
+    stream = estreams[0]
+    tgt, steps = models.TGT_TAG, w.steps
+    batches = pool.map(lambda e, s: e.encode(s), srcs)
     outs = [np.empty((len(s), steps), np.uint32) for s in srcs]
     my_tokens = sum(len(s) for s in srcs) * steps
     total_tokens = (len(w.sources) if scaling == "strong" else world * len(w.sources)) * steps
 
     def decode_step():
-        for b, o in zip(batches, outs):
-            eng.greedy(b, tgt, steps, sync_every=4, force=True, out=o)
+        pool.map(lambda e, bo: e.greedy(bo[0], tgt, steps, sync_every=4, force=True, out=bo[1]),
+                 list(zip(batches, outs)))
 
     for _ in range(max(3, args.warmup)):
         decode_step()
 
     def timed(fn, k):
+        """Device time of k calls of fn: an event on this thread's stream before,
+        and after it one that waits for every context's stream."""
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
+        e0.record(cur)
         for _ in range(k):
             fn()
-        e1.record(stream)
+        for es in estreams:
+            ev = torch.cuda.Event()
+            ev.record(es)
+            cur.wait_event(ev)
+        e1.record(cur)
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1)
         if world > 1:
@@ -372,10 +385,10 @@ def main():
             ms = float(t.item())
         return ms
 
-    l0 = eng.kernel_launches
+    l0 = pool.kernel_launches
     with ClockSampler(local) as clk:
         ms = timed(decode_step, args.steps)
-    launches = eng.kernel_launches - l0
+    launches = pool.kernel_launches - l0
     ms_step = ms / args.steps
     value = total_tokens / (ms_step / 1e3)
 
@@ -387,11 +400,14 @@ def main():
             ids_host[i, : len(r)] = r
         hosts.append((ids_host, np.array([len(r) for r in s], np.uint32)))
 
+    def e2e_one(e, item):
+        (ih, lh), o = item
+        b = e.encode_array(ih, lh)
+        e.greedy(b, tgt, steps, sync_every=4, force=True, out=o)
+        b.free()
+
     def e2e_step():
-        for (ih, lh), o in zip(hosts, outs):
-            b = eng.encode_array(ih, lh)
-            eng.greedy(b, tgt, steps, sync_every=4, force=True, out=o)
-            b.free()
+        pool.map(e2e_one, list(zip(hosts, outs)))
 
     e2e_step()
     k_e2e = max(1, min(args.steps, 3))
@@ -422,7 +438,7 @@ def main():
                        "global_batch": w.batch, "sentences": len(w.sources) * (1 if scaling == "strong" else world),
                        "decode_steps": steps, "parallelism": f"dp{world}",
                        "step": "ms_per_step = one pass over the rank's batches (each a whole forced decode)",
-                       "batches_this_rank": len(srcs),
+                       "batches_this_rank": len(srcs), "streams_per_gpu": streams,
                        "l2": "weights (%.0f MB per decoder step) exceed the 126 MB L2" % (step_bytes / 1e6)},
             "gpu_launches": launches,
             "e2e": {"value": e2e_value, "unit": "tokens/s",
@@ -449,7 +465,7 @@ def main():
         print(json.dumps(line), flush=True)
     for b in batches:
         b.free()
-    eng.close()
+    pool.close()
     if world > 1:
         dist.destroy_process_group()
 

@@ -232,6 +232,7 @@ struct StaticState {
     uint8_t *finished = nullptr;
     float *x = nullptr, *q = nullptr, *a = nullptr, *u = nullptr, *xf = nullptr;
     QAct act;                        // q8_1 tensor-core activations of the next matmul
+    QAct act2;                       // the FFN hidden rows' (written by the FFN-up epilogue)
     SplitBufs split;                 // split-K partials and tile counters
     // persistent step kernel (batches of at most 8 rows): its phase table, grid
     // barrier / abort words and shared-memory geometry
@@ -814,7 +815,9 @@ static mgb_status qprep_row(mgb_ctx *c, PrepArgs p, const QAct &act) {
     auto kern = qprep_row_kernel<MODE>;
     const size_t sh = (size_t)p.K * 4 + (MODE != PREP_PLAIN ? (size_t)p.K * 8 : 0);  // row; gamma, beta
     cudaError_t e = allow_smem(kern, sh);
-    if (e == cudaSuccess) e = launch_pdl(kern, dim3(p.rows), dim3(256), sh, c->stream, p, act);
+    // a warp per 32-value block (up to 1024 threads): the blocks' q8_1 reductions run side by side
+    const int threads = std::min(1024, std::max(256, p.K));
+    if (e == cudaSuccess) e = launch_pdl(kern, dim3(p.rows), dim3(threads), sh, c->stream, p, act);
     ++c->launches;
     return e == cudaSuccess ? MGB_OK : cuda_err(e, "activation prep launch");
 }
@@ -1114,8 +1117,10 @@ static mgb_status new_state(mgb_ctx *c, int b, int s, int m, StaticState **out) 
     }
     TRY(A((void **)&st->part_v, (size_t)4 * b * kLmParts));
     TRY(A((void **)&st->part_i, (size_t)4 * b * kLmParts));
-    if (tc_ok(c->dec[0].qkv))  // (small batches too: beam prefills can take the MMQ path)
+    if (tc_ok(c->dec[0].qkv)) {  // (small batches too: beam prefills can take the MMQ path)
         TRY(alloc_tc_act(c, b, std::max(d, g.dec_ffn), st->act, st->allocs, &st->bytes));
+        TRY(alloc_tc_act(c, b, g.dec_ffn, st->act2, st->allocs, &st->bytes));
+    }
     if (b > kSmallRows && tc_ok(c->dec[0].qkv)) {
         // split-K: the largest (rows x units) of the step's matrices, rows padded to 64
         size_t pu = 0;
@@ -1444,10 +1449,15 @@ static mgb_status launch_step(mgb_ctx *c, StaticState *st, float *logits, int fo
         // ffn_norm -> up + ReLU -> down + residual
         GemvArgs gu = mm_out(L.up, b);
         gu.y = st->u;
-        TRY((matmul<EPI_RELU, PREP_LN>(c, gu, prep_src(st->x, &L.ffn_norm), X, nullptr, sp, cls)));
         GemvArgs gd = mm_out(L.down, b);
         gd.y = st->x;
-        TRY((matmul<EPI_RESID, PREP_PLAIN>(c, gd, prep_src(st->u, nullptr), X, nullptr, sp, cls)));
+        // tensor-core path: the up epilogue writes the down matmul's q8_1
+        // activations itself (into a second buffer: the up matmul reads X)
+        const bool hq = tc && tc_ok(L.up) && tc_ok(L.down) && L.up.N % 128 == 0 && st->act2.tq;
+        if (hq) gu.qo = st->act2;
+        TRY((matmul<EPI_RELU, PREP_LN>(c, gu, prep_src(st->x, &L.ffn_norm), X, nullptr, sp, cls)));
+        if (hq) TRY(gemm_tc<EPI_RESID>(c, L.down, st->act2, b, gd, nullptr, sp));
+        else TRY((matmul<EPI_RESID, PREP_PLAIN>(c, gd, prep_src(st->u, nullptr), X, nullptr, sp, cls)));
     }
     if (!mode.lm) return MGB_OK;
     // dec_norm -> tied LM head fused with the first argmax pass -> greedy bookkeeping

@@ -792,6 +792,16 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
                     const int tok = tt * NT + n0 + lane / LPT;  // < 64 in an ARGMAX launch
                     if (tok < A.rows) argmax_merge(best_v[q][tok], best_i[q][tok], acc[0], bi[0]);
                 }
+            } else if (EPI == EPI_RELU && A.g.qo.tq) {
+                // the warp's 32 rows are one q8_1 block of the next matmul's
+                // activation row (every row live: the host requires N % 128 == 0)
+#pragma unroll
+                for (int n = 0; n < NH; ++n) {
+                    const int tok = tt * NT + n0 + n;
+                    if (tok >= A.rows) break;  // uniform across the warp
+                    const float y = __fadd_rn(acc[n], bias);
+                    store_block_tc(A.g.qo, tok, row >> 5, y > 0.0f ? y : 0.0f, lane);
+                }
             } else {
 #pragma unroll
                 for (int n = 0; n < NH; ++n) {
@@ -845,7 +855,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
 //         (the UMMA K-major no-swizzle layout);
 //   trec: per block j and row, float2 {d, s}.
 template <int MODE>
-__global__ void __launch_bounds__(256) qprep_row_kernel(PrepArgs p, QAct out) {
+__global__ void __launch_bounds__(1024) qprep_row_kernel(PrepArgs p, QAct out) {
     extern __shared__ __align__(16) float qsm[];
     __shared__ float st[2];
     const int r = blockIdx.x, K = p.K, T = K >> 5;
@@ -891,9 +901,11 @@ __global__ void __launch_bounds__(256) qprep_row_kernel(PrepArgs p, QAct out) {
     if constexpr (MODE != PREP_PLAIN) {
         if (warp == 0) {
             float sum = 0.0f;
+#pragma unroll 8
             for (int t = 0; t < T; ++t) sum = t == 0 ? xs[lane] : __fadd_rn(sum, xs[32 * t + lane]);
             const float mean = __fdiv_rn(warp_tree(sum), (float)K);
             float s2 = 0.0f;
+#pragma unroll 8
             for (int t = 0; t < T; ++t) {
                 const float c = __fsub_rn(xs[32 * t + lane], mean);
                 const float c2 = __fmul_rn(c, c);

@@ -105,6 +105,10 @@ struct GemvArgs {
     float *part_v;
     uint32_t *part_i;
     float *logits;
+    // RELU on the tensor-core path: when qo.tq is set, the outputs go out as the
+    // next matmul's q8_1 tensor-core activations (as qprep_row_kernel<PLAIN>
+    // would make them from y) instead of f32 rows
+    QAct qo;
 };
 
 // Epilogue of one output element (row of W, activation row n); v = the dot

@@ -9,10 +9,13 @@ and decodes its own length-sorted batches; results are gathered on the host.
   assign    longest-processing-time-first placement of batches on ranks by
             their decode cost, so the slowest rank finishes as early as possible
   decode    one rank's share through its own Engine (one process per GPU)
+  StreamPool  several decode contexts (CUDA streams) on one GPU, each driven by
+            its own host thread, decoding independent batches concurrently
 """
 from __future__ import annotations
 
 import heapq
+import threading
 
 
 def batches(lens: list[int], max_batch: int) -> list[list[int]]:
@@ -57,6 +60,55 @@ def decode_rank(engine, sources: list[list[int]], tgt: int, opts, world: int, ra
         for i, ids in zip(b, t.generate([sources[i] for i in b], tgt, opts)):
             out[i] = ids
     return out
+
+
+class StreamPool:
+    """`streams` decode contexts on one GPU, each with its own CUDA stream,
+    weight copy and graph cache, each driven by its own host thread (the C ABI
+    calls release the GIL): independent batches decode concurrently. A decode
+    step at batch sizes up to 64 is a chain of dependent, latency-bound launches
+    that leaves SMs idle between kernels; the chains of a few batches
+    interleave on the SMs (measured on B200 at batch 64, 16 batches: 1.25x the
+    tokens/s with 2 streams, 1.33x with 3, 1.40x with 4). Item i of a map runs
+    on context i % streams."""
+
+    def __init__(self, gguf_path: str, device: int = 0, streams: int = 3, **engine_kw):
+        from .translator import Engine
+
+        self.engines = [Engine(gguf_path, device=device, **engine_kw) for _ in range(max(1, streams))]
+
+    def __len__(self) -> int:
+        return len(self.engines)
+
+    def map(self, fn, items: list) -> list:
+        """fn(engine, item) for every item, in order per context; results in input order."""
+        n = len(self.engines)
+        out: list = [None] * len(items)
+        errors: list[BaseException] = []
+
+        def work(k: int):
+            try:
+                for i in range(k, len(items), n):
+                    out[i] = fn(self.engines[k], items[i])
+            except BaseException as e:  # noqa: BLE001 - re-raised on the caller's thread
+                errors.append(e)
+
+        threads = [threading.Thread(target=work, args=(k,)) for k in range(min(n, len(items)))]
+        for t in threads:
+            t.start()
+        for t in threads:
+            t.join()
+        if errors:
+            raise errors[0]
+        return out
+
+    @property
+    def kernel_launches(self) -> int:
+        return sum(e.kernel_launches for e in self.engines)
+
+    def close(self):
+        for e in self.engines:
+            e.close()
 
 
 def gather(local: dict[int, list[int]], n: int) -> list[list[int]] | None:
