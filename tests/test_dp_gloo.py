@@ -78,3 +78,47 @@ def test_a_failing_rank_is_reported_not_hung():
     res = _run(2, [3, 4, 5, 6], fail_rank=1)
     assert "injected rank failure" in res[1]
     assert isinstance(res[0], str)  # the surviving rank saw an error, not results
+
+
+class _FakeEngine:
+    def __init__(self, k, fail_on=None):
+        self.k, self.fail_on, self.seen = k, fail_on, []
+        self.kernel_launches = 0
+
+    def close(self):
+        pass
+
+
+def _pool(n, fail_on=None):
+    pool = dp.StreamPool.__new__(dp.StreamPool)
+    pool.engines = [_FakeEngine(k, fail_on) for k in range(n)]
+    return pool
+
+
+def test_stream_pool_maps_item_i_to_context_i_mod_n_in_order():
+    import threading
+
+    pool = _pool(3)
+    tids = {}
+
+    def fn(e, x):
+        e.seen.append(x)
+        tids.setdefault(e.k, set()).add(threading.get_ident())
+        return (e.k, x * x)
+
+    out = pool.map(fn, list(range(10)))
+    assert out == [(i % 3, i * i) for i in range(10)]
+    assert [e.seen for e in pool.engines] == [[0, 3, 6, 9], [1, 4, 7], [2, 5, 8]]
+    assert all(len(t) == 1 for t in tids.values())  # each context's items on one host thread
+
+
+def test_stream_pool_reraises_a_context_failure():
+    pool = _pool(2)
+
+    def fn(e, x):
+        if x == 3:
+            raise RuntimeError("context 1 failed")
+        return x
+
+    with pytest.raises(RuntimeError, match="context 1 failed"):
+        pool.map(fn, list(range(6)))
