@@ -333,6 +333,10 @@ struct mgb_ctx {
     uint64_t test_wait_ns = kWaitNs;
     int test_withhold_chunk = -1;
     int test_withhold_step = -1;  // the same for the persistent step kernel (MGB_TEST_WITHHOLD_STEP)
+    // tensor-core FFN: the up epilogue writes the down matmul's q8_1 activations (1)
+    // or f32 rows that a prep kernel quantizes (0, the default: the per-token
+    // quantization in the epilogue measured slower on B200); MGB_FFN_Q8 overrides
+    int ffn_q8 = 0;
     int sms = 148;  // multiprocessor count of the device (one tensor-core CTA each)
     void *enc_ws = nullptr;  // encoder temporaries (grown on demand)
     size_t enc_ws_bytes = 0;
@@ -1453,7 +1457,7 @@ static mgb_status launch_step(mgb_ctx *c, StaticState *st, float *logits, int fo
         gd.y = st->x;
         // tensor-core path: the up epilogue writes the down matmul's q8_1
         // activations itself (into a second buffer: the up matmul reads X)
-        const bool hq = tc && tc_ok(L.up) && tc_ok(L.down) && L.up.N % 128 == 0 && st->act2.tq;
+        const bool hq = c->ffn_q8 && tc && tc_ok(L.up) && tc_ok(L.down) && L.up.N % 128 == 0 && st->act2.tq;
         if (hq) gu.qo = st->act2;
         TRY((matmul<EPI_RELU, PREP_LN>(c, gu, prep_src(st->x, &L.ffn_norm), X, nullptr, sp, cls)));
         if (hq) TRY(gemm_tc<EPI_RESID>(c, L.down, st->act2, b, gd, nullptr, sp));
@@ -2087,6 +2091,7 @@ mgb_status mgb_open(const char *path, int device, const mgb_options *opts, mgb_c
     if (const char *v = getenv("MGB_TEST_WAIT_NS")) c->test_wait_ns = std::max<uint64_t>(1000, strtoull(v, nullptr, 10));
     if (const char *v = getenv("MGB_TEST_WITHHOLD_CHUNK")) c->test_withhold_chunk = atoi(v);
     if (const char *v = getenv("MGB_TEST_WITHHOLD_STEP")) c->test_withhold_step = atoi(v);
+    if (const char *v = getenv("MGB_FFN_Q8")) c->ffn_q8 = atoi(v) != 0;
     cudaDeviceGetAttribute(&c->sms, cudaDevAttrMultiProcessorCount, device);
     if (c->sms <= 0) c->sms = 148;
     {

@@ -284,11 +284,14 @@ def test_bounded_wait_in_step_kernel_is_reported(gpu, model, monkeypatch, chunk)
     np.testing.assert_array_equal(got, want_ids)
 
 
-@pytest.mark.parametrize("name,preset,b", [("mid", "q4_k_m", 64), ("mid", "q8_0", 24), ("wide", "q8_0", 64),
-                                           ("wide", "q4_k_m", 40)])
-def test_tensor_core_batches_bit_exact(gpu, model, name, preset, b):
+@pytest.mark.parametrize("name,preset,b,ffn_q8", [("mid", "q4_k_m", 64, "0"), ("mid", "q8_0", 24, "0"),
+                                                  ("wide", "q8_0", 64, "0"), ("wide", "q4_k_m", 40, "0"),
+                                                  ("wide", "q4_k_m", 40, "1"), ("mid", "q8_0", 24, "1")])
+def test_tensor_core_batches_bit_exact(gpu, model, name, preset, b, ffn_q8, monkeypatch):
     """Batches of 16+ rows run the tcgen05 matmuls (and the encoder always does for
-    quantized weights): tokens and logits equal the oracle's bit for bit."""
+    quantized weights): tokens and logits equal the oracle's bit for bit. ffn_q8 1:
+    the FFN-up epilogue quantizes the down matmul's activations itself."""
+    monkeypatch.setenv("MGB_FFN_Q8", ffn_q8)
     path = model(name, preset)
     V = models.config_of(name).vocab_size
     src = models.random_sources(b, 2, 10, V, 11, src_tag=V - 1)
