@@ -148,9 +148,10 @@ def kv_bytes(info: dict, src_lens: list[int], steps: int) -> int:
 
 
 def cpu_sample(w) -> tuple[int, int]:
-    """Rows and forced steps of the CPU baseline's bounded sample (seconds of work)."""
+    """Rows and forced steps of the CPU baseline's bounded sample (about 10 s of
+    work on 16 host threads for a batch of 64)."""
     rows = min(w.batch, len(w.sources))
-    return rows, (2 if rows > 8 else 8)
+    return rows, (6 if rows > 8 else 16)
 
 
 def cpu_baseline(w):
