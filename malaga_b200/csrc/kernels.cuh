@@ -148,6 +148,34 @@ __device__ __forceinline__ void epilogue_store(const GemvArgs &g, int row, int n
     }
 }
 
+// epilogue_store with its operands read beforehand: the row's bias b, the
+// residual value resid (RESID) and the decode step (QKV).
+template <int EPI>
+__device__ __forceinline__ void epilogue_pre(const GemvArgs &g, int row, int n, float v, float b, float resid,
+                                             int step) {
+    const Matrix &W = g.W;
+    if constexpr (EPI == EPI_STORE) {
+        g.y[(size_t)n * W.N + row] = W.bias ? __fadd_rn(v, b) : v;
+    } else if constexpr (EPI == EPI_RELU) {
+        const float y = __fadd_rn(v, b);
+        g.y[(size_t)n * W.N + row] = y > 0.0f ? y : 0.0f;
+    } else if constexpr (EPI == EPI_RESID) {
+        g.y[(size_t)n * W.N + row] = __fadd_rn(__fadd_rn(v, b), resid);
+    } else if constexpr (EPI == EPI_QKV) {
+        const float y = __fadd_rn(v, b);
+        const int dm = g.H * g.hd;
+        if (row < dm) {
+            g.q[(size_t)n * dm + row] = y;
+        } else {
+            const int c = row - dm, which = c / dm, h = (c % dm) / g.hd, t = c % g.hd;
+            const size_t at = (((size_t)n * g.H + h) * g.m + step) * g.hd + t;
+            void *cache = which == 0 ? g.kc : g.vc;
+            if (g.kv_f32) reinterpret_cast<float *>(cache)[at] = y;
+            else reinterpret_cast<__half *>(cache)[at] = __float2half_rn(y);
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------
 // Tensor-core activation layout (QAct, written for the tensor-core matmul)
 

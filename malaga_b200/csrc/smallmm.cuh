@@ -473,8 +473,32 @@ __global__ void __launch_bounds__(256) small_mm_kernel(const __grid_constant__ S
             best_v[warp][lane] = kNegInf;
             best_i[warp][lane] = 0xffffffffu;
         }
+    // CTAs with one chunk (the decode step's matrices): the epilogue's bias
+    // values (weights) now, its residual values and the decode step right after
+    // the dependency wait, so the stores after the dot products wait on no load
+    constexpr bool PRE_EPI = EPI == EPI_STORE || EPI == EPI_RELU || EPI == EPI_RESID || EPI == EPI_QKV;
+    const bool pre = PRE_EPI && nchunks == 1;
+    float pb[R], px[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        pb[r] = 0.0f;
+        px[r] = 0.0f;
+        const int row = r0 + warp + 8 * r;
+        if (pre && W.bias && warp + 8 * r < r1 - r0 && row < W.N) pb[r] = __ldg(W.bias + row);
+    }
     pdl_launch_dependents();
     pdl_wait();
+    int step = 0;
+    if constexpr (EPI == EPI_QKV)
+        if (pre) step = (int)*g.step;
+    if constexpr (EPI == EPI_RESID)
+        if (pre)
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const int row = r0 + warp + 8 * r;
+                if (warp + 8 * r < r1 - r0 && row < W.N && lane < NC && n0 + lane < g.rows)
+                    px[r] = __ldcg(g.y + (size_t)(n0 + lane) * W.N + row);
+            }
     SmAct s;
     s.q = reinterpret_cast<int8_t *>(act);
     s.d = reinterpret_cast<float *>(act + (size_t)NC * K);
@@ -521,6 +545,8 @@ __global__ void __launch_bounds__(256) small_mm_kernel(const __grid_constant__ S
                 if constexpr (EPI == EPI_ARGMAX) {
                     if (g.logits) g.logits[(size_t)(n0 + n) * W.N + row] = out[r][n];
                     argmax_merge(bv, bi, out[r][n], (uint32_t)row);
+                } else if (pre) {
+                    epilogue_pre<EPI>(g, row, n0 + n, out[r][n], pb[r], px[r], step);
                 } else {
                     epilogue_store<EPI>(g, row, n0 + n, out[r][n]);
                 }
