@@ -114,7 +114,10 @@ DESCRIBE = {
     "c1": "batch 1, source 32 random ids + language tag + </s>, 32 forced greedy steps",
     "c2": "batch 64 (q8_0 weights), source lengths U[8,64], 64 forced greedy steps",
     "c2q4": "batch 64, source lengths U[8,64], 64 forced greedy steps",
+    "c4": "1024 sentences (source lengths lognormal, median 28, 8-128) in 8 length-sorted batches of 128, "
+          "128 forced greedy steps per batch, batches placed on the ranks by LPT",
 }
+MODEL_NAMES = {"600m": "NLLB-600M", "3.3b": "NLLB-3.3B"}
 
 # The LM-head kernel each batch size runs (the roofline's dominant kernel).
 def lm_kernel(rows: int, preset: str) -> str:
@@ -151,6 +154,8 @@ def cpu_sample(w) -> tuple[int, int]:
     """Rows and forced steps of the CPU baseline's bounded sample (about 10 s of
     work on 16 host threads for a batch of 64)."""
     rows = min(w.batch, len(w.sources))
+    if w.model == "3.3b":
+        return 16, 2
     return rows, (6 if rows > 8 else 16)
 
 
@@ -183,11 +188,14 @@ def run_reference(args, w):
     cb = dict(results[-1])
     cb["value"] = v
     rows, sample_steps = cpu_sample(w)
-    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
+    line = {"impl": "reference",
+            "metric": METRIC if w.model == "600m" else "C4: decoded tokens/s NLLB-3.3B q4_k_m b128 @1/2/4/8 B200",
+            "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * rows * sample_steps / v,
-            "higher_is_better": True, "scaling": "strong" if w.name == "dp600" else "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong" if w.name in ("dp600", "c4") else "weak",
+            "vs_baseline": None,
             "dtype": "int8 dot / f32", "data": "synthetic",
-            "config": {"workload": w.name, "model": f"nllb-600m-{w.preset} (random init)", "sample_rows": rows,
+            "config": {"workload": w.name, "model": f"nllb-{w.model}-{w.preset} (random init)", "sample_rows": rows,
                        "decode_steps_sampled": sample_steps},
             "cpu_baseline": cb, "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                                         "d2h_bytes_per_step": 0}}
@@ -303,12 +311,13 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="dp600", choices=["dp600", "c2q4", "c2", "c1", "c5"])
+    ap.add_argument("--workload", default="dp600", choices=["dp600", "c2q4", "c2", "c1", "c5", "c4"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-b1", action="store_true")
-    ap.add_argument("--streams", type=int, default=4,
-                    help="decode contexts (CUDA streams) per GPU for independent batches (dp.StreamPool)")
+    ap.add_argument("--streams", type=int, default=None,
+                    help="decode contexts (CUDA streams) per GPU for independent batches (dp.StreamPool); "
+                         "default 4, 2 for c4 (3.3B: larger states)")
     args = ap.parse_args()
     if args.workload == "c5" and args.impl == "ours":
         return run_c5(args)
@@ -334,7 +343,7 @@ def main():
     # this rank's share: length-sorted batches of w.batch placed by LPT (a
     # single-batch workload is replicated on every rank instead)
     lens_all = [len(s) for s in w.sources]
-    if w.name == "dp600":
+    if w.name in ("dp600", "c4"):
         share = dp.shard(lens_all, world, rank, w.batch, lambda b: w.steps)
         scaling = "strong"
     else:
@@ -343,8 +352,9 @@ def main():
     srcs = [[w.sources[i] for i in b] for b in share]
     # independent batches decode on `streams` contexts of this GPU at once
     # (dp.StreamPool); batch i belongs to context i % streams
-    streams = max(1, min(args.streams, len(srcs)))
-    pool = dp.StreamPool(path, device=local, streams=streams)
+    streams = max(1, min(args.streams or (2 if w.model == "3.3b" else 4), len(srcs)))
+    # (3.3B states at batch 128 are ~7 GB each: room for every source-length bucket)
+    pool = dp.StreamPool(path, device=local, streams=streams, graph_cache_mb=65536 if w.model == "3.3b" else 8192)
     eng = pool.engines[0]
     info = eng.info
     cur = torch.cuda.current_stream()
@@ -432,10 +442,12 @@ def main():
 
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "metric": METRIC if w.model == "600m" else "C4: decoded tokens/s NLLB-3.3B q4_k_m b128 @1/2/4/8 B200",
+            "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": scaling,
             "vs_baseline": None, "dtype": "int8 dot / f32 (q8_1 activations x GGUF blocks)", "data": "synthetic",
-            "config": {"workload": f"{w.name}: NLLB-600M {w.preset} (random init, seed {w.seed}), {DESCRIBE[w.name]}",
+            "config": {"workload": f"{w.name}: {MODEL_NAMES[w.model]} {w.preset} (random init, seed {w.seed}), "
+                                   f"{DESCRIBE[w.name]}",
                        "global_batch": w.batch, "sentences": len(w.sources) * (1 if scaling == "strong" else world),
                        "decode_steps": steps, "parallelism": f"dp{world}",
                        "step": "ms_per_step = one pass over the rank's batches (each a whole forced decode)",

@@ -1699,7 +1699,7 @@ static mgb_status acquire_state(mgb_ctx *c, const mgb_batch *B, int max_new, boo
     const Config &g = c->cfg;
     const int n = B->b * rep, H = g.dec_heads, hd = g.d / H;
     const int b = pad_rows ? (int)next_pow2((uint32_t)n) : n;
-    if (b > 64) return set_err(MGB_ERR_INVALID, "batch of %d rows exceeds 64", n);
+    if (b > 128) return set_err(MGB_ERR_INVALID, "batch of %d rows exceeds 128", n);
     const int s = bucket(B->s, 16, g.max_pos), m = bucket(max_new + 2, 32, g.max_pos);
     StaticState *st = nullptr;
     for (auto &e : c->cache)

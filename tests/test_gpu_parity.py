@@ -286,7 +286,8 @@ def test_bounded_wait_in_step_kernel_is_reported(gpu, model, monkeypatch, chunk)
 
 @pytest.mark.parametrize("name,preset,b,ffn_q8", [("mid", "q4_k_m", 64, "0"), ("mid", "q8_0", 24, "0"),
                                                   ("wide", "q8_0", 64, "0"), ("wide", "q4_k_m", 40, "0"),
-                                                  ("wide", "q4_k_m", 40, "1"), ("mid", "q8_0", 24, "1")])
+                                                  ("wide", "q4_k_m", 40, "1"), ("mid", "q8_0", 24, "1"),
+                                                  ("mid", "q4_k_m", 128, "0")])
 def test_tensor_core_batches_bit_exact(gpu, model, name, preset, b, ffn_q8, monkeypatch):
     """Batches of 16+ rows run the tcgen05 matmuls (and the encoder always does for
     quantized weights): tokens and logits equal the oracle's bit for bit. ffn_q8 1:
