@@ -166,6 +166,8 @@ def cpu_baseline(w):
     import oracle
 
     path = models.model_path(w.model, w.preset, w.seed)
+    # every host core (torchrun sets OMP_NUM_THREADS=1 for its processes)
+    oracle.lib().orc_set_threads(len(os.sched_getaffinity(0)))
     orc = oracle.Oracle(path)
     rows, sample_steps = cpu_sample(w)
     src = sorted(w.sources, key=len, reverse=True)[:rows]

@@ -55,6 +55,7 @@ def lib():
         L.orc_log.argtypes = [f]
         L.orc_log.restype = f
         L.orc_threads.restype = i
+        L.orc_set_threads.argtypes = [i]
         L.orc_matmul.argtypes = [i, vp, ctypes.c_long, ctypes.c_long, vp, i, i, i, vp]
         L.orc_matmul.restype = i
         L.orc_quantize_q81.argtypes = [vp, i, i, vp, vp, vp]

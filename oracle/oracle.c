@@ -1283,3 +1283,13 @@ ORC_EXPORT int orc_threads(void) {
     return 1;
 #endif
 }
+
+/* Threads of the following parallel regions (a launcher may have set
+ * OMP_NUM_THREADS=1 for its processes). */
+ORC_EXPORT void orc_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
