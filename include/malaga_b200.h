@@ -121,6 +121,21 @@ MGB_API mgb_status mgb_greedy(mgb_ctx *ctx, const mgb_batch *batch, uint32_t tgt
 MGB_API mgb_status mgb_greedy_logits(mgb_ctx *ctx, const mgb_batch *batch, uint32_t tgt_lang, uint32_t max_new,
                              int force_steps, uint32_t *out_ids, float *logits);
 
+/* Index of the vocabulary shortlist stored for language code `code` (GGUF
+ * metadata nllb.shortlist.<code> with tensor lm_head.<code>.weight, written by
+ * the converter's shortlist option, convert.rs:218-232), or -1. */
+MGB_API int mgb_shortlist_find(const mgb_ctx *ctx, const char *code);
+
+/* mgb_greedy over a vocabulary shortlist (--fast-vocab, not exact; model.rs:229-250,
+ * 556-612, graph.rs:98-105, malaga.cu:280-326): each step scores the shortlist's
+ * rows of the LM head plus the row's source tokens (dot products of the final
+ * LayerNorm output with their embeddings) and picks the best of the two lists
+ * (lowest index on ties, shortlist first). decoder_start and tgt_lang must be
+ * in the shortlist (translator.rs:186-192), else MGB_ERR_INVALID. */
+MGB_API mgb_status mgb_greedy_shortlist(mgb_ctx *ctx, const mgb_batch *batch, uint32_t tgt_lang, int shortlist,
+                                uint32_t max_new, uint32_t sync_every, int force_steps, uint32_t *out_ids,
+                                uint32_t *out_lens);
+
 /* Beam search over an encoded batch (Translator::beam_search, translator.rs:250-358):
  * beam width k (1..8), length penalty (score / (len+1)^penalty), at most max_new
  * tokens; batch * k <= 64 rows. The prefix [decoder_start, tgt_lang] is fed first.

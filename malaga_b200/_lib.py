@@ -41,6 +41,8 @@ SIGNATURES = {
     "mgb_batch_free": (None, [_vp]),
     "mgb_batch_cross": (_i, [_vp, _vp, _u32, _i, _vp]),
     "mgb_greedy": (_i, [_vp, _vp, _u32, _u32, _u32, _i, _vp, _vp]),
+    "mgb_shortlist_find": (_i, [_vp, ctypes.c_char_p]),
+    "mgb_greedy_shortlist": (_i, [_vp, _vp, _u32, _i, _u32, _u32, _i, _vp, _vp]),
     "mgb_beam": (_i, [_vp, _vp, _u32, _u32, ctypes.c_float, _u32, _vp, _vp]),
     "mgb_greedy_logits": (_i, [_vp, _vp, _u32, _u32, _i, _vp, _vp]),
     "mgb_clear_cache": (_i, [_vp]),

@@ -164,8 +164,15 @@ def _tokenizer_json(cfg: NllbConfig, langs: list[str], words: int) -> str:
 
 
 def convert(cfg: NllbConfig, get: Callable[[str], np.ndarray], out: str, preset: str = "q4_k_m",
-            name: str = "nllb", tokenizer_json: str | None = None) -> None:
-    """Writes the GGUF file of convert.rs:196-319 from HF-named f32 tensors."""
+            name: str = "nllb", tokenizer_json: str | None = None,
+            shortlists: dict[str, list[int]] | None = None) -> None:
+    """Writes the GGUF file of convert.rs:196-319 from HF-named f32 tensors.
+
+    shortlists: {language code: vocabulary ids} for `--fast-vocab` decoding
+    (convert.rs:218-232): each is stored sorted as `nllb.shortlist.<code>` with
+    its reduced LM head `lm_head.<code>.weight` (the embedding rows of those ids,
+    quantized like the embedding). The reference builds the ids from a corpus
+    with the tokenizer and adds the language token; callers pass the ids."""
     lin, down, emb = PRESETS[preset]
     enc_s = np.float32((cfg.d_model // cfg.encoder_attention_heads) ** -0.5)
     dec_s = np.float32((cfg.d_model // cfg.decoder_attention_heads) ** -0.5)
@@ -177,6 +184,14 @@ def convert(cfg: NllbConfig, get: Callable[[str], np.ndarray], out: str, preset:
 
     d, V = cfg.d_model, cfg.vocab_size
     add("token_embd.weight", (V, d), emb, lambda: get("model.shared.weight"))
+    sl_meta = []
+    for code, ids in (shortlists or {}).items():
+        ids = sorted({int(i) for i in ids})
+        if not ids or ids[0] < 0 or ids[-1] >= V:
+            raise ValueError(f"shortlist {code}: ids outside the vocabulary")
+        idx = np.array(ids, np.int64)
+        add(f"lm_head.{code}.weight", (len(ids), d), emb, lambda idx=idx: get("model.shared.weight")[idx])
+        sl_meta.append((f"{ARCH}.shortlist.{code}", ids))
     for side, n_layers, s, ffn in (("encoder", cfg.encoder_layers, enc_s, cfg.encoder_ffn_dim),
                                    ("decoder", cfg.decoder_layers, dec_s, cfg.decoder_ffn_dim)):
         short = side[:3]
@@ -231,7 +246,7 @@ def convert(cfg: NllbConfig, get: Callable[[str], np.ndarray], out: str, preset:
         ("general.source.url", f"https://huggingface.co/{name}"),
         ("tokenizer.ggml.model", "nllb"),
         ("tokenizer.huggingface.json", tokenizer_json),
-    ] + cfg.to_gguf()
+    ] + cfg.to_gguf() + sl_meta
     tmp = out + ".partial"
     G.write_gguf(tmp, meta, plans)
     os.replace(tmp, out)

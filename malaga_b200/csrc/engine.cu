@@ -93,6 +93,7 @@ struct GgufFile {
     void *map = MAP_FAILED;
     size_t size = 0;
     std::map<std::string, uint64_t> u32;
+    std::map<std::string, std::vector<uint32_t>> u32arr;  // arrays of u32 / i32 (shortlists)
     std::map<std::string, GgufTensor> tensors;
     ~GgufFile() {
         if (map != MAP_FAILED) munmap(map, size);
@@ -164,6 +165,14 @@ mgb_status parse_gguf(const char *path, GgufFile &f) {
         } else if (t == 10 || t == 11) {
             if (!need(8)) return set_err(MGB_ERR_IO, "truncated GGUF metadata");
             f.u32[key] = r64();
+        } else if (t == 9 && need(12) && (((const uint32_t *)p)[0] == 4 || ((const uint32_t *)p)[0] == 5)) {
+            r32();
+            const uint64_t n = r64();
+            if (n > (uint64_t)(end - p) / 4) return set_err(MGB_ERR_IO, "truncated GGUF metadata");
+            std::vector<uint32_t> &v = f.u32arr[key];
+            v.resize(n);
+            memcpy(v.data(), p, 4 * n);
+            p += 4 * n;
         } else if (!skip(t)) {
             return set_err(MGB_ERR_IO, "bad GGUF metadata value for %s", key.c_str());
         }
@@ -242,6 +251,12 @@ struct StaticState {
     unsigned long long *trace = nullptr;  // phase timing (MGB_STEP_TRACE)
     std::vector<StepPhase> phase_host;
     std::string trace_path;
+    // --fast-vocab (shortlist index >= 0): the rows' source ids [b][s] (pad past
+    // each row's length) and the best source-token logit of each row
+    int sl = -1;
+    uint32_t *src_ids = nullptr;
+    float *src_v = nullptr;
+    uint32_t *src_i = nullptr;
     int step_slots = 0, step_slot_bytes = 0, step_act_bytes = 0, step_ctas = 0;
     size_t step_smem = 0;
     // beam search (allocated on first use): step logits, top-k, row sources, and
@@ -271,6 +286,7 @@ struct mgb_batch {
     size_t cross_bytes = 0;
     void *buf = nullptr;     // one device buffer: cross, then d_lens (from the context's batch pool)
     size_t buf_bytes = 0;
+    std::vector<uint32_t> src;  // source ids [b][s] (a shortlist decode scores them, graph.rs:98-105)
     mgb_ctx *owner = nullptr;
 };
 
@@ -312,6 +328,15 @@ struct mgb_ctx {
     std::vector<PoolBuf> batch_pool;  // freed batches' buffers
     size_t batch_pool_bytes = 0;
     std::unordered_set<mgb_batch *> batches;  // live batches (detached by mgb_close)
+    // vocabulary shortlists (GGUF nllb.shortlist.<code> + lm_head.<code>.weight,
+    // convert.rs:218-232; model.rs:229-250): sorted ids and the reduced LM head
+    struct Shortlist {
+        std::string code;
+        std::vector<uint32_t> ids;
+        Matrix W;
+        const uint32_t *d_ids = nullptr;
+    };
+    std::vector<Shortlist> shortlists;
     size_t weight_bytes = 0, step_bytes = 0;
     uint32_t *d_err = nullptr;  // device-side error flags (a bounded wait ran out)
     int tc_min_nt = 8;  // narrowest token tile of the tensor-core matmul (MGB_TC_MIN_NT)
@@ -600,6 +625,19 @@ static mgb_status load_model(mgb_ctx *c, const char *path) {
 
     Loader L{c, &f};
     const int d = g.d;
+    c->shortlists.clear();
+    for (const auto &kv : f.u32arr) {
+        const std::string pre = "nllb.shortlist.";
+        if (kv.first.compare(0, pre.size(), pre) != 0) continue;
+        mgb_ctx::Shortlist sl;
+        sl.code = kv.first.substr(pre.size());
+        sl.ids = kv.second;
+        for (size_t i = 0; i < sl.ids.size(); ++i)
+            if (sl.ids[i] >= (uint32_t)g.V || (i && sl.ids[i] <= sl.ids[i - 1]))
+                return set_err(MGB_ERR_IO, "shortlist %s: ids not sorted within the vocabulary", sl.code.c_str());
+        if (sl.ids.empty()) continue;
+        c->shortlists.push_back(std::move(sl));
+    }
     c->enc.resize(g.enc_layers);
     c->dec.resize(g.dec_layers);
     for (int pass = 0; pass < 2; ++pass) {
@@ -634,6 +672,12 @@ static mgb_status load_model(mgb_ctx *c, const char *path) {
         }
         TRY(P.norm("enc.output_norm", d, c->enc_norm));
         TRY(P.norm("dec.output_norm", d, c->dec_norm));
+        for (mgb_ctx::Shortlist &sl : c->shortlists) {
+            TRY(P.matrix("lm_head." + sl.code, sl.W, (long)sl.ids.size(), d, false));
+            const size_t o = L.reserve(4 * sl.ids.size());
+            if (pass == 1) memcpy(L.host.data() + o, sl.ids.data(), 4 * sl.ids.size());
+            P.ptr(reinterpret_cast<const uint8_t **>(const_cast<const uint32_t **>(&sl.d_ids)), o);
+        }
         // Sinusoidal position table [max_pos + pad + 1, d] (model.rs:325-340, 361-366).
         const int n_pos = g.max_pos + g.pad + 1;
         size_t off = L.reserve((size_t)n_pos * d * 4);
@@ -1177,6 +1221,23 @@ static mgb_status matmul(mgb_ctx *c, const GemvArgs &g, const PrepArgs &p, const
 static mgb_status finalize(mgb_ctx *c, StaticState *st, int parts, int force) {
     const Config &g = c->cfg;
     const int threads = std::min(1024, std::max(32, 32 * st->b));
+    if (st->sl >= 0) {  // --fast-vocab: source-token logits, then the concat argmax
+        const mgb_ctx::Shortlist &sl = c->shortlists[st->sl];
+        const size_t sh = (size_t)4 * g.d;
+        cudaError_t e = allow_smem(src_logits_kernel, sh);
+        if (e == cudaSuccess)
+            e = launch_pdl(src_logits_kernel, dim3(st->b), dim3(256), sh, c->stream, (const float *)st->x,
+                           c->dec_norm.g, c->dec_norm.b, g.d, c->embed, (const uint32_t *)st->src_ids, st->s,
+                           (int)sl.ids.size(), st->src_v, st->src_i);
+        ++c->launches;
+        if (e != cudaSuccess) return cuda_err(e, "source logits launch");
+        e = launch_pdl(greedy_finalize_sl_kernel, dim3(1), dim3(threads), 0, c->stream, (const float *)st->part_v,
+                       (const uint32_t *)st->part_i, parts, st->b, (const float *)st->src_v,
+                       (const uint32_t *)st->src_i, sl.d_ids, (int)sl.ids.size(), (const uint32_t *)st->src_ids, st->s,
+                       st->finished, st->ids, st->out, st->m, st->step, (uint32_t)g.eos, (uint32_t)g.pad, force);
+        ++c->launches;
+        return e == cudaSuccess ? MGB_OK : cuda_err(e, "finalize launch");
+    }
     cudaError_t e = launch_pdl(greedy_finalize_kernel, dim3(1), dim3(threads), 0, c->stream,
                                (const float *)st->part_v, (const uint32_t *)st->part_i, parts, st->b,
                                st->finished, st->ids, st->out, st->m, st->step, (uint32_t)g.eos, (uint32_t)g.pad,
@@ -1464,8 +1525,9 @@ static mgb_status launch_step(mgb_ctx *c, StaticState *st, float *logits, int fo
         else TRY((matmul<EPI_RESID, PREP_PLAIN>(c, gd, prep_src(st->u, nullptr), X, nullptr, sp, cls)));
     }
     if (!mode.lm) return MGB_OK;
-    // dec_norm -> tied LM head fused with the first argmax pass -> greedy bookkeeping
-    GemvArgs gl = mm_out(c->embed, b);
+    // dec_norm -> tied LM head (or the shortlist's reduced head) fused with the
+    // first argmax pass -> greedy bookkeeping
+    GemvArgs gl = mm_out(st->sl >= 0 ? c->shortlists[st->sl].W : c->embed, b);
     gl.part_v = st->part_v;
     gl.part_i = st->part_i;
     gl.logits = logits;
@@ -1598,6 +1660,7 @@ static mgb_status encode(mgb_ctx *c, const uint32_t *ids, const uint32_t *lens, 
     B->s = S;
     B->owner = c;
     B->lens.assign(lens, lens + b);
+    B->src.assign(ids, ids + (size_t)b * S);
     const int Hd = g.dec_heads, hdd = d / Hd;
     const size_t per = (size_t)b * Hd * S * hdd;
     B->cross_bytes = per * 4 * 2 * g.dec_layers;
@@ -1695,7 +1758,7 @@ static mgb_status reset_finished(mgb_ctx *c, StaticState *st, int active) {
 // loads the batch into it (graph.rs:236-268).
 // rep > 1: every sentence fills rep consecutive rows (beam search).
 static mgb_status acquire_state(mgb_ctx *c, const mgb_batch *B, int max_new, bool pad_rows, StaticState **out,
-                                int rep = 1) {
+                                int rep = 1, int sl = -1) {
     const Config &g = c->cfg;
     const int n = B->b * rep, H = g.dec_heads, hd = g.d / H;
     const int b = pad_rows ? (int)next_pow2((uint32_t)n) : n;
@@ -1703,10 +1766,19 @@ static mgb_status acquire_state(mgb_ctx *c, const mgb_batch *B, int max_new, boo
     const int s = bucket(B->s, 16, g.max_pos), m = bucket(max_new + 2, 32, g.max_pos);
     StaticState *st = nullptr;
     for (auto &e : c->cache)
-        if (e->b == b && e->s == s && e->m == m) st = e.get();
+        if (e->b == b && e->s == s && e->m == m && e->sl == sl) st = e.get();  // (graph.rs:243 key)
     if (!st) {
         TRY(new_state(c, b, s, m, &st));
         c->cache.emplace_back(st);
+        if (sl >= 0) {
+            st->sl = sl;
+            for (void **p : {(void **)&st->src_ids, (void **)&st->src_v, (void **)&st->src_i}) {
+                const size_t n = p == (void **)&st->src_ids ? (size_t)4 * b * s : (size_t)4 * b;
+                TRY(c->dalloc(p, n));
+                st->allocs.push_back(*p);
+                st->bytes += n;
+            }
+        }
         evict(c, st);
     }
     st->last_used = ++c->clock;
@@ -1720,6 +1792,13 @@ static mgb_status acquire_state(mgb_ctx *c, const mgb_batch *B, int max_new, boo
             cross_load_kernel<<<c->sms * 4, 256, 0, c->stream>>>(B->cross + per * (2 * l + 1), st->cv[l], 1, n, rep,
                                                                  H, B->s, s, hd);
         }));
+    }
+    if (sl >= 0) {  // source ids of every row, pad past its length (graph.rs:98-105)
+        std::vector<uint32_t> ids((size_t)b * s, (uint32_t)g.pad);
+        for (int i = 0; i < n; ++i)
+            for (int j = 0; j < (int)B->lens[i / rep] && j < s; ++j) ids[(size_t)i * s + j] = B->src[(size_t)(i / rep) * B->s + j];
+        CK(cudaMemcpyAsync(st->src_ids, ids.data(), 4 * ids.size(), cudaMemcpyHostToDevice, c->stream));
+        CK(cudaStreamSynchronize(c->stream));
     }
     std::vector<uint32_t> lens(b, 1);
     for (int i = 0; i < n; ++i) lens[i] = B->lens[i / rep];
@@ -1966,12 +2045,12 @@ static mgb_status run_beam(mgb_ctx *c, const mgb_batch *B, uint32_t tgt, int k, 
 }
 
 static mgb_status run_greedy(mgb_ctx *c, const mgb_batch *B, uint32_t tgt, int max_new, int sync_every, int force,
-                             uint32_t *out_ids, uint32_t *out_lens, float *logits_host) {
+                             uint32_t *out_ids, uint32_t *out_lens, float *logits_host, int sl = -1) {
     const Config &g = c->cfg;
     const int n = B->b;
     const bool capture = c->capture && c->opts.use_graphs && !logits_host;
     StaticState *st = nullptr;
-    TRY(acquire_state(c, B, max_new, capture, &st));
+    TRY(acquire_state(c, B, max_new, capture, &st, 1, sl));
     const int b = st->b, m = st->m;
     float *d_logits = nullptr;
     if (logits_host) {
@@ -2208,22 +2287,48 @@ static mgb_status check_greedy(mgb_ctx *c, const mgb_batch *B, uint32_t tgt, uin
     return MGB_OK;
 }
 
-mgb_status mgb_greedy(mgb_ctx *c, const mgb_batch *B, uint32_t tgt, uint32_t max_new, uint32_t sync_every, int force,
-                      uint32_t *out_ids, uint32_t *out_lens) {
+static mgb_status greedy_api(mgb_ctx *c, const mgb_batch *B, uint32_t tgt, uint32_t max_new, uint32_t sync_every,
+                             int force, uint32_t *out_ids, uint32_t *out_lens, int sl) {
     TRY(check_greedy(c, B, tgt, max_new));
     if (!out_ids) return set_err(MGB_ERR_INVALID, "null out_ids");
     CK(cudaSetDevice(c->device));
-    mgb_status s = run_greedy(c, B, tgt, (int)max_new, std::max(1u, sync_every), force, out_ids, out_lens, nullptr);
+    mgb_status s = run_greedy(c, B, tgt, (int)max_new, std::max(1u, sync_every), force, out_ids, out_lens, nullptr, sl);
     if (s == MGB_OK) return s;
     if (s == MGB_ERR_OOM && c->capture && c->opts.use_graphs) {
         // graph.rs:214-222: drop graphs for good and retry eagerly
         std::string why = g_err;
         c->capture = false;
         clear_cache(c);
-        s = run_greedy(c, B, tgt, (int)max_new, std::max(1u, sync_every), force, out_ids, out_lens, nullptr);
+        s = run_greedy(c, B, tgt, (int)max_new, std::max(1u, sync_every), force, out_ids, out_lens, nullptr, sl);
         if (s != MGB_OK) g_err = why + "; retry without graphs: " + g_err;
     }
     return s;
+}
+
+mgb_status mgb_greedy(mgb_ctx *c, const mgb_batch *B, uint32_t tgt, uint32_t max_new, uint32_t sync_every, int force,
+                      uint32_t *out_ids, uint32_t *out_lens) {
+    return greedy_api(c, B, tgt, max_new, sync_every, force, out_ids, out_lens, -1);
+}
+
+int mgb_shortlist_find(const mgb_ctx *c, const char *code) {
+    if (!c || !code) return -1;
+    for (size_t i = 0; i < c->shortlists.size(); ++i)
+        if (c->shortlists[i].code == code) return (int)i;
+    return -1;
+}
+
+mgb_status mgb_greedy_shortlist(mgb_ctx *c, const mgb_batch *B, uint32_t tgt, int shortlist, uint32_t max_new,
+                                uint32_t sync_every, int force, uint32_t *out_ids, uint32_t *out_lens) {
+    if (!c) return set_err(MGB_ERR_INVALID, "null argument");
+    if (shortlist < 0 || shortlist >= (int)c->shortlists.size())
+        return set_err(MGB_ERR_INVALID, "no shortlist %d", shortlist);
+    // the forced start tokens must be in the shortlist (translator.rs:186-192)
+    const std::vector<uint32_t> &ids = c->shortlists[shortlist].ids;
+    for (uint32_t t : {(uint32_t)c->cfg.start, tgt})
+        if (!std::binary_search(ids.begin(), ids.end(), t))
+            return set_err(MGB_ERR_INVALID, "token %u missing from shortlist %s", t,
+                           c->shortlists[shortlist].code.c_str());
+    return greedy_api(c, B, tgt, max_new, sync_every, force, out_ids, out_lens, shortlist);
 }
 
 mgb_status mgb_beam(mgb_ctx *c, const mgb_batch *B, uint32_t tgt, uint32_t k, float length_penalty, uint32_t max_new,

@@ -418,6 +418,97 @@ __global__ void greedy_finalize_kernel(const float *pv, const uint32_t *pi, int 
     if (threadIdx.x == 0) *step = s + 1;
 }
 
+// --fast-vocab (model.rs:595-604): the logits of the row's source tokens next
+// to the shortlist's. h = dec_norm(x[row]) (the LM head's LayerNorm: SUM32
+// statistics, ((x - mean) * rstd) * g + b), then for each source position j of
+// the state, dot(h, E[src_ids[row][j]]) in the F32 order (lane l's FMA chain
+// over elements l, l+32, ..., then the butterfly at 16, 8, 4, 2, 1; row_dots in
+// malaga.cu:230-243 is fast-math and not restatable); the row's best (value,
+// V1 + j), the lowest j on ties. One CTA per row.
+__global__ void __launch_bounds__(256) src_logits_kernel(const float *x, const float *gamma, const float *beta, int d,
+                                                         Matrix E, const uint32_t *src_ids, int S, int V1,
+                                                         float *best_v, uint32_t *best_i) {
+    extern __shared__ __align__(16) float hs[];  // [d]
+    __shared__ float stat[2];
+    __shared__ float wv[8];
+    __shared__ uint32_t wi[8];
+    const int row = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, T = d >> 5;
+    pdl_launch_dependents();
+    pdl_wait();
+    for (int i = threadIdx.x; i < d; i += blockDim.x) hs[i] = __ldcg(x + (size_t)row * d + i);
+    __syncthreads();
+    if (warp == 0) {
+        float sum = 0.0f;
+        for (int t = 0; t < T; ++t) sum = t == 0 ? hs[lane] : __fadd_rn(sum, hs[32 * t + lane]);
+        const float mean = __fdiv_rn(warp_tree(sum), (float)d);
+        float s2 = 0.0f;
+        for (int t = 0; t < T; ++t) {
+            const float c = __fsub_rn(hs[32 * t + lane], mean);
+            const float c2 = __fmul_rn(c, c);
+            s2 = t == 0 ? c2 : __fadd_rn(s2, c2);
+        }
+        const float var = __fdiv_rn(warp_tree(s2), (float)d);
+        if (lane == 0) {
+            stat[0] = mean;
+            stat[1] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < d; i += blockDim.x)
+        hs[i] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(hs[i], stat[0]), stat[1]), __ldg(gamma + i)), __ldg(beta + i));
+    __syncthreads();
+    float bv = kNegInf;
+    uint32_t bi = 0xffffffffu;
+    for (int j = warp; j < S; j += 8) {
+        const int id = (int)src_ids[(size_t)row * S + j];
+        float acc = 0.0f;
+        for (int i = lane; i < d; i += 32) acc = __fmaf_rn(deq_elem(E, id, i), hs[i], acc);
+        argmax_merge(bv, bi, warp_sum_bf(acc), (uint32_t)(V1 + j));
+    }
+    if (lane == 0) {
+        wv[warp] = bv;
+        wi[warp] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < 8; ++w) argmax_merge(bv, bi, wv[w], wi[w]);
+        best_v[row] = bv;
+        best_i[row] = bi;
+    }
+}
+
+// greedy_finalize_kernel over the virtual row concat(shortlist logits, source
+// logits) (malaga.cu:280-326 with vocab_map and src_ids): the LM head's
+// partials index the shortlist rows, the source candidate is index V1 + j;
+// the winner maps to sl_ids[i] or the row's source token j.
+__global__ void greedy_finalize_sl_kernel(const float *pv, const uint32_t *pi, int parts, int rows, const float *sv,
+                                          const uint32_t *si, const uint32_t *sl_ids, int V1, const uint32_t *src_ids,
+                                          int S, uint8_t *finished, uint32_t *ids, uint32_t *out, int m,
+                                          uint32_t *step, uint32_t eos, uint32_t pad, int force) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const uint32_t s = *step;
+    for (int row = w; row < rows; row += nw) {
+        float best = kNegInf;
+        uint32_t bi = 0xffffffffu;
+        for (int p = lane; p < parts; p += 32) argmax_merge(best, bi, pv[(size_t)row * parts + p], pi[(size_t)row * parts + p]);
+        warp_argmax(best, bi);
+        if (lane == 0) {
+            argmax_merge(best, bi, sv[row], si[row]);
+            uint32_t tok = bi < (uint32_t)V1           ? sl_ids[bi]
+                           : bi < (uint32_t)(V1 + S) ? src_ids[(size_t)row * S + (bi - V1)]
+                                                     : pad;  // (no finite candidate)
+            if (finished[row]) tok = pad;
+            if (!force && tok == eos) finished[row] = 1;
+            ids[row] = tok;
+            out[(size_t)row * m + s] = tok;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) *step = s + 1;
+}
+
 // Encoder input: x = E[id] * scale + pos[p]; padded tokens use id = pad, p = pad.
 __global__ void __launch_bounds__(256) embed_tokens_kernel(Matrix E, const uint32_t *ids, const uint32_t *lens, int S,
                                                            int rows, const float *pos_table, uint32_t pad,

@@ -63,6 +63,29 @@ def model_path(name: str, preset: str, seed: int = 0, directory: str | None = No
     return path
 
 
+def synthetic_shortlist(vocab: int, n: int, seed: int, keep: list[int]) -> list[int]:
+    """A vocabulary shortlist for tests and benches: the special tokens 0-3 (kept by
+    convert.rs:190), the ids in `keep` (language tokens) and n seeded ids."""
+    ids = set(range(4)) | set(int(k) for k in keep)
+    ids |= set(int(x) for x in C.seeded_uniform_u32(n, seed, 5, 4, vocab))
+    return sorted(ids)
+
+
+def shortlist_model_path(name: str, preset: str, seed: int, shortlists: dict[str, list[int]],
+                         directory: str | None = None) -> str:
+    """Path of the GGUF for (architecture, preset, seed) with vocabulary shortlists
+    ({language code: ids}, --fast-vocab), generated on first use."""
+    directory = directory or MODEL_DIR
+    os.makedirs(directory, exist_ok=True)
+    tag = "-".join(f"{k}{len(v)}" for k, v in sorted(shortlists.items()))
+    path = os.path.join(directory, f"{name}-{preset}-s{seed}-sl-{tag}.gguf")
+    if not os.path.exists(path):
+        cfg, std = SPECS[name]
+        C.convert(cfg, C.random_init_source(cfg, seed, std), path, preset, f"synthetic-nllb-{name}",
+                  shortlists=shortlists)
+    return path
+
+
 def config_of(name: str) -> C.NllbConfig:
     return C.TINY if name == "tiny" else SPECS[name][0]
 

@@ -38,6 +38,11 @@ class GenOptions:
     # benchmark uses 1.5 * len + 8).
     budget_scale: float = 2.0
     budget_extra: int = 16
+    # --fast-vocab (translator.rs:30-34, off by default, not exact): the language
+    # code of the GGUF shortlist to decode over (the reference derives it from
+    # tgt_lang through the tokenizer); used for greedy decoding when the model has
+    # it and it contains the forced start tokens, else the full vocabulary.
+    shortlist: str | None = None
 
 
 class Batch:
@@ -123,14 +128,23 @@ class Engine:
         return Batch(self, h.value, [int(x) for x in lens], int(lens.max()))
 
     def greedy(self, batch: Batch, tgt_lang: int, max_new: int, sync_every: int = 4, force: bool = False,
-               out: np.ndarray | None = None) -> tuple[np.ndarray, np.ndarray]:
-        """Raw columns [b, max_new] (pad after eos) and the lengths before eos."""
+               out: np.ndarray | None = None, shortlist: int = -1) -> tuple[np.ndarray, np.ndarray]:
+        """Raw columns [b, max_new] (pad after eos) and the lengths before eos;
+        shortlist >= 0 decodes over that vocabulary shortlist (--fast-vocab)."""
         if out is None:
             out = np.empty((batch.size, max_new), np.uint32)
         lens = np.empty(batch.size, np.uint32)
-        check(_lib.load().mgb_greedy(self.h, batch.h, tgt_lang, max_new, sync_every, int(force), out.ctypes.data,
-                                     lens.ctypes.data))
+        if shortlist >= 0:
+            check(_lib.load().mgb_greedy_shortlist(self.h, batch.h, tgt_lang, shortlist, max_new, sync_every,
+                                                   int(force), out.ctypes.data, lens.ctypes.data))
+        else:
+            check(_lib.load().mgb_greedy(self.h, batch.h, tgt_lang, max_new, sync_every, int(force),
+                                         out.ctypes.data, lens.ctypes.data))
         return out, lens
+
+    def shortlist(self, code: str) -> int:
+        """Index of the GGUF's vocabulary shortlist for language `code`, or -1."""
+        return _lib.load().mgb_shortlist_find(self.h, code.encode())
 
     def beam(self, batch: Batch, tgt_lang: int, k: int, max_new: int,
              length_penalty: float = 1.0) -> tuple[np.ndarray, np.ndarray]:
@@ -185,7 +199,16 @@ class Translator:
             if opts.beam_size > 1:
                 out, lens = self.engine.beam(batch, tgt_lang, opts.beam_size, max_new, opts.length_penalty)
             else:
-                out, lens = self.engine.greedy(batch, tgt_lang, max_new, max(1, opts.sync_every), opts.force_steps)
+                sl = self.engine.shortlist(opts.shortlist) if opts.shortlist else -1
+                try:
+                    out, lens = self.engine.greedy(batch, tgt_lang, max_new, max(1, opts.sync_every), opts.force_steps,
+                                                   shortlist=sl)
+                except MgbError as e:
+                    if sl < 0 or "missing from shortlist" not in str(e):
+                        raise
+                    # start tokens outside the shortlist: the full vocabulary (translator.rs:189-192)
+                    out, lens = self.engine.greedy(batch, tgt_lang, max_new, max(1, opts.sync_every),
+                                                   opts.force_steps)
         finally:
             batch.free()
         res = []

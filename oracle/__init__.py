@@ -50,6 +50,7 @@ def lib():
         L.orc_enc_cross.argtypes = [vp, vp, i, i, vp]
         L.orc_greedy.argtypes = [vp, vp, u32, i, i, vp, vp]
         L.orc_beam.argtypes = [vp, vp, u32, i, f, i, vp, vp]
+        L.orc_greedy_sl.argtypes = [vp, vp, vp, vp, i, u32, i, i, vp, i, i, vp]
         L.orc_exp.argtypes = [f]
         L.orc_exp.restype = f
         L.orc_log.argtypes = [f]
@@ -110,6 +111,18 @@ class Oracle:
         lib().orc_greedy(self.h, enc.h, tgt, max_new, int(force), out.ctypes.data,
                          lg.ctypes.data if logits else None)
         return (out, lg) if logits else out
+
+    def greedy_shortlist(self, src: list[list[int]], tgt: int, max_new: int, sl_ids: list[int], s_bucket: int,
+                         force: bool = False):
+        """Raw greedy columns [b, max_new] over a vocabulary shortlist (sorted ids)
+        and the source tokens, the state's source bucket being s_bucket."""
+        enc = self.encode(src)
+        ids, lens = pad_batch(src, self.cfg["pad"])
+        sl = np.ascontiguousarray(sl_ids, np.uint32)
+        out = np.zeros((enc.b, max_new), np.uint32)
+        lib().orc_greedy_sl(self.h, enc.h, ids.ctypes.data, lens.ctypes.data, ids.shape[1], tgt, max_new, int(force),
+                            sl.ctypes.data, len(sl), s_bucket, out.ctypes.data)
+        return out
 
     def beam(self, src: list[list[int]], tgt: int, k: int, max_new: int, length_penalty: float = 1.0):
         enc = self.encode(src)

@@ -1029,6 +1029,62 @@ ORC_EXPORT int orc_greedy(orc_model *M, orc_enc *E, uint32_t tgt, int max_new, i
     return max_new;
 }
 
+/*
+ * Greedy decoding over a vocabulary shortlist (--fast-vocab, not exact;
+ * model.rs:556-612, graph.rs:98-105, malaga.cu:280-326). Each step scores, per
+ * row, the LM head rows of the shortlist ids (rows of the tied embedding, so
+ * their logits are those of the full head) followed by the row's S source
+ * positions (its source ids, pad past its length), scored as
+ * dot(dec_norm(x), E[id]) in the F32 order (f32_out); the first maximum of that
+ * list wins and maps back to its token. The next input embedding is E[token],
+ * as the reference's shortlist or source-embedding row of the token.
+ * src: [b][src_stride] ids, lens: [b]; S: the state's source bucket.
+ */
+ORC_EXPORT int orc_greedy_sl(orc_model *M, orc_enc *E, const uint32_t *src, const uint32_t *lens, int src_stride,
+                             uint32_t tgt, int max_new, int force_steps, const uint32_t *sl_ids, int V1, int S,
+                             uint32_t *out) {
+    const cfg_t *c = &M->c;
+    const int b = E->b, m = max_new + 2, d = c->d;
+    dstate_t St;
+    int cls = 1;
+    while (cls < b) cls <<= 1; /* graph.rs:242 */
+    dstate_init(M, &St, b, m, cls);
+    uint32_t *ids = malloc(b * sizeof(uint32_t));
+    uint8_t *fin = calloc(b, 1);
+    float *erow = malloc((size_t)d * sizeof(float));
+    for (int r = 0; r < b; ++r) ids[r] = (uint32_t)c->start;
+    dec_step(M, E, &St, ids, 0, NULL, 1);
+    for (int r = 0; r < b; ++r) ids[r] = tgt;
+    for (int st = 1; st <= max_new; ++st) {
+        dec_step(M, E, &St, ids, st, NULL, 1);
+        for (int r = 0; r < b; ++r) {
+            float best = -INFINITY;
+            uint32_t bi = 0, tok;
+            const float *lg = St.logits + (size_t)r * c->V;
+            for (int i = 0; i < V1; ++i)
+                if (lg[sl_ids[i]] > best) { best = lg[sl_ids[i]]; bi = (uint32_t)i; }
+            for (int j = 0; j < S; ++j) {
+                const uint32_t id = j < (int)lens[r] ? src[(size_t)r * src_stride + j] : (uint32_t)c->pad;
+                for (int i = 0; i < d; ++i) erow[i] = deq(M->embed, id, i);
+                const float v = f32_out(erow, St.h + (size_t)r * d, d);
+                if (v > best) { best = v; bi = (uint32_t)(V1 + j); }
+            }
+            if (bi < (uint32_t)V1) tok = sl_ids[bi];
+            else {
+                const int j = (int)bi - V1;
+                tok = j < (int)lens[r] ? src[(size_t)r * src_stride + j] : (uint32_t)c->pad;
+            }
+            if (fin[r]) tok = (uint32_t)c->pad;
+            if (!force_steps && tok == (uint32_t)c->eos) fin[r] = 1;
+            ids[r] = tok;
+            out[(size_t)r * max_new + st - 1] = tok;
+        }
+    }
+    free(ids); free(fin); free(erow);
+    dstate_free(&St);
+    return max_new;
+}
+
 /* ------------------------------------------------------------------------ */
 /* Beam search (translator.rs:250-358)                                       */
 

@@ -101,3 +101,23 @@ def test_workloads_match_baseline_configs():
     assert all(4 <= t < 256206 for s in w.sources for t in s[1:-1])
     c1 = models.workload("c1")
     assert len(c1.sources) == 1 and len(c1.sources[0]) == 34 and c1.steps == 32
+
+
+def test_shortlist_metadata_and_reduced_head(model_dir):
+    """--fast-vocab shortlists (convert.rs:218-232): nllb.shortlist.<code> holds the
+    sorted ids, lm_head.<code>.weight the embedding rows of those ids, quantized
+    like the embedding (so its bytes are the embedding's rows)."""
+    from gguf import GGUFReader
+
+    V = models.config_of("mid").vocab_size
+    ids = models.synthetic_shortlist(V, 300, 7, [V - 2])
+    path = models.shortlist_model_path("mid", "q4_k_m", 0, {"xx_Test": ids}, model_dir)
+    meta, infos = G.read_metadata(path)
+    assert meta["nllb.shortlist.xx_Test"] == ids
+    d = models.config_of("mid").d_model
+    shape, ty, _ = infos["lm_head.xx_Test.weight"]
+    assert shape == (len(ids), d) and ty == infos["token_embd.weight"][1]
+    r = GGUFReader(path)
+    t = {x.name: np.asarray(x.data) for x in r.tensors}
+    emb, head = t["token_embd.weight"], t["lm_head.xx_Test.weight"]
+    assert np.array_equal(head.reshape(len(ids), -1), emb.reshape(V, -1)[ids])

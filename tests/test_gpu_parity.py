@@ -373,3 +373,50 @@ def test_small_batches_bit_exact(gpu, model, preset, n, step_kernel, monkeypatch
         f"max |diff| {np.abs(got_logits - want_logits).max()}"
     out, _ = eng.greedy(eng.encode(src), V - 2, 6, force=True)  # CUDA-graph replay
     np.testing.assert_array_equal(out, want_ids)
+
+
+def _bucket(n, lo, hi):
+    """engine.cu bucket(): the next power of two >= max(n, lo), at most hi, at least n."""
+    v = 1
+    while v < max(n, lo):
+        v <<= 1
+    return max(min(v, hi), n)
+
+
+@pytest.mark.parametrize("name,preset,n", [("wide", "q4_k_m", 1), ("wide", "q8_0", 3), ("wide", "q4_k_m", 40),
+                                           ("mid", "q4_k_m", 6)])
+def test_fast_vocab_shortlist_bit_exact(gpu, model_dir, name, preset, n):
+    """--fast-vocab (model.rs:556-612, malaga.cu:280-326): the LM head over the
+    shortlist's rows plus the source tokens' logits, the first maximum of the
+    concatenated list mapped back to its token; tokens equal the oracle's."""
+    cfg = models.config_of(name)
+    V = cfg.vocab_size
+    tgt = V - 2
+    ids = models.synthetic_shortlist(V, V // 8, 9, [tgt])
+    path = models.shortlist_model_path(name, preset, 0, {"xx_Test": ids}, model_dir)
+    src = models.random_sources(n, 3, 20, V, 31, src_tag=V - 1)
+    eng = Engine(path)
+    sl = eng.shortlist("xx_Test")
+    assert sl == 0 and eng.shortlist("yy_None") == -1
+    got, _ = eng.greedy(eng.encode(src), tgt, 8, shortlist=sl)
+    s_bucket = _bucket(max(len(r) for r in src), 16, cfg.max_position_embeddings)
+    want = oracle.Oracle(path).greedy_shortlist(src, tgt, 8, ids, s_bucket)
+    np.testing.assert_array_equal(got, want)
+    # graph replay of the cached shortlist state
+    again, _ = eng.greedy(eng.encode(src), tgt, 8, shortlist=sl)
+    np.testing.assert_array_equal(again, want)
+
+
+def test_fast_vocab_requires_the_start_tokens(gpu, model_dir):
+    """translator.rs:186-192: a shortlist without the forced tokens is refused by
+    the engine; Translator falls back to the full vocabulary."""
+    V = models.config_of("mid").vocab_size
+    ids = models.synthetic_shortlist(V, 200, 3, [])  # no target language token
+    path = models.shortlist_model_path("mid", "q4_k_m", 0, {"zz_Test": ids}, model_dir)
+    src = models.random_sources(2, 3, 10, V, 5, src_tag=V - 1)
+    eng = Engine(path)
+    with pytest.raises(MgbError):
+        eng.greedy(eng.encode(src), V - 2, 4, shortlist=eng.shortlist("zz_Test"))
+    t = Translator(eng)
+    full = t.generate(src, V - 2, GenOptions(max_new_tokens=6))
+    assert t.generate(src, V - 2, GenOptions(max_new_tokens=6, shortlist="zz_Test")) == full
