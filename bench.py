@@ -204,7 +204,7 @@ def run_reference(args, w):
     print(json.dumps(line), flush=True)
 
 
-def bench_b1(eng, torch, stream, info, hbm):
+def bench_b1(eng, torch, stream, info, hbm, sl=-1):
     """Config 1 as the reference's bench: p50 over 20 whole sentences (host ids ->
     encode -> 32 forced steps -> host ids) after 3 warm-ups; also the device time."""
     w = models.workload("c1")
@@ -219,7 +219,7 @@ def bench_b1(eng, torch, stream, info, hbm):
         t0 = time.perf_counter()
         e0.record(stream)
         b = eng.encode_array(ids, lens)
-        eng.greedy(b, models.TGT_TAG, w.steps, sync_every=4, force=True, out=out)
+        eng.greedy(b, models.TGT_TAG, w.steps, sync_every=4, force=True, out=out, shortlist=sl)
         e1.record(stream)
         torch.cuda.synchronize()
         t1 = time.perf_counter()
@@ -229,12 +229,12 @@ def bench_b1(eng, torch, stream, info, hbm):
             dev.append(e0.elapsed_time(e1))
     # the decode alone (graph replay), for the per-step roofline
     b = eng.encode_array(ids, lens)
-    eng.greedy(b, models.TGT_TAG, w.steps, sync_every=4, force=True, out=out)
+    eng.greedy(b, models.TGT_TAG, w.steps, sync_every=4, force=True, out=out, shortlist=sl)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     e0.record(stream)
     for _ in range(5):
-        eng.greedy(b, models.TGT_TAG, w.steps, sync_every=4, force=True, out=out)
+        eng.greedy(b, models.TGT_TAG, w.steps, sync_every=4, force=True, out=out, shortlist=sl)
     e1.record(stream)
     torch.cuda.synchronize()
     dec_ms = e0.elapsed_time(e1) / 5
@@ -317,6 +317,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-b1", action="store_true")
+    ap.add_argument("--fast-vocab", type=int, default=0, metavar="N",
+                    help="decode over a synthetic vocabulary shortlist of N ids (--fast-vocab: not exact, "
+                         "off by default); the LM-head roofline stays the full head's")
     ap.add_argument("--streams", type=int, default=None,
                     help="decode contexts (CUDA streams) per GPU for independent batches (dp.StreamPool); "
                          "default 4, 2 for c4 (3.3B: larger states)")
@@ -335,12 +338,22 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600),
                                 device_id=torch.device("cuda", local))
+    def model_file():
+        if not args.fast_vocab:
+            return models.model_path(w.model, w.preset, w.seed)
+        # the same weights plus a synthetic shortlist holding the forced tokens
+        V = models.config_of(w.model).vocab_size
+        return models.shortlist_model_path(
+            w.model, w.preset, w.seed,
+            {"syn_Latn": models.synthetic_shortlist(V, args.fast_vocab, 11, [models.TGT_TAG])})
+
     # rank 0 generates the model file; the others wait for it
     if rank == 0:
-        path = models.model_path(w.model, w.preset, w.seed)
+        model_file()
     if world > 1:
         dist.barrier()
-    path = models.model_path(w.model, w.preset, w.seed)
+    path = model_file()
+    sl = 0 if args.fast_vocab else -1
 
     # this rank's share: length-sorted batches of w.batch placed by LPT (a
     # single-batch workload is replicated on every rank instead)
@@ -369,7 +382,7 @@ def main():
     total_tokens = (len(w.sources) if scaling == "strong" else world * len(w.sources)) * steps
 
     def decode_step():
-        pool.map(lambda e, bo: e.greedy(bo[0], tgt, steps, sync_every=4, force=True, out=bo[1]),
+        pool.map(lambda e, bo: e.greedy(bo[0], tgt, steps, sync_every=4, force=True, out=bo[1], shortlist=sl),
                  list(zip(batches, outs)))
 
     for _ in range(max(3, args.warmup)):
@@ -416,7 +429,7 @@ def main():
     def e2e_one(e, item):
         (ih, lh), o = item
         b = e.encode_array(ih, lh)
-        e.greedy(b, tgt, steps, sync_every=4, force=True, out=o)
+        e.greedy(b, tgt, steps, sync_every=4, force=True, out=o, shortlist=sl)
         b.free()
 
     def e2e_step():
@@ -440,7 +453,7 @@ def main():
     b1 = None
     if rank == 0 and world == 1 and not args.no_b1:
         if w.model == "600m" and w.preset == "q4_k_m":
-            b1 = bench_b1(eng, torch, stream, info, hbm)
+            b1 = bench_b1(eng, torch, stream, info, hbm, sl)
 
     if rank == 0:
         line = {
@@ -454,6 +467,8 @@ def main():
                        "decode_steps": steps, "parallelism": f"dp{world}",
                        "step": "ms_per_step = one pass over the rank's batches (each a whole forced decode)",
                        "batches_this_rank": len(srcs), "streams_per_gpu": streams,
+                       **({"fast_vocab": f"shortlist of {args.fast_vocab} synthetic ids + source tokens (not exact)"}
+                          if args.fast_vocab else {}),
                        "l2": "weights (%.0f MB per decoder step) exceed the 126 MB L2" % (step_bytes / 1e6)},
             "gpu_launches": launches,
             "e2e": {"value": e2e_value, "unit": "tokens/s",

@@ -252,9 +252,10 @@ struct StaticState {
     std::vector<StepPhase> phase_host;
     std::string trace_path;
     // --fast-vocab (shortlist index >= 0): the rows' source ids [b][s] (pad past
-    // each row's length) and the best source-token logit of each row
+    // each row's length) and the best source-token logit of each 8 positions
     int sl = -1;
     uint32_t *src_ids = nullptr;
+    float *src_emb = nullptr;  // their embedding rows, f32 [b][s][d]
     float *src_v = nullptr;
     uint32_t *src_i = nullptr;
     int step_slots = 0, step_slot_bytes = 0, step_act_bytes = 0, step_ctas = 0;
@@ -1225,15 +1226,17 @@ static mgb_status finalize(mgb_ctx *c, StaticState *st, int parts, int force) {
         const mgb_ctx::Shortlist &sl = c->shortlists[st->sl];
         const size_t sh = (size_t)4 * g.d;
         cudaError_t e = allow_smem(src_logits_kernel, sh);
+        const int sparts = (st->s + 7) / 8;  // source partials per row (8 positions a CTA)
         if (e == cudaSuccess)
-            e = launch_pdl(src_logits_kernel, dim3(st->b), dim3(256), sh, c->stream, (const float *)st->x,
-                           c->dec_norm.g, c->dec_norm.b, g.d, c->embed, (const uint32_t *)st->src_ids, st->s,
-                           (int)sl.ids.size(), st->src_v, st->src_i);
+            e = launch_pdl(src_logits_kernel, dim3(st->b, sparts), dim3(256), sh, c->stream, (const float *)st->x,
+                           c->dec_norm.g, c->dec_norm.b, g.d, (const float *)st->src_emb, st->s, (int)sl.ids.size(),
+                           st->src_v, st->src_i);
         ++c->launches;
         if (e != cudaSuccess) return cuda_err(e, "source logits launch");
         e = launch_pdl(greedy_finalize_sl_kernel, dim3(1), dim3(threads), 0, c->stream, (const float *)st->part_v,
                        (const uint32_t *)st->part_i, parts, st->b, (const float *)st->src_v,
-                       (const uint32_t *)st->src_i, sl.d_ids, (int)sl.ids.size(), (const uint32_t *)st->src_ids, st->s,
+                       (const uint32_t *)st->src_i, sparts, sl.d_ids, (int)sl.ids.size(),
+                       (const uint32_t *)st->src_ids, st->s,
                        st->finished, st->ids, st->out, st->m, st->step, (uint32_t)g.eos, (uint32_t)g.pad, force);
         ++c->launches;
         return e == cudaSuccess ? MGB_OK : cuda_err(e, "finalize launch");
@@ -1772,8 +1775,9 @@ static mgb_status acquire_state(mgb_ctx *c, const mgb_batch *B, int max_new, boo
         c->cache.emplace_back(st);
         if (sl >= 0) {
             st->sl = sl;
-            for (void **p : {(void **)&st->src_ids, (void **)&st->src_v, (void **)&st->src_i}) {
-                const size_t n = p == (void **)&st->src_ids ? (size_t)4 * b * s : (size_t)4 * b;
+            for (void **p : {(void **)&st->src_ids, (void **)&st->src_v, (void **)&st->src_i, (void **)&st->src_emb}) {
+                // ids [b][s]; partials [b][ceil(s / 8)]; embeddings [b][s][d]
+                const size_t n = (size_t)4 * b * s * (p == (void **)&st->src_emb ? g.d : 1);
                 TRY(c->dalloc(p, n));
                 st->allocs.push_back(*p);
                 st->bytes += n;
@@ -1798,6 +1802,9 @@ static mgb_status acquire_state(mgb_ctx *c, const mgb_batch *B, int max_new, boo
         for (int i = 0; i < n; ++i)
             for (int j = 0; j < (int)B->lens[i / rep] && j < s; ++j) ids[(size_t)i * s + j] = B->src[(size_t)(i / rep) * B->s + j];
         CK(cudaMemcpyAsync(st->src_ids, ids.data(), 4 * ids.size(), cudaMemcpyHostToDevice, c->stream));
+        TRY(launch_check(c, [&] {
+            src_embed_kernel<<<c->sms * 4, 256, 0, c->stream>>>(c->embed, st->src_ids, b * s, g.d, st->src_emb);
+        }));
         CK(cudaStreamSynchronize(c->stream));
     }
     std::vector<uint32_t> lens(b, 1);

@@ -418,16 +418,25 @@ __global__ void greedy_finalize_kernel(const float *pv, const uint32_t *pi, int 
     if (threadIdx.x == 0) *step = s + 1;
 }
 
+// --fast-vocab: the source tokens' embedding rows E[src_ids] (dequantized, f32
+// [n][d]), made once per batch as the reference's src_emb (graph.rs:98-105).
+__global__ void src_embed_kernel(Matrix E, const uint32_t *src_ids, int n, int d, float *out) {
+    const size_t total = (size_t)n * d;
+    for (size_t k = blockIdx.x * (size_t)blockDim.x + threadIdx.x; k < total; k += (size_t)gridDim.x * blockDim.x)
+        out[k] = deq_elem(E, (int)src_ids[k / d], (int)(k % d));
+}
+
 // --fast-vocab (model.rs:595-604): the logits of the row's source tokens next
 // to the shortlist's. h = dec_norm(x[row]) (the LM head's LayerNorm: SUM32
 // statistics, ((x - mean) * rstd) * g + b), then for each source position j of
-// the state, dot(h, E[src_ids[row][j]]) in the F32 order (lane l's FMA chain
+// the state, dot(h, src_emb[row][j]) in the F32 order (lane l's FMA chain
 // over elements l, l+32, ..., then the butterfly at 16, 8, 4, 2, 1; row_dots in
 // malaga.cu:230-243 is fast-math and not restatable); the row's best (value,
-// V1 + j), the lowest j on ties. One CTA per row.
+// V1 + j), the lowest j on ties. CTA (row, p) takes positions 8p..8p+7 (a warp
+// each; the LayerNorm is recomputed per CTA) and writes partial p of the row.
 __global__ void __launch_bounds__(256) src_logits_kernel(const float *x, const float *gamma, const float *beta, int d,
-                                                         Matrix E, const uint32_t *src_ids, int S, int V1,
-                                                         float *best_v, uint32_t *best_i) {
+                                                         const float *src_emb, int S, int V1, float *best_v,
+                                                         uint32_t *best_i) {
     extern __shared__ __align__(16) float hs[];  // [d]
     __shared__ float stat[2];
     __shared__ float wv[8];
@@ -459,10 +468,12 @@ __global__ void __launch_bounds__(256) src_logits_kernel(const float *x, const f
     __syncthreads();
     float bv = kNegInf;
     uint32_t bi = 0xffffffffu;
-    for (int j = warp; j < S; j += 8) {
-        const int id = (int)src_ids[(size_t)row * S + j];
+    const int j = 8 * blockIdx.y + warp;
+    if (j < S) {
+        const float *e = src_emb + ((size_t)row * S + j) * d;
         float acc = 0.0f;
-        for (int i = lane; i < d; i += 32) acc = __fmaf_rn(deq_elem(E, id, i), hs[i], acc);
+#pragma unroll 8
+        for (int i = lane; i < d; i += 32) acc = __fmaf_rn(__ldg(e + i), hs[i], acc);
         argmax_merge(bv, bi, warp_sum_bf(acc), (uint32_t)(V1 + j));
     }
     if (lane == 0) {
@@ -472,19 +483,19 @@ __global__ void __launch_bounds__(256) src_logits_kernel(const float *x, const f
     __syncthreads();
     if (threadIdx.x == 0) {
         for (int w = 1; w < 8; ++w) argmax_merge(bv, bi, wv[w], wi[w]);
-        best_v[row] = bv;
-        best_i[row] = bi;
+        best_v[(size_t)row * gridDim.y + blockIdx.y] = bv;
+        best_i[(size_t)row * gridDim.y + blockIdx.y] = bi;
     }
 }
 
 // greedy_finalize_kernel over the virtual row concat(shortlist logits, source
 // logits) (malaga.cu:280-326 with vocab_map and src_ids): the LM head's
-// partials index the shortlist rows, the source candidate is index V1 + j;
-// the winner maps to sl_ids[i] or the row's source token j.
+// partials index the shortlist rows, the source partials index V1 + j; the
+// winner (lowest index on ties) maps to sl_ids[i] or the row's source token j.
 __global__ void greedy_finalize_sl_kernel(const float *pv, const uint32_t *pi, int parts, int rows, const float *sv,
-                                          const uint32_t *si, const uint32_t *sl_ids, int V1, const uint32_t *src_ids,
-                                          int S, uint8_t *finished, uint32_t *ids, uint32_t *out, int m,
-                                          uint32_t *step, uint32_t eos, uint32_t pad, int force) {
+                                          const uint32_t *si, int sparts, const uint32_t *sl_ids, int V1,
+                                          const uint32_t *src_ids, int S, uint8_t *finished, uint32_t *ids,
+                                          uint32_t *out, int m, uint32_t *step, uint32_t eos, uint32_t pad, int force) {
     pdl_launch_dependents();
     pdl_wait();
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -493,9 +504,10 @@ __global__ void greedy_finalize_sl_kernel(const float *pv, const uint32_t *pi, i
         float best = kNegInf;
         uint32_t bi = 0xffffffffu;
         for (int p = lane; p < parts; p += 32) argmax_merge(best, bi, pv[(size_t)row * parts + p], pi[(size_t)row * parts + p]);
+        for (int p = lane; p < sparts; p += 32)
+            argmax_merge(best, bi, sv[(size_t)row * sparts + p], si[(size_t)row * sparts + p]);
         warp_argmax(best, bi);
         if (lane == 0) {
-            argmax_merge(best, bi, sv[row], si[row]);
             uint32_t tok = bi < (uint32_t)V1           ? sl_ids[bi]
                            : bi < (uint32_t)(V1 + S) ? src_ids[(size_t)row * S + (bi - V1)]
                                                      : pad;  // (no finite candidate)
