@@ -363,6 +363,10 @@ struct mgb_ctx {
     // or f32 rows that a prep kernel quantizes (0, the default: the per-token
     // quantization in the epilogue measured slower on B200); MGB_FFN_Q8 overrides
     int ffn_q8 = 0;
+    // small-batch matmuls: CTAs per cluster sharing the q8_1 quantization of the
+    // input rows (1: each CTA quantizes all of them; 8 measured fastest on B200 at
+    // batch 1: 0.80 vs 0.88 ms per step); MGB_SMALL_CLUSTER overrides
+    int small_cluster = 8;
     int sms = 148;  // multiprocessor count of the device (one tensor-core CTA each)
     void *enc_ws = nullptr;  // encoder temporaries (grown on demand)
     size_t enc_ws_bytes = 0;
@@ -733,6 +737,27 @@ static cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, size_t
     return cudaLaunchKernelEx(&cfg, k, args...);
 }
 
+// launch_pdl with thread-block clusters of `cluster` CTAs along x (grid.x a multiple of it).
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl_cluster(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                                      int cluster, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = (unsigned)cluster;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = cluster > 1 ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, k, args...);
+}
+
 // Raises a kernel's dynamic shared-memory limit to the full 227 KB once
 // (before any graph capture: the first step of every shape runs eagerly).
 // (per device: one process may drive several GPUs, one context each)
@@ -787,7 +812,7 @@ template <int TYPE, int EPI, int MODE, int NC, int R>
 static cudaError_t small_launch(mgb_ctx *c, const SmallArgs &a, int grid, size_t smem) {
     auto kern = small_mm_kernel<TYPE, EPI, MODE, NC, NC <= 4 ? 4 : 2, R>;
     cudaError_t e = allow_smem(kern, smem);
-    return e == cudaSuccess ? launch_pdl(kern, dim3(grid), dim3(256), smem, c->stream, a) : e;
+    return e == cudaSuccess ? launch_pdl_cluster(kern, dim3(grid), dim3(256), smem, c->stream, a.cluster, a) : e;
 }
 
 template <int TYPE, int EPI, int MODE, int NC>
@@ -804,6 +829,10 @@ static mgb_status small_t(mgb_ctx *c, const GemvArgs &g, const PrepArgs &p, int 
     int grid = std::min(groups, 2 * c->sms);
     const int rpc = (groups + grid - 1) / grid * 8;
     grid = (W.Np + rpc - 1) / rpc;
+    // clusters share the activation quantization (CTAs past the rows only quantize);
+    // not the LM head, a long weight stream that runs slower in clusters (co-scheduling)
+    const int cluster = TYPE != T_F32 && EPI != EPI_ARGMAX && c->small_cluster > 1 ? c->small_cluster : 1;
+    grid = (grid + cluster - 1) / cluster * cluster;
     if (ctas) *ctas = grid;
     // launches of at most 8 activation rows (more only for F32 weights)
     for (int n0 = 0; n0 < g.rows; n0 += kSmallRows) {
@@ -820,6 +849,7 @@ static mgb_status small_t(mgb_ctx *c, const GemvArgs &g, const PrepArgs &p, int 
         a.err = c->d_err;
         a.wait_ns = c->test_wait_ns;
         a.withhold_chunk = c->test_withhold_chunk;
+        a.cluster = cluster;
         const size_t act = small_act_bytes(NC, W.K, TYPE, MODE), sb = (size_t)8 * R * RB;
         while (a.stages > 1 && (size_t)a.stages * sb + act > c->smem_optin) --a.stages;
         const size_t smem = (size_t)a.stages * sb + act;
@@ -2178,6 +2208,10 @@ mgb_status mgb_open(const char *path, int device, const mgb_options *opts, mgb_c
     if (const char *v = getenv("MGB_TEST_WITHHOLD_CHUNK")) c->test_withhold_chunk = atoi(v);
     if (const char *v = getenv("MGB_TEST_WITHHOLD_STEP")) c->test_withhold_step = atoi(v);
     if (const char *v = getenv("MGB_FFN_Q8")) c->ffn_q8 = atoi(v) != 0;
+    if (const char *v = getenv("MGB_SMALL_CLUSTER")) {
+        const int k = atoi(v);
+        c->small_cluster = k == 2 || k == 4 || k == 8 ? k : 1;
+    }
     cudaDeviceGetAttribute(&c->sms, cudaDevAttrMultiProcessorCount, device);
     if (c->sms <= 0) c->sms = 148;
     {

@@ -68,6 +68,10 @@ struct SmallArgs {
     // copy is withheld (-1: none), so that a bounded wait runs out.
     uint64_t wait_ns;
     int withhold_chunk;
+    // CTAs per thread-block cluster (1: none): the CTAs of a cluster share the
+    // q8_1 quantization of the input rows (each takes 1/cluster of the blocks and
+    // writes them into every CTA's shared memory)
+    int cluster;
 };
 
 __host__ __device__ inline size_t small_act_bytes(int NC, int K, int type, int mode) {
@@ -327,10 +331,14 @@ struct NoMark {
     __device__ void operator()(int) const {}
 };
 
-// `mark(k)` is called after each of its three stages (timing probes).
+// `mark(k)` is called after each of its three stages (timing probes). With
+// csize > 1 (a cluster of csize CTAs, this one of rank crank, all started) the
+// CTA quantizes blocks [crank * per, (crank + 1) * per) of the NC * K/32 and
+// stores each into the activations of every CTA of the cluster, then waits at a
+// cluster barrier: the same values as quantizing all of them, written once.
 template <int MODE, bool F32W, typename Mark = NoMark>
 __device__ void small_prologue(const PrepArgs &p, int n0, const SmAct &s, int NC, uint8_t *lnbuf, bool write_x,
-                               int nthr, CtaSync sync, Mark &&mark = Mark{}) {
+                               int nthr, CtaSync sync, Mark &&mark = Mark{}, int crank = 0, int csize = 1) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = nthr >> 5;
     const int K = p.K, T = K >> 5, rows = min(NC, p.rows - n0);
     const float *pos = nullptr;
@@ -390,16 +398,17 @@ __device__ void small_prologue(const PrepArgs &p, int n0, const SmAct &s, int NC
         sync();
         mark(2);
     }
-    // (row, block) tasks; loads of 8 tasks in flight per warp
+    // (row, block) tasks [lo, hi); loads of 8 tasks in flight per warp
     constexpr int PIPE = 8;
-    const int tasks = NC * T;
-    for (int base = warp; base < tasks; base += nw * PIPE) {
+    const int tasks = NC * T, per = (tasks + csize - 1) / csize;
+    const int lo = min(tasks, crank * per), hi = min(tasks, lo + per);
+    for (int base = lo + warp; base < hi; base += nw * PIPE) {
         float y[PIPE];
 #pragma unroll
         for (int u = 0; u < PIPE; ++u) {
             const int task = base + u * nw, n = task / T, i = 32 * (task % T) + lane;
             y[u] = 0.0f;
-            if (task < tasks && n < rows) {
+            if (task < hi && n < rows) {
                 if constexpr (MODE == PREP_PLAIN) y[u] = __ldcg(p.x + (size_t)(n0 + n) * K + i);
                 else y[u] = xs[(size_t)n * K + i];
             }
@@ -407,7 +416,7 @@ __device__ void small_prologue(const PrepArgs &p, int n0, const SmAct &s, int NC
 #pragma unroll
         for (int u = 0; u < PIPE; ++u) {
             const int task = base + u * nw;
-            if (task >= tasks) break;  // uniform across the warp
+            if (task >= hi) break;  // uniform across the warp
             const int n = task / T, t = task % T, i = 32 * t + lane;
             float v = y[u];
             if constexpr (MODE != PREP_PLAIN)
@@ -418,12 +427,21 @@ __device__ void small_prologue(const PrepArgs &p, int n0, const SmAct &s, int NC
             } else {
                 float d, sm;
                 const int q = q81_block(v, d, sm);
-                s.q[(size_t)n * K + i] = (int8_t)q;
-                if (lane == 0) s.d[n * T + t] = d;
+                if (csize == 1) {
+                    s.q[(size_t)n * K + i] = (int8_t)q;
+                    if (lane == 0) s.d[n * T + t] = d;
+                } else {
+                    const uint32_t aq = smem_u32(s.q + (size_t)n * K + i), ad = smem_u32(s.d + n * T + t);
+                    for (int c = 0; c < csize; ++c) {
+                        st_cluster_u8(aq, (uint32_t)c, (uint32_t)(q & 0xff));
+                        if (lane == 0) st_cluster_f32(ad, (uint32_t)c, d);
+                    }
+                }
             }
         }
     }
-    sync();
+    if (csize > 1) cluster_sync();
+    else sync();
     mark(3);
 }
 
@@ -486,6 +504,10 @@ __global__ void __launch_bounds__(256) small_mm_kernel(const __grid_constant__ S
         const int row = r0 + warp + 8 * r;
         if (pre && W.bias && warp + 8 * r < r1 - r0 && row < W.N) pb[r] = __ldg(W.bias + row);
     }
+    // a cluster's CTAs write into each other's shared memory: all must have started
+    const int csize = STAGED ? A.cluster : 1;
+    const uint32_t crank = csize > 1 ? cluster_rank() : 0u;
+    if (csize > 1) cluster_sync();
     pdl_launch_dependents();
     pdl_wait();
     int step = 0;
@@ -504,7 +526,8 @@ __global__ void __launch_bounds__(256) small_mm_kernel(const __grid_constant__ S
     s.d = reinterpret_cast<float *>(act + (size_t)NC * K);
     s.xf = reinterpret_cast<float *>(act + (size_t)NC * K + (size_t)NC * (K / 32) * 4);
     uint8_t *lnbuf = reinterpret_cast<uint8_t *>(s.xf) + (TYPE == T_F32 ? (size_t)NC * K * 4 : 0);
-    small_prologue<MODE, TYPE == T_F32>(A.p, n0, s, NC, lnbuf, blockIdx.x == 0, blockDim.x, CtaSync{0, 0});
+    small_prologue<MODE, TYPE == T_F32>(A.p, n0, s, NC, lnbuf, blockIdx.x == 0, blockDim.x, CtaSync{0, 0}, NoMark{},
+                                        (int)crank, csize);
 
     float bv = kNegInf;
     uint32_t bi = 0xffffffffu;

@@ -93,4 +93,31 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64
     }
 }
 
+// Thread-block clusters: this CTA's rank and the cluster size; a full cluster
+// barrier (hardware; every thread of every CTA of the cluster arrives, release /
+// acquire ordering of shared-memory writes across the cluster).
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Stores into the shared memory of CTA `rank` of the cluster at the offset of
+// this CTA's shared address `a` (distributed shared memory).
+__device__ __forceinline__ void st_cluster_u8(uint32_t a, uint32_t rank, uint32_t v) {
+    uint32_t ra;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(rank));
+    asm volatile("st.shared::cluster.u8 [%0], %1;" ::"r"(ra), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void st_cluster_f32(uint32_t a, uint32_t rank, float v) {
+    uint32_t ra;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(rank));
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
+}
+
 }  // namespace mgb
