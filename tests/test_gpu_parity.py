@@ -352,6 +352,24 @@ def test_beam_one_equals_greedy_on_device(gpu, model):
     assert [[int(x) for x in out[i, : lens[i]]] for i in range(len(src))] == greedy
 
 
+@pytest.mark.parametrize("cluster", ["1", "2", "4"])
+@pytest.mark.parametrize("n", [1, 6])
+def test_small_batch_cluster_sizes_bit_exact(gpu, model, n, cluster, monkeypatch):
+    """The small-batch matmuls share their input's q8_1 quantization across a
+    cluster of CTAs (8 by default, MGB_SMALL_CLUSTER); every cluster size, and
+    none, gives the oracle's tokens and logits bit for bit."""
+    monkeypatch.setenv("MGB_SMALL_CLUSTER", cluster)
+    monkeypatch.setenv("MGB_STEP_KERNEL", "0")
+    path = model("wide", "q4_k_m")
+    V = models.config_of("wide").vocab_size
+    src = mid_sentences(V, n=n, seed=23)
+    want_ids, want_logits = oracle.Oracle(path).greedy(src, V - 2, 4, force=True, logits=True)
+    eng = Engine(path)
+    got_ids, got_logits = eng.greedy_logits(eng.encode(src), V - 2, 4, force=True)
+    np.testing.assert_array_equal(got_ids, want_ids)
+    assert np.array_equal(got_logits.view(np.uint32), want_logits.view(np.uint32))
+
+
 @pytest.mark.parametrize("step_kernel", ["1", "0"])
 @pytest.mark.parametrize("preset", ["q4_k_m", "q8_0"])
 @pytest.mark.parametrize("n", [1, 2, 3, 5, 8])
