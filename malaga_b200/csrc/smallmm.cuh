@@ -316,9 +316,9 @@ __device__ __forceinline__ float small_input(const PrepArgs &p, const float *pos
         return __ldcg(p.x + (size_t)n * p.K + i);
 }
 
-// A CTA-wide barrier over the first `n` threads: __syncthreads when id is 0,
-// else named barrier `id` (the persistent step kernel's compute warps, whose
-// producer warp does not take part).
+// A barrier over the prologue's threads: __syncthreads when id is 0, else
+// named barrier `id` over the first `n` threads (a caller whose other warps do
+// not take part in the prologue).
 struct CtaSync {
     int id, n;
     __device__ __forceinline__ void operator()() const {
