@@ -256,6 +256,58 @@ def bench_b1(eng, torch, stream, info, hbm, sl=-1):
     }
 
 
+def run_c3(args):
+    """Config 3: beam search (beam 4, length penalty 1.0) over 16 sources of 48
+    tokens, at most 96 steps, NLLB-1.3B q4_k_m (random init, seed 2), through
+    Engine.encode_array + Engine.beam (mgb_encode + mgb_beam) from host ids: the
+    best hypotheses' tokens per second of device time (events around each whole
+    call pair on the engine's stream), after --warmup untimed runs."""
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    import torch
+
+    from malaga_b200 import Engine
+
+    w = models.workload("c3")
+    path = models.model_path(w.model, w.preset, w.seed)
+    eng = Engine(path)
+    stream = torch.cuda.ExternalStream(eng.stream)
+    ids = np.array(w.sources, np.uint32)
+    lens = np.array([len(r) for r in w.sources], np.uint32)
+
+    def once():
+        b = eng.encode_array(ids, lens)
+        out, olens = eng.beam(b, models.TGT_TAG, 4, w.steps, 1.0)
+        b.free()
+        return int(olens.sum())
+
+    for _ in range(max(3, args.warmup)):
+        once()
+    ms, toks, wall = [], 0, time.perf_counter()
+    for _ in range(args.steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        toks += once()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms.append(e0.elapsed_time(e1))
+    wall = time.perf_counter() - wall
+    total = sum(ms) / 1e3
+    line = {"metric": "C3: beam-4 decoded tokens/s NLLB-1.3B q4_k_m b16", "value": toks / total, "unit": "tokens/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": statistics.median(ms),
+            "higher_is_better": True, "data": "synthetic",
+            "beam_rows_steps_per_s": 16 * 4 * w.steps * args.steps / total,
+            "e2e": {"value": toks / wall, "unit": "tokens/s", "h2d_bytes_per_step": int(ids.nbytes + lens.nbytes),
+                    "d2h_bytes_per_step": int(16 * w.steps * 4 + 16 * 4)},
+            "config": {"workload": "c3: NLLB-1.3B q4_k_m (random init, seed 2), beam 4, length penalty 1.0, 16 "
+                                   "sources of 48 ids, at most 96 steps (64 beam rows per step)",
+                       "step": "ms_per_step = one encode + beam search of the batch"}}
+    print(json.dumps(line), flush=True)
+    eng.close()
+
+
 def run_c5(args):
     """Config 5: server dynamic batching (malaga_b200/server.py) on NLLB-600M
     q4_k_m over --gpus GPUs of one process (--streams worker threads, each with
@@ -313,7 +365,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="dp600", choices=["dp600", "c2q4", "c2", "c1", "c5", "c4"])
+    ap.add_argument("--workload", default="dp600", choices=["dp600", "c2q4", "c2", "c1", "c5", "c4", "c3"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-b1", action="store_true")
@@ -326,6 +378,8 @@ def main():
     args = ap.parse_args()
     if args.workload == "c5" and args.impl == "ours":
         return run_c5(args)
+    if args.workload == "c3" and args.impl == "ours":
+        return run_c3(args)
     w = models.workload(args.workload)
     if args.impl == "reference":
         return run_reference(args, w)

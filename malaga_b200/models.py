@@ -140,6 +140,8 @@ def workload(key: str) -> Workload:
         return Workload("c2q4", "600m", "q4_k_m", 0, 64, 64, src)
     if key == "c5":  # server simulation: 4096 single-sentence requests, lengths lognormal(24), 4..96
         return Workload("c5", "600m", "q4_k_m", 0, 64, 0, lognormal_sources(4096, 24, 4, 96, V, 4))
+    if key == "c3":  # 1.3B q4_k_m (seed 2), beam 4 over 16 sources of 48 tokens, at most 96 steps
+        return Workload("c3", "1.3b", "q4_k_m", 2, 16, 96, random_sources(16, 48, 48, V, 2, fixed_len=48))
     if key == "c4":  # 3.3B q4_k_m (seed 3), 1024 sentences lognormal(28) clipped 8..128, batches of 128,
         # 128 forced steps, partitioned over the GPUs like dp600
         return Workload("c4", "3.3b", "q4_k_m", 3, 128, 128, lognormal_sources(1024, 28, 8, 128, V, 3))
