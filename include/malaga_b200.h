@@ -145,6 +145,15 @@ MGB_API mgb_status mgb_greedy_shortlist(mgb_ctx *ctx, const mgb_batch *batch, ui
 MGB_API mgb_status mgb_beam(mgb_ctx *ctx, const mgb_batch *batch, uint32_t tgt_lang, uint32_t k, float length_penalty,
                     uint32_t max_new, uint32_t *out_ids, uint32_t *out_lens);
 
+/* The device half of one beam-search step on caller logits: per row,
+ * log_softmax (model.rs:615-617) and the k largest values with their indices
+ * (translator.rs:343-358, k argmax passes: larger value first, lower index on
+ * ties), on the kernel mgb_beam runs. logits: host [rows, vocab] f32;
+ * vals / idx: host [rows, k]. A row with fewer than k non-NaN values pads with
+ * (-inf, 0); NaN logits are never selected. k in 1..8. */
+MGB_API mgb_status mgb_log_softmax_topk(mgb_ctx *ctx, const float *logits, uint32_t rows, uint32_t vocab, uint32_t k,
+                                float *vals, uint32_t *idx);
+
 /* Frees every cached static state and CUDA graph (GraphCache::clear, graph.rs:193-200). */
 MGB_API mgb_status mgb_clear_cache(mgb_ctx *ctx);
 

@@ -44,6 +44,7 @@ SIGNATURES = {
     "mgb_shortlist_find": (_i, [_vp, ctypes.c_char_p]),
     "mgb_greedy_shortlist": (_i, [_vp, _vp, _u32, _i, _u32, _u32, _i, _vp, _vp]),
     "mgb_beam": (_i, [_vp, _vp, _u32, _u32, ctypes.c_float, _u32, _vp, _vp]),
+    "mgb_log_softmax_topk": (_i, [_vp, _vp, _u32, _u32, _u32, _vp, _vp]),
     "mgb_greedy_logits": (_i, [_vp, _vp, _u32, _u32, _i, _vp, _vp]),
     "mgb_clear_cache": (_i, [_vp]),
     "mgb_cuda_stream": (_vp, [_vp]),

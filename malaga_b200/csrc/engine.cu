@@ -1859,7 +1859,8 @@ static mgb_status ensure_beam(mgb_ctx *c, StaticState *st) {
         st->bytes += n;
         return MGB_OK;
     };
-    TRY(A((void **)&st->beam_logits, (size_t)4 * b * g.V));
+    // + 16 bytes: the top-k kernel's bulk copies round a row's end up to 16 bytes
+    TRY(A((void **)&st->beam_logits, (size_t)4 * b * g.V + 16));
     TRY(A((void **)&st->beam_vals, (size_t)4 * b * 8));
     TRY(A((void **)&st->beam_idx, (size_t)4 * b * 8));
     TRY(A((void **)&st->beam_from, (size_t)4 * b));
@@ -1871,6 +1872,33 @@ static mgb_status ensure_beam(mgb_ctx *c, StaticState *st) {
         TRY(A((void **)&st->cv32[l], (size_t)4 * b * H * st->s * hd));
     }
     return MGB_OK;
+}
+
+// Log-softmax statistics and top-k of rows of logits on the device
+// (beam_topk_kernel). `logits` holds rows x V floats and at least 16 bytes
+// more (the kernel's bulk copies round a row's end up to 16 bytes).
+template <int K>
+static mgb_status beam_topk_k(mgb_ctx *c, const float *logits, int rows, int V, float *vals, uint32_t *idx) {
+    cudaError_t e = allow_smem(beam_topk_kernel<K>, kTopkSmem);
+    if (e == cudaSuccess) {
+        beam_topk_kernel<K><<<rows, kTopkThreads, kTopkSmem, c->stream>>>(logits, V, vals, idx, c->d_err);
+        e = cudaGetLastError();
+    }
+    ++c->launches;
+    return e == cudaSuccess ? MGB_OK : cuda_err(e, "top-k launch");
+}
+
+static mgb_status beam_topk(mgb_ctx *c, const float *logits, int rows, int V, int k, float *vals, uint32_t *idx) {
+    switch (k) {
+        case 1: return beam_topk_k<1>(c, logits, rows, V, vals, idx);
+        case 2: return beam_topk_k<2>(c, logits, rows, V, vals, idx);
+        case 3: return beam_topk_k<3>(c, logits, rows, V, vals, idx);
+        case 4: return beam_topk_k<4>(c, logits, rows, V, vals, idx);
+        case 5: return beam_topk_k<5>(c, logits, rows, V, vals, idx);
+        case 6: return beam_topk_k<6>(c, logits, rows, V, vals, idx);
+        case 7: return beam_topk_k<7>(c, logits, rows, V, vals, idx);
+        default: return beam_topk_k<8>(c, logits, rows, V, vals, idx);
+    }
 }
 
 // Rust's f32::total_cmp key (IEEE total order as a signed integer).
@@ -1942,18 +1970,7 @@ static mgb_status run_beam(mgb_ctx *c, const mgb_batch *B, uint32_t tgt, int k, 
     };
     std::vector<Cand> cands((size_t)k * k);
     for (int step = 1; step <= max_new; ++step) {
-        TRY(launch_check(c, [&] {
-            switch (k) {
-                case 1: beam_topk_kernel<1><<<rows, 256, 0, c->stream>>>(st->beam_logits, V, st->beam_vals, st->beam_idx); break;
-                case 2: beam_topk_kernel<2><<<rows, 256, 0, c->stream>>>(st->beam_logits, V, st->beam_vals, st->beam_idx); break;
-                case 3: beam_topk_kernel<3><<<rows, 256, 0, c->stream>>>(st->beam_logits, V, st->beam_vals, st->beam_idx); break;
-                case 4: beam_topk_kernel<4><<<rows, 256, 0, c->stream>>>(st->beam_logits, V, st->beam_vals, st->beam_idx); break;
-                case 5: beam_topk_kernel<5><<<rows, 256, 0, c->stream>>>(st->beam_logits, V, st->beam_vals, st->beam_idx); break;
-                case 6: beam_topk_kernel<6><<<rows, 256, 0, c->stream>>>(st->beam_logits, V, st->beam_vals, st->beam_idx); break;
-                case 7: beam_topk_kernel<7><<<rows, 256, 0, c->stream>>>(st->beam_logits, V, st->beam_vals, st->beam_idx); break;
-                default: beam_topk_kernel<8><<<rows, 256, 0, c->stream>>>(st->beam_logits, V, st->beam_vals, st->beam_idx); break;
-            }
-        }));
+        TRY(beam_topk(c, st->beam_logits, rows, V, k, st->beam_vals, st->beam_idx));
         CK(cudaMemcpyAsync(vals.data(), st->beam_vals, 4 * vals.size(), cudaMemcpyDeviceToHost, c->stream));
         CK(cudaMemcpyAsync(idx.data(), st->beam_idx, 4 * idx.size(), cudaMemcpyDeviceToHost, c->stream));
         CK(cudaStreamSynchronize(c->stream));
@@ -2381,6 +2398,38 @@ mgb_status mgb_beam(mgb_ctx *c, const mgb_batch *B, uint32_t tgt, uint32_t k, fl
                                                 (unsigned long long)B->b * k);
     CK(cudaSetDevice(c->device));
     return run_beam(c, B, tgt, (int)k, length_penalty, (int)max_new, out_ids, out_lens);
+}
+
+mgb_status mgb_log_softmax_topk(mgb_ctx *c, const float *logits, uint32_t rows, uint32_t vocab, uint32_t k,
+                                float *vals, uint32_t *idx) {
+    if (!c || !logits || !vals || !idx) return set_err(MGB_ERR_INVALID, "null argument");
+    if (rows == 0 || vocab == 0) return set_err(MGB_ERR_INVALID, "empty input");
+    if (k < 1 || k > 8) return set_err(MGB_ERR_INVALID, "k = %u outside 1..8", k);
+    if ((uint64_t)rows * vocab > (1ull << 31)) return set_err(MGB_ERR_INVALID, "rows x vocab exceeds 2^31");
+    CK(cudaSetDevice(c->device));
+    const size_t n = (size_t)rows * vocab;
+    void *d_x = nullptr, *d_v = nullptr, *d_i = nullptr;
+    mgb_status s = c->dalloc(&d_x, 4 * n + 16);
+    if (s == MGB_OK) s = c->dalloc(&d_v, (size_t)4 * rows * k);
+    if (s == MGB_OK) s = c->dalloc(&d_i, (size_t)4 * rows * k);
+    uint32_t derr = 0;
+    if (s == MGB_OK) {
+        cudaMemcpyAsync(d_x, logits, 4 * n, cudaMemcpyHostToDevice, c->stream);
+        s = beam_topk(c, (const float *)d_x, (int)rows, (int)vocab, (int)k, (float *)d_v, (uint32_t *)d_i);
+    }
+    if (s == MGB_OK) {
+        cudaMemcpyAsync(vals, d_v, (size_t)4 * rows * k, cudaMemcpyDeviceToHost, c->stream);
+        cudaMemcpyAsync(idx, d_i, (size_t)4 * rows * k, cudaMemcpyDeviceToHost, c->stream);
+        cudaMemcpyAsync(&derr, c->d_err, 4, cudaMemcpyDeviceToHost, c->stream);
+        if (cudaStreamSynchronize(c->stream) != cudaSuccess) s = cuda_err(cudaGetLastError(), "top-k");
+    }
+    if (s == MGB_OK && derr) {
+        cudaMemsetAsync(c->d_err, 0, 4, c->stream);
+        s = set_err(MGB_ERR_CUDA, "a device-side wait ran out of time (flags %u)", derr);
+    }
+    for (void *p : {d_x, d_v, d_i})
+        if (p) cudaFree(p);
+    return s;
 }
 
 mgb_status mgb_greedy_logits(mgb_ctx *c, const mgb_batch *B, uint32_t tgt, uint32_t max_new, int force,

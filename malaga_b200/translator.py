@@ -156,6 +156,18 @@ class Engine:
                                    lens.ctypes.data))
         return out, lens
 
+    def log_softmax_topk(self, logits: np.ndarray, k: int) -> tuple[np.ndarray, np.ndarray]:
+        """Per row of `logits` [rows, vocab] f32: log_softmax and its k largest
+        values with their indices (translator.rs:343-358), on beam search's
+        device kernel. Returns (vals [rows, k] f32, idx [rows, k] u32)."""
+        x = np.ascontiguousarray(logits, np.float32)
+        rows, vocab = x.shape
+        vals = np.empty((rows, k), np.float32)
+        idx = np.empty((rows, k), np.uint32)
+        check(_lib.load().mgb_log_softmax_topk(self.h, x.ctypes.data, rows, vocab, k, vals.ctypes.data,
+                                               idx.ctypes.data))
+        return vals, idx
+
     def greedy_logits(self, batch: Batch, tgt_lang: int, max_new: int, force: bool = False):
         out = np.empty((batch.size, max_new), np.uint32)
         logits = np.empty((max_new, batch.size, self.info["vocab_size"]), np.float32)

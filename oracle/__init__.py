@@ -60,6 +60,7 @@ def lib():
         L.orc_matmul.argtypes = [i, vp, ctypes.c_long, ctypes.c_long, vp, i, i, i, vp]
         L.orc_matmul.restype = i
         L.orc_quantize_q81.argtypes = [vp, i, i, vp, vp, vp]
+        L.orc_log_softmax_topk.argtypes = [vp, i, i, i, vp, vp]
         _lib = L
     return _lib
 
@@ -176,6 +177,17 @@ def quantize_q81(x: np.ndarray):
     s = np.zeros((rows, k // 32), np.float32)
     lib().orc_quantize_q81(x.ctypes.data, rows, k, q.ctypes.data, d.ctypes.data, s.ctypes.data)
     return q, d, s
+
+
+def log_softmax_topk(x: np.ndarray, k: int) -> tuple[np.ndarray, np.ndarray]:
+    """Per row of x [rows, n] f32: log_softmax (SUM32 order) and its top k by k
+    argmax passes (translator.rs:343-358). Returns (vals [rows, k], idx [rows, k])."""
+    x = np.ascontiguousarray(x, np.float32)
+    rows, n = x.shape
+    vals = np.empty((rows, k), np.float32)
+    idx = np.empty((rows, k), np.uint32)
+    lib().orc_log_softmax_topk(x.ctypes.data, rows, n, k, vals.ctypes.data, idx.ctypes.data)
+    return vals, idx
 
 
 def strip_eos(row, eos: int) -> list[int]:

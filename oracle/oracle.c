@@ -1151,6 +1151,35 @@ static void log_softmax_row(const float *x, int n, float *y, float *tmp) {
     for (int i = 0; i < n; ++i) y[i] = (x[i] - mx) - ls;
 }
 
+/* top-k of one row by k argmax passes (translator.rs:343-358): highest value,
+ * lowest index on ties, each index taken once. */
+static void topk_row(const float *lp, int n, int k, float *vals, uint32_t *idx) {
+    for (int j = 0; j < k; ++j) {
+        float best = -INFINITY;
+        uint32_t bi = 0;
+        int found = 0;
+        for (int i = 0; i < n; ++i) {
+            int taken = 0;
+            for (int q = 0; q < j; ++q) taken |= idx[q] == (uint32_t)i;
+            if (taken) continue;
+            if (!found || lp[i] > best) { best = lp[i]; bi = (uint32_t)i; found = 1; }
+        }
+        vals[j] = best;
+        idx[j] = bi;
+    }
+}
+
+/* log_softmax + top-k of rows x n logits (the device half of a beam step). */
+ORC_EXPORT void orc_log_softmax_topk(const float *x, int rows, int n, int k, float *vals, uint32_t *idx) {
+    float *y = malloc((size_t)n * sizeof(float)), *tmp = malloc((size_t)n * sizeof(float));
+    for (int r = 0; r < rows; ++r) {
+        log_softmax_row(x + (size_t)r * n, n, y, tmp);
+        topk_row(y, n, k, vals + (size_t)r * k, idx + (size_t)r * k);
+    }
+    free(y);
+    free(tmp);
+}
+
 /*
  * Batched beam search with beam k and length penalty lp; returns the best
  * hypothesis per sentence into out[b, max_new] (padded with pad) and its
@@ -1204,20 +1233,7 @@ ORC_EXPORT int orc_beam(orc_model *M, orc_enc *E, uint32_t tgt, int k, float lp,
     for (int step = 1; step <= max_new; ++step) {
         for (int r = 0; r < rows; ++r) {
             log_softmax_row(S.logits + (size_t)r * V, V, lp_row, tmp);
-            /* top-k by k argmax passes: highest value, lowest index on ties */
-            for (int j = 0; j < k; ++j) {
-                float best = -INFINITY;
-                uint32_t bi = 0;
-                int found = 0;
-                for (int i = 0; i < V; ++i) {
-                    int taken = 0;
-                    for (int q = 0; q < j; ++q) taken |= idx[(size_t)r * k + q] == (uint32_t)i;
-                    if (taken) continue;
-                    if (!found || lp_row[i] > best) { best = lp_row[i]; bi = (uint32_t)i; found = 1; }
-                }
-                vals[(size_t)r * k + j] = best;
-                idx[(size_t)r * k + j] = bi;
-            }
+            topk_row(lp_row, V, k, vals + (size_t)r * k, idx + (size_t)r * k);
         }
         int nr = 0;
         for (int s = 0; s < b; ++s) {

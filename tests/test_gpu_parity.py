@@ -341,6 +341,40 @@ def test_beam_config3_row_shape_full_vocabulary(gpu, model):
     assert got == [[int(t) for t in r] for r in want]
 
 
+def _topk_rows(rng, V):
+    """Adversarial logits rows of width V (finite or partly -inf)."""
+    rows = [rng.standard_normal(V).astype(np.float32) * 4.0,                  # spread, one clear leader
+            rng.integers(-3, 4, V).astype(np.float32),                         # massive ties
+            np.full(V, 1.5, np.float32),                                       # all equal
+            (rng.standard_normal(V) * 100.0).astype(np.float32)]              # most exps underflow
+    r = rng.standard_normal(V).astype(np.float32)
+    r[rng.random(V) < 0.9] = -np.inf                                           # mostly -inf
+    r[0] = 0.25
+    rows.append(r)
+    r = np.full(V, -np.inf, np.float32)
+    r[V - 1] = -7.0                                                            # one finite value, last index
+    rows.append(r)
+    return np.stack(rows)
+
+
+@pytest.mark.parametrize("V", [1, 5, 31, 33, 4096, 4097, 12289, 256206, 600000])
+@pytest.mark.parametrize("k", [1, 4, 8])
+def test_log_softmax_topk_kernel_bit_exact(gpu, model, V, k):
+    """The beam step's device half (log_softmax + top-k, translator.rs:343-358)
+    on caller logits: values as f32 bit patterns and indices equal the oracle's
+    on ties, all-equal rows, underflowing exponentials, -inf runs, rows shorter
+    than k (padded with (-inf, 0)), rows that start off a 16-byte boundary (odd
+    rows of odd V), one to 147 streamed chunks and rows too long to keep chunk
+    maxima (600000 > 128 chunks: every chunk scanned)."""
+    rng = np.random.default_rng(V * 10 + k)
+    x = _topk_rows(rng, V)
+    want_v, want_i = oracle.log_softmax_topk(x, k)
+    eng = Engine(model("tiny", "q8_0"))
+    got_v, got_i = eng.log_softmax_topk(x, k)
+    np.testing.assert_array_equal(got_i, want_i)
+    assert np.array_equal(got_v.view(np.uint32), want_v.view(np.uint32)), (got_v, want_v)
+
+
 def test_beam_one_equals_greedy_on_device(gpu, model):
     """pipeline.rs:60-69: beam 1 gives the greedy output."""
     path = model("tiny", "q8_0")

@@ -62,6 +62,22 @@ def test_exp_and_log_accuracy():
     assert (np.abs(lg - rl) / np.spacing(np.abs(rl).astype(np.float32))).max() <= 2.0
 
 
+def test_log_softmax_topk_semantics():
+    """translator.rs:343-358: k argmax passes -- larger value first, lower index
+    on ties, each index once; log_softmax values match float64 to a few ulp."""
+    rng = np.random.default_rng(5)
+    x = np.stack([rng.integers(-2, 3, 1000).astype(np.float32), rng.standard_normal(1000).astype(np.float32)])
+    vals, idx = oracle.log_softmax_topk(x, 6)
+    for r in range(2):
+        want = sorted(range(1000), key=lambda i: (-x[r, i], i))[:6]
+        assert list(idx[r]) == want
+        ref = x[r].astype(np.float64) - x[r].max()
+        ref = ref - np.log(np.exp(ref).sum())
+        np.testing.assert_allclose(vals[r], ref[want], rtol=0, atol=1e-5)
+    v, i = oracle.log_softmax_topk(np.array([[3.0, 1.0]], np.float32), 4)  # fewer values than k
+    assert list(i[0]) == [0, 1, 0, 0] and np.isneginf(v[0, 2:]).all()
+
+
 def _tiny_src():
     return [[254] + C.tiny_sentence(3 + 4 * i, i) + [2] for i in range(6)]
 
