@@ -69,8 +69,10 @@ class StreamPool:
     step at batch sizes up to 64 is a chain of dependent, latency-bound launches
     that leaves SMs idle between kernels; the chains of a few batches
     interleave on the SMs (measured on B200 at batch 64, 16 batches: 1.25x the
-    tokens/s with 2 streams, 1.33x with 3, 1.40x with 4). Item i of a map runs
-    on context i % streams."""
+    tokens/s with 2 streams, 1.33x with 3, 1.40x with 4). With more than one
+    context open on a device the tensor-core matmuls pick SM-time-efficient
+    token tiles (at least 32 tokens), which takes 4 streams to 1.56x and 8 to
+    1.85x the one-stream rate. Item i of a map runs on context i % streams."""
 
     def __init__(self, gguf_path: str, device: int = 0, streams: int = 3, **engine_kw):
         from .translator import Engine
