@@ -193,6 +193,13 @@ struct Geo {
     static constexpr int oEND = RS * STAGE + AG * AGB;
 };
 
+// Tokens per TMEM read batch of the Q6_K epilogue (four values per token and
+// unit): 8 leaves the 168-register epilogue room to interleave token pairs
+// (batch-64 LM head 253.5 -> 250.6 us, A/B on one B200; 16 for the other types).
+#ifndef MGB_TC_Q6_CH
+#define MGB_TC_Q6_CH 8
+#endif
+
 constexpr int kThreads = 384;  // 12 warps
 constexpr int kProducerWarp = 10, kMmaWarp = 11;
 // Epilogue warps 0..EW-1 and converter warps EW..9: narrow tiles (NT <= 16)
@@ -668,7 +675,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1) gemm_tc_kernel(const __grid_c
                         const int u = G::Q8 ? 8 * s + b : 4 * s + b / 2;  // unit index in the row
                         // TMEM -> registers in chunks of up to 16 tokens: the unit's
                         // blocks (and Q6_K halves) loaded together, then one wait
-                        constexpr int CH = NH < 16 ? NH : 16, NC = NH / CH;
+                        constexpr int CHM = G::Q6 ? MGB_TC_Q6_CH : 16;
+                        constexpr int CH = NH < CHM ? NH : CHM, NC = NH / CH;
 #pragma unroll
                         for (int c = 0; c < NC; ++c) {
                             int va0[CH], vb0[CH], va1[CH], vb1[CH];
