@@ -41,11 +41,13 @@ constexpr size_t kTopkSmem = ((size_t)kTopkNs * kTopkSlot + 2 * kTopkCh + (size_
 //     largest chunk maxima are K elements >= that maximum). Rows of more than
 //     kTopkMaxCh chunks scan every chunk.
 // NaN logits are never selected; a row with fewer than K selectable values
-// pads with (-inf, 0). A bulk copy that does not land within the wait limit
-// sets flag 8 in *err and ends the CTA without output.
+// pads with (-inf, 0). A bulk copy that does not land within wait_ns sets
+// flag 8 in *err and ends the CTA without output (`withhold`: a test hook, the
+// ring position whose copy row 0 never issues; -1 in use).
 template <int K>
 __global__ void __launch_bounds__(kTopkThreads, 1)
-    beam_topk_kernel(const float *logits, int V, float *vals, uint32_t *idx, uint32_t *err) {
+    beam_topk_kernel(const float *logits, int V, float *vals, uint32_t *idx, uint32_t *err, uint64_t wait_ns,
+                     int withhold) {
     extern __shared__ __align__(16) float tk_sm[];
     float *ring = tk_sm;                           // [kTopkNs][kTopkSlot]
     float *ebuf = ring + kTopkNs * kTopkSlot;      // [2][kTopkCh] exponentials
@@ -67,6 +69,7 @@ __global__ void __launch_bounds__(kTopkThreads, 1)
     // the top-k pass over its chunk list (issued once the list is known)
     int issued = 0;  // thread 0: copies issued so far
     auto issue = [&](int q, int c) {
+        if (r == 0 && q == withhold) return;  // never issued: its wait runs out
         const int n = min(kTopkCh, V - c * kTopkCh) + sh;
         const uint32_t bytes = (uint32_t)((n * 4 + 15) & ~15);
         uint64_t *b = &full[q % kTopkNs];
@@ -88,14 +91,15 @@ __global__ void __launch_bounds__(kTopkThreads, 1)
         // still in flight, write nothing
         if (tid == 0) {
             atomicOr(err, 8u);
-            for (int k = q; k < issued; ++k) mbar_wait(&full[k % kTopkNs], (uint32_t)((k / kTopkNs) & 1));
+            for (int k = q; k < issued; ++k)
+                if (!(r == 0 && k == withhold)) mbar_wait(&full[k % kTopkNs], (uint32_t)((k / kTopkNs) & 1), wait_ns);
         }
     };
 
     // 1. maxima (order-free)
     float m = kNegInf;
     for (int c = 0; c < nch; ++c, ++q) {
-        const bool got = mbar_wait(&full[q % kTopkNs], (uint32_t)((q / kTopkNs) & 1));
+        const bool got = mbar_wait(&full[q % kTopkNs], (uint32_t)((q / kTopkNs) & 1), wait_ns);
         float cm = kNegInf;
         if (got) {
             const float *s = ring + (q % kTopkNs) * kTopkSlot + sh;
@@ -128,7 +132,7 @@ __global__ void __launch_bounds__(kTopkThreads, 1)
     for (int c = 0; c <= nch; ++c) {
         bool got = true;
         if (warp != 0 && c < nch) {
-            got = mbar_wait(&full[q % kTopkNs], (uint32_t)((q / kTopkNs) & 1));
+            got = mbar_wait(&full[q % kTopkNs], (uint32_t)((q / kTopkNs) & 1), wait_ns);
             if (got) {
                 const float *s = ring + (q % kTopkNs) * kTopkSlot + sh;
                 const int n = min(kTopkCh, V - c * kTopkCh), n32 = (n + 31) & ~31;
@@ -202,7 +206,7 @@ __global__ void __launch_bounds__(kTopkThreads, 1)
         bi[j] = 0xffffffffu;
     }
     for (int i = 0; i < nl; ++i, ++q) {
-        const bool got = mbar_wait(&full[q % kTopkNs], (uint32_t)((q / kTopkNs) & 1));
+        const bool got = mbar_wait(&full[q % kTopkNs], (uint32_t)((q / kTopkNs) & 1), wait_ns);
         if (got) {
             const int c = chunk_of(i), n = min(kTopkCh, V - c * kTopkCh);
             const float *s = ring + (q % kTopkNs) * kTopkSlot + sh;

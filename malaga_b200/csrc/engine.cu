@@ -360,6 +360,7 @@ struct mgb_ctx {
     // out and the error word reports it. Off unless the variables are set.
     uint64_t test_wait_ns = kWaitNs;
     int test_withhold_chunk = -1;
+    int test_withhold_topk = -1;  // ring position whose copy row 0 of the top-k kernel withholds (MGB_TEST_WITHHOLD_TOPK)
     int test_withhold_step = -1;  // the same for the persistent step kernel (MGB_TEST_WITHHOLD_STEP)
     // tensor-core FFN: the up epilogue writes the down matmul's q8_1 activations (1)
     // or f32 rows that a prep kernel quantizes (0, the default: the per-token
@@ -1915,7 +1916,8 @@ template <int K>
 static mgb_status beam_topk_k(mgb_ctx *c, const float *logits, int rows, int V, float *vals, uint32_t *idx) {
     cudaError_t e = allow_smem(beam_topk_kernel<K>, kTopkSmem);
     if (e == cudaSuccess) {
-        beam_topk_kernel<K><<<rows, kTopkThreads, kTopkSmem, c->stream>>>(logits, V, vals, idx, c->d_err);
+        beam_topk_kernel<K><<<rows, kTopkThreads, kTopkSmem, c->stream>>>(logits, V, vals, idx, c->d_err,
+                                                                           c->test_wait_ns, c->test_withhold_topk);
         e = cudaGetLastError();
     }
     ++c->launches;
@@ -2257,6 +2259,7 @@ mgb_status mgb_open(const char *path, int device, const mgb_options *opts, mgb_c
     if (const char *v = getenv("MGB_STEP_TRACE")) c->step_trace = v;
     if (const char *v = getenv("MGB_TEST_WAIT_NS")) c->test_wait_ns = std::max<uint64_t>(1000, strtoull(v, nullptr, 10));
     if (const char *v = getenv("MGB_TEST_WITHHOLD_CHUNK")) c->test_withhold_chunk = atoi(v);
+    if (const char *v = getenv("MGB_TEST_WITHHOLD_TOPK")) c->test_withhold_topk = atoi(v);
     if (const char *v = getenv("MGB_TEST_WITHHOLD_STEP")) c->test_withhold_step = atoi(v);
     if (const char *v = getenv("MGB_FFN_Q8")) c->ffn_q8 = atoi(v) != 0;
     if (const char *v = getenv("MGB_SMALL_CLUSTER")) {

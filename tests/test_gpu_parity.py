@@ -398,6 +398,33 @@ def test_log_softmax_topk_kernel_bit_exact(gpu, model, V, k):
     assert np.array_equal(got_v.view(np.uint32), want_v.view(np.uint32)), (got_v, want_v)
 
 
+@pytest.mark.parametrize("position", [0, 70, 130])
+def test_topk_bounded_wait_that_runs_out_is_reported(gpu, model, position, monkeypatch):
+    """The top-k kernel's bounded waits: the test hook withholds the bulk copy at
+    one ring position of row 0 (positions 0-64: the max pass of a 65-chunk row,
+    65-129: the exponential pass, 130: the first chunk of the top-k pass) and shortens the limit to 20 ms; the kernel sets the
+    error word and returns, the call fails with MGB_ERR_CUDA, and a context
+    opened afterwards gives the oracle's result."""
+    from malaga_b200 import _lib
+
+    rng = np.random.default_rng(position)
+    x = rng.standard_normal((3, 4096 * 64 + 5)).astype(np.float32)  # 65 chunks per row
+    x[0, 4096 * 64 + 2] = 9.0  # row 0's winner in its last chunk: the top-k pass fetches it
+    monkeypatch.setenv("MGB_TEST_WAIT_NS", "20000000")
+    monkeypatch.setenv("MGB_TEST_WITHHOLD_TOPK", str(position))
+    eng = Engine(model("tiny", "q8_0"))
+    with pytest.raises(MgbError) as e:
+        eng.log_softmax_topk(x, 4)
+    assert e.value.code == _lib.MGB_ERR_CUDA
+    assert "ran out of time" in str(e.value)
+    eng.close()
+    monkeypatch.delenv("MGB_TEST_WITHHOLD_TOPK")
+    want_v, want_i = oracle.log_softmax_topk(x, 4)
+    got_v, got_i = Engine(model("tiny", "q8_0")).log_softmax_topk(x, 4)
+    np.testing.assert_array_equal(got_i, want_i)
+    assert np.array_equal(got_v.view(np.uint32), want_v.view(np.uint32))
+
+
 def test_beam_one_equals_greedy_on_device(gpu, model):
     """pipeline.rs:60-69: beam 1 gives the greedy output."""
     path = model("tiny", "q8_0")
