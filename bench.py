@@ -374,7 +374,7 @@ def main():
                          "off by default); the LM-head roofline stays the full head's")
     ap.add_argument("--streams", type=int, default=None,
                     help="decode contexts (CUDA streams) per GPU for independent batches (dp.StreamPool); "
-                         "default 8, 2 for c4 (3.3B: larger states)")
+                         "default 8, 4 for c4 (3.3B: larger states)")
     args = ap.parse_args()
     if args.workload == "c5" and args.impl == "ours":
         return run_c5(args)
@@ -421,7 +421,7 @@ def main():
     srcs = [[w.sources[i] for i in b] for b in share]
     # independent batches decode on `streams` contexts of this GPU at once
     # (dp.StreamPool); batch i belongs to context i % streams
-    streams = max(1, min(args.streams or (2 if w.model == "3.3b" else 8), len(srcs)))
+    streams = max(1, min(args.streams or (4 if w.model == "3.3b" else 8), len(srcs)))
     # (3.3B states at batch 128 are ~7 GB each: room for every source-length bucket)
     pool = dp.StreamPool(path, device=local, streams=streams, graph_cache_mb=65536 if w.model == "3.3b" else 8192)
     eng = pool.engines[0]
