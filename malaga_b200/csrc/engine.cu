@@ -928,12 +928,12 @@ static size_t tc_smem(int type, int nt) {
 // Open contexts per device. Every tensor-core CTA holds an SM, and narrow token
 // tiles repeat a weight tile's conversion once per tile: the fastest launch
 // alone on a GPU, but the most SM time per token. With one context the matmuls
-// choose the fastest launch; with several (independent batches decoding
-// concurrently, dp.StreamPool) the GPU's SM time is the bound, and tiles of at
-// least 32 tokens (or one tile for a smaller batch) give more tokens per second:
-// batch-64 decode on NLLB-600M q4_k_m, B200, measured 64.3k tokens/s with
-// 8-token floors and 70.9k with 32 on 4 contexts, 83.9k on 8; one context loses
-// 30 % with the 32 floor.
+// choose the fastest launch; the more contexts decode concurrently
+// (dp.StreamPool), the more the GPU's SM time is the bound and the wider the
+// narrowest tile: 16 tokens for 2-3 contexts, 32 from 4 (or one tile for a
+// smaller batch). Batch-64 decode on NLLB-600M q4_k_m, B200, tokens/s by floor
+// 8 / 16 / 32: 2 contexts 56.5k / 60.2k / 53.0k, 4 contexts 64.1k / 69.1k /
+// 70.7k; 8 contexts with 32: 83.9k; one context loses 30 % with 32.
 static std::mutex g_ctx_mu;
 static std::map<int, int> g_ctx_open;
 
@@ -950,9 +950,11 @@ static void count_context(int device, int delta) {
 
 static int tc_floor(const mgb_ctx *c, int rows) {
     if (c->tc_min_nt > 0) return c->tc_min_nt;
-    if (contexts_on(c->device) <= 1) return 8;
+    const int open = contexts_on(c->device);
+    if (open <= 1) return 8;
+    const int cap = open >= 4 ? 32 : 16;
     int f = 8;
-    while (f < 32 && f < rows) f *= 2;
+    while (f < cap && f < rows) f *= 2;
     return f;
 }
 

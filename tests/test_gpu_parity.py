@@ -305,24 +305,24 @@ def test_tensor_core_batches_bit_exact(gpu, model, name, preset, b, ffn_q8, monk
         f"max |diff| {np.abs(got_logits - want_logits).max()}"
 
 
-@pytest.mark.parametrize("mode", ["two_contexts", "64"])
+@pytest.mark.parametrize("mode", ["two_contexts", "four_contexts", "64"])
 @pytest.mark.parametrize("name,preset,b", [("mid", "q4_k_m", 64), ("wide", "q4_k_m", 40)])
 def test_tensor_core_tile_floors_bit_exact(gpu, model, name, preset, b, mode, monkeypatch):
-    """With several contexts open on the device the tensor-core matmuls use token
-    tiles of at least 32 tokens (64 with MGB_TC_MIN_NT=64); the tiles change
-    which CTA forms an output, not its arithmetic: tokens and logits equal the
-    oracle's bit for bit."""
-    if mode != "two_contexts":
+    """With several contexts open on the device the tensor-core matmuls use wider
+    token tiles (16 tokens at least for two contexts, 32 from four, 64 with
+    MGB_TC_MIN_NT=64); the tiles change which CTA forms an output, not its
+    arithmetic: tokens and logits equal the oracle's bit for bit."""
+    if mode == "64":
         monkeypatch.setenv("MGB_TC_MIN_NT", mode)
     path = model(name, preset)
     V = models.config_of(name).vocab_size
     src = models.random_sources(b, 2, 10, V, 11, src_tag=V - 1)
     want_ids, want_logits = oracle.Oracle(path).greedy(src, V - 2, 3, force=True, logits=True)
     eng = Engine(path)
-    other = Engine(path) if mode == "two_contexts" else None
+    others = [Engine(path) for _ in range({"two_contexts": 1, "four_contexts": 3}.get(mode, 0))]
     got_ids, got_logits = eng.greedy_logits(eng.encode(src), V - 2, 3, force=True)
-    if other is not None:
-        other.close()
+    for o in others:
+        o.close()
     np.testing.assert_array_equal(got_ids, want_ids)
     assert np.array_equal(got_logits.view(np.uint32), want_logits.view(np.uint32)), \
         f"max |diff| {np.abs(got_logits - want_logits).max()}"
