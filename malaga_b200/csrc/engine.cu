@@ -922,9 +922,6 @@ static size_t tc_smem(int type, int nt) {
     }
 }
 
-// Token tile (activation rows per tile, at least min_nt) of a tensor-core
-// matmul: the one that needs the fewest waves of tiles over the SMs, on a tie
-// the narrowest, whose tiles finish soonest; persistent CTAs, one per SM.
 // Open contexts per device. Every tensor-core CTA holds an SM, and narrow token
 // tiles repeat a weight tile's conversion once per tile: the fastest launch
 // alone on a GPU, but the most SM time per token. With one context the matmuls
@@ -933,7 +930,9 @@ static size_t tc_smem(int type, int nt) {
 // narrowest tile: 16 tokens for 2-3 contexts, 32 from 4 (or one tile for a
 // smaller batch). Batch-64 decode on NLLB-600M q4_k_m, B200, tokens/s by floor
 // 8 / 16 / 32: 2 contexts 56.5k / 60.2k / 53.0k, 4 contexts 64.1k / 69.1k /
-// 70.7k; 8 contexts with 32: 83.9k; one context loses 30 % with 32.
+// 70.7k; 8 contexts with 32: 83.9k; one context loses 30 % with 32. The floor
+// is read when a step is launched or captured: a CUDA graph keeps the tiles of
+// its capture (dp.StreamPool opens all its contexts before the first decode).
 static std::mutex g_ctx_mu;
 static std::map<int, int> g_ctx_open;
 
@@ -958,6 +957,9 @@ static int tc_floor(const mgb_ctx *c, int rows) {
     return f;
 }
 
+// Token tile (activation rows per tile, at least min_nt) of a tensor-core
+// matmul: the one that needs the fewest waves of tiles over the SMs, on a tie
+// the narrowest, whose tiles finish soonest; persistent CTAs, one per SM.
 static void tc_shape(const Matrix &W, int rows, int sms, int min_nt, int &nt, int &grid) {
     const int row_tiles = W.Np / 128;
     long best = 0;
