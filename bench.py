@@ -295,7 +295,7 @@ def run_c3(args):
         ms.append(e0.elapsed_time(e1))
     wall = time.perf_counter() - wall
     total = sum(ms) / 1e3
-    line = {"metric": "C3: beam-4 decoded tokens/s NLLB-1.3B q4_k_m b16", "value": toks / total, "unit": "tokens/s",
+    line = {"metric": C3_METRIC, "value": toks / total, "unit": "tokens/s",
             "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": statistics.median(ms),
             "higher_is_better": True, "data": "synthetic",
             "beam_rows_steps_per_s": 16 * 4 * w.steps * args.steps / total,
@@ -304,8 +304,57 @@ def run_c3(args):
             "config": {"workload": "c3: NLLB-1.3B q4_k_m (random init, seed 2), beam 4, length penalty 1.0, 16 "
                                    "sources of 48 ids, at most 96 steps (64 beam rows per step)",
                        "step": "ms_per_step = one encode + beam search of the batch"}}
-    print(json.dumps(line), flush=True)
     eng.close()
+    if not args.no_cpu_baseline:
+        try:
+            line["cpu_baseline"] = c3_cpu_sample()
+        except Exception as e:  # reported, never fatal
+            line["cpu_baseline"] = {"error": str(e)}
+    print(json.dumps(line), flush=True)
+
+
+C3_METRIC = "C3: beam-4 decoded tokens/s NLLB-1.3B q4_k_m b16"
+
+
+def c3_cpu_sample() -> dict:
+    """Config 3 on the oracle (the CPU restatement of encode + beam search,
+    translator.rs:250-358, OpenMP on every host core): a bounded sample of the
+    workload -- its first source, beam 4, at most 3 tokens -- timed whole; value
+    = the best hypothesis' tokens per second."""
+    import oracle
+
+    w = models.workload("c3")
+    path = models.model_path(w.model, w.preset, w.seed)
+    oracle.lib().orc_set_threads(len(os.sched_getaffinity(0)))
+    orc = oracle.Oracle(path)
+    src, max_new = w.sources[:1], 3
+    t0 = time.perf_counter()
+    out = orc.beam(src, models.TGT_TAG, 4, max_new)
+    dt = time.perf_counter() - t0
+    return {"value": max(1, sum(len(r) for r in out)) / dt, "unit": "tokens/s", "cores": oracle.lib().orc_threads(),
+            "kind": "port", "sample": f"1 source of {len(src[0])} ids, beam 4, at most {max_new} tokens "
+                                      f"(encode + beam), {dt:.1f} s", "seconds": dt}
+
+
+def run_reference_c3(args):
+    """Config 3's reference arm, rank 0 only: c3_cpu_sample per step, the
+    median over --steps after --warmup."""
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    results = [c3_cpu_sample() for _ in range(args.warmup + args.steps)][args.warmup:]
+    v = statistics.median(r["value"] for r in results)
+    cb = dict(results[-1])
+    cb["value"] = v
+    line = {"impl": "reference", "metric": C3_METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * statistics.median(r["seconds"] for r in results),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 dot / f32",
+            "data": "synthetic",
+            "config": {"workload": "c3", "model": "nllb-1.3b-q4_k_m (random init)", "sample": cb["sample"]},
+            "cpu_baseline": cb, "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                                        "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
 
 
 def run_c5(args):
@@ -378,8 +427,8 @@ def main():
     args = ap.parse_args()
     if args.workload == "c5" and args.impl == "ours":
         return run_c5(args)
-    if args.workload == "c3" and args.impl == "ours":
-        return run_c3(args)
+    if args.workload == "c3":
+        return run_c3(args) if args.impl == "ours" else run_reference_c3(args)
     w = models.workload(args.workload)
     if args.impl == "reference":
         return run_reference(args, w)
