@@ -51,6 +51,8 @@ import numpy as np  # noqa: E402
 from malaga_b200 import dp, models  # noqa: E402
 
 METRIC = "decoded tokens/s NLLB-600M q4_k_m b64 @1/2/4/8 B200; p50 ms/sentence b1"
+C4_METRIC = "C4: decoded tokens/s NLLB-3.3B q4_k_m b128 @1/2/4/8 B200"
+C5_METRIC = "C5 server: sustained decoded tokens/s; p50/p99 ms request latency"
 
 
 def dist_env():
@@ -191,7 +193,7 @@ def run_reference(args, w):
     cb["value"] = v
     rows, sample_steps = cpu_sample(w)
     line = {"impl": "reference",
-            "metric": METRIC if w.model == "600m" else "C4: decoded tokens/s NLLB-3.3B q4_k_m b128 @1/2/4/8 B200",
+            "metric": C5_METRIC if w.name == "c5" else (METRIC if w.model == "600m" else C4_METRIC),
             "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * rows * sample_steps / v,
             "higher_is_better": True, "scaling": "strong" if w.name in ("dp600", "c4") else "weak",
@@ -397,7 +399,7 @@ def run_c5(args):
     stream()  # warm-up: graph capture of every (batch, source, output) bucket
     lat, span, toks = stream()
     srv.close()
-    line = {"metric": "C5 server: sustained decoded tokens/s; p50/p99 ms request latency", "value": toks / span,
+    line = {"metric": C5_METRIC, "value": toks / span,
             "unit": "tokens/s", "n_gpus": args.gpus, "higher_is_better": True, "data": "synthetic",
             "p50_ms": float(np.percentile(lat, 50)), "p99_ms": float(np.percentile(lat, 99)),
             "mean_ms": float(lat.mean()), "requests": len(lat), "decoded_tokens": toks, "seconds": span,
@@ -560,7 +562,7 @@ def main():
 
     if rank == 0:
         line = {
-            "metric": METRIC if w.model == "600m" else "C4: decoded tokens/s NLLB-3.3B q4_k_m b128 @1/2/4/8 B200",
+            "metric": METRIC if w.model == "600m" else C4_METRIC,
             "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": scaling,
             "vs_baseline": None, "dtype": "int8 dot / f32 (q8_1 activations x GGUF blocks)", "data": "synthetic",
